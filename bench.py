@@ -1,0 +1,397 @@
+#!/usr/bin/env python
+"""Benchmark: compressed-KV decode attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (config 1): batch 32 per GPU, 32 query heads / 8 kv heads,
+head_dim 128, 8192 cached tokens per sequence, 32 layers, 4-bit K and V
+packed. One step = for every layer: quantize-append the new token's K and V
+of all 32 sequences, then decode attention for the 32 query heads over the
+whole context. Synthetic seeded data: K, V ~ N(0, 1) with 4 outlier channels
+per kv head scaled x8; queries ~ N(0, 1/sqrt(128)) read as a standard
+deviation, softmax scale 1. The 9 GB cache is far larger than L2 (126 MB),
+so every step streams it from HBM (no flush needed).
+
+`value` is whole-job decode tokens/s with inputs resident in HBM. `e2e`
+drives the same step through the C ABI with pinned host buffers: the query,
+new K/V and output cross PCIe every layer, and every call returns its result
+to the host. Under torchrun each rank runs its own 32 sequences (weak
+scaling, no collective on the data path).
+
+`--impl reference` times the reference's CPU path (the oracle's C++
+restatement of turboquant-cache SimpleCache: attend_keys, softmax,
+attend_values) on a bounded sample on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "compressed-KV decode attn GB/s & tokens/s vs HBM roofline; quantize-append GB/s"
+CFG = dict(batch=32, hq=32, hkv=8, dim=128, ctx=8192, layers=32, k_bits=4, v_bits=4)
+BYTES_PER_TOKEN_HEAD = 8 * 8 + 8 * 8 + 4 + 4  # 4-bit d=128: 8 K words + 8 V words + 2 sigma = 136 B
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per decode launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "k_decode_mma_config1.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the oracle (C++ restatement of SimpleCache decode)
+# ----------------------------------------------------------------------------
+def cpu_attend_sample(seq_data, hq: int, hkv: int, dim: int, threads: int, budget_s: float, seed: int = 7):
+    """Time decode for one (sequence, layer) of config 1 on the CPU oracle.
+
+    seq_data: per kv head (k_words [n,W], k_sigma [n], v_words, v_sigma).
+    Runs query heads until `budget_s` of wall time or all hq heads are done;
+    returns seconds for all hq heads (extrapolated) and the heads run.
+    """
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import pyoracle as orc
+    from concurrent.futures import ThreadPoolExecutor
+
+    orc.build()
+    t = orc.Tables.generate(dim, CFG["k_bits"], 64, 42)
+    comp = orc.Compressor(t)
+    sc = orc.SimpleCache(comp, comp, 1, hkv, dim)
+    for h, (kw, ks, vw, vs) in enumerate(seq_data):
+        sc.load(0, h, 0, kw, ks)
+        sc.load(0, h, 1, vw, vs)
+    q = (orc.gauss_f32(seed, hq * dim).reshape(hq, dim) * np.float32(dim ** -0.5)).astype(np.float32)
+    G = hq // hkv
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        while done < hq:
+            batch = list(range(done, min(hq, done + threads)))
+            list(ex.map(lambda h: sc.attend(0, h // G, q[h], 1.0), batch))
+            done += len(batch)
+            if time.perf_counter() - t0 > budget_s:
+                break
+    el = time.perf_counter() - t0
+    return el * hq / done, done
+
+
+def synth_seq_on_cpu(n: int, hkv: int, dim: int, seed: int):
+    """One sequence of config-1 K/V compressed by the oracle (reference arm)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import pyoracle as orc
+    from concurrent.futures import ThreadPoolExecutor
+
+    orc.build()
+    t = orc.Tables.generate(dim, CFG["k_bits"], 64, 42)
+    comp = orc.Compressor(t)
+
+    def one(h):
+        out = []
+        for side in (0, 1):
+            x = orc.gauss_f32(seed * 1000 + 2 * h + side, n * dim).reshape(n, dim)
+            rng = np.random.default_rng(seed + h)
+            x[:, rng.choice(dim, 4, replace=False)] *= np.float32(8.0)
+            s1, _, _, sc = comp.compress(x)
+            out += [s1, sc]
+        return out
+
+    with ThreadPoolExecutor(max_workers=os.cpu_count() or 1) as ex:
+        return list(ex.map(one, range(hkv)))
+
+
+def run_reference(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return  # rank 0 alone times the CPU reference
+    hq, hkv, dim, ctx, L, B = CFG["hq"], CFG["hkv"], CFG["dim"], CFG["ctx"], CFG["layers"], CFG["batch"]
+    threads = os.cpu_count() or 1
+    data = synth_seq_on_cpu(ctx, hkv, dim, 11)
+    per = []
+    for k in range(args.warmup + args.steps):
+        s, heads = cpu_attend_sample(data, hq, hkv, dim, threads, budget_s=2.0, seed=100 + k)
+        if k >= args.warmup:
+            per.append(s)
+    sample_s = statistics.median(per)
+    step_s = sample_s * L * B  # one (seq, layer) sample scaled to the whole step
+    tok_s = B / step_s
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config1 decode: batch 32, 32q/8kv, d128, ctx 8192, 32 layers, 4-bit K/V",
+                   "sample": "one (sequence, layer) per step, scaled by layers x batch"},
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"1 of {L * B} (sequence, layer) pairs per step: {hq} query heads over "
+                                   f"{ctx} tokens, oracle C++ restatement of SimpleCache, {threads} threads"},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# Our arm
+# ----------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    rank, local, world = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    lc = importlib.import_module("lumen-rs_b200")
+    B, hq, hkv, D, ctx, L = CFG["batch"], CFG["hq"], CFG["hkv"], CFG["dim"], CFG["ctx"], CFG["layers"]
+    steps, warm = args.steps, args.warmup
+    total_new = steps + warm + (args.e2e_steps if rank == 0 else 0) + 1
+    pages_per_seq = (ctx + total_new + 255) // 256 + 1
+    codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
+    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=B, max_pages=L * B * pages_per_seq + 64,
+                           max_pages_per_seq=pages_per_seq, device=local)
+    ids = list(range(B))
+    stream_ptr = cache.stream()
+    s = torch.cuda.ExternalStream(stream_ptr, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + 7919 * rank)
+    sel = torch.Generator(device="cpu")
+    sel.manual_seed(99)
+    outl = torch.stack([torch.randperm(D, generator=sel)[:4] for _ in range(hkv)])  # [hkv, 4]
+    scale_vec = torch.ones(hkv, D)
+    for h in range(hkv):
+        scale_vec[h, outl[h]] = 8.0
+    scale_vec = scale_vec.to(dev).view(1, hkv, 1, D)
+
+    def kv_block(n):
+        x = torch.randn((B, hkv, n, D), generator=gen, device=dev, dtype=torch.float32) * scale_vec
+        return x.to(torch.bfloat16).contiguous()
+
+    # ---- fill the cache: 8192 tokens per sequence per layer (untimed) ----
+    t_fill = time.time()
+    with torch.cuda.stream(s):
+        for layer in range(L):
+            for c0 in range(0, ctx, 2048):
+                k, v = kv_block(2048), kv_block(2048)
+                torch.cuda.current_stream().synchronize()
+                cache.append(layer, ids, k, v, stream=stream_ptr)
+    torch.cuda.synchronize()
+    fill_s = time.time() - t_fill
+
+    # per-step inputs, device resident
+    qs = (torch.randn((L, B, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    k1 = torch.stack([kv_block(1) for _ in range(L)])
+    v1 = torch.stack([kv_block(1) for _ in range(L)])
+    out = torch.empty((L, B, hq, D), device=dev, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+
+    def step():
+        for layer in range(L):
+            cache.append(layer, ids, k1[layer], v1[layer], stream=stream_ptr)
+            cache.decode_attn(layer, ids, qs[layer], hq, 1.0, out=out[layer], out_dtype=lc.LC_BF16,
+                              stream=stream_ptr)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ctx0 = cache.ring_state(0, 0)["view_len"]
+    launches0 = cache.kernel_launches()
+    cache.timing(1)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(s)
+        for _ in range(steps):
+            step()
+        ev1.record(s)
+        ev1.synchronize()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    dec_ms, dec_n, app_ms, app_n = cache.timing(0)
+    launches = cache.kernel_launches() - launches0
+    ctx1 = cache.ring_state(0, 0)["view_len"]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_step = elapsed_ms / steps
+    tok_s = world * B * steps / (elapsed_ms / 1e3)
+    # algorithmic bytes: every attended token's packed K/V words and sigmas, once per kv head
+    tokens_attended = B * steps * sum(range(ctx0 + 1, ctx0 + 1 + steps)) / steps  # per layer over the run
+    kv_bytes_per_launch = B * hkv * BYTES_PER_TOKEN_HEAD * (ctx0 + 1 + ctx1) / 2.0
+    dec_avg_ms = dec_ms / max(dec_n, 1)
+    achieved = kv_bytes_per_launch / (dec_avg_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+    decode_gbs = world * kv_bytes_per_launch * L * steps / (elapsed_ms / 1e3) / 1e9
+    # append: bf16 in (2 x 256 B per vector pair of K,V), packed words + sigma out
+    app_vecs = B * hkv * 2
+    app_bytes = app_vecs * (D * 2 + 8 * 8 + 4)
+    app_avg_ms = app_ms / max(app_n, 1)
+
+    result = None
+    if rank == 0:
+        # ---- e2e through the C ABI with pinned host buffers ----
+        qh = qs[:, :].cpu().pin_memory()
+        kh, vh = k1.cpu().pin_memory(), v1.cpu().pin_memory()
+        oh = torch.empty((L, B, hq, D), dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            for layer in range(L):
+                cache.append(layer, ids, kh[layer], vh[layer])
+                cache.decode_attn(layer, ids, qh[layer], hq, 1.0, out=oh[layer], out_dtype=lc.LC_BF16)
+
+        e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+        h2d = L * (B * hq * D * 2 + 2 * B * hkv * D * 2)
+        d2h = L * B * hq * D * 2
+        # ---- CPU baseline: oracle decode of one (seq, layer) sample ----
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            f = cache.fetch(0, 0)
+            data = [(f["k_words"][h], f["k_sigma"][h], f["v_words"][h], f["v_sigma"][h]) for h in range(hkv)]
+            sample_s, heads = cpu_attend_sample(data, hq, hkv, D, threads=1, budget_s=args.cpu_budget)
+            cpu_tok_s = B / (sample_s * L * B)
+            cpu = {"value": cpu_tok_s, "unit": "tok/s", "cores": 1, "kind": "port",
+                   "sample": f"{heads} of {hq} query heads of one (sequence, layer) over {ctx1} tokens "
+                             f"(attend_keys + softmax + attend_values, oracle C++), scaled to {L} layers x {B} seqs"}
+        result = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config1 decode: batch 32/GPU, 32q/8kv, d128, ctx 8192 (+1 per step), "
+                                   "32 layers, 4-bit K/V packed; append + decode per layer",
+                       "global_batch": world * B, "seq_len": ctx, "parallelism": f"request-shard x{world}",
+                       "l2": "inputs larger than L2 (9.1 GB cache per GPU)",
+                       "queries": "bf16 N(0, std 1/sqrt(128)), scale 1.0"},
+            "decode_gbs": decode_gbs,
+            "append": {"gbs": app_bytes / (app_avg_ms / 1e3) / 1e9, "vectors_per_s": app_vecs / (app_avg_ms / 1e3),
+                       "avg_launch_us": app_avg_ms * 1e3, "mode": "strict bit-exact"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profile_traffic(),
+                         "kernel": "k_decode_mma", "avg_launch_us": dec_avg_ms * 1e3, "launches": dec_n,
+                         "bytes_per_launch": kv_bytes_per_launch, "peak_source": f"{peak_kind} hbm_gbs"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": B / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_s * 1e3},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "fill_s": fill_s,
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    cache.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU-baseline sampling")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

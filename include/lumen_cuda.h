@@ -1,0 +1,292 @@
+/*
+ * lumen_cuda.h — C ABI of the B200 (sm_100a) TurboQuant KV cache.
+ *
+ * This is the drop-in boundary for the TurboQuant compressed-KV path of
+ * rabbitson87/lumen-rs. Every entry point names the reference interface it
+ * replaces (paths are inside that project):
+ *   crates/lumen-core/src/compressor.rs        TurboQuantCompressor
+ *   crates/lumen-core/src/{rotation,lloyd_max,qjl}.rs   table files
+ *   crates/turboquant-cache/src/traits.rs      trait KVCache
+ *   crates/turboquant-cache/src/simple.rs      SimpleCache
+ *   crates/lumen-mlx/src/native_cache.rs       NativeRotatingKvCacheTurboQuant
+ *   crates/lumen-mlx/src/turboquant.rs         turboquant_fused_attn
+ *
+ * Conventions
+ *  - Every call returns an int status: LC_OK (0) or a negative LC_ERR_*.
+ *    lc_last_error() returns a message for the last failure on this thread.
+ *    No C++ exception crosses the ABI.
+ *  - Plain pointers and sizes only. A data pointer may be host memory or
+ *    device memory of the cache's device; the library tells them apart and
+ *    stages host buffers itself. Caller buffers are borrowed for the call.
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the library's
+ *    own stream for that object. Calls that return host results synchronise.
+ *  - A handle is thread-compatible, not thread-safe: one thread at a time,
+ *    matching the reference's `&mut self`.
+ */
+#ifndef LUMEN_CUDA_H
+#define LUMEN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define LC_OK 0
+#define LC_ERR_INVALID (-1)  /* bad argument, shape or handle */
+#define LC_ERR_BITS (-2)     /* bit width outside the accepted range */
+#define LC_ERR_REFUSED (-3)  /* rollback refused (native_cache.rs:304-335) */
+#define LC_ERR_CUDA (-4)     /* CUDA runtime error */
+#define LC_ERR_TIMEOUT (-5)  /* a bounded device wait ran out */
+#define LC_ERR_NOMEM (-6)    /* page pool or device memory exhausted */
+#define LC_ERR_IO (-7)       /* file I/O failure */
+#define LC_ERR_MAGIC (-8)    /* table file with the wrong magic */
+#define LC_ERR_STATE (-9)    /* call not valid in the handle's state */
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* lc_last_error(void);
+
+/* Element types of caller tensors. */
+#define LC_F32 0
+#define LC_BF16 1
+#define LC_F16 2
+
+/* ---- codec tables (one TurboQuantCompressor) --------------------------- */
+typedef struct lc_codec lc_codec;
+
+/* TurboQuantCompressor::new (compressor.rs:20-32): rotation from `seed`,
+ * QJL projection from `seed + 1`, Lloyd-Max codebook with `lloyd_max_iter`
+ * EM iterations. The rotation and projection come from this library's own
+ * seeded generator (SplitMix64 + Box-Muller, then the reference's
+ * Gram-Schmidt construction), not from Rust's StdRng: for the reference's
+ * exact tables, load its files with lc_codec_from_files. bits: 1..8. */
+int lc_codec_new(uint32_t bits, uint64_t qjl_m, uint64_t seed, uint64_t lloyd_max_iter,
+                 uint64_t head_dim, lc_codec** out);
+
+/* TurboQuantCompressor::from_files (compressor.rs:43-58): TQCB codebook
+ * (lloyd_max.rs:187-213), TQRM rotation (rotation.rs:130-150) and TQJL
+ * projection (qjl.rs:248-272) files. */
+int lc_codec_from_files(const char* codebook_path, const char* rotation_path, const char* qjl_path,
+                        lc_codec** out);
+
+/* Same tables from host arrays: rotation [d*d] row-major f32, boundaries
+ * [2^bits + 1] f64 (first -inf, last +inf), centroids [2^bits] f64, qjl
+ * projection [m*d] row-major f32 (may be NULL when qjl_m == 0). */
+int lc_codec_from_tables(uint64_t head_dim, uint32_t bits, uint64_t qjl_m, const float* rotation,
+                         const double* boundaries, const double* centroids, const float* qjl_proj,
+                         lc_codec** out);
+
+/* RotationMatrix::save / LloydMaxCodebook::save / QJLProjector::save. */
+int lc_codec_save(const lc_codec* c, const char* codebook_path, const char* rotation_path,
+                  const char* qjl_path);
+
+/* Copy the tables out (any pointer may be NULL). */
+int lc_codec_tables(const lc_codec* c, float* rotation, double* boundaries, double* centroids,
+                    float* qjl_proj);
+
+/* head_dim, bits, qjl_m. */
+int lc_codec_shape(const lc_codec* c, uint64_t* head_dim, uint32_t* bits, uint64_t* qjl_m);
+
+void lc_codec_free(lc_codec* c);
+
+/* ---- bit packing (bitpack.rs:11-52) ------------------------------------ */
+/* packed_words(n, bits): u64 words for n codes, 64/bits codes per word. */
+uint64_t lc_packed_words(uint64_t n, uint32_t bits);
+
+/* ---- the cache --------------------------------------------------------- */
+typedef struct lc_cache lc_cache;
+
+/* Store flags. */
+#define LC_STORE_K_QJL 1u /* keep the K stage-2 QJL bits + residual norm */
+#define LC_STORE_V_QJL 2u /* keep the V stage-2 QJL bits + residual norm */
+
+typedef struct lc_cache_config {
+  int32_t n_layers;
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t max_seqs;  /* sequence slots 0..max_seqs-1 */
+  int64_t max_pages; /* page pool size; a page holds 256 tokens of every kv head of one layer */
+  int64_t max_pages_per_seq; /* block-table width per (sequence, layer) */
+  uint32_t store_flags;      /* LC_STORE_* */
+  int32_t device;            /* CUDA device ordinal */
+  int32_t step_prealloc;     /* 1: S=1 updates write in place (LUMEN_NATIVE_KV_STEP_PREALLOC) */
+  int32_t reserved;
+  /* Per-layer ring geometry; NULL => every layer is full (append-only).
+   * max_size 0 marks a full layer; otherwise the sliding window size, with
+   * keep sink tokens (native_cache.rs:1541-1550: keep < max_size). */
+  const int64_t* layer_max_size;
+  const int64_t* layer_keep;
+} lc_cache_config;
+
+/* SimpleCache::new (simple.rs:60-74) generalised to many sequences and to
+ * mlx-lm ring layers. k_codec and v_codec may be the same handle; both must
+ * have head_dim == config->head_dim. The codecs are copied to the device. */
+int lc_cache_create(const lc_cache_config* config, const lc_codec* k_codec, const lc_codec* v_codec,
+                    lc_cache** out);
+void lc_cache_destroy(lc_cache* cache);
+
+/* KVCache::store (traits.rs:14, simple.rs:123-135) for one (seq, layer,
+ * kv head): keys/values [n_tokens, head_dim] f32, compressed on the GPU.
+ * Full layers only; heads of a layer may hold different lengths. */
+int lc_store(lc_cache* cache, int32_t seq, int32_t layer, int32_t head, const float* keys,
+             const float* values, int64_t n_tokens);
+
+/* KVCache::attend_keys (traits.rs:19; compressor.rs:165-184): stage-1
+ * scores of `query` [head_dim] f32 against every cached key of (seq,
+ * layer, head). scores: n_scores >= lc_seq_len floats. */
+int lc_attend_keys(lc_cache* cache, int32_t seq, int32_t layer, int32_t head, const float* query,
+                   float* scores, int64_t n_scores);
+
+/* KVCache::attend_values (traits.rs:24; simple.rs:76-99, 142-155):
+ * sum_t w_t * R^T(c_t * sigma_t), weights with |w| < 1e-10 skipped.
+ * out: head_dim floats. */
+int lc_attend_values(lc_cache* cache, int32_t seq, int32_t layer, int32_t head, const float* weights,
+                     int64_t n_weights, float* out);
+
+/* KVCache::seq_len (traits.rs:27). Negative on error. */
+int64_t lc_seq_len(const lc_cache* cache, int32_t seq, int32_t layer, int32_t head);
+
+/* KVCache::clear (traits.rs:30): every sequence, every layer. */
+int lc_clear(lc_cache* cache);
+
+/* KVCache::truncate (traits.rs:36, simple.rs:174-185): cap every head of
+ * (seq, layer) at n_keep tokens; no-op when already shorter. */
+int lc_truncate(lc_cache* cache, int32_t seq, int32_t layer, int64_t n_keep);
+
+/* Quantize-on-append + NativeRotatingKvCacheTurboQuant::update_and_fetch
+ * (native_cache.rs:1756-1793; with LC_STORE_K_QJL set, update_and_fetch_qjl
+ * :1805-1856). keys/values: [n_seqs, n_kv_heads, n_tokens, head_dim] of
+ * `dtype`, un-rotated; the kernel rotates, normalises, quantizes, packs and
+ * (if stored) computes the QJL bits exactly as compress_one
+ * (compressor.rs:61-107). Every listed sequence advances by n_tokens. */
+int lc_append(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+              const void* keys, const void* values, int32_t dtype, int64_t n_tokens, void* stream);
+
+/* NativeRotatingKvCacheTurboQuant::truncate_to (native_cache.rs:1728-1746
+ * -> ring_truncate :304-335): LC_ERR_REFUSED if target > offset or the ring
+ * has rotated (offset > max_size). */
+int lc_truncate_to(lc_cache* cache, int32_t seq, int32_t layer, int64_t target);
+
+/* Prefix reuse through the block table: dst (emptied first) receives the
+ * first prefix_len tokens of src in every layer by sharing src's pages
+ * (copy-on-write); no data is copied. The reference shares prefixes only for
+ * plain layers (native_cache.rs:459-527) and deep-clones TurboQuant layers
+ * (:1581-1610); sharing is refused like a rollback when a ring has rotated. */
+int lc_fork(lc_cache* cache, int32_t src_seq, int32_t dst_seq, int64_t prefix_len);
+
+/* Drop every page of one sequence (all layers). */
+int lc_release(lc_cache* cache, int32_t seq);
+
+/* Ring counters of (seq, layer): offset (tokens ever pushed), idx (write
+ * index), buf_len (backing buffer length, cached_len), view_len (tokens the
+ * last update returned / decode attends). Any pointer may be NULL. */
+int lc_ring_state(const lc_cache* cache, int32_t seq, int32_t layer, int64_t* offset, int64_t* idx,
+                  int64_t* buf_len, int64_t* view_len);
+
+/* What lc_fetch copies out. */
+#define LC_FETCH_VIEW 0    /* the tokens update_and_fetch returned */
+#define LC_FETCH_BACKING 1 /* the whole backing buffer (padding, stale slots) */
+
+typedef struct lc_fetch_out {
+  uint64_t* k_words;  /* [n_kv_heads, n, packed_words(d, k_bits)] */
+  float* k_sigma;     /* [n_kv_heads, n] */
+  uint64_t* v_words;  /* [n_kv_heads, n, packed_words(d, v_bits)] */
+  float* v_sigma;     /* [n_kv_heads, n] */
+  uint64_t* k_qjl;    /* [n_kv_heads, n, ceil(m/64)] (LC_STORE_K_QJL) */
+  float* k_rnorm;     /* [n_kv_heads, n] */
+  uint64_t* v_qjl;    /* [n_kv_heads, n, ceil(m/64)] (LC_STORE_V_QJL) */
+  float* v_rnorm;     /* [n_kv_heads, n] */
+} lc_fetch_out;
+
+/* Copy (seq, layer)'s stored vectors to host buffers in the reference's
+ * CompressedVector layout (config.rs:30-46): packed u64 code words, sigma,
+ * QJL words, residual norm. NULL fields are skipped. *n_out gets n. */
+int lc_fetch(lc_cache* cache, int32_t seq, int32_t layer, int32_t which, lc_fetch_out* out,
+             int64_t max_tokens, int64_t* n_out);
+
+/* Decode flags. */
+#define LC_Q_ROTATED 1u   /* q is already R q (Gemma path); skip the rotation */
+#define LC_OUT_ROTATED 2u /* leave the output in the rotated basis (R baked into Wo) */
+
+/* Decode attention over the compressed cache, one query token per
+ * sequence: out = softmax(scale * q K_dq^T) V_dq for every query head, with
+ * GQA (query head h reads kv head h / (n_q_heads / n_kv_heads)).
+ * turboquant_fused_attn (turboquant.rs:887-923) / SimpleCache attend_keys +
+ * softmax + attend_values. q, out: [n_seqs, n_q_heads, head_dim]. */
+int lc_decode_attn(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+                   const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags,
+                   void* out, int32_t out_dtype, void* stream);
+
+/* Same, but stop before normalisation and return the softmax partials of
+ * the whole local context per (seq, q head): m (log2 domain, max of
+ * scale*log2(e)*score), l (sum of 2^(s-m)), o [head_dim] (unnormalised, in
+ * the rotated basis). For one context split by sequence across devices. */
+int lc_decode_attn_partials(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+                            const void* q, int32_t q_dtype, int32_t n_q_heads, float scale,
+                            uint32_t flags, float* m, float* l, float* o, void* stream);
+
+/* Merge n_parts sets of partials [n_parts, n_rows] (m, l) and
+ * [n_parts, n_rows, head_dim] (o) into out [n_rows, head_dim], un-rotating
+ * with the cache's V rotation unless LC_OUT_ROTATED. */
+int lc_merge_partials(lc_cache* cache, int32_t n_parts, int32_t n_rows, const float* m,
+                      const float* l, const float* o, uint32_t flags, void* out, int32_t out_dtype,
+                      void* stream);
+
+/* Device id, stream and last-kernel count (kernels this library launched). */
+int lc_cache_info(const lc_cache* cache, int32_t* device, void** stream, uint64_t* kernel_launches);
+
+/* Per-kernel device time from CUDA events recorded on the launching stream
+ * around the split-K attention kernel and the quantize-append kernel.
+ * mode 1: start recording (clears earlier records); mode 0: stop and
+ * report; mode 2: report and keep recording. Reporting synchronises the
+ * recorded events. Any output pointer may be NULL. */
+int lc_cache_timing(lc_cache* cache, int32_t mode, double* decode_ms, uint64_t* decode_launches,
+                    double* append_ms, uint64_t* append_launches);
+
+/* ---- the raw ring (native_cache.rs:65-335) ------------------------------
+ * N parallel buffers of arbitrary row width moving in lockstep, with
+ * mlx-lm RotatingKVCache semantics: the update path of
+ * NativeRotatingKvCacheTurboQuant::update_and_fetch(_qjl) on pre-quantized
+ * tuples, device-resident. */
+typedef struct lc_ring lc_ring;
+
+/* n_bufs buffers, row_bytes[i] bytes per (head, token) row. */
+int lc_ring_create(int32_t n_heads, int64_t max_size, int64_t keep, int32_t n_bufs,
+                   const int64_t* row_bytes, int32_t device, lc_ring** out);
+
+/* ring_update (native_cache.rs:277-290): news[i] is [n_heads, n_tokens,
+ * row_bytes[i]] (host or device). prealloc mirrors
+ * LUMEN_NATIVE_KV_STEP_PREALLOC. */
+int lc_ring_update(lc_ring* ring, const void* const* news, int64_t n_tokens, int32_t prealloc,
+                   void* stream);
+
+/* ring_truncate (native_cache.rs:304-335). */
+int lc_ring_truncate_to(lc_ring* ring, int64_t target);
+
+int lc_ring_counters(const lc_ring* ring, int64_t* offset, int64_t* idx, int64_t* buf_len,
+                     int64_t* view_len);
+
+/* Copy buffer `buf` ([n_heads, n, row_bytes]) to host: which =
+ * LC_FETCH_VIEW (what the last update returned) or LC_FETCH_BACKING. Returns
+ * n via *n_out; LC_ERR_STATE when the ring holds no buffers yet. */
+int lc_ring_read(lc_ring* ring, int32_t buf, int32_t which, void* dst, int64_t dst_bytes,
+                 int64_t* n_out);
+
+/* NativeRotatingKvCacheTurboQuant::clear (native_cache.rs:1712-1721). */
+int lc_ring_clear(lc_ring* ring);
+
+/* deep_clone (native_cache.rs:1581-1610). */
+int lc_ring_deep_clone(const lc_ring* ring, lc_ring** out);
+
+void lc_ring_destroy(lc_ring* ring);
+
+/* Library version string. */
+const char* lc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUMEN_CUDA_H */

@@ -1,0 +1,262 @@
+// Quantize-on-append, strict mode: one fused kernel that rotates, normalises,
+// quantizes, packs and (optionally) computes the QJL stage-2 bits of every
+// appended K/V vector and writes them into the cache pages.
+//
+// Bit-identical to the reference CPU compressor
+// (crates/lumen-core/src/compressor.rs:61-107): every f32 operation is an
+// explicit round-to-nearest intrinsic (__fmul_rn/__fadd_rn/__fsub_rn/
+// __fdiv_rn/__fsqrt_rn, never contracted into an FMA) and every sum runs in
+// the reference's order:
+//   rotated[i]   = sum_j R[i][j] * x[j]            j ascending (rotation.rs:91-99)
+//   norm_sq      = sum_i rotated[i]^2              i ascending (compressor.rs:70)
+//   scale        = sqrt(norm_sq / d)                            (:71)
+//   code[i]      = #{k : !(rotated[i]*inv < t_k)}               (lloyd_max.rs:132-143)
+//   recon[i]     = sum_j R[j][i] * (c[code_j]*scale) j ascending (rotation.rs:102-113)
+//   rnorm        = sqrt(sum_i (x[i]-recon[i])^2)                (compressor.rs:87-93)
+//   qjl bit r    = (sum_j Phi[r][j] * res[j]) >= 0              (qjl.rs:57-74)
+// The f64 boundary compare is replaced by an f32 compare against
+// t_k = the smallest f32 >= boundary_k, which gives the same answer for every
+// f32 input (x < b <=> x < t_k; NaN falls through to the top code).
+//
+// Work split: a CTA of `dim` threads handles kNB vectors at a time; thread i
+// owns output coordinate i of all kNB vectors (kNB independent dependency
+// chains per thread), the per-vector sequential norms run one vector per
+// thread. The path is bound by FP32 issue (about 2*d^2 + m*d non-fused
+// multiply/add pairs per vector), not by HBM.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+
+namespace lc {
+
+namespace {
+
+constexpr int kNB = 8;  // vectors per CTA pass
+
+struct AppendDev {
+  CodecDev codec[2];
+  const void* src[2];
+  int32_t dtype, n_seqs, h_in, h_base;
+  int64_t n_tok;
+  const uint64_t* dst_page;
+  const int32_t* dst_row;
+  int32_t heads;
+  int64_t off[kMaxRoles];
+  int64_t row[kMaxRoles];
+  int32_t role_words[2], role_sigma[2], role_qjl[2], role_rnorm[2];
+};
+
+__device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) {
+  if (dtype == LC_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dtype == LC_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+__global__ void k_append_strict(AppendDev a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int side = blockIdx.y;
+  const CodecDev c = a.codec[side];
+  const int D = c.dim;
+  const int i = threadIdx.x;  // output coordinate
+  const int M = c.m;
+  const bool stage2 = a.role_qjl[side] >= 0;
+
+  float* xs = reinterpret_cast<float*>(smem);      // [kNB][D]
+  float* ys = xs + kNB * D;                        // [kNB][D] rotated, then dequantized*scale
+  float* rs = ys + kNB * D;                        // [kNB][D] residual
+  float* vscale = rs + kNB * D;                    // [kNB]
+  float* vinv = vscale + kNB;                      // [kNB]
+  float* vrn = vinv + kNB;                         // [kNB]
+  uint32_t* qbits = reinterpret_cast<uint32_t*>(vrn + kNB);  // [kNB][ceil(M/32)]
+  const int qw32 = (M + 31) / 32;
+  uint8_t* codes = reinterpret_cast<uint8_t*>(qbits + kNB * (qw32 > 0 ? qw32 : 1));  // [kNB][D]
+
+  const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
+  const void* src = a.src[side];
+  const int n1 = c.n_levels - 1;
+
+  for (int64_t v0 = (int64_t)blockIdx.x * kNB; v0 < n_vec; v0 += (int64_t)gridDim.x * kNB) {
+    const int nb = (int)(n_vec - v0 < kNB ? n_vec - v0 : kNB);
+    // ---- load the batch (input layout [n_seqs][h_in][n_tok][D]) ----
+    for (int v = 0; v < kNB; ++v) xs[v * D + i] = v < nb ? load_elem(src, a.dtype, (v0 + v) * D + i) : 0.0f;
+    __syncthreads();
+
+    // ---- rotated[i] = sum_j R[i][j] * x[j] (rotation.rs:91-99) ----
+    float acc[kNB];
+#pragma unroll
+    for (int v = 0; v < kNB; ++v) acc[v] = -0.0f;
+    for (int j = 0; j < D; ++j) {
+      const float r = __ldg(c.RT + (int64_t)j * D + i);
+#pragma unroll
+      for (int v = 0; v < kNB; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(r, xs[v * D + j]));
+    }
+#pragma unroll
+    for (int v = 0; v < kNB; ++v) ys[v * D + i] = acc[v];
+    __syncthreads();
+
+    // ---- scale = sqrt(norm_sq / d), one vector per thread (compressor.rs:70-71) ----
+    if (i < kNB) {
+      float s = -0.0f;
+      for (int k = 0; k < D; ++k) {
+        const float y = ys[i * D + k];
+        s = __fadd_rn(s, __fmul_rn(y, y));
+      }
+      const float sc = __fsqrt_rn(__fdiv_rn(s, (float)D));
+      vscale[i] = sc;
+      vinv[i] = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+
+    // ---- codes and dequantized*scale (compressor.rs:73-83) ----
+#pragma unroll
+    for (int v = 0; v < kNB; ++v) {
+      const float sc = vscale[v];
+      int code = 0;
+      if (!(sc < 1e-10f)) {
+        const float yn = __fmul_rn(ys[v * D + i], vinv[v]);
+        for (int k = 0; k < n1; ++k) code += !(yn < c.thr[k]);
+      }
+      codes[v * D + i] = (uint8_t)code;
+      ys[v * D + i] = __fmul_rn(c.cent[code], sc);
+    }
+    __syncthreads();
+
+    if (stage2) {
+      // ---- recon[i] = sum_j R[j][i] * deq[j] (rotation.rs:102-113), residual ----
+#pragma unroll
+      for (int v = 0; v < kNB; ++v) acc[v] = 0.0f;
+      for (int j = 0; j < D; ++j) {
+        const float r = __ldg(c.R + (int64_t)j * D + i);
+#pragma unroll
+        for (int v = 0; v < kNB; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(r, ys[v * D + j]));
+      }
+#pragma unroll
+      for (int v = 0; v < kNB; ++v) rs[v * D + i] = __fsub_rn(xs[v * D + i], acc[v]);
+      __syncthreads();
+      // ---- residual norm (compressor.rs:88-93) ----
+      if (i < kNB) {
+        float s = 0.0f;
+        for (int k = 0; k < D; ++k) {
+          const float r = rs[i * D + k];
+          s = __fadd_rn(s, __fmul_rn(r, r));
+        }
+        vrn[i] = __fsqrt_rn(s);
+      }
+      // ---- QJL sign bits (qjl.rs:57-74) ----
+      for (int rbase = 0; rbase < M; rbase += D) {
+        const int r = rbase + i;
+        for (int v = 0; v < kNB; ++v) {
+          bool bit = false;
+          if (r < M) {
+            float dot = -0.0f;
+            for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(__ldg(c.PT + (int64_t)j * M + r), rs[v * D + j]));
+            bit = dot >= 0.0f;
+          }
+          const unsigned bal = __ballot_sync(0xffffffffu, bit);
+          if ((i & 31) == 0 && r < M + 31) {
+            const int wi = r >> 5;
+            if (wi < qw32) qbits[v * qw32 + wi] = bal;
+          }
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---- pack and write (bitpack.rs:17-30) ----
+    const int cpw = 64 / c.bits;
+    const int W = c.words;
+    for (int u = i; u < nb * W; u += D) {
+      const int v = u / W, w = u % W;
+      uint64_t word = 0;
+      for (int k = 0; k < cpw; ++k) {
+        const int idx = w * cpw + k;
+        if (idx < D) word |= (uint64_t)codes[v * D + idx] << (k * c.bits);
+      }
+      const int64_t g = v0 + v;
+      const int64_t t = g % a.n_tok;
+      const int64_t sh = g / a.n_tok;
+      const int hl = (int)(sh % a.h_in);
+      const int64_t s = sh / a.h_in;
+      const int64_t slot = s * a.n_tok + t;
+      uint8_t* page = reinterpret_cast<uint8_t*>(a.dst_page[slot]);
+      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.dst_row[slot];
+      const int rw = a.role_words[side];
+      reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
+    }
+    for (int v = i; v < nb; v += D) {
+      const int64_t g = v0 + v;
+      const int64_t t = g % a.n_tok;
+      const int64_t sh = g / a.n_tok;
+      const int hl = (int)(sh % a.h_in);
+      const int64_t s = sh / a.h_in;
+      const int64_t slot = s * a.n_tok + t;
+      uint8_t* page = reinterpret_cast<uint8_t*>(a.dst_page[slot]);
+      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.dst_row[slot];
+      const int rsg = a.role_sigma[side];
+      *reinterpret_cast<float*>(page + a.off[rsg] + hr * a.row[rsg]) = vscale[v];
+      if (stage2) {
+        const int rq = a.role_qjl[side], rr = a.role_rnorm[side];
+        uint64_t* qdst = reinterpret_cast<uint64_t*>(page + a.off[rq] + hr * a.row[rq]);
+        for (int w = 0; w < c.qwords; ++w) {
+          const uint64_t lo = 2 * w < qw32 ? qbits[v * qw32 + 2 * w] : 0u;
+          const uint64_t hi = 2 * w + 1 < qw32 ? qbits[v * qw32 + 2 * w + 1] : 0u;
+          qdst[w] = lo | (hi << 32);
+        }
+        *reinterpret_cast<float*>(page + a.off[rr] + hr * a.row[rr]) = vrn[v];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+size_t append_smem_bytes(int d, int m) {
+  const int qw32 = (m + 31) / 32;
+  return (size_t)(3 * kNB * d + 3 * kNB) * sizeof(float) + (size_t)kNB * (qw32 > 0 ? qw32 : 1) * 4 +
+         (size_t)kNB * d + 16;
+}
+
+void launch_append(const AppendArgs& a, cudaStream_t s) {
+  const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
+  if (n_vec <= 0) return;
+  AppendDev d;
+  d.codec[0] = a.codec[0];
+  d.codec[1] = a.codec[1];
+  d.src[0] = a.src[0];
+  d.src[1] = a.src[1];
+  d.dtype = a.dtype;
+  d.n_seqs = a.n_seqs;
+  d.h_in = a.h_in;
+  d.h_base = a.h_base;
+  d.n_tok = a.n_tok;
+  d.dst_page = a.dst_page;
+  d.dst_row = a.dst_row;
+  d.heads = a.layout.heads;
+  for (int r = 0; r < kMaxRoles; ++r) {
+    d.off[r] = a.layout.off[r];
+    d.row[r] = a.layout.row[r];
+  }
+  for (int k = 0; k < 2; ++k) {
+    d.role_words[k] = a.role_words[k];
+    d.role_sigma[k] = a.role_sigma[k];
+    d.role_qjl[k] = a.role_qjl[k];
+    d.role_rnorm[k] = a.role_rnorm[k];
+  }
+  const int D = a.codec[0].dim;
+  const int M = a.codec[0].m > a.codec[1].m ? a.codec[0].m : a.codec[1].m;
+  const size_t smem = append_smem_bytes(D, M);
+  static bool attr_set = false;
+  if (!attr_set) {
+    LC_CUDA(cudaFuncSetAttribute(k_append_strict, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_set = true;
+  }
+  int64_t batches = (n_vec + kNB - 1) / kNB;
+  int64_t max_blocks = 148 * 8;
+  dim3 grid((unsigned)(batches < max_blocks ? batches : max_blocks), 2);
+  k_append_strict<<<grid, D, smem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
+}
+
+}  // namespace lc

@@ -1,0 +1,792 @@
+// lc_cache: the TurboQuant KV cache on one GPU.
+//
+// State per (sequence, layer) is one RingCore (the reference's
+// NativeRotatingKvCacheTurboQuant bookkeeping, native_cache.rs:1517-1862)
+// over pages of one shared pool. A page holds 256 tokens of every kv head
+// of a layer for each role:
+//   0 K code words  [H][256][words_K] u64     (bitpack.rs layout)
+//   1 V code words  [H][256][words_V] u64
+//   2 K sigma       [H][256] f32
+//   3 V sigma       [H][256] f32
+//   4 K QJL words   [H][256][ceil(m/64)] u64  (LC_STORE_K_QJL)
+//   5 K residual    [H][256] f32
+//   6 V QJL words, 7 V residual               (LC_STORE_V_QJL)
+// Full layers (the reference's append-only TurboQuant layers, keep = 0) use
+// an unbounded ring; sliding layers use (max_size, keep). Prefix reuse shares
+// pages between sequences and copies a page on its first write.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+
+#include "codec.h"
+#include "kernels.h"
+#include "ring.h"
+
+namespace lc {
+
+namespace {
+constexpr int64_t kFullMax = int64_t(1) << 50;  // "never wraps"
+constexpr int R_KW = 0, R_VW = 1, R_KS = 2, R_VS = 3, R_KQ = 4, R_KR = 5, R_VQ = 6, R_VR = 7;
+
+struct SeqLayer {
+  RingCore ring;
+  std::vector<int64_t> head_len;  // non-empty: per-head lengths (KVCache::store on a full layer)
+  bool dirty = true;              // device block-table row out of date
+};
+
+template <class T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  void ensure(size_t want, cudaStream_t s) {
+    if (want <= n) return;
+    if (p) {
+      LC_CUDA(cudaStreamSynchronize(s));
+      cudaFree(p);
+      p = nullptr;
+    }
+    const size_t grow = std::max(want, n + n / 2);
+    cudaError_t e = cudaMalloc(&p, grow * sizeof(T));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+      LC_THROW(LC_ERR_NOMEM, "scratch allocation failed");
+    }
+    n = grow;
+  }
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+}  // namespace
+
+}  // namespace lc
+
+using namespace lc;
+
+struct lc_cache {
+  lc_cache_config cfg{};
+  std::vector<int64_t> max_size, keep;
+  Codec kc, vc;
+  CodecOnDevice dk, dv;
+  PageLayout layout;
+  PagePool pool;
+  UploadArena arena;
+  RingOps ops;
+  cudaStream_t stream = nullptr;
+  uint64_t launches = 0;
+  std::vector<SeqLayer> st;  // [seq * n_layers + layer]
+  uint64_t* d_table = nullptr;  // [n_layers][max_seqs][max_pages_per_seq]
+  cudaEvent_t ev_copy = nullptr;
+  DevBuf<uint8_t> in_k, in_v, qbuf, outbuf, fetchbuf;
+  DevBuf<float> q_rot, part, hook_a, hook_b, hook_c;
+  DevBuf<__half> q_h;
+  // kernel timing (lc_cache_timing)
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> t_decode, t_append;
+
+  cudaEvent_t take_event() {
+    if (ev_used == ev_pool.size()) {
+      cudaEvent_t e;
+      LC_CUDA(cudaEventCreate(&e));
+      ev_pool.push_back(e);
+    }
+    return ev_pool[ev_used++];
+  }
+  // Records an event pair around f() on stream s when timing is on.
+  template <class F>
+  void timed(std::vector<std::pair<cudaEvent_t, cudaEvent_t>>& rec, cudaStream_t s, F&& f) {
+    if (!timing) {
+      f();
+      return;
+    }
+    cudaEvent_t a = take_event(), b = take_event();
+    LC_CUDA(cudaEventRecord(a, s));
+    f();
+    LC_CUDA(cudaEventRecord(b, s));
+    rec.emplace_back(a, b);
+  }
+
+  SeqLayer& at(int32_t seq, int32_t layer) { return st[(size_t)seq * cfg.n_layers + layer]; }
+  const SeqLayer& at(int32_t seq, int32_t layer) const { return st[(size_t)seq * cfg.n_layers + layer]; }
+  bool full(int32_t layer) const { return max_size[layer] >= kFullMax; }
+  void check(int32_t seq, int32_t layer) const {
+    LC_REQUIRE(seq >= 0 && seq < cfg.max_seqs, LC_ERR_INVALID, "sequence id out of range");
+    LC_REQUIRE(layer >= 0 && layer < cfg.n_layers, LC_ERR_INVALID, "layer out of range");
+  }
+  uint64_t* table_row(int32_t seq, int32_t layer) const {
+    return d_table + ((size_t)layer * cfg.max_seqs + seq) * cfg.max_pages_per_seq;
+  }
+  cudaStream_t pick(void* s) const { return s ? static_cast<cudaStream_t>(s) : stream; }
+
+  // Upload (seq, layer)'s page addresses if they changed.
+  void sync_table(int32_t seq, int32_t layer, cudaStream_t s) {
+    SeqLayer& sl = at(seq, layer);
+    if (!sl.dirty) return;
+    LC_REQUIRE((int64_t)sl.ring.pages.size() <= cfg.max_pages_per_seq, LC_ERR_NOMEM,
+               "sequence longer than max_pages_per_seq pages");
+    const std::vector<uint64_t> addrs = ops.page_addrs(sl.ring);
+    if (!addrs.empty()) {
+      void* src = arena.put(addrs.data(), addrs.size() * 8, s);
+      LC_CUDA(cudaMemcpyAsync(table_row(seq, layer), src, addrs.size() * 8, cudaMemcpyDeviceToDevice, s));
+    }
+    sl.dirty = false;
+  }
+
+  // Device pointer for a caller buffer: device memory is used in place, host
+  // memory is copied into `buf`.
+  const void* stage_in(const void* p, size_t bytes, DevBuf<uint8_t>& buf, cudaStream_t s, bool& host) {
+    host = !is_device_ptr(p);
+    if (!host) return p;
+    buf.ensure(bytes, s);
+    LC_CUDA(cudaMemcpyAsync(buf.p, p, bytes, cudaMemcpyHostToDevice, s));
+    return buf.p;
+  }
+
+  ~lc_cache() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+    if (d_table) cudaFree(d_table);
+    if (ev_copy) cudaEventDestroy(ev_copy);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+namespace {
+
+size_t dtype_size(int32_t dt) {
+  if (dt == LC_F32) return 4;
+  if (dt == LC_BF16 || dt == LC_F16) return 2;
+  LC_THROW(LC_ERR_INVALID, "unknown dtype");
+}
+
+// Build the quantize-append for rows already prepared in the rings.
+void run_append(lc_cache* c, int32_t n_seqs, int32_t h_in, int32_t h_base, int64_t n_tok,
+                const std::vector<uint64_t>& dst_page, const std::vector<int32_t>& dst_row, const void* k,
+                const void* v, int32_t dtype, cudaStream_t s) {
+  AppendArgs a;
+  a.codec[0] = c->dk.view();
+  a.codec[1] = c->dv.view();
+  a.src[0] = k;
+  a.src[1] = v;
+  a.dtype = dtype;
+  a.n_seqs = n_seqs;
+  a.h_in = h_in;
+  a.h_base = h_base;
+  a.n_tok = n_tok;
+  a.dst_page = c->arena.put_vec(dst_page, s);
+  a.dst_row = c->arena.put_vec(dst_row, s);
+  a.layout = c->layout;
+  a.role_words[0] = R_KW;
+  a.role_words[1] = R_VW;
+  a.role_sigma[0] = R_KS;
+  a.role_sigma[1] = R_VS;
+  if (c->cfg.store_flags & LC_STORE_K_QJL) {
+    a.role_qjl[0] = R_KQ;
+    a.role_rnorm[0] = R_KR;
+  }
+  if (c->cfg.store_flags & LC_STORE_V_QJL) {
+    a.role_qjl[1] = R_VQ;
+    a.role_rnorm[1] = R_VR;
+  }
+  c->timed(c->t_append, s, [&] { launch_append(a, s); });
+  ++c->launches;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lc_cache_create(const lc_cache_config* cfg, const lc_codec* kcodec, const lc_codec* vcodec, lc_cache** out) {
+  return abi_guard([&] {
+    LC_REQUIRE(cfg && kcodec && vcodec && out, LC_ERR_INVALID, "null argument");
+    *out = nullptr;
+    LC_REQUIRE(cfg->n_layers > 0 && cfg->n_kv_heads > 0 && cfg->max_seqs > 0 && cfg->max_pages > 0 &&
+                   cfg->max_pages_per_seq > 0,
+               LC_ERR_INVALID, "cache config sizes must be > 0");
+    LC_REQUIRE((uint64_t)cfg->head_dim == kcodec->c.dim && (uint64_t)cfg->head_dim == vcodec->c.dim, LC_ERR_INVALID,
+               "codec head_dim differs from config head_dim");
+    LC_REQUIRE(kcodec->c.bits >= 2 && kcodec->c.bits <= 8 && vcodec->c.bits >= 2 && vcodec->c.bits <= 8,
+               LC_ERR_BITS, "cache bits must be in [2, 8] (native_cache.rs:1546-1549)");
+    if (cfg->store_flags & LC_STORE_K_QJL) LC_REQUIRE(kcodec->c.m > 0, LC_ERR_INVALID, "K QJL needs qjl_m > 0");
+    if (cfg->store_flags & LC_STORE_V_QJL) LC_REQUIRE(vcodec->c.m > 0, LC_ERR_INVALID, "V QJL needs qjl_m > 0");
+    std::unique_ptr<lc_cache> c(new lc_cache);
+    c->cfg = *cfg;
+    c->cfg.layer_max_size = nullptr;
+    c->cfg.layer_keep = nullptr;
+    for (int32_t l = 0; l < cfg->n_layers; ++l) {
+      int64_t ms = cfg->layer_max_size ? cfg->layer_max_size[l] : 0;
+      int64_t kp = cfg->layer_keep ? cfg->layer_keep[l] : 0;
+      if (ms == 0) {
+        ms = kFullMax;
+        kp = 0;
+      }
+      LC_REQUIRE(ms > 0, LC_ERR_INVALID, "TurboQuant cache: max_size must be > 0");
+      LC_REQUIRE(kp >= 0 && kp < ms, LC_ERR_INVALID, "TurboQuant cache: keep must be < max_size");
+      c->max_size.push_back(ms);
+      c->keep.push_back(kp);
+    }
+    c->kc = kcodec->c;
+    c->vc = vcodec->c;
+    LC_CUDA(cudaSetDevice(cfg->device));
+    LC_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    LC_CUDA(cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming));
+    c->dk.upload(c->kc);
+    c->dv.upload(c->vc);
+    const int64_t H = cfg->n_kv_heads;
+    std::vector<int64_t> rows = {(int64_t)c->kc.words() * 8, (int64_t)c->vc.words() * 8, 4, 4};
+    if (cfg->store_flags & (LC_STORE_K_QJL | LC_STORE_V_QJL)) {
+      rows.push_back((cfg->store_flags & LC_STORE_K_QJL) ? (int64_t)c->kc.qwords() * 8 : 8);
+      rows.push_back(4);
+    }
+    if (cfg->store_flags & LC_STORE_V_QJL) {
+      rows.push_back((int64_t)c->vc.qwords() * 8);
+      rows.push_back(4);
+    }
+    c->layout = PageLayout::make((int32_t)H, rows);
+    c->pool.init(c->layout, cfg->max_pages, cfg->device, true);
+    c->arena.init(16 << 20);
+    c->ops.pool = &c->pool;
+    c->ops.arena = &c->arena;
+    c->ops.stream = c->stream;
+    c->ops.launches = &c->launches;
+    c->st.resize((size_t)cfg->max_seqs * cfg->n_layers);
+    for (int32_t s = 0; s < cfg->max_seqs; ++s)
+      for (int32_t l = 0; l < cfg->n_layers; ++l) {
+        c->at(s, l).ring.max_size = c->max_size[l];
+        c->at(s, l).ring.keep = c->keep[l];
+      }
+    const size_t tbytes = (size_t)cfg->n_layers * cfg->max_seqs * cfg->max_pages_per_seq * 8;
+    LC_CUDA(cudaMalloc(&c->d_table, tbytes));
+    LC_CUDA(cudaMemset(c->d_table, 0, tbytes));
+    *out = c.release();
+  });
+}
+
+void lc_cache_destroy(lc_cache* c) {
+  if (!c) return;
+  cudaSetDevice(c->cfg.device);
+  delete c;
+}
+
+int lc_cache_info(const lc_cache* c, int32_t* device, void** stream, uint64_t* kernel_launches) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    if (device) *device = c->cfg.device;
+    if (stream) *stream = c->stream;
+    if (kernel_launches) *kernel_launches = c->launches;
+  });
+}
+
+int lc_cache_timing(lc_cache* c, int32_t mode, double* decode_ms, uint64_t* decode_launches, double* append_ms,
+                    uint64_t* append_launches) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    LC_REQUIRE(mode >= 0 && mode <= 2, LC_ERR_INVALID, "timing mode must be 0, 1 or 2");
+    if (mode == 1) {
+      c->t_decode.clear();
+      c->t_append.clear();
+      c->ev_used = 0;
+      c->timing = true;
+      return;
+    }
+    auto sum = [](const std::vector<std::pair<cudaEvent_t, cudaEvent_t>>& v) {
+      double ms = 0;
+      for (const auto& p : v) {
+        LC_CUDA(cudaEventSynchronize(p.second));
+        float t = 0;
+        LC_CUDA(cudaEventElapsedTime(&t, p.first, p.second));
+        ms += t;
+      }
+      return ms;
+    };
+    if (decode_ms) *decode_ms = sum(c->t_decode);
+    if (decode_launches) *decode_launches = c->t_decode.size();
+    if (append_ms) *append_ms = sum(c->t_append);
+    if (append_launches) *append_launches = c->t_append.size();
+    if (mode == 0) c->timing = false;
+  });
+}
+
+int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+              const void* values, int32_t dtype, int64_t n_tokens, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && seq_ids && keys && values, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_seqs > 0 && n_tokens > 0, LC_ERR_INVALID, "n_seqs and n_tokens must be > 0");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->pick(stream);
+    c->ops.stream = s;
+    const size_t esz = dtype_size(dtype);
+    const int32_t H = c->cfg.n_kv_heads;
+    std::vector<uint64_t> dst_page((size_t)n_seqs * n_tokens);
+    std::vector<int32_t> dst_row((size_t)n_seqs * n_tokens);
+    for (int32_t b = 0; b < n_seqs; ++b) {
+      const int32_t seq = seq_ids[b];
+      c->check(seq, layer);
+      for (int32_t b2 = 0; b2 < b; ++b2) LC_REQUIRE(seq_ids[b2] != seq, LC_ERR_INVALID, "duplicate sequence id");
+      SeqLayer& sl = c->at(seq, layer);
+      if (!sl.head_len.empty()) {
+        for (int64_t hl : sl.head_len)
+          LC_REQUIRE(hl == sl.head_len[0], LC_ERR_STATE, "heads of this layer hold different lengths");
+        sl.head_len.clear();
+      }
+      const int64_t w = c->ops.prepare_update(sl.ring, n_tokens, c->cfg.step_prealloc != 0);
+      sl.dirty = true;
+      for (int64_t t = 0; t < n_tokens; ++t) {
+        const int64_t r = w + t;
+        dst_page[(size_t)b * n_tokens + t] = c->pool.addr(sl.ring.pages[r / kPageTokens]);
+        dst_row[(size_t)b * n_tokens + t] = (int32_t)(r % kPageTokens);
+      }
+    }
+    const size_t bytes = (size_t)n_seqs * H * n_tokens * c->cfg.head_dim * esz;
+    bool hk = false, hv = false;
+    const void* dk = c->stage_in(keys, bytes, c->in_k, s, hk);
+    const void* dv = c->stage_in(values, bytes, c->in_v, s, hv);
+    if (hk || hv) LC_CUDA(cudaEventRecord(c->ev_copy, s));
+    run_append(c, n_seqs, H, 0, n_tokens, dst_page, dst_row, dk, dv, dtype, s);
+    if (hk || hv) LC_CUDA(cudaEventSynchronize(c->ev_copy));
+    c->ops.stream = c->stream;
+  });
+}
+
+int lc_store(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float* keys, const float* values,
+             int64_t n_tokens) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && keys && values, LC_ERR_INVALID, "null argument");
+    c->check(seq, layer);
+    LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
+    LC_REQUIRE(c->full(layer), LC_ERR_STATE, "store() is for full layers; sliding layers use lc_append");
+    if (n_tokens <= 0) return;
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    c->ops.stream = s;
+    SeqLayer& sl = c->at(seq, layer);
+    if (sl.head_len.empty()) sl.head_len.assign(c->cfg.n_kv_heads, sl.ring.offset);
+    const int64_t start = sl.head_len[head];
+    const int64_t end = start + n_tokens;
+    const int64_t new_len = std::max(sl.ring.offset, end);
+    // Full layer kept as an exact-size buffer holding the longest head.
+    if (!sl.ring.has || new_len > sl.ring.buf_len) {
+      const int64_t need = (new_len + kPageTokens - 1) / kPageTokens;
+      while ((int64_t)sl.ring.pages.size() < need) sl.ring.pages.push_back(c->pool.alloc());
+      sl.ring.has = true;
+      sl.ring.buf_len = new_len;
+    }
+    c->ops.make_private(sl.ring, start, end);
+    sl.ring.offset = new_len;
+    sl.ring.idx = new_len;
+    sl.ring.view_len = new_len;
+    sl.head_len[head] = end;
+    sl.dirty = true;
+    std::vector<uint64_t> dst_page(n_tokens);
+    std::vector<int32_t> dst_row(n_tokens);
+    for (int64_t t = 0; t < n_tokens; ++t) {
+      const int64_t r = start + t;
+      dst_page[t] = c->pool.addr(sl.ring.pages[r / kPageTokens]);
+      dst_row[t] = (int32_t)(r % kPageTokens);
+    }
+    const size_t bytes = (size_t)n_tokens * c->cfg.head_dim * 4;
+    bool hk = false, hv = false;
+    const void* dk = c->stage_in(keys, bytes, c->in_k, s, hk);
+    const void* dv = c->stage_in(values, bytes, c->in_v, s, hv);
+    run_append(c, 1, 1, head, n_tokens, dst_page, dst_row, dk, dv, LC_F32, s);
+    LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int64_t lc_seq_len(const lc_cache* c, int32_t seq, int32_t layer, int32_t head) {
+  int64_t r = -1;
+  const int st = abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    c->check(seq, layer);
+    LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
+    const SeqLayer& sl = c->at(seq, layer);
+    r = sl.head_len.empty() ? sl.ring.view_len : sl.head_len[head];
+  });
+  return st == LC_OK ? r : (int64_t)st;
+}
+
+int lc_attend_keys(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float* query, float* scores,
+                   int64_t n_scores) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && query && scores, LC_ERR_INVALID, "null argument");
+    c->check(seq, layer);
+    LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    const SeqLayer& sl = c->at(seq, layer);
+    const int64_t n = sl.head_len.empty() ? sl.ring.view_len : sl.head_len[head];
+    LC_REQUIRE(n_scores >= n, LC_ERR_INVALID, "scores buffer too small");
+    const int D = c->cfg.head_dim;
+    c->hook_a.ensure(D, s);
+    c->hook_b.ensure(D, s);
+    c->hook_c.ensure(std::max<int64_t>(n, 1), s);
+    bool hq = false;
+    DevBuf<uint8_t> tmp;
+    const float* dq = static_cast<const float*>(c->stage_in(query, D * 4, c->qbuf, s, hq));
+    const uint64_t* pages = c->arena.put_vec(c->ops.page_addrs(sl.ring), s);
+    launch_attend_keys(dq, c->dk.view(), pages, c->layout, R_KW, R_KS, head, n, c->hook_b.p, c->hook_c.p, s);
+    c->launches += 2;
+    LC_CUDA(cudaMemcpyAsync(scores, c->hook_c.p, n * 4, cudaMemcpyDefault, s));
+    LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int lc_attend_values(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float* weights, int64_t n_weights,
+                     float* out) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && weights && out, LC_ERR_INVALID, "null argument");
+    c->check(seq, layer);
+    LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    const SeqLayer& sl = c->at(seq, layer);
+    const int64_t n = sl.head_len.empty() ? sl.ring.view_len : sl.head_len[head];
+    LC_REQUIRE(n_weights == n, LC_ERR_INVALID, "weights length differs from seq_len");
+    const int D = c->cfg.head_dim;
+    c->hook_a.ensure(D, s);
+    bool hw = false;
+    const float* dw = n > 0 ? static_cast<const float*>(c->stage_in(weights, n * 4, c->qbuf, s, hw)) : nullptr;
+    const uint64_t* pages = c->arena.put_vec(c->ops.page_addrs(sl.ring), s);
+    launch_attend_values(dw, c->dv.view(), pages, c->layout, R_VW, R_VS, head, n, c->hook_a.p, s);
+    ++c->launches;
+    LC_CUDA(cudaMemcpyAsync(out, c->hook_a.p, D * 4, cudaMemcpyDefault, s));
+    LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int lc_clear(lc_cache* c) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    LC_CUDA(cudaStreamSynchronize(c->stream));
+    for (auto& sl : c->st) {
+      c->ops.clear(sl.ring);
+      sl.head_len.clear();
+      sl.dirty = true;
+    }
+  });
+}
+
+int lc_release(lc_cache* c, int32_t seq) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    for (int32_t l = 0; l < c->cfg.n_layers; ++l) {
+      c->check(seq, l);
+      SeqLayer& sl = c->at(seq, l);
+      c->ops.clear(sl.ring);
+      sl.head_len.clear();
+      sl.dirty = true;
+    }
+  });
+}
+
+int lc_truncate(lc_cache* c, int32_t seq, int32_t layer, int64_t n_keep) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    c->check(seq, layer);
+    LC_REQUIRE(n_keep >= 0, LC_ERR_INVALID, "n_keep must be >= 0");
+    SeqLayer& sl = c->at(seq, layer);
+    if (!sl.head_len.empty()) {
+      int64_t mx = 0;
+      for (auto& hl : sl.head_len) {
+        hl = std::min(hl, n_keep);
+        mx = std::max(mx, hl);
+      }
+      sl.ring.offset = sl.ring.idx = sl.ring.view_len = mx;
+      sl.dirty = true;
+      return;
+    }
+    if (sl.ring.offset <= n_keep) return;
+    if (!c->ops.truncate_to(sl.ring, n_keep))
+      LC_THROW(LC_ERR_REFUSED, "truncate: post-rotation rollback not supported");
+    sl.dirty = true;
+  });
+}
+
+int lc_truncate_to(lc_cache* c, int32_t seq, int32_t layer, int64_t target) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    c->check(seq, layer);
+    SeqLayer& sl = c->at(seq, layer);
+    LC_REQUIRE(sl.head_len.empty(), LC_ERR_STATE, "truncate_to on a layer filled per head; use lc_truncate");
+    if (!c->ops.truncate_to(sl.ring, target)) {
+      if (target > sl.ring.offset)
+        LC_THROW(LC_ERR_REFUSED, "truncate_to: target " + std::to_string(target) + " > offset " +
+                                     std::to_string(sl.ring.offset));
+      LC_THROW(LC_ERR_REFUSED, "truncate_to: post-rotation rollback not supported (offset=" +
+                                   std::to_string(sl.ring.offset) + " > max_size=" +
+                                   std::to_string(sl.ring.max_size) + ")");
+    }
+    sl.dirty = true;
+  });
+}
+
+int lc_fork(lc_cache* c, int32_t src, int32_t dst, int64_t prefix_len) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    LC_REQUIRE(src != dst, LC_ERR_INVALID, "fork onto itself");
+    LC_REQUIRE(prefix_len >= 0, LC_ERR_INVALID, "prefix_len must be >= 0");
+    for (int32_t l = 0; l < c->cfg.n_layers; ++l) {
+      c->check(src, l);
+      c->check(dst, l);
+      const SeqLayer& s = c->at(src, l);
+      int64_t avail = s.ring.offset;
+      if (!s.head_len.empty()) avail = *std::min_element(s.head_len.begin(), s.head_len.end());
+      LC_REQUIRE(prefix_len <= avail && prefix_len <= (s.ring.has ? s.ring.buf_len : 0), LC_ERR_REFUSED,
+                 "fork: prefix longer than the source holds");
+      LC_REQUIRE(s.ring.offset <= s.ring.max_size, LC_ERR_REFUSED, "fork: source ring has rotated");
+    }
+    for (int32_t l = 0; l < c->cfg.n_layers; ++l) {
+      SeqLayer& d = c->at(dst, l);
+      c->ops.clear(d.ring);
+      d.head_len.clear();
+      d.ring = c->ops.share_prefix(c->at(src, l).ring, prefix_len);
+      d.ring.max_size = c->max_size[l];
+      d.ring.keep = c->keep[l];
+      d.dirty = true;
+    }
+  });
+}
+
+int lc_ring_state(const lc_cache* c, int32_t seq, int32_t layer, int64_t* offset, int64_t* idx, int64_t* buf_len,
+                  int64_t* view_len) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    c->check(seq, layer);
+    const SeqLayer& sl = c->at(seq, layer);
+    if (offset) *offset = sl.ring.offset;
+    if (idx) *idx = sl.ring.idx;
+    if (buf_len) *buf_len = sl.ring.has ? sl.ring.buf_len : 0;
+    if (view_len) *view_len = sl.ring.view_len;
+  });
+}
+
+int lc_fetch(lc_cache* c, int32_t seq, int32_t layer, int32_t which, lc_fetch_out* out, int64_t max_tokens,
+             int64_t* n_out) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && out, LC_ERR_INVALID, "null argument");
+    c->check(seq, layer);
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    const SeqLayer& sl = c->at(seq, layer);
+    const int64_t n = which == LC_FETCH_BACKING ? (sl.ring.has ? sl.ring.buf_len : 0) : sl.ring.view_len;
+    if (n_out) *n_out = n;
+    LC_REQUIRE(n <= max_tokens, LC_ERR_INVALID, "max_tokens smaller than the stored length");
+    if (n == 0) return;
+    const PageLayout& L = c->layout;
+    int64_t lin_off[kMaxRoles] = {};
+    size_t total = 0;
+    for (int k = 0; k < L.n_roles; ++k) {
+      lin_off[k] = (int64_t)total;
+      total += (size_t)L.heads * n * L.row[k];
+      total = (total + 255) & ~size_t(255);
+    }
+    c->fetchbuf.ensure(total, s);
+    c->ops.stream = s;
+    read_rows(c->ops, sl.ring, 0, n, c->fetchbuf.p, lin_off);
+    void* dsts[kMaxRoles] = {out->k_words, out->v_words, out->k_sigma, out->v_sigma, nullptr, nullptr, nullptr,
+                             nullptr};
+    if (c->cfg.store_flags & (LC_STORE_K_QJL | LC_STORE_V_QJL)) {
+      if (c->cfg.store_flags & LC_STORE_K_QJL) {
+        dsts[R_KQ] = out->k_qjl;
+        dsts[R_KR] = out->k_rnorm;
+      }
+      if (c->cfg.store_flags & LC_STORE_V_QJL) {
+        dsts[R_VQ] = out->v_qjl;
+        dsts[R_VR] = out->v_rnorm;
+      }
+    }
+    for (int k = 0; k < L.n_roles; ++k) {
+      if (!dsts[k]) continue;
+      LC_CUDA(cudaMemcpyAsync(dsts[k], c->fetchbuf.p + lin_off[k], (size_t)L.heads * n * L.row[k], cudaMemcpyDefault,
+                              s));
+    }
+    LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+static void decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
+                          int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s,
+                          int64_t* n_chunks_out) {
+  LC_REQUIRE(c && seq_ids && q, LC_ERR_INVALID, "null argument");
+  LC_REQUIRE(n_seqs > 0, LC_ERR_INVALID, "n_seqs must be > 0");
+  const int32_t hkv = c->cfg.n_kv_heads;
+  LC_REQUIRE(n_q_heads > 0 && n_q_heads % hkv == 0, LC_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads");
+  const int32_t D = c->cfg.head_dim;
+  const int G = n_q_heads / hkv;
+  LC_CUDA(cudaSetDevice(c->cfg.device));
+  std::vector<int64_t> info((size_t)n_seqs * 2);
+  int64_t max_len = 0;
+  for (int32_t b = 0; b < n_seqs; ++b) {
+    const int32_t seq = seq_ids[b];
+    c->check(seq, layer);
+    SeqLayer& sl = c->at(seq, layer);
+    int64_t n = sl.ring.view_len;
+    if (!sl.head_len.empty()) {
+      for (int64_t hl : sl.head_len)
+        LC_REQUIRE(hl == sl.head_len[0], LC_ERR_STATE, "heads of this layer hold different lengths");
+      n = sl.head_len[0];
+    }
+    c->sync_table(seq, layer, s);
+    info[2 * b] = n;
+    info[2 * b + 1] = (int64_t)layer * c->cfg.max_seqs + seq;
+    max_len = std::max(max_len, n);
+  }
+  const int64_t* dinfo = c->arena.put_vec(info, s);
+  const int64_t rows = (int64_t)n_seqs * n_q_heads;
+  bool hq = false;
+  const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
+  c->q_rot.ensure((size_t)rows * D, s);
+  c->q_h.ensure((size_t)rows * D, s);
+  launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0, scale * 1.4426950408889634f,
+                  c->q_rot.p, c->q_h.p, s);
+  ++c->launches;
+  const int ppc = 4;
+  const int64_t max_pages = (max_len + kPageTokens - 1) / kPageTokens;
+  const int64_t n_chunks = std::max<int64_t>(1, (max_pages + ppc - 1) / ppc);
+  c->part.ensure((size_t)rows * n_chunks * (D + 2), s);
+  DecodeArgs a;
+  a.table = c->d_table;
+  a.table_stride = c->cfg.max_pages_per_seq;
+  a.seqinfo = dinfo;
+  a.layout = c->layout;
+  a.role_kw = R_KW;
+  a.role_vw = R_VW;
+  a.role_ks = R_KS;
+  a.role_vs = R_VS;
+  a.n_seqs = n_seqs;
+  a.hkv = hkv;
+  a.hq = n_q_heads;
+  a.dim = D;
+  a.kbits = (int)c->kc.bits;
+  a.vbits = (int)c->vc.bits;
+  a.pages_per_chunk = ppc;
+  a.n_chunks = (int32_t)n_chunks;
+  a.q_rot = c->q_rot.p;
+  a.q_h = c->q_h.p;
+  a.kcent = c->dk.cent_d;
+  a.vcent = c->dv.cent_d;
+  a.part = c->part.p;
+  (void)G;
+  c->timed(c->t_decode, s, [&] { launch_decode_partials(a, s); });
+  ++c->launches;
+  if (hq) LC_CUDA(cudaEventRecord(c->ev_copy, s));
+  *n_chunks_out = n_chunks;
+}
+
+int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
+                   int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, void* out, int32_t out_dtype,
+                   void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(out, LC_ERR_INVALID, "null out");
+    cudaStream_t s = c ? c->pick(stream) : nullptr;
+    int64_t n_chunks = 0;
+    decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, &n_chunks);
+    const int32_t D = c->cfg.head_dim;
+    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
+    const bool host_out = !is_device_ptr(out);
+    void* dout = out;
+    if (host_out) {
+      c->outbuf.ensure(obytes, s);
+      dout = c->outbuf.p;
+    }
+    launch_merge(c->part.p, (int32_t)rows, (int32_t)n_chunks, D, n_chunks * (D + 2), D + 2,
+                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, s);
+    ++c->launches;
+    if (host_out) {
+      LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
+      LC_CUDA(cudaStreamSynchronize(s));
+    } else if (!is_device_ptr(q)) {
+      LC_CUDA(cudaEventSynchronize(c->ev_copy));
+    }
+  });
+}
+
+int lc_decode_attn_partials(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
+                            int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, float* m, float* l,
+                            float* o, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(m && l && o, LC_ERR_INVALID, "null output");
+    cudaStream_t s = c ? c->pick(stream) : nullptr;
+    int64_t n_chunks = 0;
+    decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, &n_chunks);
+    const int32_t D = c->cfg.head_dim;
+    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    const bool dev = is_device_ptr(m) && is_device_ptr(l) && is_device_ptr(o);
+    float *dm = m, *dl = l, *dov = o;
+    if (!dev) {
+      c->outbuf.ensure((size_t)rows * (D + 2) * 4, s);
+      dm = reinterpret_cast<float*>(c->outbuf.p);
+      dl = dm + rows;
+      dov = dl + rows;
+    }
+    launch_merge(c->part.p, (int32_t)rows, (int32_t)n_chunks, D, n_chunks * (D + 2), D + 2, nullptr, nullptr,
+                 LC_F32, dm, dl, dov, s);
+    ++c->launches;
+    if (!dev) {
+      LC_CUDA(cudaMemcpyAsync(m, dm, rows * 4, cudaMemcpyDefault, s));
+      LC_CUDA(cudaMemcpyAsync(l, dl, rows * 4, cudaMemcpyDefault, s));
+      LC_CUDA(cudaMemcpyAsync(o, dov, (size_t)rows * D * 4, cudaMemcpyDefault, s));
+      LC_CUDA(cudaStreamSynchronize(s));
+    } else if (!is_device_ptr(q)) {
+      LC_CUDA(cudaEventSynchronize(c->ev_copy));
+    }
+  });
+}
+
+int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float* m, const float* l, const float* o,
+                      uint32_t flags, void* out, int32_t out_dtype, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && m && l && o && out, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_parts > 0 && n_rows > 0, LC_ERR_INVALID, "n_parts and n_rows must be > 0");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->pick(stream);
+    const int32_t D = c->cfg.head_dim;
+    // pack into [rows][parts][D+2] (m, l, o) so the merge kernel reads one layout
+    std::vector<float> packed;
+    const bool dev = is_device_ptr(m) && is_device_ptr(l) && is_device_ptr(o);
+    std::vector<float> hm, hl, ho;
+    const float *pm = m, *pl = l, *po = o;
+    if (dev) {
+      hm.resize((size_t)n_parts * n_rows);
+      hl.resize(hm.size());
+      ho.resize((size_t)n_parts * n_rows * D);
+      LC_CUDA(cudaMemcpyAsync(hm.data(), m, hm.size() * 4, cudaMemcpyDeviceToHost, s));
+      LC_CUDA(cudaMemcpyAsync(hl.data(), l, hl.size() * 4, cudaMemcpyDeviceToHost, s));
+      LC_CUDA(cudaMemcpyAsync(ho.data(), o, ho.size() * 4, cudaMemcpyDeviceToHost, s));
+      LC_CUDA(cudaStreamSynchronize(s));
+      pm = hm.data();
+      pl = hl.data();
+      po = ho.data();
+    }
+    packed.resize((size_t)n_rows * n_parts * (D + 2));
+    for (int32_t r = 0; r < n_rows; ++r)
+      for (int32_t p = 0; p < n_parts; ++p) {
+        float* dst = &packed[((size_t)r * n_parts + p) * (D + 2)];
+        dst[0] = pm[(size_t)p * n_rows + r];
+        dst[1] = pl[(size_t)p * n_rows + r];
+        std::memcpy(dst + 2, po + ((size_t)p * n_rows + r) * D, D * 4);
+      }
+    c->part.ensure(packed.size(), s);
+    LC_CUDA(cudaMemcpyAsync(c->part.p, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice, s));
+    const size_t obytes = (size_t)n_rows * D * dtype_size(out_dtype);
+    const bool host_out = !is_device_ptr(out);
+    void* dout = out;
+    if (host_out) {
+      c->outbuf.ensure(obytes, s);
+      dout = c->outbuf.p;
+    }
+    launch_merge(c->part.p, n_rows, n_parts, D, (int64_t)n_parts * (D + 2), D + 2,
+                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, s);
+    ++c->launches;
+    if (host_out) LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
+    LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+}  // extern "C"

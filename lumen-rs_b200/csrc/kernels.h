@@ -1,0 +1,92 @@
+// Launchers for the sm_100a kernels (defined in the .cu files).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.h"
+
+namespace lc {
+
+// ---- row copies between paged and linear spaces (ring_kernels.cu) --------
+struct CopyRowsArgs {
+  RowSpace src, dst;
+  PageLayout layout;
+  const int64_t* src_rows = nullptr;  // device: source row of dst row i; null -> src_begin + i
+  int64_t src_begin = 0, dst_begin = 0, n = 0;
+  int32_t zero = 0;           // write zeros instead of copying
+  uint32_t role_mask = ~0u;   // roles to touch
+};
+void launch_copy_rows(const CopyRowsArgs& a, cudaStream_t s);
+
+// ---- codec tables on the device ------------------------------------------
+struct CodecDev {
+  int32_t dim = 0, bits = 0, n_levels = 0, m = 0, words = 0, qwords = 0;
+  const float* R = nullptr;     // [d][d] row-major (R[i][j])
+  const float* RT = nullptr;    // [d][d] RT[j][i] = R[i][j]
+  const float* PT = nullptr;    // [d][m] PT[j][r] = Phi[r][j]
+  const float* thr = nullptr;   // [n-1] smallest f32 >= boundary[k], k = 1..n-1
+  const float* cent = nullptr;  // [n] centroids as f32 (lloyd_max.rs:157-159)
+};
+
+// ---- quantize-append (append.cu) ------------------------------------------
+// Vectors are enumerated (seq s, head hl, token t) over src[side]
+// [n_seqs][h_in][n_tok][dim]; vector (s, hl, t) lands in page dst_page[s*n_tok+t],
+// row dst_row[s*n_tok+t], head h_base + hl.
+struct AppendArgs {
+  CodecDev codec[2];
+  const void* src[2] = {nullptr, nullptr};
+  int32_t dtype = LC_F32;
+  int32_t n_seqs = 0, h_in = 0, h_base = 0;
+  int64_t n_tok = 0;
+  const uint64_t* dst_page = nullptr;
+  const int32_t* dst_row = nullptr;
+  PageLayout layout;
+  int32_t role_words[2] = {-1, -1}, role_sigma[2] = {-1, -1};
+  int32_t role_qjl[2] = {-1, -1}, role_rnorm[2] = {-1, -1};
+};
+void launch_append(const AppendArgs& a, cudaStream_t s);
+// Dynamic shared memory the append kernel needs for head_dim d and qjl m.
+size_t append_smem_bytes(int d, int m);
+
+// ---- decode attention (decode.cu) ------------------------------------------
+struct DecodeArgs {
+  const uint64_t* table = nullptr;  // block table: row seq_ids[b] holds the page addresses of sequence b
+  int64_t table_stride = 0;         // u64 entries per table row
+  const int64_t* seqinfo = nullptr; // [n_seqs][2]: (tokens to attend, table row)
+  PageLayout layout;
+  int32_t role_kw = 0, role_vw = 1, role_ks = 2, role_vs = 3;
+  int32_t n_seqs = 0, hkv = 0, hq = 0, dim = 0;
+  int32_t kbits = 4, vbits = 4;
+  int32_t pages_per_chunk = 4;
+  int32_t n_chunks = 0;           // chunks per (seq, kv head)
+  const float* q_rot = nullptr;   // [n_seqs][hq][dim] f32, rotated and scaled by scale*log2(e)
+  const __half* q_h = nullptr;    // same in f16
+  const float* kcent = nullptr;   // [2^kbits]
+  const float* vcent = nullptr;   // [2^vbits]
+  float* part = nullptr;          // [n_seqs][hkv][n_chunks][G][dim + 2]  (m, l, o...)
+};
+
+// q_rot[s][h][:] = (R q[s][h]) * qscale (R applied unless q_is_rotated)
+void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* R,
+                     bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s);
+void launch_decode_partials(const DecodeArgs& a, cudaStream_t s);
+
+// ---- parity hooks of the KVCache trait (hooks.cu): bit-exact in the
+// reference's f32 order ----
+// scores[t] = (sum_j (Rq)_j * c[code_tj]) * sigma_t for t < n   (compressor.rs:165-184)
+void launch_attend_keys(const float* q, const CodecDev& kc, const uint64_t* pages, const PageLayout& L, int role_kw,
+                        int role_ks, int head, int64_t n, float* rq_scratch, float* scores, cudaStream_t s);
+// out[i] = sum_t sum_j R[j][i] * (c[code_tj] * (sigma_t * w_t)), |w_t| >= 1e-10   (simple.rs:76-99, 142-155)
+void launch_attend_values(const float* w, const CodecDev& vc, const uint64_t* pages, const PageLayout& L,
+                          int role_vw, int role_vs, int head, int64_t n, float* out, cudaStream_t s);
+// Combine chunk partials [rows][n_parts][dim+2] -> (m, l, o) per row, or the
+// normalised output out[rows][dim] (un-rotated with R^T unless R == null).
+void launch_merge(const float* part, int32_t n_rows, int32_t n_parts, int32_t dim, int64_t part_stride_row,
+                  int64_t part_stride_part, const float* R, void* out, int32_t out_dtype, float* m_out,
+                  float* l_out, float* o_out, cudaStream_t s);
+bool decode_fast_path(int dim, int kbits, int vbits, int G);
+
+}  // namespace lc
