@@ -230,7 +230,7 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     lc = importlib.import_module("lumen-rs_b200")
-    B, hq, hkv, D, ctx, L = CFG["batch"], CFG["hq"], CFG["hkv"], CFG["dim"], CFG["ctx"], CFG["layers"]
+    B, hq, hkv, D, ctx, L = CFG["batch"], CFG["hq"], CFG["hkv"], CFG["dim"], CFG["ctx"], args.layers
     steps, warm = args.steps, args.warmup
     total_new = steps + warm + (args.e2e_steps if rank == 0 else 0) + 1
     pages_per_seq = (ctx + total_new + 255) // 256 + 1
@@ -305,7 +305,6 @@ def run_ours(args):
     ms_step = elapsed_ms / steps
     tok_s = world * B * steps / (elapsed_ms / 1e3)
     # algorithmic bytes: every attended token's packed K/V words and sigmas, once per kv head
-    tokens_attended = B * steps * sum(range(ctx0 + 1, ctx0 + 1 + steps)) / steps  # per layer over the run
     kv_bytes_per_launch = B * hkv * BYTES_PER_TOKEN_HEAD * (ctx0 + 1 + ctx1) / 2.0
     dec_avg_ms = dec_ms / max(dec_n, 1)
     achieved = kv_bytes_per_launch / (dec_avg_ms / 1e3) / 1e9
@@ -332,7 +331,7 @@ def run_ours(args):
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
             e2e_step()
-        e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+        e2e_s = (time.perf_counter() - t0) / max(args.e2e_steps, 1)
         h2d = L * (B * hq * D * 2 + 2 * B * hkv * D * 2)
         d2h = L * B * hq * D * 2
         # ---- CPU baseline: oracle decode of one (seq, layer) sample ----
@@ -349,8 +348,8 @@ def run_ours(args):
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "config1 decode: batch 32/GPU, 32q/8kv, d128, ctx 8192 (+1 per step), "
-                                   "32 layers, 4-bit K/V packed; append + decode per layer",
+            "config": {"workload": f"config1 decode: batch 32/GPU, 32q/8kv, d128, ctx 8192 (+1 per step), "
+                                   f"{L} layers, 4-bit K/V packed; append + decode per layer",
                        "global_batch": world * B, "seq_len": ctx, "parallelism": f"request-shard x{world}",
                        "l2": "inputs larger than L2 (9.1 GB cache per GPU)",
                        "queries": "bf16 N(0, std 1/sqrt(128)), scale 1.0"},
@@ -382,6 +381,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers (32 = config 1; fewer for profiling)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -166,6 +166,20 @@ def _dtype_code(x) -> int:
     return {"torch.float32": LC_F32, "torch.bfloat16": LC_BF16, "torch.float16": LC_F16}[name]
 
 
+def _auto_stream(stream, *tensors):
+    """The stream to run on: the caller's, else torch's current stream when a
+    CUDA tensor is passed (so torch's allocator and our kernels stay ordered),
+    else the library's own stream (None)."""
+    if stream is not None:
+        return getattr(stream, "cuda_stream", stream)
+    for t in tensors:
+        if t is not None and getattr(t, "is_cuda", False):
+            import torch
+
+            return torch.cuda.current_stream(t.device).cuda_stream
+    return None
+
+
 def packed_words(n: int, bits: int) -> int:
     """bitpack.rs:11-14"""
     return int(lib().lc_packed_words(n, bits))
@@ -311,6 +325,7 @@ class CudaKvCache:
         """Quantize-append keys/values [n_seqs, n_kv_heads, n_tokens, head_dim] (un-rotated)."""
         ids = np.ascontiguousarray(seq_ids, np.int32)
         n_tok = keys.shape[2]
+        stream = _auto_stream(stream, keys, values)
         _check(lib().lc_append(self._h, layer, len(ids), _ptr(ids), _ptr(keys), _ptr(values), _dtype_code(keys),
                                n_tok, stream))
 
@@ -360,6 +375,7 @@ class CudaKvCache:
         if out is None:
             out = np.empty((len(ids), n_q_heads, self.head_dim), np.float32)
             out_dtype = LC_F32
+        stream = _auto_stream(stream, q, out)
         _check(lib().lc_decode_attn(self._h, layer, len(ids), _ptr(ids), _ptr(q), _dtype_code(q), n_q_heads,
                                     scale, flags, _ptr(out), out_dtype, stream))
         return out
@@ -372,6 +388,7 @@ class CudaKvCache:
             m = np.empty(rows, np.float32)
             l = np.empty(rows, np.float32)
             o = np.empty((rows, self.head_dim), np.float32)
+        stream = _auto_stream(stream, q, m)
         _check(lib().lc_decode_attn_partials(self._h, layer, len(ids), _ptr(ids), _ptr(q), _dtype_code(q), n_q_heads,
                                              scale, flags, _ptr(m), _ptr(l), _ptr(o), stream))
         return m, l, o
@@ -382,6 +399,7 @@ class CudaKvCache:
         if out is None:
             out = np.empty((n_rows, self.head_dim), np.float32)
             out_dtype = LC_F32
+        stream = _auto_stream(stream, m, out)
         _check(lib().lc_merge_partials(self._h, n_parts, n_rows, _ptr(m), _ptr(l), _ptr(o), flags, _ptr(out),
                                        out_dtype, stream))
         return out

@@ -53,31 +53,69 @@ __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) 
   return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// Shared memory: [tables (TAB: RT, then R and PT when stage 2 runs)]
+// [per group: xs, ys, rs [kNB][D], vscale, vinv, vrn [kNB], qbits, codes].
+struct GroupBufs {
+  float *xs, *ys, *rs, *vscale, *vinv, *vrn;
+  uint32_t* qbits;
+  uint8_t* codes;
+};
+
+__device__ __forceinline__ size_t group_bytes(int D, int qw32) {
+  return (size_t)(3 * kNB * D + 3 * kNB) * 4 + (size_t)kNB * (qw32 > 0 ? qw32 : 1) * 4 + (size_t)kNB * D;
+}
+
+template <bool TAB>
 __global__ void k_append_strict(AppendDev a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int side = blockIdx.y;
   const CodecDev c = a.codec[side];
   const int D = c.dim;
-  const int i = threadIdx.x;  // output coordinate
   const int M = c.m;
   const bool stage2 = a.role_qjl[side] >= 0;
-
-  float* xs = reinterpret_cast<float*>(smem);      // [kNB][D]
-  float* ys = xs + kNB * D;                        // [kNB][D] rotated, then dequantized*scale
-  float* rs = ys + kNB * D;                        // [kNB][D] residual
-  float* vscale = rs + kNB * D;                    // [kNB]
-  float* vinv = vscale + kNB;                      // [kNB]
-  float* vrn = vinv + kNB;                         // [kNB]
-  uint32_t* qbits = reinterpret_cast<uint32_t*>(vrn + kNB);  // [kNB][ceil(M/32)]
+  const int grp = threadIdx.x / D;  // vector group inside the CTA
+  const int i = threadIdx.x % D;    // output coordinate
   const int qw32 = (M + 31) / 32;
+
+  // ---- tables: rotation^T (always), rotation and Phi^T (stage 2) ----
+  const float* RT = c.RT;
+  const float* R = c.R;
+  const float* PT = c.PT;
+  size_t off = 0;
+  if (TAB) {
+    float* sRT = reinterpret_cast<float*>(smem);
+    for (int k = threadIdx.x; k < D * D; k += blockDim.x) sRT[k] = c.RT[k];
+    RT = sRT;
+    off = (size_t)D * D * 4;
+    if (stage2) {
+      float* sR = reinterpret_cast<float*>(smem + off);
+      for (int k = threadIdx.x; k < D * D; k += blockDim.x) sR[k] = c.R[k];
+      float* sPT = sR + D * D;
+      for (int k = threadIdx.x; k < D * M; k += blockDim.x) sPT[k] = c.PT[k];
+      R = sR;
+      PT = sPT;
+      off += (size_t)(D * D + D * M) * 4;
+    }
+  }
+  uint8_t* gb = smem + off + group_bytes(D, qw32) * grp;
+  float* xs = reinterpret_cast<float*>(gb);  // [kNB][D]
+  float* ys = xs + kNB * D;                  // rotated, then dequantized*scale
+  float* rs = ys + kNB * D;                  // residual
+  float* vscale = rs + kNB * D;
+  float* vinv = vscale + kNB;
+  float* vrn = vinv + kNB;
+  uint32_t* qbits = reinterpret_cast<uint32_t*>(vrn + kNB);                           // [kNB][qw32]
   uint8_t* codes = reinterpret_cast<uint8_t*>(qbits + kNB * (qw32 > 0 ? qw32 : 1));  // [kNB][D]
 
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const void* src = a.src[side];
   const int n1 = c.n_levels - 1;
+  const int groups = blockDim.x / D;
+  __syncthreads();
 
-  for (int64_t v0 = (int64_t)blockIdx.x * kNB; v0 < n_vec; v0 += (int64_t)gridDim.x * kNB) {
-    const int nb = (int)(n_vec - v0 < kNB ? n_vec - v0 : kNB);
+  for (int64_t base = (int64_t)blockIdx.x * groups * kNB; base < n_vec; base += (int64_t)gridDim.x * groups * kNB) {
+    const int64_t v0 = base + (int64_t)grp * kNB;
+    const int nb = v0 < n_vec ? (int)(n_vec - v0 < kNB ? n_vec - v0 : kNB) : 0;
     // ---- load the batch (input layout [n_seqs][h_in][n_tok][D]) ----
     for (int v = 0; v < kNB; ++v) xs[v * D + i] = v < nb ? load_elem(src, a.dtype, (v0 + v) * D + i) : 0.0f;
     __syncthreads();
@@ -86,8 +124,9 @@ __global__ void k_append_strict(AppendDev a) {
     float acc[kNB];
 #pragma unroll
     for (int v = 0; v < kNB; ++v) acc[v] = -0.0f;
+#pragma unroll 4
     for (int j = 0; j < D; ++j) {
-      const float r = __ldg(c.RT + (int64_t)j * D + i);
+      const float r = RT[j * D + i];
 #pragma unroll
       for (int v = 0; v < kNB; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(r, xs[v * D + j]));
     }
@@ -126,8 +165,9 @@ __global__ void k_append_strict(AppendDev a) {
       // ---- recon[i] = sum_j R[j][i] * deq[j] (rotation.rs:102-113), residual ----
 #pragma unroll
       for (int v = 0; v < kNB; ++v) acc[v] = 0.0f;
+#pragma unroll 4
       for (int j = 0; j < D; ++j) {
-        const float r = __ldg(c.R + (int64_t)j * D + i);
+        const float r = R[j * D + i];
 #pragma unroll
         for (int v = 0; v < kNB; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(r, ys[v * D + j]));
       }
@@ -150,11 +190,11 @@ __global__ void k_append_strict(AppendDev a) {
           bool bit = false;
           if (r < M) {
             float dot = -0.0f;
-            for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(__ldg(c.PT + (int64_t)j * M + r), rs[v * D + j]));
+            for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(PT[j * M + r], rs[v * D + j]));
             bit = dot >= 0.0f;
           }
           const unsigned bal = __ballot_sync(0xffffffffu, bit);
-          if ((i & 31) == 0 && r < M + 31) {
+          if ((i & 31) == 0) {
             const int wi = r >> 5;
             if (wi < qw32) qbits[v * qw32 + wi] = bal;
           }
@@ -214,8 +254,7 @@ __global__ void k_append_strict(AppendDev a) {
 
 size_t append_smem_bytes(int d, int m) {
   const int qw32 = (m + 31) / 32;
-  return (size_t)(3 * kNB * d + 3 * kNB) * sizeof(float) + (size_t)kNB * (qw32 > 0 ? qw32 : 1) * 4 +
-         (size_t)kNB * d + 16;
+  return (size_t)(3 * kNB * d + 3 * kNB) * 4 + (size_t)kNB * (qw32 > 0 ? qw32 : 1) * 4 + (size_t)kNB * d;
 }
 
 void launch_append(const AppendArgs& a, cudaStream_t s) {
@@ -238,24 +277,33 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
     d.off[r] = a.layout.off[r];
     d.row[r] = a.layout.row[r];
   }
+  bool stage2 = false;
   for (int k = 0; k < 2; ++k) {
     d.role_words[k] = a.role_words[k];
     d.role_sigma[k] = a.role_sigma[k];
     d.role_qjl[k] = a.role_qjl[k];
     d.role_rnorm[k] = a.role_rnorm[k];
+    stage2 = stage2 || a.role_qjl[k] >= 0;
   }
   const int D = a.codec[0].dim;
   const int M = a.codec[0].m > a.codec[1].m ? a.codec[0].m : a.codec[1].m;
-  const size_t smem = append_smem_bytes(D, M);
-  static bool attr_set = false;
-  if (!attr_set) {
-    LC_CUDA(cudaFuncSetAttribute(k_append_strict, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    attr_set = true;
+  const int groups = D <= 256 ? 2 : 1;
+  const size_t per_group = append_smem_bytes(D, M);
+  const size_t tables = (size_t)D * D * 4 + (stage2 ? (size_t)(D * D + D * M) * 4 : 0);
+  const size_t limit = 220 * 1024;
+  const bool tab = tables + groups * per_group <= limit;
+  const size_t smem = (tab ? tables : 0) + groups * per_group;
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_append_strict<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+    LC_CUDA(cudaFuncSetAttribute(k_append_strict<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+    attr = true;
   }
-  int64_t batches = (n_vec + kNB - 1) / kNB;
-  int64_t max_blocks = 148 * 8;
+  const int64_t batches = (n_vec + (int64_t)groups * kNB - 1) / ((int64_t)groups * kNB);
+  const int64_t max_blocks = (int64_t)num_sms() * (tab ? 1 : 4);
   dim3 grid((unsigned)(batches < max_blocks ? batches : max_blocks), 2);
-  k_append_strict<<<grid, D, smem, s>>>(d);
+  if (tab) k_append_strict<true><<<grid, D * groups, smem, s>>>(d);
+  else k_append_strict<false><<<grid, D * groups, smem, s>>>(d);
   LC_CUDA(cudaGetLastError());
 }
 

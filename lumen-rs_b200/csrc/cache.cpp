@@ -323,18 +323,32 @@ int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids
     const int32_t H = c->cfg.n_kv_heads;
     std::vector<uint64_t> dst_page((size_t)n_seqs * n_tokens);
     std::vector<int32_t> dst_row((size_t)n_seqs * n_tokens);
+    // Validate everything and bound the pages this call may take before any
+    // ring moves, so a refused call leaves the cache unchanged.
+    int64_t need = 0;
     for (int32_t b = 0; b < n_seqs; ++b) {
       const int32_t seq = seq_ids[b];
       c->check(seq, layer);
       for (int32_t b2 = 0; b2 < b; ++b2) LC_REQUIRE(seq_ids[b2] != seq, LC_ERR_INVALID, "duplicate sequence id");
-      SeqLayer& sl = c->at(seq, layer);
-      if (!sl.head_len.empty()) {
+      const SeqLayer& sl = c->at(seq, layer);
+      if (!sl.head_len.empty())
         for (int64_t hl : sl.head_len)
           LC_REQUIRE(hl == sl.head_len[0], LC_ERR_STATE, "heads of this layer hold different lengths");
-        sl.head_len.clear();
-      }
+      need += c->ops.new_pages_bound(sl.ring, n_tokens, c->cfg.step_prealloc != 0);
+      const int64_t held = sl.ring.has ? std::max(sl.ring.buf_len, sl.ring.offset) : 0;
+      const int64_t rows = std::min(held + std::max<int64_t>(n_tokens, kPageTokens), sl.ring.max_size - 1 + n_tokens);
+      LC_REQUIRE((rows + kPageTokens - 1) / kPageTokens <= c->cfg.max_pages_per_seq, LC_ERR_NOMEM,
+                 "append would exceed max_pages_per_seq pages for a sequence");
+    }
+    LC_REQUIRE(need <= c->pool.free_pages(), LC_ERR_NOMEM,
+               "page pool too small for this append (" + std::to_string(c->pool.free_pages()) + " pages free)");
+    for (int32_t b = 0; b < n_seqs; ++b) {
+      const int32_t seq = seq_ids[b];
+      SeqLayer& sl = c->at(seq, layer);
+      sl.head_len.clear();
+      const std::vector<int32_t> before = sl.ring.pages;
       const int64_t w = c->ops.prepare_update(sl.ring, n_tokens, c->cfg.step_prealloc != 0);
-      sl.dirty = true;
+      if (sl.ring.pages != before) sl.dirty = true;
       for (int64_t t = 0; t < n_tokens; ++t) {
         const int64_t r = w + t;
         dst_page[(size_t)b * n_tokens + t] = c->pool.addr(sl.ring.pages[r / kPageTokens]);
@@ -438,7 +452,7 @@ int lc_attend_keys(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const 
 int lc_attend_values(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float* weights, int64_t n_weights,
                      float* out) {
   return abi_guard([&] {
-    LC_REQUIRE(c && weights && out, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(c && out && (weights || n_weights == 0), LC_ERR_INVALID, "null argument");
     c->check(seq, layer);
     LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
     LC_CUDA(cudaSetDevice(c->cfg.device));
@@ -609,18 +623,20 @@ int lc_fetch(lc_cache* c, int32_t seq, int32_t layer, int32_t which, lc_fetch_ou
   });
 }
 
-static void decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
-                          int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s,
-                          int64_t* n_chunks_out) {
+struct DecodeRun {
+  int32_t rows = 0, G = 1, max_slots = 1;
+  const int32_t* cnt = nullptr;
+};
+
+static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
+                               int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s) {
   LC_REQUIRE(c && seq_ids && q, LC_ERR_INVALID, "null argument");
   LC_REQUIRE(n_seqs > 0, LC_ERR_INVALID, "n_seqs must be > 0");
   const int32_t hkv = c->cfg.n_kv_heads;
   LC_REQUIRE(n_q_heads > 0 && n_q_heads % hkv == 0, LC_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads");
   const int32_t D = c->cfg.head_dim;
-  const int G = n_q_heads / hkv;
   LC_CUDA(cudaSetDevice(c->cfg.device));
-  std::vector<int64_t> info((size_t)n_seqs * 2);
-  int64_t max_len = 0;
+  std::vector<int64_t> info((size_t)n_seqs * 2), lens(n_seqs);
   for (int32_t b = 0; b < n_seqs; ++b) {
     const int32_t seq = seq_ids[b];
     c->check(seq, layer);
@@ -634,9 +650,12 @@ static void decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int3
     c->sync_table(seq, layer, s);
     info[2 * b] = n;
     info[2 * b + 1] = (int64_t)layer * c->cfg.max_seqs + seq;
-    max_len = std::max(max_len, n);
+    lens[b] = n;
   }
+  const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits);
   const int64_t* dinfo = c->arena.put_vec(info, s);
+  const int64_t* dseg = plan.flat ? c->arena.put_vec(plan.seg, s) : nullptr;
+  const int32_t* dcnt = c->arena.put_vec(plan.cnt, s);
   const int64_t rows = (int64_t)n_seqs * n_q_heads;
   bool hq = false;
   const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
@@ -645,14 +664,12 @@ static void decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int3
   launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0, scale * 1.4426950408889634f,
                   c->q_rot.p, c->q_h.p, s);
   ++c->launches;
-  const int ppc = 4;
-  const int64_t max_pages = (max_len + kPageTokens - 1) / kPageTokens;
-  const int64_t n_chunks = std::max<int64_t>(1, (max_pages + ppc - 1) / ppc);
-  c->part.ensure((size_t)rows * n_chunks * (D + 2), s);
+  c->part.ensure((size_t)rows * plan.max_slots * (D + 2), s);
   DecodeArgs a;
   a.table = c->d_table;
   a.table_stride = c->cfg.max_pages_per_seq;
   a.seqinfo = dinfo;
+  a.seg = dseg;
   a.layout = c->layout;
   a.role_kw = R_KW;
   a.role_vw = R_VW;
@@ -664,18 +681,20 @@ static void decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int3
   a.dim = D;
   a.kbits = (int)c->kc.bits;
   a.vbits = (int)c->vc.bits;
-  a.pages_per_chunk = ppc;
-  a.n_chunks = (int32_t)n_chunks;
   a.q_rot = c->q_rot.p;
   a.q_h = c->q_h.p;
   a.kcent = c->dk.cent_d;
   a.vcent = c->dv.cent_d;
   a.part = c->part.p;
-  (void)G;
-  c->timed(c->t_decode, s, [&] { launch_decode_partials(a, s); });
+  c->timed(c->t_decode, s, [&] { launch_decode_partials(a, plan, s); });
   ++c->launches;
   if (hq) LC_CUDA(cudaEventRecord(c->ev_copy, s));
-  *n_chunks_out = n_chunks;
+  DecodeRun r;
+  r.rows = (int32_t)rows;
+  r.G = n_q_heads / hkv;
+  r.max_slots = plan.max_slots;
+  r.cnt = dcnt;
+  return r;
 }
 
 int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
@@ -684,10 +703,9 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
   return abi_guard([&] {
     LC_REQUIRE(out, LC_ERR_INVALID, "null out");
     cudaStream_t s = c ? c->pick(stream) : nullptr;
-    int64_t n_chunks = 0;
-    decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, &n_chunks);
+    const DecodeRun run = decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s);
     const int32_t D = c->cfg.head_dim;
-    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    const int64_t rows = run.rows;
     const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
     const bool host_out = !is_device_ptr(out);
     void* dout = out;
@@ -695,7 +713,7 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    launch_merge(c->part.p, (int32_t)rows, (int32_t)n_chunks, D, n_chunks * (D + 2), D + 2,
+    launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
                  (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, s);
     ++c->launches;
     if (host_out) {
@@ -713,10 +731,9 @@ int lc_decode_attn_partials(lc_cache* c, int32_t layer, int32_t n_seqs, const in
   return abi_guard([&] {
     LC_REQUIRE(m && l && o, LC_ERR_INVALID, "null output");
     cudaStream_t s = c ? c->pick(stream) : nullptr;
-    int64_t n_chunks = 0;
-    decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, &n_chunks);
+    const DecodeRun run = decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s);
     const int32_t D = c->cfg.head_dim;
-    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    const int64_t rows = run.rows;
     const bool dev = is_device_ptr(m) && is_device_ptr(l) && is_device_ptr(o);
     float *dm = m, *dl = l, *dov = o;
     if (!dev) {
@@ -725,8 +742,8 @@ int lc_decode_attn_partials(lc_cache* c, int32_t layer, int32_t n_seqs, const in
       dl = dm + rows;
       dov = dl + rows;
     }
-    launch_merge(c->part.p, (int32_t)rows, (int32_t)n_chunks, D, n_chunks * (D + 2), D + 2, nullptr, nullptr,
-                 LC_F32, dm, dl, dov, s);
+    launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D, nullptr, nullptr, LC_F32, dm, dl, dov,
+                 s);
     ++c->launches;
     if (!dev) {
       LC_CUDA(cudaMemcpyAsync(m, dm, rows * 4, cudaMemcpyDefault, s));
@@ -781,8 +798,8 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    launch_merge(c->part.p, n_rows, n_parts, D, (int64_t)n_parts * (D + 2), D + 2,
-                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, s);
+    launch_merge(c->part.p, nullptr, 1, n_parts, n_rows, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout,
+                 out_dtype, nullptr, nullptr, nullptr, s);
     ++c->launches;
     if (host_out) LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
     LC_CUDA(cudaStreamSynchronize(s));

@@ -8,19 +8,27 @@
 // accumulated in the rotated basis and un-rotated once per query head.
 //
 // Kernels
-//  k_rotate_q      q' = (R q) * scale * log2(e), f32 + f16 copies
-//  k_decode_mma    4-bit K/V, d = 128: the GQA tile on the tensor cores.
-//                  Codes are dequantized straight into mma.sync fragments
-//                  (a 256-entry byte -> half2 centroid-pair table in shared
-//                  memory, one copy per lane so every lookup is
-//                  bank-conflict-free); S^T = K_dq Q^T and O^T = V_dq^T P^T
-//                  run as m16n8k16 f16 MMAs with f32 accumulation.
-//  k_decode_generic any bit width / head_dim: CUDA-core fallback.
-//  k_merge         combines the split-K partials, normalises, un-rotates.
-// Streaming reads of the compressed pages are the roofline (HBM): per
-// (token, kv head) 8*words_K + 8*words_V + 8 bytes.
-#include <cuda_fp16.h>
+//  k_rotate_q       q' = (R q) * scale * log2(e), f32 + f16 copies.
+//  k_decode_flat    4-bit K/V, d = 128 (the hot path). Persistent: one CTA of
+//                   16 warps per SM. The (sequence, kv head, 16-token tile)
+//                   space is cut into equal contiguous ranges, one per warp,
+//                   so ragged batches stay balanced; a warp writes one softmax
+//                   partial per (sequence, kv head) segment it touches. Each
+//                   warp streams its tiles through a 3-stage cp.async ring in
+//                   shared memory (coalesced 16-byte copies of the packed K/V
+//                   words and sigmas straight from the pages). Codes are
+//                   dequantized into mma.sync fragments through a 256-entry
+//                   byte -> half2 centroid-pair table kept once per lane
+//                   (bank-conflict-free lookups); S^T = K_dq Q^T and
+//                   O^T = V_dq^T P^T run as m16n8k16 f16 MMAs with f32
+//                   accumulation, the GQA query heads of a kv head forming the
+//                   MMA's N dimension.
+//  k_decode_generic any bit width / head_dim: CUDA-core fallback, chunked.
+//  k_merge          combines the partials, normalises, un-rotates (R^T).
+// Roofline: HBM. Algorithmic bytes per (token, kv head) = 8*words_K +
+// 8*words_V + 8 (136 B for 4-bit d=128), read once.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <cfloat>
 
@@ -30,9 +38,8 @@ namespace lc {
 
 namespace {
 
-constexpr float kLog2e = 1.4426950408889634f;
-// Lazy rescale threshold (log2 units): the running max is only moved when a
-// new score exceeds it by more than this, bounding p by 2^kTau.
+// Lazy rescale threshold (log2 units): the running max only moves when a new
+// score exceeds it by more than this, which bounds p by 2^kTau.
 constexpr float kTau = 8.0f;
 
 __device__ __forceinline__ float load_any(const void* p, int dtype, int64_t i) {
@@ -86,7 +93,10 @@ __global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const fl
 struct DecodeDev {
   const uint64_t* table;
   int64_t table_stride;
-  const int64_t* seqinfo;
+  const int64_t* seqinfo;  // [n_seqs][2] (tokens, table row)
+  const int64_t* seg;      // flat: [n_seqs + 1] first tile of sequence b (all kv heads)
+  int64_t per_warp, total_tiles;
+  int32_t max_slots;
   int64_t off_kw, off_vw, off_ks, off_vs;
   int32_t row_kw, row_vw;
   int32_t n_seqs, hkv, hq, dim, kbits, vbits, pages_per_chunk, n_chunks, G;
@@ -99,10 +109,14 @@ struct DecodeDev {
 
 // ---------------------------------------------------------------------------
 // Fast path: 4-bit K and V, head_dim 128, up to 8 query heads per kv head.
-// CTA = 4 warps; a warp streams one page (256 tokens) in tiles of 16 tokens.
 // ---------------------------------------------------------------------------
-constexpr int kMmaWarps = 4;
+constexpr int kFlatWarps = 16;
+constexpr int kStages = 3;
 constexpr int kLutBytes = 256 * 64 * 4;  // [byte][64 slots]: K table slots 0..31, V table 32..63
+constexpr int kVStride = 96;             // V rows padded to 96 B: conflict-free 8-byte reads
+constexpr int kStK = 0, kStV = 1024, kStKs = kStV + 16 * kVStride, kStVs = kStKs + 64;
+constexpr int kStageBytes = kStVs + 64;  // 2688
+constexpr int kFlatSmem = kLutBytes + kFlatWarps * kStages * kStageBytes;
 
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
@@ -114,19 +128,79 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
 
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// Table lookup: byte k of x selects a half2 centroid pair; the lane's own
-// copy (slot lane) keeps the 32 lookups of a warp in 32 distinct banks.
+// Byte k of x selects a half2 centroid pair; the lane's own copy (slot lane)
+// keeps the 32 lookups of a warp in 32 distinct banks.
 __device__ __forceinline__ uint32_t lut_get(const uint8_t* lut, uint32_t x, uint32_t laneword, uint32_t sel,
                                             int slot_off) {
   const uint32_t off = __byte_perm(x, laneword, sel);
   return *reinterpret_cast<const uint32_t*>(lut + slot_off + off);
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_stages() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kStages - 1) : "memory");
+}
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+struct Cursor {
+  int b, kvh;
+  int64_t tile;
+};
+
+__device__ __forceinline__ int64_t seq_tiles(const DecodeDev& a, int b) { return (a.seqinfo[2 * b] + 15) >> 4; }
+
+__device__ __forceinline__ Cursor locate(const DecodeDev& a, int64_t x) {
+  int lo = 0, hi = a.n_seqs - 1;  // last b with seg[b] <= x and tiles
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a.seg[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  while (seq_tiles(a, lo) == 0) ++lo;  // x < total, so a later sequence holds it
+  const int64_t nt = seq_tiles(a, lo);
+  const int64_t off = x - a.seg[lo];
+  Cursor c;
+  c.b = lo;
+  c.kvh = (int)(off / nt);
+  c.tile = off % nt;
+  return c;
+}
+
+__device__ __forceinline__ void advance(const DecodeDev& a, Cursor& c) {
+  if (++c.tile >= seq_tiles(a, c.b)) {
+    c.tile = 0;
+    if (++c.kvh == a.hkv) {
+      c.kvh = 0;
+      do {
+        ++c.b;
+      } while (c.b < a.n_seqs && seq_tiles(a, c.b) == 0);
+    }
+  }
+}
+
+// Issue the 16-byte copies of one tile (K words, V words, sigma_K, sigma_V)
+// into a stage; every lane copies its share.
+__device__ __forceinline__ void issue_tile(const DecodeDev& a, const Cursor& c, uint32_t st, int lane) {
+  const uint64_t* trow = a.table + a.seqinfo[2 * c.b + 1] * a.table_stride;
+  const uint8_t* page = reinterpret_cast<const uint8_t*>(__ldg(trow + (c.tile >> 4)));
+  const int64_t hr = (int64_t)c.kvh * kPageTokens + (c.tile & 15) * 16;
+  const uint8_t* k = page + a.off_kw + hr * 64;
+  const uint8_t* v = page + a.off_vw + hr * 64;
+  cp_async16(st + kStK + lane * 16, k + lane * 16);
+  cp_async16(st + kStK + (lane + 32) * 16, k + (lane + 32) * 16);
+  cp_async16(st + kStV + (lane >> 2) * kVStride + (lane & 3) * 16, v + lane * 16);
+  cp_async16(st + kStV + ((lane + 32) >> 2) * kVStride + (lane & 3) * 16, v + (lane + 32) * 16);
+  if (lane < 4) cp_async16(st + kStKs + lane * 16, page + a.off_ks + hr * 4 + lane * 16);
+  else if (lane < 8) cp_async16(st + kStVs + (lane - 4) * 16, page + a.off_vs + hr * 4 + (lane - 4) * 16);
+}
+
 template <int G>
-__global__ void __launch_bounds__(kMmaWarps * 32) k_decode_mma(DecodeDev a) {
-  extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a) {
+  extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* lut = smem;
-  float* wpart = reinterpret_cast<float*>(smem + kLutBytes);  // [kMmaWarps][G][130]
   constexpr int D = 128;
   constexpr int PS = D + 2;
 
@@ -140,169 +214,47 @@ __global__ void __launch_bounds__(kMmaWarps * 32) k_decode_mma(DecodeDev a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t laneword = (uint32_t)lane << 2;
-  const int64_t total = (int64_t)a.n_seqs * a.hkv * a.n_chunks;
+  const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
+  const int64_t begin = w * a.per_warp;
+  const int64_t end = min(begin + a.per_warp, a.total_tiles);
+  if (begin >= end) return;
+  uint8_t* stages = smem + kLutBytes + warp * kStages * kStageBytes;
+  const uint32_t st0 = (uint32_t)__cvta_generic_to_shared(stages);
 
-  for (int64_t item = blockIdx.x; item < total; item += gridDim.x) {
-    const int chunk = (int)(item % a.n_chunks);
-    const int64_t rest = item / a.n_chunks;
-    const int kvh = (int)(rest % a.hkv);
-    const int s = (int)(rest / a.hkv);
-    const int64_t n_valid = a.seqinfo[2 * s];
-    const uint64_t* trow = a.table + a.seqinfo[2 * s + 1] * a.table_stride;
-    const int64_t page_idx = (int64_t)chunk * kMmaWarps + warp;
-    const int64_t tok0 = page_idx * kPageTokens;
-
-    // B fragments of Q^T: k-step st covers dims 32t + 4st + {0,1} and {2,3}.
-    uint32_t qb[8][2];
-    {
-      const __half* qrow = a.q_h + ((int64_t)s * a.hq + (int64_t)kvh * G + (g < G ? g : 0)) * D;
+  // ---- prologue: fill the ring ----
+  Cursor pc = locate(a, begin);
+  Cursor cc = pc;
 #pragma unroll
-      for (int st = 0; st < 8; ++st) {
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(qrow + 32 * t + 4 * st);
-        qb[st][0] = g < G ? p[0] : 0u;
-        qb[st][1] = g < G ? p[1] : 0u;
-      }
+  for (int s = 0; s < kStages; ++s) {
+    if (begin + s < end) {
+      issue_tile(a, pc, st0 + s * kStageBytes, lane);
+      advance(a, pc);
     }
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float oacc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+    cp_commit();
+  }
 
-    if (tok0 < n_valid) {
-      const uint8_t* page = reinterpret_cast<const uint8_t*>(trow[page_idx]);
-      const uint8_t* kb = page + a.off_kw + (int64_t)kvh * kPageTokens * 64;
-      const uint8_t* vb = page + a.off_vw + (int64_t)kvh * kPageTokens * 64;
-      const float* ksg = reinterpret_cast<const float*>(page + a.off_ks) + (int64_t)kvh * kPageTokens;
-      const float* vsg = reinterpret_cast<const float*>(page + a.off_vs) + (int64_t)kvh * kPageTokens;
-      const int64_t rem = n_valid - tok0;
-      const int ntiles = rem >= kPageTokens ? 16 : (int)((rem + 15) / 16);
+  int cur_b = -1, cur_kvh = -1;
+  int64_t n_valid = 0;
+  uint32_t qb[8][2];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float oacc[8][4];
+  int64_t slot_base = 0;
 
-      uint4 nk0, nk1;
-      uint2 nv[4];
-      float nks0, nks1, nvs0, nvs1;
-      auto load_tile = [&](int tile) {
-        const int r = tile * 16;
-        nk0 = *reinterpret_cast<const uint4*>(kb + (r + g) * 64 + 16 * t);
-        nk1 = *reinterpret_cast<const uint4*>(kb + (r + g + 8) * 64 + 16 * t);
-        nv[0] = *reinterpret_cast<const uint2*>(vb + (r + t) * 64 + 8 * g);
-        nv[1] = *reinterpret_cast<const uint2*>(vb + (r + t + 8) * 64 + 8 * g);
-        nv[2] = *reinterpret_cast<const uint2*>(vb + (r + t + 4) * 64 + 8 * g);
-        nv[3] = *reinterpret_cast<const uint2*>(vb + (r + t + 12) * 64 + 8 * g);
-        nks0 = ksg[r + g];
-        nks1 = ksg[r + g + 8];
-        nvs0 = vsg[r + g];
-        nvs1 = vsg[r + g + 8];
-      };
-      load_tile(0);
-      for (int tile = 0; tile < ntiles; ++tile) {
-        const uint4 k0 = nk0, k1 = nk1;
-        const uint2 v0 = nv[0], v1 = nv[1], v2 = nv[2], v3 = nv[3];
-        const float ks0 = nks0, ks1 = nks1, vs0 = nvs0, vs1 = nvs1;
-        if (tile + 1 < ntiles) load_tile(tile + 1);
-
-        // ---- S^T[16 tok x 8 heads] = K_dq Q^T ----
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t kx[4] = {k0.x, k0.y, k0.z, k0.w};
-        const uint32_t ky[4] = {k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t s0 = 0x5504u | ((2u * h) << 4), s1 = 0x5504u | ((2u * h + 1u) << 4);
-            const uint32_t a0 = lut_get(lut, kx[j], laneword, s0, 0);
-            const uint32_t a2 = lut_get(lut, kx[j], laneword, s1, 0);
-            const uint32_t a1 = lut_get(lut, ky[j], laneword, s0, 0);
-            const uint32_t a3 = lut_get(lut, ky[j], laneword, s1, 0);
-            mma16816(sc, a0, a1, a2, a3, qb[2 * j + h][0], qb[2 * j + h][1]);
-          }
-        }
-        // ---- online softmax (log2 domain) ----
-        const int64_t tg = tok0 + tile * 16 + g;
-        const bool ok0 = tg < n_valid, ok1 = tg + 8 < n_valid;
-        const float s00 = ok0 ? sc[0] * ks0 : -INFINITY;  // token g,   head 2t
-        const float s01 = ok0 ? sc[1] * ks0 : -INFINITY;  // token g,   head 2t+1
-        const float s10 = ok1 ? sc[2] * ks1 : -INFINITY;  // token g+8, head 2t
-        const float s11 = ok1 ? sc[3] * ks1 : -INFINITY;  // token g+8, head 2t+1
-        float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-        }
-        if (mx0 > m0 + kTau) {
-          const float al = exp2f(m0 - mx0);
-          l0 *= al;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            oacc[i][0] *= al;
-            oacc[i][2] *= al;
-          }
-          m0 = mx0;
-        }
-        if (mx1 > m1 + kTau) {
-          const float al = exp2f(m1 - mx1);
-          l1 *= al;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            oacc[i][1] *= al;
-            oacc[i][3] *= al;
-          }
-          m1 = mx1;
-        }
-        const float p00 = ok0 ? exp2f(s00 - m0) : 0.f, p10 = ok1 ? exp2f(s10 - m0) : 0.f;
-        const float p01 = ok0 ? exp2f(s01 - m1) : 0.f, p11 = ok1 ? exp2f(s11 - m1) : 0.f;
-        l0 += p00 + p10;
-        l1 += p01 + p11;
-        const float w0 = ok0 ? vs0 : 0.f, w1 = ok1 ? vs1 : 0.f;
-        const uint32_t h0 = h2_as_u32(__floats2half2_rn(p00 * w0, p10 * w1));  // head 2t:   tokens g, g+8
-        const uint32_t h1 = h2_as_u32(__floats2half2_rn(p01 * w0, p11 * w1));  // head 2t+1: tokens g, g+8
-        // ---- transpose P into the B fragment of P^T: head g, tokens (t, t+8), (t+4, t+12) ----
-        const int src0 = t * 4 + (g >> 1), src1 = (t + 4) * 4 + (g >> 1);
-        const uint32_t r00 = __shfl_sync(0xffffffffu, h0, src0), r01 = __shfl_sync(0xffffffffu, h1, src0);
-        const uint32_t r10 = __shfl_sync(0xffffffffu, h0, src1), r11 = __shfl_sync(0xffffffffu, h1, src1);
-        uint32_t pb0 = (g & 1) ? r01 : r00, pb1 = (g & 1) ? r11 : r10;
-        if (g >= G) pb0 = pb1 = 0u;
-        // ---- O^T[128 dims x 8 heads] += V_dq^T P^T ----
-        // pair 0 = tokens (t, t+8), pair 1 = tokens (t+4, t+12); word g = dims 16g..16g+15
-        uint32_t ev[2][2], od[2][2];
-        {
-          const uint32_t A0[2] = {v0.x, v0.y}, B0[2] = {v1.x, v1.y};
-          const uint32_t A1[2] = {v2.x, v2.y}, B1[2] = {v3.x, v3.y};
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            ev[0][hh] = (A0[hh] & 0x0F0F0F0Fu) | ((B0[hh] & 0x0F0F0F0Fu) << 4);
-            od[0][hh] = ((A0[hh] >> 4) & 0x0F0F0F0Fu) | (B0[hh] & 0xF0F0F0F0u);
-            ev[1][hh] = (A1[hh] & 0x0F0F0F0Fu) | ((B1[hh] & 0x0F0F0F0Fu) << 4);
-            od[1][hh] = ((A1[hh] >> 4) & 0x0F0F0F0Fu) | (B1[hh] & 0xF0F0F0F0u);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int hh = i >> 2;
-          const uint32_t sel = 0x5504u | ((uint32_t)(i & 3) << 4);
-          const uint32_t a0 = lut_get(lut, ev[0][hh], laneword, sel, 128);
-          const uint32_t a1 = lut_get(lut, od[0][hh], laneword, sel, 128);
-          const uint32_t a2 = lut_get(lut, ev[1][hh], laneword, sel, 128);
-          const uint32_t a3 = lut_get(lut, od[1][hh], laneword, sel, 128);
-          mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
-        }
-      }
-    }
-    // ---- warp partial: reduce l over the 8 lanes sharing t ----
+  auto flush = [&]() {
+    float L0 = l0, L1 = l1;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
-      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+      L0 += __shfl_xor_sync(0xffffffffu, L0, o);
+      L1 += __shfl_xor_sync(0xffffffffu, L1, o);
     }
-    float* wp = wpart + warp * G * PS;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int hd = 2 * t + e;
       if (hd < G) {
-        float* row = wp + hd * PS;
+        float* row = a.part + (slot_base * G + hd) * PS;
         if (g == 0) {
           row[0] = e ? m1 : m0;
-          row[1] = e ? l1 : l0;
+          row[1] = e ? L1 : L0;
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -311,44 +263,157 @@ __global__ void __launch_bounds__(kMmaWarps * 32) k_decode_mma(DecodeDev a) {
         }
       }
     }
-    __syncthreads();
-    // ---- merge the CTA's warps and write the chunk partial ----
-    for (int u = threadIdx.x; u < G * (D + 2); u += blockDim.x) {
-      const int hd = u / (D + 2), k = u % (D + 2);
-      float M = -INFINITY;
+  };
+
+  for (int64_t x = begin; x < end; ++x) {
+    const int stage = (int)((x - begin) % kStages);
+    if (cc.b != cur_b || cc.kvh != cur_kvh) {
+      if (cur_b >= 0) flush();
+      cur_b = cc.b;
+      cur_kvh = cc.kvh;
+      n_valid = a.seqinfo[2 * cur_b];
+      const int64_t seg_start = a.seg[cur_b] + (int64_t)cur_kvh * seq_tiles(a, cur_b);
+      slot_base = ((int64_t)cur_b * a.hkv + cur_kvh) * a.max_slots + (w - seg_start / a.per_warp);
+      const __half* qrow = a.q_h + ((int64_t)cur_b * a.hq + (int64_t)cur_kvh * G + (g < G ? g : 0)) * D;
 #pragma unroll
-      for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, wpart[(w * G + hd) * PS]);
-      float val;
-      if (k == 0) {
-        val = M;
-      } else {
-        val = 0.f;
+      for (int st = 0; st < 8; ++st) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(qrow + 32 * t + 4 * st);
+        qb[st][0] = g < G ? p[0] : 0u;
+        qb[st][1] = g < G ? p[1] : 0u;
+      }
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
 #pragma unroll
-        for (int w = 0; w < kMmaWarps; ++w) {
-          const float mw = wpart[(w * G + hd) * PS];
-          if (mw != -INFINITY) val += exp2f(mw - M) * wpart[(w * G + hd) * PS + k];
+      for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+    }
+    cp_wait_stages();
+    __syncwarp();
+    const uint8_t* st = stages + stage * kStageBytes;
+    const int64_t tok = cc.tile * 16;
+
+    // ---- S^T[16 tok x 8 heads] = K_dq Q^T ----
+    const uint4 k0 = *reinterpret_cast<const uint4*>(st + kStK + g * 64 + 16 * t);
+    const uint4 k1 = *reinterpret_cast<const uint4*>(st + kStK + (g + 8) * 64 + 16 * t);
+    const float ks0 = reinterpret_cast<const float*>(st + kStKs)[g];
+    const float ks1 = reinterpret_cast<const float*>(st + kStKs)[g + 8];
+    const float vs0 = reinterpret_cast<const float*>(st + kStVs)[g];
+    const float vs1 = reinterpret_cast<const float*>(st + kStVs)[g + 8];
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const uint32_t kx[4] = {k0.x, k0.y, k0.z, k0.w};
+      const uint32_t ky[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t s0 = 0x5504u | ((2u * h) << 4), s1 = 0x5504u | ((2u * h + 1u) << 4);
+          const uint32_t a0 = lut_get(lut, kx[j], laneword, s0, 0);
+          const uint32_t a2 = lut_get(lut, kx[j], laneword, s1, 0);
+          const uint32_t a1 = lut_get(lut, ky[j], laneword, s0, 0);
+          const uint32_t a3 = lut_get(lut, ky[j], laneword, s1, 0);
+          mma16816(sc, a0, a1, a2, a3, qb[2 * j + h][0], qb[2 * j + h][1]);
         }
       }
-      const int64_t row = (int64_t)s * a.hq + (int64_t)kvh * G + hd;
-      a.part[(row * a.n_chunks + chunk) * PS + k] = val;
     }
-    __syncthreads();
+    // ---- online softmax (log2 domain) ----
+    const bool ok0 = tok + g < n_valid, ok1 = tok + g + 8 < n_valid;
+    const float s00 = ok0 ? sc[0] * ks0 : -INFINITY;  // token g,   head 2t
+    const float s01 = ok0 ? sc[1] * ks0 : -INFINITY;  // token g,   head 2t+1
+    const float s10 = ok1 ? sc[2] * ks1 : -INFINITY;  // token g+8, head 2t
+    const float s11 = ok1 ? sc[3] * ks1 : -INFINITY;  // token g+8, head 2t+1
+    float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    if (mx0 > m0 + kTau) {
+      const float al = exp2f(m0 - mx0);
+      l0 *= al;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        oacc[i][0] *= al;
+        oacc[i][2] *= al;
+      }
+      m0 = mx0;
+    }
+    if (mx1 > m1 + kTau) {
+      const float al = exp2f(m1 - mx1);
+      l1 *= al;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        oacc[i][1] *= al;
+        oacc[i][3] *= al;
+      }
+      m1 = mx1;
+    }
+    const float p00 = ok0 ? exp2f(s00 - m0) : 0.f, p10 = ok1 ? exp2f(s10 - m0) : 0.f;
+    const float p01 = ok0 ? exp2f(s01 - m1) : 0.f, p11 = ok1 ? exp2f(s11 - m1) : 0.f;
+    l0 += p00 + p10;
+    l1 += p01 + p11;
+    const float w0 = ok0 ? vs0 : 0.f, w1 = ok1 ? vs1 : 0.f;
+    const uint32_t h0 = h2_as_u32(__floats2half2_rn(p00 * w0, p10 * w1));  // head 2t:   tokens g, g+8
+    const uint32_t h1 = h2_as_u32(__floats2half2_rn(p01 * w0, p11 * w1));  // head 2t+1: tokens g, g+8
+    // ---- transpose P into the B fragment of P^T: head g, tokens (t, t+8), (t+4, t+12) ----
+    const int src0 = t * 4 + (g >> 1), src1 = (t + 4) * 4 + (g >> 1);
+    const uint32_t r00 = __shfl_sync(0xffffffffu, h0, src0), r01 = __shfl_sync(0xffffffffu, h1, src0);
+    const uint32_t r10 = __shfl_sync(0xffffffffu, h0, src1), r11 = __shfl_sync(0xffffffffu, h1, src1);
+    uint32_t pb0 = (g & 1) ? r01 : r00, pb1 = (g & 1) ? r11 : r10;
+    if (g >= G) pb0 = pb1 = 0u;
+    // ---- O^T[128 dims x 8 heads] += V_dq^T P^T ----
+    {
+      const uint2 v0 = *reinterpret_cast<const uint2*>(st + kStV + t * kVStride + 8 * g);
+      const uint2 v1 = *reinterpret_cast<const uint2*>(st + kStV + (t + 8) * kVStride + 8 * g);
+      const uint2 v2 = *reinterpret_cast<const uint2*>(st + kStV + (t + 4) * kVStride + 8 * g);
+      const uint2 v3 = *reinterpret_cast<const uint2*>(st + kStV + (t + 12) * kVStride + 8 * g);
+      uint32_t ev[2][2], od[2][2];
+      const uint32_t A0[2] = {v0.x, v0.y}, B0[2] = {v1.x, v1.y};
+      const uint32_t A1[2] = {v2.x, v2.y}, B1[2] = {v3.x, v3.y};
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        ev[0][hh] = (A0[hh] & 0x0F0F0F0Fu) | ((B0[hh] & 0x0F0F0F0Fu) << 4);
+        od[0][hh] = ((A0[hh] >> 4) & 0x0F0F0F0Fu) | (B0[hh] & 0xF0F0F0F0u);
+        ev[1][hh] = (A1[hh] & 0x0F0F0F0Fu) | ((B1[hh] & 0x0F0F0F0Fu) << 4);
+        od[1][hh] = ((A1[hh] >> 4) & 0x0F0F0F0Fu) | (B1[hh] & 0xF0F0F0F0u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int hh = i >> 2;
+        const uint32_t sel = 0x5504u | ((uint32_t)(i & 3) << 4);
+        const uint32_t a0 = lut_get(lut, ev[0][hh], laneword, sel, 128);
+        const uint32_t a1 = lut_get(lut, od[0][hh], laneword, sel, 128);
+        const uint32_t a2 = lut_get(lut, ev[1][hh], laneword, sel, 128);
+        const uint32_t a3 = lut_get(lut, od[1][hh], laneword, sel, 128);
+        mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+    // ---- refill this stage with tile x + kStages ----
+    __syncwarp();
+    if (x + kStages < end) {
+      issue_tile(a, pc, st0 + stage * kStageBytes, lane);
+      advance(a, pc);
+    }
+    cp_commit();
+    advance(a, cc);
   }
+  cp_wait_all();
+  flush();
 }
 
 // ---------------------------------------------------------------------------
-// Generic path: any bit width, head_dim = 32*KPL, GS query heads per CTA.
+// Generic path: any bit width, head_dim = 32*KPL, GS query heads per CTA,
+// chunks of pages_per_chunk pages; partial slot = chunk.
 // ---------------------------------------------------------------------------
 template <int KPL, int GS>
 __global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
   extern __shared__ __align__(16) float gsm[];
-  const int D = 32 * KPL;
-  const int PS = D + 2;
+  constexpr int D = 32 * KPL;
+  constexpr int PS = D + 2;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = blockDim.x >> 5;
-  float* kc = gsm;             // [256]
-  float* vc = gsm + 256;       // [256]
-  float* wpart = gsm + 512;    // [nw][GS][PS]
+  float* kc = gsm;           // [256]
+  float* vc = gsm + 256;     // [256]
+  float* wpart = gsm + 512;  // [nw][GS][PS]
   for (int i = threadIdx.x; i < (1 << a.kbits); i += blockDim.x) kc[i] = a.kcent[i];
   for (int i = threadIdx.x; i < (1 << a.vbits); i += blockDim.x) vc[i] = a.vcent[i];
   __syncthreads();
@@ -398,8 +463,8 @@ __global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
 #pragma unroll
         for (int k = 0; k < KPL; ++k) {
           const int d = lane + 32 * k;
-          const uint64_t w = kw[(int64_t)tt * kw_row + d / kcpw];
-          const float c = kc[(w >> ((d % kcpw) * a.kbits)) & kmask];
+          const uint64_t wk = kw[(int64_t)tt * kw_row + d / kcpw];
+          const float c = kc[(wk >> ((d % kcpw) * a.kbits)) & kmask];
 #pragma unroll
           for (int g = 0; g < GS; ++g) part[g] = fmaf(q[g][k], c, part[g]);
           const uint64_t wv = vw[(int64_t)tt * vw_row + d / vcpw];
@@ -450,23 +515,24 @@ __global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
           if (mw != -INFINITY) val += exp2f(mw - M) * wpart[(w * GS + g) * PS + k];
         }
       }
-      const int64_t row = (int64_t)s * a.hq + qh0 + g;
-      a.part[(row * a.n_chunks + chunk) * PS + k] = val;
+      const int64_t slot = ((int64_t)s * a.hkv + kvh) * a.max_slots + chunk;
+      a.part[(slot * a.G + grp * GS + g) * PS + k] = val;
     }
     __syncthreads();
   }
 }
 
 // ---------------------------------------------------------------------------
-// Merge: rows of partials -> normalised (optionally un-rotated) output, or
-// merged partials. Block: dim threads, kMergeRows rows per block.
+// Merge: partial slots of row r = (group r / G, head r % G) at
+//   part + ((group * max_slots + c) * G + r % G) * PS,  c < cnt[group]
+// -> normalised (optionally un-rotated) output, and/or merged (m, l, o).
 // ---------------------------------------------------------------------------
 constexpr int kMergeRows = 8;
 
 struct MergeDev {
   const float* part;
-  int64_t stride_row, stride_part;
-  int32_t n_rows, n_parts, D;
+  const int32_t* cnt;
+  int32_t G, max_slots, n_rows, D;
   const float* R;
   void* out;
   int32_t out_dtype;
@@ -480,16 +546,21 @@ __global__ void k_merge(MergeDev a) {
   const int i = threadIdx.x;
   const int r0 = blockIdx.x * kMergeRows;
   const int D = a.D;
+  const int PS = D + 2;
   for (int r = 0; r < kMergeRows; ++r) {
     const int row = r0 + r;
     float val = 0.f;
     if (row < a.n_rows) {
-      const float* p = a.part + (int64_t)row * a.stride_row;
+      const int64_t group = row / a.G;
+      const int gh = row % a.G;
+      const int n = a.cnt ? a.cnt[group] : a.max_slots;
+      const float* p = a.part + (group * a.max_slots * a.G + gh) * PS;
+      const int64_t cs = (int64_t)a.G * PS;
       float M = -INFINITY;
-      for (int c = 0; c < a.n_parts; ++c) M = fmaxf(M, p[(int64_t)c * a.stride_part]);
+      for (int c = 0; c < n; ++c) M = fmaxf(M, p[c * cs]);
       float L = 0.f, O = 0.f;
-      for (int c = 0; c < a.n_parts; ++c) {
-        const float* pc = p + (int64_t)c * a.stride_part;
+      for (int c = 0; c < n; ++c) {
+        const float* pc = p + c * cs;
         if (pc[0] == -INFINITY) continue;
         const float w = exp2f(pc[0] - M);
         L += w * pc[1];
@@ -528,31 +599,14 @@ __global__ void k_merge(MergeDev a) {
 
 int g_num_sms = 0;
 
-int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
-
 template <int G>
-void launch_mma_g(const DecodeDev& d, cudaStream_t s) {
-  const size_t smem = kLutBytes + (size_t)kMmaWarps * G * 130 * sizeof(float);
+void launch_flat_g(const DecodeDev& d, int grid, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_decode_mma<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    LC_CUDA(cudaFuncSetAttribute(k_decode_flat<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlatSmem));
     attr = true;
   }
-  int per_sm = 0;
-  LC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mma<G>, kMmaWarps * 32, smem));
-  if (per_sm < 1) per_sm = 1;
-  const int64_t total = (int64_t)d.n_seqs * d.hkv * d.n_chunks;
-  int64_t grid = (int64_t)num_sms() * per_sm;
-  if (grid > total) grid = total;
-  k_decode_mma<G><<<(unsigned)grid, kMmaWarps * 32, smem, s>>>(d);
+  k_decode_flat<G><<<(unsigned)grid, kFlatWarps * 32, kFlatSmem, s>>>(d);
   LC_CUDA(cudaGetLastError());
 }
 
@@ -577,16 +631,65 @@ void launch_generic_t(const DecodeDev& d, cudaStream_t s) {
 
 template <int KPL>
 void launch_generic_k(const DecodeDev& d, cudaStream_t s) {
-  constexpr int cap = 32 / KPL > 0 ? 32 / KPL : 1;  // keep GS*KPL <= 32 registers per array
-  if (cap >= 4 && d.G % 4 == 0) return launch_generic_t<KPL, 4>(d, s);
-  if (cap >= 2 && d.G % 2 == 0) return launch_generic_t<KPL, 2>(d, s);
+  if constexpr (KPL <= 8) {
+    if (d.G % 4 == 0) return launch_generic_t<KPL, 4>(d, s);
+  }
+  if (d.G % 2 == 0) return launch_generic_t<KPL, 2>(d, s);
   return launch_generic_t<KPL, 1>(d, s);
 }
 
 }  // namespace
 
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
 bool decode_fast_path(int dim, int kbits, int vbits, int G) {
   return dim == 128 && kbits == 4 && vbits == 4 && G >= 1 && G <= 8;
+}
+
+DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits) {
+  DecodePlan p;
+  const int G = hq / hkv;
+  const int n = (int)lens.size();
+  p.cnt.assign((size_t)n * hkv, 0);
+  if (decode_fast_path(dim, kbits, vbits, G)) {
+    p.flat = true;
+    p.grid = num_sms();
+    p.seg.assign(n + 1, 0);
+    for (int b = 0; b < n; ++b) p.seg[b + 1] = p.seg[b] + (int64_t)hkv * ((lens[b] + 15) / 16);
+    p.total_tiles = p.seg[n];
+    const int64_t W = (int64_t)p.grid * kFlatWarps;
+    p.per_warp = p.total_tiles > 0 ? (p.total_tiles + W - 1) / W : 1;
+    int32_t mx = 1;
+    for (int b = 0; b < n; ++b) {
+      const int64_t nt = (lens[b] + 15) / 16;
+      if (nt == 0) continue;
+      for (int h = 0; h < hkv; ++h) {
+        const int64_t s0 = p.seg[b] + (int64_t)h * nt;
+        const int32_t c = (int32_t)((s0 + nt - 1) / p.per_warp - s0 / p.per_warp + 1);
+        p.cnt[(size_t)b * hkv + h] = c;
+        mx = c > mx ? c : mx;
+      }
+    }
+    p.max_slots = mx;
+  } else {
+    p.flat = false;
+    int64_t mx = 0;
+    for (int64_t L : lens) mx = L > mx ? L : mx;
+    const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
+    p.pages_per_chunk = 4;
+    p.n_chunks = (int32_t)((pages + 3) / 4 > 0 ? (pages + 3) / 4 : 1);
+    p.max_slots = p.n_chunks;
+    for (auto& c : p.cnt) c = p.n_chunks;
+  }
+  return p;
 }
 
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* RT,
@@ -598,11 +701,15 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
   LC_CUDA(cudaGetLastError());
 }
 
-void launch_decode_partials(const DecodeArgs& a, cudaStream_t s) {
+void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream_t s) {
   DecodeDev d;
   d.table = a.table;
   d.table_stride = a.table_stride;
   d.seqinfo = a.seqinfo;
+  d.seg = a.seg;
+  d.per_warp = p.per_warp;
+  d.total_tiles = p.total_tiles;
+  d.max_slots = p.max_slots;
   d.off_kw = a.layout.off[a.role_kw];
   d.off_vw = a.layout.off[a.role_vw];
   d.off_ks = a.layout.off[a.role_ks];
@@ -615,24 +722,25 @@ void launch_decode_partials(const DecodeArgs& a, cudaStream_t s) {
   d.dim = a.dim;
   d.kbits = a.kbits;
   d.vbits = a.vbits;
-  d.pages_per_chunk = a.pages_per_chunk;
-  d.n_chunks = a.n_chunks;
+  d.pages_per_chunk = p.pages_per_chunk;
+  d.n_chunks = p.n_chunks;
   d.G = a.hq / a.hkv;
   d.q_rot = a.q_rot;
   d.q_h = a.q_h;
   d.kcent = a.kcent;
   d.vcent = a.vcent;
   d.part = a.part;
-  if (decode_fast_path(a.dim, a.kbits, a.vbits, d.G) && a.pages_per_chunk == kMmaWarps) {
+  if (p.flat) {
+    if (p.total_tiles == 0) return;
     switch (d.G) {
-      case 1: return launch_mma_g<1>(d, s);
-      case 2: return launch_mma_g<2>(d, s);
-      case 3: return launch_mma_g<3>(d, s);
-      case 4: return launch_mma_g<4>(d, s);
-      case 5: return launch_mma_g<5>(d, s);
-      case 6: return launch_mma_g<6>(d, s);
-      case 7: return launch_mma_g<7>(d, s);
-      default: return launch_mma_g<8>(d, s);
+      case 1: return launch_flat_g<1>(d, p.grid, s);
+      case 2: return launch_flat_g<2>(d, p.grid, s);
+      case 3: return launch_flat_g<3>(d, p.grid, s);
+      case 4: return launch_flat_g<4>(d, p.grid, s);
+      case 5: return launch_flat_g<5>(d, p.grid, s);
+      case 6: return launch_flat_g<6>(d, p.grid, s);
+      case 7: return launch_flat_g<7>(d, p.grid, s);
+      default: return launch_flat_g<8>(d, p.grid, s);
     }
   }
   switch (a.dim) {
@@ -644,11 +752,11 @@ void launch_decode_partials(const DecodeArgs& a, cudaStream_t s) {
   }
 }
 
-void launch_merge(const float* part, int32_t n_rows, int32_t n_parts, int32_t dim, int64_t stride_row,
-                  int64_t stride_part, const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out,
-                  float* o_out, cudaStream_t s) {
+void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
+                  const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
+                  cudaStream_t s) {
   if (n_rows <= 0) return;
-  MergeDev d{part, stride_row, stride_part, n_rows, n_parts, dim, R, out, out_dtype, m_out, l_out, o_out};
+  MergeDev d{part, cnt, G, max_slots, n_rows, dim, R, out, out_dtype, m_out, l_out, o_out};
   const int blocks = (n_rows + kMergeRows - 1) / kMergeRows;
   k_merge<<<blocks, dim, kMergeRows * dim * sizeof(float), s>>>(d);
   LC_CUDA(cudaGetLastError());

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "common.h"
 
@@ -56,23 +57,37 @@ struct DecodeArgs {
   const uint64_t* table = nullptr;  // block table: row seq_ids[b] holds the page addresses of sequence b
   int64_t table_stride = 0;         // u64 entries per table row
   const int64_t* seqinfo = nullptr; // [n_seqs][2]: (tokens to attend, table row)
+  const int64_t* seg = nullptr;     // flat path: [n_seqs + 1] tile prefix over (seq, kv head)
   PageLayout layout;
   int32_t role_kw = 0, role_vw = 1, role_ks = 2, role_vs = 3;
   int32_t n_seqs = 0, hkv = 0, hq = 0, dim = 0;
   int32_t kbits = 4, vbits = 4;
-  int32_t pages_per_chunk = 4;
-  int32_t n_chunks = 0;           // chunks per (seq, kv head)
   const float* q_rot = nullptr;   // [n_seqs][hq][dim] f32, rotated and scaled by scale*log2(e)
   const __half* q_h = nullptr;    // same in f16
   const float* kcent = nullptr;   // [2^kbits]
   const float* vcent = nullptr;   // [2^vbits]
-  float* part = nullptr;          // [n_seqs][hkv][n_chunks][G][dim + 2]  (m, l, o...)
+  float* part = nullptr;          // [n_seqs][hkv][max_slots][G][dim + 2]  (m, l, o...)
 };
+
+// How a decode call is split: the flat tile-balanced fast path (one partial
+// slot per warp range touching a (seq, kv head)) or the chunked generic path
+// (one slot per chunk of pages_per_chunk pages).
+struct DecodePlan {
+  bool flat = false;
+  int32_t grid = 0;
+  int64_t per_warp = 1, total_tiles = 0;
+  int32_t max_slots = 1;
+  int32_t pages_per_chunk = 4, n_chunks = 1;
+  std::vector<int64_t> seg;  // [n_seqs + 1]
+  std::vector<int32_t> cnt;  // [n_seqs * hkv] slots used per (seq, kv head)
+};
+DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits);
+int num_sms();
 
 // q_rot[s][h][:] = (R q[s][h]) * qscale (R applied unless q_is_rotated)
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* R,
                      bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s);
-void launch_decode_partials(const DecodeArgs& a, cudaStream_t s);
+void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream_t s);
 
 // ---- parity hooks of the KVCache trait (hooks.cu): bit-exact in the
 // reference's f32 order ----
@@ -82,11 +97,13 @@ void launch_attend_keys(const float* q, const CodecDev& kc, const uint64_t* page
 // out[i] = sum_t sum_j R[j][i] * (c[code_tj] * (sigma_t * w_t)), |w_t| >= 1e-10   (simple.rs:76-99, 142-155)
 void launch_attend_values(const float* w, const CodecDev& vc, const uint64_t* pages, const PageLayout& L,
                           int role_vw, int role_vs, int head, int64_t n, float* out, cudaStream_t s);
-// Combine chunk partials [rows][n_parts][dim+2] -> (m, l, o) per row, or the
-// normalised output out[rows][dim] (un-rotated with R^T unless R == null).
-void launch_merge(const float* part, int32_t n_rows, int32_t n_parts, int32_t dim, int64_t part_stride_row,
-                  int64_t part_stride_part, const float* R, void* out, int32_t out_dtype, float* m_out,
-                  float* l_out, float* o_out, cudaStream_t s);
+// Combine partial slots -> (m, l, o) per row and/or the normalised output
+// out[rows][dim] (un-rotated with R^T unless R == null). Row r's slots are
+// part + (((r / G) * max_slots + c) * G + r % G) * (dim + 2), c < cnt[r / G]
+// (cnt == null: max_slots for every row).
+void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
+                  const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
+                  cudaStream_t s);
 bool decode_fast_path(int dim, int kbits, int vbits, int G);
 
 }  // namespace lc

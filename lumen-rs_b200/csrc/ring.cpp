@@ -223,6 +223,21 @@ int64_t RingOps::prepare_update(RingCore& r, int64_t S, bool prealloc) {
   return kept;
 }
 
+int64_t RingOps::new_pages_bound(const RingCore& r, int64_t S, bool prealloc) const {
+  if (S == 1 && prealloc) {
+    int64_t n = 1;  // copy-on-write of the written page
+    int64_t buf = r.has ? r.buf_len : 0;
+    if (!r.has || (r.offset >= buf && buf < r.max_size)) {
+      n += 1;
+      buf += std::min<int64_t>(kPageTokens, r.max_size - r.offset);
+    }
+    if (buf > r.max_size) n += pages_for(r.max_size);  // one-time trim regathers
+    return n;
+  }
+  if (!r.has) return pages_for(S);
+  return pages_for(std::min(std::max(r.buf_len, r.idx), r.max_size) + S) + 1;  // worst case: full regather
+}
+
 bool RingOps::truncate_to(RingCore& r, int64_t target) {
   if (target > r.offset) return false;
   if (target == r.offset) return true;

@@ -90,6 +90,8 @@ struct RingOps {
   // reorders as the reference does and returns the first logical row of the
   // S new tokens (rows [w, w+S) are private pages, ready to be written).
   int64_t prepare_update(RingCore& r, int64_t S, bool prealloc);
+  // Upper bound on the fresh pages prepare_update(r, S, prealloc) can take.
+  int64_t new_pages_bound(const RingCore& r, int64_t S, bool prealloc) const;
   // ring_truncate (native_cache.rs:304-335); false where the reference errs.
   bool truncate_to(RingCore& r, int64_t target);
   void clear(RingCore& r);

@@ -149,7 +149,10 @@ def test_append_errors(lc, orc, gpu):
         cache.append(0, [5], x, x)  # bad sequence id
     with pytest.raises(lc.LumenError):
         cache.append(3, [0], x, x)  # bad layer
-    big = np.zeros((1, 2, 600, 128), np.float32)
+    big = np.zeros((1, 2, 1200, 128), np.float32)
     with pytest.raises(lc.LumenError) as e:
         cache.append(0, [0], big, big)  # more pages than the pool holds
-    assert e.value.code == lc.LC_ERR_NOMEM if hasattr(lc, "LC_ERR_NOMEM") else -6
+    assert e.value.code == lc.LC_ERR_NOMEM
+    assert cache.ring_state(0, 0) == dict(offset=0, idx=0, buf_len=0, view_len=0)  # refused before any change
+    cache.append(0, [0], x, x)
+    assert cache.ring_state(0, 0)["view_len"] == 1

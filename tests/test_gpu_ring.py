@@ -118,7 +118,7 @@ def test_sliding_layer_holds_the_window(lc, orc, gpu, prealloc):
     scale = 1.0 / np.sqrt(dim)
     out = cache.decode_attn(0, [0], q, hq, scale)
     exp = np.stack([ref.attend(0, h // 2, q[0, h], scale) for h in range(hq)])
-    assert np.abs(out[0] - exp).max() <= 2e-3
+    assert (np.abs(out[0] - exp) - (2e-3 + 1e-3 * np.abs(exp))).max() <= 0  # 2e-3 abs + 1e-3 rel
     assert helpers.rel_mse(exp, out[0]) <= 1e-3
     # post-rotation rollback refused (native_cache.rs:318-327)
     with pytest.raises(lc.LumenError) as e:
@@ -154,9 +154,9 @@ def test_prefix_fork_copy_on_write(lc, orc, gpu):
     np.testing.assert_array_equal(b["k_words"], c["k_words"])
     np.testing.assert_array_equal(b["v_sigma"], c["v_sigma"])
     q = helpers.queries(orc, 3, 2, hq, dim)
-    o1 = cache.decode_attn(1, [1, 2], q, hq, 1.0 / np.sqrt(dim))
-    np.testing.assert_array_equal(o1[0], o1[1]) if False else None
-    assert np.abs(o1[0] - cache.decode_attn(1, [2], q[:1], hq, 1.0 / np.sqrt(dim))[0]).max() <= 1e-6
+    qq = np.ascontiguousarray(np.stack([q[0], q[0]]))
+    o1 = cache.decode_attn(1, [1, 2], qq, hq, 1.0 / np.sqrt(dim))
+    np.testing.assert_array_equal(o1[0], o1[1])  # shared pages read exactly like private ones
     # fork past what the source holds is refused
     with pytest.raises(lc.LumenError):
         cache.fork(0, 2, 5000)
