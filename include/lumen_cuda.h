@@ -19,7 +19,9 @@
  *    device memory of the cache's device; the library tells them apart and
  *    stages host buffers itself. Caller buffers are borrowed for the call.
  *  - `stream` is a cudaStream_t passed as void*; NULL means the library's
- *    own stream for that object. Calls that return host results synchronise.
+ *    own (non-blocking) stream for that object; pass cudaStreamLegacy
+ *    ((void*)0x1) for the legacy default stream. Calls that return host
+ *    results synchronise.
  *  - A handle is thread-compatible, not thread-safe: one thread at a time,
  *    matching the reference's `&mut self`.
  */

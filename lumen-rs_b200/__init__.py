@@ -38,6 +38,9 @@ LC_F32, LC_BF16, LC_F16 = 0, 1, 2
 LC_STORE_K_QJL, LC_STORE_V_QJL = 1, 2
 LC_FETCH_VIEW, LC_FETCH_BACKING = 0, 1
 LC_Q_ROTATED, LC_OUT_ROTATED = 1, 2
+# cudaStreamLegacy: the legacy default stream (torch's default stream, handle 0).
+# A NULL stream in the C ABI means the library's own stream instead.
+CUDA_STREAM_LEGACY = 0x1
 
 # Every symbol include/lumen_cuda.h declares.
 ABI_SYMBOLS = [
@@ -171,12 +174,13 @@ def _auto_stream(stream, *tensors):
     CUDA tensor is passed (so torch's allocator and our kernels stay ordered),
     else the library's own stream (None)."""
     if stream is not None:
-        return getattr(stream, "cuda_stream", stream)
+        s = getattr(stream, "cuda_stream", stream)
+        return s if s else CUDA_STREAM_LEGACY
     for t in tensors:
         if t is not None and getattr(t, "is_cuda", False):
             import torch
 
-            return torch.cuda.current_stream(t.device).cuda_stream
+            return torch.cuda.current_stream(t.device).cuda_stream or CUDA_STREAM_LEGACY
     return None
 
 

@@ -626,6 +626,7 @@ int lc_fetch(lc_cache* c, int32_t seq, int32_t layer, int32_t which, lc_fetch_ou
 struct DecodeRun {
   int32_t rows = 0, G = 1, max_slots = 1;
   const int32_t* cnt = nullptr;
+  float oscale = 1.0f;  // 1 / V table scale of the fast path
 };
 
 static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
@@ -661,8 +662,9 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
   c->q_rot.ensure((size_t)rows * D, s);
   c->q_h.ensure((size_t)rows * D, s);
-  launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0, scale * 1.4426950408889634f,
-                  c->q_rot.p, c->q_h.p, s);
+  const float kalpha = plan.flat ? c->dk.alpha : 1.0f, valpha = plan.flat ? c->dv.alpha : 1.0f;
+  launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0,
+                  scale * 1.4426950408889634f / kalpha, c->q_rot.p, c->q_h.p, s);
   ++c->launches;
   c->part.ensure((size_t)rows * plan.max_slots * (D + 2), s);
   DecodeArgs a;
@@ -685,6 +687,8 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   a.q_h = c->q_h.p;
   a.kcent = c->dk.cent_d;
   a.vcent = c->dv.cent_d;
+  a.kalpha = kalpha;
+  a.valpha = valpha;
   a.part = c->part.p;
   c->timed(c->t_decode, s, [&] { launch_decode_partials(a, plan, s); });
   ++c->launches;
@@ -694,6 +698,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   r.G = n_q_heads / hkv;
   r.max_slots = plan.max_slots;
   r.cnt = dcnt;
+  r.oscale = 1.0f / valpha;
   return r;
 }
 
@@ -714,7 +719,7 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
       dout = c->outbuf.p;
     }
     launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
-                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, s);
+                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, run.oscale, s);
     ++c->launches;
     if (host_out) {
       LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
@@ -743,7 +748,7 @@ int lc_decode_attn_partials(lc_cache* c, int32_t layer, int32_t n_seqs, const in
       dov = dl + rows;
     }
     launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D, nullptr, nullptr, LC_F32, dm, dl, dov,
-                 s);
+                 run.oscale, s);
     ++c->launches;
     if (!dev) {
       LC_CUDA(cudaMemcpyAsync(m, dm, rows * 4, cudaMemcpyDefault, s));
@@ -799,7 +804,7 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
       dout = c->outbuf.p;
     }
     launch_merge(c->part.p, nullptr, 1, n_parts, n_rows, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout,
-                 out_dtype, nullptr, nullptr, nullptr, s);
+                 out_dtype, nullptr, nullptr, nullptr, 1.0f, s);
     ++c->launches;
     if (host_out) LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
     LC_CUDA(cudaStreamSynchronize(s));

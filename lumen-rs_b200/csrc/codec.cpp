@@ -247,6 +247,41 @@ static float f32_ceil_of(double b) {
   return t;
 }
 
+// Nearest f16 value of a positive normal-range float (11 significant bits).
+static double round_f16(double x) {
+  int e = 0;
+  std::frexp(x, &e);  // x = m * 2^e, m in [0.5, 1)
+  const double ulp = std::ldexp(1.0, e - 11);
+  return std::nearbyint(x / ulp) * ulp;
+}
+
+// alpha in [1, 2) minimising max_k |f16(alpha c_k) - alpha c_k| / |alpha c_k|.
+static float f16_table_scale(const std::vector<double>& cents) {
+  std::vector<double> mags;
+  for (double v : cents) {
+    const double a = std::fabs((double)(float)v);
+    if (a > 0) mags.push_back(a);
+  }
+  if (mags.empty()) return 1.0f;
+  double best = 1e30;
+  float best_a = 1.0f;
+  const int steps = 1 << 18;
+  for (int k = 0; k < steps; ++k) {
+    const float a = 1.0f + (float)k / steps;
+    double worst = 0;
+    for (double mg : mags) {
+      const double x = (double)((float)mg * a);
+      worst = std::max(worst, std::fabs(round_f16(x) - x) / x);
+      if (worst >= best) break;
+    }
+    if (worst < best) {
+      best = worst;
+      best_a = a;
+    }
+  }
+  return best_a;
+}
+
 void CodecOnDevice::upload(const Codec& c) {
   free();
   dim = (int)c.dim;
@@ -269,6 +304,7 @@ void CodecOnDevice::upload(const Codec& c) {
   up(PTd, PT);
   up(thr_d, thr);
   up(cent_d, cent);
+  alpha = c.bits <= 4 ? f16_table_scale(c.cents) : 1.0f;
 }
 
 void CodecOnDevice::free() {

@@ -34,6 +34,10 @@ struct Codec {
 // Device tables in the layouts the kernels read.
 struct CodecOnDevice {
   int dim = 0, bits = 0, m = 0;
+  // Scale for the f16 centroid tables of the tensor-core decode: alpha*c_k
+  // rounds to f16 with the smallest worst-case relative error over the
+  // codebook (1 when not searched). Scores and outputs divide it back out.
+  float alpha = 1.0f;
   float* R = nullptr;
   float* RTd = nullptr;
   float* PTd = nullptr;

@@ -104,6 +104,7 @@ struct DecodeDev {
   const __half* q_h;
   const float* kcent;
   const float* vcent;
+  float kalpha, valpha;
   float* part;
 };
 
@@ -207,7 +208,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
   for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
     const int e = idx >> 6, slot = idx & 63;
     const float* cent = slot < 32 ? a.kcent : a.vcent;
-    reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(cent[e & 15], cent[e >> 4]));
+    const float al = slot < 32 ? a.kalpha : a.valpha;
+    reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(cent[e & 15] * al, cent[e >> 4] * al));
   }
   __syncthreads();
 
@@ -352,14 +354,23 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
     l0 += p00 + p10;
     l1 += p01 + p11;
     const float w0 = ok0 ? vs0 : 0.f, w1 = ok1 ? vs1 : 0.f;
-    const uint32_t h0 = h2_as_u32(__floats2half2_rn(p00 * w0, p10 * w1));  // head 2t:   tokens g, g+8
-    const uint32_t h1 = h2_as_u32(__floats2half2_rn(p01 * w0, p11 * w1));  // head 2t+1: tokens g, g+8
+    // p' = p * sigma_V as an f16 hi + lo pair: the PV products carry the
+    // centroid rounding only, not the rounding of p'.
+    const float pv00 = p00 * w0, pv10 = p10 * w1, pv01 = p01 * w0, pv11 = p11 * w1;
+    const __half2 h0h = __floats2half2_rn(pv00, pv10);  // head 2t:   tokens g, g+8
+    const __half2 h1h = __floats2half2_rn(pv01, pv11);  // head 2t+1: tokens g, g+8
+    const float2 f0 = __half22float2(h0h), f1 = __half22float2(h1h);
+    const uint32_t h0 = h2_as_u32(h0h), h1 = h2_as_u32(h1h);
+    const uint32_t h0l = h2_as_u32(__floats2half2_rn(pv00 - f0.x, pv10 - f0.y));
+    const uint32_t h1l = h2_as_u32(__floats2half2_rn(pv01 - f1.x, pv11 - f1.y));
     // ---- transpose P into the B fragment of P^T: head g, tokens (t, t+8), (t+4, t+12) ----
     const int src0 = t * 4 + (g >> 1), src1 = (t + 4) * 4 + (g >> 1);
-    const uint32_t r00 = __shfl_sync(0xffffffffu, h0, src0), r01 = __shfl_sync(0xffffffffu, h1, src0);
-    const uint32_t r10 = __shfl_sync(0xffffffffu, h0, src1), r11 = __shfl_sync(0xffffffffu, h1, src1);
-    uint32_t pb0 = (g & 1) ? r01 : r00, pb1 = (g & 1) ? r11 : r10;
-    if (g >= G) pb0 = pb1 = 0u;
+    const bool odd = g & 1;
+    uint32_t pb0 = __shfl_sync(0xffffffffu, odd ? h1 : h0, src0);
+    uint32_t pb1 = __shfl_sync(0xffffffffu, odd ? h1 : h0, src1);
+    uint32_t pc0 = __shfl_sync(0xffffffffu, odd ? h1l : h0l, src0);
+    uint32_t pc1 = __shfl_sync(0xffffffffu, odd ? h1l : h0l, src1);
+    if (g >= G) pb0 = pb1 = pc0 = pc1 = 0u;
     // ---- O^T[128 dims x 8 heads] += V_dq^T P^T ----
     {
       const uint2 v0 = *reinterpret_cast<const uint2*>(st + kStV + t * kVStride + 8 * g);
@@ -385,6 +396,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
         const uint32_t a2 = lut_get(lut, ev[1][hh], laneword, sel, 128);
         const uint32_t a3 = lut_get(lut, od[1][hh], laneword, sel, 128);
         mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
+        mma16816(oacc[i], a0, a1, a2, a3, pc0, pc1);
       }
     }
     // ---- refill this stage with tile x + kStages ----
@@ -533,6 +545,7 @@ struct MergeDev {
   const float* part;
   const int32_t* cnt;
   int32_t G, max_slots, n_rows, D;
+  float oscale;
   const float* R;
   void* out;
   int32_t out_dtype;
@@ -566,6 +579,7 @@ __global__ void k_merge(MergeDev a) {
         L += w * pc[1];
         O += w * pc[2 + i];
       }
+      O *= a.oscale;
       if (a.o_out) {
         a.o_out[(int64_t)row * D + i] = O;
         if (i == 0) {
@@ -729,6 +743,8 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
   d.q_h = a.q_h;
   d.kcent = a.kcent;
   d.vcent = a.vcent;
+  d.kalpha = a.kalpha;
+  d.valpha = a.valpha;
   d.part = a.part;
   if (p.flat) {
     if (p.total_tiles == 0) return;
@@ -754,9 +770,9 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
 
 void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
-                  cudaStream_t s) {
+                  float oscale, cudaStream_t s) {
   if (n_rows <= 0) return;
-  MergeDev d{part, cnt, G, max_slots, n_rows, dim, R, out, out_dtype, m_out, l_out, o_out};
+  MergeDev d{part, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out, o_out};
   const int blocks = (n_rows + kMergeRows - 1) / kMergeRows;
   k_merge<<<blocks, dim, kMergeRows * dim * sizeof(float), s>>>(d);
   LC_CUDA(cudaGetLastError());

@@ -66,6 +66,7 @@ struct DecodeArgs {
   const __half* q_h = nullptr;    // same in f16
   const float* kcent = nullptr;   // [2^kbits]
   const float* vcent = nullptr;   // [2^vbits]
+  float kalpha = 1.0f, valpha = 1.0f;  // f16 table scales of the fast path
   float* part = nullptr;          // [n_seqs][hkv][max_slots][G][dim + 2]  (m, l, o...)
 };
 
@@ -103,7 +104,7 @@ void launch_attend_values(const float* w, const CodecDev& vc, const uint64_t* pa
 // (cnt == null: max_slots for every row).
 void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
-                  cudaStream_t s);
+                  float oscale, cudaStream_t s);
 bool decode_fast_path(int dim, int kbits, int vbits, int G);
 
 }  // namespace lc

@@ -235,7 +235,26 @@ int64_t RingOps::new_pages_bound(const RingCore& r, int64_t S, bool prealloc) co
     return n;
   }
   if (!r.has) return pages_for(S);
-  return pages_for(std::min(std::max(r.buf_len, r.idx), r.max_size) + S) + 1;  // worst case: full regather
+  // the same decisions prepare_update takes, without side effects
+  const int64_t buf = r.buf_len, idx = r.idx, keep = r.keep;
+  int64_t held;
+  bool identity = true;
+  if (idx == buf) {
+    held = buf;
+  } else if (idx < r.offset) {
+    identity = false;
+    held = std::min(keep, buf) + std::max<int64_t>(buf - idx, 0) + std::max<int64_t>(idx - keep, 0);
+  } else {
+    held = std::min(idx, buf);
+  }
+  const int64_t trim = std::max<int64_t>(held + 1 - r.max_size, 0);
+  if (trim > 0) {
+    identity = false;
+    held = std::min(keep, held) + std::max<int64_t>(held - trim - keep, 0);
+  }
+  const int64_t n_new = held + S;
+  if (identity) return std::max<int64_t>(pages_for(n_new) - (int64_t)r.pages.size(), 0) + 1;
+  return pages_for(n_new);
 }
 
 bool RingOps::truncate_to(RingCore& r, int64_t target) {
