@@ -56,7 +56,7 @@ def measured_peaks():
 
 def profile_traffic():
     """dram bytes per decode launch from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "k_decode_mma_config1.md")
+    p = os.path.join(ROOT, "profiles", "k_decode_flat_config1.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -358,7 +358,7 @@ def run_ours(args):
                        "avg_launch_us": app_avg_ms * 1e3, "mode": "strict bit-exact"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profile_traffic(),
-                         "kernel": "k_decode_mma", "avg_launch_us": dec_avg_ms * 1e3, "launches": dec_n,
+                         "kernel": "k_decode_flat", "avg_launch_us": dec_avg_ms * 1e3, "launches": dec_n,
                          "bytes_per_launch": kv_bytes_per_launch, "peak_source": f"{peak_kind} hbm_gbs"},
             "cpu_baseline": cpu,
             "e2e": {"value": B / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -33,6 +33,9 @@ namespace lc {
 namespace {
 
 constexpr int kNB = 8;  // vectors per CTA pass
+// Appends of at most this many vectors per side take the warp-per-vector
+// kernel (latency-bound decode steps); larger ones the table-in-smem kernel.
+constexpr int64_t kSmallAppend = 16384;
 
 struct AppendDev {
   CodecDev codec[2];
@@ -250,6 +253,135 @@ __global__ void k_append_strict(AppendDev a) {
   }
 }
 
+// Small appends (decode steps: a few hundred vectors): one warp per vector so
+// every vector's sequential chains run concurrently; lane l owns outputs
+// l, l+32, ...; the tables are read through L1. Same operation order as
+// k_append_strict.
+constexpr int kWarpVecs = 4;
+
+template <int R>  // head_dim / 32
+__global__ void __launch_bounds__(kWarpVecs * 32) k_append_warp(AppendDev a) {
+  constexpr int D = 32 * R;
+  __shared__ float sx[kWarpVecs][D], sy[kWarpVecs][D], sr[kWarpVecs][D];
+  __shared__ uint8_t scode[kWarpVecs][D];
+  __shared__ uint32_t sq[kWarpVecs][16];  // QJL bits, up to 512 rows
+  const int side = blockIdx.y;
+  const CodecDev& c = a.codec[side];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
+  const int64_t v = (int64_t)blockIdx.x * kWarpVecs + warp;
+  if (v >= n_vec) return;
+  const bool stage2 = a.role_qjl[side] >= 0;
+  float* x = sx[warp];
+  float* y = sy[warp];
+  const void* src = a.src[side];
+#pragma unroll
+  for (int r = 0; r < R; ++r) x[lane + 32 * r] = load_elem(src, a.dtype, v * D + lane + 32 * r);
+  __syncwarp();
+  // rotated[i] = sum_j R[i][j] x[j] (rotation.rs:91-99)
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = -0.0f;
+#pragma unroll 4
+  for (int j = 0; j < D; ++j) {
+    const float xj = x[j];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(c.RT + j * D + lane + 32 * r), xj));
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) y[lane + 32 * r] = acc[r];
+  __syncwarp();
+  // scale (compressor.rs:70-71), sequential in lane 0
+  float sc = 0.f, inv = 0.f;
+  if (lane == 0) {
+    float s = -0.0f;
+    for (int k = 0; k < D; ++k) s = __fadd_rn(s, __fmul_rn(y[k], y[k]));
+    sc = __fsqrt_rn(__fdiv_rn(s, (float)D));
+    inv = __fdiv_rn(1.0f, sc);
+  }
+  sc = __shfl_sync(0xffffffffu, sc, 0);
+  inv = __shfl_sync(0xffffffffu, inv, 0);
+  const int n1 = c.n_levels - 1;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane + 32 * r;
+    int code = 0;
+    if (!(sc < 1e-10f)) {
+      const float yn = __fmul_rn(y[i], inv);
+      for (int k = 0; k < n1; ++k) code += !(yn < __ldg(c.thr + k));
+    }
+    scode[warp][i] = (uint8_t)code;
+    y[i] = __fmul_rn(__ldg(c.cent + code), sc);
+  }
+  __syncwarp();
+  float rn = 0.f;
+  if (stage2) {
+    float* res = sr[warp];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < D; ++j) {
+      const float yj = y[j];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(c.R + j * D + lane + 32 * r), yj));
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) res[lane + 32 * r] = __fsub_rn(x[lane + 32 * r], acc[r]);
+    __syncwarp();
+    if (lane == 0) {
+      float s = 0.0f;
+      for (int k = 0; k < D; ++k) s = __fadd_rn(s, __fmul_rn(res[k], res[k]));
+      rn = __fsqrt_rn(s);
+    }
+    const int M = c.m;
+    for (int rb = 0; rb < M; rb += 32) {
+      const int row = rb + lane;
+      bool bit = false;
+      if (row < M) {
+        float dot = -0.0f;
+        for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(__ldg(c.PT + j * M + row), res[j]));
+        bit = dot >= 0.0f;
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, bit);
+      if (lane == 0 && (rb >> 5) < 16) sq[warp][rb >> 5] = bal;
+    }
+    __syncwarp();
+  }
+  // ---- pack and write (bitpack.rs:17-30) ----
+  const int64_t t = v % a.n_tok;
+  const int64_t sh = v / a.n_tok;
+  const int hl = (int)(sh % a.h_in);
+  const int64_t s = sh / a.h_in;
+  const int64_t slot = s * a.n_tok + t;
+  uint8_t* page = reinterpret_cast<uint8_t*>(a.dst_page[slot]);
+  const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.dst_row[slot];
+  const int cpw = 64 / c.bits;
+  for (int w = lane; w < c.words; w += 32) {
+    uint64_t word = 0;
+    for (int k = 0; k < cpw; ++k) {
+      const int idx = w * cpw + k;
+      if (idx < D) word |= (uint64_t)scode[warp][idx] << (k * c.bits);
+    }
+    const int rw = a.role_words[side];
+    reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
+  }
+  if (lane == 0) {
+    const int rsg = a.role_sigma[side];
+    *reinterpret_cast<float*>(page + a.off[rsg] + hr * a.row[rsg]) = sc;
+    if (stage2) {
+      const int rq = a.role_qjl[side], rr = a.role_rnorm[side];
+      uint64_t* qdst = reinterpret_cast<uint64_t*>(page + a.off[rq] + hr * a.row[rq]);
+      const int qw32 = (c.m + 31) / 32;
+      for (int w = 0; w < c.qwords; ++w) {
+        const uint64_t lo = 2 * w < qw32 ? sq[warp][2 * w] : 0u;
+        const uint64_t hi = 2 * w + 1 < qw32 ? sq[warp][2 * w + 1] : 0u;
+        qdst[w] = lo | (hi << 32);
+      }
+      *reinterpret_cast<float*>(page + a.off[rr] + hr * a.row[rr]) = rn;
+    }
+  }
+}
+
 }  // namespace
 
 size_t append_smem_bytes(int d, int m) {
@@ -287,6 +419,18 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
   }
   const int D = a.codec[0].dim;
   const int M = a.codec[0].m > a.codec[1].m ? a.codec[0].m : a.codec[1].m;
+  if (n_vec <= kSmallAppend && M <= 512) {
+    const dim3 grid((unsigned)((n_vec + kWarpVecs - 1) / kWarpVecs), 2);
+    switch (D) {
+      case 64: k_append_warp<2><<<grid, kWarpVecs * 32, 0, s>>>(d); break;
+      case 128: k_append_warp<4><<<grid, kWarpVecs * 32, 0, s>>>(d); break;
+      case 256: k_append_warp<8><<<grid, kWarpVecs * 32, 0, s>>>(d); break;
+      default: goto batch;
+    }
+    LC_CUDA(cudaGetLastError());
+    return;
+  }
+batch:
   const int groups = D <= 256 ? 2 : 1;
   const size_t per_group = append_smem_bytes(D, M);
   const size_t tables = (size_t)D * D * 4 + (stage2 ? (size_t)(D * D + D * M) * 4 : 0);

@@ -110,14 +110,20 @@ struct DecodeDev {
 
 // ---------------------------------------------------------------------------
 // Fast path: 4-bit K and V, head_dim 128, up to 8 query heads per kv head.
+// A tile is 32 tokens of one (sequence, kv head); a page holds 8 tiles.
 // ---------------------------------------------------------------------------
 constexpr int kFlatWarps = 16;
-constexpr int kStages = 3;
-constexpr int kLutBytes = 256 * 64 * 4;  // [byte][64 slots]: K table slots 0..31, V table 32..63
-constexpr int kVStride = 96;             // V rows padded to 96 B: conflict-free 8-byte reads
-constexpr int kStK = 0, kStV = 1024, kStKs = kStV + 16 * kVStride, kStVs = kStKs + 64;
-constexpr int kStageBytes = kStVs + 64;  // 2688
-constexpr int kFlatSmem = kLutBytes + kFlatWarps * kStages * kStageBytes;
+constexpr int kTileTok = 32;
+constexpr int kStages = 2;
+constexpr int kStK = 0;                    // [32 rows][64 B] K words
+constexpr int kStV = 2048;                 // [32 rows][64 B] V words, 16-B chunks XOR-swizzled by (row & 2)
+constexpr int kStKs = 4096, kStVs = 4224;  // [32] sigma_K, sigma_V
+constexpr int kStageBytes = 4352;
+constexpr int kWarpBytes = kStages * kStageBytes;
+constexpr int kLutBytes = 65536;  // [byte][64 slots] u32: K table in slots 0..31, V table in 32..63
+// The table sits at a 64 KiB-aligned shared address so one byte permute forms
+// a lookup address; warps' stages fill the space before and after it.
+constexpr int kFlatSmem = kLutBytes + (kFlatWarps + 1) * kWarpBytes;
 
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
@@ -129,81 +135,175 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
 
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// Byte k of x selects a half2 centroid pair; the lane's own copy (slot lane)
-// keeps the 32 lookups of a warp in 32 distinct banks.
-__device__ __forceinline__ uint32_t lut_get(const uint8_t* lut, uint32_t x, uint32_t laneword, uint32_t sel,
-                                            int slot_off) {
-  const uint32_t off = __byte_perm(x, laneword, sel);
-  return *reinterpret_cast<const uint32_t*>(lut + slot_off + off);
+// Table lookup. addr = [lane*4 | byte k of x | table base bits 16..31]: the
+// lane's own copy of the entry (bank = lane, conflict-free across the warp).
+__device__ __forceinline__ uint32_t lut_k(uint32_t x, uint32_t lanebase, uint32_t k) {
+  uint32_t v;
+  asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(__byte_perm(x, lanebase, 0x7604u | (k << 4))));
+  return v;
+}
+__device__ __forceinline__ uint32_t lut_v(uint32_t x, uint32_t lanebase, uint32_t k) {
+  uint32_t v;
+  asm("ld.shared.u32 %0, [%1+128];" : "=r"(v) : "r"(__byte_perm(x, lanebase, 0x7604u | (k << 4))));
+  return v;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_stages() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(kStages - 1) : "memory");
-}
+__device__ __forceinline__ void cp_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
-struct Cursor {
-  int b, kvh;
-  int64_t tile;
+// Walks (sequence, kv head, tile) in flat order; nt = tiles per kv head of b.
+struct Walk {
+  int b, kvh, tile, nt;
 };
 
-__device__ __forceinline__ int64_t seq_tiles(const DecodeDev& a, int b) { return (a.seqinfo[2 * b] + 15) >> 4; }
+__device__ __forceinline__ int tiles_of(const DecodeDev& a, int b) {
+  return (int)((a.seqinfo[2 * b] + kTileTok - 1) / kTileTok);
+}
 
-__device__ __forceinline__ Cursor locate(const DecodeDev& a, int64_t x) {
-  int lo = 0, hi = a.n_seqs - 1;  // last b with seg[b] <= x and tiles
+__device__ __forceinline__ Walk locate(const DecodeDev& a, int64_t x) {
+  int lo = 0, hi = a.n_seqs - 1;  // last b with seg[b] <= x (a sequence with tiles)
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (a.seg[mid] <= x) lo = mid;
     else hi = mid - 1;
   }
-  while (seq_tiles(a, lo) == 0) ++lo;  // x < total, so a later sequence holds it
-  const int64_t nt = seq_tiles(a, lo);
+  Walk w;
+  w.b = lo;
+  w.nt = tiles_of(a, lo);
   const int64_t off = x - a.seg[lo];
-  Cursor c;
-  c.b = lo;
-  c.kvh = (int)(off / nt);
-  c.tile = off % nt;
-  return c;
+  w.kvh = (int)(off / w.nt);
+  w.tile = (int)(off % w.nt);
+  return w;
 }
 
-__device__ __forceinline__ void advance(const DecodeDev& a, Cursor& c) {
-  if (++c.tile >= seq_tiles(a, c.b)) {
-    c.tile = 0;
-    if (++c.kvh == a.hkv) {
-      c.kvh = 0;
-      do {
-        ++c.b;
-      } while (c.b < a.n_seqs && seq_tiles(a, c.b) == 0);
+__device__ __forceinline__ void step(const DecodeDev& a, Walk& w) {
+  if (++w.tile < w.nt) return;
+  w.tile = 0;
+  if (++w.kvh < a.hkv) return;
+  w.kvh = 0;
+  do {
+    ++w.b;
+  } while (w.b < a.n_seqs && (w.nt = tiles_of(a, w.b)) == 0);
+}
+
+// Producer: issues the 16-byte copies of one tile into a stage; caches the
+// page address (it changes every 8 tiles).
+struct Producer {
+  Walk w;
+  const uint8_t* page;
+  int page_b, page_kvh, page_idx;
+
+  __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
+    const int pidx = w.tile >> 3;
+    if (pidx != page_idx || w.b != page_b) {
+      const uint64_t* trow = a.table + a.seqinfo[2 * w.b + 1] * a.table_stride;
+      page = reinterpret_cast<const uint8_t*>(__ldg(trow + pidx));
+      page_idx = pidx;
+      page_b = w.b;
+    }
+    const int64_t hr = (int64_t)w.kvh * kPageTokens + (w.tile & 7) * kTileTok;
+    const uint8_t* k = page + a.off_kw + hr * 64;
+    const uint8_t* v = page + a.off_vw + hr * 64;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = lane + 32 * q;  // 16-byte chunk: row c >> 2, part c & 3
+      cp_async16(st + kStK + c * 16, k + c * 16);
+      const int r = c >> 2;
+      cp_async16(st + kStV + r * 64 + (((c & 3) ^ (r & 2)) << 4), v + c * 16);
+    }
+    if (lane < 8) cp_async16(st + kStKs + lane * 16, page + a.off_ks + hr * 4 + lane * 16);
+    else if (lane < 16) cp_async16(st + kStVs + (lane - 8) * 16, page + a.off_vs + hr * 4 + (lane - 8) * 16);
+  }
+};
+
+// 16 tokens of the tile (rows r0..r0+15): S^T = K_dq Q^T into sc.
+__device__ __forceinline__ void qk16(const uint8_t* st, int r0, int g, int t, uint32_t lanebase,
+                                     const uint32_t (&qb)[8][2], float* sc) {
+  const uint4 k0 = *reinterpret_cast<const uint4*>(st + kStK + (r0 + g) * 64 + 16 * t);
+  const uint4 k1 = *reinterpret_cast<const uint4*>(st + kStK + (r0 + g + 8) * 64 + 16 * t);
+  const uint32_t kx[4] = {k0.x, k0.y, k0.z, k0.w};
+  const uint32_t ky[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t a0 = lut_k(kx[j], lanebase, 2 * h);
+      const uint32_t a2 = lut_k(kx[j], lanebase, 2 * h + 1);
+      const uint32_t a1 = lut_k(ky[j], lanebase, 2 * h);
+      const uint32_t a3 = lut_k(ky[j], lanebase, 2 * h + 1);
+      mma16816(sc, a0, a1, a2, a3, qb[2 * j + h][0], qb[2 * j + h][1]);
     }
   }
 }
 
-// Issue the 16-byte copies of one tile (K words, V words, sigma_K, sigma_V)
-// into a stage; every lane copies its share.
-__device__ __forceinline__ void issue_tile(const DecodeDev& a, const Cursor& c, uint32_t st, int lane) {
-  const uint64_t* trow = a.table + a.seqinfo[2 * c.b + 1] * a.table_stride;
-  const uint8_t* page = reinterpret_cast<const uint8_t*>(__ldg(trow + (c.tile >> 4)));
-  const int64_t hr = (int64_t)c.kvh * kPageTokens + (c.tile & 15) * 16;
-  const uint8_t* k = page + a.off_kw + hr * 64;
-  const uint8_t* v = page + a.off_vw + hr * 64;
-  cp_async16(st + kStK + lane * 16, k + lane * 16);
-  cp_async16(st + kStK + (lane + 32) * 16, k + (lane + 32) * 16);
-  cp_async16(st + kStV + (lane >> 2) * kVStride + (lane & 3) * 16, v + lane * 16);
-  cp_async16(st + kStV + ((lane + 32) >> 2) * kVStride + (lane & 3) * 16, v + (lane + 32) * 16);
-  if (lane < 4) cp_async16(st + kStKs + lane * 16, page + a.off_ks + hr * 4 + lane * 16);
-  else if (lane < 8) cp_async16(st + kStVs + (lane - 4) * 16, page + a.off_vs + hr * 4 + (lane - 4) * 16);
+// 16 tokens (rows r0..r0+15): O^T += V_dq^T P^T for the hi and lo parts of P.
+__device__ __forceinline__ void pv16(const uint8_t* st, int r0, int g, int t, uint32_t lanebase, uint32_t pb0,
+                                     uint32_t pb1, uint32_t pc0, uint32_t pc1, float (&oacc)[8][4]) {
+  // rows (tokens) t, t+8 (pair 0) and t+4, t+12 (pair 1); word g = dims 16g..16g+15
+  auto vrow = [&](int r) -> uint2 {
+    return *reinterpret_cast<const uint2*>(st + kStV + r * 64 + ((((g >> 1) ^ (r & 2))) << 4) + (g & 1) * 8);
+  };
+  const uint2 v0 = vrow(r0 + t), v1 = vrow(r0 + t + 8), v2 = vrow(r0 + t + 4), v3 = vrow(r0 + t + 12);
+  uint32_t ev[2][2], od[2][2];
+  const uint32_t A0[2] = {v0.x, v0.y}, B0[2] = {v1.x, v1.y};
+  const uint32_t A1[2] = {v2.x, v2.y}, B1[2] = {v3.x, v3.y};
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    ev[0][hh] = (A0[hh] & 0x0F0F0F0Fu) | ((B0[hh] & 0x0F0F0F0Fu) << 4);
+    od[0][hh] = ((A0[hh] >> 4) & 0x0F0F0F0Fu) | (B0[hh] & 0xF0F0F0F0u);
+    ev[1][hh] = (A1[hh] & 0x0F0F0F0Fu) | ((B1[hh] & 0x0F0F0F0Fu) << 4);
+    od[1][hh] = ((A1[hh] >> 4) & 0x0F0F0F0Fu) | (B1[hh] & 0xF0F0F0F0u);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int hh = i >> 2;
+    const uint32_t k = (uint32_t)(i & 3);
+    const uint32_t a0 = lut_v(ev[0][hh], lanebase, k);
+    const uint32_t a1 = lut_v(od[0][hh], lanebase, k);
+    const uint32_t a2 = lut_v(ev[1][hh], lanebase, k);
+    const uint32_t a3 = lut_v(od[1][hh], lanebase, k);
+    mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
+    mma16816(oacc[i], a0, a1, a2, a3, pc0, pc1);
+  }
+}
+
+// p' = p * sigma_V for (token u, token u+8) of heads 2t and 2t+1 as f16 hi +
+// lo pairs, moved into the P^T B fragments of head g: tokens (t, t+8) from
+// lane (t, g/2) and (t+4, t+12) from lane (t+4, g/2).
+__device__ __forceinline__ void p_frag(float p00, float p10, float p01, float p11, int g, int t, int G,
+                                       uint32_t& pb0, uint32_t& pb1, uint32_t& pc0, uint32_t& pc1) {
+  const __half2 h0h = __floats2half2_rn(p00, p10);  // head 2t
+  const __half2 h1h = __floats2half2_rn(p01, p11);  // head 2t+1
+  const float2 f0 = __half22float2(h0h), f1 = __half22float2(h1h);
+  const uint32_t h0 = h2_as_u32(h0h), h1 = h2_as_u32(h1h);
+  const uint32_t l0 = h2_as_u32(__floats2half2_rn(p00 - f0.x, p10 - f0.y));
+  const uint32_t l1 = h2_as_u32(__floats2half2_rn(p01 - f1.x, p11 - f1.y));
+  const int src0 = t * 4 + (g >> 1), src1 = (t + 4) * 4 + (g >> 1);
+  const bool odd = g & 1;
+  const uint32_t x00 = __shfl_sync(0xffffffffu, h0, src0), x01 = __shfl_sync(0xffffffffu, h1, src0);
+  const uint32_t x10 = __shfl_sync(0xffffffffu, h0, src1), x11 = __shfl_sync(0xffffffffu, h1, src1);
+  const uint32_t y00 = __shfl_sync(0xffffffffu, l0, src0), y01 = __shfl_sync(0xffffffffu, l1, src0);
+  const uint32_t y10 = __shfl_sync(0xffffffffu, l0, src1), y11 = __shfl_sync(0xffffffffu, l1, src1);
+  pb0 = odd ? x01 : x00;
+  pb1 = odd ? x11 : x10;
+  pc0 = odd ? y01 : y00;
+  pc1 = odd ? y11 : y10;
+  if (g >= G) pb0 = pb1 = pc0 = pc1 = 0u;
 }
 
 template <int G>
 __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* lut = smem;
   constexpr int D = 128;
   constexpr int PS = D + 2;
+  const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+  const uint32_t lut_off = (65536u - (s0 & 0xFFFFu)) & 0xFFFFu;
+  const int n_before = (int)(lut_off / kWarpBytes);
+  uint8_t* lut = smem + lut_off;
 
   for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
     const int e = idx >> 6, slot = idx & 63;
@@ -215,34 +315,121 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t laneword = (uint32_t)lane << 2;
+  const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
   const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
   const int64_t begin = w * a.per_warp;
   const int64_t end = min(begin + a.per_warp, a.total_tiles);
   if (begin >= end) return;
-  uint8_t* stages = smem + kLutBytes + warp * kStages * kStageBytes;
+  uint8_t* stages = warp < n_before ? smem + warp * kWarpBytes
+                                    : smem + lut_off + kLutBytes + (warp - n_before) * kWarpBytes;
   const uint32_t st0 = (uint32_t)__cvta_generic_to_shared(stages);
 
-  // ---- prologue: fill the ring ----
-  Cursor pc = locate(a, begin);
-  Cursor cc = pc;
+  Producer pr;
+  pr.w = locate(a, begin);
+  pr.page = nullptr;
+  pr.page_b = -1;
+  pr.page_idx = -1;
+  Walk cw = pr.w;
 #pragma unroll
   for (int s = 0; s < kStages; ++s) {
     if (begin + s < end) {
-      issue_tile(a, pc, st0 + s * kStageBytes, lane);
-      advance(a, pc);
+      pr.issue(a, st0 + s * kStageBytes, lane);
+      step(a, pr.w);
     }
     cp_commit();
   }
 
-  int cur_b = -1, cur_kvh = -1;
-  int64_t n_valid = 0;
-  uint32_t qb[8][2];
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  float oacc[8][4];
-  int64_t slot_base = 0;
+  int64_t x = begin;
+  while (x < end) {
+    // ---- a new (sequence, kv head) segment ----
+    const int b = cw.b, kvh = cw.kvh;
+    const int n_valid = (int)a.seqinfo[2 * b];
+    const int64_t seg_first = a.seg[b] + (int64_t)kvh * cw.nt;
+    const int64_t seg_end = min(end, seg_first + cw.nt);
+    const int64_t slot_base = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / a.per_warp);
+    uint32_t qb[8][2];
+    {
+      const __half* qrow = a.q_h + ((int64_t)b * a.hq + (int64_t)kvh * G + (g < G ? g : 0)) * D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(qrow + 32 * t + 4 * j);
+        qb[j][0] = g < G ? p[0] : 0u;
+        qb[j][1] = g < G ? p[1] : 0u;
+      }
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float oacc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
 
-  auto flush = [&]() {
+    for (; x < seg_end; ++x) {
+      const int stage = (int)((x - begin) & 1);
+      const int tok = cw.tile * kTileTok;
+      cp_wait_one();
+      __syncwarp();
+      const uint8_t* st = stages + stage * kStageBytes;
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      qk16(st, 0, g, t, lanebase, qb, sa);
+      qk16(st, 16, g, t, lanebase, qb, sb);
+      const float* ks = reinterpret_cast<const float*>(st + kStKs);
+      const float* vs = reinterpret_cast<const float*>(st + kStVs);
+      // tokens of this thread: u0 = g, u1 = g+8, u2 = 16+g, u3 = 24+g
+      const bool ok0 = tok + g < n_valid, ok1 = tok + g + 8 < n_valid;
+      const bool ok2 = tok + g + 16 < n_valid, ok3 = tok + g + 24 < n_valid;
+      const float k0 = ks[g], k1 = ks[g + 8], k2 = ks[g + 16], k3 = ks[g + 24];
+      // s[u][e]: token u, head 2t+e (log2 domain)
+      const float s00 = ok0 ? sa[0] * k0 : -INFINITY, s01 = ok0 ? sa[1] * k0 : -INFINITY;
+      const float s10 = ok1 ? sa[2] * k1 : -INFINITY, s11 = ok1 ? sa[3] * k1 : -INFINITY;
+      const float s20 = ok2 ? sb[0] * k2 : -INFINITY, s21 = ok2 ? sb[1] * k2 : -INFINITY;
+      const float s30 = ok3 ? sb[2] * k3 : -INFINITY, s31 = ok3 ? sb[3] * k3 : -INFINITY;
+      float mx0 = fmaxf(fmaxf(s00, s10), fmaxf(s20, s30));
+      float mx1 = fmaxf(fmaxf(s01, s11), fmaxf(s21, s31));
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      if (mx0 > m0 + kTau) {
+        const float al = exp2f(m0 - mx0);
+        l0 *= al;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          oacc[i][0] *= al;
+          oacc[i][2] *= al;
+        }
+        m0 = mx0;
+      }
+      if (mx1 > m1 + kTau) {
+        const float al = exp2f(m1 - mx1);
+        l1 *= al;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          oacc[i][1] *= al;
+          oacc[i][3] *= al;
+        }
+        m1 = mx1;
+      }
+      const float p00 = exp2f(s00 - m0), p10 = exp2f(s10 - m0), p20 = exp2f(s20 - m0), p30 = exp2f(s30 - m0);
+      const float p01 = exp2f(s01 - m1), p11 = exp2f(s11 - m1), p21 = exp2f(s21 - m1), p31 = exp2f(s31 - m1);
+      l0 += (p00 + p10) + (p20 + p30);
+      l1 += (p01 + p11) + (p21 + p31);
+      const float w0 = ok0 ? vs[g] : 0.f, w1 = ok1 ? vs[g + 8] : 0.f;
+      const float w2 = ok2 ? vs[g + 16] : 0.f, w3 = ok3 ? vs[g + 24] : 0.f;
+      uint32_t pb0, pb1, pc0, pc1;
+      p_frag(p00 * w0, p10 * w1, p01 * w0, p11 * w1, g, t, G, pb0, pb1, pc0, pc1);
+      pv16(st, 0, g, t, lanebase, pb0, pb1, pc0, pc1, oacc);
+      p_frag(p20 * w2, p30 * w3, p21 * w2, p31 * w3, g, t, G, pb0, pb1, pc0, pc1);
+      pv16(st, 16, g, t, lanebase, pb0, pb1, pc0, pc1, oacc);
+      // ---- refill this stage with tile x + kStages ----
+      __syncwarp();
+      if (x + kStages < end) {
+        pr.issue(a, st0 + stage * kStageBytes, lane);
+        step(a, pr.w);
+      }
+      cp_commit();
+      step(a, cw);
+    }
+    // ---- flush the segment's partial ----
     float L0 = l0, L1 = l1;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
@@ -265,151 +452,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
         }
       }
     }
-  };
-
-  for (int64_t x = begin; x < end; ++x) {
-    const int stage = (int)((x - begin) % kStages);
-    if (cc.b != cur_b || cc.kvh != cur_kvh) {
-      if (cur_b >= 0) flush();
-      cur_b = cc.b;
-      cur_kvh = cc.kvh;
-      n_valid = a.seqinfo[2 * cur_b];
-      const int64_t seg_start = a.seg[cur_b] + (int64_t)cur_kvh * seq_tiles(a, cur_b);
-      slot_base = ((int64_t)cur_b * a.hkv + cur_kvh) * a.max_slots + (w - seg_start / a.per_warp);
-      const __half* qrow = a.q_h + ((int64_t)cur_b * a.hq + (int64_t)cur_kvh * G + (g < G ? g : 0)) * D;
-#pragma unroll
-      for (int st = 0; st < 8; ++st) {
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(qrow + 32 * t + 4 * st);
-        qb[st][0] = g < G ? p[0] : 0u;
-        qb[st][1] = g < G ? p[1] : 0u;
-      }
-      m0 = m1 = -INFINITY;
-      l0 = l1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
-    }
-    cp_wait_stages();
-    __syncwarp();
-    const uint8_t* st = stages + stage * kStageBytes;
-    const int64_t tok = cc.tile * 16;
-
-    // ---- S^T[16 tok x 8 heads] = K_dq Q^T ----
-    const uint4 k0 = *reinterpret_cast<const uint4*>(st + kStK + g * 64 + 16 * t);
-    const uint4 k1 = *reinterpret_cast<const uint4*>(st + kStK + (g + 8) * 64 + 16 * t);
-    const float ks0 = reinterpret_cast<const float*>(st + kStKs)[g];
-    const float ks1 = reinterpret_cast<const float*>(st + kStKs)[g + 8];
-    const float vs0 = reinterpret_cast<const float*>(st + kStVs)[g];
-    const float vs1 = reinterpret_cast<const float*>(st + kStVs)[g + 8];
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const uint32_t kx[4] = {k0.x, k0.y, k0.z, k0.w};
-      const uint32_t ky[4] = {k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t s0 = 0x5504u | ((2u * h) << 4), s1 = 0x5504u | ((2u * h + 1u) << 4);
-          const uint32_t a0 = lut_get(lut, kx[j], laneword, s0, 0);
-          const uint32_t a2 = lut_get(lut, kx[j], laneword, s1, 0);
-          const uint32_t a1 = lut_get(lut, ky[j], laneword, s0, 0);
-          const uint32_t a3 = lut_get(lut, ky[j], laneword, s1, 0);
-          mma16816(sc, a0, a1, a2, a3, qb[2 * j + h][0], qb[2 * j + h][1]);
-        }
-      }
-    }
-    // ---- online softmax (log2 domain) ----
-    const bool ok0 = tok + g < n_valid, ok1 = tok + g + 8 < n_valid;
-    const float s00 = ok0 ? sc[0] * ks0 : -INFINITY;  // token g,   head 2t
-    const float s01 = ok0 ? sc[1] * ks0 : -INFINITY;  // token g,   head 2t+1
-    const float s10 = ok1 ? sc[2] * ks1 : -INFINITY;  // token g+8, head 2t
-    const float s11 = ok1 ? sc[3] * ks1 : -INFINITY;  // token g+8, head 2t+1
-    float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    if (mx0 > m0 + kTau) {
-      const float al = exp2f(m0 - mx0);
-      l0 *= al;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        oacc[i][0] *= al;
-        oacc[i][2] *= al;
-      }
-      m0 = mx0;
-    }
-    if (mx1 > m1 + kTau) {
-      const float al = exp2f(m1 - mx1);
-      l1 *= al;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        oacc[i][1] *= al;
-        oacc[i][3] *= al;
-      }
-      m1 = mx1;
-    }
-    const float p00 = ok0 ? exp2f(s00 - m0) : 0.f, p10 = ok1 ? exp2f(s10 - m0) : 0.f;
-    const float p01 = ok0 ? exp2f(s01 - m1) : 0.f, p11 = ok1 ? exp2f(s11 - m1) : 0.f;
-    l0 += p00 + p10;
-    l1 += p01 + p11;
-    const float w0 = ok0 ? vs0 : 0.f, w1 = ok1 ? vs1 : 0.f;
-    // p' = p * sigma_V as an f16 hi + lo pair: the PV products carry the
-    // centroid rounding only, not the rounding of p'.
-    const float pv00 = p00 * w0, pv10 = p10 * w1, pv01 = p01 * w0, pv11 = p11 * w1;
-    const __half2 h0h = __floats2half2_rn(pv00, pv10);  // head 2t:   tokens g, g+8
-    const __half2 h1h = __floats2half2_rn(pv01, pv11);  // head 2t+1: tokens g, g+8
-    const float2 f0 = __half22float2(h0h), f1 = __half22float2(h1h);
-    const uint32_t h0 = h2_as_u32(h0h), h1 = h2_as_u32(h1h);
-    const uint32_t h0l = h2_as_u32(__floats2half2_rn(pv00 - f0.x, pv10 - f0.y));
-    const uint32_t h1l = h2_as_u32(__floats2half2_rn(pv01 - f1.x, pv11 - f1.y));
-    // ---- transpose P into the B fragment of P^T: head g, tokens (t, t+8), (t+4, t+12) ----
-    const int src0 = t * 4 + (g >> 1), src1 = (t + 4) * 4 + (g >> 1);
-    const bool odd = g & 1;
-    uint32_t pb0 = __shfl_sync(0xffffffffu, odd ? h1 : h0, src0);
-    uint32_t pb1 = __shfl_sync(0xffffffffu, odd ? h1 : h0, src1);
-    uint32_t pc0 = __shfl_sync(0xffffffffu, odd ? h1l : h0l, src0);
-    uint32_t pc1 = __shfl_sync(0xffffffffu, odd ? h1l : h0l, src1);
-    if (g >= G) pb0 = pb1 = pc0 = pc1 = 0u;
-    // ---- O^T[128 dims x 8 heads] += V_dq^T P^T ----
-    {
-      const uint2 v0 = *reinterpret_cast<const uint2*>(st + kStV + t * kVStride + 8 * g);
-      const uint2 v1 = *reinterpret_cast<const uint2*>(st + kStV + (t + 8) * kVStride + 8 * g);
-      const uint2 v2 = *reinterpret_cast<const uint2*>(st + kStV + (t + 4) * kVStride + 8 * g);
-      const uint2 v3 = *reinterpret_cast<const uint2*>(st + kStV + (t + 12) * kVStride + 8 * g);
-      uint32_t ev[2][2], od[2][2];
-      const uint32_t A0[2] = {v0.x, v0.y}, B0[2] = {v1.x, v1.y};
-      const uint32_t A1[2] = {v2.x, v2.y}, B1[2] = {v3.x, v3.y};
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        ev[0][hh] = (A0[hh] & 0x0F0F0F0Fu) | ((B0[hh] & 0x0F0F0F0Fu) << 4);
-        od[0][hh] = ((A0[hh] >> 4) & 0x0F0F0F0Fu) | (B0[hh] & 0xF0F0F0F0u);
-        ev[1][hh] = (A1[hh] & 0x0F0F0F0Fu) | ((B1[hh] & 0x0F0F0F0Fu) << 4);
-        od[1][hh] = ((A1[hh] >> 4) & 0x0F0F0F0Fu) | (B1[hh] & 0xF0F0F0F0u);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int hh = i >> 2;
-        const uint32_t sel = 0x5504u | ((uint32_t)(i & 3) << 4);
-        const uint32_t a0 = lut_get(lut, ev[0][hh], laneword, sel, 128);
-        const uint32_t a1 = lut_get(lut, od[0][hh], laneword, sel, 128);
-        const uint32_t a2 = lut_get(lut, ev[1][hh], laneword, sel, 128);
-        const uint32_t a3 = lut_get(lut, od[1][hh], laneword, sel, 128);
-        mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
-        mma16816(oacc[i], a0, a1, a2, a3, pc0, pc1);
-      }
-    }
-    // ---- refill this stage with tile x + kStages ----
-    __syncwarp();
-    if (x + kStages < end) {
-      issue_tile(a, pc, st0 + stage * kStageBytes, lane);
-      advance(a, pc);
-    }
-    cp_commit();
-    advance(a, cc);
   }
   cp_wait_all();
-  flush();
 }
 
 // ---------------------------------------------------------------------------
@@ -677,13 +721,13 @@ DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int di
     p.flat = true;
     p.grid = num_sms();
     p.seg.assign(n + 1, 0);
-    for (int b = 0; b < n; ++b) p.seg[b + 1] = p.seg[b] + (int64_t)hkv * ((lens[b] + 15) / 16);
+    for (int b = 0; b < n; ++b) p.seg[b + 1] = p.seg[b] + (int64_t)hkv * ((lens[b] + kTileTok - 1) / kTileTok);
     p.total_tiles = p.seg[n];
     const int64_t W = (int64_t)p.grid * kFlatWarps;
     p.per_warp = p.total_tiles > 0 ? (p.total_tiles + W - 1) / W : 1;
     int32_t mx = 1;
     for (int b = 0; b < n; ++b) {
-      const int64_t nt = (lens[b] + 15) / 16;
+      const int64_t nt = (lens[b] + kTileTok - 1) / kTileTok;
       if (nt == 0) continue;
       for (int h = 0; h < hkv; ++h) {
         const int64_t s0 = p.seg[b] + (int64_t)h * nt;
