@@ -254,31 +254,71 @@ __global__ void k_append_strict(AppendDev a) {
 }
 
 // Small appends (decode steps: a few hundred vectors): one warp per vector so
-// every vector's sequential chains run concurrently; lane l owns outputs
-// l, l+32, ...; the tables are read through L1. Same operation order as
-// k_append_strict.
-constexpr int kWarpVecs = 4;
+// every vector's chains run concurrently, 16 vectors per CTA sharing the
+// tables staged once in shared memory (TAB) or read through L1. Lane l owns
+// outputs l, l+32, ...; sequential sums of squares are formed as exact
+// products in parallel and added in order by lane 0 (the same f32 result
+// as the reference's fold). Operation order as k_append_strict.
+constexpr int kWarpVecs = 16;
 
-template <int R>  // head_dim / 32
-__global__ void __launch_bounds__(kWarpVecs * 32) k_append_warp(AppendDev a) {
+__device__ __forceinline__ float seq_sum(const float* v, int n, float init) {
+  float s = init;
+#pragma unroll 8
+  for (int k = 0; k < n; ++k) s = __fadd_rn(s, v[k]);
+  return s;
+}
+
+template <int R, bool TAB>  // R = head_dim / 32
+__global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(AppendDev a) {
   constexpr int D = 32 * R;
-  __shared__ float sx[kWarpVecs][D], sy[kWarpVecs][D], sr[kWarpVecs][D];
-  __shared__ uint8_t scode[kWarpVecs][D];
-  __shared__ uint32_t sq[kWarpVecs][16];  // QJL bits, up to 512 rows
+  extern __shared__ __align__(16) uint8_t smem[];
   const int side = blockIdx.y;
   const CodecDev& c = a.codec[side];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool stage2 = a.role_qjl[side] >= 0;
+  const int M = c.m;
+  const int n1 = c.n_levels - 1;
+  // ---- shared: [thr 256][cent 256][per warp: x, y, r (D each), sq 16 u32, codes D][tables] ----
+  float* sthr = reinterpret_cast<float*>(smem);
+  float* scent = sthr + 256;
+  uint8_t* wb = smem + 2048 + (size_t)warp * (3 * D * 4 + 64 + D);
+  float* x = reinterpret_cast<float*>(wb);
+  float* y = x + D;
+  float* res = y + D;
+  uint32_t* sq = reinterpret_cast<uint32_t*>(res + D);
+  uint8_t* scode = reinterpret_cast<uint8_t*>(sq + 16);
+  const float* RT = c.RT;
+  const float* Rm = c.R;
+  const float* PT = c.PT;
+  {
+    float* tab = reinterpret_cast<float*>(smem + 2048 + (size_t)kWarpVecs * (3 * D * 4 + 64 + D));
+    for (int k = threadIdx.x; k < n1; k += blockDim.x) sthr[k] = c.thr[k];
+    for (int k = threadIdx.x; k <= n1; k += blockDim.x) scent[k] = c.cent[k];
+    if (TAB) {
+      const float4* src = reinterpret_cast<const float4*>(c.RT);
+      float4* dst = reinterpret_cast<float4*>(tab);
+      for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) dst[k] = __ldg(src + k);
+      RT = tab;
+      if (stage2) {
+        float* tr = tab + D * D;
+        const float4* s2 = reinterpret_cast<const float4*>(c.R);
+        for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(tr)[k] = __ldg(s2 + k);
+        float* tp = tr + D * D;
+        for (int k = threadIdx.x; k < D * M; k += blockDim.x) tp[k] = __ldg(c.PT + k);
+        Rm = tr;
+        PT = tp;
+      }
+    }
+  }
+  __syncthreads();
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const int64_t v = (int64_t)blockIdx.x * kWarpVecs + warp;
-  if (v >= n_vec) return;
-  const bool stage2 = a.role_qjl[side] >= 0;
-  float* x = sx[warp];
-  float* y = sy[warp];
+  if (v >= n_vec) return;  // no block-wide barrier after this point
   const void* src = a.src[side];
 #pragma unroll
   for (int r = 0; r < R; ++r) x[lane + 32 * r] = load_elem(src, a.dtype, v * D + lane + 32 * r);
   __syncwarp();
-  // rotated[i] = sum_j R[i][j] x[j] (rotation.rs:91-99)
+  // ---- rotated[i] = sum_j R[i][j] x[j] (rotation.rs:91-99) ----
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = -0.0f;
@@ -286,67 +326,71 @@ __global__ void __launch_bounds__(kWarpVecs * 32) k_append_warp(AppendDev a) {
   for (int j = 0; j < D; ++j) {
     const float xj = x[j];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(c.RT + j * D + lane + 32 * r), xj));
+    for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(RT[j * D + lane + 32 * r], xj));
   }
 #pragma unroll
-  for (int r = 0; r < R; ++r) y[lane + 32 * r] = acc[r];
+  for (int r = 0; r < R; ++r) {
+    y[lane + 32 * r] = acc[r];
+    res[lane + 32 * r] = __fmul_rn(acc[r], acc[r]);
+  }
   __syncwarp();
-  // scale (compressor.rs:70-71), sequential in lane 0
+  // ---- scale (compressor.rs:70-71) ----
   float sc = 0.f, inv = 0.f;
   if (lane == 0) {
-    float s = -0.0f;
-    for (int k = 0; k < D; ++k) s = __fadd_rn(s, __fmul_rn(y[k], y[k]));
-    sc = __fsqrt_rn(__fdiv_rn(s, (float)D));
+    sc = __fsqrt_rn(__fdiv_rn(seq_sum(res, D, -0.0f), (float)D));
     inv = __fdiv_rn(1.0f, sc);
   }
   sc = __shfl_sync(0xffffffffu, sc, 0);
   inv = __shfl_sync(0xffffffffu, inv, 0);
-  const int n1 = c.n_levels - 1;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = lane + 32 * r;
     int code = 0;
     if (!(sc < 1e-10f)) {
-      const float yn = __fmul_rn(y[i], inv);
-      for (int k = 0; k < n1; ++k) code += !(yn < __ldg(c.thr + k));
+      const float yn = __fmul_rn(acc[r], inv);
+      for (int k = 0; k < n1; ++k) code += !(yn < sthr[k]);
     }
-    scode[warp][i] = (uint8_t)code;
-    y[i] = __fmul_rn(__ldg(c.cent + code), sc);
+    scode[i] = (uint8_t)code;
+    y[i] = __fmul_rn(scent[code], sc);
   }
   __syncwarp();
   float rn = 0.f;
   if (stage2) {
-    float* res = sr[warp];
+    // ---- recon[i] = sum_j R[j][i] deq[j] (rotation.rs:102-113), residual, norm ----
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = 0.0f;
 #pragma unroll 4
     for (int j = 0; j < D; ++j) {
       const float yj = y[j];
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(c.R + j * D + lane + 32 * r), yj));
+      for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(Rm[j * D + lane + 32 * r], yj));
     }
+    float rr[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) res[lane + 32 * r] = __fsub_rn(x[lane + 32 * r], acc[r]);
+    for (int r = 0; r < R; ++r) rr[r] = __fsub_rn(x[lane + 32 * r], acc[r]);
     __syncwarp();
-    if (lane == 0) {
-      float s = 0.0f;
-      for (int k = 0; k < D; ++k) s = __fadd_rn(s, __fmul_rn(res[k], res[k]));
-      rn = __fsqrt_rn(s);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      y[lane + 32 * r] = rr[r];                       // residual
+      res[lane + 32 * r] = __fmul_rn(rr[r], rr[r]);   // its squares
     }
-    const int M = c.m;
+    __syncwarp();
+    if (lane == 0) rn = __fsqrt_rn(seq_sum(res, D, 0.0f));
+    // ---- QJL sign bits (qjl.rs:57-74) ----
     for (int rb = 0; rb < M; rb += 32) {
       const int row = rb + lane;
       bool bit = false;
       if (row < M) {
         float dot = -0.0f;
-        for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(__ldg(c.PT + j * M + row), res[j]));
+#pragma unroll 4
+        for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(PT[j * M + row], y[j]));
         bit = dot >= 0.0f;
       }
       const unsigned bal = __ballot_sync(0xffffffffu, bit);
-      if (lane == 0 && (rb >> 5) < 16) sq[warp][rb >> 5] = bal;
+      if (lane == 0 && (rb >> 5) < 16) sq[rb >> 5] = bal;
     }
-    __syncwarp();
   }
+  __syncwarp();
   // ---- pack and write (bitpack.rs:17-30) ----
   const int64_t t = v % a.n_tok;
   const int64_t sh = v / a.n_tok;
@@ -360,7 +404,7 @@ __global__ void __launch_bounds__(kWarpVecs * 32) k_append_warp(AppendDev a) {
     uint64_t word = 0;
     for (int k = 0; k < cpw; ++k) {
       const int idx = w * cpw + k;
-      if (idx < D) word |= (uint64_t)scode[warp][idx] << (k * c.bits);
+      if (idx < D) word |= (uint64_t)scode[idx] << (k * c.bits);
     }
     const int rw = a.role_words[side];
     reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
@@ -369,17 +413,36 @@ __global__ void __launch_bounds__(kWarpVecs * 32) k_append_warp(AppendDev a) {
     const int rsg = a.role_sigma[side];
     *reinterpret_cast<float*>(page + a.off[rsg] + hr * a.row[rsg]) = sc;
     if (stage2) {
-      const int rq = a.role_qjl[side], rr = a.role_rnorm[side];
+      const int rq = a.role_qjl[side], rrl = a.role_rnorm[side];
       uint64_t* qdst = reinterpret_cast<uint64_t*>(page + a.off[rq] + hr * a.row[rq]);
-      const int qw32 = (c.m + 31) / 32;
+      const int qw32 = (M + 31) / 32;
       for (int w = 0; w < c.qwords; ++w) {
-        const uint64_t lo = 2 * w < qw32 ? sq[warp][2 * w] : 0u;
-        const uint64_t hi = 2 * w + 1 < qw32 ? sq[warp][2 * w + 1] : 0u;
+        const uint64_t lo = 2 * w < qw32 ? sq[2 * w] : 0u;
+        const uint64_t hi = 2 * w + 1 < qw32 ? sq[2 * w + 1] : 0u;
         qdst[w] = lo | (hi << 32);
       }
-      *reinterpret_cast<float*>(page + a.off[rr] + hr * a.row[rr]) = rn;
+      *reinterpret_cast<float*>(page + a.off[rrl] + hr * a.row[rrl]) = rn;
     }
   }
+}
+
+template <int R>
+void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, cudaStream_t s) {
+  constexpr int D = 32 * R;
+  const size_t base = 2048 + (size_t)kWarpVecs * (3 * D * 4 + 64 + D);
+  const size_t tables = (size_t)D * D * 4 + (stage2 ? (size_t)(D * D + D * M) * 4 : 0);
+  const bool tab = base + tables <= 200 * 1024;
+  const size_t smem = base + (tab ? tables : 0);
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_append_warp<R, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_append_warp<R, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr = true;
+  }
+  const dim3 grid((unsigned)((n_vec + kWarpVecs - 1) / kWarpVecs), 2);
+  if (tab) k_append_warp<R, true><<<grid, kWarpVecs * 32, smem, s>>>(d);
+  else k_append_warp<R, false><<<grid, kWarpVecs * 32, smem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
 }
 
 }  // namespace
@@ -419,18 +482,12 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
   }
   const int D = a.codec[0].dim;
   const int M = a.codec[0].m > a.codec[1].m ? a.codec[0].m : a.codec[1].m;
-  if (n_vec <= kSmallAppend && M <= 512) {
-    const dim3 grid((unsigned)((n_vec + kWarpVecs - 1) / kWarpVecs), 2);
-    switch (D) {
-      case 64: k_append_warp<2><<<grid, kWarpVecs * 32, 0, s>>>(d); break;
-      case 128: k_append_warp<4><<<grid, kWarpVecs * 32, 0, s>>>(d); break;
-      case 256: k_append_warp<8><<<grid, kWarpVecs * 32, 0, s>>>(d); break;
-      default: goto batch;
-    }
-    LC_CUDA(cudaGetLastError());
+  if (n_vec <= kSmallAppend && M <= 512 && (D == 64 || D == 128 || D == 256)) {
+    if (D == 64) launch_warp_append<2>(d, stage2, M, n_vec, s);
+    else if (D == 128) launch_warp_append<4>(d, stage2, M, n_vec, s);
+    else launch_warp_append<8>(d, stage2, M, n_vec, s);
     return;
   }
-batch:
   const int groups = D <= 256 ? 2 : 1;
   const size_t per_group = append_smem_bytes(D, M);
   const size_t tables = (size_t)D * D * 4 + (stage2 ? (size_t)(D * D + D * M) * 4 : 0);

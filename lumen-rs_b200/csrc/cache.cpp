@@ -122,6 +122,18 @@ struct lc_cache {
   }
   cudaStream_t pick(void* s) const { return s ? static_cast<cudaStream_t>(s) : stream; }
 
+  // Device work on the cache is serialised across streams: before work on
+  // `s`, wait for everything issued on the stream used last.
+  cudaStream_t last = nullptr;
+  cudaEvent_t ev_order = nullptr;
+  void order(cudaStream_t s) {
+    if (last && last != s) {
+      LC_CUDA(cudaEventRecord(ev_order, last));
+      LC_CUDA(cudaStreamWaitEvent(s, ev_order, 0));
+    }
+    last = s;
+  }
+
   // Upload (seq, layer)'s page addresses if they changed.
   void sync_table(int32_t seq, int32_t layer, cudaStream_t s) {
     SeqLayer& sl = at(seq, layer);
@@ -147,7 +159,9 @@ struct lc_cache {
   }
 
   ~lc_cache() {
+    if (last) cudaStreamSynchronize(last);
     if (stream) cudaStreamSynchronize(stream);
+    if (ev_order) cudaEventDestroy(ev_order);
     for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
     if (d_table) cudaFree(d_table);
     if (ev_copy) cudaEventDestroy(ev_copy);
@@ -234,6 +248,7 @@ int lc_cache_create(const lc_cache_config* cfg, const lc_codec* kcodec, const lc
     LC_CUDA(cudaSetDevice(cfg->device));
     LC_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     LC_CUDA(cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming));
+    LC_CUDA(cudaEventCreateWithFlags(&c->ev_order, cudaEventDisableTiming));
     c->dk.upload(c->kc);
     c->dv.upload(c->vc);
     const int64_t H = cfg->n_kv_heads;
@@ -318,6 +333,7 @@ int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids
     LC_REQUIRE(n_seqs > 0 && n_tokens > 0, LC_ERR_INVALID, "n_seqs and n_tokens must be > 0");
     LC_CUDA(cudaSetDevice(c->cfg.device));
     cudaStream_t s = c->pick(stream);
+    c->order(s);
     c->ops.stream = s;
     const size_t esz = dtype_size(dtype);
     const int32_t H = c->cfg.n_kv_heads;
@@ -376,6 +392,7 @@ int lc_store(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float*
     if (n_tokens <= 0) return;
     LC_CUDA(cudaSetDevice(c->cfg.device));
     cudaStream_t s = c->stream;
+    c->order(s);
     c->ops.stream = s;
     SeqLayer& sl = c->at(seq, layer);
     if (sl.head_len.empty()) sl.head_len.assign(c->cfg.n_kv_heads, sl.ring.offset);
@@ -431,6 +448,7 @@ int lc_attend_keys(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const 
     LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
     LC_CUDA(cudaSetDevice(c->cfg.device));
     cudaStream_t s = c->stream;
+    c->order(s);
     const SeqLayer& sl = c->at(seq, layer);
     const int64_t n = sl.head_len.empty() ? sl.ring.view_len : sl.head_len[head];
     LC_REQUIRE(n_scores >= n, LC_ERR_INVALID, "scores buffer too small");
@@ -457,6 +475,7 @@ int lc_attend_values(lc_cache* c, int32_t seq, int32_t layer, int32_t head, cons
     LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
     LC_CUDA(cudaSetDevice(c->cfg.device));
     cudaStream_t s = c->stream;
+    c->order(s);
     const SeqLayer& sl = c->at(seq, layer);
     const int64_t n = sl.head_len.empty() ? sl.ring.view_len : sl.head_len[head];
     LC_REQUIRE(n_weights == n, LC_ERR_INVALID, "weights length differs from seq_len");
@@ -476,6 +495,7 @@ int lc_clear(lc_cache* c) {
   return abi_guard([&] {
     LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
     LC_CUDA(cudaSetDevice(c->cfg.device));
+    if (c->last) LC_CUDA(cudaStreamSynchronize(c->last));
     LC_CUDA(cudaStreamSynchronize(c->stream));
     for (auto& sl : c->st) {
       c->ops.clear(sl.ring);
@@ -586,6 +606,7 @@ int lc_fetch(lc_cache* c, int32_t seq, int32_t layer, int32_t which, lc_fetch_ou
     c->check(seq, layer);
     LC_CUDA(cudaSetDevice(c->cfg.device));
     cudaStream_t s = c->stream;
+    c->order(s);
     const SeqLayer& sl = c->at(seq, layer);
     const int64_t n = which == LC_FETCH_BACKING ? (sl.ring.has ? sl.ring.buf_len : 0) : sl.ring.view_len;
     if (n_out) *n_out = n;
@@ -637,6 +658,8 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   LC_REQUIRE(n_q_heads > 0 && n_q_heads % hkv == 0, LC_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads");
   const int32_t D = c->cfg.head_dim;
   LC_CUDA(cudaSetDevice(c->cfg.device));
+  c->order(s);
+  c->ops.stream = s;
   std::vector<int64_t> info((size_t)n_seqs * 2), lens(n_seqs);
   for (int32_t b = 0; b < n_seqs; ++b) {
     const int32_t seq = seq_ids[b];
@@ -768,6 +791,7 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
     LC_REQUIRE(n_parts > 0 && n_rows > 0, LC_ERR_INVALID, "n_parts and n_rows must be > 0");
     LC_CUDA(cudaSetDevice(c->cfg.device));
     cudaStream_t s = c->pick(stream);
+    c->order(s);
     const int32_t D = c->cfg.head_dim;
     // pack into [rows][parts][D+2] (m, l, o) so the merge kernel reads one layout
     std::vector<float> packed;

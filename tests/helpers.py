@@ -56,3 +56,26 @@ def rel_mse(ref, got):
     ref = np.asarray(ref, np.float64)
     got = np.asarray(got, np.float64)
     return float(np.mean((ref - got) ** 2) / (np.mean(ref ** 2) + 1e-12))
+
+
+ATTN_ATOL = 2e-3
+ATTN_RTOL = 1e-3
+ATTN_REL_MSE = 1e-3
+
+
+def attn_close(got, ref):
+    """Attention-output parity: for every output row (one query head's
+    head_dim vector) max|got - ref| <= 2e-3 + 1e-3 * max|ref row|, and over all
+    outputs the relative MSE of turboquant.rs:993-1003 <= 1e-3.
+
+    The relative part is taken against the row's scale: the output is
+    R^T o, and the rotation spreads a rounding of o evenly over every
+    element of the row, small elements included. Returns (ok, message)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref)
+    scale = np.abs(ref).max(axis=-1, keepdims=True)
+    excess = float((err - (ATTN_ATOL + ATTN_RTOL * scale)).max())
+    rm = rel_mse(ref, got)
+    ok = excess <= 0 and rm <= ATTN_REL_MSE
+    return ok, f"max_abs={err.max():.3e} worst excess={excess:.3e} rel_mse={rm:.3e}"

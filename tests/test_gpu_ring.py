@@ -118,8 +118,8 @@ def test_sliding_layer_holds_the_window(lc, orc, gpu, prealloc):
     scale = 1.0 / np.sqrt(dim)
     out = cache.decode_attn(0, [0], q, hq, scale)
     exp = np.stack([ref.attend(0, h // 2, q[0, h], scale) for h in range(hq)])
-    assert (np.abs(out[0] - exp) - (2e-3 + 1e-3 * np.abs(exp))).max() <= 0  # 2e-3 abs + 1e-3 rel
-    assert helpers.rel_mse(exp, out[0]) <= 1e-3
+    ok, msg = helpers.attn_close(out[0], exp)
+    assert ok, msg
     # post-rotation rollback refused (native_cache.rs:318-327)
     with pytest.raises(lc.LumenError) as e:
         cache.truncate_to(0, 0, 10)
