@@ -31,6 +31,7 @@
 #include <cuda_fp16.h>
 
 #include <cfloat>
+#include <type_traits>
 
 #include "kernels.h"
 
@@ -146,6 +147,13 @@ __device__ __forceinline__ uint32_t lut_v(uint32_t x, uint32_t lanebase, uint32_
   uint32_t v;
   asm("ld.shared.u32 %0, [%1+128];" : "=r"(v) : "r"(__byte_perm(x, lanebase, 0x7604u | (k << 4))));
   return v;
+}
+
+// 2^x on the SFU (ex2.approx.ftz: -inf -> 0, relative error ~2^-22).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -362,11 +370,11 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
 #pragma unroll
     for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
 
-    for (; x < seg_end; ++x) {
+    // One 32-token tile; MASKED only for a sequence's last, partial tile.
+    auto tile = [&](auto masked) {
+      constexpr bool MASKED = decltype(masked)::value;
       const int stage = (int)((x - begin) & 1);
       const int tok = cw.tile * kTileTok;
-      cp_wait_one();
-      __syncwarp();
       const uint8_t* st = stages + stage * kStageBytes;
       float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
       qk16(st, 0, g, t, lanebase, qb, sa);
@@ -374,8 +382,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
       const float* ks = reinterpret_cast<const float*>(st + kStKs);
       const float* vs = reinterpret_cast<const float*>(st + kStVs);
       // tokens of this thread: u0 = g, u1 = g+8, u2 = 16+g, u3 = 24+g
-      const bool ok0 = tok + g < n_valid, ok1 = tok + g + 8 < n_valid;
-      const bool ok2 = tok + g + 16 < n_valid, ok3 = tok + g + 24 < n_valid;
+      const bool ok0 = !MASKED || tok + g < n_valid, ok1 = !MASKED || tok + g + 8 < n_valid;
+      const bool ok2 = !MASKED || tok + g + 16 < n_valid, ok3 = !MASKED || tok + g + 24 < n_valid;
       const float k0 = ks[g], k1 = ks[g + 8], k2 = ks[g + 16], k3 = ks[g + 24];
       // s[u][e]: token u, head 2t+e (log2 domain)
       const float s00 = ok0 ? sa[0] * k0 : -INFINITY, s01 = ok0 ? sa[1] * k0 : -INFINITY;
@@ -390,7 +398,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
       }
       if (mx0 > m0 + kTau) {
-        const float al = exp2f(m0 - mx0);
+        const float al = ex2(m0 - mx0);
         l0 *= al;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -400,7 +408,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
         m0 = mx0;
       }
       if (mx1 > m1 + kTau) {
-        const float al = exp2f(m1 - mx1);
+        const float al = ex2(m1 - mx1);
         l1 *= al;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -409,8 +417,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
         }
         m1 = mx1;
       }
-      const float p00 = exp2f(s00 - m0), p10 = exp2f(s10 - m0), p20 = exp2f(s20 - m0), p30 = exp2f(s30 - m0);
-      const float p01 = exp2f(s01 - m1), p11 = exp2f(s11 - m1), p21 = exp2f(s21 - m1), p31 = exp2f(s31 - m1);
+      const float p00 = ex2(s00 - m0), p10 = ex2(s10 - m0), p20 = ex2(s20 - m0), p30 = ex2(s30 - m0);
+      const float p01 = ex2(s01 - m1), p11 = ex2(s11 - m1), p21 = ex2(s21 - m1), p31 = ex2(s31 - m1);
       l0 += (p00 + p10) + (p20 + p30);
       l1 += (p01 + p11) + (p21 + p31);
       const float w0 = ok0 ? vs[g] : 0.f, w1 = ok1 ? vs[g + 8] : 0.f;
@@ -420,10 +428,17 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
       pv16(st, 0, g, t, lanebase, pb0, pb1, pc0, pc1, oacc);
       p_frag(p20 * w2, p30 * w3, p21 * w2, p31 * w3, g, t, G, pb0, pb1, pc0, pc1);
       pv16(st, 16, g, t, lanebase, pb0, pb1, pc0, pc1, oacc);
+    };
+
+    for (; x < seg_end; ++x) {
+      cp_wait_one();
+      __syncwarp();
+      if (cw.tile * kTileTok + kTileTok <= n_valid) tile(std::integral_constant<bool, false>());
+      else tile(std::integral_constant<bool, true>());
       // ---- refill this stage with tile x + kStages ----
       __syncwarp();
       if (x + kStages < end) {
-        pr.issue(a, st0 + stage * kStageBytes, lane);
+        pr.issue(a, st0 + (int)((x - begin) & 1) * kStageBytes, lane);
         step(a, pr.w);
       }
       cp_commit();
