@@ -290,12 +290,14 @@ def run_ours(args):
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         ev0.record(s)
+        h0 = time.perf_counter()
         for _ in range(steps):
             step()
+        host_ms = (time.perf_counter() - h0) * 1e3 / steps
         ev1.record(s)
         ev1.synchronize()
     elapsed_ms = ev0.elapsed_time(ev1)
-    dec_ms, dec_n, app_ms, app_n = cache.timing(0)
+    dec_ms, dec_n, app_ms, app_n, other_ms = cache.timing(0)
     launches = cache.kernel_launches() - launches0
     ctx1 = cache.ring_state(0, 0)["view_len"]
     if world > 1:
@@ -364,6 +366,8 @@ def run_ours(args):
             "e2e": {"value": B / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_s * 1e3},
             "gpu_launches": launches,
+            "breakdown_ms_per_step": {"decode_attn": dec_ms / steps, "append": app_ms / steps,
+                                      "rotate_merge": other_ms / steps, "host_issue": host_ms},
             "clocks": clk.summary(),
             "fill_s": fill_s,
         }

@@ -240,12 +240,13 @@ int lc_merge_partials(lc_cache* cache, int32_t n_parts, int32_t n_rows, const fl
 int lc_cache_info(const lc_cache* cache, int32_t* device, void** stream, uint64_t* kernel_launches);
 
 /* Per-kernel device time from CUDA events recorded on the launching stream
- * around the split-K attention kernel and the quantize-append kernel.
+ * around the split-K attention kernel and the quantize-append kernel (and,
+ * in other_ms, the query rotation and partial-merge kernels of decode).
  * mode 1: start recording (clears earlier records); mode 0: stop and
  * report; mode 2: report and keep recording. Reporting synchronises the
  * recorded events. Any output pointer may be NULL. */
 int lc_cache_timing(lc_cache* cache, int32_t mode, double* decode_ms, uint64_t* decode_launches,
-                    double* append_ms, uint64_t* append_launches);
+                    double* append_ms, uint64_t* append_launches, double* other_ms);
 
 /* ---- the raw ring (native_cache.rs:65-335) ------------------------------
  * N parallel buffers of arbitrary row width moving in lockstep, with

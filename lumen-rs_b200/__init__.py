@@ -105,7 +105,7 @@ def lib():
         "lc_cache_destroy": (None, [vp]),
         "lc_cache_info": (C.c_int, [vp, C.POINTER(i32), pp, C.POINTER(u64)]),
         "lc_cache_timing": (C.c_int, [vp, i32, C.POINTER(C.c_double), C.POINTER(u64), C.POINTER(C.c_double),
-                                      C.POINTER(u64)]),
+                                      C.POINTER(u64), C.POINTER(C.c_double)]),
         "lc_store": (C.c_int, [vp, i32, i32, i32, vp, vp, i64]),
         "lc_attend_keys": (C.c_int, [vp, i32, i32, i32, vp, vp, i64]),
         "lc_attend_values": (C.c_int, [vp, i32, i32, i32, vp, i64, vp]),
@@ -314,10 +314,10 @@ class CudaKvCache:
 
     def timing(self, mode: int):
         """lc_cache_timing: 1 start, 0 stop+report, 2 report. Returns
-        (decode_ms, decode_launches, append_ms, append_launches)."""
-        dm, dn, am, an = C.c_double(), C.c_uint64(), C.c_double(), C.c_uint64()
-        _check(lib().lc_cache_timing(self._h, mode, C.byref(dm), C.byref(dn), C.byref(am), C.byref(an)))
-        return dm.value, dn.value, am.value, an.value
+        (decode_ms, decode_launches, append_ms, append_launches, other_ms)."""
+        dm, dn, am, an, om = C.c_double(), C.c_uint64(), C.c_double(), C.c_uint64(), C.c_double()
+        _check(lib().lc_cache_timing(self._h, mode, C.byref(dm), C.byref(dn), C.byref(am), C.byref(an), C.byref(om)))
+        return dm.value, dn.value, am.value, an.value, om.value
 
     def stream(self) -> int:
         s = C.c_void_p()

@@ -86,7 +86,7 @@ struct lc_cache {
   bool timing = false;
   std::vector<cudaEvent_t> ev_pool;
   size_t ev_used = 0;
-  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> t_decode, t_append;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> t_decode, t_append, t_other;
 
   cudaEvent_t take_event() {
     if (ev_used == ev_pool.size()) {
@@ -297,13 +297,14 @@ int lc_cache_info(const lc_cache* c, int32_t* device, void** stream, uint64_t* k
 }
 
 int lc_cache_timing(lc_cache* c, int32_t mode, double* decode_ms, uint64_t* decode_launches, double* append_ms,
-                    uint64_t* append_launches) {
+                    uint64_t* append_launches, double* other_ms) {
   return abi_guard([&] {
     LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
     LC_REQUIRE(mode >= 0 && mode <= 2, LC_ERR_INVALID, "timing mode must be 0, 1 or 2");
     if (mode == 1) {
       c->t_decode.clear();
       c->t_append.clear();
+      c->t_other.clear();
       c->ev_used = 0;
       c->timing = true;
       return;
@@ -322,6 +323,7 @@ int lc_cache_timing(lc_cache* c, int32_t mode, double* decode_ms, uint64_t* deco
     if (decode_launches) *decode_launches = c->t_decode.size();
     if (append_ms) *append_ms = sum(c->t_append);
     if (append_launches) *append_launches = c->t_append.size();
+    if (other_ms) *other_ms = sum(c->t_other);
     if (mode == 0) c->timing = false;
   });
 }
@@ -686,8 +688,10 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   c->q_rot.ensure((size_t)rows * D, s);
   c->q_h.ensure((size_t)rows * D, s);
   const float kalpha = plan.flat ? c->dk.alpha : 1.0f, valpha = plan.flat ? c->dv.alpha : 1.0f;
-  launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0,
-                  scale * 1.4426950408889634f / kalpha, c->q_rot.p, c->q_h.p, s);
+  c->timed(c->t_other, s, [&] {
+    launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0,
+                    scale * 1.4426950408889634f / kalpha, c->q_rot.p, c->q_h.p, s);
+  });
   ++c->launches;
   c->part.ensure((size_t)rows * plan.max_slots * (D + 2), s);
   DecodeArgs a;
@@ -741,8 +745,11 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
-                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, run.oscale, s);
+    c->timed(c->t_other, s, [&] {
+      launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
+                   (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, run.oscale,
+                   s);
+    });
     ++c->launches;
     if (host_out) {
       LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));

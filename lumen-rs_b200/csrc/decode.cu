@@ -56,17 +56,24 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 }
 
 // ---------------------------------------------------------------------------
-// q' = R q * qscale. Block: dim threads, 8 rows per block.
+// q' = R q * qscale. Block: dim threads, kRotRows rows; R^T staged in shared
+// memory when it fits (head_dim <= 128), else read through L1.
 // ---------------------------------------------------------------------------
-constexpr int kRotRows = 8;
+constexpr int kRotRows = 16;
 
-__global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const float* RT, int rotated,
-                           float qscale, float* q_rot, __half* q_h) {
-  extern __shared__ float sq[];  // [kRotRows][D]
+template <bool SMEM_R>
+__global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const float* RT, int rotated, float qscale,
+                           float* q_rot, __half* q_h) {
+  extern __shared__ __align__(16) float sq[];  // [kRotRows][D] (+ [D][D] R^T)
   const int i = threadIdx.x;
   const int r0 = blockIdx.x * kRotRows;
+  float* srt = sq + kRotRows * D;
   for (int r = 0; r < kRotRows; ++r)
     sq[r * D + i] = (r0 + r < n_rows) ? load_any(q, dtype, (int64_t)(r0 + r) * D + i) : 0.0f;
+  if (SMEM_R && !rotated) {
+    const float4* src = reinterpret_cast<const float4*>(RT);
+    for (int k = i; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(srt)[k] = __ldg(src + k);
+  }
   __syncthreads();
   float acc[kRotRows];
   if (rotated) {
@@ -75,10 +82,15 @@ __global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const fl
   } else {
 #pragma unroll
     for (int r = 0; r < kRotRows; ++r) acc[r] = 0.0f;
-    for (int j = 0; j < D; ++j) {
-      const float w = __ldg(RT + (int64_t)j * D + i);  // R[i][j]
+    for (int j = 0; j < D; j += 4) {
+      float w[4];
 #pragma unroll
-      for (int r = 0; r < kRotRows; ++r) acc[r] = fmaf(w, sq[r * D + j], acc[r]);
+      for (int u = 0; u < 4; ++u) w[u] = SMEM_R ? srt[(j + u) * D + i] : __ldg(RT + (int64_t)(j + u) * D + i);
+#pragma unroll
+      for (int r = 0; r < kRotRows; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(sq + r * D + j);
+        acc[r] = fmaf(w[0], x.x, fmaf(w[1], x.y, fmaf(w[2], x.z, fmaf(w[3], x.w, acc[r]))));
+      }
     }
   }
 #pragma unroll
@@ -598,7 +610,7 @@ __global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
 //   part + ((group * max_slots + c) * G + r % G) * PS,  c < cnt[group]
 // -> normalised (optionally un-rotated) output, and/or merged (m, l, o).
 // ---------------------------------------------------------------------------
-constexpr int kMergeRows = 8;
+constexpr int kMergeRows = 8;  // rows per merge block
 
 struct MergeDev {
   const float* part;
@@ -613,12 +625,18 @@ struct MergeDev {
   float* o_out;
 };
 
+template <bool SMEM_R>
 __global__ void k_merge(MergeDev a) {
-  extern __shared__ float so[];  // [kMergeRows][D]
+  extern __shared__ __align__(16) float so[];  // [kMergeRows][D] (+ [D][D] R)
   const int i = threadIdx.x;
   const int r0 = blockIdx.x * kMergeRows;
   const int D = a.D;
   const int PS = D + 2;
+  float* sr = so + kMergeRows * D;
+  if (SMEM_R && a.R && a.out) {
+    const float4* src = reinterpret_cast<const float4*>(a.R);
+    for (int k = i; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(sr)[k] = __ldg(src + k);
+  }
   for (int r = 0; r < kMergeRows; ++r) {
     const int row = r0 + r;
     float val = 0.f;
@@ -656,10 +674,15 @@ __global__ void k_merge(MergeDev a) {
   if (a.R) {
 #pragma unroll
     for (int r = 0; r < kMergeRows; ++r) acc[r] = 0.f;
-    for (int j = 0; j < D; ++j) {
-      const float w = __ldg(a.R + (int64_t)j * D + i);  // (R^T)[i][j] = R[j][i]
+    for (int j = 0; j < D; j += 4) {
+      float w[4];
 #pragma unroll
-      for (int r = 0; r < kMergeRows; ++r) acc[r] = fmaf(w, so[r * D + j], acc[r]);
+      for (int u = 0; u < 4; ++u) w[u] = SMEM_R ? sr[(j + u) * D + i] : __ldg(a.R + (int64_t)(j + u) * D + i);
+#pragma unroll
+      for (int r = 0; r < kMergeRows; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(so + r * D + j);
+        acc[r] = fmaf(w[0], x.x, fmaf(w[1], x.y, fmaf(w[2], x.z, fmaf(w[3], x.w, acc[r]))));
+      }
     }
   } else {
 #pragma unroll
@@ -769,8 +792,18 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
                      bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s) {
   if (n_rows <= 0) return;
   const int blocks = (n_rows + kRotRows - 1) / kRotRows;
-  k_rotate_q<<<blocks, dim, kRotRows * dim * sizeof(float), s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0,
-                                                                 qscale, q_rot, q_h);
+  const bool smem_r = dim <= 128;
+  const size_t smem = ((size_t)kRotRows * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    attr = true;
+  }
+  if (smem_r)
+    k_rotate_q<true><<<blocks, dim, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
+  else
+    k_rotate_q<false><<<blocks, dim, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
   LC_CUDA(cudaGetLastError());
 }
 
@@ -833,7 +866,16 @@ void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_
   if (n_rows <= 0) return;
   MergeDev d{part, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out, o_out};
   const int blocks = (n_rows + kMergeRows - 1) / kMergeRows;
-  k_merge<<<blocks, dim, kMergeRows * dim * sizeof(float), s>>>(d);
+  const bool smem_r = dim <= 128 && R && out;
+  const size_t smem = ((size_t)kMergeRows * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_merge<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_merge<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    attr = true;
+  }
+  if (smem_r) k_merge<true><<<blocks, dim, smem, s>>>(d);
+  else k_merge<false><<<blocks, dim, smem, s>>>(d);
   LC_CUDA(cudaGetLastError());
 }
 
