@@ -82,6 +82,7 @@ struct lc_cache {
   DevBuf<uint8_t> in_k, in_v, qbuf, outbuf, fetchbuf;
   DevBuf<float> q_rot, part, hook_a, hook_b, hook_c;
   DevBuf<__half> q_h;
+  std::vector<uint8_t> blob;  // host staging of one call's metadata
   // kernel timing (lc_cache_timing)
   bool timing = false;
   std::vector<cudaEvent_t> ev_pool;
@@ -191,8 +192,17 @@ void run_append(lc_cache* c, int32_t n_seqs, int32_t h_in, int32_t h_base, int64
   a.h_in = h_in;
   a.h_base = h_base;
   a.n_tok = n_tok;
-  a.dst_page = c->arena.put_vec(dst_page, s);
-  a.dst_row = c->arena.put_vec(dst_row, s);
+  {
+    // one upload: [page addresses u64 | rows i32]
+    const size_t n = dst_page.size();
+    std::vector<uint8_t>& blob = c->blob;
+    blob.resize(n * 12);
+    std::memcpy(blob.data(), dst_page.data(), n * 8);
+    std::memcpy(blob.data() + n * 8, dst_row.data(), n * 4);
+    const uint8_t* d = static_cast<const uint8_t*>(c->arena.put(blob.data(), blob.size(), s));
+    a.dst_page = reinterpret_cast<const uint64_t*>(d);
+    a.dst_row = reinterpret_cast<const int32_t*>(d + n * 8);
+  }
   a.layout = c->layout;
   a.role_words[0] = R_KW;
   a.role_words[1] = R_VW;
@@ -650,6 +660,7 @@ struct DecodeRun {
   int32_t rows = 0, G = 1, max_slots = 1;
   const int32_t* cnt = nullptr;
   float oscale = 1.0f;  // 1 / V table scale of the fast path
+  bool host_q = false;  // q was staged from host memory
 };
 
 static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
@@ -679,9 +690,16 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     lens[b] = n;
   }
   const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits);
-  const int64_t* dinfo = c->arena.put_vec(info, s);
-  const int64_t* dseg = plan.flat ? c->arena.put_vec(plan.seg, s) : nullptr;
-  const int32_t* dcnt = c->arena.put_vec(plan.cnt, s);
+  // one upload: [seqinfo i64 | seg i64 | cnt i32]
+  const size_t b_info = info.size() * 8, b_seg = plan.flat ? plan.seg.size() * 8 : 0, b_cnt = plan.cnt.size() * 4;
+  c->blob.resize(b_info + b_seg + b_cnt);
+  std::memcpy(c->blob.data(), info.data(), b_info);
+  if (b_seg) std::memcpy(c->blob.data() + b_info, plan.seg.data(), b_seg);
+  std::memcpy(c->blob.data() + b_info + b_seg, plan.cnt.data(), b_cnt);
+  const uint8_t* dblob = static_cast<const uint8_t*>(c->arena.put(c->blob.data(), c->blob.size(), s));
+  const int64_t* dinfo = reinterpret_cast<const int64_t*>(dblob);
+  const int64_t* dseg = plan.flat ? reinterpret_cast<const int64_t*>(dblob + b_info) : nullptr;
+  const int32_t* dcnt = reinterpret_cast<const int32_t*>(dblob + b_info + b_seg);
   const int64_t rows = (int64_t)n_seqs * n_q_heads;
   bool hq = false;
   const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
@@ -726,6 +744,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   r.max_slots = plan.max_slots;
   r.cnt = dcnt;
   r.oscale = 1.0f / valpha;
+  r.host_q = hq;
   return r;
 }
 
@@ -754,7 +773,7 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
     if (host_out) {
       LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
       LC_CUDA(cudaStreamSynchronize(s));
-    } else if (!is_device_ptr(q)) {
+    } else if (run.host_q) {
       LC_CUDA(cudaEventSynchronize(c->ev_copy));
     }
   });
@@ -785,7 +804,7 @@ int lc_decode_attn_partials(lc_cache* c, int32_t layer, int32_t n_seqs, const in
       LC_CUDA(cudaMemcpyAsync(l, dl, rows * 4, cudaMemcpyDefault, s));
       LC_CUDA(cudaMemcpyAsync(o, dov, (size_t)rows * D * 4, cudaMemcpyDefault, s));
       LC_CUDA(cudaStreamSynchronize(s));
-    } else if (!is_device_ptr(q)) {
+    } else if (run.host_q) {
       LC_CUDA(cudaEventSynchronize(c->ev_copy));
     }
   });

@@ -56,49 +56,55 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 }
 
 // ---------------------------------------------------------------------------
-// q' = R q * qscale. Block: dim threads, kRotRows rows; R^T staged in shared
-// memory when it fits (head_dim <= 128), else read through L1.
+// q' = R q * qscale. Block: 4*dim threads, kRotRows rows: thread (i, rg)
+// computes output i of rows rg, rg+4, ...; R^T is staged in shared memory
+// when it fits (head_dim <= 128), else read through L1.
 // ---------------------------------------------------------------------------
-constexpr int kRotRows = 16;
+constexpr int kRotRows = 32;
 
-template <bool SMEM_R>
+template <bool SMEM_R, int kRotGroups>
 __global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const float* RT, int rotated, float qscale,
                            float* q_rot, __half* q_h) {
   extern __shared__ __align__(16) float sq[];  // [kRotRows][D] (+ [D][D] R^T)
-  const int i = threadIdx.x;
+  const int i = threadIdx.x % D, rg = threadIdx.x / D;
   const int r0 = blockIdx.x * kRotRows;
   float* srt = sq + kRotRows * D;
-  for (int r = 0; r < kRotRows; ++r)
-    sq[r * D + i] = (r0 + r < n_rows) ? load_any(q, dtype, (int64_t)(r0 + r) * D + i) : 0.0f;
+  for (int k = threadIdx.x; k < kRotRows * D; k += blockDim.x) {
+    const int r = k / D;
+    sq[k] = (r0 + r < n_rows) ? load_any(q, dtype, (int64_t)r0 * D + k) : 0.0f;
+  }
   if (SMEM_R && !rotated) {
     const float4* src = reinterpret_cast<const float4*>(RT);
-    for (int k = i; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(srt)[k] = __ldg(src + k);
+#pragma unroll 4
+    for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(srt)[k] = __ldg(src + k);
   }
   __syncthreads();
-  float acc[kRotRows];
+  constexpr int RPT = kRotRows / kRotGroups;  // rows per thread
+  float acc[RPT];
   if (rotated) {
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r) acc[r] = sq[r * D + i];
+    for (int r = 0; r < RPT; ++r) acc[r] = sq[(rg + kRotGroups * r) * D + i];
   } else {
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r) acc[r] = 0.0f;
+    for (int r = 0; r < RPT; ++r) acc[r] = 0.0f;
     for (int j = 0; j < D; j += 4) {
       float w[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) w[u] = SMEM_R ? srt[(j + u) * D + i] : __ldg(RT + (int64_t)(j + u) * D + i);
 #pragma unroll
-      for (int r = 0; r < kRotRows; ++r) {
-        const float4 x = *reinterpret_cast<const float4*>(sq + r * D + j);
+      for (int r = 0; r < RPT; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(sq + (rg + kRotGroups * r) * D + j);
         acc[r] = fmaf(w[0], x.x, fmaf(w[1], x.y, fmaf(w[2], x.z, fmaf(w[3], x.w, acc[r]))));
       }
     }
   }
 #pragma unroll
-  for (int r = 0; r < kRotRows; ++r) {
-    if (r0 + r < n_rows) {
+  for (int r = 0; r < RPT; ++r) {
+    const int row = r0 + rg + kRotGroups * r;
+    if (row < n_rows) {
       const float v = acc[r] * qscale;
-      q_rot[(int64_t)(r0 + r) * D + i] = v;
-      q_h[(int64_t)(r0 + r) * D + i] = __float2half_rn(v);
+      q_rot[(int64_t)row * D + i] = v;
+      q_h[(int64_t)row * D + i] = __float2half_rn(v);
     }
   }
 }
@@ -610,7 +616,6 @@ __global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
 //   part + ((group * max_slots + c) * G + r % G) * PS,  c < cnt[group]
 // -> normalised (optionally un-rotated) output, and/or merged (m, l, o).
 // ---------------------------------------------------------------------------
-constexpr int kMergeRows = 8;  // rows per merge block
 
 struct MergeDev {
   const float* part;
@@ -625,72 +630,88 @@ struct MergeDev {
   float* o_out;
 };
 
+// One warp per row: every slot's (m, l) and o are read at once (lane c holds
+// slot c's max; each lane accumulates head_dim/32 contiguous dims), then the
+// block un-rotates its rows with R staged in shared memory.
+constexpr int kMergeWarps = 8;
+
 template <bool SMEM_R>
-__global__ void k_merge(MergeDev a) {
-  extern __shared__ __align__(16) float so[];  // [kMergeRows][D] (+ [D][D] R)
-  const int i = threadIdx.x;
-  const int r0 = blockIdx.x * kMergeRows;
+__global__ void __launch_bounds__(kMergeWarps * 32) k_merge(MergeDev a) {
+  extern __shared__ __align__(16) float so[];  // [kMergeWarps][D] (+ [D][D] R)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = a.D;
   const int PS = D + 2;
-  float* sr = so + kMergeRows * D;
+  const int per = D / 32;  // dims per lane
+  float* sr = so + kMergeWarps * D;
   if (SMEM_R && a.R && a.out) {
     const float4* src = reinterpret_cast<const float4*>(a.R);
-    for (int k = i; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(sr)[k] = __ldg(src + k);
+#pragma unroll 4
+    for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(sr)[k] = __ldg(src + k);
   }
-  for (int r = 0; r < kMergeRows; ++r) {
-    const int row = r0 + r;
-    float val = 0.f;
-    if (row < a.n_rows) {
-      const int64_t group = row / a.G;
-      const int gh = row % a.G;
-      const int n = a.cnt ? a.cnt[group] : a.max_slots;
-      const float* p = a.part + (group * a.max_slots * a.G + gh) * PS;
-      const int64_t cs = (int64_t)a.G * PS;
-      float M = -INFINITY;
-      for (int c = 0; c < n; ++c) M = fmaxf(M, p[c * cs]);
-      float L = 0.f, O = 0.f;
-      for (int c = 0; c < n; ++c) {
-        const float* pc = p + c * cs;
-        if (pc[0] == -INFINITY) continue;
-        const float w = exp2f(pc[0] - M);
-        L += w * pc[1];
-        O += w * pc[2 + i];
-      }
-      O *= a.oscale;
-      if (a.o_out) {
-        a.o_out[(int64_t)row * D + i] = O;
-        if (i == 0) {
-          a.m_out[row] = M;
-          a.l_out[row] = L;
-        }
-      }
-      val = L > 0.f ? O / L : 0.f;
+  const int row = blockIdx.x * kMergeWarps + warp;
+  float* orow = so + warp * D;
+  if (row < a.n_rows) {
+    const int64_t group = row / a.G;
+    const int gh = row % a.G;
+    const int n = a.cnt ? a.cnt[group] : a.max_slots;
+    const float* p = a.part + (group * a.max_slots * a.G + gh) * PS;
+    const int64_t cs = (int64_t)a.G * PS;
+    float M = -INFINITY;
+    for (int c = lane; c < n; c += 32) M = fmaxf(M, p[c * cs]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    float O[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) O[k] = 0.f;
+    for (int c = 0; c < n; ++c) {
+      const float* pc = p + c * cs;
+      const float mc = pc[0];
+      const float w = mc == -INFINITY ? 0.f : exp2f(mc - M);
+      L += w * pc[1];
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k < per) O[k] += w * pc[2 + lane * per + k];
     }
-    so[r * D + i] = val;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      if (k < per) {
+        const float ov = O[k] * a.oscale;
+        if (a.o_out) a.o_out[(int64_t)row * D + lane * per + k] = ov;
+        orow[lane * per + k] = L > 0.f ? ov / L : 0.f;
+      }
+    }
+    if (a.o_out && lane == 0) {
+      a.m_out[row] = M;
+      a.l_out[row] = L;
+    }
+  } else {
+    for (int k = lane; k < D; k += 32) orow[k] = 0.f;
   }
   if (!a.out) return;
   __syncthreads();
-  float acc[kMergeRows];
-  if (a.R) {
-#pragma unroll
-    for (int r = 0; r < kMergeRows; ++r) acc[r] = 0.f;
-    for (int j = 0; j < D; j += 4) {
-      float w[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) w[u] = SMEM_R ? sr[(j + u) * D + i] : __ldg(a.R + (int64_t)(j + u) * D + i);
-#pragma unroll
-      for (int r = 0; r < kMergeRows; ++r) {
-        const float4 x = *reinterpret_cast<const float4*>(so + r * D + j);
-        acc[r] = fmaf(w[0], x.x, fmaf(w[1], x.y, fmaf(w[2], x.z, fmaf(w[3], x.w, acc[r]))));
+  // out[row][i] = sum_j R[j][i] * o[row][j]
+  for (int idx = threadIdx.x; idx < kMergeWarps * D; idx += blockDim.x) {
+    const int r = idx / D, i = idx % D;
+    const int rr = blockIdx.x * kMergeWarps + r;
+    if (rr >= a.n_rows) continue;
+    float acc;
+    if (a.R) {
+      acc = 0.f;
+      const float* x = so + r * D;
+      for (int j = 0; j < D; j += 4) {
+        const float4 xv = *reinterpret_cast<const float4*>(x + j);
+        const float w0 = SMEM_R ? sr[j * D + i] : __ldg(a.R + (int64_t)j * D + i);
+        const float w1 = SMEM_R ? sr[(j + 1) * D + i] : __ldg(a.R + (int64_t)(j + 1) * D + i);
+        const float w2 = SMEM_R ? sr[(j + 2) * D + i] : __ldg(a.R + (int64_t)(j + 2) * D + i);
+        const float w3 = SMEM_R ? sr[(j + 3) * D + i] : __ldg(a.R + (int64_t)(j + 3) * D + i);
+        acc = fmaf(w0, xv.x, fmaf(w1, xv.y, fmaf(w2, xv.z, fmaf(w3, xv.w, acc))));
       }
+    } else {
+      acc = so[r * D + i];
     }
-  } else {
-#pragma unroll
-    for (int r = 0; r < kMergeRows; ++r) acc[r] = so[r * D + i];
+    store_any(a.out, a.out_dtype, (int64_t)rr * D + i, acc);
   }
-#pragma unroll
-  for (int r = 0; r < kMergeRows; ++r)
-    if (r0 + r < a.n_rows) store_any(a.out, a.out_dtype, (int64_t)(r0 + r) * D + i, acc[r]);
 }
 
 int g_num_sms = 0;
@@ -794,16 +815,20 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
   const int blocks = (n_rows + kRotRows - 1) / kRotRows;
   const bool smem_r = dim <= 128;
   const size_t smem = ((size_t)kRotRows * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
+  const int groups = dim <= 256 ? 4 : 2;  // threads = groups * dim <= 1024
+  const int threads = dim * groups;
   static bool attr = false;
   if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
     attr = true;
   }
-  if (smem_r)
-    k_rotate_q<true><<<blocks, dim, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
-  else
-    k_rotate_q<false><<<blocks, dim, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
+  const int rot = q_is_rotated ? 1 : 0;
+  if (smem_r) k_rotate_q<true, 4><<<blocks, threads, smem, s>>>(q, q_dtype, n_rows, dim, RT, rot, qscale, q_rot, q_h);
+  else if (groups == 4)
+    k_rotate_q<false, 4><<<blocks, threads, smem, s>>>(q, q_dtype, n_rows, dim, RT, rot, qscale, q_rot, q_h);
+  else k_rotate_q<false, 2><<<blocks, threads, smem, s>>>(q, q_dtype, n_rows, dim, RT, rot, qscale, q_rot, q_h);
   LC_CUDA(cudaGetLastError());
 }
 
@@ -865,17 +890,17 @@ void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_
                   float oscale, cudaStream_t s) {
   if (n_rows <= 0) return;
   MergeDev d{part, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out, o_out};
-  const int blocks = (n_rows + kMergeRows - 1) / kMergeRows;
+  const int blocks = (n_rows + kMergeWarps - 1) / kMergeWarps;
   const bool smem_r = dim <= 128 && R && out;
-  const size_t smem = ((size_t)kMergeRows * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
+  const size_t smem = ((size_t)kMergeWarps * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
   static bool attr = false;
   if (!attr) {
     LC_CUDA(cudaFuncSetAttribute(k_merge<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
     LC_CUDA(cudaFuncSetAttribute(k_merge<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
     attr = true;
   }
-  if (smem_r) k_merge<true><<<blocks, dim, smem, s>>>(d);
-  else k_merge<false><<<blocks, dim, smem, s>>>(d);
+  if (smem_r) k_merge<true><<<blocks, kMergeWarps * 32, smem, s>>>(d);
+  else k_merge<false><<<blocks, kMergeWarps * 32, smem, s>>>(d);
   LC_CUDA(cudaGetLastError());
 }
 
