@@ -221,6 +221,38 @@ int lc_decode_attn(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t
                    const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags,
                    void* out, int32_t out_dtype, void* stream);
 
+/* Bytes of the fixed device scratch lc_decode_attn_noalloc uses, per device. */
+#define LC_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* lc_decode_attn for callers that cannot allocate device memory while they
+ * decode: an engine that reserved all free HBM for its own pool before its
+ * serving loop (cudaMalloc then fails), or a loop that must not take the
+ * device-wide synchronisation of cudaFree. No counterpart in the reference:
+ * its decode runs inside MLX, which allocates per call.
+ *
+ * Same arguments, results and error codes as lc_decode_attn, except:
+ *  - q and out must be device memory (LC_ERR_INVALID otherwise).
+ *  - All scratch (rotated queries, split-K partials, per-call metadata) is a
+ *    fixed device array of LC_NOALLOC_SCRATCH_BYTES (32 MiB) per device plus
+ *    a fixed 1 MiB host staging array. A call that needs more returns
+ *    LC_ERR_NOMEM, with the bytes needed in lc_last_error(). The need is
+ *    about rows * head_dim * 6 + rows * splits * (head_dim + 2) * 4 bytes
+ *    for rows = n_seqs * n_q_heads, where splits is the number of split-K
+ *    partials per row (12 for 32 sequences x 8 kv heads at 8K tokens: about
+ *    7 MB in all).
+ *  - A successful call makes no cudaMalloc, cudaMallocHost or cudaFree and
+ *    calls no allocating library routine.
+ *  - The first call on a device sets the scratch up: with that device
+ *    current it looks up the array's address (cudaGetSymbolAddress). Make
+ *    that first call before any stream capture.
+ *  - Every call on a device, from any cache, uses the same scratch: calls
+ *    that overlap on the GPU (issued on different streams without ordering)
+ *    race and return wrong results. Issue them on one stream, or order them.
+ *  - The kernels it launches are not timed by lc_cache_timing. */
+int lc_decode_attn_noalloc(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+                           const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags,
+                           void* out, int32_t out_dtype, void* stream);
+
 /* Same, but stop before normalisation and return the softmax partials of
  * the whole local context per (seq, q head): m (log2 domain, max of
  * scale*log2(e)*score), l (sum of 2^(s-m)), o [head_dim] (unnormalised, in

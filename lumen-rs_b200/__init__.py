@@ -48,7 +48,7 @@ ABI_SYMBOLS = [
     "lc_codec_tables", "lc_codec_shape", "lc_codec_free", "lc_packed_words", "lc_cache_create",
     "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_values", "lc_seq_len", "lc_clear",
     "lc_truncate", "lc_append", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
-    "lc_decode_attn", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
+    "lc_decode_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
     "lc_ring_deep_clone", "lc_ring_destroy", "lc_version",
@@ -119,6 +119,7 @@ def lib():
         "lc_ring_state": (C.c_int, [vp, i32, i32, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
         "lc_fetch": (C.c_int, [vp, i32, i32, i32, C.POINTER(lc_fetch_out), i64, C.POINTER(i64)]),
         "lc_decode_attn": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
+        "lc_decode_attn_noalloc": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_partials": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, vp, vp, vp]),
         "lc_merge_partials": (C.c_int, [vp, i32, i32, vp, vp, vp, u32, vp, i32, vp]),
         "lc_ring_create": (C.c_int, [i32, i64, i64, i32, vp, i32, pp]),

@@ -861,4 +861,134 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
   });
 }
 
+// lc_decode_attn with every byte of scratch taken from fixed arrays
+// (noalloc.cu): for callers that cannot allocate device memory while they
+// decode. The work is lc_decode_attn's (query rotation, split-K partials,
+// merge); only where the scratch and the per-call metadata live differs.
+// Every slot the merge reads is written by the partials kernel first, so
+// nothing in the scratch has to start at zero.
+int lc_decode_attn_noalloc(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
+                           int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, void* out,
+                           int32_t out_dtype, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && seq_ids && q && out, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_seqs > 0, LC_ERR_INVALID, "n_seqs must be > 0");
+    const int32_t hkv = c->cfg.n_kv_heads, D = c->cfg.head_dim;
+    LC_REQUIRE(n_q_heads > 0 && n_q_heads % hkv == 0, LC_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads");
+    dtype_size(q_dtype);
+    dtype_size(out_dtype);
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    LC_REQUIRE(is_device_ptr(q) && is_device_ptr(out), LC_ERR_INVALID,
+               "lc_decode_attn_noalloc needs q and out in device memory");
+    std::lock_guard<std::mutex> lock(noalloc_mutex());
+    uint8_t* const dscr = noalloc_device_scratch(c->cfg.device);
+    uint8_t* const hst = noalloc_host_staging();
+    auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+
+    // host staging: [seqinfo i64 2n | lens i64 n | seg i64 n+1 | cnt i32 n*hkv] then dirty table rows
+    const size_t b_info = (size_t)n_seqs * 16, b_lens = (size_t)n_seqs * 8, b_seg = (size_t)(n_seqs + 1) * 8,
+                 b_cnt = (size_t)n_seqs * hkv * 4;
+    const size_t b_meta = b_info + b_lens + b_seg + b_cnt;
+    LC_REQUIRE(b_meta <= kNoallocHostBytes, LC_ERR_NOMEM,
+               "lc_decode_attn_noalloc: " + std::to_string(b_meta) + " bytes of metadata exceed the fixed " +
+                   std::to_string(kNoallocHostBytes) + "-byte host staging");
+    int64_t* info = reinterpret_cast<int64_t*>(hst);
+    int64_t* lens = reinterpret_cast<int64_t*>(hst + b_info);
+    int64_t* seg = reinterpret_cast<int64_t*>(hst + b_info + b_lens);
+    int32_t* cnt = reinterpret_cast<int32_t*>(hst + b_info + b_lens + b_seg);
+    size_t host_used = up(b_meta);
+    for (int32_t b = 0; b < n_seqs; ++b) {
+      const int32_t seq = seq_ids[b];
+      c->check(seq, layer);
+      const SeqLayer& sl = c->at(seq, layer);
+      int64_t n = sl.ring.view_len;
+      if (!sl.head_len.empty()) {
+        for (int64_t hl : sl.head_len)
+          LC_REQUIRE(hl == sl.head_len[0], LC_ERR_STATE, "heads of this layer hold different lengths");
+        n = sl.head_len[0];
+      }
+      LC_REQUIRE((int64_t)sl.ring.pages.size() <= c->cfg.max_pages_per_seq, LC_ERR_NOMEM,
+                 "sequence longer than max_pages_per_seq pages");
+      if (sl.dirty) host_used += up(sl.ring.pages.size() * 8);
+      info[2 * b] = n;
+      info[2 * b + 1] = (int64_t)layer * c->cfg.max_seqs + seq;
+      lens[b] = n;
+    }
+    LC_REQUIRE(host_used <= kNoallocHostBytes, LC_ERR_NOMEM,
+               "lc_decode_attn_noalloc: " + std::to_string(host_used) + " bytes of metadata and block-table rows " +
+                   "exceed the fixed " + std::to_string(kNoallocHostBytes) + "-byte host staging");
+    DecodePlan plan;
+    plan_decode_into(lens, n_seqs, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits, plan, seg, cnt);
+
+    // device scratch: [seqinfo | seg | cnt] [q_rot f32 rows*D] [q_h f16 rows*D] [partials f32 rows*slots*(D+2)]
+    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    const size_t d_meta = up(b_info + b_seg + b_cnt), d_qrot = up((size_t)rows * D * 4), d_qh = up((size_t)rows * D * 2),
+                 d_part = up((size_t)rows * plan.max_slots * (D + 2) * 4);
+    const size_t need = d_meta + d_qrot + d_qh + d_part;
+    LC_REQUIRE(need <= (size_t)LC_NOALLOC_SCRATCH_BYTES, LC_ERR_NOMEM,
+               "lc_decode_attn_noalloc: this call needs " + std::to_string(need) +
+                   " bytes of scratch; the fixed maximum is " + std::to_string((size_t)LC_NOALLOC_SCRATCH_BYTES) +
+                   " (LC_NOALLOC_SCRATCH_BYTES); split the batch or use lc_decode_attn");
+
+    // Checks done: from here on only device work is issued.
+    cudaStream_t s = c->pick(stream);
+    c->order(s);
+    size_t hoff = up(b_meta);
+    for (int32_t b = 0; b < n_seqs; ++b) {
+      SeqLayer& sl = c->at(seq_ids[b], layer);
+      if (!sl.dirty) continue;
+      const size_t np = sl.ring.pages.size();
+      uint64_t* addrs = reinterpret_cast<uint64_t*>(hst + hoff);
+      for (size_t i = 0; i < np; ++i) addrs[i] = c->pool.addr(sl.ring.pages[i]);
+      if (np) LC_CUDA(cudaMemcpyAsync(c->table_row(seq_ids[b], layer), addrs, np * 8, cudaMemcpyHostToDevice, s));
+      hoff += up(np * 8);
+      sl.dirty = false;
+    }
+    // one metadata copy, laid out [seqinfo | seg | cnt] on the device
+    uint8_t* const dmeta = dscr;
+    LC_CUDA(cudaMemcpyAsync(dmeta, info, b_info, cudaMemcpyHostToDevice, s));
+    LC_CUDA(cudaMemcpyAsync(dmeta + b_info, seg, b_seg + b_cnt, cudaMemcpyHostToDevice, s));
+    const int64_t* dinfo = reinterpret_cast<const int64_t*>(dmeta);
+    const int64_t* dseg = plan.flat ? reinterpret_cast<const int64_t*>(dmeta + b_info) : nullptr;
+    const int32_t* dcnt = reinterpret_cast<const int32_t*>(dmeta + b_info + b_seg);
+    float* const q_rot = reinterpret_cast<float*>(dscr + d_meta);
+    __half* const q_h = reinterpret_cast<__half*>(dscr + d_meta + d_qrot);
+    float* const part = reinterpret_cast<float*>(dscr + d_meta + d_qrot + d_qh);
+
+    const float kalpha = plan.flat ? c->dk.alpha : 1.0f, valpha = plan.flat ? c->dv.alpha : 1.0f;
+    launch_rotate_q(q, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0,
+                    scale * 1.4426950408889634f / kalpha, q_rot, q_h, s);
+    ++c->launches;
+    DecodeArgs a;
+    a.table = c->d_table;
+    a.table_stride = c->cfg.max_pages_per_seq;
+    a.seqinfo = dinfo;
+    a.seg = dseg;
+    a.layout = c->layout;
+    a.role_kw = R_KW;
+    a.role_vw = R_VW;
+    a.role_ks = R_KS;
+    a.role_vs = R_VS;
+    a.n_seqs = n_seqs;
+    a.hkv = hkv;
+    a.hq = n_q_heads;
+    a.dim = D;
+    a.kbits = (int)c->kc.bits;
+    a.vbits = (int)c->vc.bits;
+    a.q_rot = q_rot;
+    a.q_h = q_h;
+    a.kcent = c->dk.cent_d;
+    a.vcent = c->dv.cent_d;
+    a.kalpha = kalpha;
+    a.valpha = valpha;
+    a.part = part;
+    launch_decode_partials(a, plan, s);
+    ++c->launches;
+    launch_merge(part, dcnt, n_q_heads / hkv, plan.max_slots, (int32_t)rows, D,
+                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, out, out_dtype, nullptr, nullptr, nullptr,
+                 1.0f / valpha, s);
+    ++c->launches;
+  });
+}
+
 }  // extern "C"

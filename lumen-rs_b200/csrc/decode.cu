@@ -809,6 +809,42 @@ DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int di
   return p;
 }
 
+void plan_decode_into(const int64_t* lens, int n, int hkv, int hq, int dim, int kbits, int vbits, DecodePlan& p,
+                      int64_t* seg, int32_t* cnt) {
+  const int G = hq / hkv;
+  for (int64_t i = 0; i < (int64_t)n * hkv; ++i) cnt[i] = 0;
+  if (decode_fast_path(dim, kbits, vbits, G)) {
+    p.flat = true;
+    p.grid = num_sms();
+    seg[0] = 0;
+    for (int b = 0; b < n; ++b) seg[b + 1] = seg[b] + (int64_t)hkv * ((lens[b] + kTileTok - 1) / kTileTok);
+    p.total_tiles = seg[n];
+    const int64_t W = (int64_t)p.grid * kFlatWarps;
+    p.per_warp = p.total_tiles > 0 ? (p.total_tiles + W - 1) / W : 1;
+    int32_t mx = 1;
+    for (int b = 0; b < n; ++b) {
+      const int64_t nt = (lens[b] + kTileTok - 1) / kTileTok;
+      if (nt == 0) continue;
+      for (int h = 0; h < hkv; ++h) {
+        const int64_t s0 = seg[b] + (int64_t)h * nt;
+        const int32_t c = (int32_t)((s0 + nt - 1) / p.per_warp - s0 / p.per_warp + 1);
+        cnt[(size_t)b * hkv + h] = c;
+        mx = c > mx ? c : mx;
+      }
+    }
+    p.max_slots = mx;
+  } else {
+    p.flat = false;
+    int64_t mx = 0;
+    for (int b = 0; b < n; ++b) mx = lens[b] > mx ? lens[b] : mx;
+    const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
+    p.pages_per_chunk = 4;
+    p.n_chunks = (int32_t)((pages + 3) / 4 > 0 ? (pages + 3) / 4 : 1);
+    p.max_slots = p.n_chunks;
+    for (int64_t i = 0; i < (int64_t)n * hkv; ++i) cnt[i] = p.n_chunks;
+  }
+}
+
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* RT,
                      bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s) {
   if (n_rows <= 0) return;

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <vector>
 
 #include "common.h"
@@ -106,5 +107,21 @@ void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
                   float oscale, cudaStream_t s);
 bool decode_fast_path(int dim, int kbits, int vbits, int G);
+
+// ---- fixed scratch of lc_decode_attn_noalloc (noalloc.cu) -----------------
+// plan_decode's partition written into caller arrays seg [n + 1] (flat path
+// only) and cnt [n * hkv], with no allocation; p.seg / p.cnt stay empty.
+void plan_decode_into(const int64_t* lens, int n, int hkv, int hq, int dim, int kbits, int vbits, DecodePlan& p,
+                      int64_t* seg, int32_t* cnt);
+// Host staging bytes of one lc_decode_attn_noalloc call.
+constexpr size_t kNoallocHostBytes = size_t(1) << 20;
+// Held for the whole host side of an lc_decode_attn_noalloc call; guards
+// the staging array and the per-device set-up below.
+std::mutex& noalloc_mutex();
+uint8_t* noalloc_host_staging();
+// Device address of the LC_NOALLOC_SCRATCH_BYTES array on `device`, which
+// must be current; the first call per device looks it up
+// (cudaGetSymbolAddress). Call with noalloc_mutex() held.
+uint8_t* noalloc_device_scratch(int device);
 
 }  // namespace lc
