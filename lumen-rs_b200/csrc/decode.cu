@@ -246,6 +246,44 @@ struct Producer {
   }
 };
 
+// Producer with the next page address loaded ahead: a switch to the
+// following page of the same sequence, or to page 0 of the next kv head,
+// finds its address already in a register instead of waiting on a global
+// load.
+struct PrefetchProducer {
+  Walk w;
+  const uint8_t* page;
+  int page_b, page_idx;
+  uint64_t next;  // address of page next_idx of sequence next_b
+  int next_b, next_idx;
+
+  __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
+    const int pidx = w.tile >> 3;
+    if (pidx != page_idx || w.b != page_b) {
+      const uint64_t* trow = a.table + a.seqinfo[2 * w.b + 1] * a.table_stride;
+      page = reinterpret_cast<const uint8_t*>((w.b == next_b && pidx == next_idx) ? next : __ldg(trow + pidx));
+      page_idx = pidx;
+      page_b = w.b;
+      const int npages = (w.nt + 7) >> 3;
+      next_b = w.b;
+      next_idx = pidx + 1 < npages ? pidx + 1 : 0;
+      next = __ldg(trow + next_idx);
+    }
+    const int64_t hr = (int64_t)w.kvh * kPageTokens + (w.tile & 7) * kTileTok;
+    const uint8_t* k = page + a.off_kw + hr * 64;
+    const uint8_t* v = page + a.off_vw + hr * 64;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = lane + 32 * q;  // 16-byte chunk: row c >> 2, part c & 3
+      cp_async16(st + kStK + c * 16, k + c * 16);
+      const int r = c >> 2;
+      cp_async16(st + kStV + r * 64 + (((c & 3) ^ (r & 2)) << 4), v + c * 16);
+    }
+    if (lane < 8) cp_async16(st + kStKs + lane * 16, page + a.off_ks + hr * 4 + lane * 16);
+    else if (lane < 16) cp_async16(st + kStVs + (lane - 8) * 16, page + a.off_vs + hr * 4 + (lane - 8) * 16);
+  }
+};
+
 // 16 tokens of the tile (rows r0..r0+15): S^T = K_dq Q^T into sc.
 __device__ __forceinline__ void qk16(const uint8_t* st, int r0, int g, int t, uint32_t lanebase,
                                      const uint32_t (&qb)[8][2], float* sc) {
@@ -319,6 +357,243 @@ __device__ __forceinline__ void p_frag(float p00, float p10, float p01, float p1
   pc0 = odd ? y01 : y00;
   pc1 = odd ? y11 : y10;
   if (g >= G) pb0 = pb1 = pc0 = pc1 = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Pair layout for G <= 4. The MMA's 8 columns carry (head, part) pairs,
+// n = 2 * head + part: part 0 is the f16 value and part 1 its f16 residual,
+// for q in S^T = K_dq Q^T and for p' in O^T = V_dq^T P^T. Adding the two
+// columns back gives f32-accurate q and p' at no extra MMA, and lane (g, t)
+// then owns head t: scores of tokens g, g + 8 (+16, +24) and output
+// columns 2t, 2t + 1 (dims 16g .. 16g + 15).
+// ---------------------------------------------------------------------------
+
+// 16 tokens (rows r0..r0+15) into two independent accumulators (even and
+// odd k steps), so consecutive MMAs do not wait on each other.
+__device__ __forceinline__ void qk16_2(const uint8_t* st, int r0, int g, int t, uint32_t lanebase,
+                                       const uint32_t (&qb)[8][2], float* c0, float* c1) {
+  const uint4 k0 = *reinterpret_cast<const uint4*>(st + kStK + (r0 + g) * 64 + 16 * t);
+  const uint4 k1 = *reinterpret_cast<const uint4*>(st + kStK + (r0 + g + 8) * 64 + 16 * t);
+  const uint32_t kx[4] = {k0.x, k0.y, k0.z, k0.w};
+  const uint32_t ky[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t a0 = lut_k(kx[j], lanebase, 2 * h);
+      const uint32_t a2 = lut_k(kx[j], lanebase, 2 * h + 1);
+      const uint32_t a1 = lut_k(ky[j], lanebase, 2 * h);
+      const uint32_t a3 = lut_k(ky[j], lanebase, 2 * h + 1);
+      mma16816(h ? c1 : c0, a0, a1, a2, a3, qb[2 * j + h][0], qb[2 * j + h][1]);
+    }
+  }
+}
+
+// 16 tokens (rows r0..r0+15): O^T += V_dq^T P^T, one MMA per dim tile.
+__device__ __forceinline__ void pv16_1(const uint8_t* st, int r0, int g, int t, uint32_t lanebase, uint32_t pb0,
+                                       uint32_t pb1, float (&oacc)[8][4]) {
+  auto vrow = [&](int r) -> uint2 {
+    return *reinterpret_cast<const uint2*>(st + kStV + r * 64 + ((((g >> 1) ^ (r & 2))) << 4) + (g & 1) * 8);
+  };
+  const uint2 v0 = vrow(r0 + t), v1 = vrow(r0 + t + 8), v2 = vrow(r0 + t + 4), v3 = vrow(r0 + t + 12);
+  uint32_t ev[2][2], od[2][2];
+  const uint32_t A0[2] = {v0.x, v0.y}, B0[2] = {v1.x, v1.y};
+  const uint32_t A1[2] = {v2.x, v2.y}, B1[2] = {v3.x, v3.y};
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    ev[0][hh] = (A0[hh] & 0x0F0F0F0Fu) | ((B0[hh] & 0x0F0F0F0Fu) << 4);
+    od[0][hh] = ((A0[hh] >> 4) & 0x0F0F0F0Fu) | (B0[hh] & 0xF0F0F0F0u);
+    ev[1][hh] = (A1[hh] & 0x0F0F0F0Fu) | ((B1[hh] & 0x0F0F0F0Fu) << 4);
+    od[1][hh] = ((A1[hh] >> 4) & 0x0F0F0F0Fu) | (B1[hh] & 0xF0F0F0F0u);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int hh = i >> 2;
+    const uint32_t k = (uint32_t)(i & 3);
+    const uint32_t a0 = lut_v(ev[0][hh], lanebase, k);
+    const uint32_t a1 = lut_v(od[0][hh], lanebase, k);
+    const uint32_t a2 = lut_v(ev[1][hh], lanebase, k);
+    const uint32_t a3 = lut_v(od[1][hh], lanebase, k);
+    mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
+  }
+}
+
+// P^T B fragments of column g = 2 * head + part for k slots (2t, 2t+1) =
+// tokens (t, t+8) and (2t+8, 2t+9) = tokens (t+4, t+12) of a 16-token half.
+// This lane holds p' of its own head t for tokens (g, g+8): pu, pv.
+__device__ __forceinline__ void p_pairs(float pu, float pv, int g, int t, int G, uint32_t& pb0, uint32_t& pb1) {
+  const __half2 hi = __floats2half2_rn(pu, pv);
+  const float2 f = __half22float2(hi);
+  const uint32_t h = h2_as_u32(hi), l = h2_as_u32(__floats2half2_rn(pu - f.x, pv - f.y));
+  const int head = g >> 1;
+  const int src0 = t * 4 + head, src1 = (t + 4) * 4 + head;
+  const uint32_t x0 = __shfl_sync(0xffffffffu, h, src0), y0 = __shfl_sync(0xffffffffu, l, src0);
+  const uint32_t x1 = __shfl_sync(0xffffffffu, h, src1), y1 = __shfl_sync(0xffffffffu, l, src1);
+  const bool lo = g & 1;
+  pb0 = lo ? y0 : x0;
+  pb1 = lo ? y1 : x1;
+  if (head >= G) pb0 = pb1 = 0u;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(DecodeDev a) {
+  static_assert(G >= 1 && G <= 4, "pair layout holds 4 heads");
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int D = 128;
+  constexpr int PS = D + 2;
+  const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+  const uint32_t lut_off = (65536u - (s0 & 0xFFFFu)) & 0xFFFFu;
+  const int n_before = (int)(lut_off / kWarpBytes);
+  uint8_t* lut = smem + lut_off;
+
+  for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
+    const int e = idx >> 6, slot = idx & 63;
+    const float* cent = slot < 32 ? a.kcent : a.vcent;
+    const float al = slot < 32 ? a.kalpha : a.valpha;
+    reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(cent[e & 15] * al, cent[e >> 4] * al));
+  }
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
+  const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
+  const int64_t begin = w * a.per_warp;
+  const int64_t end = min(begin + a.per_warp, a.total_tiles);
+  if (begin >= end) return;
+  uint8_t* stages = warp < n_before ? smem + warp * kWarpBytes
+                                    : smem + lut_off + kLutBytes + (warp - n_before) * kWarpBytes;
+  const uint32_t st0 = (uint32_t)__cvta_generic_to_shared(stages);
+
+  PrefetchProducer pr;
+  pr.w = locate(a, begin);
+  pr.page = nullptr;
+  pr.page_b = -1;
+  pr.page_idx = -1;
+  pr.next = 0;
+  pr.next_b = -1;
+  pr.next_idx = -1;
+  Walk cw = pr.w;
+#pragma unroll
+  for (int s = 0; s < kStages; ++s) {
+    if (begin + s < end) {
+      pr.issue(a, st0 + s * kStageBytes, lane);
+      step(a, pr.w);
+    }
+    cp_commit();
+  }
+
+  int64_t x = begin;
+  while (x < end) {
+    // ---- a new (sequence, kv head) segment ----
+    const int b = cw.b, kvh = cw.kvh;
+    const int n_valid = (int)a.seqinfo[2 * b];
+    const int64_t seg_first = a.seg[b] + (int64_t)kvh * cw.nt;
+    const int64_t seg_end = min(end, seg_first + cw.nt);
+    const int64_t slot_base = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / a.per_warp);
+    // B fragments of Q: column g = (head g/2, part g&1), dims 32t + 4s + {0,1} / {2,3}
+    uint32_t qb[8][2];
+    {
+      const int head = g >> 1;
+      const bool lo = g & 1;
+      const float* qrow = a.q_rot + ((int64_t)b * a.hq + (int64_t)kvh * G + (head < G ? head : 0)) * D + 32 * t;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const float4 v = *reinterpret_cast<const float4*>(qrow + 4 * s);
+        const __half2 h01 = __floats2half2_rn(v.x, v.y), h23 = __floats2half2_rn(v.z, v.w);
+        uint32_t r0 = h2_as_u32(h01), r1 = h2_as_u32(h23);
+        if (lo) {
+          const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+          r0 = h2_as_u32(__floats2half2_rn(v.x - f01.x, v.y - f01.y));
+          r1 = h2_as_u32(__floats2half2_rn(v.z - f23.x, v.w - f23.y));
+        }
+        qb[s][0] = head < G ? r0 : 0u;
+        qb[s][1] = head < G ? r1 : 0u;
+      }
+    }
+    float m = -INFINITY, l = 0.f;
+    float oacc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+
+    auto tile = [&](auto masked) {
+      constexpr bool MASKED = decltype(masked)::value;
+      const int stage = (int)((x - begin) & 1);
+      const int tok = cw.tile * kTileTok;
+      const uint8_t* st = stages + stage * kStageBytes;
+      float sa0[4] = {0.f, 0.f, 0.f, 0.f}, sa1[4] = {0.f, 0.f, 0.f, 0.f};
+      float sb0[4] = {0.f, 0.f, 0.f, 0.f}, sb1[4] = {0.f, 0.f, 0.f, 0.f};
+      qk16_2(st, 0, g, t, lanebase, qb, sa0, sa1);
+      qk16_2(st, 16, g, t, lanebase, qb, sb0, sb1);
+      const float* ks = reinterpret_cast<const float*>(st + kStKs);
+      const float* vs = reinterpret_cast<const float*>(st + kStVs);
+      // this lane: head t, tokens u0 = g, u1 = g + 8, u2 = 16 + g, u3 = 24 + g
+      const bool ok0 = !MASKED || tok + g < n_valid, ok1 = !MASKED || tok + g + 8 < n_valid;
+      const bool ok2 = !MASKED || tok + g + 16 < n_valid, ok3 = !MASKED || tok + g + 24 < n_valid;
+      const float z0 = ((sa0[0] + sa1[0]) + (sa0[1] + sa1[1])) * ks[g];
+      const float z1 = ((sa0[2] + sa1[2]) + (sa0[3] + sa1[3])) * ks[g + 8];
+      const float z2 = ((sb0[0] + sb1[0]) + (sb0[1] + sb1[1])) * ks[g + 16];
+      const float z3 = ((sb0[2] + sb1[2]) + (sb0[3] + sb1[3])) * ks[g + 24];
+      const float s0_ = ok0 ? z0 : -INFINITY, s1_ = ok1 ? z1 : -INFINITY;
+      const float s2_ = ok2 ? z2 : -INFINITY, s3_ = ok3 ? z3 : -INFINITY;
+      float mx = fmaxf(fmaxf(s0_, s1_), fmaxf(s2_, s3_));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      if (mx > m + kTau) {
+        const float al = ex2(m - mx);
+        l *= al;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          oacc[i][0] *= al;
+          oacc[i][1] *= al;
+          oacc[i][2] *= al;
+          oacc[i][3] *= al;
+        }
+        m = mx;
+      }
+      const float p0 = ex2(s0_ - m), p1 = ex2(s1_ - m), p2 = ex2(s2_ - m), p3 = ex2(s3_ - m);
+      l += (p0 + p1) + (p2 + p3);
+      const float w0 = ok0 ? vs[g] : 0.f, w1 = ok1 ? vs[g + 8] : 0.f;
+      const float w2 = ok2 ? vs[g + 16] : 0.f, w3 = ok3 ? vs[g + 24] : 0.f;
+      uint32_t pb0, pb1;
+      p_pairs(p0 * w0, p1 * w1, g, t, G, pb0, pb1);
+      pv16_1(st, 0, g, t, lanebase, pb0, pb1, oacc);
+      p_pairs(p2 * w2, p3 * w3, g, t, G, pb0, pb1);
+      pv16_1(st, 16, g, t, lanebase, pb0, pb1, oacc);
+    };
+
+    for (; x < seg_end; ++x) {
+      cp_wait_one();
+      __syncwarp();
+      if (cw.tile * kTileTok + kTileTok <= n_valid) tile(std::integral_constant<bool, false>());
+      else tile(std::integral_constant<bool, true>());
+      __syncwarp();
+      if (x + kStages < end) {
+        pr.issue(a, st0 + (int)((x - begin) & 1) * kStageBytes, lane);
+        step(a, pr.w);
+      }
+      cp_commit();
+      step(a, cw);
+    }
+    // ---- flush the segment's partial: head t, dims 16g + 2i (+1) ----
+    float L = l;
+    L += __shfl_xor_sync(0xffffffffu, L, 4);
+    L += __shfl_xor_sync(0xffffffffu, L, 8);
+    L += __shfl_xor_sync(0xffffffffu, L, 16);
+    if (t < G) {
+      float* row = a.part + (slot_base * G + t) * PS;
+      if (g == 0) {
+        row[0] = m;
+        row[1] = L;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float2*>(row + 2 + 16 * g + 2 * i) =
+            make_float2(oacc[i][0] + oacc[i][1], oacc[i][2] + oacc[i][3]);
+    }
+  }
+  cp_wait_all();
 }
 
 template <int G>
@@ -727,6 +1002,17 @@ void launch_flat_g(const DecodeDev& d, int grid, cudaStream_t s) {
   LC_CUDA(cudaGetLastError());
 }
 
+template <int G>
+void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_decode_pair<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlatSmem));
+    attr = true;
+  }
+  k_decode_pair<G><<<(unsigned)grid, kFlatWarps * 32, kFlatSmem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
+}
+
 template <int KPL, int GS>
 void launch_generic_t(const DecodeDev& d, cudaStream_t s) {
   const int nw = 4;
@@ -902,10 +1188,10 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
   if (p.flat) {
     if (p.total_tiles == 0) return;
     switch (d.G) {
-      case 1: return launch_flat_g<1>(d, p.grid, s);
-      case 2: return launch_flat_g<2>(d, p.grid, s);
-      case 3: return launch_flat_g<3>(d, p.grid, s);
-      case 4: return launch_flat_g<4>(d, p.grid, s);
+      case 1: return launch_pair_g<1>(d, p.grid, s);
+      case 2: return launch_pair_g<2>(d, p.grid, s);
+      case 3: return launch_pair_g<3>(d, p.grid, s);
+      case 4: return launch_pair_g<4>(d, p.grid, s);
       case 5: return launch_flat_g<5>(d, p.grid, s);
       case 6: return launch_flat_g<6>(d, p.grid, s);
       case 7: return launch_flat_g<7>(d, p.grid, s);
