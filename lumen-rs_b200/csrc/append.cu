@@ -254,18 +254,26 @@ __global__ void k_append_strict(AppendDev a) {
 }
 
 // Small appends (decode steps: a few hundred vectors): one warp per vector so
-// every vector's chains run concurrently, 16 vectors per CTA sharing the
+// every vector's chains run concurrently, kWarpVecs vectors per CTA sharing the
 // tables staged once in shared memory (TAB) or read through L1. Lane l owns
 // outputs l, l+32, ...; sequential sums of squares are formed as exact
 // products in parallel and added in order by lane 0 (the same f32 result
 // as the reference's fold). Operation order as k_append_strict.
-constexpr int kWarpVecs = 16;
+constexpr int kWarpVecs = 4;
 
 __device__ __forceinline__ float seq_sum(const float* v, int n, float init) {
   float s = init;
 #pragma unroll 8
   for (int k = 0; k < n; ++k) s = __fadd_rn(s, v[k]);
   return s;
+}
+
+// n16 16-byte chunks global -> shared with cp.async, issued without waiting.
+__device__ __forceinline__ void stage16(void* dst, const void* src, int n16) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  const char* g = static_cast<const char*>(src);
+  for (int k = threadIdx.x; k < n16; k += blockDim.x)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d + k * 16), "l"(g + (size_t)k * 16) : "memory");
 }
 
 template <int R, bool TAB>  // R = head_dim / 32
@@ -295,19 +303,18 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(AppendDev a) 
     for (int k = threadIdx.x; k < n1; k += blockDim.x) sthr[k] = c.thr[k];
     for (int k = threadIdx.x; k <= n1; k += blockDim.x) scent[k] = c.cent[k];
     if (TAB) {
-      const float4* src = reinterpret_cast<const float4*>(c.RT);
-      float4* dst = reinterpret_cast<float4*>(tab);
-      for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) dst[k] = __ldg(src + k);
+      // all table copies in flight at once: one L2 round trip
+      stage16(tab, c.RT, D * D / 4);
       RT = tab;
       if (stage2) {
         float* tr = tab + D * D;
-        const float4* s2 = reinterpret_cast<const float4*>(c.R);
-        for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(tr)[k] = __ldg(s2 + k);
         float* tp = tr + D * D;
-        for (int k = threadIdx.x; k < D * M; k += blockDim.x) tp[k] = __ldg(c.PT + k);
+        stage16(tr, c.R, D * D / 4);
+        stage16(tp, c.PT, D * M / 4);
         Rm = tr;
         PT = tp;
       }
+      asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
     }
   }
   __syncthreads();

@@ -82,6 +82,7 @@ struct lc_cache {
   DevBuf<uint8_t> in_k, in_v, qbuf, outbuf, fetchbuf;
   DevBuf<float> q_rot, part, hook_a, hook_b, hook_c;
   DevBuf<__half> q_h;
+  DevBuf<int32_t> ctr;  // fused decode arrival counters (zero between launches)
   std::vector<uint8_t> blob;  // host staging of one call's metadata
   // kernel timing (lc_cache_timing)
   bool timing = false;
@@ -661,10 +662,14 @@ struct DecodeRun {
   const int32_t* cnt = nullptr;
   float oscale = 1.0f;  // 1 / V table scale of the fast path
   bool host_q = false;  // q was staged from host memory
+  bool fused = false;   // the output is written: no merge launch needed
 };
 
+// fused_out: device output of a full attention call (lc_decode_attn), which
+// the one-launch kernel writes when the plan allows; null for partials.
 static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
-                               int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s) {
+                               int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s,
+                               void* fused_out = nullptr, int32_t out_dtype = LC_F32) {
   LC_REQUIRE(c && seq_ids && q, LC_ERR_INVALID, "null argument");
   LC_REQUIRE(n_seqs > 0, LC_ERR_INVALID, "n_seqs must be > 0");
   const int32_t hkv = c->cfg.n_kv_heads;
@@ -690,33 +695,49 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     lens[b] = n;
   }
   const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits);
-  // one upload: [seqinfo i64 | seg i64 | cnt i32]
-  const size_t b_info = info.size() * 8, b_seg = plan.flat ? plan.seg.size() * 8 : 0, b_cnt = plan.cnt.size() * 4;
-  c->blob.resize(b_info + b_seg + b_cnt);
-  std::memcpy(c->blob.data(), info.data(), b_info);
-  if (b_seg) std::memcpy(c->blob.data() + b_info, plan.seg.data(), b_seg);
-  std::memcpy(c->blob.data() + b_info + b_seg, plan.cnt.data(), b_cnt);
-  const uint8_t* dblob = static_cast<const uint8_t*>(c->arena.put(c->blob.data(), c->blob.size(), s));
-  const int64_t* dinfo = reinterpret_cast<const int64_t*>(dblob);
-  const int64_t* dseg = plan.flat ? reinterpret_cast<const int64_t*>(dblob + b_info) : nullptr;
-  const int32_t* dcnt = reinterpret_cast<const int32_t*>(dblob + b_info + b_seg);
+  const bool fused = fused_out && decode_fusable(plan, n_q_heads / hkv);
+  // The one-launch path of small calls passes its arrays in the launch
+  // parameters; otherwise one upload: [seqinfo i64 | seg i64 | cnt i32].
+  const bool inl = fused && decode_inline_fits(n_seqs, hkv);
+  const int64_t* dinfo = nullptr;
+  const int64_t* dseg = nullptr;
+  const int32_t* dcnt = nullptr;
+  if (!inl) {
+    const size_t b_info = info.size() * 8, b_seg = plan.flat ? plan.seg.size() * 8 : 0, b_cnt = plan.cnt.size() * 4;
+    c->blob.resize(b_info + b_seg + b_cnt);
+    std::memcpy(c->blob.data(), info.data(), b_info);
+    if (b_seg) std::memcpy(c->blob.data() + b_info, plan.seg.data(), b_seg);
+    std::memcpy(c->blob.data() + b_info + b_seg, plan.cnt.data(), b_cnt);
+    const uint8_t* dblob = static_cast<const uint8_t*>(c->arena.put(c->blob.data(), c->blob.size(), s));
+    dinfo = reinterpret_cast<const int64_t*>(dblob);
+    dseg = plan.flat ? reinterpret_cast<const int64_t*>(dblob + b_info) : nullptr;
+    dcnt = reinterpret_cast<const int32_t*>(dblob + b_info + b_seg);
+  }
   const int64_t rows = (int64_t)n_seqs * n_q_heads;
   bool hq = false;
   const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
-  c->q_rot.ensure((size_t)rows * D, s);
-  c->q_h.ensure((size_t)rows * D, s);
   const float kalpha = plan.flat ? c->dk.alpha : 1.0f, valpha = plan.flat ? c->dv.alpha : 1.0f;
-  c->timed(c->t_other, s, [&] {
-    launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0,
-                    scale * 1.4426950408889634f / kalpha, c->q_rot.p, c->q_h.p, s);
-  });
-  ++c->launches;
+  const float qscale = scale * 1.4426950408889634f / kalpha;
+  if (!fused) {
+    c->q_rot.ensure((size_t)rows * D, s);
+    c->q_h.ensure((size_t)rows * D, s);
+    c->timed(c->t_other, s, [&] {
+      launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0, qscale, c->q_rot.p,
+                      c->q_h.p, s);
+    });
+    ++c->launches;
+  }
   c->part.ensure((size_t)rows * plan.max_slots * (D + 2), s);
   DecodeArgs a;
   a.table = c->d_table;
   a.table_stride = c->cfg.max_pages_per_seq;
   a.seqinfo = dinfo;
   a.seg = dseg;
+  if (inl) {
+    a.h_seqinfo = info.data();
+    a.h_seg = plan.seg.data();
+    a.h_cnt = plan.cnt.data();
+  }
   a.layout = c->layout;
   a.role_kw = R_KW;
   a.role_vw = R_VW;
@@ -735,10 +756,35 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   a.kalpha = kalpha;
   a.valpha = valpha;
   a.part = c->part.p;
-  c->timed(c->t_decode, s, [&] { launch_decode_partials(a, plan, s); });
+  if (fused) {
+    const size_t nctr = (size_t)n_seqs * hkv, before = c->ctr.n;
+    c->ctr.ensure(nctr, s);
+    if (c->ctr.n != before) LC_CUDA(cudaMemsetAsync(c->ctr.p, 0, c->ctr.n * sizeof(int32_t), s));
+    const size_t esz = dtype_size(out_dtype);
+    for (int32_t b = 0; b < n_seqs; ++b)  // rows of empty sequences are zero
+      if (lens[b] == 0)
+        LC_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(fused_out) + (size_t)b * n_q_heads * D * esz, 0,
+                                (size_t)n_q_heads * D * esz, s));
+    FusedArgs f;
+    f.q = dq;
+    f.q_dtype = q_dtype;
+    f.q_rotated = (flags & LC_Q_ROTATED) ? 1 : 0;
+    f.qscale = qscale;
+    f.qRT = c->dk.RTd;
+    f.vR = (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R;
+    f.cnt = dcnt;
+    f.ctr = c->ctr.p;
+    f.out = fused_out;
+    f.out_dtype = out_dtype;
+    f.oscale = 1.0f / valpha;
+    c->timed(c->t_decode, s, [&] { launch_decode_fused(a, plan, f, s); });
+  } else {
+    c->timed(c->t_decode, s, [&] { launch_decode_partials(a, plan, s); });
+  }
   ++c->launches;
   if (hq) LC_CUDA(cudaEventRecord(c->ev_copy, s));
   DecodeRun r;
+  r.fused = fused;
   r.rows = (int32_t)rows;
   r.G = n_q_heads / hkv;
   r.max_slots = plan.max_slots;
@@ -754,9 +800,10 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
   return abi_guard([&] {
     LC_REQUIRE(out, LC_ERR_INVALID, "null out");
     cudaStream_t s = c ? c->pick(stream) : nullptr;
-    const DecodeRun run = decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s);
+    LC_REQUIRE(c && n_q_heads > 0 && n_seqs > 0, LC_ERR_INVALID, "bad decode arguments");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
     const int32_t D = c->cfg.head_dim;
-    const int64_t rows = run.rows;
+    const int64_t rows = (int64_t)n_seqs * n_q_heads;
     const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
     const bool host_out = !is_device_ptr(out);
     void* dout = out;
@@ -764,12 +811,16 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    c->timed(c->t_other, s, [&] {
-      launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
-                   (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr, run.oscale,
-                   s);
-    });
-    ++c->launches;
+    const DecodeRun run =
+        decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, dout, out_dtype);
+    if (!run.fused) {
+      c->timed(c->t_other, s, [&] {
+        launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
+                     (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr,
+                     run.oscale, s);
+      });
+      ++c->launches;
+    }
     if (host_out) {
       LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
       LC_CUDA(cudaStreamSynchronize(s));

@@ -9,7 +9,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/lumen_cuda.h"
+#include "lumen_cuda.h"
 
 namespace lc {
 

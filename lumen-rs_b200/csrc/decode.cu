@@ -30,7 +30,9 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
+#include <cstring>
 #include <type_traits>
 
 #include "kernels.h"
@@ -56,51 +58,56 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 }
 
 // ---------------------------------------------------------------------------
-// q' = R q * qscale. Block: 4*dim threads, kRotRows rows: thread (i, rg)
-// computes output i of rows rg, rg+4, ...; R^T is staged in shared memory
-// when it fits (head_dim <= 128), else read through L1.
+// q' = R q * qscale for kRotRows rows per block of head_dim threads: thread
+// i computes output i of every row, reading R^T[j][i] straight from global
+// memory (coalesced; R^T is L2-resident) and the rows from shared memory
+// (broadcast). Small blocks keep the whole GPU busy at decode batch sizes.
 // ---------------------------------------------------------------------------
-constexpr int kRotRows = 32;
+constexpr int kRotRows = 8;
+// acc[r] += sum_{u < C} M[(j0 + u) * D + i] * x[r][j0 + u] for NR rows of x in
+// shared memory (row stride D): the C loads of M are all in flight before the
+// first multiply, one L2 round trip per call.
+template <int C, int NR>
+__device__ __forceinline__ void mat_chunk(const float* __restrict__ M, int D, int i, int j0, const float* x,
+                                          float (&acc)[NR]) {
+  float w[C];
+#pragma unroll
+  for (int u = 0; u < C; ++u) w[u] = __ldg(M + (int64_t)(j0 + u) * D + i);
+#pragma unroll
+  for (int u = 0; u < C; u += 4) {
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const float4 v = *reinterpret_cast<const float4*>(x + r * D + j0 + u);
+      acc[r] = fmaf(w[u + 3], v.w, fmaf(w[u + 2], v.z, fmaf(w[u + 1], v.y, fmaf(w[u], v.x, acc[r]))));
+    }
+  }
+}
 
-template <bool SMEM_R, int kRotGroups>
-__global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const float* RT, int rotated, float qscale,
-                           float* q_rot, __half* q_h) {
-  extern __shared__ __align__(16) float sq[];  // [kRotRows][D] (+ [D][D] R^T)
-  const int i = threadIdx.x % D, rg = threadIdx.x / D;
+// acc[r] += sum_j M[j * D + i] * x[r][j] over all j < D (D a multiple of 32).
+template <int NR>
+__device__ __forceinline__ void mat_col(const float* __restrict__ M, int D, int i, const float* x, float (&acc)[NR]) {
+  int j0 = 0;
+  for (; j0 + 64 <= D; j0 += 64) mat_chunk<64, NR>(M, D, i, j0, x, acc);
+  if (j0 < D) mat_chunk<32, NR>(M, D, i, j0, x, acc);
+}
+
+__global__ void __launch_bounds__(512) k_rotate_q(const void* q, int dtype, int n_rows, int D, const float* RT,
+                                                  int rotated, float qscale, float* q_rot, __half* q_h) {
+  extern __shared__ __align__(16) float sq[];  // [kRotRows][D]
+  const int i = threadIdx.x;
   const int r0 = blockIdx.x * kRotRows;
-  float* srt = sq + kRotRows * D;
   for (int k = threadIdx.x; k < kRotRows * D; k += blockDim.x) {
     const int r = k / D;
     sq[k] = (r0 + r < n_rows) ? load_any(q, dtype, (int64_t)r0 * D + k) : 0.0f;
   }
-  if (SMEM_R && !rotated) {
-    const float4* src = reinterpret_cast<const float4*>(RT);
-#pragma unroll 4
-    for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(srt)[k] = __ldg(src + k);
-  }
   __syncthreads();
-  constexpr int RPT = kRotRows / kRotGroups;  // rows per thread
-  float acc[RPT];
-  if (rotated) {
+  float acc[kRotRows];
 #pragma unroll
-    for (int r = 0; r < RPT; ++r) acc[r] = sq[(rg + kRotGroups * r) * D + i];
-  } else {
+  for (int r = 0; r < kRotRows; ++r) acc[r] = rotated ? sq[r * D + i] : 0.0f;
+  if (!rotated) mat_col<kRotRows>(RT, D, i, sq, acc);
 #pragma unroll
-    for (int r = 0; r < RPT; ++r) acc[r] = 0.0f;
-    for (int j = 0; j < D; j += 4) {
-      float w[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) w[u] = SMEM_R ? srt[(j + u) * D + i] : __ldg(RT + (int64_t)(j + u) * D + i);
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const float4 x = *reinterpret_cast<const float4*>(sq + (rg + kRotGroups * r) * D + j);
-        acc[r] = fmaf(w[0], x.x, fmaf(w[1], x.y, fmaf(w[2], x.z, fmaf(w[3], x.w, acc[r]))));
-      }
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < RPT; ++r) {
-    const int row = r0 + rg + kRotGroups * r;
+  for (int r = 0; r < kRotRows; ++r) {
+    const int row = r0 + r;
     if (row < n_rows) {
       const float v = acc[r] * qscale;
       q_rot[(int64_t)row * D + i] = v;
@@ -108,6 +115,14 @@ __global__ void k_rotate_q(const void* q, int dtype, int n_rows, int D, const fl
     }
   }
 }
+
+// Per-call arrays of small calls travel in the launch parameters
+// (__grid_constant__): no host-to-device copy between kernels.
+struct InlineMeta {
+  int64_t seqinfo[2 * kInlineSeqs];
+  int64_t seg[kInlineSeqs + 1];
+  int32_t cnt[kInlineCnt];
+};
 
 struct DecodeDev {
   const uint64_t* table;
@@ -125,6 +140,21 @@ struct DecodeDev {
   const float* vcent;
   float kalpha, valpha;
   float* part;
+  // fused path (k_decode_pair<G, true>)
+  const void* q_in;
+  int32_t q_dtype, q_rotated;
+  float qscale;
+  const float* qRT;      // K codec R^T: q' = R q
+  const float* vR;       // V codec R: out = R^T o (null: leave rotated)
+  const int32_t* cnt;    // [n_seqs * hkv] partial slots
+  int32_t* ctr;          // [n_seqs * hkv] arrival counters, zero between launches
+  void* out;
+  int32_t out_dtype;
+  float oscale;
+  InlineMeta meta;  // seqinfo / seg / cnt when those pointers are null
+  __device__ __forceinline__ const int64_t* si() const { return seqinfo ? seqinfo : meta.seqinfo; }
+  __device__ __forceinline__ const int64_t* sg() const { return seg ? seg : meta.seg; }
+  __device__ __forceinline__ const int32_t* ct() const { return cnt ? cnt : meta.cnt; }
 };
 
 // ---------------------------------------------------------------------------
@@ -187,20 +217,50 @@ struct Walk {
 };
 
 __device__ __forceinline__ int tiles_of(const DecodeDev& a, int b) {
-  return (int)((a.seqinfo[2 * b] + kTileTok - 1) / kTileTok);
+  return (int)((a.si()[2 * b] + kTileTok - 1) / kTileTok);
 }
 
 __device__ __forceinline__ Walk locate(const DecodeDev& a, int64_t x) {
   int lo = 0, hi = a.n_seqs - 1;  // last b with seg[b] <= x (a sequence with tiles)
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (a.seg[mid] <= x) lo = mid;
+    if (a.sg()[mid] <= x) lo = mid;
     else hi = mid - 1;
   }
   Walk w;
   w.b = lo;
   w.nt = tiles_of(a, lo);
-  const int64_t off = x - a.seg[lo];
+  const int64_t off = x - a.sg()[lo];
+  w.kvh = (int)(off / w.nt);
+  w.tile = (int)(off % w.nt);
+  return w;
+}
+
+// locate() by a whole warp: lanes test 32 candidate sequences per load
+// (first block starts at stride 32 when there are more than 32 sequences),
+// so the search costs one or two global round trips instead of log2(n).
+__device__ __forceinline__ Walk locate_warp(const DecodeDev& a, int64_t x, int lane) {
+  const int n = a.n_seqs;
+  int base = 0;
+  if (n > 32) {
+    for (int k0 = 0; k0 * 32 < n; k0 += 32) {
+      const int b = (k0 + lane) * 32;
+      const unsigned m = __ballot_sync(0xffffffffu, b < n && a.sg()[b] <= x);
+      if (m) base = (k0 + 31 - __clz((int)m)) * 32;
+      if (m != 0xffffffffu) break;
+    }
+  }
+  const int bl = base + lane;
+  const int64_t sv = bl <= n ? a.sg()[bl] : INT64_MAX;
+  const unsigned m = __ballot_sync(0xffffffffu, bl < n && sv <= x);
+  const int k = 31 - __clz((int)m);  // seg[base] <= x, so m != 0
+  const int64_t s0 = __shfl_sync(0xffffffffu, sv, k);
+  const int64_t s1n = __shfl_sync(0xffffffffu, sv, (k + 1) & 31);
+  const int64_t s1 = k < 31 ? s1n : a.sg()[base + 32];
+  Walk w;
+  w.b = base + k;
+  w.nt = (int)((s1 - s0) / a.hkv);
+  const int64_t off = x - s0;
   w.kvh = (int)(off / w.nt);
   w.tile = (int)(off % w.nt);
   return w;
@@ -226,7 +286,7 @@ struct Producer {
   __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
     const int pidx = w.tile >> 3;
     if (pidx != page_idx || w.b != page_b) {
-      const uint64_t* trow = a.table + a.seqinfo[2 * w.b + 1] * a.table_stride;
+      const uint64_t* trow = a.table + a.si()[2 * w.b + 1] * a.table_stride;
       page = reinterpret_cast<const uint8_t*>(__ldg(trow + pidx));
       page_idx = pidx;
       page_b = w.b;
@@ -260,7 +320,7 @@ struct PrefetchProducer {
   __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
     const int pidx = w.tile >> 3;
     if (pidx != page_idx || w.b != page_b) {
-      const uint64_t* trow = a.table + a.seqinfo[2 * w.b + 1] * a.table_stride;
+      const uint64_t* trow = a.table + a.si()[2 * w.b + 1] * a.table_stride;
       page = reinterpret_cast<const uint8_t*>((w.b == next_b && pidx == next_idx) ? next : __ldg(trow + pidx));
       page_idx = pidx;
       page_b = w.b;
@@ -435,8 +495,104 @@ __device__ __forceinline__ void p_pairs(float pu, float pv, int g, int t, int G,
   if (head >= G) pb0 = pb1 = 0u;
 }
 
+// Fused path: rows of query / output kept in shared memory per CTA. A CTA
+// touches at most kFusedSegs (sequence, kv head) segments (plan_decode
+// checks), i.e. kFusedSegs * G <= 32 rows.
+constexpr int kFusedSegs = 8;
+constexpr int kFusedRows = 32;
+constexpr int kFusedSmem = kFlatSmem + kFusedRows * 128 * 4;
+
+// Merge of one (sequence, kv head)'s split partials by the warp that
+// completed it: all G heads at once, lane c holding slot c's (m, l) of each
+// head and accumulating dims 4 lane .. 4 lane + 3; the normalised rows
+// (rotated basis) go to dst [G][128]. Partials written by other SMs are
+// read from L2 (ld.global.cg).
 template <int G>
-__global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(DecodeDev a) {
+__device__ __forceinline__ void merge_segment(const DecodeDev& a, int sid, int lane, float* dst) {
+  constexpr int D = 128, PS = D + 2;
+  const int n = a.ct()[sid];
+  const int64_t cs = (int64_t)G * PS;
+  const float* p = a.part + (int64_t)sid * a.max_slots * cs;
+  float M[G], L[G], o[G][4];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    M[h] = -INFINITY;
+    L[h] = 0.f;
+    o[h][0] = o[h][1] = o[h][2] = o[h][3] = 0.f;
+  }
+  // slot maxima; slots 0..31 keep (m, l) in registers for the weights
+  float mc[G], lc[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    mc[h] = lane < n ? __ldcg(p + lane * cs + h * PS) : -INFINITY;
+    lc[h] = lane < n ? __ldcg(p + lane * cs + h * PS + 1) : 0.f;
+    M[h] = mc[h];
+  }
+  for (int c = lane + 32; c < n; c += 32) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) M[h] = fmaxf(M[h], __ldcg(p + c * cs + h * PS));
+  }
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M[h] = fmaxf(M[h], __shfl_xor_sync(0xffffffffu, M[h], off));
+  }
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    float wl[G];
+    const int c = c0 + lane;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      if (c0 > 0) {
+        mc[h] = c < n ? __ldcg(p + c * cs + h * PS) : -INFINITY;
+        lc[h] = c < n ? __ldcg(p + c * cs + h * PS + 1) : 0.f;
+      }
+      wl[h] = mc[h] == -INFINITY ? 0.f : exp2f(mc[h] - M[h]);
+      L[h] += wl[h] * lc[h];
+    }
+    const int nn = min(32, n - c0);
+#pragma unroll 8
+    for (int u = 0; u < nn; ++u) {
+      const float* pc = p + (int64_t)(c0 + u) * cs + 2 + 4 * lane;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float wv = __shfl_sync(0xffffffffu, wl[h], u);
+        const float2 v0 = __ldcg(reinterpret_cast<const float2*>(pc + h * PS));
+        const float2 v1 = __ldcg(reinterpret_cast<const float2*>(pc + h * PS + 2));
+        o[h][0] = fmaf(wv, v0.x, o[h][0]);
+        o[h][1] = fmaf(wv, v0.y, o[h][1]);
+        o[h][2] = fmaf(wv, v1.x, o[h][2]);
+        o[h][3] = fmaf(wv, v1.y, o[h][3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L[h] += __shfl_xor_sync(0xffffffffu, L[h], off);
+    const float inv = L[h] > 0.f ? a.oscale / L[h] : 0.f;
+    *reinterpret_cast<float4*>(dst + h * D + 4 * lane) =
+        make_float4(o[h][0] * inv, o[h][1] * inv, o[h][2] * inv, o[h][3] * inv);
+  }
+}
+
+// acc[r] = sum_j R^T[j][i] q[rg + 4r][j] for NR rows: every R^T element is
+// read once from shared memory and applied to all NR rows.
+template <int NR>
+__device__ __forceinline__ void rot_rows(const float* Rs, const float* qs, int rg, int i, float (&acc)[kFusedRows / 4]) {
+  constexpr int D = 128;
+#pragma unroll 4
+  for (int j = 0; j < D; j += 4) {
+    const float w0 = Rs[j * D + i], w1 = Rs[(j + 1) * D + i], w2 = Rs[(j + 2) * D + i], w3 = Rs[(j + 3) * D + i];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const float4 xv = *reinterpret_cast<const float4*>(qs + (rg + 4 * r) * D + j);
+      acc[r] = fmaf(w3, xv.w, fmaf(w2, xv.z, fmaf(w1, xv.y, fmaf(w0, xv.x, acc[r]))));
+    }
+  }
+}
+
+template <int G, bool FUSED>
+__global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid_constant__ DecodeDev a) {
   static_assert(G >= 1 && G <= 4, "pair layout holds 4 heads");
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int D = 128;
@@ -446,33 +602,24 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(DecodeDev a)
   const int n_before = (int)(lut_off / kWarpBytes);
   uint8_t* lut = smem + lut_off;
 
-  for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
-    const int e = idx >> 6, slot = idx & 63;
-    const float* cent = slot < 32 ? a.kcent : a.vcent;
-    const float al = slot < 32 ? a.kalpha : a.valpha;
-    reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(cent[e & 15] * al, cent[e >> 4] * al));
-  }
-  __syncthreads();
-
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
   const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
   const int64_t begin = w * a.per_warp;
   const int64_t end = min(begin + a.per_warp, a.total_tiles);
-  if (begin >= end) return;
   uint8_t* stages = warp < n_before ? smem + warp * kWarpBytes
                                     : smem + lut_off + kLutBytes + (warp - n_before) * kWarpBytes;
   const uint32_t st0 = (uint32_t)__cvta_generic_to_shared(stages);
 
   PrefetchProducer pr;
-  pr.w = locate(a, begin);
   pr.page = nullptr;
   pr.page_b = -1;
   pr.page_idx = -1;
   pr.next = 0;
   pr.next_b = -1;
   pr.next_idx = -1;
+  if (begin < end) pr.w = locate_warp(a, begin, lane);
   Walk cw = pr.w;
 #pragma unroll
   for (int s = 0; s < kStages; ++s) {
@@ -483,12 +630,88 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(DecodeDev a)
     cp_commit();
   }
 
+  // ---- fused: q' = R q * qscale for this CTA's segments, into qs, with
+  // R^T staged over the (not yet built) lookup table ----
+  float* qs = reinterpret_cast<float*>(smem + kFlatSmem);  // [kFusedRows][D]
+  __shared__ int merged[kFusedSegs];
+  int sid0 = 0, nrows = 0;
+  if constexpr (FUSED) {
+    const int64_t cb = (int64_t)blockIdx.x * kFlatWarps * a.per_warp;
+    const int64_t ce = min(cb + (int64_t)kFlatWarps * a.per_warp, a.total_tiles);
+    if (cb < ce) {
+      const Walk f = locate_warp(a, cb, lane), e = locate_warp(a, ce - 1, lane);
+      sid0 = f.b * a.hkv + f.kvh;
+      nrows = (e.b * a.hkv + e.kvh - sid0 + 1) * G;
+    }
+    if (threadIdx.x < kFusedSegs) merged[threadIdx.x] = 0;
+    float* Rs = reinterpret_cast<float*>(lut);
+    if (!a.q_rotated) {
+      const uint32_t rd = (uint32_t)__cvta_generic_to_shared(Rs);
+#pragma unroll
+      for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
+        const int k = threadIdx.x + it * kFlatWarps * 32;
+        cp_async16(rd + k * 16, a.qRT + 4 * k);
+      }
+    }
+    cp_commit();
+#pragma unroll
+    for (int it = 0; it < kFusedRows * D / (kFlatWarps * 32); ++it) {
+      const int k = threadIdx.x + it * kFlatWarps * 32;
+      if (k < nrows * D) {
+        const int r = k >> 7, j = k & 127;
+        const int sid = sid0 + r / G;
+        const int64_t row = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G;
+        qs[k] = load_any(a.q_in, a.q_dtype, row * D + j);
+      }
+    }
+    cp_wait_all();
+    __syncthreads();
+    const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
+    constexpr int RPT = kFusedRows / 4;  // rows rg, rg + 4, ... of this thread
+    const int my_rows = nrows > rg ? (nrows - rg + 3) / 4 : 0;
+    float acc[RPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) acc[r] = (a.q_rotated && r < my_rows) ? qs[(rg + 4 * r) * D + i] : 0.f;
+    if (!a.q_rotated) {
+      switch (my_rows) {  // exact row counts: no predicated-off work
+        case 1: rot_rows<1>(Rs, qs, rg, i, acc); break;
+        case 2: rot_rows<2>(Rs, qs, rg, i, acc); break;
+        case 3: rot_rows<3>(Rs, qs, rg, i, acc); break;
+        case 4: rot_rows<4>(Rs, qs, rg, i, acc); break;
+        case 5: rot_rows<5>(Rs, qs, rg, i, acc); break;
+        case 6: rot_rows<6>(Rs, qs, rg, i, acc); break;
+        case 7: rot_rows<7>(Rs, qs, rg, i, acc); break;
+        case 8: rot_rows<8>(Rs, qs, rg, i, acc); break;
+        default: break;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < RPT; ++r)
+      if (rg + 4 * r < nrows) qs[(rg + 4 * r) * D + i] = acc[r] * a.qscale;
+  }
+  // ---- centroid-pair lookup table: lane l < 16 holds K centroid l, lane
+  // 16 + l V centroid l (scaled); entry (e, slot) = (c[e & 15], c[e >> 4]) ----
+  {
+    const float cl = lane < 16 ? a.kcent[lane] * a.kalpha : a.vcent[lane - 16] * a.valpha;
+#pragma unroll
+    for (int it = 0; it < 256 * 64 / (kFlatWarps * 32); ++it) {
+      const int idx = threadIdx.x + it * kFlatWarps * 32;
+      const int e = idx >> 6, vside = (idx & 63) >= 32 ? 16 : 0;
+      const float lo = __shfl_sync(0xffffffffu, cl, vside + (e & 15));
+      const float hi = __shfl_sync(0xffffffffu, cl, vside + (e >> 4));
+      reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(lo, hi));
+    }
+  }
+  __syncthreads();
+  if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
+
   int64_t x = begin;
   while (x < end) {
     // ---- a new (sequence, kv head) segment ----
     const int b = cw.b, kvh = cw.kvh;
-    const int n_valid = (int)a.seqinfo[2 * b];
-    const int64_t seg_first = a.seg[b] + (int64_t)kvh * cw.nt;
+    const int n_valid = (int)a.si()[2 * b];
+    const int64_t seg_first = a.sg()[b] + (int64_t)kvh * cw.nt;
     const int64_t seg_end = min(end, seg_first + cw.nt);
     const int64_t slot_base = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / a.per_warp);
     // B fragments of Q: column g = (head g/2, part g&1), dims 32t + 4s + {0,1} / {2,3}
@@ -496,7 +719,9 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(DecodeDev a)
     {
       const int head = g >> 1;
       const bool lo = g & 1;
-      const float* qrow = a.q_rot + ((int64_t)b * a.hq + (int64_t)kvh * G + (head < G ? head : 0)) * D + 32 * t;
+      const int hsel = head < G ? head : 0;
+      const float* qrow = FUSED ? qs + ((b * a.hkv + kvh - sid0) * G + hsel) * D + 32 * t
+                                : a.q_rot + ((int64_t)b * a.hq + (int64_t)kvh * G + hsel) * D + 32 * t;
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const float4 v = *reinterpret_cast<const float4*>(qrow + 4 * s);
@@ -592,12 +817,66 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(DecodeDev a)
         *reinterpret_cast<float2*>(row + 2 + 16 * g + 2 * i) =
             make_float2(oacc[i][0] + oacc[i][1], oacc[i][2] + oacc[i][3]);
     }
+    if constexpr (FUSED) {
+      // The warp that completes a segment's last slot merges the segment's
+      // partials into its q' rows in qs (no warp of this CTA reads them again).
+      __threadfence();
+      __syncwarp();
+      const int sid = b * a.hkv + kvh;
+      int old = 0;
+      if (lane == 0) old = atomicAdd(a.ctr + sid, 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == a.ct()[sid] - 1) {
+        __threadfence();
+        if (lane == 0) {
+          a.ctr[sid] = 0;  // zero again for the next launch
+          merged[sid - sid0] = 1;
+        }
+        merge_segment<G>(a, sid, lane, qs + (sid - sid0) * G * D);
+      }
+    }
   }
   cp_wait_all();
+  if constexpr (FUSED) {
+    // ---- un-rotate the merged rows: out = R^T o, R staged over the table ----
+    __syncthreads();
+    float* Rs = reinterpret_cast<float*>(lut);
+    if (a.vR) {
+      const uint32_t rd = (uint32_t)__cvta_generic_to_shared(Rs);
+#pragma unroll
+      for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
+        const int k = threadIdx.x + it * kFlatWarps * 32;
+        cp_async16(rd + k * 16, a.vR + 4 * k);
+      }
+      cp_commit();
+      cp_wait_all();
+      __syncthreads();
+    }
+    const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
+    for (int r = rg; r < nrows; r += 4) {
+      if (!merged[r / G]) continue;
+      const int sid = sid0 + r / G;
+      const int64_t orow = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G;
+      float v;
+      if (a.vR) {
+        const float* xr = qs + r * D;
+        float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 8
+        for (int j = 0; j < D; j += 2) {
+          acc0 = fmaf(Rs[j * D + i], xr[j], acc0);
+          acc1 = fmaf(Rs[(j + 1) * D + i], xr[j + 1], acc1);
+        }
+        v = acc0 + acc1;
+      } else {
+        v = qs[r * D + i];
+      }
+      store_any(a.out, a.out_dtype, orow * D + i, v);
+    }
+  }
 }
 
 template <int G>
-__global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a) {
+__global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid_constant__ DecodeDev a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int D = 128;
   constexpr int PS = D + 2;
@@ -644,8 +923,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
   while (x < end) {
     // ---- a new (sequence, kv head) segment ----
     const int b = cw.b, kvh = cw.kvh;
-    const int n_valid = (int)a.seqinfo[2 * b];
-    const int64_t seg_first = a.seg[b] + (int64_t)kvh * cw.nt;
+    const int n_valid = (int)a.si()[2 * b];
+    const int64_t seg_first = a.sg()[b] + (int64_t)kvh * cw.nt;
     const int64_t seg_end = min(end, seg_first + cw.nt);
     const int64_t slot_base = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / a.per_warp);
     uint32_t qb[8][2];
@@ -769,7 +1048,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(DecodeDev a)
 // chunks of pages_per_chunk pages; partial slot = chunk.
 // ---------------------------------------------------------------------------
 template <int KPL, int GS>
-__global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
+__global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ DecodeDev a) {
   extern __shared__ __align__(16) float gsm[];
   constexpr int D = 32 * KPL;
   constexpr int PS = D + 2;
@@ -793,8 +1072,8 @@ __global__ void __launch_bounds__(128) k_decode_generic(DecodeDev a) {
     rest /= groups;
     const int kvh = (int)(rest % a.hkv);
     const int s = (int)(rest / a.hkv);
-    const int64_t n_valid = a.seqinfo[2 * s];
-    const uint64_t* trow = a.table + a.seqinfo[2 * s + 1] * a.table_stride;
+    const int64_t n_valid = a.si()[2 * s];
+    const uint64_t* trow = a.table + a.si()[2 * s + 1] * a.table_stride;
     const int qh0 = kvh * a.G + grp * GS;
 
     float q[GS][KPL], o[GS][KPL], m[GS], l[GS];
@@ -905,24 +1184,20 @@ struct MergeDev {
   float* o_out;
 };
 
-// One warp per row: every slot's (m, l) and o are read at once (lane c holds
-// slot c's max; each lane accumulates head_dim/32 contiguous dims), then the
-// block un-rotates its rows with R staged in shared memory.
+// One warp per row merges the row's split partials: lane c holds slot c's
+// max and weight (32 slots at a time, shuffled to the warp as the slots are
+// summed, four slots' loads in flight), each lane accumulating head_dim/32
+// contiguous dims. The block then un-rotates its rows: thread i computes
+// output dim i of 4 rows, reading R[j][i] straight from global memory
+// (coalesced, L2-resident).
 constexpr int kMergeWarps = 8;
 
-template <bool SMEM_R>
-__global__ void __launch_bounds__(kMergeWarps * 32) k_merge(MergeDev a) {
-  extern __shared__ __align__(16) float so[];  // [kMergeWarps][D] (+ [D][D] R)
+__global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
+  extern __shared__ __align__(16) float so[];  // [kMergeWarps][D]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = a.D;
   const int PS = D + 2;
-  const int per = D / 32;  // dims per lane
-  float* sr = so + kMergeWarps * D;
-  if (SMEM_R && a.R && a.out) {
-    const float4* src = reinterpret_cast<const float4*>(a.R);
-#pragma unroll 4
-    for (int k = threadIdx.x; k < D * D / 4; k += blockDim.x) reinterpret_cast<float4*>(sr)[k] = __ldg(src + k);
-  }
+  const int per = D / 32;  // dims per lane (even)
   const int row = blockIdx.x * kMergeWarps + warp;
   float* orow = so + warp * D;
   if (row < a.n_rows) {
@@ -939,15 +1214,30 @@ __global__ void __launch_bounds__(kMergeWarps * 32) k_merge(MergeDev a) {
     float O[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) O[k] = 0.f;
-    for (int c = 0; c < n; ++c) {
-      const float* pc = p + c * cs;
-      const float mc = pc[0];
-      const float w = mc == -INFINITY ? 0.f : exp2f(mc - M);
-      L += w * pc[1];
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      float wl = 0.f;
+      if (c0 + lane < n) {
+        const float mc = p[(c0 + lane) * cs];
+        wl = mc == -INFINITY ? 0.f : exp2f(mc - M);
+        L += wl * p[(c0 + lane) * cs + 1];
+      }
+      const int nn = min(32, n - c0);
+#pragma unroll 8
+      for (int u = 0; u < nn; ++u) {
+        const float w = __shfl_sync(0xffffffffu, wl, u);
+        const float2* pc = reinterpret_cast<const float2*>(p + (c0 + u) * cs + 2 + lane * per);
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (k < per) O[k] += w * pc[2 + lane * per + k];
+        for (int k = 0; k < 8; ++k) {
+          if (2 * k < per) {
+            const float2 v = pc[k];
+            O[2 * k] = fmaf(w, v.x, O[2 * k]);
+            O[2 * k + 1] = fmaf(w, v.y, O[2 * k + 1]);
+          }
+        }
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
       if (k < per) {
@@ -966,26 +1256,18 @@ __global__ void __launch_bounds__(kMergeWarps * 32) k_merge(MergeDev a) {
   if (!a.out) return;
   __syncthreads();
   // out[row][i] = sum_j R[j][i] * o[row][j]
-  for (int idx = threadIdx.x; idx < kMergeWarps * D; idx += blockDim.x) {
-    const int r = idx / D, i = idx % D;
-    const int rr = blockIdx.x * kMergeWarps + r;
-    if (rr >= a.n_rows) continue;
-    float acc;
-    if (a.R) {
-      acc = 0.f;
-      const float* x = so + r * D;
-      for (int j = 0; j < D; j += 4) {
-        const float4 xv = *reinterpret_cast<const float4*>(x + j);
-        const float w0 = SMEM_R ? sr[j * D + i] : __ldg(a.R + (int64_t)j * D + i);
-        const float w1 = SMEM_R ? sr[(j + 1) * D + i] : __ldg(a.R + (int64_t)(j + 1) * D + i);
-        const float w2 = SMEM_R ? sr[(j + 2) * D + i] : __ldg(a.R + (int64_t)(j + 2) * D + i);
-        const float w3 = SMEM_R ? sr[(j + 3) * D + i] : __ldg(a.R + (int64_t)(j + 3) * D + i);
-        acc = fmaf(w0, xv.x, fmaf(w1, xv.y, fmaf(w2, xv.z, fmaf(w3, xv.w, acc))));
-      }
-    } else {
-      acc = so[r * D + i];
+  const int r_lo = blockIdx.x * kMergeWarps;
+  for (int u = threadIdx.x; u < 2 * D; u += blockDim.x) {
+    const int i = u % D, rs = (u / D) * 4;
+    float acc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r] = a.R ? 0.f : so[(rs + r) * D + i];
+    if (a.R) mat_col<4>(a.R, D, i, so + rs * D, acc);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int rr = r_lo + rs + r;
+      if (rr < a.n_rows) store_any(a.out, a.out_dtype, (int64_t)rr * D + i, acc[r]);
     }
-    store_any(a.out, a.out_dtype, (int64_t)rr * D + i, acc);
   }
 }
 
@@ -1002,14 +1284,15 @@ void launch_flat_g(const DecodeDev& d, int grid, cudaStream_t s) {
   LC_CUDA(cudaGetLastError());
 }
 
-template <int G>
+template <int G, bool FUSED>
 void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
+  constexpr int smem = FUSED ? kFusedSmem : kFlatSmem;
   static bool attr = false;
   if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_decode_pair<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlatSmem));
+    LC_CUDA(cudaFuncSetAttribute(k_decode_pair<G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  k_decode_pair<G><<<(unsigned)grid, kFlatWarps * 32, kFlatSmem, s>>>(d);
+  k_decode_pair<G, FUSED><<<(unsigned)grid, kFlatWarps * 32, smem, s>>>(d);
   LC_CUDA(cudaGetLastError());
 }
 
@@ -1057,6 +1340,31 @@ bool decode_fast_path(int dim, int kbits, int vbits, int G) {
   return dim == 128 && kbits == 4 && vbits == 4 && G >= 1 && G <= 8;
 }
 
+// Most (sequence, kv head) segments any CTA's tile range touches.
+static int32_t max_cta_segments(const int64_t* seg, const int64_t* lens, int n, int hkv, int64_t total, int64_t pw,
+                                int grid) {
+  if (total <= 0) return 0;
+  auto sid_of = [&](int64_t x) {
+    int lo = 0, hi = n - 1;  // last b with seg[b] <= x
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (seg[mid] <= x) lo = mid;
+      else hi = mid - 1;
+    }
+    const int64_t nt = (lens[lo] + kTileTok - 1) / kTileTok;
+    return (int64_t)lo * hkv + (x - seg[lo]) / nt;
+  };
+  int64_t mx = 0;
+  const int64_t span = (int64_t)kFlatWarps * pw;
+  for (int c = 0; c < grid; ++c) {
+    const int64_t cb = (int64_t)c * span;
+    if (cb >= total) break;
+    const int64_t ce = std::min(cb + span, total) - 1;
+    mx = std::max(mx, sid_of(ce) - sid_of(cb) + 1);
+  }
+  return (int32_t)mx;
+}
+
 DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits) {
   DecodePlan p;
   const int G = hq / hkv;
@@ -1082,6 +1390,7 @@ DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int di
       }
     }
     p.max_slots = mx;
+    p.max_cta_segs = max_cta_segments(p.seg.data(), lens.data(), n, hkv, p.total_tiles, p.per_warp, p.grid);
   } else {
     p.flat = false;
     int64_t mx = 0;
@@ -1135,27 +1444,20 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
                      bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s) {
   if (n_rows <= 0) return;
   const int blocks = (n_rows + kRotRows - 1) / kRotRows;
-  const bool smem_r = dim <= 128;
-  const size_t smem = ((size_t)kRotRows * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
-  const int groups = dim <= 256 ? 4 : 2;  // threads = groups * dim <= 1024
-  const int threads = dim * groups;
-  static bool attr = false;
-  if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    LC_CUDA(cudaFuncSetAttribute(k_rotate_q<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    attr = true;
-  }
-  const int rot = q_is_rotated ? 1 : 0;
-  if (smem_r) k_rotate_q<true, 4><<<blocks, threads, smem, s>>>(q, q_dtype, n_rows, dim, RT, rot, qscale, q_rot, q_h);
-  else if (groups == 4)
-    k_rotate_q<false, 4><<<blocks, threads, smem, s>>>(q, q_dtype, n_rows, dim, RT, rot, qscale, q_rot, q_h);
-  else k_rotate_q<false, 2><<<blocks, threads, smem, s>>>(q, q_dtype, n_rows, dim, RT, rot, qscale, q_rot, q_h);
+  const size_t smem = (size_t)kRotRows * dim * sizeof(float);
+  k_rotate_q<<<blocks, dim, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
   LC_CUDA(cudaGetLastError());
 }
 
-void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream_t s) {
-  DecodeDev d;
+static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
+  DecodeDev d{};
+  if (!a.seqinfo) {
+    LC_REQUIRE(a.h_seqinfo && a.n_seqs <= kInlineSeqs && (int64_t)a.n_seqs * a.hkv <= kInlineCnt, LC_ERR_STATE,
+               "inline decode metadata does not fit");
+    std::memcpy(d.meta.seqinfo, a.h_seqinfo, (size_t)a.n_seqs * 2 * sizeof(int64_t));
+    if (a.h_seg) std::memcpy(d.meta.seg, a.h_seg, (size_t)(a.n_seqs + 1) * sizeof(int64_t));
+    if (a.h_cnt) std::memcpy(d.meta.cnt, a.h_cnt, (size_t)a.n_seqs * a.hkv * sizeof(int32_t));
+  }
   d.table = a.table;
   d.table_stride = a.table_stride;
   d.seqinfo = a.seqinfo;
@@ -1185,13 +1487,18 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
   d.kalpha = a.kalpha;
   d.valpha = a.valpha;
   d.part = a.part;
+  return d;
+}
+
+void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream_t s) {
+  const DecodeDev d = make_dev(a, p);
   if (p.flat) {
     if (p.total_tiles == 0) return;
     switch (d.G) {
-      case 1: return launch_pair_g<1>(d, p.grid, s);
-      case 2: return launch_pair_g<2>(d, p.grid, s);
-      case 3: return launch_pair_g<3>(d, p.grid, s);
-      case 4: return launch_pair_g<4>(d, p.grid, s);
+      case 1: return launch_pair_g<1, false>(d, p.grid, s);
+      case 2: return launch_pair_g<2, false>(d, p.grid, s);
+      case 3: return launch_pair_g<3, false>(d, p.grid, s);
+      case 4: return launch_pair_g<4, false>(d, p.grid, s);
       case 5: return launch_flat_g<5>(d, p.grid, s);
       case 6: return launch_flat_g<6>(d, p.grid, s);
       case 7: return launch_flat_g<7>(d, p.grid, s);
@@ -1207,22 +1514,39 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
   }
 }
 
+bool decode_fusable(const DecodePlan& p, int G) { return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs; }
+
+void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedArgs& f, cudaStream_t s) {
+  LC_REQUIRE(decode_fusable(p, a.hq / a.hkv), LC_ERR_STATE, "decode plan is not fusable");
+  if (p.total_tiles == 0) return;
+  DecodeDev d = make_dev(a, p);
+  d.q_in = f.q;
+  d.q_dtype = f.q_dtype;
+  d.q_rotated = f.q_rotated;
+  d.qscale = f.qscale;
+  d.qRT = f.qRT;
+  d.vR = f.vR;
+  d.cnt = f.cnt;
+  d.ctr = f.ctr;
+  d.out = f.out;
+  d.out_dtype = f.out_dtype;
+  d.oscale = f.oscale;
+  switch (d.G) {
+    case 1: return launch_pair_g<1, true>(d, p.grid, s);
+    case 2: return launch_pair_g<2, true>(d, p.grid, s);
+    case 3: return launch_pair_g<3, true>(d, p.grid, s);
+    default: return launch_pair_g<4, true>(d, p.grid, s);
+  }
+}
+
 void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
                   float oscale, cudaStream_t s) {
   if (n_rows <= 0) return;
   MergeDev d{part, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out, o_out};
   const int blocks = (n_rows + kMergeWarps - 1) / kMergeWarps;
-  const bool smem_r = dim <= 128 && R && out;
-  const size_t smem = ((size_t)kMergeWarps * dim + (smem_r ? (size_t)dim * dim : 0)) * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_merge<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    LC_CUDA(cudaFuncSetAttribute(k_merge<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    attr = true;
-  }
-  if (smem_r) k_merge<true><<<blocks, kMergeWarps * 32, smem, s>>>(d);
-  else k_merge<false><<<blocks, kMergeWarps * 32, smem, s>>>(d);
+  const size_t smem = (size_t)kMergeWarps * dim * sizeof(float);
+  k_merge<<<blocks, kMergeWarps * 32, smem, s>>>(d);
   LC_CUDA(cudaGetLastError());
 }
 

@@ -69,7 +69,19 @@ struct DecodeArgs {
   const float* vcent = nullptr;   // [2^vbits]
   float kalpha = 1.0f, valpha = 1.0f;  // f16 table scales of the fast path
   float* part = nullptr;          // [n_seqs][hkv][max_slots][G][dim + 2]  (m, l, o...)
+  // With seqinfo == nullptr the per-call arrays are host copies passed in the
+  // launch parameters (decode_inline_fits): seqinfo, seg, cnt as above.
+  const int64_t* h_seqinfo = nullptr;
+  const int64_t* h_seg = nullptr;
+  const int32_t* h_cnt = nullptr;
 };
+
+// Per-call decode arrays that fit in the launch parameters.
+constexpr int kInlineSeqs = 64;
+constexpr int kInlineCnt = 1024;
+inline bool decode_inline_fits(int n_seqs, int hkv) {
+  return n_seqs <= kInlineSeqs && (int64_t)n_seqs * hkv <= kInlineCnt;
+}
 
 // How a decode call is split: the flat tile-balanced fast path (one partial
 // slot per warp range touching a (seq, kv head)) or the chunked generic path
@@ -80,6 +92,7 @@ struct DecodePlan {
   int64_t per_warp = 1, total_tiles = 0;
   int32_t max_slots = 1;
   int32_t pages_per_chunk = 4, n_chunks = 1;
+  int32_t max_cta_segs = 0;  // flat: most (seq, kv head) segments one CTA touches
   std::vector<int64_t> seg;  // [n_seqs + 1]
   std::vector<int32_t> cnt;  // [n_seqs * hkv] slots used per (seq, kv head)
 };
@@ -90,6 +103,25 @@ int num_sms();
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* R,
                      bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s);
 void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream_t s);
+
+// One-launch decode for the flat path with G <= 4 when every CTA touches few
+// enough segments (decode_fusable): the kernel rotates its queries, and the
+// warp completing a (seq, kv head) merges its partials; the CTA then writes
+// the un-rotated rows. Rows of sequences with no tokens are not written.
+struct FusedArgs {
+  const void* q = nullptr;       // [n_seqs][hq][dim] raw queries
+  int32_t q_dtype = 0, q_rotated = 0;
+  float qscale = 1.0f;           // scale * log2(e) / kalpha
+  const float* qRT = nullptr;    // K codec R^T
+  const float* vR = nullptr;     // V codec R; null leaves the output rotated
+  const int32_t* cnt = nullptr;  // [n_seqs * hkv] partial slots (plan.cnt on the device)
+  int32_t* ctr = nullptr;        // [n_seqs * hkv] zero on entry; left zero
+  void* out = nullptr;
+  int32_t out_dtype = 0;
+  float oscale = 1.0f;           // 1 / valpha
+};
+bool decode_fusable(const DecodePlan& p, int G);
+void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedArgs& f, cudaStream_t s);
 
 // ---- parity hooks of the KVCache trait (hooks.cu): bit-exact in the
 // reference's f32 order ----
