@@ -770,7 +770,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     f.q_dtype = q_dtype;
     f.q_rotated = (flags & LC_Q_ROTATED) ? 1 : 0;
     f.qscale = qscale;
-    f.qRT = c->dk.RTd;
+    f.qR = c->dk.R;
     f.vR = (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R;
     f.cnt = dcnt;
     f.ctr = c->ctr.p;

@@ -144,7 +144,7 @@ struct DecodeDev {
   const void* q_in;
   int32_t q_dtype, q_rotated;
   float qscale;
-  const float* qRT;      // K codec R^T: q' = R q
+  const float* qR;       // K codec R (row-major): q' = R q
   const float* vR;       // V codec R: out = R^T o (null: leave rotated)
   const int32_t* cnt;    // [n_seqs * hkv] partial slots
   int32_t* ctr;          // [n_seqs * hkv] arrival counters, zero between launches
@@ -330,17 +330,21 @@ struct PrefetchProducer {
       next = __ldg(trow + next_idx);
     }
     const int64_t hr = (int64_t)w.kvh * kPageTokens + (w.tile & 7) * kTileTok;
-    const uint8_t* k = page + a.off_kw + hr * 64;
-    const uint8_t* v = page + a.off_vw + hr * 64;
+    // chunk c = lane + 32 q: row c >> 2 = lane / 4 + 8 q, part c & 3 = lane & 3;
+    // the V swizzle (part ^ (row & 2)) depends on the lane only
+    const uint8_t* k = page + a.off_kw + hr * 64 + lane * 16;
+    const uint8_t* v = page + a.off_vw + hr * 64 + lane * 16;
+    const uint32_t vdst = st + kStV + (lane >> 2) * 64 + (((lane & 3) ^ ((lane >> 2) & 2)) << 4);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int c = lane + 32 * q;  // 16-byte chunk: row c >> 2, part c & 3
-      cp_async16(st + kStK + c * 16, k + c * 16);
-      const int r = c >> 2;
-      cp_async16(st + kStV + r * 64 + (((c & 3) ^ (r & 2)) << 4), v + c * 16);
+      cp_async16(st + kStK + lane * 16 + q * 512, k + q * 512);
+      cp_async16(vdst + q * 512, v + q * 512);
     }
-    if (lane < 8) cp_async16(st + kStKs + lane * 16, page + a.off_ks + hr * 4 + lane * 16);
-    else if (lane < 16) cp_async16(st + kStVs + (lane - 8) * 16, page + a.off_vs + hr * 4 + (lane - 8) * 16);
+    if (lane < 16) {
+      const bool kside = lane < 8;
+      cp_async16(st + (kside ? kStKs : kStVs) + (lane & 7) * 16,
+                 page + (kside ? a.off_ks : a.off_vs) + hr * 4 + (lane & 7) * 16);
+    }
   }
 };
 
@@ -450,12 +454,15 @@ __device__ __forceinline__ void qk16_2(const uint8_t* st, int r0, int g, int t, 
 }
 
 // 16 tokens (rows r0..r0+15): O^T += V_dq^T P^T, one MMA per dim tile.
-__device__ __forceinline__ void pv16_1(const uint8_t* st, int r0, int g, int t, uint32_t lanebase, uint32_t pb0,
-                                       uint32_t pb1, float (&oacc)[8][4]) {
-  auto vrow = [&](int r) -> uint2 {
-    return *reinterpret_cast<const uint2*>(st + kStV + r * 64 + ((((g >> 1) ^ (r & 2))) << 4) + (g & 1) * 8);
-  };
-  const uint2 v0 = vrow(r0 + t), v1 = vrow(r0 + t + 8), v2 = vrow(r0 + t + 4), v3 = vrow(r0 + t + 12);
+// vl = the lane's constant part of its V row offsets (see pair_vlane).
+template <int R0>
+__device__ __forceinline__ void pv16_1(const uint8_t* st, uint32_t vl, uint32_t lanebase, uint32_t pb0, uint32_t pb1,
+                                       float (&oacc)[8][4]) {
+  const uint8_t* vb = st + kStV + vl + R0 * 64;
+  const uint2 v0 = *reinterpret_cast<const uint2*>(vb);         // token t
+  const uint2 v1 = *reinterpret_cast<const uint2*>(vb + 512);   // token t + 8
+  const uint2 v2 = *reinterpret_cast<const uint2*>(vb + 256);   // token t + 4
+  const uint2 v3 = *reinterpret_cast<const uint2*>(vb + 768);   // token t + 12
   uint32_t ev[2][2], od[2][2];
   const uint32_t A0[2] = {v0.x, v0.y}, B0[2] = {v1.x, v1.y};
   const uint32_t A1[2] = {v2.x, v2.y}, B1[2] = {v3.x, v3.y};
@@ -476,6 +483,13 @@ __device__ __forceinline__ void pv16_1(const uint8_t* st, int r0, int g, int t, 
     const uint32_t a3 = lut_v(od[1][hh], lanebase, k);
     mma16816(oacc[i], a0, a1, a2, a3, pb0, pb1);
   }
+}
+
+// Lane (g, t)'s constant V offset within a stage: rows r0 + t + {0, 4, 8, 12}
+// all have bit 1 equal to t's, so the XOR swizzle of the 16-byte chunk
+// (g / 2) ^ (row & 2) is fixed per lane; 8-byte half g & 1.
+__device__ __forceinline__ uint32_t pair_vlane(int g, int t) {
+  return (uint32_t)(t * 64 + (((g >> 1) ^ (t & 2)) << 4) + (g & 1) * 8);
 }
 
 // P^T B fragments of column g = 2 * head + part for k slots (2t, 2t+1) =
@@ -575,18 +589,45 @@ __device__ __forceinline__ void merge_segment(const DecodeDev& a, int sid, int l
   }
 }
 
-// acc[r] = sum_j R^T[j][i] q[rg + 4r][j] for NR rows: every R^T element is
-// read once from shared memory and applied to all NR rows.
+// Centroid-pair lookup table: lane l < 16 holds K centroid l, lane 16 + l V
+// centroid l (scaled); entry (e, slot) = (c[e & 15], c[e >> 4]), slots 0..31
+// K and 32..63 V.
+__device__ __forceinline__ void build_lut(uint8_t* lut, const DecodeDev& a, int lane) {
+  const float cl = lane < 16 ? a.kcent[lane] * a.kalpha : a.vcent[lane - 16] * a.valpha;
+#pragma unroll
+  for (int it = 0; it < 256 * 64 / (kFlatWarps * 32); ++it) {
+    const int idx = threadIdx.x + it * kFlatWarps * 32;
+    const int e = idx >> 6, vside = (idx & 63) >= 32 ? 16 : 0;
+    const float lo = __shfl_sync(0xffffffffu, cl, vside + (e & 15));
+    const float hi = __shfl_sync(0xffffffffu, cl, vside + (e >> 4));
+    reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(lo, hi));
+  }
+}
+
+// Fused prologue: row i of the K rotation R (512 B, padded to 528 B so the
+// 16-byte reads of eight consecutive rows hit distinct banks) lives in warp
+// (i / 8)'s second pipeline stage until the warps start their second tiles.
+constexpr int kRRowBytes = 528;
+__device__ __forceinline__ uint8_t* r_row(uint8_t* smem, int n_before, uint32_t lut_off, int i) {
+  const int wi = i >> 3;
+  uint8_t* st = wi < n_before ? smem + wi * kWarpBytes : smem + lut_off + kLutBytes + (wi - n_before) * kWarpBytes;
+  return st + kStageBytes + (i & 7) * kRRowBytes;
+}
+
+// acc[r] = sum_j R[i][j] q[rg + 2r][j] for NR rows: four weights per 16-byte
+// read of R's row i, each applied to all NR rows.
+constexpr int kRotGroups = 2;  // thread groups covering R once each
 template <int NR>
-__device__ __forceinline__ void rot_rows(const float* Rs, const float* qs, int rg, int i, float (&acc)[kFusedRows / 4]) {
+__device__ __forceinline__ void rot_rows(const float* ri, const float* qs, int rg,
+                                         float (&acc)[kFusedRows / kRotGroups]) {
   constexpr int D = 128;
-#pragma unroll 4
+#pragma unroll 2
   for (int j = 0; j < D; j += 4) {
-    const float w0 = Rs[j * D + i], w1 = Rs[(j + 1) * D + i], w2 = Rs[(j + 2) * D + i], w3 = Rs[(j + 3) * D + i];
+    const float4 w = *reinterpret_cast<const float4*>(ri + j);
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
-      const float4 xv = *reinterpret_cast<const float4*>(qs + (rg + 4 * r) * D + j);
-      acc[r] = fmaf(w3, xv.w, fmaf(w2, xv.z, fmaf(w1, xv.y, fmaf(w0, xv.x, acc[r]))));
+      const float4 xv = *reinterpret_cast<const float4*>(qs + (rg + kRotGroups * r) * D + j);
+      acc[r] = fmaf(w.w, xv.w, fmaf(w.z, xv.z, fmaf(w.y, xv.y, fmaf(w.x, xv.x, acc[r]))));
     }
   }
 }
@@ -605,6 +646,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
+  const uint32_t vl = pair_vlane(g, t);
   const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
   const int64_t begin = w * a.per_warp;
   const int64_t end = min(begin + a.per_warp, a.total_tiles);
@@ -621,17 +663,23 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   pr.next_idx = -1;
   if (begin < end) pr.w = locate_warp(a, begin, lane);
   Walk cw = pr.w;
-#pragma unroll
-  for (int s = 0; s < kStages; ++s) {
-    if (begin + s < end) {
-      pr.issue(a, st0 + s * kStageBytes, lane);
+  // first tile now; the fused prologue borrows every warp's second stage
+  // for R^T, so there the second tile is issued after the rotation
+  if (begin < end) {
+    pr.issue(a, st0, lane);
+    step(a, pr.w);
+  }
+  cp_commit();
+  if (!FUSED) {
+    if (begin + 1 < end) {
+      pr.issue(a, st0 + kStageBytes, lane);
       step(a, pr.w);
     }
     cp_commit();
   }
 
   // ---- fused: q' = R q * qscale for this CTA's segments, into qs, with
-  // R^T staged over the (not yet built) lookup table ----
+  // R^T staged in the warps' second stages while the table is built ----
   float* qs = reinterpret_cast<float*>(smem + kFlatSmem);  // [kFusedRows][D]
   __shared__ int merged[kFusedSegs];
   int sid0 = 0, nrows = 0;
@@ -644,13 +692,12 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       nrows = (e.b * a.hkv + e.kvh - sid0 + 1) * G;
     }
     if (threadIdx.x < kFusedSegs) merged[threadIdx.x] = 0;
-    float* Rs = reinterpret_cast<float*>(lut);
     if (!a.q_rotated) {
-      const uint32_t rd = (uint32_t)__cvta_generic_to_shared(Rs);
 #pragma unroll
       for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
-        const int k = threadIdx.x + it * kFlatWarps * 32;
-        cp_async16(rd + k * 16, a.qRT + 4 * k);
+        const int k = threadIdx.x + it * kFlatWarps * 32;  // row k / 32, chunk k % 32
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(r_row(smem, n_before, lut_off, k >> 5)) + (k & 31) * 16;
+        cp_async16(dst, a.qR + 4 * k);
       }
     }
     cp_commit();
@@ -664,47 +711,54 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
         qs[k] = load_any(a.q_in, a.q_dtype, row * D + j);
       }
     }
+    build_lut(lut, a, lane);  // while R^T is in flight
     cp_wait_all();
     __syncthreads();
+    // threads 0..255: output dim i of rows rg, rg + 2, ... (two groups, so R is
+    // read twice from shared memory); the other warps wait at the barrier
     const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
-    constexpr int RPT = kFusedRows / 4;  // rows rg, rg + 4, ... of this thread
-    const int my_rows = nrows > rg ? (nrows - rg + 3) / 4 : 0;
+    constexpr int RPT = kFusedRows / kRotGroups;
+    const int my_rows = (rg < kRotGroups && nrows > rg) ? (nrows - rg + kRotGroups - 1) / kRotGroups : 0;
     float acc[RPT];
 #pragma unroll
-    for (int r = 0; r < RPT; ++r) acc[r] = (a.q_rotated && r < my_rows) ? qs[(rg + 4 * r) * D + i] : 0.f;
-    if (!a.q_rotated) {
+    for (int r = 0; r < RPT; ++r) acc[r] = (a.q_rotated && r < my_rows) ? qs[(rg + kRotGroups * r) * D + i] : 0.f;
+    if (!a.q_rotated && my_rows > 0) {
+      const float* ri = reinterpret_cast<const float*>(r_row(smem, n_before, lut_off, i));
       switch (my_rows) {  // exact row counts: no predicated-off work
-        case 1: rot_rows<1>(Rs, qs, rg, i, acc); break;
-        case 2: rot_rows<2>(Rs, qs, rg, i, acc); break;
-        case 3: rot_rows<3>(Rs, qs, rg, i, acc); break;
-        case 4: rot_rows<4>(Rs, qs, rg, i, acc); break;
-        case 5: rot_rows<5>(Rs, qs, rg, i, acc); break;
-        case 6: rot_rows<6>(Rs, qs, rg, i, acc); break;
-        case 7: rot_rows<7>(Rs, qs, rg, i, acc); break;
-        case 8: rot_rows<8>(Rs, qs, rg, i, acc); break;
+        case 1: rot_rows<1>(ri, qs, rg, acc); break;
+        case 2: rot_rows<2>(ri, qs, rg, acc); break;
+        case 3: rot_rows<3>(ri, qs, rg, acc); break;
+        case 4: rot_rows<4>(ri, qs, rg, acc); break;
+        case 5: rot_rows<5>(ri, qs, rg, acc); break;
+        case 6: rot_rows<6>(ri, qs, rg, acc); break;
+        case 7: rot_rows<7>(ri, qs, rg, acc); break;
+        case 8: rot_rows<8>(ri, qs, rg, acc); break;
+        case 9: rot_rows<9>(ri, qs, rg, acc); break;
+        case 10: rot_rows<10>(ri, qs, rg, acc); break;
+        case 11: rot_rows<11>(ri, qs, rg, acc); break;
+        case 12: rot_rows<12>(ri, qs, rg, acc); break;
+        case 13: rot_rows<13>(ri, qs, rg, acc); break;
+        case 14: rot_rows<14>(ri, qs, rg, acc); break;
+        case 15: rot_rows<15>(ri, qs, rg, acc); break;
+        case 16: rot_rows<16>(ri, qs, rg, acc); break;
         default: break;
       }
     }
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < RPT; ++r)
-      if (rg + 4 * r < nrows) qs[(rg + 4 * r) * D + i] = acc[r] * a.qscale;
+      if (r < my_rows) qs[(rg + kRotGroups * r) * D + i] = acc[r] * a.qscale;
   }
-  // ---- centroid-pair lookup table: lane l < 16 holds K centroid l, lane
-  // 16 + l V centroid l (scaled); entry (e, slot) = (c[e & 15], c[e >> 4]) ----
-  {
-    const float cl = lane < 16 ? a.kcent[lane] * a.kalpha : a.vcent[lane - 16] * a.valpha;
-#pragma unroll
-    for (int it = 0; it < 256 * 64 / (kFlatWarps * 32); ++it) {
-      const int idx = threadIdx.x + it * kFlatWarps * 32;
-      const int e = idx >> 6, vside = (idx & 63) >= 32 ? 16 : 0;
-      const float lo = __shfl_sync(0xffffffffu, cl, vside + (e & 15));
-      const float hi = __shfl_sync(0xffffffffu, cl, vside + (e >> 4));
-      reinterpret_cast<uint32_t*>(lut)[idx] = h2_as_u32(__floats2half2_rn(lo, hi));
-    }
-  }
+  if (!FUSED) build_lut(lut, a, lane);
   __syncthreads();
   if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
+  if (FUSED) {  // second tile, into the stage R^T no longer needs
+    if (begin + 1 < end) {
+      pr.issue(a, st0 + kStageBytes, lane);
+      step(a, pr.w);
+    }
+    cp_commit();
+  }
 
   int64_t x = begin;
   while (x < end) {
@@ -783,9 +837,9 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       const float w2 = ok2 ? vs[g + 16] : 0.f, w3 = ok3 ? vs[g + 24] : 0.f;
       uint32_t pb0, pb1;
       p_pairs(p0 * w0, p1 * w1, g, t, G, pb0, pb1);
-      pv16_1(st, 0, g, t, lanebase, pb0, pb1, oacc);
+      pv16_1<0>(st, vl, lanebase, pb0, pb1, oacc);
       p_pairs(p2 * w2, p3 * w3, g, t, G, pb0, pb1);
-      pv16_1(st, 16, g, t, lanebase, pb0, pb1, oacc);
+      pv16_1<16>(st, vl, lanebase, pb0, pb1, oacc);
     };
 
     for (; x < seg_end; ++x) {
@@ -1524,7 +1578,7 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
   d.q_dtype = f.q_dtype;
   d.q_rotated = f.q_rotated;
   d.qscale = f.qscale;
-  d.qRT = f.qRT;
+  d.qR = f.qR;
   d.vR = f.vR;
   d.cnt = f.cnt;
   d.ctr = f.ctr;

@@ -112,7 +112,7 @@ struct FusedArgs {
   const void* q = nullptr;       // [n_seqs][hq][dim] raw queries
   int32_t q_dtype = 0, q_rotated = 0;
   float qscale = 1.0f;           // scale * log2(e) / kalpha
-  const float* qRT = nullptr;    // K codec R^T
+  const float* qR = nullptr;     // K codec R (row-major)
   const float* vR = nullptr;     // V codec R; null leaves the output rotated
   const int32_t* cnt = nullptr;  // [n_seqs * hkv] partial slots (plan.cnt on the device)
   int32_t* ctr = nullptr;        // [n_seqs * hkv] zero on entry; left zero
