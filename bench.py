@@ -56,7 +56,7 @@ def measured_peaks():
 
 def profile_traffic():
     """dram bytes per decode launch from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "k_decode_flat_config1.md")
+    p = os.path.join(ROOT, "profiles", "k_decode_pair_config1.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -232,7 +232,7 @@ def run_ours(args):
     lc = importlib.import_module("lumen-rs_b200")
     B, hq, hkv, D, ctx, L = CFG["batch"], CFG["hq"], CFG["hkv"], CFG["dim"], CFG["ctx"], args.layers
     steps, warm = args.steps, args.warmup
-    total_new = steps + warm + (args.e2e_steps if rank == 0 else 0) + 8
+    total_new = steps + warm + args.e2e_steps + 8
     pages_per_seq = (ctx + total_new + 255) // 256 + 1
     codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
     cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=B, max_pages=L * B * pages_per_seq + 64,
@@ -325,25 +325,32 @@ def run_ours(args):
     app_bytes = app_vecs * (D * 2 + 8 * 8 + 4)
     app_avg_ms = app_ms / max(app_n, 1)
 
+    # ---- e2e through the C ABI with pinned host buffers, every rank ----
+    qh = qs[:, :].cpu().pin_memory()
+    kh, vh = k1.cpu().pin_memory(), v1.cpu().pin_memory()
+    oh = torch.empty((L, B, hq, D), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        for layer in range(L):
+            cache.append(layer, ids, kh[layer], vh[layer])
+            cache.decode_attn(layer, ids, qh[layer], hq, 1.0, out=oh[layer], out_dtype=lc.LC_BF16)
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / max(args.e2e_steps, 1)
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    h2d = L * (B * hq * D * 2 + 2 * B * hkv * D * 2)
+    d2h = L * B * hq * D * 2
+
     result = None
     if rank == 0:
-        # ---- e2e through the C ABI with pinned host buffers ----
-        qh = qs[:, :].cpu().pin_memory()
-        kh, vh = k1.cpu().pin_memory(), v1.cpu().pin_memory()
-        oh = torch.empty((L, B, hq, D), dtype=torch.bfloat16).pin_memory()
-
-        def e2e_step():
-            for layer in range(L):
-                cache.append(layer, ids, kh[layer], vh[layer])
-                cache.decode_attn(layer, ids, qh[layer], hq, 1.0, out=oh[layer], out_dtype=lc.LC_BF16)
-
-        e2e_step()
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e2e_s = (time.perf_counter() - t0) / max(args.e2e_steps, 1)
-        h2d = L * (B * hq * D * 2 + 2 * B * hkv * D * 2)
-        d2h = L * B * hq * D * 2
         # ---- CPU baseline: oracle decode of one (seq, layer) sample ----
         cpu = None
         if world == 1 and not args.no_cpu:
@@ -368,18 +375,109 @@ def run_ours(args):
                        "avg_launch_us": app_avg_ms * 1e3, "mode": "strict bit-exact"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profile_traffic(),
-                         "kernel": "k_decode_flat", "avg_launch_us": dec_avg_ms * 1e3, "launches": dec_n,
+                         "kernel": "k_decode_pair<4, fused>", "avg_launch_us": dec_avg_ms * 1e3, "launches": dec_n,
                          "bytes_per_launch": kv_bytes_timed, "peak_source": f"{peak_kind} hbm_gbs"},
             "cpu_baseline": cpu,
-            "e2e": {"value": B / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_s * 1e3},
+            "e2e": {"value": world * B / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1e3, "per": "GPU (bytes), whole job (value)"},
             "gpu_launches": launches,
             "breakdown_ms_per_step": {"decode_attn": dec_ms / t_steps, "append": app_ms / t_steps,
-                                      "rotate_merge": other_ms / t_steps, "host_issue": host_ms},
+                                      "other_kernels": other_ms / t_steps, "host_issue": host_ms},
             "clocks": clk.summary(),
             "fill_s": fill_s,
         }
         print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    cache.close()
+
+
+# ----------------------------------------------------------------------------
+# Config 4, second half: one 1,048,576-token sequence split by sequence
+# ----------------------------------------------------------------------------
+def run_longctx(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, local, world = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    lc = importlib.import_module("lumen-rs_b200")
+    split = importlib.import_module("lumen-rs_b200.split")
+    hq, hkv, D, L = CFG["hq"], CFG["hkv"], CFG["dim"], args.layers
+    n_ctx = args.ctx_tokens
+    lo, hi = split.shard_range(n_ctx, rank, world)
+    steps, warm = args.steps, args.warmup
+    extra = steps + warm + 8 if rank == split.owner_of_next(world) else 0
+    pages = (hi - lo + extra + 255) // 256 + 1
+    codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
+    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=1, max_pages=L * pages + 16, max_pages_per_seq=pages,
+                           device=local)
+    s = torch.cuda.ExternalStream(cache.stream(), device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242 + rank)
+    t_fill = time.time()
+    chunk = 16384
+    with torch.cuda.stream(s):
+        for layer in range(L):
+            for c0 in range(lo, hi, chunk):
+                n = min(chunk, hi - c0)
+                k = torch.randn((1, hkv, n, D), generator=gen, device=dev).to(torch.bfloat16)
+                v = torch.randn((1, hkv, n, D), generator=gen, device=dev).to(torch.bfloat16)
+                torch.cuda.current_stream().synchronize()
+                cache.append(layer, [0], k, v, stream=cache.stream())
+    torch.cuda.synchronize()
+    fill_s = time.time() - t_fill
+    dec = split.SplitSequenceDecoder(cache, seq_id=0)
+    owner = rank == split.owner_of_next(world)
+    qs = (torch.randn((L, 1, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    k1 = torch.randn((L, 1, hkv, 1, D), generator=gen, device=dev).to(torch.bfloat16)
+    v1 = torch.randn((L, 1, hkv, 1, D), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty((L, hq, D), device=dev, dtype=torch.float32)
+
+    def step():
+        for layer in range(L):
+            if owner:
+                cache.append(layer, [0], k1[layer], v1[layer])
+            dec.decode(layer, qs[layer], hq, 1.0, out=out[layer])
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(steps):
+            step()
+        ev1.record()
+        ev1.synchronize()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_step = elapsed_ms / steps
+    kv_bytes = n_ctx * hkv * BYTES_PER_TOKEN_HEAD * L  # one pass over the whole context, all ranks together
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": steps / (elapsed_ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"config4 long context: 1 sequence of {n_ctx} tokens split by sequence over "
+                                   f"{world} GPU(s), {L} layers, 32q/8kv, d128, 4-bit K/V; per layer partials + "
+                                   f"NCCL all-gather of (m, l, o) + merge",
+                       "global_batch": 1, "seq_len": n_ctx, "parallelism": f"sequence-split x{world}"},
+            "decode_gbs": kv_bytes / (ms_step / 1e3) / 1e9,
+            "clocks": clk.summary(), "fill_s": fill_s, "mode": "longctx",
+        }), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -396,11 +494,16 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers (32 = config 1; fewer for profiling)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="decode", choices=["decode", "longctx"],
+                    help="decode: config 1 request-sharded; longctx: config 4's 1M-token sequence split by sequence")
+    ap.add_argument("--ctx-tokens", type=int, default=1 << 20, help="longctx: tokens of the split sequence")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "longctx":
+        run_longctx(args)
     else:
         run_ours(args)
 

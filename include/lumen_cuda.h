@@ -263,7 +263,11 @@ int lc_decode_attn_partials(lc_cache* cache, int32_t layer, int32_t n_seqs, cons
 
 /* Merge n_parts sets of partials [n_parts, n_rows] (m, l) and
  * [n_parts, n_rows, head_dim] (o) into out [n_rows, head_dim], un-rotating
- * with the cache's V rotation unless LC_OUT_ROTATED. */
+ * with the cache's V rotation unless LC_OUT_ROTATED: the combine of partial
+ * softmax states of native_quant_attention.rs:190-207, for one context split
+ * by sequence (e.g. partials all-gathered from the ranks holding its
+ * shards). Device inputs are read in place; with device inputs and output
+ * the call is asynchronous on `stream`. */
 int lc_merge_partials(lc_cache* cache, int32_t n_parts, int32_t n_rows, const float* m,
                       const float* l, const float* o, uint32_t flags, void* out, int32_t out_dtype,
                       void* stream);

@@ -870,33 +870,20 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
     cudaStream_t s = c->pick(stream);
     c->order(s);
     const int32_t D = c->cfg.head_dim;
-    // pack into [rows][parts][D+2] (m, l, o) so the merge kernel reads one layout
-    std::vector<float> packed;
+    const size_t nml = (size_t)n_parts * n_rows, no = nml * D;
+    // device inputs are read in place; host inputs are staged as [m | l | o]
     const bool dev = is_device_ptr(m) && is_device_ptr(l) && is_device_ptr(o);
-    std::vector<float> hm, hl, ho;
-    const float *pm = m, *pl = l, *po = o;
-    if (dev) {
-      hm.resize((size_t)n_parts * n_rows);
-      hl.resize(hm.size());
-      ho.resize((size_t)n_parts * n_rows * D);
-      LC_CUDA(cudaMemcpyAsync(hm.data(), m, hm.size() * 4, cudaMemcpyDeviceToHost, s));
-      LC_CUDA(cudaMemcpyAsync(hl.data(), l, hl.size() * 4, cudaMemcpyDeviceToHost, s));
-      LC_CUDA(cudaMemcpyAsync(ho.data(), o, ho.size() * 4, cudaMemcpyDeviceToHost, s));
-      LC_CUDA(cudaStreamSynchronize(s));
-      pm = hm.data();
-      pl = hl.data();
-      po = ho.data();
+    const float *dm = m, *dl = l, *dov = o;
+    if (!dev) {
+      c->part.ensure(2 * nml + no, s);
+      float* base = c->part.p;
+      LC_CUDA(cudaMemcpyAsync(base, m, nml * 4, cudaMemcpyDefault, s));
+      LC_CUDA(cudaMemcpyAsync(base + nml, l, nml * 4, cudaMemcpyDefault, s));
+      LC_CUDA(cudaMemcpyAsync(base + 2 * nml, o, no * 4, cudaMemcpyDefault, s));
+      dm = base;
+      dl = base + nml;
+      dov = base + 2 * nml;
     }
-    packed.resize((size_t)n_rows * n_parts * (D + 2));
-    for (int32_t r = 0; r < n_rows; ++r)
-      for (int32_t p = 0; p < n_parts; ++p) {
-        float* dst = &packed[((size_t)r * n_parts + p) * (D + 2)];
-        dst[0] = pm[(size_t)p * n_rows + r];
-        dst[1] = pl[(size_t)p * n_rows + r];
-        std::memcpy(dst + 2, po + ((size_t)p * n_rows + r) * D, D * 4);
-      }
-    c->part.ensure(packed.size(), s);
-    LC_CUDA(cudaMemcpyAsync(c->part.p, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice, s));
     const size_t obytes = (size_t)n_rows * D * dtype_size(out_dtype);
     const bool host_out = !is_device_ptr(out);
     void* dout = out;
@@ -904,11 +891,11 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    launch_merge(c->part.p, nullptr, 1, n_parts, n_rows, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout,
-                 out_dtype, nullptr, nullptr, nullptr, 1.0f, s);
+    launch_merge_parts(dm, dl, dov, n_parts, n_rows, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype,
+                       s);
     ++c->launches;
     if (host_out) LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
-    LC_CUDA(cudaStreamSynchronize(s));
+    if (host_out || !dev) LC_CUDA(cudaStreamSynchronize(s));
   });
 }
 

@@ -1226,7 +1226,10 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
 // ---------------------------------------------------------------------------
 
 struct MergeDev {
-  const float* part;
+  const float* part;    // packed slots, or null: the separate arrays below
+  const float* m_in;    // [slots][n_rows]
+  const float* l_in;    // [slots][n_rows]
+  const float* o_in;    // [slots][n_rows][D]
   const int32_t* cnt;
   int32_t G, max_slots, n_rows, D;
   float oscale;
@@ -1258,10 +1261,24 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
     const int64_t group = row / a.G;
     const int gh = row % a.G;
     const int n = a.cnt ? a.cnt[group] : a.max_slots;
-    const float* p = a.part + (group * a.max_slots * a.G + gh) * PS;
-    const int64_t cs = (int64_t)a.G * PS;
+    // slot c of this row: m at pm[c * ms], l at pl[c * ms], o at po + c * os
+    const float *pm, *pl, *po;
+    int64_t ms, os;
+    if (a.part) {
+      const float* p = a.part + (group * a.max_slots * a.G + gh) * PS;
+      pm = p;
+      pl = p + 1;
+      po = p + 2;
+      ms = os = (int64_t)a.G * PS;
+    } else {
+      pm = a.m_in + row;
+      pl = a.l_in + row;
+      po = a.o_in + (int64_t)row * D;
+      ms = a.n_rows;
+      os = (int64_t)a.n_rows * D;
+    }
     float M = -INFINITY;
-    for (int c = lane; c < n; c += 32) M = fmaxf(M, p[c * cs]);
+    for (int c = lane; c < n; c += 32) M = fmaxf(M, pm[c * ms]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float L = 0.f;
@@ -1271,15 +1288,15 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
     for (int c0 = 0; c0 < n; c0 += 32) {
       float wl = 0.f;
       if (c0 + lane < n) {
-        const float mc = p[(c0 + lane) * cs];
+        const float mc = pm[(c0 + lane) * ms];
         wl = mc == -INFINITY ? 0.f : exp2f(mc - M);
-        L += wl * p[(c0 + lane) * cs + 1];
+        L += wl * pl[(c0 + lane) * ms];
       }
       const int nn = min(32, n - c0);
 #pragma unroll 8
       for (int u = 0; u < nn; ++u) {
         const float w = __shfl_sync(0xffffffffu, wl, u);
-        const float2* pc = reinterpret_cast<const float2*>(p + (c0 + u) * cs + 2 + lane * per);
+        const float2* pc = reinterpret_cast<const float2*>(po + (c0 + u) * os + lane * per);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           if (2 * k < per) {
@@ -1597,7 +1614,18 @@ void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
                   float oscale, cudaStream_t s) {
   if (n_rows <= 0) return;
-  MergeDev d{part, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out, o_out};
+  MergeDev d{part, nullptr, nullptr, nullptr, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out,
+             o_out};
+  const int blocks = (n_rows + kMergeWarps - 1) / kMergeWarps;
+  const size_t smem = (size_t)kMergeWarps * dim * sizeof(float);
+  k_merge<<<blocks, kMergeWarps * 32, smem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
+}
+
+void launch_merge_parts(const float* m, const float* l, const float* o, int32_t n_parts, int32_t n_rows, int32_t dim,
+                        const float* R, void* out, int32_t out_dtype, cudaStream_t s) {
+  if (n_rows <= 0) return;
+  MergeDev d{nullptr, m, l, o, nullptr, 1, n_parts, n_rows, dim, 1.0f, R, out, out_dtype, nullptr, nullptr, nullptr};
   const int blocks = (n_rows + kMergeWarps - 1) / kMergeWarps;
   const size_t smem = (size_t)kMergeWarps * dim * sizeof(float);
   k_merge<<<blocks, kMergeWarps * 32, smem, s>>>(d);

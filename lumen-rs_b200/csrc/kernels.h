@@ -138,6 +138,11 @@ void launch_attend_values(const float* w, const CodecDev& vc, const uint64_t* pa
 void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
                   float oscale, cudaStream_t s);
+// Merge n_parts partials laid out as separate arrays m, l [n_parts][n_rows]
+// and o [n_parts][n_rows][dim] (e.g. gathered from the ranks of a split
+// sequence), un-rotating by R unless it is null.
+void launch_merge_parts(const float* m, const float* l, const float* o, int32_t n_parts, int32_t n_rows, int32_t dim,
+                        const float* R, void* out, int32_t out_dtype, cudaStream_t s);
 bool decode_fast_path(int dim, int kbits, int vbits, int G);
 
 // ---- fixed scratch of lc_decode_attn_noalloc (noalloc.cu) -----------------
