@@ -13,10 +13,11 @@ deviation, softmax scale 1. The 9 GB cache is far larger than L2 (126 MB),
 so every step streams it from HBM (no flush needed).
 
 `value` is whole-job decode tokens/s with inputs resident in HBM. `e2e`
-drives the same step through the C ABI with pinned host buffers: the query,
-new K/V and output cross PCIe every layer, and every call returns its result
-to the host. Under torchrun each rank runs its own 32 sequences (weak
-scaling, no collective on the data path).
+drives the same step through the public API from pinned host memory: every
+step copies its inputs (all layers' queries and new K/V) to the device,
+runs the layers, and reads every output back before the next step. Under
+torchrun each rank runs its own 32 sequences (weak scaling, no collective on
+the data path).
 
 `--impl reference` times the reference's CPU path (the oracle's C++
 restatement of turboquant-cache SimpleCache: attend_keys, softmax,
@@ -25,6 +26,7 @@ attend_values) on a bounded sample on all host cores.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import importlib
 import json
 import os
@@ -81,6 +83,27 @@ class ClockSampler:
         self.lines = []
 
     def __enter__(self):
+        self.nvml = False
+        try:  # NVML in a thread: a sample every few ms, so short timed regions get many
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.h = None
+            try:  # the CUDA device by PCI address (NVML and CUDA orders can differ)
+                import torch
+
+                pr = torch.cuda.get_device_properties(self.device)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(self.device)
+            self.nvml = True
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=self._poll, args=(pynvml,), daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = False
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
@@ -95,7 +118,27 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def _poll(self, nv):
+        bits = [("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                ("sw_power_cap", 0x4)]
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                r = get(self.h)
+                flags = ["Active" if r & b else "Not Active" for _, b in bits]
+                self.lines.append(",".join([str(self.device), str(sm), str(mx), "0", hex(r)] + flags))
+            except Exception:
+                pass
+            self.stop.wait(0.004)
+
     def __exit__(self, *a):
+        if self.nvml:
+            self.stop.set()
+            self.t.join(timeout=2)
+            return
         if self.proc:
             self.proc.terminate()
             try:
@@ -296,7 +339,7 @@ def run_ours(args):
         ev1.record(s)
         ev1.synchronize()
     elapsed_ms = ev0.elapsed_time(ev1)
-    launches = cache.kernel_launches() - launches0
+    launches = cache.kernel_launches() - launches0  # timed region only
     ctx1 = cache.ring_state(0, 0)["view_len"]
     # per-kernel device times: CUDA events around each launch, a separate pass
     t_steps = max(2, min(steps, 5))
@@ -305,8 +348,6 @@ def run_ours(args):
         step()
     dec_ms, dec_n, app_ms, app_n, other_ms = cache.timing(0)
     ctx2 = cache.ring_state(0, 0)["view_len"]
-    launches = cache.kernel_launches() - launches0
-    ctx1 = cache.ring_state(0, 0)["view_len"]
     if world > 1:
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -325,15 +366,25 @@ def run_ours(args):
     app_bytes = app_vecs * (D * 2 + 8 * 8 + 4)
     app_avg_ms = app_ms / max(app_n, 1)
 
-    # ---- e2e through the C ABI with pinned host buffers, every rank ----
-    qh = qs[:, :].cpu().pin_memory()
+    # ---- e2e through the public API, every rank: each step copies its inputs
+    # (all layers' q and new K/V) from pinned host memory to the device, runs
+    # the layers, and reads all outputs back to pinned host memory ----
+    qh = qs.cpu().pin_memory()
     kh, vh = k1.cpu().pin_memory(), v1.cpu().pin_memory()
     oh = torch.empty((L, B, hq, D), dtype=torch.bfloat16).pin_memory()
+    qd, kd, vd = torch.empty_like(qs), torch.empty_like(k1), torch.empty_like(v1)
+    od = torch.empty_like(out)
 
     def e2e_step():
+        # torch's current stream for the copies and the cache calls alike
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
         for layer in range(L):
-            cache.append(layer, ids, kh[layer], vh[layer])
-            cache.decode_attn(layer, ids, qh[layer], hq, 1.0, out=oh[layer], out_dtype=lc.LC_BF16)
+            cache.append(layer, ids, kd[layer], vd[layer])
+            cache.decode_attn(layer, ids, qd[layer], hq, 1.0, out=od[layer], out_dtype=lc.LC_BF16)
+        oh.copy_(od, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
 
     e2e_step()
     if world > 1:
@@ -485,6 +536,7 @@ def run_longctx(args):
 
 
 def main():
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

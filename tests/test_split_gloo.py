@@ -132,3 +132,50 @@ def test_shard_range_partition():
             assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         split.shard_range(10, 2, 2)
+
+
+def _worker_rank_fails(rank, world, port, result_dir):
+    """Rank 1 leaves before the gather; rank 0's decode must fail, not hang."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import helpers
+    import pyoracle as orc
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=3))
+    if rank == 1:
+        return  # leaves between steps, with nothing of its own in flight
+    split = importlib.import_module("lumen-rs_b200.split")
+    dim, hkv, hq, n_tok = 64, 2, 8, 64
+    t = orc.Tables.generate(dim, 4, 0, 42)
+    kv = helpers.kv(orc, 31, 2, hkv, n_tok, dim)
+    lo, hi = split.shard_range(n_tok, rank, world)
+    dec = split.SplitSequenceDecoder(OracleShard(orc, t, kv[0], kv[1], lo, hi))
+    q = torch.from_numpy(helpers.queries(orc, 5, 1, hq, dim))
+    try:
+        dec.decode(0, q, hq, scale=1.0 / np.sqrt(dim))
+        status = "completed"
+    except Exception as e:  # the collective's timeout or closed-connection error
+        status = "error: " + type(e).__name__
+    with open(os.path.join(result_dir, "rank0.txt"), "w") as f:
+        f.write(status)
+
+
+def test_split_decode_peer_failure_is_an_error(tmp_path):
+    """A rank that exits before the partials all-gather: the surviving rank's
+    split decode raises within the process-group timeout instead of hanging."""
+    import time
+
+    import torch.multiprocessing as mp
+
+    t0 = time.time()
+    mp.spawn(_worker_rank_fails, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    status = (tmp_path / "rank0.txt").read_text()
+    assert status.startswith("error"), status
+    assert time.time() - t0 < 120
