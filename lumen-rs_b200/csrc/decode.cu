@@ -492,23 +492,6 @@ __device__ __forceinline__ uint32_t pair_vlane(int g, int t) {
   return (uint32_t)(t * 64 + (((g >> 1) ^ (t & 2)) << 4) + (g & 1) * 8);
 }
 
-// P^T B fragments of column g = 2 * head + part for k slots (2t, 2t+1) =
-// tokens (t, t+8) and (2t+8, 2t+9) = tokens (t+4, t+12) of a 16-token half.
-// This lane holds p' of its own head t for tokens (g, g+8): pu, pv.
-__device__ __forceinline__ void p_pairs(float pu, float pv, int g, int t, int G, uint32_t& pb0, uint32_t& pb1) {
-  const __half2 hi = __floats2half2_rn(pu, pv);
-  const float2 f = __half22float2(hi);
-  const uint32_t h = h2_as_u32(hi), l = h2_as_u32(__floats2half2_rn(pu - f.x, pv - f.y));
-  const int head = g >> 1;
-  const int src0 = t * 4 + head, src1 = (t + 4) * 4 + head;
-  const uint32_t x0 = __shfl_sync(0xffffffffu, h, src0), y0 = __shfl_sync(0xffffffffu, l, src0);
-  const uint32_t x1 = __shfl_sync(0xffffffffu, h, src1), y1 = __shfl_sync(0xffffffffu, l, src1);
-  const bool lo = g & 1;
-  pb0 = lo ? y0 : x0;
-  pb1 = lo ? y1 : x1;
-  if (head >= G) pb0 = pb1 = 0u;
-}
-
 // Fused path: rows of query / output kept in shared memory per CTA. A CTA
 // touches at most kFusedSegs (sequence, kv head) segments (plan_decode
 // checks), i.e. kFusedSegs * G <= 32 rows.
@@ -632,6 +615,35 @@ __device__ __forceinline__ void rot_rows(const float* ri, const float* qs, int r
   }
 }
 
+// P^T B fragments of both 16-token halves through shared memory, in the
+// stage's K area (read completely by then). Lane (g, t) holds p' of head t
+// for tokens (g, g + 8) of half 0 (pa, pb) and of half 1 (pc, pd) and writes
+// the f16 value and residual pairs; lane (g, t) then reads column g = (head
+// g / 2, part g & 1) at token pairs t (b0) and t + 4 (b1). Word of (half,
+// part, head, pair): half * 64 + part * 32 + head * 8 + (pair ^ 4 part), so
+// both the writes and the reads of a warp hit 32 distinct banks.
+__device__ __forceinline__ void p_exchange(const uint8_t* st, float pa, float pb_, float pc, float pd, int g, int t,
+                                           int G, uint32_t (&pb)[2][2]) {
+  uint32_t* ps = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(st) + kStK);
+  const __half2 h0 = __floats2half2_rn(pa, pb_), h1 = __floats2half2_rn(pc, pd);
+  const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+  const uint32_t l0 = h2_as_u32(__floats2half2_rn(pa - f0.x, pb_ - f0.y));
+  const uint32_t l1 = h2_as_u32(__floats2half2_rn(pc - f1.x, pd - f1.y));
+  __syncwarp();
+  ps[t * 8 + g] = h2_as_u32(h0);
+  ps[32 + t * 8 + (g ^ 4)] = l0;
+  ps[64 + t * 8 + g] = h2_as_u32(h1);
+  ps[96 + t * 8 + (g ^ 4)] = l1;
+  __syncwarp();
+  const int head = g >> 1, part = g & 1;
+  const int base = part * 32 + head * 8, sw = part << 2;
+  const bool live = head < G;
+  pb[0][0] = live ? ps[base + (t ^ sw)] : 0u;
+  pb[0][1] = live ? ps[base + ((t + 4) ^ sw)] : 0u;
+  pb[1][0] = live ? ps[64 + base + (t ^ sw)] : 0u;
+  pb[1][1] = live ? ps[64 + base + ((t + 4) ^ sw)] : 0u;
+}
+
 template <int G, bool FUSED>
 __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid_constant__ DecodeDev a) {
   static_assert(G >= 1 && G <= 4, "pair layout holds 4 heads");
@@ -647,9 +659,11 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
   const uint32_t vl = pair_vlane(g, t);
-  const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
-  const int64_t begin = w * a.per_warp;
-  const int64_t end = min(begin + a.per_warp, a.total_tiles);
+  // tile indices fit in 32 bits (plan_decode: total_tiles < 2^31)
+  const int w = blockIdx.x * kFlatWarps + warp;
+  const int pw = (int)a.per_warp;
+  const int begin = w * pw;
+  const int end = min(begin + pw, (int)a.total_tiles);
   uint8_t* stages = warp < n_before ? smem + warp * kWarpBytes
                                     : smem + lut_off + kLutBytes + (warp - n_before) * kWarpBytes;
   const uint32_t st0 = (uint32_t)__cvta_generic_to_shared(stages);
@@ -684,8 +698,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   __shared__ int merged[kFusedSegs];
   int sid0 = 0, nrows = 0;
   if constexpr (FUSED) {
-    const int64_t cb = (int64_t)blockIdx.x * kFlatWarps * a.per_warp;
-    const int64_t ce = min(cb + (int64_t)kFlatWarps * a.per_warp, a.total_tiles);
+    const int cb = blockIdx.x * kFlatWarps * pw;
+    const int ce = min(cb + kFlatWarps * pw, (int)a.total_tiles);
     if (cb < ce) {
       const Walk f = locate_warp(a, cb, lane), e = locate_warp(a, ce - 1, lane);
       sid0 = f.b * a.hkv + f.kvh;
@@ -760,14 +774,13 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     cp_commit();
   }
 
-  int64_t x = begin;
+  int x = begin;
   while (x < end) {
     // ---- a new (sequence, kv head) segment ----
     const int b = cw.b, kvh = cw.kvh;
     const int n_valid = (int)a.si()[2 * b];
-    const int64_t seg_first = a.sg()[b] + (int64_t)kvh * cw.nt;
-    const int64_t seg_end = min(end, seg_first + cw.nt);
-    const int64_t slot_base = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / a.per_warp);
+    const int seg_first = (int)a.sg()[b] + kvh * cw.nt;
+    const int seg_end = min(end, seg_first + cw.nt);
     // B fragments of Q: column g = (head g/2, part g&1), dims 32t + 4s + {0,1} / {2,3}
     uint32_t qb[8][2];
     {
@@ -797,8 +810,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
 
     auto tile = [&](auto masked) {
       constexpr bool MASKED = decltype(masked)::value;
-      const int stage = (int)((x - begin) & 1);
-      const int tok = cw.tile * kTileTok;
+      const int stage = (x - begin) & 1;
+      const int tok = (x - seg_first) * kTileTok;
       const uint8_t* st = stages + stage * kStageBytes;
       float sa0[4] = {0.f, 0.f, 0.f, 0.f}, sa1[4] = {0.f, 0.f, 0.f, 0.f};
       float sb0[4] = {0.f, 0.f, 0.f, 0.f}, sb1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -815,45 +828,56 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       const float z3 = ((sb0[2] + sb1[2]) + (sb0[3] + sb1[3])) * ks[g + 24];
       const float s0_ = ok0 ? z0 : -INFINITY, s1_ = ok1 ? z1 : -INFINITY;
       const float s2_ = ok2 ? z2 : -INFINITY, s3_ = ok3 ? z3 : -INFINITY;
+      // lazy rescale: the running max m moves only when some score exceeds it
+      // by more than kTau, which a warp vote detects without the cross-lane
+      // max; the reduction and rescale run only then
       float mx = fmaxf(fmaxf(s0_, s1_), fmaxf(s2_, s3_));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      if (mx > m + kTau) {
-        const float al = ex2(m - mx);
-        l *= al;
+      if (__any_sync(0xffffffffu, mx > m + kTau)) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        if (mx > m + kTau) {
+          const float al = ex2(m - mx);
+          l *= al;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          oacc[i][0] *= al;
-          oacc[i][1] *= al;
-          oacc[i][2] *= al;
-          oacc[i][3] *= al;
+          for (int i = 0; i < 8; ++i) {
+            oacc[i][0] *= al;
+            oacc[i][1] *= al;
+            oacc[i][2] *= al;
+            oacc[i][3] *= al;
+          }
+          m = mx;
         }
-        m = mx;
       }
       const float p0 = ex2(s0_ - m), p1 = ex2(s1_ - m), p2 = ex2(s2_ - m), p3 = ex2(s3_ - m);
       l += (p0 + p1) + (p2 + p3);
       const float w0 = ok0 ? vs[g] : 0.f, w1 = ok1 ? vs[g + 8] : 0.f;
       const float w2 = ok2 ? vs[g + 16] : 0.f, w3 = ok3 ? vs[g + 24] : 0.f;
-      uint32_t pb0, pb1;
-      p_pairs(p0 * w0, p1 * w1, g, t, G, pb0, pb1);
-      pv16_1<0>(st, vl, lanebase, pb0, pb1, oacc);
-      p_pairs(p2 * w2, p3 * w3, g, t, G, pb0, pb1);
-      pv16_1<16>(st, vl, lanebase, pb0, pb1, oacc);
+      // P^T fragments through shared memory (this stage's K bytes are spent)
+      uint32_t pb[2][2];
+      p_exchange(st, p0 * w0, p1 * w1, p2 * w2, p3 * w3, g, t, G, pb);
+      pv16_1<0>(st, vl, lanebase, pb[0][0], pb[0][1], oacc);
+      pv16_1<16>(st, vl, lanebase, pb[1][0], pb[1][1], oacc);
     };
 
     for (; x < seg_end; ++x) {
       cp_wait_one();
       __syncwarp();
-      if (cw.tile * kTileTok + kTileTok <= n_valid) tile(std::integral_constant<bool, false>());
+      if ((x - seg_first) * kTileTok + kTileTok <= n_valid) tile(std::integral_constant<bool, false>());
       else tile(std::integral_constant<bool, true>());
       __syncwarp();
       if (x + kStages < end) {
-        pr.issue(a, st0 + (int)((x - begin) & 1) * kStageBytes, lane);
+        pr.issue(a, st0 + ((x - begin) & 1) * kStageBytes, lane);
         step(a, pr.w);
       }
       cp_commit();
-      step(a, cw);
+    }
+    // the next segment in flat order (kv heads of b, then sequences with tiles)
+    if (++cw.kvh == a.hkv) {
+      cw.kvh = 0;
+      do {
+        ++cw.b;
+      } while (cw.b < a.n_seqs && (cw.nt = tiles_of(a, cw.b)) == 0);
     }
     // ---- flush the segment's partial: head t, dims 16g + 2i (+1) ----
     float L = l;
@@ -861,7 +885,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     L += __shfl_xor_sync(0xffffffffu, L, 8);
     L += __shfl_xor_sync(0xffffffffu, L, 16);
     if (t < G) {
-      float* row = a.part + (slot_base * G + t) * PS;
+      const int64_t slot = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / pw);
+      float* row = a.part + (slot * G + t) * PS;
       if (g == 0) {
         row[0] = m;
         row[1] = L;
@@ -1521,6 +1546,8 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
 }
 
 static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
+  LC_REQUIRE(p.total_tiles < (int64_t(1) << 31) - (int64_t)kFlatWarps * 148 * 2, LC_ERR_INVALID,
+             "decode call too large: split it (at most 2^31 tiles of 32 tokens x kv head)");
   DecodeDev d{};
   if (!a.seqinfo) {
     LC_REQUIRE(a.h_seqinfo && a.n_seqs <= kInlineSeqs && (int64_t)a.n_seqs * a.hkv <= kInlineCnt, LC_ERR_STATE,
