@@ -771,7 +771,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     f.q_rotated = (flags & LC_Q_ROTATED) ? 1 : 0;
     f.qscale = qscale;
     f.qR = c->dk.R;
-    f.vR = (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R;
+    f.vRT = (flags & LC_OUT_ROTATED) ? nullptr : c->dv.RTd;
     f.cnt = dcnt;
     f.ctr = c->ctr.p;
     f.out = fused_out;

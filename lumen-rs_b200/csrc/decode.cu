@@ -145,7 +145,7 @@ struct DecodeDev {
   int32_t q_dtype, q_rotated;
   float qscale;
   const float* qR;       // K codec R (row-major): q' = R q
-  const float* vR;       // V codec R: out = R^T o (null: leave rotated)
+  const float* vRT;      // V codec R^T (row-major): out = R^T o (null: leave rotated)
   const int32_t* cnt;    // [n_seqs * hkv] partial slots
   int32_t* ctr;          // [n_seqs * hkv] arrival counters, zero between launches
   void* out;
@@ -498,79 +498,7 @@ __device__ __forceinline__ uint32_t pair_vlane(int g, int t) {
 constexpr int kFusedSegs = 8;
 constexpr int kFusedRows = 32;
 constexpr int kFusedSmem = kFlatSmem + kFusedRows * 128 * 4;
-
-// Merge of one (sequence, kv head)'s split partials by the warp that
-// completed it: all G heads at once, lane c holding slot c's (m, l) of each
-// head and accumulating dims 4 lane .. 4 lane + 3; the normalised rows
-// (rotated basis) go to dst [G][128]. Partials written by other SMs are
-// read from L2 (ld.global.cg).
-template <int G>
-__device__ __forceinline__ void merge_segment(const DecodeDev& a, int sid, int lane, float* dst) {
-  constexpr int D = 128, PS = D + 2;
-  const int n = a.ct()[sid];
-  const int64_t cs = (int64_t)G * PS;
-  const float* p = a.part + (int64_t)sid * a.max_slots * cs;
-  float M[G], L[G], o[G][4];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    M[h] = -INFINITY;
-    L[h] = 0.f;
-    o[h][0] = o[h][1] = o[h][2] = o[h][3] = 0.f;
-  }
-  // slot maxima; slots 0..31 keep (m, l) in registers for the weights
-  float mc[G], lc[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    mc[h] = lane < n ? __ldcg(p + lane * cs + h * PS) : -INFINITY;
-    lc[h] = lane < n ? __ldcg(p + lane * cs + h * PS + 1) : 0.f;
-    M[h] = mc[h];
-  }
-  for (int c = lane + 32; c < n; c += 32) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) M[h] = fmaxf(M[h], __ldcg(p + c * cs + h * PS));
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M[h] = fmaxf(M[h], __shfl_xor_sync(0xffffffffu, M[h], off));
-  }
-  for (int c0 = 0; c0 < n; c0 += 32) {
-    float wl[G];
-    const int c = c0 + lane;
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      if (c0 > 0) {
-        mc[h] = c < n ? __ldcg(p + c * cs + h * PS) : -INFINITY;
-        lc[h] = c < n ? __ldcg(p + c * cs + h * PS + 1) : 0.f;
-      }
-      wl[h] = mc[h] == -INFINITY ? 0.f : exp2f(mc[h] - M[h]);
-      L[h] += wl[h] * lc[h];
-    }
-    const int nn = min(32, n - c0);
-#pragma unroll 8
-    for (int u = 0; u < nn; ++u) {
-      const float* pc = p + (int64_t)(c0 + u) * cs + 2 + 4 * lane;
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float wv = __shfl_sync(0xffffffffu, wl[h], u);
-        const float2 v0 = __ldcg(reinterpret_cast<const float2*>(pc + h * PS));
-        const float2 v1 = __ldcg(reinterpret_cast<const float2*>(pc + h * PS + 2));
-        o[h][0] = fmaf(wv, v0.x, o[h][0]);
-        o[h][1] = fmaf(wv, v0.y, o[h][1]);
-        o[h][2] = fmaf(wv, v1.x, o[h][2]);
-        o[h][3] = fmaf(wv, v1.y, o[h][3]);
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L[h] += __shfl_xor_sync(0xffffffffu, L[h], off);
-    const float inv = L[h] > 0.f ? a.oscale / L[h] : 0.f;
-    *reinterpret_cast<float4*>(dst + h * D + 4 * lane) =
-        make_float4(o[h][0] * inv, o[h][1] * inv, o[h][2] * inv, o[h][3] * inv);
-  }
-}
+constexpr int kMergeMaxSlots = kLutBytes / 4 / kFusedRows;  // slot weights per row in the table area
 
 // Centroid-pair lookup table: lane l < 16 holds K centroid l, lane 16 + l V
 // centroid l (scaled); entry (e, slot) = (c[e & 15], c[e >> 4]), slots 0..31
@@ -897,59 +825,156 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
             make_float2(oacc[i][0] + oacc[i][1], oacc[i][2] + oacc[i][3]);
     }
     if constexpr (FUSED) {
-      // The warp that completes a segment's last slot merges the segment's
-      // partials into its q' rows in qs (no warp of this CTA reads them again).
+      // Count this warp's slot of the segment; the warp that completes it
+      // marks the segment for this CTA's epilogue to merge.
       __threadfence();
       __syncwarp();
       const int sid = b * a.hkv + kvh;
       int old = 0;
       if (lane == 0) old = atomicAdd(a.ctr + sid, 1);
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == a.ct()[sid] - 1) {
-        __threadfence();
-        if (lane == 0) {
-          a.ctr[sid] = 0;  // zero again for the next launch
-          merged[sid - sid0] = 1;
-        }
-        merge_segment<G>(a, sid, lane, qs + (sid - sid0) * G * D);
+      if (old == a.ct()[sid] - 1 && lane == 0) {
+        a.ctr[sid] = 0;  // zero again for the next launch
+        merged[sid - sid0] = 1;
       }
     }
   }
   cp_wait_all();
   if constexpr (FUSED) {
-    // ---- un-rotate the merged rows: out = R^T o, R staged over the table ----
+    // ---- epilogue: the whole CTA merges the segments its warps completed
+    // (their q' rows in qs are no longer read) and writes them un-rotated ----
     __syncthreads();
-    float* Rs = reinterpret_cast<float*>(lut);
-    if (a.vR) {
-      const uint32_t rd = (uint32_t)__cvta_generic_to_shared(Rs);
+    __shared__ int mrow[kFusedRows];  // rows of the merged segments, compacted
+    __shared__ int n_mrows;
+    if (threadIdx.x == 0) {
+      int k = 0;
+      for (int r = 0; r < nrows; ++r)
+        if (merged[r / G]) mrow[k++] = r;
+      n_mrows = k;
+    }
+    __syncthreads();
+    const int nm = n_mrows;
+    if (nm == 0) return;  // uniform over the CTA
+    __threadfence();      // the other warps' partials, read below from L2
+    // V's R^T rows into the second pipeline stages, free now
+    if (a.vRT) {
 #pragma unroll
       for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
         const int k = threadIdx.x + it * kFlatWarps * 32;
-        cp_async16(rd + k * 16, a.vR + 4 * k);
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(r_row(smem, n_before, lut_off, k >> 5)) + (k & 31) * 16;
+        cp_async16(dst, a.vRT + 4 * k);
       }
-      cp_commit();
-      cp_wait_all();
-      __syncthreads();
     }
-    const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
-    for (int r = rg; r < nrows; r += 4) {
-      if (!merged[r / G]) continue;
+    cp_commit();
+    // slot weights 2^(m_c - M) per merged row into the table area, warp per row
+    float* wt = reinterpret_cast<float*>(lut);  // [kFusedRows][kMergeMaxSlots]
+    __shared__ float linv[kFusedRows];
+    for (int k = warp; k < nm; k += kFlatWarps) {
+      const int r = mrow[k];
       const int sid = sid0 + r / G;
-      const int64_t orow = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G;
-      float v;
-      if (a.vR) {
-        const float* xr = qs + r * D;
-        float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll 8
-        for (int j = 0; j < D; j += 2) {
-          acc0 = fmaf(Rs[j * D + i], xr[j], acc0);
-          acc1 = fmaf(Rs[(j + 1) * D + i], xr[j + 1], acc1);
+      const int n = a.ct()[sid];
+      const float* pr_ = a.part + ((int64_t)sid * a.max_slots * G + r % G) * PS;
+      const int64_t cs = (int64_t)G * PS;
+      float mc = lane < n ? __ldcg(pr_ + lane * cs) : -INFINITY;
+      float lc = lane < n ? __ldcg(pr_ + lane * cs + 1) : 0.f;
+      float M = mc;
+      for (int c = lane + 32; c < n; c += 32) M = fmaxf(M, __ldcg(pr_ + c * cs));
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.f;
+      for (int c = lane; c < n; c += 32) {
+        if (c >= 32) {
+          mc = __ldcg(pr_ + c * cs);
+          lc = __ldcg(pr_ + c * cs + 1);
         }
-        v = acc0 + acc1;
-      } else {
-        v = qs[r * D + i];
+        const float wv = mc == -INFINITY ? 0.f : exp2f(mc - M);
+        L += wv * lc;
+        wt[k * kMergeMaxSlots + c] = wv;
       }
-      store_any(a.out, a.out_dtype, orow * D + i, v);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (lane == 0) linv[k] = L > 0.f ? a.oscale / L : 0.f;
+    }
+    __syncthreads();
+    // o[k][i] = sum_c w_c o_c[k][i] / L for the compacted rows k, into qs:
+    // thread items u = tid + 512 j (j < 4), 8 slots of every item in flight
+    constexpr int NT = kFlatWarps * 32;
+    float* om = qs;  // [nm][D] over the q' rows, no longer read
+    for (int u0 = 0; u0 < nm * D; u0 += 4 * NT) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const float* po[4];
+      const float* wr[4];
+      int n[4];
+      int64_t cs[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + threadIdx.x + j * NT;
+        const int k = u < nm * D ? (u >> 7) : 0;
+        const int r = mrow[k], i = u & (D - 1);
+        const int sid = sid0 + r / G;
+        n[j] = u < nm * D ? a.ct()[sid] : 0;
+        po[j] = a.part + ((int64_t)sid * a.max_slots * G + r % G) * PS + 2 + i;
+        cs[j] = (int64_t)G * PS;
+        wr[j] = wt + k * kMergeMaxSlots;
+      }
+      const int nmax = max(max(n[0], n[1]), max(n[2], n[3]));
+      for (int c0 = 0; c0 < nmax; c0 += 8) {
+        float v[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) v[j][c] = c0 + c < n[j] ? __ldcg(po[j] + (c0 + c) * cs[j]) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c0 + c < n[j]) acc[j] = fmaf(wr[j][c0 + c], v[j][c], acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + threadIdx.x + j * NT;
+        if (u < nm * D) om[u] = acc[j] * linv[u >> 7];
+      }
+    }
+    cp_wait_all();
+    __syncthreads();
+    // out = R^T o: thread (i, rg) over compacted rows rg, rg + 2, ... (two
+    // groups), R^T rows read as 16 bytes from the second stages
+    const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
+    const int my = (rg < kRotGroups && nm > rg) ? (nm - rg + kRotGroups - 1) / kRotGroups : 0;
+    float acc[kFusedRows / kRotGroups];
+#pragma unroll
+    for (int r = 0; r < kFusedRows / kRotGroups; ++r) acc[r] = (!a.vRT && r < my) ? om[(rg + kRotGroups * r) * D + i] : 0.f;
+    if (a.vRT && my > 0) {
+      const float* ri = reinterpret_cast<const float*>(r_row(smem, n_before, lut_off, i));
+      switch (my) {
+        case 1: rot_rows<1>(ri, om, rg, acc); break;
+        case 2: rot_rows<2>(ri, om, rg, acc); break;
+        case 3: rot_rows<3>(ri, om, rg, acc); break;
+        case 4: rot_rows<4>(ri, om, rg, acc); break;
+        case 5: rot_rows<5>(ri, om, rg, acc); break;
+        case 6: rot_rows<6>(ri, om, rg, acc); break;
+        case 7: rot_rows<7>(ri, om, rg, acc); break;
+        case 8: rot_rows<8>(ri, om, rg, acc); break;
+        case 9: rot_rows<9>(ri, om, rg, acc); break;
+        case 10: rot_rows<10>(ri, om, rg, acc); break;
+        case 11: rot_rows<11>(ri, om, rg, acc); break;
+        case 12: rot_rows<12>(ri, om, rg, acc); break;
+        case 13: rot_rows<13>(ri, om, rg, acc); break;
+        case 14: rot_rows<14>(ri, om, rg, acc); break;
+        case 15: rot_rows<15>(ri, om, rg, acc); break;
+        case 16: rot_rows<16>(ri, om, rg, acc); break;
+        default: break;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kFusedRows / kRotGroups; ++r) {
+      if (r < my) {
+        const int row = mrow[rg + kRotGroups * r];
+        const int sid = sid0 + row / G;
+        const int64_t orow = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + row % G;
+        store_any(a.out, a.out_dtype, orow * D + i, acc[r]);
+      }
     }
   }
 }
@@ -1612,7 +1637,9 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
   }
 }
 
-bool decode_fusable(const DecodePlan& p, int G) { return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs; }
+bool decode_fusable(const DecodePlan& p, int G) {
+  return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs && p.max_slots <= kMergeMaxSlots;
+}
 
 void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedArgs& f, cudaStream_t s) {
   LC_REQUIRE(decode_fusable(p, a.hq / a.hkv), LC_ERR_STATE, "decode plan is not fusable");
@@ -1623,7 +1650,7 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
   d.q_rotated = f.q_rotated;
   d.qscale = f.qscale;
   d.qR = f.qR;
-  d.vR = f.vR;
+  d.vRT = f.vRT;
   d.cnt = f.cnt;
   d.ctr = f.ctr;
   d.out = f.out;

@@ -113,7 +113,7 @@ struct FusedArgs {
   int32_t q_dtype = 0, q_rotated = 0;
   float qscale = 1.0f;           // scale * log2(e) / kalpha
   const float* qR = nullptr;     // K codec R (row-major)
-  const float* vR = nullptr;     // V codec R; null leaves the output rotated
+  const float* vRT = nullptr;    // V codec R^T (row-major); null leaves the output rotated
   const int32_t* cnt = nullptr;  // [n_seqs * hkv] partial slots (plan.cnt on the device)
   int32_t* ctr = nullptr;        // [n_seqs * hkv] zero on entry; left zero
   void* out = nullptr;
