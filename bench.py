@@ -535,6 +535,162 @@ def run_longctx(args):
     cache.close()
 
 
+# ----------------------------------------------------------------------------
+# Config 2: mixed precision with rotating windows
+# ----------------------------------------------------------------------------
+def run_window(args):
+    import torch
+
+    rank, local, world = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lc = importlib.import_module("lumen-rs_b200")
+    B, hq, hkv, D = 16, 16, 8, 256
+    win, glob_ctx = 1024, 32768
+    layers = [win] * 5 + [0]  # 5 sliding layers per global layer
+    L = len(layers)
+    kc = lc.TurboQuantCompressor(lc.TurboQuantConfig(3, 64, 42, 1000, D))
+    vc = lc.TurboQuantCompressor(lc.TurboQuantConfig(2, 64, 42, 1000, D))
+    steps, warm = args.steps, args.warmup
+    pages_g = (glob_ctx + steps + warm + 8 + 255) // 256 + 1
+    pages_w = win // 256 + 2
+    cache = lc.CudaKvCache(L, hkv, D, kc, vc, max_seqs=B, max_pages=B * (5 * 2 * pages_w + pages_g) + 64,
+                           max_pages_per_seq=pages_g, device=local, layer_max_size=layers, layer_keep=[0] * L)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5 + rank)
+    ids = list(range(B))
+
+    def kv(n):
+        return (torch.randn((B, hkv, n, D), generator=gen, device=dev)).to(torch.bfloat16)
+
+    t_fill = time.time()
+    for layer, ms in enumerate(layers):
+        if ms:  # sliding: one window-sized chunk, then single-token steps wrapping the ring 3 more times
+            cache.append(layer, ids, kv(win), kv(win))
+            k1f, v1f = kv(1), kv(1)
+            for _ in range(3 * win):
+                cache.append(layer, ids, k1f, v1f)
+        else:
+            for c0 in range(0, glob_ctx, 2048):
+                cache.append(layer, ids, kv(2048), kv(2048))
+    torch.cuda.synchronize()
+    fill_s = time.time() - t_fill
+    qs = (torch.randn((L, B, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    k1 = torch.stack([kv(1) for _ in range(L)])
+    v1 = torch.stack([kv(1) for _ in range(L)])
+    out = torch.empty((L, B, hq, D), device=dev, dtype=torch.bfloat16)
+
+    def step():
+        for layer in range(L):
+            cache.append(layer, ids, k1[layer], v1[layer])
+            cache.decode_attn(layer, ids, qs[layer], hq, 1.0 / D ** 0.5, out=out[layer], out_dtype=lc.LC_BF16)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    views = [cache.ring_state(0, l)["view_len"] for l in range(L)]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(steps):
+            step()
+        ev1.record()
+        ev1.synchronize()
+    ms_step = ev0.elapsed_time(ev1) / steps
+    bpt = 8 * lc.packed_words(D, 3) + 8 * lc.packed_words(D, 2) + 8  # 176 B per (token, kv head)
+    kv_bytes = B * hkv * bpt * sum(views)
+    print(json.dumps({
+        "metric": METRIC, "value": B / (ms_step / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": steps,
+        "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (generic kernel)", "data": "synthetic", "mode": "window",
+        "config": {"workload": f"config2: batch {B}, {hq}q/{hkv}kv, d{D}, 3-bit K / 2-bit V, 5 sliding layers "
+                               f"(ring {win}, wrapped 4x) + 1 global layer ({glob_ctx} tokens); append + decode "
+                               f"per layer", "views": views},
+        "decode_gbs": kv_bytes / (ms_step / 1e3) / 1e9, "bytes_per_token_head": bpt,
+        "clocks": clk.summary(), "fill_s": fill_s,
+    }), flush=True)
+    cache.close()
+
+
+# ----------------------------------------------------------------------------
+# Config 3: prefill quantize-append in 2048-token chunks + prefix reuse
+# ----------------------------------------------------------------------------
+def run_prefill(args):
+    import torch
+
+    rank, local, world = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lc = importlib.import_module("lumen-rs_b200")
+    hkv, D, L = CFG["hkv"], CFG["dim"], 1
+    B, n_new, chunk, prefix, n_req = 16, 16384, 2048, 4096, 64
+    codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
+    pages = (n_new + 255) // 256 + 1
+    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=B + 1 + n_req,
+                           max_pages=(B + 1) * pages + n_req * 2 + 64, max_pages_per_seq=pages, device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77 + rank)
+    sel = torch.Generator(device="cpu")
+    sel.manual_seed(99)
+    scale_vec = torch.ones(hkv, D)
+    for h in range(hkv):
+        scale_vec[h, torch.randperm(D, generator=sel)[:4]] = 8.0
+    scale_vec = scale_vec.to(dev).view(1, hkv, 1, D)
+    ks = [(torch.randn((B, hkv, chunk, D), generator=gen, device=dev) * scale_vec).to(torch.bfloat16)
+          for _ in range(n_new // chunk)]
+    vs = [(torch.randn((B, hkv, chunk, D), generator=gen, device=dev) * scale_vec).to(torch.bfloat16)
+          for _ in range(n_new // chunk)]
+    ids = list(range(B))
+    # warm-up on a throwaway fill, then release
+    for r in range(args.warmup):
+        cache.append(0, ids, ks[r % len(ks)], vs[r % len(vs)])
+    for b in ids:
+        cache.release(b)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for c in range(n_new // chunk):
+            cache.append(0, ids, ks[c], vs[c])
+        ev1.record()
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    vectors = B * n_new * hkv * 2
+    bytes_alg = vectors * (D * 2 + 8 * 8 + 4)  # bf16 in; packed words + sigma out
+    # prefix reuse: one 4096-token prefix shared by 64 requests through the block table
+    src = B
+    cache.append(0, [src], ks[0][:1, :, :prefix // 2].contiguous(), vs[0][:1, :, :prefix // 2].contiguous())
+    cache.append(0, [src], ks[1][:1, :, :prefix // 2].contiguous(), vs[1][:1, :, :prefix // 2].contiguous())
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for r in range(n_req):
+        cache.fork(src, B + 1 + r, prefix)
+    torch.cuda.synchronize()
+    fork_us = (time.perf_counter() - t0) * 1e6 / n_req
+    q = (torch.randn((n_req, CFG["hq"], D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    outp = torch.empty((n_req, CFG["hq"], D), device=dev, dtype=torch.bfloat16)
+    rq = [B + 1 + r for r in range(n_req)]
+    cache.decode_attn(0, rq, q, CFG["hq"], 1.0, out=outp, out_dtype=lc.LC_BF16)
+    ref0 = torch.empty((1, CFG["hq"], D), device=dev, dtype=torch.bfloat16)
+    cache.decode_attn(0, [src], q[:1], CFG["hq"], 1.0, out=ref0, out_dtype=lc.LC_BF16)
+    torch.cuda.synchronize()
+    fork_vs_src = float((outp[:1].float() - ref0.float()).abs().max())
+    print(json.dumps({
+        "metric": METRIC, "value": bytes_alg / (ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": 1,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (strict reference order)", "data": "synthetic", "mode": "prefill",
+        "config": {"workload": f"config3 prefill: {B} sequences x {n_new} new tokens appended in {chunk}-token "
+                               f"chunks, 8 kv heads, d128, 4-bit, bf16 K/V with outlier channels; "
+                               f"{n_req} requests forked from one {prefix}-token prefix (256-token pages)"},
+        "append": {"vectors_per_s": vectors / (ms / 1e3), "bytes_per_vector": D * 2 + 8 * 8 + 4,
+                   "ms_per_chunk": ms / (n_new // chunk)},
+        "prefix": {"fork_us_per_request": fork_us, "pages_shared_per_request": prefix // 256,
+                   "max_abs_fork_vs_source_decode": fork_vs_src},
+        "clocks": clk.summary(),
+    }), flush=True)
+    cache.close()
+
+
 def main():
     faulthandler.enable()
     ap = argparse.ArgumentParser()
@@ -546,8 +702,10 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers (32 = config 1; fewer for profiling)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--mode", default="decode", choices=["decode", "longctx"],
-                    help="decode: config 1 request-sharded; longctx: config 4's 1M-token sequence split by sequence")
+    ap.add_argument("--mode", default="decode", choices=["decode", "longctx", "prefill", "window"],
+                    help="decode: config 1 request-sharded; longctx: config 4's 1M-token sequence split by "
+                         "sequence; prefill: config 3 chunked quantize-append and prefix reuse; window: config 2 "
+                         "mixed precision with rotating windows")
     ap.add_argument("--ctx-tokens", type=int, default=1 << 20, help="longctx: tokens of the split sequence")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
@@ -556,6 +714,10 @@ def main():
         run_reference(args)
     elif args.mode == "longctx":
         run_longctx(args)
+    elif args.mode == "prefill":
+        run_prefill(args)
+    elif args.mode == "window":
+        run_window(args)
     else:
         run_ours(args)
 

@@ -42,12 +42,17 @@ struct AppendDev {
   const void* src[2];
   int32_t dtype, n_seqs, h_in, h_base;
   int64_t n_tok;
-  const uint64_t* dst_page;
+  const uint64_t* dst_page;  // or null: the inline copies below
   const int32_t* dst_row;
   int32_t heads;
   int64_t off[kMaxRoles];
   int64_t row[kMaxRoles];
   int32_t role_words[2], role_sigma[2], role_qjl[2], role_rnorm[2];
+  // small calls (decode steps): destinations in the launch parameters
+  uint64_t ipage[kAppendInline];
+  int32_t irow[kAppendInline];
+  __device__ __forceinline__ uint64_t page_of(int64_t slot) const { return dst_page ? dst_page[slot] : ipage[slot]; }
+  __device__ __forceinline__ int32_t row_of(int64_t slot) const { return dst_page ? dst_row[slot] : irow[slot]; }
 };
 
 __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) {
@@ -69,7 +74,7 @@ __device__ __forceinline__ size_t group_bytes(int D, int qw32) {
 }
 
 template <bool TAB>
-__global__ void k_append_strict(AppendDev a) {
+__global__ void k_append_strict(const __grid_constant__ AppendDev a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int side = blockIdx.y;
   const CodecDev c = a.codec[side];
@@ -222,8 +227,8 @@ __global__ void k_append_strict(AppendDev a) {
       const int hl = (int)(sh % a.h_in);
       const int64_t s = sh / a.h_in;
       const int64_t slot = s * a.n_tok + t;
-      uint8_t* page = reinterpret_cast<uint8_t*>(a.dst_page[slot]);
-      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.dst_row[slot];
+      uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
+      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
       const int rw = a.role_words[side];
       reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
     }
@@ -234,8 +239,8 @@ __global__ void k_append_strict(AppendDev a) {
       const int hl = (int)(sh % a.h_in);
       const int64_t s = sh / a.h_in;
       const int64_t slot = s * a.n_tok + t;
-      uint8_t* page = reinterpret_cast<uint8_t*>(a.dst_page[slot]);
-      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.dst_row[slot];
+      uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
+      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
       const int rsg = a.role_sigma[side];
       *reinterpret_cast<float*>(page + a.off[rsg] + hr * a.row[rsg]) = vscale[v];
       if (stage2) {
@@ -277,7 +282,7 @@ __device__ __forceinline__ void stage16(void* dst, const void* src, int n16) {
 }
 
 template <int R, bool TAB>  // R = head_dim / 32
-__global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(AppendDev a) {
+__global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_constant__ AppendDev a) {
   constexpr int D = 32 * R;
   extern __shared__ __align__(16) uint8_t smem[];
   const int side = blockIdx.y;
@@ -404,8 +409,8 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(AppendDev a) 
   const int hl = (int)(sh % a.h_in);
   const int64_t s = sh / a.h_in;
   const int64_t slot = s * a.n_tok + t;
-  uint8_t* page = reinterpret_cast<uint8_t*>(a.dst_page[slot]);
-  const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.dst_row[slot];
+  uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
+  const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
   const int cpw = 64 / c.bits;
   for (int w = lane; w < c.words; w += 32) {
     uint64_t word = 0;
@@ -462,7 +467,7 @@ size_t append_smem_bytes(int d, int m) {
 void launch_append(const AppendArgs& a, cudaStream_t s) {
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   if (n_vec <= 0) return;
-  AppendDev d;
+  AppendDev d{};
   d.codec[0] = a.codec[0];
   d.codec[1] = a.codec[1];
   d.src[0] = a.src[0];
@@ -474,6 +479,14 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
   d.n_tok = a.n_tok;
   d.dst_page = a.dst_page;
   d.dst_row = a.dst_row;
+  if (!a.dst_page) {
+    const int64_t slots = (int64_t)a.n_seqs * a.n_tok;
+    LC_REQUIRE(a.h_page && a.h_row && slots <= kAppendInline, LC_ERR_STATE, "inline append metadata does not fit");
+    for (int64_t i = 0; i < slots; ++i) {
+      d.ipage[i] = a.h_page[i];
+      d.irow[i] = a.h_row[i];
+    }
+  }
   d.heads = a.layout.heads;
   for (int r = 0; r < kMaxRoles; ++r) {
     d.off[r] = a.layout.off[r];

@@ -193,7 +193,10 @@ void run_append(lc_cache* c, int32_t n_seqs, int32_t h_in, int32_t h_base, int64
   a.h_in = h_in;
   a.h_base = h_base;
   a.n_tok = n_tok;
-  {
+  if ((int64_t)dst_page.size() <= kAppendInline) {  // decode steps: in the launch parameters
+    a.h_page = dst_page.data();
+    a.h_row = dst_row.data();
+  } else {
     // one upload: [page addresses u64 | rows i32]
     const size_t n = dst_page.size();
     std::vector<uint8_t>& blob = c->blob;

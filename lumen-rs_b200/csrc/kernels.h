@@ -43,12 +43,17 @@ struct AppendArgs {
   int32_t dtype = LC_F32;
   int32_t n_seqs = 0, h_in = 0, h_base = 0;
   int64_t n_tok = 0;
-  const uint64_t* dst_page = nullptr;
+  const uint64_t* dst_page = nullptr;  // [n_seqs * n_tok] device, or null: h_page / h_row
   const int32_t* dst_row = nullptr;
+  const uint64_t* h_page = nullptr;    // host copies passed in the launch parameters
+  const int32_t* h_row = nullptr;      // (at most kAppendInline slots)
   PageLayout layout;
   int32_t role_words[2] = {-1, -1}, role_sigma[2] = {-1, -1};
   int32_t role_qjl[2] = {-1, -1}, role_rnorm[2] = {-1, -1};
 };
+// Appends of at most this many (sequence, token) slots pass their destinations
+// in the launch parameters.
+constexpr int kAppendInline = 64;
 void launch_append(const AppendArgs& a, cudaStream_t s);
 // Dynamic shared memory the append kernel needs for head_dim d and qjl m.
 size_t append_smem_bytes(int d, int m);
