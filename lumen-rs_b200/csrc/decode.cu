@@ -209,6 +209,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_two() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 // Walks (sequence, kv head, tile) in flat order; nt = tiles per kv head of b.
@@ -317,7 +318,10 @@ struct PrefetchProducer {
   uint64_t next;  // address of page next_idx of sequence next_b
   int next_b, next_idx;
 
-  __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
+  // Page address of the current tile (and the next page's, ahead). Called
+  // on its own at kernel start so the first table read is in flight while
+  // the prologue does other work.
+  __device__ __forceinline__ void lookup(const DecodeDev& a) {
     const int pidx = w.tile >> 3;
     if (pidx != page_idx || w.b != page_b) {
       const uint64_t* trow = a.table + a.si()[2 * w.b + 1] * a.table_stride;
@@ -329,6 +333,10 @@ struct PrefetchProducer {
       next_idx = pidx + 1 < npages ? pidx + 1 : 0;
       next = __ldg(trow + next_idx);
     }
+  }
+
+  __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
+    lookup(a);
     const int64_t hr = (int64_t)w.kvh * kPageTokens + (w.tile & 7) * kTileTok;
     // chunk c = lane + 32 q: row c >> 2 = lane / 4 + 8 q, part c & 3 = lane & 3;
     // the V swizzle (part ^ (row & 2)) depends on the lane only
@@ -498,13 +506,15 @@ __device__ __forceinline__ uint32_t pair_vlane(int g, int t) {
 constexpr int kFusedSegs = 8;
 constexpr int kFusedRows = 32;
 constexpr int kFusedSmem = kFlatSmem + kFusedRows * 128 * 4;
-constexpr int kMergeMaxSlots = kLutBytes / 4 / kFusedRows;  // slot weights per row in the table area
 
 // Centroid-pair lookup table: lane l < 16 holds K centroid l, lane 16 + l V
 // centroid l (scaled); entry (e, slot) = (c[e & 15], c[e >> 4]), slots 0..31
 // K and 32..63 V.
-__device__ __forceinline__ void build_lut(uint8_t* lut, const DecodeDev& a, int lane) {
-  const float cl = lane < 16 ? a.kcent[lane] * a.kalpha : a.vcent[lane - 16] * a.valpha;
+__device__ __forceinline__ float lut_centroid(const DecodeDev& a, int lane) {
+  return lane < 16 ? a.kcent[lane] * a.kalpha : a.vcent[lane - 16] * a.valpha;
+}
+// cl = lut_centroid(a, lane), read at kernel start (ahead of the tile traffic)
+__device__ __forceinline__ void build_lut(uint8_t* lut, float cl) {
 #pragma unroll
   for (int it = 0; it < 256 * 64 / (kFlatWarps * 32); ++it) {
     const int idx = threadIdx.x + it * kFlatWarps * 32;
@@ -515,32 +525,73 @@ __device__ __forceinline__ void build_lut(uint8_t* lut, const DecodeDev& a, int 
   }
 }
 
-// Fused prologue: row i of the K rotation R (512 B, padded to 528 B so the
-// 16-byte reads of eight consecutive rows hit distinct banks) lives in warp
-// (i / 8)'s second pipeline stage until the warps start their second tiles.
-constexpr int kRRowBytes = 528;
-__device__ __forceinline__ uint8_t* r_row(uint8_t* smem, int n_before, uint32_t lut_off, int i) {
-  const int wi = i >> 3;
-  uint8_t* st = wi < n_before ? smem + wi * kWarpBytes : smem + lut_off + kLutBytes + (wi - n_before) * kWarpBytes;
-  return st + kStageBytes + (i & 7) * kRRowBytes;
+// ---- rotations of the fused path on the tensor cores ----
+// D[i][r] = sum_j M[i][j] x[r][j] for a 128 x 128 f32 matrix M and up to 32
+// rows x: A = M (16-row blocks mi), B = x^T (8-row blocks ni), K = j. Both
+// operands are split into f16 hi + lo parts and D = Mh xh + Mh xl + Ml xh is
+// accumulated in f32 by m16n8k16 products: the dropped Ml xl term is 2^-22
+// of the product. M is scaled by 2^8 before the split (its entries are at
+// most 1 in magnitude) so its low parts stay normal f16 numbers; the
+// caller scales D by 2^-8 (exact).
+// K is permuted inside every 16-wide step so lane t owns physical columns
+// 16 ks + 4t .. 4t + 3: logical k (2t, 2t+1) -> 4t + (0, 1) and (2t+8, 2t+9)
+// -> 4t + (2, 3). Both operands then load as one float4 per lane.
+// Rows x live in shared memory, row r at x + 128 r, column j stored at
+// j ^ 16 (r & 1): the float4 reads of rows g = 2p, 2p + 1 (one quarter-warp)
+// fall in distinct banks.
+constexpr float kRotScale = 256.f, kRotUnscale = 1.f / 256.f;
+
+__device__ __forceinline__ int rot_swz(int r, int j) { return r * 128 + (j ^ ((r & 1) << 4)); }
+
+__device__ __forceinline__ void split_h2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 f = __half22float2(h);
+  hi = h2_as_u32(h);
+  lo = h2_as_u32(__floats2half2_rn(x - f.x, y - f.y));
 }
 
-// acc[r] = sum_j R[i][j] q[rg + 2r][j] for NR rows: four weights per 16-byte
-// read of R's row i, each applied to all NR rows.
-constexpr int kRotGroups = 2;  // thread groups covering R once each
-template <int NR>
-__device__ __forceinline__ void rot_rows(const float* ri, const float* qs, int rg,
-                                         float (&acc)[kFusedRows / kRotGroups]) {
-  constexpr int D = 128;
-#pragma unroll 2
-  for (int j = 0; j < D; j += 4) {
-    const float4 w = *reinterpret_cast<const float4*>(ri + j);
+// M staged in shared memory: row i at i * 512 bytes from the base, its
+// 16-byte chunk c stored at c ^ 4 (i & 1), so the fragment reads of rows
+// g = 2p, 2p + 1 (one quarter-warp) fall in distinct banks. The prologue
+// stages R in the table area (the table is built over it afterwards); the
+// epilogue stages V's R^T in the warps' second pipeline stages (free once
+// the main loop is over), eight rows per warp.
+__device__ __forceinline__ int m_chunk(int i, int c) { return (c ^ ((i & 1) << 2)) << 4; }
+__device__ __forceinline__ uint8_t* m_row(uint8_t* smem, int n_before, uint32_t lut_off, int i) {
+  const int wi = i >> 3;
+  uint8_t* st = wi < n_before ? smem + wi * kWarpBytes : smem + lut_off + kLutBytes + (wi - n_before) * kWarpBytes;
+  return st + kStageBytes + (i & 7) * 512;
+}
+
+// d = D[16 mi + (g, g + 8)][8 ni + (2t, 2t + 1)] * 2^8 for one (mi, ni) block:
+// d[0] (g, 2t), d[1] (g, 2t + 1), d[2] (g + 8, 2t), d[3] (g + 8, 2t + 1).
+// mrow(i) is row i of M in the staged layout.
+template <class MRow>
+__device__ __forceinline__ void rot_block(MRow mrow, int mi, const float* xs, int ni, int g, int t, float (&d)[4]) {
+  float e[4] = {0.f, 0.f, 0.f, 0.f};
+  d[0] = d[1] = d[2] = d[3] = 0.f;
+  const int r = 8 * ni + g, i0 = 16 * mi + g;
+  const uint8_t* m0 = mrow(i0);
+  const uint8_t* m1 = mrow(i0 + 8);
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      const float4 xv = *reinterpret_cast<const float4*>(qs + (rg + kRotGroups * r) * D + j);
-      acc[r] = fmaf(w.w, xv.w, fmaf(w.z, xv.z, fmaf(w.y, xv.y, fmaf(w.x, xv.x, acc[r]))));
-    }
+  for (int ks = 0; ks < 8; ++ks) {
+    const float4 xv = *reinterpret_cast<const float4*>(xs + rot_swz(r, 16 * ks + 4 * t));
+    const float4 f0 = *reinterpret_cast<const float4*>(m0 + m_chunk(i0, 4 * ks + t));
+    const float4 f1 = *reinterpret_cast<const float4*>(m1 + m_chunk(i0 + 8, 4 * ks + t));
+    uint32_t bh0, bl0, bh1, bl1;
+    split_h2(xv.x, xv.y, bh0, bl0);
+    split_h2(xv.z, xv.w, bh1, bl1);
+    uint32_t ah[4], al[4];
+    split_h2(f0.x * kRotScale, f0.y * kRotScale, ah[0], al[0]);
+    split_h2(f1.x * kRotScale, f1.y * kRotScale, ah[1], al[1]);
+    split_h2(f0.z * kRotScale, f0.w * kRotScale, ah[2], al[2]);
+    split_h2(f1.z * kRotScale, f1.w * kRotScale, ah[3], al[3]);
+    mma16816(d, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+    mma16816(e, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+    mma16816(e, al[0], al[1], al[2], al[3], bh0, bh1);
   }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) d[c] += e[c];
 }
 
 // P^T B fragments of both 16-token halves through shared memory, in the
@@ -603,27 +654,35 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   pr.next = 0;
   pr.next_b = -1;
   pr.next_idx = -1;
-  if (begin < end) pr.w = locate_warp(a, begin, lane);
-  Walk cw = pr.w;
-  // first tile now; the fused prologue borrows every warp's second stage
-  // for R^T, so there the second tile is issued after the rotation
-  if (begin < end) {
-    pr.issue(a, st0, lane);
-    step(a, pr.w);
-  }
-  cp_commit();
-  if (!FUSED) {
-    if (begin + 1 < end) {
-      pr.issue(a, st0 + kStageBytes, lane);
-      step(a, pr.w);
+  float* qs = reinterpret_cast<float*>(smem + kFlatSmem);  // [kFusedRows][D]
+  __shared__ int merged[kFusedSegs];
+  // first (sequence, kv head) segment of this CTA and its query-row count,
+  // kept in shared memory (read once per segment; no register in the loop)
+  __shared__ int cta_seg[2];
+  const bool rot_q = FUSED && !a.q_rotated;
+  const float cl = lut_centroid(a, lane);
+  // fused: the K rotation R into the table area before any tile traffic
+  // (an L2 hit shared by all CTAs; the table is built over it afterwards)
+  if constexpr (FUSED) {
+    if (rot_q) {
+#pragma unroll
+      for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
+        const int k = threadIdx.x + it * kFlatWarps * 32;  // row k / 32, chunk k % 32
+        cp_async16(s0 + lut_off + (k >> 5) * 512 + m_chunk(k >> 5, k & 31), a.qR + 4 * k);
+      }
     }
     cp_commit();
   }
+  if (begin < end) {
+    pr.w = locate_warp(a, begin, lane);
+    pr.lookup(a);
+  }
+  Walk cw = pr.w;
 
-  // ---- fused: q' = R q * qscale for this CTA's segments, into qs, with
-  // R^T staged in the warps' second stages while the table is built ----
-  float* qs = reinterpret_cast<float*>(smem + kFlatSmem);  // [kFusedRows][D]
-  __shared__ int merged[kFusedSegs];
+  // fused: this CTA's segments and their query rows, loaded before the
+  // tiles are issued so they do not queue behind the tile traffic
+  constexpr int QIT = kFusedRows * D / (kFlatWarps * 32);
+  float qv[QIT];
   int sid0 = 0, nrows = 0;
   if constexpr (FUSED) {
     const int cb = blockIdx.x * kFlatWarps * pw;
@@ -633,74 +692,69 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       sid0 = f.b * a.hkv + f.kvh;
       nrows = (e.b * a.hkv + e.kvh - sid0 + 1) * G;
     }
-    if (threadIdx.x < kFusedSegs) merged[threadIdx.x] = 0;
-    if (!a.q_rotated) {
 #pragma unroll
-      for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
-        const int k = threadIdx.x + it * kFlatWarps * 32;  // row k / 32, chunk k % 32
-        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(r_row(smem, n_before, lut_off, k >> 5)) + (k & 31) * 16;
-        cp_async16(dst, a.qR + 4 * k);
-      }
-    }
-    cp_commit();
-#pragma unroll
-    for (int it = 0; it < kFusedRows * D / (kFlatWarps * 32); ++it) {
+    for (int it = 0; it < QIT; ++it) {
       const int k = threadIdx.x + it * kFlatWarps * 32;
-      if (k < nrows * D) {
-        const int r = k >> 7, j = k & 127;
+      const int r = k >> 7, j = k & 127;
+      qv[it] = 0.f;
+      if (r < nrows) {
         const int sid = sid0 + r / G;
         const int64_t row = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G;
-        qs[k] = load_any(a.q_in, a.q_dtype, row * D + j);
+        qv[it] = load_any(a.q_in, a.q_dtype, row * D + j);
       }
     }
-    build_lut(lut, a, lane);  // while R^T is in flight
-    cp_wait_all();
-    __syncthreads();
-    // threads 0..255: output dim i of rows rg, rg + 2, ... (two groups, so R is
-    // read twice from shared memory); the other warps wait at the barrier
-    const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
-    constexpr int RPT = kFusedRows / kRotGroups;
-    const int my_rows = (rg < kRotGroups && nrows > rg) ? (nrows - rg + kRotGroups - 1) / kRotGroups : 0;
-    float acc[RPT];
-#pragma unroll
-    for (int r = 0; r < RPT; ++r) acc[r] = (a.q_rotated && r < my_rows) ? qs[(rg + kRotGroups * r) * D + i] : 0.f;
-    if (!a.q_rotated && my_rows > 0) {
-      const float* ri = reinterpret_cast<const float*>(r_row(smem, n_before, lut_off, i));
-      switch (my_rows) {  // exact row counts: no predicated-off work
-        case 1: rot_rows<1>(ri, qs, rg, acc); break;
-        case 2: rot_rows<2>(ri, qs, rg, acc); break;
-        case 3: rot_rows<3>(ri, qs, rg, acc); break;
-        case 4: rot_rows<4>(ri, qs, rg, acc); break;
-        case 5: rot_rows<5>(ri, qs, rg, acc); break;
-        case 6: rot_rows<6>(ri, qs, rg, acc); break;
-        case 7: rot_rows<7>(ri, qs, rg, acc); break;
-        case 8: rot_rows<8>(ri, qs, rg, acc); break;
-        case 9: rot_rows<9>(ri, qs, rg, acc); break;
-        case 10: rot_rows<10>(ri, qs, rg, acc); break;
-        case 11: rot_rows<11>(ri, qs, rg, acc); break;
-        case 12: rot_rows<12>(ri, qs, rg, acc); break;
-        case 13: rot_rows<13>(ri, qs, rg, acc); break;
-        case 14: rot_rows<14>(ri, qs, rg, acc); break;
-        case 15: rot_rows<15>(ri, qs, rg, acc); break;
-        case 16: rot_rows<16>(ri, qs, rg, acc); break;
-        default: break;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < RPT; ++r)
-      if (r < my_rows) qs[(rg + kRotGroups * r) * D + i] = acc[r] * a.qscale;
   }
-  if (!FUSED) build_lut(lut, a, lane);
-  __syncthreads();
-  if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
-  if (FUSED) {  // second tile, into the stage R^T no longer needs
-    if (begin + 1 < end) {
-      pr.issue(a, st0 + kStageBytes, lane);
+
+  // the first two tiles, both stages
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    if (begin + k < end) {
+      pr.issue(a, st0 + k * kStageBytes, lane);
       step(a, pr.w);
     }
     cp_commit();
   }
+
+  // ---- fused: q' = R (q * qscale) into qs on the tensor cores; warp w
+  // computes output dims 16 (w & 7) .. + 15 of row blocks (w >> 3) and
+  // (w >> 3) + 2 ----
+  if constexpr (FUSED) {
+    const int nb = (nrows + 7) >> 3, mi = warp & 7, n0 = warp >> 3;
+    if (threadIdx.x < kFusedSegs) merged[threadIdx.x] = 0;
+    if (threadIdx.x == 0) {
+      cta_seg[0] = sid0;
+      cta_seg[1] = nrows;
+    }
+#pragma unroll
+    for (int it = 0; it < QIT; ++it) {
+      const int k = threadIdx.x + it * kFlatWarps * 32;
+      const int r = k >> 7, j = k & 127;
+      if (r < nb * 8) qs[rot_q ? rot_swz(r, j) : k] = qv[it] * a.qscale;
+    }
+    if (rot_q) {
+      cp_wait_two();  // R has landed; the two tiles may still be in flight
+      __syncthreads();
+      auto rrow = [&](int i) { return static_cast<const uint8_t*>(lut + i * 512); };
+      float d[2][4];
+      if (n0 < nb) rot_block(rrow, mi, qs, n0, g, t, d[0]);
+      if (n0 + 2 < nb) rot_block(rrow, mi, qs, n0 + 2, g, t, d[1]);
+      __syncthreads();  // every warp has read R and q
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int ni = n0 + 2 * u;
+        if (ni < nb) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int r = 8 * ni + 2 * t + (c & 1), i = 16 * mi + g + 8 * (c >> 1);
+            if (r < nrows) qs[r * D + i] = d[u][c] * kRotUnscale;
+          }
+        }
+      }
+    }
+  }
+  build_lut(lut, cl);
+  __syncthreads();
+  if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
 
   int x = begin;
   while (x < end) {
@@ -715,7 +769,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       const int head = g >> 1;
       const bool lo = g & 1;
       const int hsel = head < G ? head : 0;
-      const float* qrow = FUSED ? qs + ((b * a.hkv + kvh - sid0) * G + hsel) * D + 32 * t
+      const float* qrow = FUSED ? qs + ((b * a.hkv + kvh - cta_seg[0]) * G + hsel) * D + 32 * t
                                 : a.q_rot + ((int64_t)b * a.hq + (int64_t)kvh * G + hsel) * D + 32 * t;
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
@@ -835,7 +889,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       old = __shfl_sync(0xffffffffu, old, 0);
       if (old == a.ct()[sid] - 1 && lane == 0) {
         a.ctr[sid] = 0;  // zero again for the next launch
-        merged[sid - sid0] = 1;
+        merged[sid - cta_seg[0]] = 1;
       }
     }
   }
@@ -848,133 +902,117 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     __shared__ int n_mrows;
     if (threadIdx.x == 0) {
       int k = 0;
-      for (int r = 0; r < nrows; ++r)
+      for (int r = 0; r < cta_seg[1]; ++r)
         if (merged[r / G]) mrow[k++] = r;
       n_mrows = k;
     }
     __syncthreads();
-    const int nm = n_mrows;
+    const int nm = n_mrows, sid0 = cta_seg[0];
     if (nm == 0) return;  // uniform over the CTA
     __threadfence();      // the other warps' partials, read below from L2
     // V's R^T rows into the second pipeline stages, free now
     if (a.vRT) {
 #pragma unroll
       for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
-        const int k = threadIdx.x + it * kFlatWarps * 32;
-        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(r_row(smem, n_before, lut_off, k >> 5)) + (k & 31) * 16;
-        cp_async16(dst, a.vRT + 4 * k);
+        const int k = threadIdx.x + it * kFlatWarps * 32;  // row k / 32, chunk k % 32
+        const int i = k >> 5;
+        cp_async16((uint32_t)__cvta_generic_to_shared(m_row(smem, n_before, lut_off, i)) + m_chunk(i, k & 31), a.vRT + 4 * k);
       }
     }
     cp_commit();
-    // slot weights 2^(m_c - M) per merged row into the table area, warp per row
-    float* wt = reinterpret_cast<float*>(lut);  // [kFusedRows][kMergeMaxSlots]
-    __shared__ float linv[kFusedRows];
+    // merge, warp per compacted row k: lane c holds (m, l) of slot c of a
+    // group of 32; the o rows of the group's first kMergeAhead slots are
+    // loaded with them (lane: dims 2 lane, 2 lane + 1, 64 + 2 lane, + 1), so
+    // a row of up to kMergeAhead slots costs one round trip to L2. Groups
+    // fold into (M, L, acc) with an online rescale.
+    constexpr int kMergeAhead = 16;
+    float* om = qs;  // [nm][D] over the q' rows (no longer read), rot_swz layout
     for (int k = warp; k < nm; k += kFlatWarps) {
       const int r = mrow[k];
       const int sid = sid0 + r / G;
       const int n = a.ct()[sid];
-      const float* pr_ = a.part + ((int64_t)sid * a.max_slots * G + r % G) * PS;
+      const float* prow = a.part + ((int64_t)sid * a.max_slots * G + r % G) * PS;
       const int64_t cs = (int64_t)G * PS;
-      float mc = lane < n ? __ldcg(pr_ + lane * cs) : -INFINITY;
-      float lc = lane < n ? __ldcg(pr_ + lane * cs + 1) : 0.f;
-      float M = mc;
-      for (int c = lane + 32; c < n; c += 32) M = fmaxf(M, __ldcg(pr_ + c * cs));
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-      float L = 0.f;
-      for (int c = lane; c < n; c += 32) {
-        if (c >= 32) {
-          mc = __ldcg(pr_ + c * cs);
-          lc = __ldcg(pr_ + c * cs + 1);
-        }
-        const float wv = mc == -INFINITY ? 0.f : exp2f(mc - M);
-        L += wv * lc;
-        wt[k * kMergeMaxSlots + c] = wv;
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      if (lane == 0) linv[k] = L > 0.f ? a.oscale / L : 0.f;
-    }
-    __syncthreads();
-    // o[k][i] = sum_c w_c o_c[k][i] / L for the compacted rows k, into qs:
-    // thread items u = tid + 512 j (j < 4), 8 slots of every item in flight
-    constexpr int NT = kFlatWarps * 32;
-    float* om = qs;  // [nm][D] over the q' rows, no longer read
-    for (int u0 = 0; u0 < nm * D; u0 += 4 * NT) {
+      float M = -INFINITY, L = 0.f;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const float* po[4];
-      const float* wr[4];
-      int n[4];
-      int64_t cs[4];
+      for (int c0 = 0; c0 < n; c0 += 32) {
+        const int c = c0 + lane;
+        const float mc = c < n ? __ldcg(prow + c * cs) : -INFINITY;
+        const float lc = c < n ? __ldcg(prow + c * cs + 1) : 0.f;
+        float2 ov[kMergeAhead][2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int u = u0 + threadIdx.x + j * NT;
-        const int k = u < nm * D ? (u >> 7) : 0;
-        const int r = mrow[k], i = u & (D - 1);
-        const int sid = sid0 + r / G;
-        n[j] = u < nm * D ? a.ct()[sid] : 0;
-        po[j] = a.part + ((int64_t)sid * a.max_slots * G + r % G) * PS + 2 + i;
-        cs[j] = (int64_t)G * PS;
-        wr[j] = wt + k * kMergeMaxSlots;
+        for (int j = 0; j < kMergeAhead; ++j) {
+          const bool live = c0 + j < n;
+          const float* po = prow + (c0 + j) * cs + 2 + 2 * lane;
+          ov[j][0] = live ? __ldcg(reinterpret_cast<const float2*>(po)) : make_float2(0.f, 0.f);
+          ov[j][1] = live ? __ldcg(reinterpret_cast<const float2*>(po + 64)) : make_float2(0.f, 0.f);
+        }
+        float Mg = mc;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Mg = fmaxf(Mg, __shfl_xor_sync(0xffffffffu, Mg, off));
+        const float Mn = fmaxf(M, Mg);
+        const float keep = M == -INFINITY ? 0.f : ex2(M - Mn);  // rescale of what was folded so far
+        const float wc = mc == -INFINITY ? 0.f : ex2(mc - Mn);
+        float Lg = wc * lc;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Lg += __shfl_xor_sync(0xffffffffu, Lg, off);
+        L = L * keep + Lg;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] *= keep;
+#pragma unroll
+        for (int j = 0; j < kMergeAhead; ++j) {
+          const float wj = __shfl_sync(0xffffffffu, wc, j);
+          acc[0] = fmaf(wj, ov[j][0].x, acc[0]);
+          acc[1] = fmaf(wj, ov[j][0].y, acc[1]);
+          acc[2] = fmaf(wj, ov[j][1].x, acc[2]);
+          acc[3] = fmaf(wj, ov[j][1].y, acc[3]);
+        }
+        for (int j = kMergeAhead; j < 32 && c0 + j < n; ++j) {  // slots past the loaded ones
+          const float wj = __shfl_sync(0xffffffffu, wc, j);
+          const float* po = prow + (c0 + j) * cs + 2 + 2 * lane;
+          const float2 o0 = __ldcg(reinterpret_cast<const float2*>(po));
+          const float2 o1 = __ldcg(reinterpret_cast<const float2*>(po + 64));
+          acc[0] = fmaf(wj, o0.x, acc[0]);
+          acc[1] = fmaf(wj, o0.y, acc[1]);
+          acc[2] = fmaf(wj, o1.x, acc[2]);
+          acc[3] = fmaf(wj, o1.y, acc[3]);
+        }
+        M = Mn;
       }
-      const int nmax = max(max(n[0], n[1]), max(n[2], n[3]));
-      for (int c0 = 0; c0 < nmax; c0 += 8) {
-        float v[4][8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int c = 0; c < 8; ++c) v[j][c] = c0 + c < n[j] ? __ldcg(po[j] + (c0 + c) * cs[j]) : 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (c0 + c < n[j]) acc[j] = fmaf(wr[j][c0 + c], v[j][c], acc[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int u = u0 + threadIdx.x + j * NT;
-        if (u < nm * D) om[u] = acc[j] * linv[u >> 7];
-      }
+      const float li = L > 0.f ? a.oscale / L : 0.f;
+      *reinterpret_cast<float2*>(om + rot_swz(k, 2 * lane)) = make_float2(acc[0] * li, acc[1] * li);
+      *reinterpret_cast<float2*>(om + rot_swz(k, 64 + 2 * lane)) = make_float2(acc[2] * li, acc[3] * li);
     }
     cp_wait_all();
     __syncthreads();
-    // out = R^T o: thread (i, rg) over compacted rows rg, rg + 2, ... (two
-    // groups), R^T rows read as 16 bytes from the second stages
-    const int i = threadIdx.x & 127, rg = threadIdx.x >> 7;
-    const int my = (rg < kRotGroups && nm > rg) ? (nm - rg + kRotGroups - 1) / kRotGroups : 0;
-    float acc[kFusedRows / kRotGroups];
+    // out = R^T o on the tensor cores: warp w computes output dims 16 (w & 7)
+    // .. + 15 of compacted row blocks (w >> 3) and (w >> 3) + 2
+    auto out_at = [&](int k, int i, float v) {
+      const int row = mrow[k];
+      const int sid = sid0 + row / G;
+      const int64_t orow = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + row % G;
+      store_any(a.out, a.out_dtype, orow * D + i, v);
+    };
+    if (a.vRT) {
+      const int nb = (nm + 7) >> 3, mi = warp & 7, n0 = warp >> 3;
+      if (n0 < nb) {
+        auto vrow = [&](int i) { return static_cast<const uint8_t*>(m_row(smem, n_before, lut_off, i)); };
 #pragma unroll
-    for (int r = 0; r < kFusedRows / kRotGroups; ++r) acc[r] = (!a.vRT && r < my) ? om[(rg + kRotGroups * r) * D + i] : 0.f;
-    if (a.vRT && my > 0) {
-      const float* ri = reinterpret_cast<const float*>(r_row(smem, n_before, lut_off, i));
-      switch (my) {
-        case 1: rot_rows<1>(ri, om, rg, acc); break;
-        case 2: rot_rows<2>(ri, om, rg, acc); break;
-        case 3: rot_rows<3>(ri, om, rg, acc); break;
-        case 4: rot_rows<4>(ri, om, rg, acc); break;
-        case 5: rot_rows<5>(ri, om, rg, acc); break;
-        case 6: rot_rows<6>(ri, om, rg, acc); break;
-        case 7: rot_rows<7>(ri, om, rg, acc); break;
-        case 8: rot_rows<8>(ri, om, rg, acc); break;
-        case 9: rot_rows<9>(ri, om, rg, acc); break;
-        case 10: rot_rows<10>(ri, om, rg, acc); break;
-        case 11: rot_rows<11>(ri, om, rg, acc); break;
-        case 12: rot_rows<12>(ri, om, rg, acc); break;
-        case 13: rot_rows<13>(ri, om, rg, acc); break;
-        case 14: rot_rows<14>(ri, om, rg, acc); break;
-        case 15: rot_rows<15>(ri, om, rg, acc); break;
-        case 16: rot_rows<16>(ri, om, rg, acc); break;
-        default: break;
-      }
-    }
+        for (int u = 0; u < 2; ++u) {
+          const int ni = n0 + 2 * u;
+          if (ni < nb) {
+            float d[4];
+            rot_block(vrow, mi, om, ni, g, t, d);
 #pragma unroll
-    for (int r = 0; r < kFusedRows / kRotGroups; ++r) {
-      if (r < my) {
-        const int row = mrow[rg + kRotGroups * r];
-        const int sid = sid0 + row / G;
-        const int64_t orow = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + row % G;
-        store_any(a.out, a.out_dtype, orow * D + i, acc[r]);
+            for (int c = 0; c < 4; ++c) {
+              const int k = 8 * ni + 2 * t + (c & 1), i = 16 * mi + g + 8 * (c >> 1);
+              if (k < nm) out_at(k, i, d[c] * kRotUnscale);
+            }
+          }
+        }
       }
+    } else {
+      for (int u = threadIdx.x; u < nm * D; u += kFlatWarps * 32) out_at(u >> 7, u & (D - 1), om[rot_swz(u >> 7, u & (D - 1))]);
     }
   }
 }
@@ -1638,7 +1676,7 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
 }
 
 bool decode_fusable(const DecodePlan& p, int G) {
-  return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs && p.max_slots <= kMergeMaxSlots;
+  return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs;
 }
 
 void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedArgs& f, cudaStream_t s) {

@@ -97,6 +97,21 @@ def test_decode_other_geometries(lc, orc, gpu, dim, kb, vb, hkv, hq):
     _assert_close(got, _oracle(refs, q, hkv, scale))
 
 
+@pytest.mark.parametrize("hq", [32, 16, 8])
+def test_decode_many_short_sequences(lc, orc, gpu, hq):
+    """40 sequences of 33..64 tokens (two 32-token tiles per kv head): every
+    CTA of the one-launch kernel covers 8 (sequence, kv head) segments, so
+    its query rotation and output un-rotation handle 8 * G rows (32 at G=4:
+    four 8-row blocks)."""
+    rng = np.random.default_rng(5)
+    lens = [int(x) for x in rng.integers(33, 65, size=40)]
+    cache, refs, tk, tv = _setup(lc, orc, 128, 4, 4, 8, lens, 900)
+    q = helpers.queries(orc, 13, len(lens), hq, 128)
+    scale = 1.0 / np.sqrt(128)
+    got = cache.decode_attn(0, list(range(len(lens))), q, hq, scale)
+    _assert_close(got, _oracle(refs, q, 8, scale))
+
+
 def test_decode_dtypes_and_flags(lc, orc, gpu):
     import torch
 
