@@ -147,6 +147,15 @@ int lc_attend_keys(lc_cache* cache, int32_t seq, int32_t layer, int32_t head, co
 int lc_attend_values(lc_cache* cache, int32_t seq, int32_t layer, int32_t head, const float* weights,
                      int64_t n_weights, float* out);
 
+/* TurboQuantCompressor::estimate_inner_products (compressor.rs:122-159):
+ * the two-stage scores of `query` [head_dim] f32 against every cached key
+ * of (seq, layer, head): stage 1 (as lc_attend_keys) plus the QJL
+ * correction ||r|| * sqrt(pi/2) / sqrt(m) * sum_i sign_i (Phi query)_i
+ * (qjl.rs:76-119; 0 when ||r|| < 1e-10), in the reference's f32 order.
+ * Needs a cache created with LC_STORE_K_QJL (LC_ERR_STATE otherwise). */
+int lc_attend_keys_qjl(lc_cache* cache, int32_t seq, int32_t layer, int32_t head, const float* query,
+                       float* scores, int64_t n_scores);
+
 /* KVCache::seq_len (traits.rs:27). Negative on error. */
 int64_t lc_seq_len(const lc_cache* cache, int32_t seq, int32_t layer, int32_t head);
 
@@ -211,6 +220,13 @@ int lc_fetch(lc_cache* cache, int32_t seq, int32_t layer, int32_t which, lc_fetc
 /* Decode flags. */
 #define LC_Q_ROTATED 1u   /* q is already R q (Gemma path); skip the rotation */
 #define LC_OUT_ROTATED 2u /* leave the output in the rotated basis (R baked into Wo) */
+/* Score every key with the two-stage estimate of estimate_inner_products
+ * (compressor.rs:122-159): stage 1 plus the QJL stage-2 correction of the
+ * stored K sign bits and residual norm. Needs a cache created with
+ * LC_STORE_K_QJL (LC_ERR_STATE otherwise), qjl_m <= 256 and the un-rotated
+ * query (with LC_Q_ROTATED: LC_ERR_INVALID). Not taken by
+ * lc_decode_attn_noalloc (LC_ERR_INVALID). */
+#define LC_QJL_SCORES 4u
 
 /* Decode attention over the compressed cache, one query token per
  * sequence: out = softmax(scale * q K_dq^T) V_dq for every query head, with

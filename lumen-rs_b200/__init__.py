@@ -37,7 +37,7 @@ LC_ERR_TIMEOUT, LC_ERR_NOMEM, LC_ERR_IO, LC_ERR_MAGIC, LC_ERR_STATE = -5, -6, -7
 LC_F32, LC_BF16, LC_F16 = 0, 1, 2
 LC_STORE_K_QJL, LC_STORE_V_QJL = 1, 2
 LC_FETCH_VIEW, LC_FETCH_BACKING = 0, 1
-LC_Q_ROTATED, LC_OUT_ROTATED = 1, 2
+LC_Q_ROTATED, LC_OUT_ROTATED, LC_QJL_SCORES = 1, 2, 4
 # cudaStreamLegacy: the legacy default stream (torch's default stream, handle 0).
 # A NULL stream in the C ABI means the library's own stream instead.
 CUDA_STREAM_LEGACY = 0x1
@@ -46,7 +46,7 @@ CUDA_STREAM_LEGACY = 0x1
 ABI_SYMBOLS = [
     "lc_last_error", "lc_codec_new", "lc_codec_from_files", "lc_codec_from_tables", "lc_codec_save",
     "lc_codec_tables", "lc_codec_shape", "lc_codec_free", "lc_packed_words", "lc_cache_create",
-    "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_values", "lc_seq_len", "lc_clear",
+    "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_keys_qjl", "lc_attend_values", "lc_seq_len", "lc_clear",
     "lc_truncate", "lc_append", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
     "lc_decode_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_ring_create",
@@ -108,6 +108,7 @@ def lib():
                                       C.POINTER(u64), C.POINTER(C.c_double)]),
         "lc_store": (C.c_int, [vp, i32, i32, i32, vp, vp, i64]),
         "lc_attend_keys": (C.c_int, [vp, i32, i32, i32, vp, vp, i64]),
+        "lc_attend_keys_qjl": (C.c_int, [vp, i32, i32, i32, vp, vp, i64]),
         "lc_attend_values": (C.c_int, [vp, i32, i32, i32, vp, i64, vp]),
         "lc_seq_len": (i64, [vp, i32, i32, i32]),
         "lc_clear": (C.c_int, [vp]),
@@ -428,6 +429,14 @@ class CudaKvCache:
         _check(lib().lc_attend_keys(self._h, seq, layer, head, _ptr(q), _ptr(out), len(out)))
         return out[:n]
 
+    def attend_keys_qjl(self, seq, layer, head, query) -> np.ndarray:
+        """Two-stage scores: estimate_inner_products (compressor.rs:122-159)."""
+        n = self.seq_len(seq, layer, head)
+        out = np.empty(max(n, 1), np.float32)
+        q = np.ascontiguousarray(query, np.float32)
+        _check(lib().lc_attend_keys_qjl(self._h, seq, layer, head, _ptr(q), _ptr(out), len(out)))
+        return out[:n]
+
     def attend_values(self, seq, layer, head, weights) -> np.ndarray:
         w = np.ascontiguousarray(weights, np.float32)
         out = np.empty(self.head_dim, np.float32)
@@ -470,6 +479,10 @@ class SimpleCache(KVCache):
 
     def attend_keys(self, layer, head, query):
         return self._c.attend_keys(0, layer, head, query)
+
+    def estimate_inner_products(self, layer, head, query):
+        """Two-stage scores of the cached keys (compressor.rs:122-159)."""
+        return self._c.attend_keys_qjl(0, layer, head, query)
 
     def attend_values(self, layer, head, weights):
         return self._c.attend_values(0, layer, head, weights)

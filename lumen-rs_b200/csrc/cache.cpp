@@ -80,7 +80,7 @@ struct lc_cache {
   uint64_t* d_table = nullptr;  // [n_layers][max_seqs][max_pages_per_seq]
   cudaEvent_t ev_copy = nullptr;
   DevBuf<uint8_t> in_k, in_v, qbuf, outbuf, fetchbuf;
-  DevBuf<float> q_rot, part, hook_a, hook_b, hook_c;
+  DevBuf<float> q_rot, part, hook_a, hook_b, hook_c, q_proj;
   DevBuf<__half> q_h;
   DevBuf<int32_t> ctr;  // fused decode arrival counters (zero between launches)
   std::vector<uint8_t> blob;  // host staging of one call's metadata
@@ -483,6 +483,34 @@ int lc_attend_keys(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const 
   });
 }
 
+int lc_attend_keys_qjl(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float* query, float* scores,
+                       int64_t n_scores) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && query && scores, LC_ERR_INVALID, "null argument");
+    c->check(seq, layer);
+    LC_REQUIRE(head >= 0 && head < c->cfg.n_kv_heads, LC_ERR_INVALID, "head out of range");
+    LC_REQUIRE(c->cfg.store_flags & LC_STORE_K_QJL, LC_ERR_STATE, "cache does not keep the K QJL bits");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    c->order(s);
+    const SeqLayer& sl = c->at(seq, layer);
+    const int64_t n = sl.head_len.empty() ? sl.ring.view_len : sl.head_len[head];
+    LC_REQUIRE(n_scores >= n, LC_ERR_INVALID, "scores buffer too small");
+    const int D = c->cfg.head_dim;
+    c->hook_a.ensure(D, s);
+    c->hook_b.ensure((size_t)D + c->kc.m, s);
+    c->hook_c.ensure(std::max<int64_t>(n, 1), s);
+    bool hq = false;
+    const float* dq = static_cast<const float*>(c->stage_in(query, D * 4, c->qbuf, s, hq));
+    const uint64_t* pages = c->arena.put_vec(c->ops.page_addrs(sl.ring), s);
+    launch_attend_keys_qjl(dq, c->dk.view(), pages, c->layout, R_KW, R_KS, R_KQ, R_KR, head, n, c->hook_b.p,
+                           c->hook_b.p + D, c->hook_c.p, s);
+    c->launches += 3;
+    LC_CUDA(cudaMemcpyAsync(scores, c->hook_c.p, n * 4, cudaMemcpyDefault, s));
+    LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
 int lc_attend_values(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float* weights, int64_t n_weights,
                      float* out) {
   return abi_guard([&] {
@@ -697,7 +725,14 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     info[2 * b + 1] = (int64_t)layer * c->cfg.max_seqs + seq;
     lens[b] = n;
   }
-  const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits);
+  const bool qjl = (flags & LC_QJL_SCORES) != 0;
+  if (qjl) {
+    LC_REQUIRE(c->cfg.store_flags & LC_STORE_K_QJL, LC_ERR_STATE, "QJL scores: cache does not keep the K QJL bits");
+    LC_REQUIRE(!(flags & LC_Q_ROTATED), LC_ERR_INVALID, "QJL scores need the un-rotated query");
+    LC_REQUIRE(c->kc.m > 0 && c->kc.m <= (uint64_t)kMaxQjlDecode, LC_ERR_INVALID,
+               "QJL scores: qjl_m must be in [1, 256]");
+  }
+  const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits, qjl);
   const bool fused = fused_out && decode_fusable(plan, n_q_heads / hkv);
   // The one-launch path of small calls passes its arrays in the launch
   // parameters; otherwise one upload: [seqinfo i64 | seg i64 | cnt i32].
@@ -730,6 +765,13 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     });
     ++c->launches;
   }
+  if (qjl) {
+    c->q_proj.ensure((size_t)rows * c->kc.m, s);
+    c->timed(c->t_other, s, [&] {
+      launch_project_q(dq, q_dtype, (int32_t)rows, D, (int32_t)c->kc.m, c->dk.PTd, qscale, c->q_proj.p, s);
+    });
+    ++c->launches;
+  }
   c->part.ensure((size_t)rows * plan.max_slots * (D + 2), s);
   DecodeArgs a;
   a.table = c->d_table;
@@ -759,6 +801,13 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   a.kalpha = kalpha;
   a.valpha = valpha;
   a.part = c->part.p;
+  if (qjl) {
+    a.q_proj = c->q_proj.p;
+    a.role_kq = R_KQ;
+    a.role_kr = R_KR;
+    a.qjl_m = (int32_t)c->kc.m;
+    a.qjl_c = std::sqrt((float)1.5707963267948966) / std::sqrt((float)c->kc.m);
+  }
   if (fused) {
     const size_t nctr = (size_t)n_seqs * hkv, before = c->ctr.n;
     c->ctr.ensure(nctr, s);
@@ -921,6 +970,7 @@ int lc_decode_attn_noalloc(lc_cache* c, int32_t layer, int32_t n_seqs, const int
     LC_CUDA(cudaSetDevice(c->cfg.device));
     LC_REQUIRE(is_device_ptr(q) && is_device_ptr(out), LC_ERR_INVALID,
                "lc_decode_attn_noalloc needs q and out in device memory");
+    LC_REQUIRE(!(flags & LC_QJL_SCORES), LC_ERR_INVALID, "lc_decode_attn_noalloc does not take LC_QJL_SCORES");
     std::lock_guard<std::mutex> lock(noalloc_mutex());
     uint8_t* const dscr = noalloc_device_scratch(c->cfg.device);
     uint8_t* const hst = noalloc_host_staging();

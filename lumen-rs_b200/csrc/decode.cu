@@ -116,6 +116,21 @@ __global__ void __launch_bounds__(512) k_rotate_q(const void* q, int dtype, int 
   }
 }
 
+// QJL projection of the query rows for stage-2 scores: one CTA per row,
+// thread i computes q_proj[row][i] = qscale * sum_j PT[j][i] q[row][j].
+__global__ void k_project_q(const void* q, int dtype, int dim, int m, const float* PT, float qscale,
+                            float* q_proj) {
+  extern __shared__ float sq[];
+  const int64_t row = blockIdx.x;
+  for (int j = threadIdx.x; j < dim; j += blockDim.x) sq[j] = load_any(q, dtype, row * dim + j);
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < dim; ++j) acc = fmaf(PT[(int64_t)j * m + i], sq[j], acc);
+    q_proj[row * m + i] = acc * qscale;
+  }
+}
+
 // Per-call arrays of small calls travel in the launch parameters
 // (__grid_constant__): no host-to-device copy between kernels.
 struct InlineMeta {
@@ -151,6 +166,11 @@ struct DecodeDev {
   void* out;
   int32_t out_dtype;
   float oscale;
+  // QJL stage-2 scores (generic path): see DecodeArgs
+  const float* q_proj;
+  int64_t off_kq, off_kr;
+  int32_t row_kq, qjl_m;
+  float qjl_c;
   InlineMeta meta;  // seqinfo / seg / cnt when those pointers are null
   __device__ __forceinline__ const int64_t* si() const { return seqinfo ? seqinfo : meta.seqinfo; }
   __device__ __forceinline__ const int64_t* sg() const { return seg ? seg : meta.seg; }
@@ -1229,6 +1249,16 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
         o[g][k] = 0.f;
       }
     }
+    // QJL: projection rows i = lane + 32 r of (Phi q) * qscale per head
+    const bool qjl = a.q_proj != nullptr;
+    float pq[GS][kMaxQjlDecode / 32];
+#pragma unroll
+    for (int g = 0; g < GS; ++g)
+#pragma unroll
+      for (int r = 0; r < kMaxQjlDecode / 32; ++r) {
+        const int i = lane + 32 * r;
+        pq[g][r] = (qjl && i < a.qjl_m) ? a.q_proj[((int64_t)s * a.hq + qh0 + g) * a.qjl_m + i] : 0.f;
+      }
     for (int pw = warp; pw < a.pages_per_chunk; pw += nw) {
       const int64_t page_idx = (int64_t)chunk * a.pages_per_chunk + pw;
       const int64_t tok0 = page_idx * kPageTokens;
@@ -1239,6 +1269,9 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
       const float* ks = reinterpret_cast<const float*>(page + a.off_ks) + (int64_t)kvh * kPageTokens;
       const float* vs = reinterpret_cast<const float*>(page + a.off_vs) + (int64_t)kvh * kPageTokens;
       const int kw_row = a.row_kw / 8, vw_row = a.row_vw / 8;
+      const uint64_t* kq = qjl ? reinterpret_cast<const uint64_t*>(page + a.off_kq + (int64_t)kvh * kPageTokens * a.row_kq)
+                               : nullptr;
+      const float* kr = qjl ? reinterpret_cast<const float*>(page + a.off_kr) + (int64_t)kvh * kPageTokens : nullptr;
       const int nt = (int)(n_valid - tok0 < kPageTokens ? n_valid - tok0 : kPageTokens);
       for (int tt = 0; tt < nt; ++tt) {
         float part[GS];
@@ -1261,9 +1294,35 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
           for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
         }
         const float ksg = ks[tt], vsg = vs[tt];
+        // QJL stage 2 (compressor.rs:148-155, qjl.rs:86-119):
+        // ||r|| sqrt(pi/2)/sqrt(m) * sum_i sign_i (Phi q)_i, 0 when ||r|| < 1e-10
+        float cr[GS];
+#pragma unroll
+        for (int g = 0; g < GS; ++g) cr[g] = 0.f;
+        if (qjl) {
+          const uint64_t* sw = kq + (int64_t)tt * (a.row_kq / 8);
+#pragma unroll
+          for (int r = 0; r < kMaxQjlDecode / 32; ++r) {
+            const int i = lane + 32 * r;
+            if (i < a.qjl_m) {
+              const bool pos = (sw[i >> 6] >> (i & 63)) & 1ull;
+#pragma unroll
+              for (int g = 0; g < GS; ++g) cr[g] += pos ? pq[g][r] : -pq[g][r];
+            }
+          }
+#pragma unroll
+          for (int g = 0; g < GS; ++g) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) cr[g] += __shfl_xor_sync(0xffffffffu, cr[g], off);
+          }
+          const float rn = kr[tt];
+          const float rho = rn < 1e-10f ? 0.f : rn * a.qjl_c;
+#pragma unroll
+          for (int g = 0; g < GS; ++g) cr[g] *= rho;
+        }
 #pragma unroll
         for (int g = 0; g < GS; ++g) {
-          const float sc = part[g] * ksg;
+          const float sc = fmaf(part[g], ksg, cr[g]);
           const float mn = fmaxf(m[g], sc);
           const float al = exp2f(m[g] - mn);
           const float p = exp2f(sc - mn);
@@ -1524,12 +1583,13 @@ static int32_t max_cta_segments(const int64_t* seg, const int64_t* lens, int n, 
   return (int32_t)mx;
 }
 
-DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits) {
+DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits,
+                       bool generic_only) {
   DecodePlan p;
   const int G = hq / hkv;
   const int n = (int)lens.size();
   p.cnt.assign((size_t)n * hkv, 0);
-  if (decode_fast_path(dim, kbits, vbits, G)) {
+  if (!generic_only && decode_fast_path(dim, kbits, vbits, G)) {
     p.flat = true;
     p.grid = num_sms();
     p.seg.assign(n + 1, 0);
@@ -1608,6 +1668,13 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
   LC_CUDA(cudaGetLastError());
 }
 
+void launch_project_q(const void* q, int32_t dtype, int32_t n_rows, int32_t dim, int32_t m, const float* PT,
+                      float qscale, float* q_proj, cudaStream_t s) {
+  if (n_rows <= 0) return;
+  k_project_q<<<n_rows, 128, (size_t)dim * sizeof(float), s>>>(q, dtype, dim, m, PT, qscale, q_proj);
+  LC_CUDA(cudaGetLastError());
+}
+
 static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
   LC_REQUIRE(p.total_tiles < (int64_t(1) << 31) - (int64_t)kFlatWarps * 148 * 2, LC_ERR_INVALID,
              "decode call too large: split it (at most 2^31 tiles of 32 tokens x kv head)");
@@ -1648,6 +1715,16 @@ static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
   d.kalpha = a.kalpha;
   d.valpha = a.valpha;
   d.part = a.part;
+  d.q_proj = a.q_proj;
+  if (a.q_proj) {
+    LC_REQUIRE(!p.flat && a.qjl_m > 0 && a.qjl_m <= kMaxQjlDecode && a.role_kq >= 0 && a.role_kr >= 0,
+               LC_ERR_STATE, "QJL scores need the generic path, 0 < qjl_m <= 256 and stored K QJL bits");
+    d.off_kq = a.layout.off[a.role_kq];
+    d.off_kr = a.layout.off[a.role_kr];
+    d.row_kq = (int32_t)a.layout.row[a.role_kq];
+    d.qjl_m = a.qjl_m;
+    d.qjl_c = a.qjl_c;
+  }
   return d;
 }
 

@@ -79,7 +79,19 @@ struct DecodeArgs {
   const int64_t* h_seqinfo = nullptr;
   const int64_t* h_seg = nullptr;
   const int32_t* h_cnt = nullptr;
+  // QJL stage-2 scores (generic path only): q_proj [n_seqs][hq][qjl_m] f32 =
+  // (Phi q) * scale * log2(e); null: stage-1 scores.
+  const float* q_proj = nullptr;
+  int32_t role_kq = -1, role_kr = -1, qjl_m = 0;
+  float qjl_c = 0.f;  // sqrt(pi/2) / sqrt(qjl_m)
 };
+
+// Largest qjl_m the decode's QJL scores take (8 projection rows per lane).
+constexpr int kMaxQjlDecode = 256;
+
+// q_proj[r][i] = qscale * sum_j Phi[i][j] q[r][j] (PT = Phi^T, [dim][m]).
+void launch_project_q(const void* q, int32_t dtype, int32_t n_rows, int32_t dim, int32_t m, const float* PT,
+                      float qscale, float* q_proj, cudaStream_t s);
 
 // Per-call decode arrays that fit in the launch parameters.
 constexpr int kInlineSeqs = 64;
@@ -101,7 +113,10 @@ struct DecodePlan {
   std::vector<int64_t> seg;  // [n_seqs + 1]
   std::vector<int32_t> cnt;  // [n_seqs * hkv] slots used per (seq, kv head)
 };
-DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits);
+// generic_only: take the chunked generic path even where the fast path
+// applies (QJL scores).
+DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits,
+                       bool generic_only = false);
 int num_sms();
 
 // q_rot[s][h][:] = (R q[s][h]) * qscale (R applied unless q_is_rotated)
@@ -131,6 +146,10 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
 // ---- parity hooks of the KVCache trait (hooks.cu): bit-exact in the
 // reference's f32 order ----
 // scores[t] = (sum_j (Rq)_j * c[code_tj]) * sigma_t for t < n   (compressor.rs:165-184)
+// estimate_inner_products: stage 1 + QJL stage 2 (pq_scratch: m floats).
+void launch_attend_keys_qjl(const float* q, const CodecDev& kc, const uint64_t* pages, const PageLayout& L,
+                            int role_kw, int role_ks, int role_kq, int role_kr, int head, int64_t n,
+                            float* rq_scratch, float* pq_scratch, float* scores, cudaStream_t s);
 void launch_attend_keys(const float* q, const CodecDev& kc, const uint64_t* pages, const PageLayout& L, int role_kw,
                         int role_ks, int head, int64_t n, float* rq_scratch, float* scores, cudaStream_t s);
 // out[i] = sum_t sum_j R[j][i] * (c[code_tj] * (sigma_t * w_t)), |w_t| >= 1e-10   (simple.rs:76-99, 142-155)

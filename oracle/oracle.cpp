@@ -432,6 +432,14 @@ void orc_sc_attend_keys(const orc_simple_cache* s, int layer, int head, const fl
     orc_estimate_stage1(s->kc, query, l.n, l.s1.data(), l.scale.data(), out);
 }
 
+// The two-stage scores of a (layer, head)'s keys: estimate_inner_products
+// (compressor.rs:122-159) over the stored stage-1 words, scales, QJL words
+// and residual norms. SimpleCache itself scores with stage 1 only.
+void orc_sc_attend_keys_qjl(const orc_simple_cache* s, int layer, int head, const float* query, float* out) {
+    const orc_cv_list& l = s->keys[(size_t)layer * s->n_heads + head];
+    orc_estimate_two_stage(s->kc, query, l.n, l.s1.data(), l.scale.data(), l.s2.data(), l.rnorm.data(), out);
+}
+
 // simple.rs:76-99 + 142-155: per-token un-rotation of c*sigma*w.
 void orc_sc_attend_values(const orc_simple_cache* s, int layer, int head, const float* weights, float* out) {
     const orc_cv_list& l = s->values[(size_t)layer * s->n_heads + head];
@@ -520,10 +528,13 @@ void orc_sc_load(orc_simple_cache* s, int layer, int head, int side, int64_t n, 
 // scores = attend_keys(q) * scale, w = softmax(scores) (max-subtracted, f64
 // normaliser), out = attend_values(w). One (layer, kv-head, query) per call.
 // ---------------------------------------------------------------------------
-void orc_sc_attend(const orc_simple_cache* s, int layer, int head, const float* query, float scale, float* out) {
+// qjl != 0: score with the two-stage estimate (orc_sc_attend_keys_qjl).
+void orc_sc_attend_ex(const orc_simple_cache* s, int layer, int head, const float* query, float scale, int qjl,
+                      float* out) {
     const orc_cv_list& l = s->keys[(size_t)layer * s->n_heads + head];
     std::vector<float> sc(l.n > 0 ? l.n : 1), w(l.n > 0 ? l.n : 1);
-    orc_sc_attend_keys(s, layer, head, query, sc.data());
+    if (qjl) orc_sc_attend_keys_qjl(s, layer, head, query, sc.data());
+    else orc_sc_attend_keys(s, layer, head, query, sc.data());
     double mx = -INFINITY;
     for (int64_t t = 0; t < l.n; ++t) mx = std::max(mx, (double)sc[t] * (double)scale);
     double sum = 0.0;
@@ -531,6 +542,10 @@ void orc_sc_attend(const orc_simple_cache* s, int layer, int head, const float* 
     for (int64_t t = 0; t < l.n; ++t) w[t] = (float)(std::exp((double)sc[t] * (double)scale - mx) / sum);
     if (l.n == 0) { for (int i = 0; i < s->dim; ++i) out[i] = 0.0f; return; }
     orc_sc_attend_values(s, layer, head, w.data(), out);
+}
+
+void orc_sc_attend(const orc_simple_cache* s, int layer, int head, const float* query, float scale, float* out) {
+    orc_sc_attend_ex(s, layer, head, query, scale, 0, out);
 }
 
 // ---------------------------------------------------------------------------

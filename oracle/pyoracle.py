@@ -85,6 +85,8 @@ def lib():
         L.orc_sc_seq_len.restype = C.c_int64
         L.orc_sc_seq_len.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.orc_sc_attend_keys.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
+        L.orc_sc_attend_keys_qjl.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
+        L.orc_sc_attend_ex.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int, _f32p]
         L.orc_sc_attend_values.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, _f32p]
         L.orc_sc_clear.argtypes = [C.c_void_p]
@@ -297,14 +299,22 @@ class SimpleCache:
         lib().orc_sc_attend_keys(self._h, layer, head, np.ascontiguousarray(q, np.float32), out)
         return out[: self.seq_len(layer, head)]
 
+    def attend_keys_qjl(self, layer, head, q):
+        """Two-stage scores: estimate_inner_products (compressor.rs:122-159)."""
+        out = np.empty(max(self.seq_len(layer, head), 1), np.float32)
+        lib().orc_sc_attend_keys_qjl(self._h, layer, head, np.ascontiguousarray(q, np.float32), out)
+        return out[: self.seq_len(layer, head)]
+
     def attend_values(self, layer, head, w):
         out = np.empty(self.dim, np.float32)
         lib().orc_sc_attend_values(self._h, layer, head, np.ascontiguousarray(w, np.float32), out)
         return out
 
-    def attend(self, layer, head, q, scale=1.0):
+    def attend(self, layer, head, q, scale=1.0, qjl=False):
+        """softmax(scale * scores) then attend_values; qjl: two-stage scores."""
         out = np.empty(self.dim, np.float32)
-        lib().orc_sc_attend(self._h, layer, head, np.ascontiguousarray(q, np.float32), float(scale), out)
+        lib().orc_sc_attend_ex(self._h, layer, head, np.ascontiguousarray(q, np.float32), float(scale),
+                               1 if qjl else 0, out)
         return out
 
     def clear(self):

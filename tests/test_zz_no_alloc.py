@@ -91,6 +91,9 @@ def test_noalloc_refusals(lc, orc, gpu):
     st = lc.lib().lc_decode_attn_noalloc(cache._h, 0, 2, ids.ctypes.data, q_host.data_ptr(), lc.LC_BF16, 32,
                                          C.c_float(1.0), 0, out.data_ptr(), lc.LC_F32, None)
     assert st == lc.LC_ERR_INVALID and b"device memory" in lc.lib().lc_last_error()
+    # QJL scores are not taken here
+    st = _noalloc(lc, cache, ids, q, 32, 1.0, lc.LC_QJL_SCORES, out, lc.LC_F32)
+    assert st == lc.LC_ERR_INVALID and b"LC_QJL_SCORES" in lc.lib().lc_last_error()
     # 2 x 32768 query heads: rows * head_dim * 6 alone is 48 MiB > 32 MiB
     big_hq = 8 * 1024 * 4
     qb = torch.zeros((2, big_hq, dim), dtype=torch.bfloat16, device="cuda")
