@@ -217,6 +217,39 @@ typedef struct lc_fetch_out {
 int lc_fetch(lc_cache* cache, int32_t seq, int32_t layer, int32_t which, lc_fetch_out* out,
              int64_t max_tokens, int64_t* n_out);
 
+/* ---- LKV2 snapshots (crates/lumen-mlx/src/kv_disk.rs) ----------------------
+ * The reference's on-disk prompt-cache format (layout kv_disk.rs:285-323):
+ * "LKV2", version 2, a JSON KvManifest with its CRC-32, then typed records
+ * each with its CRC-32. A saved sequence has one LayerMeta per cache layer,
+ * kind FullTurboquant or SlidingTurboquant, carrying offset, idx, keep,
+ * max_size, bits (K; "v_bits" too when V differs) and qjl_m, and the arrays
+ * of turboquant_meta (kv_disk.rs:2000-2024): keys_codes u8 [1,H,S,D],
+ * keys_sigma f32 [1,H,S,1], values_codes, values_sigma, and with
+ * LC_STORE_K_QJL keys_signs bf16 +-1 [1,H,S,m] and keys_residual_norm f32
+ * [1,H,S,1]; with LC_STORE_V_QJL the V signs and residual norms follow in
+ * slots 6 and 7. S is the ring's backing length, rows in backing order. */
+
+/* Write sequence `seq`'s layers to `path` (written to path.tmp, then
+ * renamed). model_fingerprint may be NULL (""); prefix_tokens are stored in
+ * the manifest. LC_ERR_STATE for a layer filled by lc_store with per-head
+ * lengths; LC_ERR_IO on a write failure. */
+int lc_save_lkv2(lc_cache* cache, int32_t seq, const char* path, const char* model_fingerprint,
+                 const uint32_t* prefix_tokens, int64_t n_prefix_tokens);
+
+/* Replace sequence `seq`'s layers with the snapshot in `path`. Everything is
+ * checked before the cache changes: LC_ERR_MAGIC (magic, version), LC_ERR_IO
+ * (CRC mismatch, truncation, trailing bytes, record length != shape x dtype,
+ * malformed manifest), LC_ERR_STATE (model_fingerprint given and different),
+ * LC_ERR_BITS (bit widths), LC_ERR_INVALID (layer count, kind, max_size /
+ * keep, shapes, codes out of range, signs not +-1, missing QJL arrays the
+ * cache keeps), LC_ERR_NOMEM (not enough free pages). */
+int lc_load_lkv2(lc_cache* cache, int32_t seq, const char* path, const char* model_fingerprint);
+
+/* Read and check an LKV2 file on the host only (no device): layer count,
+ * record count and the manifest's position. Same error codes as
+ * lc_load_lkv2's file checks. */
+int lc_lkv2_info(const char* path, int64_t* n_layers, int64_t* n_records, uint64_t* position);
+
 /* Decode flags. */
 #define LC_Q_ROTATED 1u   /* q is already R q (Gemma path); skip the rotation */
 #define LC_OUT_ROTATED 2u /* leave the output in the rotated basis (R baked into Wo) */

@@ -51,7 +51,7 @@ ABI_SYMBOLS = [
     "lc_decode_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
-    "lc_ring_deep_clone", "lc_ring_destroy", "lc_version",
+    "lc_ring_deep_clone", "lc_ring_destroy", "lc_version", "lc_save_lkv2", "lc_load_lkv2", "lc_lkv2_info",
 ]
 
 
@@ -119,6 +119,9 @@ def lib():
         "lc_release": (C.c_int, [vp, i32]),
         "lc_ring_state": (C.c_int, [vp, i32, i32, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
         "lc_fetch": (C.c_int, [vp, i32, i32, i32, C.POINTER(lc_fetch_out), i64, C.POINTER(i64)]),
+        "lc_save_lkv2": (C.c_int, [vp, i32, C.c_char_p, C.c_char_p, vp, i64]),
+        "lc_load_lkv2": (C.c_int, [vp, i32, C.c_char_p, C.c_char_p]),
+        "lc_lkv2_info": (C.c_int, [C.c_char_p, C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_uint64)]),
         "lc_decode_attn": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_noalloc": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_partials": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, vp, vp, vp]),
@@ -184,6 +187,13 @@ def _auto_stream(stream, *tensors):
 
             return torch.cuda.current_stream(t.device).cuda_stream or CUDA_STREAM_LEGACY
     return None
+
+
+def lkv2_info(path) -> dict:
+    """Host-only read and check of an LKV2 snapshot (kv_disk.rs format)."""
+    nl, nr, pos = C.c_int64(), C.c_int64(), C.c_uint64()
+    _check(lib().lc_lkv2_info(os.fsencode(path), C.byref(nl), C.byref(nr), C.byref(pos)))
+    return {"layers": nl.value, "records": nr.value, "position": pos.value}
 
 
 def packed_words(n: int, bits: int) -> int:
@@ -348,6 +358,17 @@ class CudaKvCache:
         o, i, b, v = C.c_int64(), C.c_int64(), C.c_int64(), C.c_int64()
         _check(lib().lc_ring_state(self._h, seq, layer, C.byref(o), C.byref(i), C.byref(b), C.byref(v)))
         return dict(offset=o.value, idx=i.value, buf_len=b.value, view_len=v.value)
+
+    def save_lkv2(self, seq: int, path, model_fingerprint: Optional[str] = None, prefix_tokens=()):
+        """Snapshot sequence `seq`'s layers to an LKV2 file (kv_disk.rs)."""
+        toks = np.ascontiguousarray(prefix_tokens, np.uint32)
+        fp = None if model_fingerprint is None else model_fingerprint.encode()
+        _check(lib().lc_save_lkv2(self._h, seq, os.fsencode(path), fp, _ptr(toks) if len(toks) else None, len(toks)))
+
+    def load_lkv2(self, seq: int, path, model_fingerprint: Optional[str] = None):
+        """Replace sequence `seq`'s layers with an LKV2 snapshot."""
+        fp = None if model_fingerprint is None else model_fingerprint.encode()
+        _check(lib().lc_load_lkv2(self._h, seq, os.fsencode(path), fp))
 
     def fetch(self, seq: int, layer: int, which: int = LC_FETCH_VIEW):
         """Stored vectors of (seq, layer) in the reference's CompressedVector layout."""

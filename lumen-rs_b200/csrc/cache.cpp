@@ -17,10 +17,12 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <ctime>
 #include <memory>
 
 #include "codec.h"
 #include "kernels.h"
+#include "lkv2.h"
 #include "ring.h"
 
 namespace lc {
@@ -546,6 +548,321 @@ int lc_clear(lc_cache* c) {
       sl.head_len.clear();
       sl.dirty = true;
     }
+  });
+}
+
+// ---- LKV2 snapshots (kv_disk.rs) --------------------------------------------
+// One LayerMeta per cache layer, kind FullTurboquant (unbounded ring) or
+// SlidingTurboquant, with the ring bookkeeping (offset, idx, keep,
+// max_size) and the arrays of turboquant_meta (kv_disk.rs:2000-2024):
+//   0 keys_codes u8 [1, H, S, D]        1 keys_sigma f32 [1, H, S, 1]
+//   2 values_codes u8 [1, H, S, D]      3 values_sigma f32 [1, H, S, 1]
+//   4 keys_signs bf16 +-1 [1, H, S, m]  5 keys_residual_norm f32 [1, H, S, 1]
+// (4, 5 when the cache keeps the K QJL bits), S = the ring's backing length,
+// rows in backing order. When the cache keeps the V QJL bits they follow in
+// slots 6, 7 (values_signs, values_residual_norm); the reference's reader
+// uses slots 0-5 only. Codes are unpacked to one byte each and QJL bits to
+// +-1, as the reference's MLX arrays hold them. Pages move as whole page
+// images, one copy each way per page.
+namespace {
+
+constexpr uint16_t kBf16One = 0x3F80, kBf16MinusOne = 0xBF80;
+
+struct LayerRecs {
+  int64_t S = 0;
+  const Lkv2Record* r[8] = {};
+};
+
+// Byte offset of (role, head, row-in-page) in a page image.
+inline size_t img_at(const PageLayout& L, int role, int h, int t) {
+  return (size_t)(L.off[role] + ((int64_t)h * kPageTokens + t) * L.row[role]);
+}
+
+}  // namespace
+
+int lc_save_lkv2(lc_cache* c, int32_t seq, const char* path, const char* model_fingerprint,
+                 const uint32_t* prefix_tokens, int64_t n_prefix_tokens) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && path, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_prefix_tokens >= 0 && (n_prefix_tokens == 0 || prefix_tokens), LC_ERR_INVALID, "bad prefix tokens");
+    c->check(seq, 0);
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    c->order(s);
+    LC_CUDA(cudaStreamSynchronize(s));
+    const int H = c->cfg.n_kv_heads, D = c->cfg.head_dim;
+    const int kb = (int)c->kc.bits, vb = (int)c->vc.bits;
+    const bool kq = c->cfg.store_flags & LC_STORE_K_QJL, vq = c->cfg.store_flags & LC_STORE_V_QJL;
+    const int mk = (int)c->kc.m, mv = (int)c->vc.m;
+    const PageLayout& PL = c->layout;
+    Lkv2Manifest man;
+    man.model_fingerprint = model_fingerprint ? model_fingerprint : "";
+    man.created_at_unix = (uint64_t)std::time(nullptr);
+    man.prefix_tokens.assign(prefix_tokens, prefix_tokens + n_prefix_tokens);
+    man.is_deep = true;
+    std::vector<Lkv2Record> recs;
+    std::vector<uint8_t> img((size_t)PL.page_bytes);
+    for (int32_t l = 0; l < c->cfg.n_layers; ++l) {
+      const SeqLayer& sl = c->at(seq, l);
+      LC_REQUIRE(sl.head_len.empty(), LC_ERR_STATE,
+                 "LKV2: a layer holds per-head lengths (KVCache::store); only ring layers are saved");
+      const RingCore& r = sl.ring;
+      Lkv2Layer L;
+      L.kind = c->full(l) ? "FullTurboquant" : "SlidingTurboquant";
+      L.offset = (uint64_t)r.offset;
+      L.max_size = c->max_size[l];
+      L.keep = c->keep[l];
+      L.idx = r.idx;
+      L.bits = kb;
+      L.qjl_m = kq ? mk : -1;
+      L.v_bits = vb != kb ? vb : -1;
+      man.position = std::max<uint64_t>(man.position, (uint64_t)r.offset);
+      const int64_t S = r.has ? r.buf_len : 0;
+      if (S == 0) {
+        L.arrays.assign(vq ? 8 : 6, -1);
+        man.layers.push_back(L);
+        continue;
+      }
+      const int32_t S32 = (int32_t)S;
+      const size_t first = recs.size();
+      auto add = [&](uint8_t dt, std::vector<int32_t> shape) {
+        L.arrays.push_back((int64_t)recs.size());
+        recs.emplace_back();
+        Lkv2Record& rec = recs.back();
+        rec.dtype = dt;
+        rec.shape = std::move(shape);
+        rec.data.assign((size_t)(rec.elems() * lkv2_elem_size(dt)), 0);
+      };
+      add(kLkvU8, {1, H, S32, D});
+      add(kLkvF32, {1, H, S32, 1});
+      add(kLkvU8, {1, H, S32, D});
+      add(kLkvF32, {1, H, S32, 1});
+      if (kq) {
+        add(kLkvBF16, {1, H, S32, mk});
+        add(kLkvF32, {1, H, S32, 1});
+      } else {
+        L.arrays.push_back(-1);
+        L.arrays.push_back(-1);
+      }
+      if (vq) {
+        add(kLkvBF16, {1, H, S32, mv});
+        add(kLkvF32, {1, H, S32, 1});
+      }
+      Lkv2Record* kc_ = &recs[first];
+      Lkv2Record* ks_ = kc_ + 1;
+      Lkv2Record* vc_ = kc_ + 2;
+      Lkv2Record* vs_ = kc_ + 3;
+      Lkv2Record* kg_ = kq ? kc_ + 4 : nullptr;
+      Lkv2Record* kr_ = kq ? kc_ + 5 : nullptr;
+      Lkv2Record* vg_ = vq ? kc_ + (kq ? 6 : 4) : nullptr;
+      Lkv2Record* vr_ = vq ? vg_ + 1 : nullptr;
+      auto codes = [&](const uint8_t* words, int bits, uint8_t* out) {
+        const int cpw = 64 / bits;
+        const uint64_t mask = (1ull << bits) - 1;
+        for (int j = 0; j < D; ++j) {
+          uint64_t w;
+          std::memcpy(&w, words + (size_t)(j / cpw) * 8, 8);
+          out[j] = (uint8_t)((w >> ((j % cpw) * bits)) & mask);
+        }
+      };
+      auto signs = [&](const uint8_t* words, int m, uint8_t* out) {
+        for (int i = 0; i < m; ++i) {
+          uint64_t w;
+          std::memcpy(&w, words + (size_t)(i / 64) * 8, 8);
+          const uint16_t v = ((w >> (i % 64)) & 1ull) ? kBf16One : kBf16MinusOne;
+          std::memcpy(out + 2 * (size_t)i, &v, 2);
+        }
+      };
+      for (size_t p = 0; (int64_t)(p * kPageTokens) < S; ++p) {
+        LC_CUDA(cudaMemcpy(img.data(), reinterpret_cast<const void*>(c->pool.addr(r.pages[p])), img.size(),
+                           cudaMemcpyDeviceToHost));
+        const int nt = (int)std::min<int64_t>(kPageTokens, S - (int64_t)p * kPageTokens);
+        for (int h = 0; h < H; ++h)
+          for (int t = 0; t < nt; ++t) {
+            const size_t row = (size_t)h * S + p * kPageTokens + t;  // [1][H][S] index
+            codes(&img[img_at(PL, R_KW, h, t)], kb, &kc_->data[row * D]);
+            codes(&img[img_at(PL, R_VW, h, t)], vb, &vc_->data[row * D]);
+            std::memcpy(&ks_->data[row * 4], &img[img_at(PL, R_KS, h, t)], 4);
+            std::memcpy(&vs_->data[row * 4], &img[img_at(PL, R_VS, h, t)], 4);
+            if (kq) {
+              signs(&img[img_at(PL, R_KQ, h, t)], mk, &kg_->data[row * mk * 2]);
+              std::memcpy(&kr_->data[row * 4], &img[img_at(PL, R_KR, h, t)], 4);
+            }
+            if (vq) {
+              signs(&img[img_at(PL, R_VQ, h, t)], mv, &vg_->data[row * mv * 2]);
+              std::memcpy(&vr_->data[row * 4], &img[img_at(PL, R_VR, h, t)], 4);
+            }
+          }
+      }
+      man.layers.push_back(L);
+    }
+    lkv2_write(path, man, recs);
+  });
+}
+
+int lc_load_lkv2(lc_cache* c, int32_t seq, const char* path, const char* model_fingerprint) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && path, LC_ERR_INVALID, "null argument");
+    c->check(seq, 0);
+    Lkv2Manifest man;
+    std::vector<Lkv2Record> recs;
+    lkv2_read(path, man, recs);
+    if (model_fingerprint)
+      LC_REQUIRE(man.model_fingerprint == model_fingerprint, LC_ERR_STATE, "LKV2: model fingerprint differs");
+    const int H = c->cfg.n_kv_heads, D = c->cfg.head_dim;
+    const int kb = (int)c->kc.bits, vb = (int)c->vc.bits;
+    const bool kq = c->cfg.store_flags & LC_STORE_K_QJL, vq = c->cfg.store_flags & LC_STORE_V_QJL;
+    const int mk = (int)c->kc.m, mv = (int)c->vc.m;
+    LC_REQUIRE((int64_t)man.layers.size() == c->cfg.n_layers, LC_ERR_INVALID,
+               "LKV2: layer count differs from the cache");
+    // ---- validate everything before the cache changes ----
+    std::vector<LayerRecs> plan(c->cfg.n_layers);
+    int64_t pages_needed = 0;
+    for (int32_t l = 0; l < c->cfg.n_layers; ++l) {
+      const Lkv2Layer& L = man.layers[l];
+      const std::string where = "LKV2 layer " + std::to_string(l) + ": ";
+      LC_REQUIRE(L.kind == "FullTurboquant" || L.kind == "SlidingTurboquant", LC_ERR_INVALID,
+                 where + "not a TurboQuant layer (" + L.kind + ")");
+      LC_REQUIRE(L.max_size == c->max_size[l] && L.keep == c->keep[l], LC_ERR_INVALID,
+                 where + "max_size / keep differ from the cache's layer");
+      LC_REQUIRE(L.bits == kb && (L.v_bits >= 0 ? L.v_bits : L.bits) == vb, LC_ERR_BITS,
+                 where + "bit widths differ from the cache's codecs");
+      LC_REQUIRE(L.idx >= 0, LC_ERR_INVALID, where + "missing idx");
+      auto slot = [&](size_t i) -> const Lkv2Record* {
+        if (i >= L.arrays.size() || L.arrays[i] < 0) return nullptr;
+        LC_REQUIRE(L.arrays[i] < (int64_t)recs.size(), LC_ERR_INVALID, where + "array index out of range");
+        return &recs[(size_t)L.arrays[i]];
+      };
+      LayerRecs& P = plan[l];
+      for (int i = 0; i < 8; ++i) P.r[i] = slot((size_t)i);
+      if (!P.r[0]) {
+        LC_REQUIRE(!P.r[1] && !P.r[2] && !P.r[3] && L.offset == 0, LC_ERR_INVALID, where + "keys_codes missing");
+        continue;
+      }
+      const Lkv2Record& k0 = *P.r[0];
+      LC_REQUIRE(k0.shape.size() == 4 && k0.shape[0] == 1 && k0.shape[1] == H && k0.shape[3] == D, LC_ERR_INVALID,
+                 where + "keys_codes shape is not [1, n_kv_heads, S, head_dim]");
+      const int32_t S = k0.shape[2];
+      auto want = [&](const Lkv2Record* r, uint8_t dt, int32_t last, const char* what) {
+        LC_REQUIRE(r && r->dtype == dt && r->shape == std::vector<int32_t>({1, H, S, last}), LC_ERR_INVALID,
+                   where + what + " missing or of the wrong dtype/shape");
+      };
+      want(P.r[0], kLkvU8, D, "keys_codes");
+      want(P.r[1], kLkvF32, 1, "keys_sigma");
+      want(P.r[2], kLkvU8, D, "values_codes");
+      want(P.r[3], kLkvF32, 1, "values_sigma");
+      if (kq) {
+        LC_REQUIRE(L.qjl_m == mk, LC_ERR_INVALID, where + "qjl_m differs from the K codec's");
+        want(P.r[4], kLkvBF16, mk, "keys_signs");
+        want(P.r[5], kLkvF32, 1, "keys_residual_norm");
+      }
+      if (vq) {
+        want(P.r[6], kLkvBF16, mv, "values_signs");
+        want(P.r[7], kLkvF32, 1, "values_residual_norm");
+      }
+      LC_REQUIRE((int64_t)S <= (int64_t)c->cfg.max_pages_per_seq * kPageTokens, LC_ERR_NOMEM,
+                 where + "more rows than max_pages_per_seq holds");
+      LC_REQUIRE(L.idx <= S, LC_ERR_INVALID, where + "idx beyond the buffer");
+      LC_REQUIRE((int64_t)L.offset >= L.max_size || (int64_t)L.offset <= S, LC_ERR_INVALID,
+                 where + "offset beyond the buffer of a ring that has not wrapped");
+      for (uint8_t v : P.r[0]->data) LC_REQUIRE(v < (1u << kb), LC_ERR_INVALID, where + "K code out of range");
+      for (uint8_t v : P.r[2]->data) LC_REQUIRE(v < (1u << vb), LC_ERR_INVALID, where + "V code out of range");
+      for (int i : {4, 6}) {
+        if (!((i == 4 && kq) || (i == 6 && vq))) continue;
+        const std::vector<uint8_t>& d = P.r[i]->data;
+        for (size_t k = 0; k < d.size(); k += 2) {
+          const uint16_t v = (uint16_t)(d[k] | (d[k + 1] << 8));
+          LC_REQUIRE(v == kBf16One || v == kBf16MinusOne, LC_ERR_INVALID, where + "QJL sign not +-1");
+        }
+      }
+      P.S = S;
+      pages_needed += (S + kPageTokens - 1) / kPageTokens;
+    }
+    LC_REQUIRE(pages_needed <= c->pool.free_pages(), LC_ERR_NOMEM, "LKV2: page pool too small for the snapshot");
+    // ---- apply: fresh private pages per layer ----
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->stream;
+    c->order(s);
+    LC_CUDA(cudaStreamSynchronize(s));
+    const PageLayout& PL = c->layout;
+    std::vector<uint8_t> img((size_t)PL.page_bytes);
+    auto pack = [&](const uint8_t* codes, int bits, uint8_t* words) {
+      const int cpw = 64 / bits;
+      const int nw = (D + cpw - 1) / cpw;
+      for (int w = 0; w < nw; ++w) {
+        uint64_t v = 0;
+        for (int k = 0; k < cpw && w * cpw + k < D; ++k) v |= (uint64_t)codes[w * cpw + k] << (k * bits);
+        std::memcpy(words + 8 * (size_t)w, &v, 8);
+      }
+    };
+    auto unsigns = [&](const uint8_t* pm, int m, uint8_t* words) {
+      const int nw = (m + 63) / 64;
+      for (int w = 0; w < nw; ++w) {
+        uint64_t v = 0;
+        for (int i = w * 64; i < std::min(m, w * 64 + 64); ++i)
+          if (pm[2 * (size_t)i + 1] == 0x3F) v |= 1ull << (i % 64);  // +1 (0x3F80) -> bit set
+        std::memcpy(words + 8 * (size_t)w, &v, 8);
+      }
+    };
+    for (int32_t l = 0; l < c->cfg.n_layers; ++l) {
+      SeqLayer& sl = c->at(seq, l);
+      c->ops.clear(sl.ring);
+      sl.head_len.clear();
+      sl.dirty = true;
+      const Lkv2Layer& L = man.layers[l];
+      const LayerRecs& P = plan[l];
+      RingCore& r = sl.ring;
+      r.max_size = c->max_size[l];
+      r.keep = c->keep[l];
+      if (P.S == 0) continue;
+      const int64_t S = P.S;
+      try {
+        for (int64_t p = 0; p * kPageTokens < S; ++p) {
+          std::fill(img.begin(), img.end(), 0);
+          const int nt = (int)std::min<int64_t>(kPageTokens, S - p * kPageTokens);
+          for (int h = 0; h < H; ++h)
+            for (int t = 0; t < nt; ++t) {
+              const size_t row = (size_t)h * S + p * kPageTokens + t;
+              pack(&P.r[0]->data[row * D], kb, &img[img_at(PL, R_KW, h, t)]);
+              pack(&P.r[2]->data[row * D], vb, &img[img_at(PL, R_VW, h, t)]);
+              std::memcpy(&img[img_at(PL, R_KS, h, t)], &P.r[1]->data[row * 4], 4);
+              std::memcpy(&img[img_at(PL, R_VS, h, t)], &P.r[3]->data[row * 4], 4);
+              if (kq) {
+                unsigns(&P.r[4]->data[row * mk * 2], mk, &img[img_at(PL, R_KQ, h, t)]);
+                std::memcpy(&img[img_at(PL, R_KR, h, t)], &P.r[5]->data[row * 4], 4);
+              }
+              if (vq) {
+                unsigns(&P.r[6]->data[row * mv * 2], mv, &img[img_at(PL, R_VQ, h, t)]);
+                std::memcpy(&img[img_at(PL, R_VR, h, t)], &P.r[7]->data[row * 4], 4);
+              }
+            }
+          const int32_t pg = c->pool.alloc();
+          r.pages.push_back(pg);
+          LC_CUDA(cudaMemcpy(reinterpret_cast<void*>(c->pool.addr(pg)), img.data(), img.size(),
+                             cudaMemcpyHostToDevice));
+        }
+      } catch (...) {
+        c->ops.clear(r);
+        throw;
+      }
+      r.has = true;
+      r.buf_len = S;
+      r.offset = (int64_t)L.offset;
+      r.idx = L.idx;
+      r.view_len = r.offset >= r.max_size ? S : r.offset;
+    }
+  });
+}
+
+int lc_lkv2_info(const char* path, int64_t* n_layers, int64_t* n_records, uint64_t* position) {
+  return abi_guard([&] {
+    LC_REQUIRE(path, LC_ERR_INVALID, "null path");
+    Lkv2Manifest man;
+    std::vector<Lkv2Record> recs;
+    lkv2_read(path, man, recs);
+    if (n_layers) *n_layers = (int64_t)man.layers.size();
+    if (n_records) *n_records = (int64_t)recs.size();
+    if (position) *position = man.position;
   });
 }
 
