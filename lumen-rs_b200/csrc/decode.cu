@@ -149,6 +149,7 @@ struct DecodeDev {
   int64_t off_kw, off_vw, off_ks, off_vs;
   int32_t row_kw, row_vw;
   int32_t n_seqs, hkv, hq, dim, kbits, vbits, pages_per_chunk, n_chunks, G;
+  int32_t gen_tt, gen_stage;  // generic path: tokens per staged tile, bytes per stage
   const float* q_rot;
   const __half* q_h;
   const float* kcent;
@@ -1207,9 +1208,16 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid
 
 // ---------------------------------------------------------------------------
 // Generic path: any bit width, head_dim = 32*KPL, GS query heads per CTA,
-// chunks of pages_per_chunk pages; partial slot = chunk.
+// chunks of pages_per_chunk pages; partial slot = chunk. Each warp walks one
+// page at a time in tiles of gen_tt tokens (16 or 32), staged into shared
+// memory by a per-warp cp.async double buffer: K words, V words, sigma_K,
+// sigma_V of the tile are contiguous in the page, so a tile is three or four
+// flat 16-byte copies. Lane l owns dims l + 32k: its word index and bit
+// shift per dim are fixed for the kernel. Softmax uses the lazy rescale of
+// the fast path (the running max moves only when a score exceeds it by more
+// than kTau).
 // ---------------------------------------------------------------------------
-template <int KPL, int GS>
+template <int KPL, int GS, bool QJL>
 __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ DecodeDev a) {
   extern __shared__ __align__(16) float gsm[];
   constexpr int D = 32 * KPL;
@@ -1219,6 +1227,8 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
   float* kc = gsm;           // [256]
   float* vc = gsm + 256;     // [256]
   float* wpart = gsm + 512;  // [nw][GS][PS]
+  uint8_t* stage0 = reinterpret_cast<uint8_t*>(gsm + 512 + nw * GS * PS) + (size_t)warp * 2 * a.gen_stage;
+  const uint32_t st_s = (uint32_t)__cvta_generic_to_shared(stage0);
   for (int i = threadIdx.x; i < (1 << a.kbits); i += blockDim.x) kc[i] = a.kcent[i];
   for (int i = threadIdx.x; i < (1 << a.vbits); i += blockDim.x) vc[i] = a.vcent[i];
   __syncthreads();
@@ -1226,6 +1236,18 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
   const int kcpw = 64 / a.kbits, vcpw = 64 / a.vbits;
   const uint64_t kmask = (1ull << a.kbits) - 1, vmask = (1ull << a.vbits) - 1;
   const int64_t total = (int64_t)a.n_seqs * a.hkv * groups * a.n_chunks;
+  const int TT = a.gen_tt;
+  const int kw_row = a.row_kw / 8, vw_row = a.row_vw / 8;  // u64 words per token row
+  // stage: [TT][kw_row] K words | [TT][vw_row] V words | [TT] sigma_K | [TT] sigma_V
+  const int kbytes = TT * a.row_kw, vbytes = TT * a.row_vw;
+  // per dim: K word | K shift << 8 | V word << 16 | V shift << 24 (each < 256)
+  uint32_t idx[KPL];
+#pragma unroll
+  for (int k = 0; k < KPL; ++k) {
+    const int d = lane + 32 * k;
+    idx[k] = (uint32_t)(d / kcpw) | ((uint32_t)((d % kcpw) * a.kbits) << 8) | ((uint32_t)(d / vcpw) << 16) |
+             ((uint32_t)((d % vcpw) * a.vbits) << 24);
+  }
 
   for (int64_t item = blockIdx.x; item < total; item += gridDim.x) {
     const int chunk = (int)(item % a.n_chunks);
@@ -1250,12 +1272,13 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
       }
     }
     // QJL: projection rows i = lane + 32 r of (Phi q) * qscale per head
-    const bool qjl = a.q_proj != nullptr;
-    float pq[GS][kMaxQjlDecode / 32];
+    constexpr bool qjl = QJL;
+    constexpr int MQ = QJL ? kMaxQjlDecode / 32 : 1;
+    float pq[GS][MQ];
 #pragma unroll
     for (int g = 0; g < GS; ++g)
 #pragma unroll
-      for (int r = 0; r < kMaxQjlDecode / 32; ++r) {
+      for (int r = 0; r < MQ; ++r) {
         const int i = lane + 32 * r;
         pq[g][r] = (qjl && i < a.qjl_m) ? a.q_proj[((int64_t)s * a.hq + qh0 + g) * a.qjl_m + i] : 0.f;
       }
@@ -1264,74 +1287,107 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
       const int64_t tok0 = page_idx * kPageTokens;
       if (tok0 >= n_valid) break;
       const uint8_t* page = reinterpret_cast<const uint8_t*>(trow[page_idx]);
-      const uint64_t* kw = reinterpret_cast<const uint64_t*>(page + a.off_kw + (int64_t)kvh * kPageTokens * a.row_kw);
-      const uint64_t* vw = reinterpret_cast<const uint64_t*>(page + a.off_vw + (int64_t)kvh * kPageTokens * a.row_vw);
-      const float* ks = reinterpret_cast<const float*>(page + a.off_ks) + (int64_t)kvh * kPageTokens;
-      const float* vs = reinterpret_cast<const float*>(page + a.off_vs) + (int64_t)kvh * kPageTokens;
-      const int kw_row = a.row_kw / 8, vw_row = a.row_vw / 8;
+      const uint8_t* kg = page + a.off_kw + (int64_t)kvh * kPageTokens * a.row_kw;
+      const uint8_t* vg = page + a.off_vw + (int64_t)kvh * kPageTokens * a.row_vw;
+      const uint8_t* ksg = page + a.off_ks + (int64_t)kvh * kPageTokens * 4;
+      const uint8_t* vsg = page + a.off_vs + (int64_t)kvh * kPageTokens * 4;
       const uint64_t* kq = qjl ? reinterpret_cast<const uint64_t*>(page + a.off_kq + (int64_t)kvh * kPageTokens * a.row_kq)
                                : nullptr;
       const float* kr = qjl ? reinterpret_cast<const float*>(page + a.off_kr) + (int64_t)kvh * kPageTokens : nullptr;
       const int nt = (int)(n_valid - tok0 < kPageTokens ? n_valid - tok0 : kPageTokens);
-      for (int tt = 0; tt < nt; ++tt) {
-        float part[GS];
-#pragma unroll
-        for (int g = 0; g < GS; ++g) part[g] = 0.f;
-        float vv[KPL];
-#pragma unroll
-        for (int k = 0; k < KPL; ++k) {
-          const int d = lane + 32 * k;
-          const uint64_t wk = kw[(int64_t)tt * kw_row + d / kcpw];
-          const float c = kc[(wk >> ((d % kcpw) * a.kbits)) & kmask];
-#pragma unroll
-          for (int g = 0; g < GS; ++g) part[g] = fmaf(q[g][k], c, part[g]);
-          const uint64_t wv = vw[(int64_t)tt * vw_row + d / vcpw];
-          vv[k] = vc[(wv >> ((d % vcpw) * a.vbits)) & vmask];
+      const int ntiles = (nt + TT - 1) / TT;
+      // whole tiles are copied: rows past n_valid exist in the page and are not used
+      auto issue = [&](int tl, int stg) {
+        const uint32_t dst = st_s + stg * a.gen_stage;
+        const int r0 = tl * TT;
+        for (int c = lane; c * 16 < kbytes; c += 32) cp_async16(dst + c * 16, kg + (int64_t)r0 * a.row_kw + c * 16);
+        for (int c = lane; c * 16 < vbytes; c += 32)
+          cp_async16(dst + kbytes + c * 16, vg + (int64_t)r0 * a.row_vw + c * 16);
+        for (int c = lane; c * 16 < TT * 8; c += 32) {  // sigma_K then sigma_V, TT * 4 bytes each
+          const bool kside = c * 16 < TT * 4;
+          const int off = kside ? c * 16 : c * 16 - TT * 4;
+          cp_async16(dst + kbytes + vbytes + c * 16, (kside ? ksg : vsg) + (int64_t)r0 * 4 + off);
         }
-#pragma unroll
-        for (int g = 0; g < GS; ++g) {
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+        cp_commit();
+      };
+      issue(0, 0);
+      for (int tl = 0; tl < ntiles; ++tl) {
+        if (tl + 1 < ntiles) {
+          issue(tl + 1, (tl + 1) & 1);
+          cp_wait_one();
+        } else {
+          cp_wait_all();
         }
-        const float ksg = ks[tt], vsg = vs[tt];
-        // QJL stage 2 (compressor.rs:148-155, qjl.rs:86-119):
-        // ||r|| sqrt(pi/2)/sqrt(m) * sum_i sign_i (Phi q)_i, 0 when ||r|| < 1e-10
-        float cr[GS];
+        __syncwarp();
+        const uint8_t* st = stage0 + (tl & 1) * a.gen_stage;
+        const uint64_t* kw = reinterpret_cast<const uint64_t*>(st);
+        const uint64_t* vw = reinterpret_cast<const uint64_t*>(st + kbytes);
+        const float* ks = reinterpret_cast<const float*>(st + kbytes + vbytes);
+        const float* vs = ks + TT;
+        const int cnt = min(TT, nt - tl * TT);
+        for (int tt = 0; tt < cnt; ++tt) {
+          float part[GS];
 #pragma unroll
-        for (int g = 0; g < GS; ++g) cr[g] = 0.f;
-        if (qjl) {
-          const uint64_t* sw = kq + (int64_t)tt * (a.row_kq / 8);
+          for (int g = 0; g < GS; ++g) part[g] = 0.f;
+          float vv[KPL];
 #pragma unroll
-          for (int r = 0; r < kMaxQjlDecode / 32; ++r) {
-            const int i = lane + 32 * r;
-            if (i < a.qjl_m) {
-              const bool pos = (sw[i >> 6] >> (i & 63)) & 1ull;
+          for (int k = 0; k < KPL; ++k) {
+            const uint64_t wk = kw[tt * kw_row + (idx[k] & 0xFF)];
+            const float c = kc[(wk >> ((idx[k] >> 8) & 0xFF)) & kmask];
 #pragma unroll
-              for (int g = 0; g < GS; ++g) cr[g] += pos ? pq[g][r] : -pq[g][r];
+            for (int g = 0; g < GS; ++g) part[g] = fmaf(q[g][k], c, part[g]);
+            const uint64_t wv = vw[tt * vw_row + ((idx[k] >> 16) & 0xFF)];
+            vv[k] = vc[(wv >> (idx[k] >> 24)) & vmask];
+          }
+          // QJL stage 2 (compressor.rs:148-155, qjl.rs:86-119):
+          // ||r|| sqrt(pi/2)/sqrt(m) * sum_i sign_i (Phi q)_i, 0 when ||r|| < 1e-10
+          float cr[GS];
+#pragma unroll
+          for (int g = 0; g < GS; ++g) cr[g] = 0.f;
+          if constexpr (qjl) {
+            const uint64_t* sw = kq + (int64_t)(tl * TT + tt) * (a.row_kq / 8);
+#pragma unroll
+            for (int r = 0; r < MQ; ++r) {
+              const int i = lane + 32 * r;
+              if (i < a.qjl_m) {
+                const bool pos = (sw[i >> 6] >> (i & 63)) & 1ull;
+#pragma unroll
+                for (int g = 0; g < GS; ++g) cr[g] += pos ? pq[g][r] : -pq[g][r];
+              }
             }
           }
 #pragma unroll
           for (int g = 0; g < GS; ++g) {
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) cr[g] += __shfl_xor_sync(0xffffffffu, cr[g], off);
+            for (int off = 16; off > 0; off >>= 1) {
+              part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+              if (qjl) cr[g] += __shfl_xor_sync(0xffffffffu, cr[g], off);
+            }
           }
-          const float rn = kr[tt];
-          const float rho = rn < 1e-10f ? 0.f : rn * a.qjl_c;
+          float rho = 0.f;
+          if (qjl) {
+            const float rn = kr[tl * TT + tt];
+            rho = rn < 1e-10f ? 0.f : rn * a.qjl_c;
+          }
+          const float ksv = ks[tt], vsv = vs[tt];
 #pragma unroll
-          for (int g = 0; g < GS; ++g) cr[g] *= rho;
+          for (int g = 0; g < GS; ++g) {
+            const float sc = fmaf(part[g], ksv, cr[g] * rho);
+            if (sc > m[g] + kTau) {  // uniform over the warp
+              const float al = ex2(m[g] - sc);
+              l[g] *= al;
+#pragma unroll
+              for (int k = 0; k < KPL; ++k) o[g][k] *= al;
+              m[g] = sc;
+            }
+            const float p = ex2(sc - m[g]);
+            l[g] += p;
+            const float pw2 = p * vsv;
+#pragma unroll
+            for (int k = 0; k < KPL; ++k) o[g][k] = fmaf(pw2, vv[k], o[g][k]);
+          }
         }
-#pragma unroll
-        for (int g = 0; g < GS; ++g) {
-          const float sc = fmaf(part[g], ksg, cr[g]);
-          const float mn = fmaxf(m[g], sc);
-          const float al = exp2f(m[g] - mn);
-          const float p = exp2f(sc - mn);
-          l[g] = l[g] * al + p;
-          const float pw2 = p * vsg;
-#pragma unroll
-          for (int k = 0; k < KPL; ++k) o[g][k] = fmaf(pw2, vv[k], o[g][k] * al);
-          m[g] = mn;
-        }
+        __syncwarp();  // the stage is refilled by the next issue
       }
     }
     float* wp = wpart + warp * GS * PS;
@@ -1514,23 +1570,34 @@ void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
   LC_CUDA(cudaGetLastError());
 }
 
-template <int KPL, int GS>
-void launch_generic_t(const DecodeDev& d, cudaStream_t s) {
+template <int KPL, int GS, bool QJL>
+void launch_generic_q(DecodeDev d, cudaStream_t s) {
   const int nw = 4;
-  const size_t smem = (512 + (size_t)nw * GS * (32 * KPL + 2)) * sizeof(float);
+  // 32-token tiles where a token's K + V words fit 256 bytes, else 16
+  d.gen_tt = d.row_kw + d.row_vw <= 256 ? 32 : 16;
+  d.gen_stage = d.gen_tt * (d.row_kw + d.row_vw) + 2 * d.gen_tt * 4;
+  const size_t smem = (512 + (size_t)nw * GS * (32 * KPL + 2)) * sizeof(float) + (size_t)nw * 2 * d.gen_stage;
   static bool attr = false;
   if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_decode_generic<KPL, GS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    LC_CUDA(cudaFuncSetAttribute(k_decode_generic<KPL, GS, QJL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 227 * 1024));
     attr = true;
   }
+  LC_REQUIRE(smem <= 227 * 1024, LC_ERR_INVALID, "decode: head_dim / bit widths too large for the generic path");
   int per_sm = 0;
-  LC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_generic<KPL, GS>, nw * 32, smem));
+  LC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_generic<KPL, GS, QJL>, nw * 32, smem));
   if (per_sm < 1) per_sm = 1;
   const int64_t total = (int64_t)d.n_seqs * d.hkv * (d.G / GS) * d.n_chunks;
   int64_t grid = (int64_t)num_sms() * per_sm;
   if (grid > total) grid = total;
-  k_decode_generic<KPL, GS><<<(unsigned)grid, nw * 32, smem, s>>>(d);
+  k_decode_generic<KPL, GS, QJL><<<(unsigned)grid, nw * 32, smem, s>>>(d);
   LC_CUDA(cudaGetLastError());
+}
+
+template <int KPL, int GS>
+void launch_generic_t(const DecodeDev& d, cudaStream_t s) {
+  if (d.q_proj) return launch_generic_q<KPL, GS, true>(d, s);
+  return launch_generic_q<KPL, GS, false>(d, s);
 }
 
 template <int KPL>
