@@ -230,7 +230,6 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_two() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 // Walks (sequence, kv head, tile) in flat order; nt = tiles per kv head of b.
@@ -726,9 +725,12 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     }
   }
 
-  // the first two tiles, both stages
+  // The first tiles. Fused: one now, the second after the prologue; the
+  // query rows and R wait behind this burst of every warp's copies, and a
+  // tile takes longer to compute than the next one takes to arrive.
+  constexpr int kFirstTiles = FUSED ? 1 : 2;
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
+  for (int k = 0; k < kFirstTiles; ++k) {
     if (begin + k < end) {
       pr.issue(a, st0 + k * kStageBytes, lane);
       step(a, pr.w);
@@ -753,7 +755,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       if (r < nb * 8) qs[rot_q ? rot_swz(r, j) : k] = qv[it] * a.qscale;
     }
     if (rot_q) {
-      cp_wait_two();  // R has landed; the two tiles may still be in flight
+      cp_wait_one();  // R has landed; the first tile may still be in flight
       __syncthreads();
       auto rrow = [&](int i) { return static_cast<const uint8_t*>(lut + i * 512); };
       float d[2][4];
@@ -776,6 +778,13 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   build_lut(lut, cl);
   __syncthreads();
   if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
+  if constexpr (FUSED) {  // the second tile
+    if (begin + 1 < end) {
+      pr.issue(a, st0 + kStageBytes, lane);
+      step(a, pr.w);
+    }
+    cp_commit();
+  }
 
   int x = begin;
   while (x < end) {
