@@ -281,9 +281,16 @@ __device__ __forceinline__ void stage16(void* dst, const void* src, int n16) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d + k * 16), "l"(g + (size_t)k * 16) : "memory");
 }
 
+// Programmatic dependent launch (sm_90+): see launch_warp_append. Both are
+// no-ops for a kernel launched without the programmatic-serialization
+// attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 template <int R, bool TAB>  // R = head_dim / 32
 __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_constant__ AppendDev a) {
   constexpr int D = 32 * R;
+  pdl_launch_dependents();
   extern __shared__ __align__(16) uint8_t smem[];
   const int side = blockIdx.y;
   const CodecDev& c = a.codec[side];
@@ -322,6 +329,9 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
       asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
     }
   }
+  // the tables above are the codecs' constants; the inputs and the pages
+  // written below may belong to the previous kernel of the stream
+  pdl_wait();
   __syncthreads();
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const int64_t v = (int64_t)blockIdx.x * kWarpVecs + warp;
@@ -451,10 +461,20 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
     LC_CUDA(cudaFuncSetAttribute(k_append_warp<R, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr = true;
   }
-  const dim3 grid((unsigned)((n_vec + kWarpVecs - 1) / kWarpVecs), 2);
-  if (tab) k_append_warp<R, true><<<grid, kWarpVecs * 32, smem, s>>>(d);
-  else k_append_warp<R, false><<<grid, kWarpVecs * 32, smem, s>>>(d);
-  LC_CUDA(cudaGetLastError());
+  // Programmatic serialization: the table staging overlaps the previous
+  // kernel's tail (the kernel waits for it before touching inputs or pages).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((n_vec + kWarpVecs - 1) / kWarpVecs), 2);
+  cfg.blockDim = dim3(kWarpVecs * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (tab) LC_CUDA(cudaLaunchKernelEx(&cfg, k_append_warp<R, true>, d));
+  else LC_CUDA(cudaLaunchKernelEx(&cfg, k_append_warp<R, false>, d));
 }
 
 }  // namespace

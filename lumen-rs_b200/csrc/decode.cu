@@ -230,6 +230,14 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+// Programmatic dependent launch (sm_90+). launch_dependents lets the next
+// kernel of the stream be scheduled while this one runs; its CTAs take SMs
+// as this grid's CTAs exit. pdl_wait returns once the previous kernel of the
+// stream has completed and its writes are visible. Both are no-ops for a
+// kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 // Walks (sequence, kv head, tile) in flat order; nt = tiles per kv head of b.
@@ -658,6 +666,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
   const uint32_t vl = pair_vlane(g, t);
+  if constexpr (FUSED) pdl_launch_dependents();
   // tile indices fit in 32 bits (plan_decode: total_tiles < 2^31)
   const int w = blockIdx.x * kFlatWarps + warp;
   const int pw = (int)a.per_warp;
@@ -695,9 +704,13 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   }
   if (begin < end) {
     pr.w = locate_warp(a, begin, lane);
-    pr.lookup(a);
+    pr.lookup(a);  // the block table is written by host copies only
   }
   Walk cw = pr.w;
+  // fused: everything above reads constants (codec tables, launch
+  // parameters, the block table); the queries, the cache pages, the arrival
+  // counters and the partials come after the previous kernel has completed
+  if constexpr (FUSED) pdl_wait();
 
   // fused: this CTA's segments and their query rows, loaded before the
   // tiles are issued so they do not queue behind the tile traffic
@@ -1575,8 +1588,23 @@ void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
     LC_CUDA(cudaFuncSetAttribute(k_decode_pair<G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  k_decode_pair<G, FUSED><<<(unsigned)grid, kFlatWarps * 32, smem, s>>>(d);
-  LC_CUDA(cudaGetLastError());
+  if constexpr (FUSED) {
+    // programmatic serialization: the prologue overlaps the previous kernel's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kFlatWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    LC_CUDA(cudaLaunchKernelEx(&cfg, k_decode_pair<G, FUSED>, d));
+  } else {
+    k_decode_pair<G, FUSED><<<(unsigned)grid, kFlatWarps * 32, smem, s>>>(d);
+    LC_CUDA(cudaGetLastError());
+  }
 }
 
 template <int KPL, int GS, bool QJL>
