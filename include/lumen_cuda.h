@@ -270,6 +270,20 @@ int lc_decode_attn(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t
                    const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags,
                    void* out, int32_t out_dtype, void* stream);
 
+/* Masked (causal) attention of a prefill chunk over the compressed cache:
+ * the tq layers' prefill branch of gemma4_moe.rs:4636-4660 (queries against
+ * the dequantized codes, causal mask, scale) computed on the codes. The
+ * chunk's K/V must already be appended: q [n_q_tokens, n_q_heads, head_dim]
+ * holds the queries of the last n_q_tokens tokens of (seq, layer)'s view, and
+ * query i attends to the first view_len - n_q_tokens + i + 1 tokens. out has
+ * q's shape. Flags as lc_decode_attn. LC_ERR_STATE on a sliding layer whose
+ * ring has wrapped (its view is not in token order); LC_ERR_INVALID if
+ * n_q_tokens exceeds the view. Each query reads its whole prefix, so the
+ * cost grows as n_q_tokens x prefix. */
+int lc_prefill_attn(lc_cache* cache, int32_t layer, int32_t seq, const void* q, int32_t q_dtype,
+                    int32_t n_q_tokens, int32_t n_q_heads, float scale, uint32_t flags, void* out,
+                    int32_t out_dtype, void* stream);
+
 /* Bytes of the fixed device scratch lc_decode_attn_noalloc uses, per device. */
 #define LC_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 

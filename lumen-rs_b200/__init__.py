@@ -48,7 +48,7 @@ ABI_SYMBOLS = [
     "lc_codec_tables", "lc_codec_shape", "lc_codec_free", "lc_packed_words", "lc_cache_create",
     "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_keys_qjl", "lc_attend_values", "lc_seq_len", "lc_clear",
     "lc_truncate", "lc_append", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
-    "lc_decode_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
+    "lc_decode_attn", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
     "lc_ring_deep_clone", "lc_ring_destroy", "lc_version", "lc_save_lkv2", "lc_load_lkv2", "lc_lkv2_info",
@@ -124,6 +124,7 @@ def lib():
         "lc_lkv2_info": (C.c_int, [C.c_char_p, C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_uint64)]),
         "lc_decode_attn": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_noalloc": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
+        "lc_prefill_attn": (C.c_int, [vp, i32, i32, vp, i32, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_partials": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, vp, vp, vp]),
         "lc_merge_partials": (C.c_int, [vp, i32, i32, vp, vp, vp, u32, vp, i32, vp]),
         "lc_ring_create": (C.c_int, [i32, i64, i64, i32, vp, i32, pp]),
@@ -405,6 +406,19 @@ class CudaKvCache:
         stream = _auto_stream(stream, q, out)
         _check(lib().lc_decode_attn(self._h, layer, len(ids), _ptr(ids), _ptr(q), _dtype_code(q), n_q_heads,
                                     scale, flags, _ptr(out), out_dtype, stream))
+        return out
+
+    def prefill_attn(self, layer: int, seq: int, q, n_q_heads: int, scale: float = 1.0, flags: int = 0, out=None,
+                     out_dtype: int = LC_F32, stream=None):
+        """Causal attention of the last len(q) tokens of (seq, layer) over its
+        view; q [n_q_tokens, n_q_heads, head_dim]."""
+        n_tok = q.shape[0]
+        if out is None:
+            out = np.empty((n_tok, n_q_heads, self.head_dim), np.float32)
+            out_dtype = LC_F32
+        stream = _auto_stream(stream, q, out)
+        _check(lib().lc_prefill_attn(self._h, layer, seq, _ptr(q), _dtype_code(q), n_tok, n_q_heads, scale, flags,
+                                     _ptr(out), out_dtype, stream))
         return out
 
     def decode_partials(self, layer: int, seq_ids, q, n_q_heads: int, scale: float = 1.0, flags: int = 0,

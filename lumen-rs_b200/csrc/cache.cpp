@@ -1015,10 +1015,19 @@ struct DecodeRun {
 
 // fused_out: device output of a full attention call (lc_decode_attn), which
 // the one-launch kernel writes when the plan allows; null for partials.
+// Prefill attention (lc_prefill_attn): the n_seqs "sequences" are the last
+// n_seqs tokens of sequence `seq`, query b attending to the first
+// view_len - n_seqs + b + 1 tokens (causal). They share the sequence's block
+// table row, so the split-K decode runs unchanged.
+struct PrefillView {
+  int32_t seq;
+};
+
 static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
                                int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s,
-                               void* fused_out = nullptr, int32_t out_dtype = LC_F32) {
-  LC_REQUIRE(c && seq_ids && q, LC_ERR_INVALID, "null argument");
+                               void* fused_out = nullptr, int32_t out_dtype = LC_F32,
+                               const PrefillView* prefill = nullptr) {
+  LC_REQUIRE(c && (seq_ids || prefill) && q, LC_ERR_INVALID, "null argument");
   LC_REQUIRE(n_seqs > 0, LC_ERR_INVALID, "n_seqs must be > 0");
   const int32_t hkv = c->cfg.n_kv_heads;
   LC_REQUIRE(n_q_heads > 0 && n_q_heads % hkv == 0, LC_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads");
@@ -1028,7 +1037,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   c->ops.stream = s;
   std::vector<int64_t> info((size_t)n_seqs * 2), lens(n_seqs);
   for (int32_t b = 0; b < n_seqs; ++b) {
-    const int32_t seq = seq_ids[b];
+    const int32_t seq = prefill ? prefill->seq : seq_ids[b];
     c->check(seq, layer);
     SeqLayer& sl = c->at(seq, layer);
     int64_t n = sl.ring.view_len;
@@ -1037,7 +1046,15 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
         LC_REQUIRE(hl == sl.head_len[0], LC_ERR_STATE, "heads of this layer hold different lengths");
       n = sl.head_len[0];
     }
-    c->sync_table(seq, layer, s);
+    if (prefill) {
+      // the view must be in token order: a ring that has wrapped holds its
+      // window in rotated order (the window mask would need the positions)
+      LC_REQUIRE(sl.head_len.empty() ? sl.ring.offset <= sl.ring.max_size : true, LC_ERR_STATE,
+                 "prefill attention over a ring that has wrapped is not supported");
+      LC_REQUIRE(n >= n_seqs, LC_ERR_INVALID, "prefill: more query tokens than the sequence holds");
+      n = n - n_seqs + b + 1;
+    }
+    if (!prefill || b == 0) c->sync_table(seq, layer, s);
     info[2 * b] = n;
     info[2 * b + 1] = (int64_t)layer * c->cfg.max_seqs + seq;
     lens[b] = n;
@@ -1163,39 +1180,56 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   return r;
 }
 
+// lc_decode_attn and lc_prefill_attn: decode, merge if the one-launch path
+// was not taken, copy a host output back.
+static void attn_call(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const PrefillView* prefill,
+                      const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, void* out,
+                      int32_t out_dtype, void* stream) {
+  LC_REQUIRE(out, LC_ERR_INVALID, "null out");
+  cudaStream_t s = c ? c->pick(stream) : nullptr;
+  LC_REQUIRE(c && n_q_heads > 0 && n_seqs > 0, LC_ERR_INVALID, "bad decode arguments");
+  LC_CUDA(cudaSetDevice(c->cfg.device));
+  const int32_t D = c->cfg.head_dim;
+  const int64_t rows = (int64_t)n_seqs * n_q_heads;
+  const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
+  const bool host_out = !is_device_ptr(out);
+  void* dout = out;
+  if (host_out) {
+    c->outbuf.ensure(obytes, s);
+    dout = c->outbuf.p;
+  }
+  const DecodeRun run =
+      decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, dout, out_dtype, prefill);
+  if (!run.fused) {
+    c->timed(c->t_other, s, [&] {
+      launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
+                   (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr,
+                   run.oscale, s);
+    });
+    ++c->launches;
+  }
+  if (host_out) {
+    LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
+    LC_CUDA(cudaStreamSynchronize(s));
+  } else if (run.host_q) {
+    LC_CUDA(cudaEventSynchronize(c->ev_copy));
+  }
+}
+
+int lc_prefill_attn(lc_cache* c, int32_t layer, int32_t seq, const void* q, int32_t q_dtype, int32_t n_q_tokens,
+                    int32_t n_q_heads, float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    const PrefillView pv{seq};
+    attn_call(c, layer, n_q_tokens, nullptr, &pv, q, q_dtype, n_q_heads, scale, flags, out, out_dtype, stream);
+  });
+}
+
 int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
                    int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, void* out, int32_t out_dtype,
                    void* stream) {
   return abi_guard([&] {
-    LC_REQUIRE(out, LC_ERR_INVALID, "null out");
-    cudaStream_t s = c ? c->pick(stream) : nullptr;
-    LC_REQUIRE(c && n_q_heads > 0 && n_seqs > 0, LC_ERR_INVALID, "bad decode arguments");
-    LC_CUDA(cudaSetDevice(c->cfg.device));
-    const int32_t D = c->cfg.head_dim;
-    const int64_t rows = (int64_t)n_seqs * n_q_heads;
-    const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
-    const bool host_out = !is_device_ptr(out);
-    void* dout = out;
-    if (host_out) {
-      c->outbuf.ensure(obytes, s);
-      dout = c->outbuf.p;
-    }
-    const DecodeRun run =
-        decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, dout, out_dtype);
-    if (!run.fused) {
-      c->timed(c->t_other, s, [&] {
-        launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
-                     (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr,
-                     run.oscale, s);
-      });
-      ++c->launches;
-    }
-    if (host_out) {
-      LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
-      LC_CUDA(cudaStreamSynchronize(s));
-    } else if (run.host_q) {
-      LC_CUDA(cudaEventSynchronize(c->ev_copy));
-    }
+    attn_call(c, layer, n_seqs, seq_ids, nullptr, q, q_dtype, n_q_heads, scale, flags, out, out_dtype, stream);
   });
 }
 

@@ -548,6 +548,24 @@ void orc_sc_attend(const orc_simple_cache* s, int layer, int head, const float* 
     orc_sc_attend_ex(s, layer, head, query, scale, 0, out);
 }
 
+// Causal prefill: attention over the first n_keys stored tokens only
+// (softmax over those scores; the weights of later tokens are zero, which
+// attend_values skips).
+void orc_sc_attend_prefix(const orc_simple_cache* s, int layer, int head, const float* query, float scale,
+                          int64_t n_keys, float* out) {
+    const orc_cv_list& l = s->keys[(size_t)layer * s->n_heads + head];
+    if (n_keys > l.n) n_keys = l.n;
+    std::vector<float> sc(l.n > 0 ? l.n : 1), w(l.n > 0 ? l.n : 1, 0.0f);
+    if (n_keys <= 0) { for (int i = 0; i < s->dim; ++i) out[i] = 0.0f; return; }
+    orc_sc_attend_keys(s, layer, head, query, sc.data());
+    double mx = -INFINITY;
+    for (int64_t t = 0; t < n_keys; ++t) mx = std::max(mx, (double)sc[t] * (double)scale);
+    double sum = 0.0;
+    for (int64_t t = 0; t < n_keys; ++t) sum += std::exp((double)sc[t] * (double)scale - mx);
+    for (int64_t t = 0; t < n_keys; ++t) w[t] = (float)(std::exp((double)sc[t] * (double)scale - mx) / sum);
+    orc_sc_attend_values(s, layer, head, w.data(), out);
+}
+
 // ---------------------------------------------------------------------------
 // FNV-1a (golden_tests.rs:73-84), for the ring-digest model.
 // ---------------------------------------------------------------------------

@@ -87,6 +87,7 @@ def lib():
         L.orc_sc_attend_keys.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend_keys_qjl.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend_ex.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int, _f32p]
+        L.orc_sc_attend_prefix.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int64, _f32p]
         L.orc_sc_attend_values.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, _f32p]
         L.orc_sc_clear.argtypes = [C.c_void_p]
@@ -308,6 +309,13 @@ class SimpleCache:
     def attend_values(self, layer, head, w):
         out = np.empty(self.dim, np.float32)
         lib().orc_sc_attend_values(self._h, layer, head, np.ascontiguousarray(w, np.float32), out)
+        return out
+
+    def attend_prefix(self, layer, head, q, scale, n_keys):
+        """Attention over the first n_keys stored tokens (causal prefill)."""
+        out = np.empty(self.dim, np.float32)
+        lib().orc_sc_attend_prefix(self._h, layer, head, np.ascontiguousarray(q, np.float32), float(scale),
+                                   int(n_keys), out)
         return out
 
     def attend(self, layer, head, q, scale=1.0, qjl=False):
