@@ -175,6 +175,19 @@ int lc_truncate(lc_cache* cache, int32_t seq, int32_t layer, int64_t n_keep);
 int lc_append(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
               const void* keys, const void* values, int32_t dtype, int64_t n_tokens, void* stream);
 
+/* lc_append with RoPE applied to the keys first: the prefill-side fusion of
+ * the TQ layers' encode (gemma4_moe.rs:4385-4432 rotates and quantizes K
+ * after RoPE), here taking the projection outputs before RoPE. Token t of
+ * sequence b sits at position p = (tokens the layer held before the call) +
+ * t; pair i < rope_dims / 2 turns by p * rope_base^(-2i / rope_dims)
+ * (angle in f64, cos and sin rounded to f32 on the host), pairs
+ * (i, i + rope_dims / 2) or, with traditional != 0, (2i, 2i + 1); dims past
+ * rope_dims are left as they are. Values are not rotated. The result equals
+ * lc_append of the keys with that RoPE applied in f32. */
+int lc_append_rope(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+                   const void* keys, const void* values, int32_t dtype, int64_t n_tokens, int32_t rope_dims,
+                   double rope_base, int32_t traditional, void* stream);
+
 /* NativeRotatingKvCacheTurboQuant::truncate_to (native_cache.rs:1728-1746
  * -> ring_truncate :304-335): LC_ERR_REFUSED if target > offset or the ring
  * has rotated (offset > max_size). */

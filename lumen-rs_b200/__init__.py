@@ -47,7 +47,7 @@ ABI_SYMBOLS = [
     "lc_last_error", "lc_codec_new", "lc_codec_from_files", "lc_codec_from_tables", "lc_codec_save",
     "lc_codec_tables", "lc_codec_shape", "lc_codec_free", "lc_packed_words", "lc_cache_create",
     "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_keys_qjl", "lc_attend_values", "lc_seq_len", "lc_clear",
-    "lc_truncate", "lc_append", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
+    "lc_truncate", "lc_append", "lc_append_rope", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
     "lc_decode_attn", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
@@ -114,6 +114,7 @@ def lib():
         "lc_clear": (C.c_int, [vp]),
         "lc_truncate": (C.c_int, [vp, i32, i32, i64]),
         "lc_append": (C.c_int, [vp, i32, i32, vp, vp, vp, i32, i64, vp]),
+        "lc_append_rope": (C.c_int, [vp, i32, i32, vp, vp, vp, i32, i64, i32, C.c_double, i32, vp]),
         "lc_truncate_to": (C.c_int, [vp, i32, i32, i64]),
         "lc_fork": (C.c_int, [vp, i32, i32, i64]),
         "lc_release": (C.c_int, [vp, i32]),
@@ -345,6 +346,16 @@ class CudaKvCache:
         stream = _auto_stream(stream, keys, values)
         _check(lib().lc_append(self._h, layer, len(ids), _ptr(ids), _ptr(keys), _ptr(values), _dtype_code(keys),
                                n_tok, stream))
+
+    def append_rope(self, layer: int, seq_ids, keys, values, rope_dims: int, rope_base: float = 10000.0,
+                    traditional: bool = False, stream=None):
+        """append() with RoPE applied to the keys first (positions continue
+        each sequence's layer)."""
+        ids = np.ascontiguousarray(seq_ids, np.int32)
+        n_tok = keys.shape[2]
+        stream = _auto_stream(stream, keys, values)
+        _check(lib().lc_append_rope(self._h, layer, len(ids), _ptr(ids), _ptr(keys), _ptr(values), _dtype_code(keys),
+                                    n_tok, rope_dims, rope_base, 1 if traditional else 0, stream))
 
     def truncate_to(self, seq: int, layer: int, target: int):
         _check(lib().lc_truncate_to(self._h, seq, layer, target))

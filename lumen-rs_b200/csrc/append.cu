@@ -48,12 +48,28 @@ struct AppendDev {
   int64_t off[kMaxRoles];
   int64_t row[kMaxRoles];
   int32_t role_words[2], role_sigma[2], role_qjl[2], role_rnorm[2];
+  // RoPE on the K side (lc_append_rope), see AppendArgs
+  const float* rope_cs;
+  int32_t rope_half, rope_traditional;
   // small calls (decode steps): destinations in the launch parameters
   uint64_t ipage[kAppendInline];
   int32_t irow[kAppendInline];
   __device__ __forceinline__ uint64_t page_of(int64_t slot) const { return dst_page ? dst_page[slot] : ipage[slot]; }
   __device__ __forceinline__ int32_t row_of(int64_t slot) const { return dst_page ? dst_row[slot] : irow[slot]; }
 };
+
+// RoPE pair i of vector slot `slot` (sequence s, token t: slot = s * n_tok + t)
+// in place: (x0, x1) -> (x0 c - x1 s, x0 s + x1 c), f32 round-to-nearest ops
+// in that order; pairs (i, i + half) or, traditional, (2i, 2i + 1).
+__device__ __forceinline__ void rope_pair(float* x, const AppendDev& a, int64_t slot, int i) {
+  const int i0 = a.rope_traditional ? 2 * i : i;
+  const int i1 = a.rope_traditional ? 2 * i + 1 : i + a.rope_half;
+  const float* e = a.rope_cs + (slot * a.rope_half + i) * 2;
+  const float c = e[0], sn = e[1];
+  const float x0 = x[i0], x1 = x[i1];
+  x[i0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+  x[i1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+}
 
 __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) {
   if (dtype == LC_F32) return reinterpret_cast<const float*>(p)[i];
@@ -127,6 +143,15 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
     // ---- load the batch (input layout [n_seqs][h_in][n_tok][D]) ----
     for (int v = 0; v < kNB; ++v) xs[v * D + i] = v < nb ? load_elem(src, a.dtype, (v0 + v) * D + i) : 0.0f;
     __syncthreads();
+    if (side == 0 && a.rope_cs) {  // thread i rotates pair i of every vector
+      if (i < a.rope_half)
+        for (int v = 0; v < nb; ++v) {
+          const int64_t vi = v0 + v;  // (s, hl, t) over [n_seqs][h_in][n_tok]
+          const int64_t slot = (vi / ((int64_t)a.h_in * a.n_tok)) * a.n_tok + vi % a.n_tok;
+          rope_pair(xs + v * D, a, slot, i);
+        }
+      __syncthreads();
+    }
 
     // ---- rotated[i] = sum_j R[i][j] * x[j] (rotation.rs:91-99) ----
     float acc[kNB];
@@ -340,6 +365,11 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
 #pragma unroll
   for (int r = 0; r < R; ++r) x[lane + 32 * r] = load_elem(src, a.dtype, v * D + lane + 32 * r);
   __syncwarp();
+  if (side == 0 && a.rope_cs) {
+    const int64_t slot = (v / ((int64_t)a.h_in * a.n_tok)) * a.n_tok + v % a.n_tok;
+    for (int i = lane; i < a.rope_half; i += 32) rope_pair(x, a, slot, i);
+    __syncwarp();
+  }
   // ---- rotated[i] = sum_j R[i][j] x[j] (rotation.rs:91-99) ----
   float acc[R];
 #pragma unroll
@@ -499,6 +529,9 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
   d.n_tok = a.n_tok;
   d.dst_page = a.dst_page;
   d.dst_row = a.dst_row;
+  d.rope_cs = a.rope_cs;
+  d.rope_half = a.rope_half;
+  d.rope_traditional = a.rope_traditional;
   if (!a.dst_page) {
     const int64_t slots = (int64_t)a.n_seqs * a.n_tok;
     LC_REQUIRE(a.h_page && a.h_row && slots <= kAppendInline, LC_ERR_STATE, "inline append metadata does not fit");

@@ -182,10 +182,23 @@ size_t dtype_size(int32_t dt) {
 }
 
 // Build the quantize-append for rows already prepared in the rings.
+// RoPE of lc_append_rope: positions, dims and table of one call.
+struct RopeArgs {
+  int32_t dims = 0;  // rotated leading dims (even, <= head_dim)
+  double base = 10000.0;
+  int32_t traditional = 0;
+  std::vector<float> cs;  // [n_seqs * n_tok][dims / 2][cos, sin]
+};
+
 void run_append(lc_cache* c, int32_t n_seqs, int32_t h_in, int32_t h_base, int64_t n_tok,
                 const std::vector<uint64_t>& dst_page, const std::vector<int32_t>& dst_row, const void* k,
-                const void* v, int32_t dtype, cudaStream_t s) {
+                const void* v, int32_t dtype, cudaStream_t s, const RopeArgs* rope = nullptr) {
   AppendArgs a;
+  if (rope) {
+    a.rope_cs = static_cast<const float*>(c->arena.put(rope->cs.data(), rope->cs.size() * sizeof(float), s));
+    a.rope_half = rope->dims / 2;
+    a.rope_traditional = rope->traditional;
+  }
   a.codec[0] = c->dk.view();
   a.codec[1] = c->dv.view();
   a.src[0] = k;
@@ -344,9 +357,9 @@ int lc_cache_timing(lc_cache* c, int32_t mode, double* decode_ms, uint64_t* deco
   });
 }
 
-int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
-              const void* values, int32_t dtype, int64_t n_tokens, void* stream) {
-  return abi_guard([&] {
+static void append_impl(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+                        const void* values, int32_t dtype, int64_t n_tokens, void* stream, RopeArgs* rope) {
+  {
     LC_REQUIRE(c && seq_ids && keys && values, LC_ERR_INVALID, "null argument");
     LC_REQUIRE(n_seqs > 0 && n_tokens > 0, LC_ERR_INVALID, "n_seqs and n_tokens must be > 0");
     LC_CUDA(cudaSetDevice(c->cfg.device));
@@ -376,6 +389,23 @@ int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids
     }
     LC_REQUIRE(need <= c->pool.free_pages(), LC_ERR_NOMEM,
                "page pool too small for this append (" + std::to_string(c->pool.free_pages()) + " pages free)");
+    if (rope) {
+      // position of token t of sequence b: tokens the layer held before the
+      // call + t; angle pos * base^(-2i/dims) in f64, cos and sin rounded to f32
+      const int32_t half = rope->dims / 2;
+      rope->cs.assign((size_t)n_seqs * n_tokens * half * 2, 0.f);
+      for (int32_t b = 0; b < n_seqs; ++b) {
+        const SeqLayer& sl = c->at(seq_ids[b], layer);
+        const int64_t pos0 = sl.head_len.empty() ? sl.ring.offset : sl.head_len[0];
+        for (int64_t t = 0; t < n_tokens; ++t)
+          for (int32_t i = 0; i < half; ++i) {
+            const double ang = (double)(pos0 + t) * std::pow(rope->base, -2.0 * i / rope->dims);
+            float* e = &rope->cs[(((size_t)b * n_tokens + t) * half + i) * 2];
+            e[0] = (float)std::cos(ang);
+            e[1] = (float)std::sin(ang);
+          }
+      }
+    }
     for (int32_t b = 0; b < n_seqs; ++b) {
       const int32_t seq = seq_ids[b];
       SeqLayer& sl = c->at(seq, layer);
@@ -394,9 +424,31 @@ int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids
     const void* dk = c->stage_in(keys, bytes, c->in_k, s, hk);
     const void* dv = c->stage_in(values, bytes, c->in_v, s, hv);
     if (hk || hv) LC_CUDA(cudaEventRecord(c->ev_copy, s));
-    run_append(c, n_seqs, H, 0, n_tokens, dst_page, dst_row, dk, dv, dtype, s);
+    run_append(c, n_seqs, H, 0, n_tokens, dst_page, dst_row, dk, dv, dtype, s, rope);
     if (hk || hv) LC_CUDA(cudaEventSynchronize(c->ev_copy));
     c->ops.stream = c->stream;
+  }
+}
+
+int lc_append(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+              const void* values, int32_t dtype, int64_t n_tokens, void* stream) {
+  return abi_guard(
+      [&] { append_impl(c, layer, n_seqs, seq_ids, keys, values, dtype, n_tokens, stream, nullptr); });
+}
+
+int lc_append_rope(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+                   const void* values, int32_t dtype, int64_t n_tokens, int32_t rope_dims, double rope_base,
+                   int32_t traditional, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c, LC_ERR_INVALID, "null cache");
+    LC_REQUIRE(rope_dims > 0 && rope_dims % 2 == 0 && rope_dims <= c->cfg.head_dim, LC_ERR_INVALID,
+               "rope_dims must be even and in [2, head_dim]");
+    LC_REQUIRE(rope_base > 0.0, LC_ERR_INVALID, "rope_base must be > 0");
+    RopeArgs r;
+    r.dims = rope_dims;
+    r.base = rope_base;
+    r.traditional = traditional ? 1 : 0;
+    append_impl(c, layer, n_seqs, seq_ids, keys, values, dtype, n_tokens, stream, &r);
   });
 }
 

@@ -50,6 +50,10 @@ struct AppendArgs {
   PageLayout layout;
   int32_t role_words[2] = {-1, -1}, role_sigma[2] = {-1, -1};
   int32_t role_qjl[2] = {-1, -1}, role_rnorm[2] = {-1, -1};
+  // RoPE on the K side before the rotation (lc_append_rope): per (sequence,
+  // token) slot rope_half (cos, sin) f32 pairs; null: no RoPE
+  const float* rope_cs = nullptr;
+  int32_t rope_half = 0, rope_traditional = 0;
 };
 // Appends of at most this many (sequence, token) slots pass their destinations
 // in the launch parameters.

@@ -567,6 +567,30 @@ void orc_sc_attend_prefix(const orc_simple_cache* s, int layer, int head, const 
 }
 
 // ---------------------------------------------------------------------------
+// RoPE as lc_append_rope applies it before the compressor: token t at
+// position pos0 + t, pair i < rot_dims / 2 turned by
+// pos * base^(-2i / rot_dims) (angle in f64, cos and sin rounded to f32),
+// pairs (i, i + rot_dims / 2) or, traditional, (2i, 2i + 1); f32 products
+// and one f32 sum / difference per output, in that order.
+// ---------------------------------------------------------------------------
+void orc_rope(float* x, int64_t n, int dim, int rot_dims, int64_t pos0, double base, int traditional) {
+    const int half = rot_dims / 2;
+    for (int64_t t = 0; t < n; ++t) {
+        float* v = x + t * dim;
+        const int64_t pos = pos0 + t;
+        for (int i = 0; i < half; ++i) {
+            const double ang = (double)pos * std::pow(base, -2.0 * i / rot_dims);
+            const float c = (float)std::cos(ang), s = (float)std::sin(ang);
+            const int i0 = traditional ? 2 * i : i, i1 = traditional ? 2 * i + 1 : i + half;
+            const float x0 = v[i0], x1 = v[i1];
+            const float a = x0 * c, b = x1 * s, p = x0 * s, q = x1 * c;
+            v[i0] = a - b;
+            v[i1] = p + q;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // FNV-1a (golden_tests.rs:73-84), for the ring-digest model.
 // ---------------------------------------------------------------------------
 uint64_t orc_fnv1a(uint64_t h, const uint8_t* p, int64_t n) {

@@ -88,6 +88,7 @@ def lib():
         L.orc_sc_attend_keys_qjl.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend_ex.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int, _f32p]
         L.orc_sc_attend_prefix.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int64, _f32p]
+        L.orc_rope.argtypes = [_f32p, C.c_int64, C.c_int, C.c_int, C.c_int64, C.c_double, C.c_int]
         L.orc_sc_attend_values.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, _f32p]
         L.orc_sc_clear.argtypes = [C.c_void_p]
@@ -195,6 +196,14 @@ def qjl_project_and_pack(P: np.ndarray, res: np.ndarray) -> np.ndarray:
     lib().orc_qjl_project_and_pack(np.ascontiguousarray(P, np.float32).ravel(), m, d,
                                    np.ascontiguousarray(res, np.float32), out)
     return out
+
+
+def rope(x: np.ndarray, rot_dims: int, pos0: int, base: float = 10000.0, traditional: bool = False) -> np.ndarray:
+    """RoPE of the rows of x [n, dim] at positions pos0.. (orc_rope)."""
+    y = np.ascontiguousarray(x, np.float32).copy()
+    n, dim = y.shape
+    lib().orc_rope(y.ravel(), n, dim, rot_dims, pos0, base, 1 if traditional else 0)
+    return y
 
 
 def qjl_estimate_correction(P: np.ndarray, q: np.ndarray, packed: np.ndarray, rnorm: float) -> float:
