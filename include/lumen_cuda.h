@@ -103,6 +103,10 @@ typedef struct lc_cache lc_cache;
 /* Store flags. */
 #define LC_STORE_K_QJL 1u /* keep the K stage-2 QJL bits + residual norm */
 #define LC_STORE_V_QJL 2u /* keep the V stage-2 QJL bits + residual norm */
+/* keep per-page key bounds for page-sparse decode (LC_SPARSE_PAGES): the
+ * elementwise min and max of the dequantized rotated keys of every full
+ * 64-token page, the PageDigest of native_cache.rs:350-365 over the codes */
+#define LC_STORE_DIGEST 4u
 
 typedef struct lc_cache_config {
   int32_t n_layers;
@@ -273,6 +277,17 @@ int lc_lkv2_info(const char* path, int64_t* n_layers, int64_t* n_records, uint64
  * query (with LC_Q_ROTATED: LC_ERR_INVALID). Not taken by
  * lc_decode_attn_noalloc (LC_ERR_INVALID). */
 #define LC_QJL_SCORES 4u
+/* Page-sparse decode (sdpa_page_sparse, native_attention.rs:217-329, on the
+ * codes): once a sequence holds 16384 keys or more (SPARSE_DECODE_MIN_KEYS),
+ * each (sequence, kv head) attends to the 64-token pages whose bound
+ * sum_d max(q'_d max_d, q'_d min_d), maxed over its query heads, is largest,
+ * plus the first page and the 4 most recent full pages and the undigested
+ * tail: max(pages / 8, 64) pages in all (sparse_keep_pages). q' is the
+ * rotated query; min and max come from the digest. Needs a cache created with
+ * LC_STORE_DIGEST (LC_ERR_STATE), a full (non-sliding) layer and the 4-bit,
+ * head_dim 128, GQA <= 4 geometry (LC_ERR_INVALID otherwise); not combined
+ * with LC_QJL_SCORES. Below 16384 keys the decode is dense. */
+#define LC_SPARSE_PAGES 8u
 
 /* Decode attention over the compressed cache, one query token per
  * sequence: out = softmax(scale * q K_dq^T) V_dq for every query head, with

@@ -35,6 +35,7 @@ struct SeqLayer {
   RingCore ring;
   std::vector<int64_t> head_len;  // non-empty: per-head lengths (KVCache::store on a full layer)
   bool dirty = true;              // device block-table row out of date
+  int64_t digested = 0;           // 64-token pages whose digest is up to date (LC_STORE_DIGEST)
 };
 
 template <class T>
@@ -79,12 +80,14 @@ struct lc_cache {
   cudaStream_t stream = nullptr;
   uint64_t launches = 0;
   std::vector<SeqLayer> st;  // [seq * n_layers + layer]
+  int32_t role_dg = -1;       // page digest role (LC_STORE_DIGEST)
   uint64_t* d_table = nullptr;  // [n_layers][max_seqs][max_pages_per_seq]
   cudaEvent_t ev_copy = nullptr;
   DevBuf<uint8_t> in_k, in_v, qbuf, outbuf, fetchbuf;
   DevBuf<float> q_rot, part, hook_a, hook_b, hook_c, q_proj;
   DevBuf<__half> q_h;
   DevBuf<int32_t> ctr;  // fused decode arrival counters (zero between launches)
+  DevBuf<int32_t> tile_map;  // page-sparse decode: logical -> physical tiles
   std::vector<uint8_t> blob;  // host staging of one call's metadata
   // kernel timing (lc_cache_timing)
   bool timing = false;
@@ -290,6 +293,12 @@ int lc_cache_create(const lc_cache_config* cfg, const lc_codec* kcodec, const lc
       rows.push_back((int64_t)c->vc.qwords() * 8);
       rows.push_back(4);
     }
+    if (cfg->store_flags & LC_STORE_DIGEST) {
+      // 64 rows of head_dim / 8 bytes per 64-token page and head: min[D], max[D] f32
+      LC_REQUIRE(cfg->head_dim % 64 == 0, LC_ERR_INVALID, "LC_STORE_DIGEST needs head_dim % 64 == 0");
+      c->role_dg = (int32_t)rows.size();
+      rows.push_back((int64_t)cfg->head_dim / 8);
+    }
     c->layout = PageLayout::make((int32_t)H, rows);
     c->pool.init(c->layout, cfg->max_pages, cfg->device, true);
     c->arena.init(16 << 20);
@@ -410,6 +419,7 @@ static void append_impl(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_
       const int32_t seq = seq_ids[b];
       SeqLayer& sl = c->at(seq, layer);
       sl.head_len.clear();
+      if (!c->full(layer)) sl.digested = 0;  // a ring may move or overwrite digested rows
       const std::vector<int32_t> before = sl.ring.pages;
       const int64_t w = c->ops.prepare_update(sl.ring, n_tokens, c->cfg.step_prealloc != 0);
       if (sl.ring.pages != before) sl.dirty = true;
@@ -482,6 +492,7 @@ int lc_store(lc_cache* c, int32_t seq, int32_t layer, int32_t head, const float*
     sl.ring.view_len = new_len;
     sl.head_len[head] = end;
     sl.dirty = true;
+    sl.digested = 0;
     std::vector<uint64_t> dst_page(n_tokens);
     std::vector<int32_t> dst_row(n_tokens);
     for (int64_t t = 0; t < n_tokens; ++t) {
@@ -599,6 +610,7 @@ int lc_clear(lc_cache* c) {
       c->ops.clear(sl.ring);
       sl.head_len.clear();
       sl.dirty = true;
+      sl.digested = 0;
     }
   });
 }
@@ -861,6 +873,7 @@ int lc_load_lkv2(lc_cache* c, int32_t seq, const char* path, const char* model_f
       c->ops.clear(sl.ring);
       sl.head_len.clear();
       sl.dirty = true;
+      sl.digested = 0;
       const Lkv2Layer& L = man.layers[l];
       const LayerRecs& P = plan[l];
       RingCore& r = sl.ring;
@@ -927,6 +940,7 @@ int lc_release(lc_cache* c, int32_t seq) {
       c->ops.clear(sl.ring);
       sl.head_len.clear();
       sl.dirty = true;
+      sl.digested = 0;
     }
   });
 }
@@ -945,12 +959,14 @@ int lc_truncate(lc_cache* c, int32_t seq, int32_t layer, int64_t n_keep) {
       }
       sl.ring.offset = sl.ring.idx = sl.ring.view_len = mx;
       sl.dirty = true;
+      sl.digested = 0;
       return;
     }
     if (sl.ring.offset <= n_keep) return;
     if (!c->ops.truncate_to(sl.ring, n_keep))
       LC_THROW(LC_ERR_REFUSED, "truncate: post-rotation rollback not supported");
     sl.dirty = true;
+    sl.digested = 0;
   });
 }
 
@@ -969,6 +985,7 @@ int lc_truncate_to(lc_cache* c, int32_t seq, int32_t layer, int64_t target) {
                                    std::to_string(sl.ring.max_size) + ")");
     }
     sl.dirty = true;
+    sl.digested = 0;
   });
 }
 
@@ -991,6 +1008,7 @@ int lc_fork(lc_cache* c, int32_t src, int32_t dst, int64_t prefix_len) {
       SeqLayer& d = c->at(dst, l);
       c->ops.clear(d.ring);
       d.head_len.clear();
+      d.digested = 0;
       d.ring = c->ops.share_prefix(c->at(src, l).ring, prefix_len);
       d.ring.max_size = c->max_size[l];
       d.ring.keep = c->keep[l];
@@ -1118,8 +1136,62 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     LC_REQUIRE(c->kc.m > 0 && c->kc.m <= (uint64_t)kMaxQjlDecode, LC_ERR_INVALID,
                "QJL scores: qjl_m must be in [1, 256]");
   }
+  // ---- page-sparse decode: digest new pages, then decode logical lengths
+  // (the chosen pages and the tail) through a tile map ----
+  const bool sparse = (flags & LC_SPARSE_PAGES) != 0;
+  std::vector<int64_t> real_info;
+  int32_t map_stride = 0;
+  int32_t npad = 1;
+  if (sparse) {
+    LC_REQUIRE(c->role_dg >= 0, LC_ERR_STATE, "page-sparse decode: cache created without LC_STORE_DIGEST");
+    LC_REQUIRE(!qjl && !prefill, LC_ERR_INVALID, "page-sparse decode: not with QJL scores or prefill attention");
+    LC_REQUIRE(c->full(layer), LC_ERR_INVALID, "page-sparse decode: full (non-sliding) layers only");
+    const int G = n_q_heads / hkv;
+    LC_REQUIRE(decode_fast_path(D, (int)c->kc.bits, (int)c->vc.bits, G) && G <= 4, LC_ERR_INVALID,
+               "page-sparse decode: 4-bit K/V, head_dim 128, GQA <= 4 only");
+    real_info = info;
+    std::vector<uint64_t> dpages;
+    std::vector<int32_t> drows;
+    for (int32_t b = 0; b < n_seqs; ++b) {
+      SeqLayer& sl = c->at(seq_ids[b], layer);
+      LC_REQUIRE(sl.head_len.empty(), LC_ERR_STATE, "page-sparse decode: layer filled per head");
+      const int64_t n = lens[b], P = n / kDigestPage;
+      for (int64_t g = sl.digested; g < P; ++g) {  // pages filled since the last digest
+        dpages.push_back(c->pool.addr(sl.ring.pages[g / kGroupsPerPage]));
+        drows.push_back((int32_t)((g % kGroupsPerPage) * kDigestPage));
+      }
+      sl.digested = std::max<int64_t>(sl.digested, P);
+      int64_t keep = sparse_keep_pages(P);
+      if (n < kSparseMinKeys || P <= keep) keep = P;  // dense
+      const int64_t logical = keep * kDigestPage + (n - P * kDigestPage);
+      lens[b] = logical;
+      info[2 * b] = logical;
+      map_stride = std::max<int32_t>(map_stride, (int32_t)((logical + kTileTokens - 1) / kTileTokens));
+      while (npad < P) npad <<= 1;
+    }
+    if (!dpages.empty()) {
+      const size_t k = dpages.size();
+      c->blob.resize(k * 12);
+      std::memcpy(c->blob.data(), dpages.data(), k * 8);
+      std::memcpy(c->blob.data() + k * 8, drows.data(), k * 4);
+      const uint8_t* d = static_cast<const uint8_t*>(c->arena.put(c->blob.data(), c->blob.size(), s));
+      DigestDev dg;
+      dg.pages = reinterpret_cast<const uint64_t*>(d);
+      dg.row0 = reinterpret_cast<const int32_t*>(d + k * 8);
+      dg.cent = c->dk.cent_d;
+      dg.off_kw = c->layout.off[R_KW];
+      dg.off_ks = c->layout.off[R_KS];
+      dg.off_dg = c->layout.off[c->role_dg];
+      dg.row_kw = c->layout.row[R_KW];
+      dg.row_dg = c->layout.row[c->role_dg];
+      dg.bits = (int32_t)c->kc.bits;
+      dg.dim = D;
+      c->timed(c->t_other, s, [&] { launch_digest(dg, (int64_t)k, hkv, s); });
+      ++c->launches;
+    }
+  }
   const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits, qjl);
-  const bool fused = fused_out && decode_fusable(plan, n_q_heads / hkv);
+  const bool fused = fused_out && !sparse && decode_fusable(plan, n_q_heads / hkv);
   // The one-launch path of small calls passes its arrays in the launch
   // parameters; otherwise one upload: [seqinfo i64 | seg i64 | cnt i32].
   const bool inl = fused && decode_inline_fits(n_seqs, hkv);
@@ -1158,6 +1230,26 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     });
     ++c->launches;
   }
+  if (sparse) {  // choose the pages (q' is ready: the unfused path rotated it above)
+    c->tile_map.ensure((size_t)n_seqs * hkv * std::max(map_stride, 1), s);
+    SelectDev sd;
+    sd.seqinfo = c->arena.put_vec(real_info, s);
+    sd.table = c->d_table;
+    sd.table_stride = c->cfg.max_pages_per_seq;
+    sd.q_rot = c->q_rot.p;
+    sd.off_dg = c->layout.off[c->role_dg];
+    sd.row_dg = c->layout.row[c->role_dg];
+    sd.n_seqs = n_seqs;
+    sd.hkv = hkv;
+    sd.hq = n_q_heads;
+    sd.G = n_q_heads / hkv;
+    sd.dim = D;
+    sd.npad = npad;
+    sd.map_stride = map_stride;
+    sd.tile_map = c->tile_map.p;
+    c->timed(c->t_other, s, [&] { launch_page_select(sd, s); });
+    ++c->launches;
+  }
   c->part.ensure((size_t)rows * plan.max_slots * (D + 2), s);
   DecodeArgs a;
   a.table = c->d_table;
@@ -1187,6 +1279,10 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   a.kalpha = kalpha;
   a.valpha = valpha;
   a.part = c->part.p;
+  if (sparse) {
+    a.tile_map = c->tile_map.p;
+    a.map_stride = map_stride;
+  }
   if (qjl) {
     a.q_proj = c->q_proj.p;
     a.role_kq = R_KQ;
@@ -1373,7 +1469,8 @@ int lc_decode_attn_noalloc(lc_cache* c, int32_t layer, int32_t n_seqs, const int
     LC_CUDA(cudaSetDevice(c->cfg.device));
     LC_REQUIRE(is_device_ptr(q) && is_device_ptr(out), LC_ERR_INVALID,
                "lc_decode_attn_noalloc needs q and out in device memory");
-    LC_REQUIRE(!(flags & LC_QJL_SCORES), LC_ERR_INVALID, "lc_decode_attn_noalloc does not take LC_QJL_SCORES");
+    LC_REQUIRE(!(flags & (LC_QJL_SCORES | LC_SPARSE_PAGES)), LC_ERR_INVALID,
+               "lc_decode_attn_noalloc does not take LC_QJL_SCORES or LC_SPARSE_PAGES");
     std::lock_guard<std::mutex> lock(noalloc_mutex());
     uint8_t* const dscr = noalloc_device_scratch(c->cfg.device);
     uint8_t* const hst = noalloc_host_staging();

@@ -54,7 +54,7 @@ int abi_guard(F&& f) {
 // Tokens per page: the reference's KV_CACHE_STEP (native_cache.rs:37), the
 // ring's growth quantum and the block-table granularity.
 constexpr int kPageTokens = 256;
-constexpr int kMaxRoles = 8;
+constexpr int kMaxRoles = 9;
 
 // A page holds kPageTokens rows of every head for each role (buffer), role
 // regions back to back: role r, head h, row t lives at

@@ -172,6 +172,10 @@ struct DecodeDev {
   int64_t off_kq, off_kr;
   int32_t row_kq, qjl_m;
   float qjl_c;
+  // page-sparse decode: logical tile j of segment (b, kvh) is physical tile
+  // tile_map[(b * hkv + kvh) * map_stride + j] of the sequence (null: dense)
+  const int32_t* tile_map;
+  int32_t map_stride;
   InlineMeta meta;  // seqinfo / seg / cnt when those pointers are null
   __device__ __forceinline__ const int64_t* si() const { return seqinfo ? seqinfo : meta.seqinfo; }
   __device__ __forceinline__ const int64_t* sg() const { return seg ? seg : meta.seg; }
@@ -346,26 +350,42 @@ struct PrefetchProducer {
   uint64_t next;  // address of page next_idx of sequence next_b
   int next_b, next_idx;
 
+  // The physical tile of the current logical tile (page-sparse: through
+  // the tile map; the map row of a (sequence, kv head) lists its chosen
+  // pages' tiles in ascending order, then the tail).
+  template <bool SPARSE>
+  __device__ __forceinline__ int ptile(const DecodeDev& a) const {
+    if constexpr (SPARSE) return a.tile_map[(int64_t)(w.b * a.hkv + w.kvh) * a.map_stride + w.tile];
+    else return w.tile;
+  }
+
   // Page address of the current tile (and the next page's, ahead). Called
   // on its own at kernel start so the first table read is in flight while
-  // the prologue does other work.
+  // the prologue does other work. Page-sparse: no read-ahead (the next
+  // page need not follow).
+  template <bool SPARSE = false>
   __device__ __forceinline__ void lookup(const DecodeDev& a) {
-    const int pidx = w.tile >> 3;
+    const int pidx = ptile<SPARSE>(a) >> 3;
     if (pidx != page_idx || w.b != page_b) {
       const uint64_t* trow = a.table + a.si()[2 * w.b + 1] * a.table_stride;
-      page = reinterpret_cast<const uint8_t*>((w.b == next_b && pidx == next_idx) ? next : __ldg(trow + pidx));
+      if constexpr (SPARSE) {
+        page = reinterpret_cast<const uint8_t*>(__ldg(trow + pidx));
+      } else {
+        page = reinterpret_cast<const uint8_t*>((w.b == next_b && pidx == next_idx) ? next : __ldg(trow + pidx));
+        const int npages = (w.nt + 7) >> 3;
+        next_b = w.b;
+        next_idx = pidx + 1 < npages ? pidx + 1 : 0;
+        next = __ldg(trow + next_idx);
+      }
       page_idx = pidx;
       page_b = w.b;
-      const int npages = (w.nt + 7) >> 3;
-      next_b = w.b;
-      next_idx = pidx + 1 < npages ? pidx + 1 : 0;
-      next = __ldg(trow + next_idx);
     }
   }
 
+  template <bool SPARSE = false>
   __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
-    lookup(a);
-    const int64_t hr = (int64_t)w.kvh * kPageTokens + (w.tile & 7) * kTileTok;
+    lookup<SPARSE>(a);
+    const int64_t hr = (int64_t)w.kvh * kPageTokens + (ptile<SPARSE>(a) & 7) * kTileTok;
     // chunk c = lane + 32 q: row c >> 2 = lane / 4 + 8 q, part c & 3 = lane & 3;
     // the V swizzle (part ^ (row & 2)) depends on the lane only
     const uint8_t* k = page + a.off_kw + hr * 64 + lane * 16;
@@ -651,7 +671,7 @@ __device__ __forceinline__ void p_exchange(const uint8_t* st, float pa, float pb
   pb[1][1] = live ? ps[64 + base + ((t + 4) ^ sw)] : 0u;
 }
 
-template <int G, bool FUSED>
+template <int G, bool FUSED, bool SPARSE = false>
 __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid_constant__ DecodeDev a) {
   static_assert(G >= 1 && G <= 4, "pair layout holds 4 heads");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -704,7 +724,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   }
   if (begin < end) {
     pr.w = locate_warp(a, begin, lane);
-    pr.lookup(a);  // the block table is written by host copies only
+    pr.template lookup<SPARSE>(a);  // the block table is written by host copies only
   }
   Walk cw = pr.w;
   // fused: everything above reads constants (codec tables, launch
@@ -745,7 +765,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
 #pragma unroll
   for (int k = 0; k < kFirstTiles; ++k) {
     if (begin + k < end) {
-      pr.issue(a, st0 + k * kStageBytes, lane);
+      pr.template issue<SPARSE>(a, st0 + k * kStageBytes, lane);
       step(a, pr.w);
     }
     cp_commit();
@@ -793,7 +813,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
   if constexpr (FUSED) {  // the second tile
     if (begin + 1 < end) {
-      pr.issue(a, st0 + kStageBytes, lane);
+      pr.template issue<SPARSE>(a, st0 + kStageBytes, lane);
       step(a, pr.w);
     }
     cp_commit();
@@ -892,7 +912,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       else tile(std::integral_constant<bool, true>());
       __syncwarp();
       if (x + kStages < end) {
-        pr.issue(a, st0 + ((x - begin) & 1) * kStageBytes, lane);
+        pr.template issue<SPARSE>(a, st0 + ((x - begin) & 1) * kStageBytes, lane);
         step(a, pr.w);
       }
       cp_commit();
@@ -1580,12 +1600,12 @@ void launch_flat_g(const DecodeDev& d, int grid, cudaStream_t s) {
   LC_CUDA(cudaGetLastError());
 }
 
-template <int G, bool FUSED>
+template <int G, bool FUSED, bool SPARSE = false>
 void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
   constexpr int smem = FUSED ? kFusedSmem : kFlatSmem;
   static bool attr = false;
   if (!attr) {
-    LC_CUDA(cudaFuncSetAttribute(k_decode_pair<G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    LC_CUDA(cudaFuncSetAttribute(k_decode_pair<G, FUSED, SPARSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
   if constexpr (FUSED) {
@@ -1600,9 +1620,9 @@ void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    LC_CUDA(cudaLaunchKernelEx(&cfg, k_decode_pair<G, FUSED>, d));
+    LC_CUDA(cudaLaunchKernelEx(&cfg, k_decode_pair<G, FUSED, SPARSE>, d));
   } else {
-    k_decode_pair<G, FUSED><<<(unsigned)grid, kFlatWarps * 32, smem, s>>>(d);
+    k_decode_pair<G, FUSED, SPARSE><<<(unsigned)grid, kFlatWarps * 32, smem, s>>>(d);
     LC_CUDA(cudaGetLastError());
   }
 }
@@ -1819,6 +1839,8 @@ static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
   d.kalpha = a.kalpha;
   d.valpha = a.valpha;
   d.part = a.part;
+  d.tile_map = a.tile_map;
+  d.map_stride = a.map_stride;
   d.q_proj = a.q_proj;
   if (a.q_proj) {
     LC_REQUIRE(!p.flat && a.qjl_m > 0 && a.qjl_m <= kMaxQjlDecode && a.role_kq >= 0 && a.role_kr >= 0,
@@ -1836,6 +1858,15 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
   const DecodeDev d = make_dev(a, p);
   if (p.flat) {
     if (p.total_tiles == 0) return;
+    if (d.tile_map) {  // page-sparse: pair geometry only (checked by the caller)
+      LC_REQUIRE(d.G >= 1 && d.G <= 4, LC_ERR_INVALID, "page-sparse decode needs GQA <= 4");
+      switch (d.G) {
+        case 1: return launch_pair_g<1, false, true>(d, p.grid, s);
+        case 2: return launch_pair_g<2, false, true>(d, p.grid, s);
+        case 3: return launch_pair_g<3, false, true>(d, p.grid, s);
+        default: return launch_pair_g<4, false, true>(d, p.grid, s);
+      }
+    }
     switch (d.G) {
       case 1: return launch_pair_g<1, false>(d, p.grid, s);
       case 2: return launch_pair_g<2, false>(d, p.grid, s);

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <mutex>
 #include <vector>
@@ -87,8 +88,42 @@ struct DecodeArgs {
   // (Phi q) * scale * log2(e); null: stage-1 scores.
   const float* q_proj = nullptr;
   int32_t role_kq = -1, role_kr = -1, qjl_m = 0;
+  // page-sparse decode (flat pair path): logical -> physical tiles, see DecodeDev
+  const int32_t* tile_map = nullptr;
+  int32_t map_stride = 0;
   float qjl_c = 0.f;  // sqrt(pi/2) / sqrt(qjl_m)
 };
+
+// ---- page-sparse decode (sparse.cu) -----------------------------------------
+constexpr int kDigestPage = 64;                          // DIGEST_PAGE (native_cache.rs:351)
+constexpr int kGroupsPerPage = kPageTokens / kDigestPage;  // digest pages per cache page
+constexpr int kSparseSink = 1, kSparseRecent = 4;        // SPARSE_SINK_PAGES / _RECENT_PAGES
+constexpr int64_t kSparseMinKeys = 16384;                // SPARSE_DECODE_MIN_KEYS
+constexpr int kTileTokens = 32;                          // tokens per decode tile
+// pages kept of `pages` digested ones (sparse_keep_pages, native_attention.rs:327-329)
+inline int64_t sparse_keep_pages(int64_t pages) { return std::max<int64_t>(pages / 8, 64); }
+
+struct DigestDev {
+  const uint64_t* pages;  // [items] page address of each 64-token page to digest
+  const int32_t* row0;    // [items] its first row in the page (multiple of 64)
+  const float* cent;      // K centroids (f32)
+  int64_t off_kw, off_ks, off_dg, row_kw, row_dg;
+  int32_t bits, dim;
+};
+void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t s);
+
+struct SelectDev {
+  const int64_t* seqinfo;  // [n_seqs][2] (tokens, table row), device
+  const uint64_t* table;
+  int64_t table_stride;
+  const float* q_rot;      // [n_seqs][hq][dim] rotated, scaled queries
+  int64_t off_dg, row_dg;
+  int32_t n_seqs, hkv, hq, G, dim;
+  int32_t npad;            // power of two >= the most digested pages of any sequence
+  int32_t map_stride;      // tiles per (sequence, kv head) row of tile_map
+  int32_t* tile_map;       // [n_seqs * hkv][map_stride] logical -> physical tile
+};
+void launch_page_select(const SelectDev& a, cudaStream_t s);
 
 // Largest qjl_m the decode's QJL scores take (8 projection rows per lane).
 constexpr int kMaxQjlDecode = 256;

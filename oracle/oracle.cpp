@@ -566,6 +566,26 @@ void orc_sc_attend_prefix(const orc_simple_cache* s, int layer, int head, const 
     orc_sc_attend_values(s, layer, head, w.data(), out);
 }
 
+// Attention over a subset of the stored tokens (mask[t] != 0): the dense
+// decode of the chosen pages in page-sparse decode (sdpa over the gathered
+// keys, native_attention.rs:273-293).
+void orc_sc_attend_mask(const orc_simple_cache* s, int layer, int head, const float* query, float scale,
+                        const uint8_t* mask, float* out) {
+    const orc_cv_list& l = s->keys[(size_t)layer * s->n_heads + head];
+    std::vector<float> sc(l.n > 0 ? l.n : 1), w(l.n > 0 ? l.n : 1, 0.0f);
+    if (l.n == 0) { for (int i = 0; i < s->dim; ++i) out[i] = 0.0f; return; }
+    orc_sc_attend_keys(s, layer, head, query, sc.data());
+    double mx = -INFINITY;
+    for (int64_t t = 0; t < l.n; ++t)
+        if (mask[t]) mx = std::max(mx, (double)sc[t] * (double)scale);
+    double sum = 0.0;
+    for (int64_t t = 0; t < l.n; ++t)
+        if (mask[t]) sum += std::exp((double)sc[t] * (double)scale - mx);
+    for (int64_t t = 0; t < l.n; ++t)
+        if (mask[t]) w[t] = (float)(std::exp((double)sc[t] * (double)scale - mx) / sum);
+    orc_sc_attend_values(s, layer, head, w.data(), out);
+}
+
 // ---------------------------------------------------------------------------
 // RoPE as lc_append_rope applies it before the compressor: token t at
 // position pos0 + t, pair i < rot_dims / 2 turned by

@@ -89,6 +89,7 @@ def lib():
         L.orc_sc_attend_ex.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int, _f32p]
         L.orc_sc_attend_prefix.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, C.c_int64, _f32p]
         L.orc_rope.argtypes = [_f32p, C.c_int64, C.c_int, C.c_int, C.c_int64, C.c_double, C.c_int]
+        L.orc_sc_attend_mask.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, _u8p, _f32p]
         L.orc_sc_attend_values.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p]
         L.orc_sc_attend.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_float, _f32p]
         L.orc_sc_clear.argtypes = [C.c_void_p]
@@ -196,6 +197,55 @@ def qjl_project_and_pack(P: np.ndarray, res: np.ndarray) -> np.ndarray:
     lib().orc_qjl_project_and_pack(np.ascontiguousarray(P, np.float32).ravel(), m, d,
                                    np.ascontiguousarray(res, np.float32), out)
     return out
+
+
+# Page-sparse decode (sdpa_page_sparse, native_attention.rs:217-329) over the
+# codes: DIGEST_PAGE 64, SPARSE_SINK_PAGES 1, SPARSE_RECENT_PAGES 4,
+# SPARSE_DECODE_MIN_KEYS 16384, keep = max(pages / 8, 64).
+DIGEST_PAGE, SPARSE_SINK, SPARSE_RECENT, SPARSE_MIN_KEYS = 64, 1, 4, 16384
+
+
+def quest_select(words, sigma, cents, bits, dim, q_rot):
+    """Token mask of one (sequence, kv head) for page-sparse decode.
+
+    words [n, W] u64 and sigma [n] f32: the stored keys; cents: the codebook;
+    q_rot [G, dim]: the head group's rotated queries. The digest holds the
+    min and max of the dequantized rotated keys, f32(c[code]) * sigma in f32,
+    over each full 64-token page; a page's bound is the max over the group of
+    sum_d max(q_d max_d, q_d min_d) (in f64 here); the first and the 4 last
+    full pages are pinned; the keep largest bounds are chosen (lower page
+    index first on ties) with the undigested tail. Returns (mask [n] u8,
+    relative gap between the keep-th and the next unpinned bound, or inf)."""
+    n = words.shape[0]
+    P = n // DIGEST_PAGE
+    keep = max(P // 8, 64)
+    mask = np.ones(n, np.uint8)
+    if n < SPARSE_MIN_KEYS or P <= keep:
+        return mask, float("inf")
+    codes = unpack_codes(words, dim, bits)
+    kd = np.asarray(cents, np.float32)[codes] * sigma.astype(np.float32)[:, None]  # f32 products
+    pages = kd[: P * DIGEST_PAGE].reshape(P, DIGEST_PAGE, dim)
+    mn, mx = pages.min(1).astype(np.float64), pages.max(1).astype(np.float64)
+    q = np.asarray(q_rot, np.float64)
+    qp, qn = np.maximum(q, 0.0), np.minimum(q, 0.0)
+    bound = (qp @ mx.T + qn @ mn.T).max(0)  # [P]
+    pinned = (np.arange(P) < SPARSE_SINK) | (np.arange(P) >= P - SPARSE_RECENT)
+    order = sorted(range(P), key=lambda p: (0 if pinned[p] else 1, -bound[p], p))
+    chosen = order[:keep]
+    free = [bound[p] for p in order[keep - 1: keep + 1] if not pinned[p]]
+    gap = abs(free[0] - free[1]) / max(abs(free[0]), 1e-30) if len(free) == 2 else float("inf")
+    mask[: P * DIGEST_PAGE] = 0
+    for p in chosen:
+        mask[p * DIGEST_PAGE:(p + 1) * DIGEST_PAGE] = 1
+    return mask, gap
+
+
+def unpack_codes(words: np.ndarray, dim: int, bits: int) -> np.ndarray:
+    """bitpack::unpack_codes (bitpack.rs:35-52) over the last axis of u64 words."""
+    cpw = 64 // bits
+    j = np.arange(dim)
+    w = words[..., j // cpw]
+    return ((w >> ((j % cpw) * bits).astype(np.uint64)) & np.uint64((1 << bits) - 1)).astype(np.uint8)
 
 
 def rope(x: np.ndarray, rot_dims: int, pos0: int, base: float = 10000.0, traditional: bool = False) -> np.ndarray:
@@ -325,6 +375,13 @@ class SimpleCache:
         out = np.empty(self.dim, np.float32)
         lib().orc_sc_attend_prefix(self._h, layer, head, np.ascontiguousarray(q, np.float32), float(scale),
                                    int(n_keys), out)
+        return out
+
+    def attend_mask(self, layer, head, q, scale, mask):
+        """Attention over the stored tokens with mask[t] != 0."""
+        out = np.empty(self.dim, np.float32)
+        lib().orc_sc_attend_mask(self._h, layer, head, np.ascontiguousarray(q, np.float32), float(scale),
+                                 np.ascontiguousarray(mask, np.uint8), out)
         return out
 
     def attend(self, layer, head, q, scale=1.0, qjl=False):

@@ -1,0 +1,129 @@
+"""GPU: page-sparse decode over the codes (LC_STORE_DIGEST + LC_SPARSE_PAGES).
+
+The oracle restates the policy of sdpa_page_sparse
+(native_attention.rs:217-329) on the stored codes (pyoracle.quest_select):
+digest = min / max of f32(c[code]) * sigma per 64-token page, bound = max
+over the query group of sum_d max(q'_d max_d, q'_d min_d), first page and 4
+most recent full pages pinned, keep = max(pages / 8, 64), plus the
+undigested tail. The GPU output must match the oracle's attention over that
+token set (orc_sc_attend_mask) at the decode tolerance. The data is checked
+to leave no near-tie at the selection boundary. Queries use the configs'
+scale (std 1/sqrt(128)), which keeps the softmax clear of the f16 centroid
+limit of very peaked scores. A sequence below 16384 keys in the same call is
+dense.
+"""
+import numpy as np
+import pytest
+
+import helpers
+
+pytestmark = pytest.mark.gpu
+
+DIM, HKV, HQ = 128, 8, 32
+
+
+def _cache(lc, orc, lens, flags=None, max_size=0):
+    t = orc.Tables.generate(DIM, 4, 64, 42)
+    c = lc.TurboQuantCompressor.from_tables(t.R, t.bounds, t.cents, t.proj)
+    pages = (max(lens) + 400 + 255) // 256 + 2
+    cache = lc.CudaKvCache(1, HKV, DIM, c, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
+                           max_pages_per_seq=pages,
+                           store_flags=lc.LC_STORE_DIGEST if flags is None else flags,
+                           layer_max_size=[max_size], layer_keep=[0])
+    return t, cache
+
+
+def _fill(cache, orc, t, lens, seed):
+    """Random keys with 120 pages per head scaled by distinct factors 2 + 0.05 k:
+    scaling a key scales its sigma and keeps its codes, so those pages' bounds
+    separate cleanly and the selection boundary has no near-tie."""
+    refs, kv = [], []
+    rng = np.random.default_rng(seed)
+    for b, n in enumerate(lens):
+        K = helpers.kv(orc, seed + 2 * b, 1, HKV, n, DIM)
+        V = helpers.kv(orc, seed + 2 * b + 1, 1, HKV, n, DIM)
+        P = n // 64
+        if P > 130:
+            for h in range(HKV):
+                for k, p in enumerate(rng.choice(np.arange(1, P - 4), size=120, replace=False)):
+                    K[0, h, p * 64:(p + 1) * 64] *= np.float32(2.0 + 0.05 * k)
+        for c0 in range(0, n, 4096):
+            c1 = min(n, c0 + 4096)
+            cache.append(0, [b], np.ascontiguousarray(K[:, :, c0:c1]), np.ascontiguousarray(V[:, :, c0:c1]))
+        ref = orc.SimpleCache(orc.Compressor(t), orc.Compressor(t), 1, HKV, DIM)
+        for h in range(HKV):
+            ref.store(0, h, K[0, h], V[0, h], n)
+        refs.append(ref)
+        kv.append((K, V))
+    return refs, kv
+
+
+def _oracle(orc, t, refs, q, scale):
+    G = HQ // HKV
+    out = np.zeros((len(refs), HQ, DIM), np.float32)
+    min_gap = float("inf")
+    R = t.R.astype(np.float64)
+    for b, ref in enumerate(refs):
+        for kvh in range(HKV):
+            words, _, _, sigma = ref.read(0, kvh, 0)
+            qr = q[b, kvh * G:(kvh + 1) * G].astype(np.float64) @ R.T
+            mask, gap = orc.quest_select(words, sigma, t.cents, 4, DIM, qr)
+            min_gap = min(min_gap, gap)
+            for g in range(G):
+                out[b, kvh * G + g] = ref.attend_mask(0, kvh, q[b, kvh * G + g], scale, mask)
+    return out, min_gap
+
+
+def test_sparse_decode_matches_oracle(lc, orc, gpu):
+    lens = [20000, 5000]
+    t, cache = _cache(lc, orc, lens)
+    refs, _ = _fill(cache, orc, t, lens, 300)
+    q = helpers.queries(orc, 301, len(lens), HQ, DIM, std=DIM ** -0.5)
+    scale = 1.0 / np.sqrt(DIM)
+    got = cache.decode_attn(0, [0, 1], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    ref, gap = _oracle(orc, t, refs, q, scale)
+    assert gap > 1e-4, gap  # no near-tie at the selection boundary
+    ok, msg = helpers.attn_close(got, ref)
+    assert ok, msg
+    dense = cache.decode_attn(0, [0, 1], q, HQ, scale)
+    assert np.abs(dense[0] - got[0]).max() > 1e-4  # the long sequence really went sparse
+    ok, msg = helpers.attn_close(got[1:], dense[1:])  # the short one stayed dense
+    assert ok, msg
+    cache.close()
+
+
+def test_sparse_digest_follows_appends(lc, orc, gpu):
+    lens = [17000]
+    t, cache = _cache(lc, orc, lens)
+    refs, kv = _fill(cache, orc, t, lens, 400)
+    scale = 1.0 / np.sqrt(DIM)
+    q = helpers.queries(orc, 401, 1, HQ, DIM, std=DIM ** -0.5)
+    cache.decode_attn(0, [0], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)  # digests the first pages
+    K = helpers.kv(orc, 402, 1, HKV, 300, DIM)
+    V = helpers.kv(orc, 403, 1, HKV, 300, DIM)
+    for s0 in range(0, 300, 100):  # 300 more tokens: new full pages to digest
+        cache.append(0, [0], np.ascontiguousarray(K[:, :, s0:s0 + 100]), np.ascontiguousarray(V[:, :, s0:s0 + 100]))
+    for h in range(HKV):
+        refs[0].store(0, h, K[0, h], V[0, h], 300)
+    got = cache.decode_attn(0, [0], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    ref, gap = _oracle(orc, t, refs, q, scale)
+    assert gap > 1e-4, gap
+    ok, msg = helpers.attn_close(got, ref)
+    assert ok, msg
+    cache.close()
+
+
+def test_sparse_refusals(lc, orc, gpu):
+    q = helpers.queries(orc, 9, 1, HQ, DIM)
+    t, cache = _cache(lc, orc, [100], flags=0)
+    _fill(cache, orc, t, [100], 1)
+    with pytest.raises(lc.LumenError) as e:
+        cache.decode_attn(0, [0], q, HQ, 0.1, flags=lc.LC_SPARSE_PAGES)
+    assert e.value.code == lc.LC_ERR_STATE
+    cache.close()
+    t, cache = _cache(lc, orc, [100], max_size=1024)  # a sliding layer
+    _fill(cache, orc, t, [100], 2)
+    with pytest.raises(lc.LumenError) as e:
+        cache.decode_attn(0, [0], q, HQ, 0.1, flags=lc.LC_SPARSE_PAGES)
+    assert e.value.code == lc.LC_ERR_INVALID
+    cache.close()
