@@ -644,6 +644,71 @@ def run_window(args):
 # ----------------------------------------------------------------------------
 # Config 3: prefill quantize-append in 2048-token chunks + prefix reuse
 # ----------------------------------------------------------------------------
+def run_sparse(args):
+    """Page-sparse decode (LC_SPARSE_PAGES) against dense decode on one cache:
+    config 4's per-GPU share, 32 requests x 32768 tokens, GQA 32/8, d128,
+    4-bit; the same decode steps timed both ways (no appends in the timed
+    steps, so the digests are up to date after the warm-up)."""
+    import torch
+
+    rank, local, world = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lc = importlib.import_module("lumen-rs_b200")
+    B, hq, hkv, D, ctx = 32, CFG["hq"], CFG["hkv"], CFG["dim"], 32768
+    L = min(args.layers, 4)
+    codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
+    pages = (ctx + 255) // 256 + 1
+    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=B, max_pages=L * B * pages + 64,
+                           max_pages_per_seq=pages, store_flags=lc.LC_STORE_DIGEST, device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242 + rank)
+    ids = list(range(B))
+    for layer in range(L):
+        for c0 in range(0, ctx, 2048):
+            k = torch.randn((B, hkv, 2048, D), generator=gen, device=dev).to(torch.bfloat16)
+            v = torch.randn((B, hkv, 2048, D), generator=gen, device=dev).to(torch.bfloat16)
+            cache.append(layer, ids, k, v)
+    q = (torch.randn((L, B, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    out_d = torch.empty((L, B, hq, D), device=dev, dtype=torch.float32)
+    out_s = torch.empty((L, B, hq, D), device=dev, dtype=torch.float32)
+
+    def step(flags, out):
+        for layer in range(L):
+            cache.decode_attn(layer, ids, q[layer], hq, 1.0, flags=flags, out=out[layer], out_dtype=lc.LC_F32)
+
+    res = {}
+    with ClockSampler(local) as clk:
+        for name, flags, out in (("dense", 0, out_d), ("sparse", lc.LC_SPARSE_PAGES, out_s)):
+            for _ in range(args.warmup):
+                step(flags, out)
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            for _ in range(args.steps):
+                step(flags, out)
+            ev1.record()
+            ev1.synchronize()
+            res[name] = ev0.elapsed_time(ev1) / args.steps
+    P = ctx // 64
+    keep = max(P // 8, 64)
+    bytes_dense = L * B * hkv * ctx * BYTES_PER_TOKEN_HEAD
+    print(json.dumps({
+        "metric": METRIC, "value": B / (res["sparse"] / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["sparse"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic", "mode": "sparse",
+        "config": {"workload": f"config4 per-GPU share: {B} requests x {ctx} tokens, {hq}q/{hkv}kv, d{D}, 4-bit, "
+                               f"{L} layers; page-sparse decode (64-token pages, keep max(pages/8, 64) + sink + "
+                               f"recent + tail) vs dense", "kept_fraction": keep * 64 / ctx},
+        "dense": {"tok_s": B / (res["dense"] / 1e3), "ms_per_step": res["dense"],
+                  "decode_gbs": bytes_dense / (res["dense"] / 1e3) / 1e9},
+        "speedup_vs_dense": res["dense"] / res["sparse"],
+        "max_abs_sparse_vs_dense": float((out_s - out_d).abs().max()),
+        "clocks": clk.summary(),
+    }), flush=True)
+    cache.close()
+
+
 def run_prefill(args):
     import torch
 
@@ -731,7 +796,7 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers (32 = config 1; fewer for profiling)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--mode", default="decode", choices=["decode", "longctx", "prefill", "window"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "longctx", "prefill", "window", "sparse"],
                     help="decode: config 1 request-sharded; longctx: config 4's 1M-token sequence split by "
                          "sequence; prefill: config 3 chunked quantize-append and prefix reuse; window: config 2 "
                          "mixed precision with rotating windows")
@@ -745,6 +810,8 @@ def main():
         run_longctx(args)
     elif args.mode == "prefill":
         run_prefill(args)
+    elif args.mode == "sparse":
+        run_sparse(args)
     elif args.mode == "window":
         run_window(args)
     else:

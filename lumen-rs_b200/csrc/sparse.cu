@@ -80,6 +80,7 @@ __global__ void k_page_select(SelectDev a) {
   float* qs = reinterpret_cast<float*>(sm);  // [G][D]
   float* key = qs + G * D;                    // [npad]
   int32_t* idx = reinterpret_cast<int32_t*>(key + a.npad);
+  uint64_t* pg = reinterpret_cast<uint64_t*>(idx + a.npad);  // [npad / 4] page addresses
   const int64_t n = a.seqinfo[2 * b];
   const uint64_t* trow = a.table + a.seqinfo[2 * b + 1] * a.table_stride;
   const int P = (int)(n / kDigestPage);
@@ -94,57 +95,78 @@ __global__ void k_page_select(SelectDev a) {
   }
   for (int i = threadIdx.x; i < G * D; i += blockDim.x)
     qs[i] = a.q_rot[((int64_t)b * a.hq + (int64_t)kvh * G) * D + i];
+  for (int i = threadIdx.x; i < (P + kGroupsPerPage - 1) / kGroupsPerPage; i += blockDim.x) pg[i] = trow[i];
   __syncthreads();
-  // bounds: warp per page
+  // bounds: a warp takes 4 pages per round trip; lane l holds dims l + 32 j
+  // of each page's min and max, read once for all G query heads
+  constexpr int kPer = 4, kDj = 4;  // pages per pass; dims per lane (head_dim 128)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int p = warp; p < a.npad; p += nw) {
-    float bound = -FLT_MAX;
-    if (p < P) {
-      if (p < kSparseSink || p >= P - kSparseRecent) {
-        bound = FLT_MAX;
-      } else {
-        const uint8_t* page = reinterpret_cast<const uint8_t*>(trow[p / kGroupsPerPage]);
-        const float* dg = reinterpret_cast<const float*>(
-            page + a.off_dg + ((int64_t)kvh * kPageTokens + (p % kGroupsPerPage) * kDigestPage) * a.row_dg);
-        for (int g = 0; g < G; ++g) {
-          float s = 0.f;
-          for (int d = lane; d < D; d += 32) {
-            const float q = qs[g * D + d];
-            s += q > 0.f ? q * dg[D + d] : q * dg[d];
-          }
+  for (int p0 = warp * kPer; p0 < a.npad; p0 += nw * kPer) {
+    float mn[kPer][kDj], mx[kPer][kDj];
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-          bound = fmaxf(bound, s);
-        }
+    for (int u = 0; u < kPer; ++u) {
+      const int p = p0 + u;
+      const bool live = p < P && p >= kSparseSink && p < P - kSparseRecent;
+      const float* dg = live ? reinterpret_cast<const float*>(
+                                   reinterpret_cast<const uint8_t*>(pg[p / kGroupsPerPage]) + a.off_dg +
+                                   ((int64_t)kvh * kPageTokens + (p % kGroupsPerPage) * kDigestPage) * a.row_dg)
+                             : nullptr;
+#pragma unroll
+      for (int j = 0; j < kDj; ++j) {
+        const int d = lane + 32 * j;
+        mn[u][j] = live && d < D ? dg[d] : 0.f;
+        mx[u][j] = live && d < D ? dg[D + d] : 0.f;
       }
     }
-    if (lane == 0) {
-      key[p] = bound;
-      idx[p] = p;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int p = p0 + u;
+      float bound = -FLT_MAX;
+      for (int g = 0; g < G; ++g) {
+        float sacc = 0.f;
+#pragma unroll
+        for (int j = 0; j < kDj; ++j) {
+          const int d = lane + 32 * j;
+          const float q = d < D ? qs[g * D + d] : 0.f;
+          sacc += q > 0.f ? q * mx[u][j] : q * mn[u][j];
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, off);
+        bound = fmaxf(bound, sacc);
+      }
+      if (p < P && (p < kSparseSink || p >= P - kSparseRecent)) bound = FLT_MAX;  // pinned
+      if (p >= P) bound = -FLT_MAX;                                             // padding
+      if (lane == 0 && p < a.npad) {
+        key[p] = bound;
+        idx[p] = p;
+      }
     }
   }
   __syncthreads();
   bitonic_desc(key, idx, a.npad);
-  // the keep chosen pages, in ascending order: flag them in key[] (reused),
-  // then compact with a block-wide count (one thread per page range)
+  // flag the keep chosen pages (key[] reused), then warp 0 compacts them in
+  // ascending page order: ballot + popcount per 32 pages
   int32_t* flag = reinterpret_cast<int32_t*>(key);
-  __syncthreads();
-  // idx[0..keep) are the chosen pages; mark them
   for (int i = threadIdx.x; i < a.npad; i += blockDim.x) flag[i] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < keep; i += blockDim.x) flag[idx[i]] = 1;
   __syncthreads();
-  if (threadIdx.x == 0) {  // serial compaction: at most a few thousand pages
-    int j = 0;
-    for (int p = 0; p < P; ++p)
-      if (flag[p]) {
-        out[2 * j] = 2 * p;
-        out[2 * j + 1] = 2 * p + 1;
-        ++j;
+  if (warp == 0) {
+    int j = 0;  // chosen pages written so far
+    for (int p0 = 0; p0 < P; p0 += 32) {
+      const int p = p0 + lane;
+      const bool on = p < P && flag[p];
+      const unsigned m = __ballot_sync(0xffffffffu, on);
+      if (on) {
+        const int pos = j + __popc(m & ((1u << lane) - 1u));
+        out[2 * pos] = 2 * p;
+        out[2 * pos + 1] = 2 * p + 1;
       }
+      j += __popc(m);
+    }
     // the undigested tail: tiles from the first token past the full pages
     const int t0 = 2 * P, t1 = (int)((n + kTileTokens - 1) / kTileTokens);
-    for (int t = t0; t < t1; ++t) out[2 * j + (t - t0)] = t;
+    for (int t = t0 + lane; t < t1; t += 32) out[2 * j + (t - t0)] = t;
   }
 }
 
@@ -157,7 +179,8 @@ void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t 
 }
 
 void launch_page_select(const SelectDev& a, cudaStream_t s) {
-  const size_t smem = (size_t)a.G * a.dim * 4 + (size_t)a.npad * 8;
+  LC_REQUIRE(a.dim <= 128, LC_ERR_INVALID, "page-sparse decode: head_dim <= 128");
+  const size_t smem = (size_t)a.G * a.dim * 4 + (size_t)a.npad * 8 + (size_t)(a.npad / kGroupsPerPage + 1) * 8;
   static bool attr = false;
   if (!attr) {
     LC_CUDA(cudaFuncSetAttribute(k_page_select, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
