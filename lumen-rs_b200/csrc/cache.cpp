@@ -1141,7 +1141,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   const bool sparse = (flags & LC_SPARSE_PAGES) != 0;
   std::vector<int64_t> real_info;
   int32_t map_stride = 0;
-  int32_t npad = 1;
+  int32_t npad = 1;  // the most full pages of any sequence
   if (sparse) {
     LC_REQUIRE(c->role_dg >= 0, LC_ERR_STATE, "page-sparse decode: cache created without LC_STORE_DIGEST");
     LC_REQUIRE(!qjl && !prefill, LC_ERR_INVALID, "page-sparse decode: not with QJL scores or prefill attention");
@@ -1167,7 +1167,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
       lens[b] = logical;
       info[2 * b] = logical;
       map_stride = std::max<int32_t>(map_stride, (int32_t)((logical + kTileTokens - 1) / kTileTokens));
-      while (npad < P) npad <<= 1;
+      npad = std::max<int32_t>(npad, (int32_t)P);
     }
     if (!dpages.empty()) {
       const size_t k = dpages.size();
@@ -1191,7 +1191,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     }
   }
   const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits, qjl);
-  const bool fused = fused_out && !sparse && decode_fusable(plan, n_q_heads / hkv);
+  const bool fused = fused_out && decode_fusable(plan, n_q_heads / hkv);
   // The one-launch path of small calls passes its arrays in the launch
   // parameters; otherwise one upload: [seqinfo i64 | seg i64 | cnt i32].
   const bool inl = fused && decode_inline_fits(n_seqs, hkv);
@@ -1230,13 +1230,16 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     });
     ++c->launches;
   }
-  if (sparse) {  // choose the pages (q' is ready: the unfused path rotated it above)
+  if (sparse) {  // choose the pages (the select kernel rotates the queries itself)
     c->tile_map.ensure((size_t)n_seqs * hkv * std::max(map_stride, 1), s);
     SelectDev sd;
     sd.seqinfo = c->arena.put_vec(real_info, s);
     sd.table = c->d_table;
     sd.table_stride = c->cfg.max_pages_per_seq;
-    sd.q_rot = c->q_rot.p;
+    sd.q = dq;
+    sd.q_dtype = q_dtype;
+    sd.q_rotated = (flags & LC_Q_ROTATED) ? 1 : 0;
+    sd.RT = c->dk.RTd;
     sd.off_dg = c->layout.off[c->role_dg];
     sd.row_dg = c->layout.row[c->role_dg];
     sd.n_seqs = n_seqs;

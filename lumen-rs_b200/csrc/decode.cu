@@ -724,7 +724,9 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   }
   if (begin < end) {
     pr.w = locate_warp(a, begin, lane);
-    pr.template lookup<SPARSE>(a);  // the block table is written by host copies only
+    // the block table is written by host copies only; a page-sparse tile
+    // map by the selection kernel, so the fused kernel reads it after the wait
+    if constexpr (!(FUSED && SPARSE)) pr.template lookup<SPARSE>(a);
   }
   Walk cw = pr.w;
   // fused: everything above reads constants (codec tables, launch
@@ -1906,6 +1908,14 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
   d.out = f.out;
   d.out_dtype = f.out_dtype;
   d.oscale = f.oscale;
+  if (d.tile_map) {  // page-sparse
+    switch (d.G) {
+      case 1: return launch_pair_g<1, true, true>(d, p.grid, s);
+      case 2: return launch_pair_g<2, true, true>(d, p.grid, s);
+      case 3: return launch_pair_g<3, true, true>(d, p.grid, s);
+      default: return launch_pair_g<4, true, true>(d, p.grid, s);
+    }
+  }
   switch (d.G) {
     case 1: return launch_pair_g<1, true>(d, p.grid, s);
     case 2: return launch_pair_g<2, true>(d, p.grid, s);

@@ -116,10 +116,12 @@ struct SelectDev {
   const int64_t* seqinfo;  // [n_seqs][2] (tokens, table row), device
   const uint64_t* table;
   int64_t table_stride;
-  const float* q_rot;      // [n_seqs][hq][dim] rotated, scaled queries
+  const void* q;           // [n_seqs][hq][dim] queries as given (q_dtype)
+  int32_t q_dtype, q_rotated;
+  const float* RT;         // [dim][dim] R^T of the key codec
   int64_t off_dg, row_dg;
   int32_t n_seqs, hkv, hq, G, dim;
-  int32_t npad;            // power of two >= the most digested pages of any sequence
+  int32_t npad;            // >= the most digested pages of any sequence
   int32_t map_stride;      // tiles per (sequence, kv head) row of tile_map
   int32_t* tile_map;       // [n_seqs * hkv][map_stride] logical -> physical tile
 };
