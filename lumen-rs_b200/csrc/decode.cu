@@ -51,6 +51,48 @@ __device__ __forceinline__ float load_any(const void* p, int dtype, int64_t i) {
   return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// v[i] = element idx[i] of an f32 / bf16 / f16 array, as f32, where ok[i]
+// (else 0). The dtype branch is taken once, so all N loads are in flight
+// before the first conversion waits on one.
+template <int N>
+__device__ __forceinline__ void load_n_any(const void* p, int dtype, const int64_t (&idx)[N], const bool (&ok)[N],
+                                           float (&v)[N]) {
+  if (dtype == LC_F32) {
+    const float* q = static_cast<const float*>(p);
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = ok[i] ? q[idx[i]] : 0.f;
+  } else {
+    const unsigned short* q = static_cast<const unsigned short*>(p);
+    unsigned short r[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) r[i] = ok[i] ? q[idx[i]] : (unsigned short)0;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      v[i] = dtype == LC_BF16 ? __uint_as_float((uint32_t)r[i] << 16) : __half2float(__ushort_as_half(r[i]));
+  }
+}
+
+// Raw bits of element idx[i] (f32, or bf16 / f16 in the low half) where
+// ok[i], else 0; raw_as_float converts one. The loads do not wait.
+template <int N>
+__device__ __forceinline__ void load_n_raw(const void* p, int dtype, const int64_t (&idx)[N], const bool (&ok)[N],
+                                           uint32_t (&r)[N]) {
+  if (dtype == LC_F32) {
+    const uint32_t* q = static_cast<const uint32_t*>(p);
+#pragma unroll
+    for (int i = 0; i < N; ++i) r[i] = ok[i] ? q[idx[i]] : 0u;
+  } else {
+    const unsigned short* q = static_cast<const unsigned short*>(p);
+#pragma unroll
+    for (int i = 0; i < N; ++i) r[i] = ok[i] ? (uint32_t)q[idx[i]] : 0u;
+  }
+}
+__device__ __forceinline__ float raw_as_float(uint32_t r, int dtype) {
+  if (dtype == LC_F32) return __uint_as_float(r);
+  if (dtype == LC_BF16) return __uint_as_float(r << 16);
+  return __half2float(__ushort_as_half((unsigned short)r));
+}
+
 __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v) {
   if (dtype == LC_F32) reinterpret_cast<float*>(p)[i] = v;
   else if (dtype == LC_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
@@ -96,9 +138,18 @@ __global__ void __launch_bounds__(512) k_rotate_q(const void* q, int dtype, int 
   extern __shared__ __align__(16) float sq[];  // [kRotRows][D]
   const int i = threadIdx.x;
   const int r0 = blockIdx.x * kRotRows;
-  for (int k = threadIdx.x; k < kRotRows * D; k += blockDim.x) {
-    const int r = k / D;
-    sq[k] = (r0 + r < n_rows) ? load_any(q, dtype, (int64_t)r0 * D + k) : 0.0f;
+  {  // blockDim.x == D: thread i loads column i of the kRotRows rows
+    int64_t idx[kRotRows];
+    bool ok[kRotRows];
+    float v[kRotRows];
+#pragma unroll
+    for (int r = 0; r < kRotRows; ++r) {
+      idx[r] = (int64_t)(r0 + r) * D + i;
+      ok[r] = r0 + r < n_rows;
+    }
+    load_n_any(q, dtype, idx, ok, v);
+#pragma unroll
+    for (int r = 0; r < kRotRows; ++r) sq[r * D + i] = v[r];
   }
   __syncthreads();
   float acc[kRotRows];
@@ -349,43 +400,53 @@ struct PrefetchProducer {
   int page_b, page_idx;
   uint64_t next;  // address of page next_idx of sequence next_b
   int next_b, next_idx;
-
-  // The physical tile of the current logical tile (page-sparse: through
-  // the tile map; the map row of a (sequence, kv head) lists its chosen
-  // pages' tiles in ascending order, then the tail).
-  template <bool SPARSE>
-  __device__ __forceinline__ int ptile(const DecodeDev& a) const {
-    if constexpr (SPARSE) return a.tile_map[(int64_t)(w.b * a.hkv + w.kvh) * a.map_stride + w.tile];
-    else return w.tile;
-  }
+  // Page-sparse: lane j holds the physical tile (win_ph) and its page
+  // address (win_pg) of logical tile win_t0 + j of segment win_seg, read
+  // 32 tiles at a time; cur_ph is the current tile's.
+  int win_seg, win_t0, win_ph, cur_ph;
+  uint64_t win_pg;
 
   // Page address of the current tile (and the next page's, ahead). Called
   // on its own at kernel start so the first table read is in flight while
-  // the prologue does other work. Page-sparse: no read-ahead (the next
-  // page need not follow).
+  // the prologue does other work. Page-sparse: the window of 32 tile-map
+  // entries and their page addresses, refilled when the walk leaves it.
   template <bool SPARSE = false>
-  __device__ __forceinline__ void lookup(const DecodeDev& a) {
-    const int pidx = ptile<SPARSE>(a) >> 3;
-    if (pidx != page_idx || w.b != page_b) {
-      const uint64_t* trow = a.table + a.si()[2 * w.b + 1] * a.table_stride;
-      if constexpr (SPARSE) {
-        page = reinterpret_cast<const uint8_t*>(__ldg(trow + pidx));
-      } else {
+  __device__ __forceinline__ void lookup(const DecodeDev& a, int lane) {
+    if constexpr (SPARSE) {
+      const int seg = w.b * a.hkv + w.kvh;
+      if (seg != win_seg || (unsigned)(w.tile - win_t0) >= 32u) {
+        win_seg = seg;
+        win_t0 = w.tile;
+        const int t = w.tile + lane;
+        win_ph = 0;
+        win_pg = 0;
+        if (t < w.nt) {
+          win_ph = a.tile_map[(int64_t)seg * a.map_stride + t];
+          win_pg = __ldg(a.table + a.si()[2 * w.b + 1] * a.table_stride + (win_ph >> 3));
+        }
+      }
+      const int j = w.tile - win_t0;
+      cur_ph = __shfl_sync(0xffffffffu, win_ph, j);
+      page = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, win_pg, j));
+    } else {
+      const int pidx = w.tile >> 3;
+      if (pidx != page_idx || w.b != page_b) {
+        const uint64_t* trow = a.table + a.si()[2 * w.b + 1] * a.table_stride;
         page = reinterpret_cast<const uint8_t*>((w.b == next_b && pidx == next_idx) ? next : __ldg(trow + pidx));
         const int npages = (w.nt + 7) >> 3;
         next_b = w.b;
         next_idx = pidx + 1 < npages ? pidx + 1 : 0;
         next = __ldg(trow + next_idx);
+        page_idx = pidx;
+        page_b = w.b;
       }
-      page_idx = pidx;
-      page_b = w.b;
     }
   }
 
   template <bool SPARSE = false>
   __device__ __forceinline__ void issue(const DecodeDev& a, uint32_t st, int lane) {
-    lookup<SPARSE>(a);
-    const int64_t hr = (int64_t)w.kvh * kPageTokens + (ptile<SPARSE>(a) & 7) * kTileTok;
+    lookup<SPARSE>(a, lane);
+    const int64_t hr = (int64_t)w.kvh * kPageTokens + ((SPARSE ? cur_ph : w.tile) & 7) * kTileTok;
     // chunk c = lane + 32 q: row c >> 2 = lane / 4 + 8 q, part c & 3 = lane & 3;
     // the V swizzle (part ^ (row & 2)) depends on the lane only
     const uint8_t* k = page + a.off_kw + hr * 64 + lane * 16;
@@ -600,10 +661,10 @@ __device__ __forceinline__ void split_h2(float x, float y, uint32_t& hi, uint32_
 
 // M staged in shared memory: row i at i * 512 bytes from the base, its
 // 16-byte chunk c stored at c ^ 4 (i & 1), so the fragment reads of rows
-// g = 2p, 2p + 1 (one quarter-warp) fall in distinct banks. The prologue
-// stages R in the table area (the table is built over it afterwards); the
-// epilogue stages V's R^T in the warps' second pipeline stages (free once
-// the main loop is over), eight rows per warp.
+// g = 2p, 2p + 1 (one quarter-warp) fall in distinct banks. Both live in
+// the warps' second pipeline stages, eight rows per warp: the prologue's R
+// (the second tile is issued after the rotation) and the epilogue's V R^T
+// (free once the main loop is over).
 __device__ __forceinline__ int m_chunk(int i, int c) { return (c ^ ((i & 1) << 2)) << 4; }
 __device__ __forceinline__ uint8_t* m_row(uint8_t* smem, int n_before, uint32_t lut_off, int i) {
   const int wi = i >> 3;
@@ -703,6 +764,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   pr.next = 0;
   pr.next_b = -1;
   pr.next_idx = -1;
+  pr.win_seg = -1;
+  pr.win_t0 = 0;
   float* qs = reinterpret_cast<float*>(smem + kFlatSmem);  // [kFusedRows][D]
   __shared__ int merged[kFusedSegs];
   // first (sequence, kv head) segment of this CTA and its query-row count,
@@ -710,14 +773,17 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   __shared__ int cta_seg[2];
   const bool rot_q = FUSED && !a.q_rotated;
   const float cl = lut_centroid(a, lane);
-  // fused: the K rotation R into the table area before any tile traffic
-  // (an L2 hit shared by all CTAs; the table is built over it afterwards)
+  // fused: the K rotation R into the warps' second pipeline stages (free
+  // until the second tile is issued after the prologue), before any tile
+  // traffic; an L2 hit shared by all CTAs
   if constexpr (FUSED) {
     if (rot_q) {
 #pragma unroll
       for (int it = 0; it < D * D / 4 / (kFlatWarps * 32); ++it) {
         const int k = threadIdx.x + it * kFlatWarps * 32;  // row k / 32, chunk k % 32
-        cp_async16(s0 + lut_off + (k >> 5) * 512 + m_chunk(k >> 5, k & 31), a.qR + 4 * k);
+        const int i = k >> 5;
+        cp_async16((uint32_t)__cvta_generic_to_shared(m_row(smem, n_before, lut_off, i)) + m_chunk(i, k & 31),
+                   a.qR + 4 * k);
       }
     }
     cp_commit();
@@ -726,18 +792,11 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     pr.w = locate_warp(a, begin, lane);
     // the block table is written by host copies only; a page-sparse tile
     // map by the selection kernel, so the fused kernel reads it after the wait
-    if constexpr (!(FUSED && SPARSE)) pr.template lookup<SPARSE>(a);
+    if constexpr (!(FUSED && SPARSE)) pr.template lookup<SPARSE>(a, lane);
   }
   Walk cw = pr.w;
-  // fused: everything above reads constants (codec tables, launch
-  // parameters, the block table); the queries, the cache pages, the arrival
-  // counters and the partials come after the previous kernel has completed
-  if constexpr (FUSED) pdl_wait();
-
-  // fused: this CTA's segments and their query rows, loaded before the
-  // tiles are issued so they do not queue behind the tile traffic
-  constexpr int QIT = kFusedRows * D / (kFlatWarps * 32);
-  float qv[QIT];
+  // fused: this CTA's segments and their query-row count (host-written
+  // arrays only, so before the wait)
   int sid0 = 0, nrows = 0;
   if constexpr (FUSED) {
     const int cb = blockIdx.x * kFlatWarps * pw;
@@ -747,22 +806,35 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       sid0 = f.b * a.hkv + f.kvh;
       nrows = (e.b * a.hkv + e.kvh - sid0 + 1) * G;
     }
+    // the centroid-pair table from constants, while the reads above are in
+    // flight (read only after the barrier that follows the rotation)
+    build_lut(lut, cl);
+  }
+  // fused: everything above reads constants (codec tables, launch
+  // parameters, the block table); the queries, the cache pages, the arrival
+  // counters and the partials come after the previous kernel has completed
+  if constexpr (FUSED) pdl_wait();
+
+  // fused: the query rows' raw loads go out first, then the first tile; the
+  // conversion waits on the rows after both are in flight
+  constexpr int QIT = kFusedRows * D / (kFlatWarps * 32);
+  uint32_t qraw[QIT];
+  if constexpr (FUSED) {
+    int64_t qidx[QIT];
+    bool qok[QIT];
 #pragma unroll
     for (int it = 0; it < QIT; ++it) {
       const int k = threadIdx.x + it * kFlatWarps * 32;
       const int r = k >> 7, j = k & 127;
-      qv[it] = 0.f;
-      if (r < nrows) {
-        const int sid = sid0 + r / G;
-        const int64_t row = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G;
-        qv[it] = load_any(a.q_in, a.q_dtype, row * D + j);
-      }
+      const int sid = sid0 + r / G;
+      qidx[it] = ((int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G) * D + j;
+      qok[it] = r < nrows;
     }
+    load_n_raw(a.q_in, a.q_dtype, qidx, qok, qraw);
   }
 
-  // The first tiles. Fused: one now, the second after the prologue; the
-  // query rows and R wait behind this burst of every warp's copies, and a
-  // tile takes longer to compute than the next one takes to arrive.
+  // The first tiles. Fused: one now, the second after the prologue; a tile
+  // takes longer to compute than the next one takes to arrive.
   constexpr int kFirstTiles = FUSED ? 1 : 2;
 #pragma unroll
   for (int k = 0; k < kFirstTiles; ++k) {
@@ -787,12 +859,12 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     for (int it = 0; it < QIT; ++it) {
       const int k = threadIdx.x + it * kFlatWarps * 32;
       const int r = k >> 7, j = k & 127;
-      if (r < nb * 8) qs[rot_q ? rot_swz(r, j) : k] = qv[it] * a.qscale;
+      if (r < nb * 8) qs[rot_q ? rot_swz(r, j) : k] = raw_as_float(qraw[it], a.q_dtype) * a.qscale;
     }
     if (rot_q) {
       cp_wait_one();  // R has landed; the first tile may still be in flight
       __syncthreads();
-      auto rrow = [&](int i) { return static_cast<const uint8_t*>(lut + i * 512); };
+      auto rrow = [&](int i) { return static_cast<const uint8_t*>(m_row(smem, n_before, lut_off, i)); };
       float d[2][4];
       if (n0 < nb) rot_block(rrow, mi, qs, n0, g, t, d[0]);
       if (n0 + 2 < nb) rot_block(rrow, mi, qs, n0 + 2, g, t, d[1]);
@@ -809,11 +881,12 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
         }
       }
     }
+  } else {
+    build_lut(lut, cl);
   }
-  build_lut(lut, cl);
-  __syncthreads();
+  __syncthreads();  // the table, and the fused q' rows
   if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
-  if constexpr (FUSED) {  // the second tile
+  if constexpr (FUSED) {  // the second tile (over R, read by every warp by now)
     if (begin + 1 < end) {
       pr.template issue<SPARSE>(a, st0 + kStageBytes, lane);
       step(a, pr.w);
