@@ -58,9 +58,9 @@ def _fill(cache, orc, t, lens, seed):
     return refs, kv
 
 
-def _oracle(orc, t, refs, q, scale):
-    G = HQ // HKV
-    out = np.zeros((len(refs), HQ, DIM), np.float32)
+def _oracle(orc, t, refs, q, scale, hq=HQ):
+    G = hq // HKV
+    out = np.zeros((len(refs), hq, DIM), np.float32)
     min_gap = float("inf")
     R = t.R.astype(np.float64)
     for b, ref in enumerate(refs):
@@ -126,4 +126,46 @@ def test_sparse_refusals(lc, orc, gpu):
     with pytest.raises(lc.LumenError) as e:
         cache.decode_attn(0, [0], q, HQ, 0.1, flags=lc.LC_SPARSE_PAGES)
     assert e.value.code == lc.LC_ERR_INVALID
+    cache.close()
+
+
+@pytest.mark.parametrize("hq,qkind", [(8, "f32"), (16, "f16"), (16, "rotated"), (24, "f32")])
+def test_sparse_group_sizes_and_query_forms(lc, orc, gpu, hq, qkind):
+    """GQA 1, 2 and 3 (the select kernel's head loop and the fused decode's
+    G instantiations), f16 queries, and queries passed already rotated
+    (LC_Q_ROTATED), against the same oracle selection."""
+    lens = [18000]
+    t, cache = _cache(lc, orc, lens)
+    refs, _ = _fill(cache, orc, t, lens, 500 + hq)
+    q = helpers.queries(orc, 501 + hq, len(lens), hq, DIM, std=DIM ** -0.5)
+    scale = 1.0 / np.sqrt(DIM)
+    flags = lc.LC_SPARSE_PAGES
+    if qkind == "f16":
+        q = q.astype(np.float16).astype(np.float32)  # the oracle sees the f16 values
+        qg = q.astype(np.float16)
+    elif qkind == "rotated":
+        qg = (q.astype(np.float64) @ t.R.astype(np.float64).T).astype(np.float32)
+        flags |= lc.LC_Q_ROTATED
+    else:
+        qg = q
+    got = cache.decode_attn(0, [0], qg, hq, scale, flags=flags)
+    ref, gap = _oracle(orc, t, refs, q, scale, hq)
+    assert gap > 1e-4, gap
+    ok, msg = helpers.attn_close(got, ref)
+    assert ok, msg
+    cache.close()
+
+
+def test_sparse_partials_path(lc, orc, gpu):
+    """lc_decode_attn_partials with LC_SPARSE_PAGES (the unfused decode over
+    the tile map plus the slot merge) finishes to the fused call's output."""
+    lens = [20000, 17000]
+    t, cache = _cache(lc, orc, lens)
+    _fill(cache, orc, t, lens, 700)
+    q = helpers.queries(orc, 701, len(lens), HQ, DIM, std=DIM ** -0.5)
+    scale = 1.0 / np.sqrt(DIM)
+    fused = cache.decode_attn(0, [0, 1], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    m, l, o = cache.decode_partials(0, [0, 1], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    out = cache.merge_partials(m[None], l[None], o[None]).reshape(fused.shape)
+    np.testing.assert_allclose(out, fused, rtol=0, atol=2e-5)
     cache.close()
