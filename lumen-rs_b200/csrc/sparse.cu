@@ -65,18 +65,29 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 }
 constexpr uint32_t kPinnedKey = 0xFFFFFFFFu;
 constexpr int kSelThreads = 512;
+constexpr int kSelStages = 4;  // digest ring stages (1 KB pages) per warp: 3 in flight ahead
+
+__device__ __forceinline__ void sel_cp16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void sel_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void sel_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
 // One CTA per (sequence, kv head), head_dim 128, G <= 4:
 //   1. q' = R q for the G query heads (q as given unless already rotated),
 //      split into its positive and negative parts: the bound of a page is
 //      max_g sum_d (q'+_d max_d + q'-_d min_d), the same sum as
 //      sum_d max(q'_d max_d, q'_d min_d) since max_d >= min_d;
-//   2. bounds: 8 lanes per page (float4 columns 4c + 32j of min and max),
-//      4 pages per warp pass;
+//   2. bounds: a warp per page, its digest streamed into a per-warp ring
+//      by cp.async 3 pages ahead; lane l takes dims l + 32 j, whose q'+ and
+//      q'- for every head it keeps in registers;
 //   3. the keep-th largest key by a 4-pass radix select over bytes, and how
 //      many keys equal to it are taken (lowest pages first);
-//   4. warp 0 writes the chosen pages' tiles in ascending order, then the
-//      undigested tail.
+//   4. the chosen pages' tiles in ascending order (per-warp chunks with
+//      prefix offsets), then the undigested tail.
 // The decode that follows is launched programmatically: its prologue reads
 // nothing this kernel writes and may start on SMs this grid has left.
 __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
@@ -100,7 +111,8 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   float* qp = reinterpret_cast<float*>(sm);  // [G][D] positive part of q'
   float* qn = qp + G * D;                     // [G][D] negative part
   float* qx = qn + G * D;                     // [G][D] the queries as given
-  uint32_t* key = reinterpret_cast<uint32_t*>(qx + G * D);                // [npad]
+  float* ring = qx + G * D;                   // [warps][kSelStages][256] digest pages
+  uint32_t* key = reinterpret_cast<uint32_t*>(ring + (kSelThreads / 32) * kSelStages * 256);  // [npad]
   uint64_t* pg = reinterpret_cast<uint64_t*>(key + ((a.npad + 1) & ~1));  // [npad / 4] page addresses
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel[2];
@@ -109,6 +121,30 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   for (int i = tid; i < G * D; i += NT) qx[i] = q_elem(a.q, a.q_dtype, q0 + i);
   for (int i = tid; i < (P + kGroupsPerPage - 1) / kGroupsPerPage; i += NT) pg[i] = trow[i];
   __syncthreads();
+
+  // the first digest pages of every warp go out before the rotation
+  const int lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = NT / 32;
+  const int K = warp < P ? (P - warp + NW - 1) / NW : 0;  // pages of this warp: warp + 16 k
+  float* wring = ring + warp * kSelStages * 256;
+  const uint32_t ring0 = (uint32_t)__cvta_generic_to_shared(wring);
+  auto live_page = [&](int p) { return p >= kSparseSink && p < P - kSparseRecent; };
+  auto issue = [&](int k) {
+    const int p = warp + NW * k;
+    if (k < K && live_page(p)) {
+      const uint8_t* dg = reinterpret_cast<const uint8_t*>(pg[p / kGroupsPerPage]) + a.off_dg +
+                          ((int64_t)kvh * kPageTokens + (p % kGroupsPerPage) * kDigestPage) * a.row_dg;
+      const uint32_t dst = ring0 + (k % kSelStages) * 1024;
+      sel_cp16(dst + lane * 16, dg + lane * 16);
+      sel_cp16(dst + 512 + lane * 16, dg + 512 + lane * 16);
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < kSelStages - 1; ++k) {
+    issue(k);
+    sel_commit();
+  }
+
   // q'_i = sum_j R[i][j] q_j: thread t takes output dim i = t % 128 of heads
   // t / 128, t / 128 + 4, ...; RT = R^T keeps each step's reads coalesced
   for (int r = tid; r < G * D; r += NT) {
@@ -125,46 +161,57 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   }
   __syncthreads();
 
-  const int lane = tid & 31, warp = tid >> 5;
-  const int sub = lane >> 3, c = lane & 7;
-  for (int p0 = warp * 4; p0 < P; p0 += (NT / 32) * 4) {
-    const int p = p0 + sub;
-    const bool live = p < P && p >= kSparseSink && p < P - kSparseRecent;
-    const float4* dg =
-        live ? reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(pg[p / kGroupsPerPage]) + a.off_dg +
-                                               ((int64_t)kvh * kPageTokens + (p % kGroupsPerPage) * kDigestPage) *
-                                                   a.row_dg)
-             : nullptr;
-    float4 mn[4], mx[4];
+  // bounds: a warp per page; each page's digest (min[128] then max[128],
+  // 1 KB) streams into the warp's ring by cp.async, kSelStages - 1 pages
+  // ahead; lane l takes dims l + 32 j, whose q'+ and q'- for every head stay
+  // in registers for the whole loop
+  float rp[4][4], rn[4][4];  // [head][j]
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      mn[j] = live ? dg[c + 8 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      mx[j] = live ? dg[D / 4 + c + 8 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int gg = g < G ? g : 0;  // heads past G repeat head 0: the max is unchanged
+      rp[g][j] = qp[gg * D + lane + 32 * j];
+      rn[g][j] = qn[gg * D + lane + 32 * j];
     }
-    float bound = -FLT_MAX;
-    for (int g = 0; g < G; ++g) {
-      const float4* p4 = reinterpret_cast<const float4*>(qp + g * D);
-      const float4* n4 = reinterpret_cast<const float4*>(qn + g * D);
-      float s = 0.f;
+  const bool hi = (lane & 16) != 0, mid = (lane & 8) != 0;
+  for (int k = 0; k < K; ++k) {
+    issue(k + kSelStages - 1);  // into the stage read at k - 1
+    sel_commit();
+    sel_wait<kSelStages - 1>();  // page k has landed
+    __syncwarp();
+    const int p = warp + NW * k;
+    if (live_page(p)) {
+      const float* st = wring + (k % kSelStages) * 256;
+      float sg[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float4 u = p4[c + 8 * j], v = n4[c + 8 * j];
-        s = fmaf(u.x, mx[j].x, s);
-        s = fmaf(u.y, mx[j].y, s);
-        s = fmaf(u.z, mx[j].z, s);
-        s = fmaf(u.w, mx[j].w, s);
-        s = fmaf(v.x, mn[j].x, s);
-        s = fmaf(v.y, mn[j].y, s);
-        s = fmaf(v.z, mn[j].z, s);
-        s = fmaf(v.w, mn[j].w, s);
+        const float mn = st[lane + 32 * j], mx = st[D + lane + 32 * j];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          sg[g] = fmaf(rp[g][j], mx, sg[g]);
+          sg[g] = fmaf(rn[g][j], mn, sg[g]);
+        }
       }
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      bound = fmaxf(bound, s);
+      // transposed reduction: lane bit 4 keeps heads {0,1} or {2,3}, bit 3
+      // one of the pair; then the sum over the other lanes, the max over heads
+      float a0 = hi ? sg[2] : sg[0], a1 = hi ? sg[3] : sg[1];
+      a0 += __shfl_xor_sync(0xffffffffu, hi ? sg[0] : sg[2], 16);
+      a1 += __shfl_xor_sync(0xffffffffu, hi ? sg[1] : sg[3], 16);
+      float v = mid ? a1 : a0;
+      v += __shfl_xor_sync(0xffffffffu, mid ? a0 : a1, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+      if (lane == 0) key[p] = order_key(v);
+    } else if (lane == 0) {
+      key[p] = kPinnedKey;
     }
-    if (c == 0 && p < P) key[p] = live ? order_key(bound) : kPinnedKey;
+    __syncwarp();  // the stage is read before it is refilled
   }
+  sel_wait<0>();
   __syncthreads();
   // radix select: T = the keep-th largest key; need = how many keys equal
   // to T are taken. Warp 0 scans the 256 bins from the top, lane l owning
@@ -217,30 +264,67 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
     pmask |= 255u << shift;
     need = sel[1];
   }
-  if (warp == 0) {
-    const uint32_t T = prefix;
-    int j = 0;             // chosen pages written so far
-    uint32_t eq_seen = 0;  // keys equal to T met so far
-    for (int p0 = 0; p0 < P; p0 += 32) {
-      const int p = p0 + lane;
-      const uint32_t k = p < P ? key[p] : 0u;
-      const bool eq = p < P && k == T;
-      const unsigned em = __ballot_sync(0xffffffffu, eq);
-      const uint32_t eq_rank = eq_seen + (uint32_t)__popc(em & ((1u << lane) - 1u));
-      const bool on = p < P && (k > T || (eq && eq_rank < need));
-      const unsigned m = __ballot_sync(0xffffffffu, on);
-      if (on) {
-        const int pos = j + __popc(m & ((1u << lane) - 1u));
-        out[2 * pos] = 2 * p;  // rows of tile_map need not be 8-byte aligned
-        out[2 * pos + 1] = 2 * p + 1;
+  // the chosen pages (key > T, and the first `need` keys equal to T in page
+  // order) in ascending order, 32 pages per warp chunk: chunk counts of
+  // ties, then of chosen pages, each turned into offsets by warp 0 (the
+  // ring area is free now)
+  const uint32_t T = prefix;
+  const int nch = (P + 31) >> 5;
+  uint32_t* c_eq = reinterpret_cast<uint32_t*>(ring);  // [nch] ties, then their offsets
+  uint32_t* c_on = c_eq + nch;                         // [nch] chosen, then their offsets
+  auto scan = [&](uint32_t* c) {                       // exclusive prefix sum by warp 0
+    uint32_t carry = 0;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      const uint32_t v = c0 + lane < nch ? c[c0 + lane] : 0u;
+      uint32_t inc = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += t;
       }
-      eq_seen += (uint32_t)__popc(em);
-      j += __popc(m);
+      if (c0 + lane < nch) c[c0 + lane] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
     }
-    // the undigested tail: tiles from the first token past the full pages
-    const int t0 = 2 * P, t1 = (int)((n + kTileTokens - 1) / kTileTokens);
-    for (int t = t0 + lane; t < t1; t += 32) out[2 * j + (t - t0)] = t;
+  };
+  const unsigned below = (1u << lane) - 1u;
+  for (int ch = warp; ch < nch; ch += NW) {
+    const int p = 32 * ch + lane;
+    const bool eq = p < P && key[p] == T;
+    const unsigned em = __ballot_sync(0xffffffffu, eq);
+    if (lane == 0) c_eq[ch] = (uint32_t)__popc(em);
   }
+  __syncthreads();
+  if (warp == 0) scan(c_eq);
+  __syncthreads();
+  for (int ch = warp; ch < nch; ch += NW) {
+    const int p = 32 * ch + lane;
+    const uint32_t k = p < P ? key[p] : 0u;
+    const bool eq = p < P && k == T;
+    const unsigned em = __ballot_sync(0xffffffffu, eq);
+    const bool on = p < P && (k > T || (eq && c_eq[ch] + (uint32_t)__popc(em & below) < need));
+    const unsigned m = __ballot_sync(0xffffffffu, on);
+    if (lane == 0) c_on[ch] = (uint32_t)__popc(m);
+  }
+  __syncthreads();
+  if (warp == 0) scan(c_on);
+  __syncthreads();
+  for (int ch = warp; ch < nch; ch += NW) {
+    const int p = 32 * ch + lane;
+    const uint32_t k = p < P ? key[p] : 0u;
+    const bool eq = p < P && k == T;
+    const unsigned em = __ballot_sync(0xffffffffu, eq);
+    const bool on = p < P && (k > T || (eq && c_eq[ch] + (uint32_t)__popc(em & below) < need));
+    const unsigned m = __ballot_sync(0xffffffffu, on);
+    if (on) {
+      const int pos = (int)c_on[ch] + __popc(m & below);
+      out[2 * pos] = 2 * p;  // rows of tile_map need not be 8-byte aligned
+      out[2 * pos + 1] = 2 * p + 1;
+    }
+  }
+  // the undigested tail, after the keep chosen pages: tiles from the first
+  // token past the full pages
+  const int t0 = 2 * P, t1 = (int)((n + kTileTokens - 1) / kTileTokens);
+  for (int t = t0 + tid; t < t1; t += NT) out[2 * keep + (t - t0)] = t;
 }
 
 }  // namespace
@@ -253,8 +337,8 @@ void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t 
 
 void launch_page_select(const SelectDev& a, cudaStream_t s) {
   LC_REQUIRE(a.dim == 128 && a.G >= 1 && a.G <= 4, LC_ERR_INVALID, "page-sparse decode: head_dim 128, GQA <= 4");
-  const size_t smem = (size_t)3 * a.G * a.dim * 4 + (size_t)((a.npad + 1) & ~1) * 4 +
-                      (size_t)(a.npad / kGroupsPerPage + 1) * 8;
+  const size_t smem = (size_t)3 * a.G * a.dim * 4 + (size_t)(kSelThreads / 32) * kSelStages * 1024 +
+                      (size_t)((a.npad + 1) & ~1) * 4 + (size_t)(a.npad / kGroupsPerPage + 1) * 8;
   static size_t max_dyn = 0;  // 227 KB less the static histogram
   if (max_dyn == 0) {
     cudaFuncAttributes fa;
