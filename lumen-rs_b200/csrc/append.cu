@@ -77,6 +77,45 @@ __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) 
   return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// x[v] = element idx[v] of an f32 / bf16 / f16 array where ok[v] (else 0);
+// the dtype branch is taken once, so all N loads are in flight together.
+template <int N>
+__device__ __forceinline__ void load_n_elem(const void* p, int dtype, const int64_t (&idx)[N], const bool (&ok)[N],
+                                            float (&x)[N]) {
+  if (dtype == LC_F32) {
+    const float* q = static_cast<const float*>(p);
+#pragma unroll
+    for (int v = 0; v < N; ++v) x[v] = ok[v] ? q[idx[v]] : 0.0f;
+  } else {
+    const unsigned short* q = static_cast<const unsigned short*>(p);
+    unsigned short r[N];
+#pragma unroll
+    for (int v = 0; v < N; ++v) r[v] = ok[v] ? q[idx[v]] : (unsigned short)0;
+#pragma unroll
+    for (int v = 0; v < N; ++v)
+      x[v] = dtype == LC_BF16 ? __uint_as_float((uint32_t)r[v] << 16) : __half2float(__ushort_as_half(r[v]));
+  }
+}
+
+// acc[v] = fl(fl(acc[v] + fl(M[j][i] x_v[j])) ...) over j = 0 .. D-1 in order
+// (round-to-nearest f32 products and sums, no contraction), M row-major with
+// row stride ld, x_v = xs + v * D. Four j per step: x rows are read as float4.
+template <int NB>
+__device__ __forceinline__ void seq_matvec(const float* M, int ld, const float* xs, int D, int i, float (&acc)[NB]) {
+#pragma unroll 2
+  for (int j = 0; j < D; j += 4) {
+    const float r0 = M[j * ld + i], r1 = M[(j + 1) * ld + i], r2 = M[(j + 2) * ld + i], r3 = M[(j + 3) * ld + i];
+#pragma unroll
+    for (int v = 0; v < NB; ++v) {
+      const float4 x = *reinterpret_cast<const float4*>(xs + v * D + j);
+      acc[v] = __fadd_rn(acc[v], __fmul_rn(r0, x.x));
+      acc[v] = __fadd_rn(acc[v], __fmul_rn(r1, x.y));
+      acc[v] = __fadd_rn(acc[v], __fmul_rn(r2, x.z));
+      acc[v] = __fadd_rn(acc[v], __fmul_rn(r3, x.w));
+    }
+  }
+}
+
 // Shared memory: [tables (TAB: RT, then R and PT when stage 2 runs)]
 // [per group: xs, ys, rs [kNB][D], vscale, vinv, vrn [kNB], qbits, codes].
 struct GroupBufs {
@@ -133,15 +172,30 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
 
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const void* src = a.src[side];
-  const int n1 = c.n_levels - 1;
   const int groups = blockDim.x / D;
+  // thresholds and centroids (bits <= 8) for the code search
+  __shared__ float sthr[256], scent[256];
+  for (int k = threadIdx.x; k < c.n_levels - 1; k += blockDim.x) sthr[k] = c.thr[k];
+  for (int k = threadIdx.x; k < c.n_levels; k += blockDim.x) scent[k] = c.cent[k];
   __syncthreads();
 
   for (int64_t base = (int64_t)blockIdx.x * groups * kNB; base < n_vec; base += (int64_t)gridDim.x * groups * kNB) {
     const int64_t v0 = base + (int64_t)grp * kNB;
     const int nb = v0 < n_vec ? (int)(n_vec - v0 < kNB ? n_vec - v0 : kNB) : 0;
     // ---- load the batch (input layout [n_seqs][h_in][n_tok][D]) ----
-    for (int v = 0; v < kNB; ++v) xs[v * D + i] = v < nb ? load_elem(src, a.dtype, (v0 + v) * D + i) : 0.0f;
+    {
+      int64_t idx[kNB];
+      bool ok[kNB];
+      float xv[kNB];
+#pragma unroll
+      for (int v = 0; v < kNB; ++v) {
+        idx[v] = (v0 + v) * D + i;
+        ok[v] = v < nb;
+      }
+      load_n_elem(src, a.dtype, idx, ok, xv);
+#pragma unroll
+      for (int v = 0; v < kNB; ++v) xs[v * D + i] = xv[v];
+    }
     __syncthreads();
     if (side == 0 && a.rope_cs) {  // thread i rotates pair i of every vector
       if (i < a.rope_half)
@@ -157,12 +211,7 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
     float acc[kNB];
 #pragma unroll
     for (int v = 0; v < kNB; ++v) acc[v] = -0.0f;
-#pragma unroll 4
-    for (int j = 0; j < D; ++j) {
-      const float r = RT[j * D + i];
-#pragma unroll
-      for (int v = 0; v < kNB; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(r, xs[v * D + j]));
-    }
+    seq_matvec(RT, D, xs, D, i, acc);
 #pragma unroll
     for (int v = 0; v < kNB; ++v) ys[v * D + i] = acc[v];
     __syncthreads();
@@ -186,11 +235,15 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
       const float sc = vscale[v];
       int code = 0;
       if (!(sc < 1e-10f)) {
+        // the count of thresholds t with !(yn < t) (lloyd_max.rs:132-143's
+        // linear scan) by binary search: the thresholds ascend, so that
+        // predicate holds on a prefix of them (on all of them for NaN)
         const float yn = __fmul_rn(ys[v * D + i], vinv[v]);
-        for (int k = 0; k < n1; ++k) code += !(yn < c.thr[k]);
+        for (int step = c.n_levels >> 1; step > 0; step >>= 1)
+          if (!(yn < sthr[code + step - 1])) code += step;
       }
       codes[v * D + i] = (uint8_t)code;
-      ys[v * D + i] = __fmul_rn(c.cent[code], sc);
+      ys[v * D + i] = __fmul_rn(scent[code], sc);
     }
     __syncthreads();
 
@@ -198,12 +251,7 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
       // ---- recon[i] = sum_j R[j][i] * deq[j] (rotation.rs:102-113), residual ----
 #pragma unroll
       for (int v = 0; v < kNB; ++v) acc[v] = 0.0f;
-#pragma unroll 4
-      for (int j = 0; j < D; ++j) {
-        const float r = R[j * D + i];
-#pragma unroll
-        for (int v = 0; v < kNB; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(r, ys[v * D + j]));
-      }
+      seq_matvec(R, D, ys, D, i, acc);
 #pragma unroll
       for (int v = 0; v < kNB; ++v) rs[v * D + i] = __fsub_rn(xs[v * D + i], acc[v]);
       __syncthreads();
@@ -219,13 +267,12 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
       // ---- QJL sign bits (qjl.rs:57-74) ----
       for (int rbase = 0; rbase < M; rbase += D) {
         const int r = rbase + i;
+        float dot[kNB];
+#pragma unroll
+        for (int v = 0; v < kNB; ++v) dot[v] = -0.0f;
+        if (r < M) seq_matvec(PT, M, rs, D, r, dot);
         for (int v = 0; v < kNB; ++v) {
-          bool bit = false;
-          if (r < M) {
-            float dot = -0.0f;
-            for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(PT[j * M + r], rs[v * D + j]));
-            bit = dot >= 0.0f;
-          }
+          const bool bit = r < M && dot[v] >= 0.0f;
           const unsigned bal = __ballot_sync(0xffffffffu, bit);
           if ((i & 31) == 0) {
             const int wi = r >> 5;
