@@ -350,6 +350,18 @@ def run_ours(args):
         step()
     dec_ms, dec_n, app_ms, app_n, other_ms = cache.timing(0)
     ctx2 = cache.ring_state(0, 0)["view_len"]
+    # the same step with R folded into the query and output projections, as
+    # the reference's Gemma path does (gemma4_moe.rs:4705-4765): the decode
+    # takes rotated queries and returns rotated outputs (per-launch events)
+    rot_flags = lc.LC_Q_ROTATED | lc.LC_OUT_ROTATED
+    cache.timing(1)
+    for _ in range(t_steps):
+        for layer in range(L):
+            cache.append(layer, ids, k1[layer], v1[layer], stream=stream_ptr)
+            cache.decode_attn(layer, ids, qs[layer], hq, 1.0, flags=rot_flags, out=out[layer],
+                              out_dtype=lc.LC_BF16, stream=stream_ptr)
+    rdec_ms, rdec_n, _, _, _ = cache.timing(0)
+    ctx3 = cache.ring_state(0, 0)["view_len"]
     if world > 1:
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -361,6 +373,8 @@ def run_ours(args):
     kv_bytes_timed = B * hkv * BYTES_PER_TOKEN_HEAD * (ctx1 + 1 + ctx2) / 2.0
     dec_avg_ms = dec_ms / max(dec_n, 1)
     achieved = kv_bytes_timed / (dec_avg_ms / 1e3) / 1e9
+    rdec_avg_ms = rdec_ms / max(rdec_n, 1)
+    rot_achieved = B * hkv * BYTES_PER_TOKEN_HEAD * (ctx2 + 1 + ctx3) / 2.0 / (rdec_avg_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
     decode_gbs = world * kv_bytes_per_launch * L * steps / (elapsed_ms / 1e3) / 1e9
     # append: bf16 in (2 x 256 B per vector pair of K,V), packed words + sigma out
@@ -455,6 +469,10 @@ def run_ours(args):
                          "frac": achieved / peak, "traffic": profile_traffic(),
                          "kernel": "k_decode_pair<4, fused>", "avg_launch_us": dec_avg_ms * 1e3, "launches": dec_n,
                          "bytes_per_launch": kv_bytes_timed, "peak_source": f"{peak_kind} hbm_gbs"},
+            "weights_rotated": {"flags": "LC_Q_ROTATED | LC_OUT_ROTATED (R folded into Wq / Wo as in the "
+                                         "reference's Gemma path)",
+                                "avg_launch_us": rdec_avg_ms * 1e3, "achieved_gbs": rot_achieved,
+                                "frac": rot_achieved / peak, "launches": rdec_n},
             "cpu_baseline": cpu,
             "e2e": {"value": world * B / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1e3, "per": "GPU (bytes), whole job (value)",
