@@ -661,6 +661,12 @@ def run_window(args):
         ev1.record()
         ev1.synchronize()
     ms_step = ev0.elapsed_time(ev1) / steps
+    # per-launch device times (CUDA events around each launch), a separate pass
+    t_steps = max(2, min(steps, 5))
+    cache.timing(1)
+    for _ in range(t_steps):
+        step()
+    dec_ms, dec_n, app_ms, app_n, other_ms = cache.timing(0)
     bpt = 8 * lc.packed_words(D, 3) + 8 * lc.packed_words(D, 2) + 8  # 176 B per (token, kv head)
     kv_bytes = B * hkv * bpt * sum(views)
     print(json.dumps({
@@ -671,6 +677,8 @@ def run_window(args):
                                f"(ring {win}, wrapped 4x) + 1 global layer ({glob_ctx} tokens); append + decode "
                                f"per layer", "views": views},
         "decode_gbs": kv_bytes / (ms_step / 1e3) / 1e9, "bytes_per_token_head": bpt,
+        "breakdown_ms_per_step": {"decode_attn": dec_ms / t_steps, "append": app_ms / t_steps,
+                                  "other_kernels (query rotation, merge)": other_ms / t_steps},
         "clocks": clk.summary(), "fill_s": fill_s,
     }), flush=True)
     cache.close()

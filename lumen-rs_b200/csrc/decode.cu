@@ -100,12 +100,16 @@ __device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v
 }
 
 // ---------------------------------------------------------------------------
-// q' = R q * qscale for kRotRows rows per block of head_dim threads: thread
-// i computes output i of every row, reading R^T[j][i] straight from global
-// memory (coalesced; R^T is L2-resident) and the rows from shared memory
-// (broadcast). Small blocks keep the whole GPU busy at decode batch sizes.
+// q' = R q * qscale for kRotRows rows per block: block (x, y) takes rows
+// kRotRows x .. + kRotRows - 1 and output dims 64 y .. 64 y + 63. Its 256
+// threads are 4 slices of 64: slice js sums j in [js D/4, (js + 1) D/4) for
+// its output dim, reading R^T[j][i] straight from global memory (coalesced;
+// R^T is L2-resident) and the rows from shared memory (broadcast); the four
+// partial sums are added through shared memory. So a thread makes one round
+// trip for the rows and one or two for R^T, and many SMs are busy at decode
+// batch sizes, each reading only its columns of R^T.
 // ---------------------------------------------------------------------------
-constexpr int kRotRows = 8;
+constexpr int kRotRows = 8, kRotDims = 64, kRotSplit = 4;
 // acc[r] += sum_{u < C} M[(j0 + u) * D + i] * x[r][j0 + u] for NR rows of x in
 // shared memory (row stride D): the C loads of M are all in flight before the
 // first multiply, one L2 round trip per call.
@@ -133,36 +137,60 @@ __device__ __forceinline__ void mat_col(const float* __restrict__ M, int D, int 
   if (j0 < D) mat_chunk<32, NR>(M, D, i, j0, x, acc);
 }
 
-__global__ void __launch_bounds__(512) k_rotate_q(const void* q, int dtype, int n_rows, int D, const float* RT,
-                                                  int rotated, float qscale, float* q_rot, __half* q_h) {
-  extern __shared__ __align__(16) float sq[];  // [kRotRows][D]
-  const int i = threadIdx.x;
+__global__ void __launch_bounds__(kRotDims * kRotSplit) k_rotate_q(const void* q, int dtype, int n_rows, int D,
+                                                                const float* RT, int rotated, float qscale,
+                                                                float* q_rot, __half* q_h) {
+  extern __shared__ __align__(16) float sq[];  // [kRotRows][D], then [kRotSplit][kRotRows][kRotDims]
+  float* red = sq + kRotRows * D;
+  const int il = threadIdx.x % kRotDims, js = threadIdx.x / kRotDims;
+  const int i = blockIdx.y * kRotDims + il;
   const int r0 = blockIdx.x * kRotRows;
-  {  // blockDim.x == D: thread i loads column i of the kRotRows rows
-    int64_t idx[kRotRows];
-    bool ok[kRotRows];
-    float v[kRotRows];
+  // the kRotRows rows, 8 loads per thread in flight at a time
+  for (int k0 = threadIdx.x; k0 < kRotRows * D; k0 += 8 * blockDim.x) {
+    int64_t idx[8];
+    bool ok[8];
+    float v[8];
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r) {
-      idx[r] = (int64_t)(r0 + r) * D + i;
-      ok[r] = r0 + r < n_rows;
+    for (int u = 0; u < 8; ++u) {
+      const int k = k0 + u * blockDim.x;
+      idx[u] = (int64_t)r0 * D + k;
+      ok[u] = k < kRotRows * D && r0 + k / D < n_rows;
     }
     load_n_any(q, dtype, idx, ok, v);
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r) sq[r * D + i] = v[r];
+    for (int u = 0; u < 8; ++u) {
+      const int k = k0 + u * blockDim.x;
+      if (k < kRotRows * D) sq[k] = v[u];
+    }
   }
   __syncthreads();
-  float acc[kRotRows];
+  if (!rotated) {
+    float acc[kRotRows];
 #pragma unroll
-  for (int r = 0; r < kRotRows; ++r) acc[r] = rotated ? sq[r * D + i] : 0.0f;
-  if (!rotated) mat_col<kRotRows>(RT, D, i, sq, acc);
+    for (int r = 0; r < kRotRows; ++r) acc[r] = 0.0f;
+    const int jl = D / kRotSplit, jb = js * jl;
+    int j0 = jb;
+    for (; j0 + 64 <= jb + jl; j0 += 64) mat_chunk<64, kRotRows>(RT, D, i, j0, sq, acc);
+    for (; j0 + 16 <= jb + jl; j0 += 16) mat_chunk<16, kRotRows>(RT, D, i, j0, sq, acc);
 #pragma unroll
-  for (int r = 0; r < kRotRows; ++r) {
+    for (int r = 0; r < kRotRows; ++r) red[(js * kRotRows + r) * kRotDims + il] = acc[r];
+  }
+  __syncthreads();
+  // rows js, js + 4 of this block's 64 dims: the four slices' sums in order
+#pragma unroll
+  for (int rr = 0; rr < kRotRows / kRotSplit; ++rr) {
+    const int r = js + kRotSplit * rr;
     const int row = r0 + r;
+    float v = sq[r * D + i];
+    if (!rotated) {
+      v = red[(0 * kRotRows + r) * kRotDims + il];
+#pragma unroll
+      for (int t = 1; t < kRotSplit; ++t) v += red[(t * kRotRows + r) * kRotDims + il];
+    }
     if (row < n_rows) {
-      const float v = acc[r] * qscale;
-      q_rot[(int64_t)row * D + i] = v;
-      q_h[(int64_t)row * D + i] = __float2half_rn(v);
+      const float o = v * qscale;
+      q_rot[(int64_t)row * D + i] = o;
+      q_h[(int64_t)row * D + i] = __float2half_rn(o);
     }
   }
 }
@@ -1566,9 +1594,9 @@ struct MergeDev {
 // summed, four slots' loads in flight), each lane accumulating head_dim/32
 // contiguous dims. The block then un-rotates its rows: thread i computes
 // output dim i of 4 rows, reading R[j][i] straight from global memory
-// (coalesced, L2-resident).
-constexpr int kMergeWarps = 8;
-
+// (coalesced, L2-resident). W rows per block (a multiple of 4): 8, or 4 at
+// head_dim >= 256, where fewer rows per block put more SMs to work.
+template <int kMergeWarps>
 __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
   extern __shared__ __align__(16) float so[];  // [kMergeWarps][D]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1648,7 +1676,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
   __syncthreads();
   // out[row][i] = sum_j R[j][i] * o[row][j]
   const int r_lo = blockIdx.x * kMergeWarps;
-  for (int u = threadIdx.x; u < 2 * D; u += blockDim.x) {
+  for (int u = threadIdx.x; u < (kMergeWarps / 4) * D; u += blockDim.x) {
     const int i = u % D, rs = (u / D) * 4;
     float acc[4];
 #pragma unroll
@@ -1861,9 +1889,11 @@ void plan_decode_into(const int64_t* lens, int n, int hkv, int hq, int dim, int 
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* RT,
                      bool q_is_rotated, float qscale, float* q_rot, __half* q_h, cudaStream_t s) {
   if (n_rows <= 0) return;
-  const int blocks = (n_rows + kRotRows - 1) / kRotRows;
-  const size_t smem = (size_t)kRotRows * dim * sizeof(float);
-  k_rotate_q<<<blocks, dim, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
+  LC_REQUIRE(dim % 64 == 0, LC_ERR_INVALID, "decode: head_dim must be 64, 128, 256 or 512");
+  const dim3 grid((unsigned)((n_rows + kRotRows - 1) / kRotRows), (unsigned)(dim / kRotDims));
+  const size_t smem = ((size_t)kRotRows * dim + (size_t)kRotSplit * kRotRows * kRotDims) * sizeof(float);
+  k_rotate_q<<<grid, kRotDims * kRotSplit, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale,
+                                                      q_rot, q_h);
   LC_CUDA(cudaGetLastError());
 }
 
@@ -1997,26 +2027,33 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
   }
 }
 
+template <int W>
+static void launch_merge_w(const MergeDev& d, cudaStream_t s) {
+  const int blocks = (d.n_rows + W - 1) / W;
+  const size_t smem = (size_t)W * d.D * sizeof(float);
+  k_merge<W><<<blocks, W * 32, smem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
+}
+
+static void launch_merge_dev(const MergeDev& d, cudaStream_t s) {
+  if (d.D >= 256) launch_merge_w<4>(d, s);
+  else launch_merge_w<8>(d, s);
+}
+
 void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_slots, int32_t n_rows, int32_t dim,
                   const float* R, void* out, int32_t out_dtype, float* m_out, float* l_out, float* o_out,
                   float oscale, cudaStream_t s) {
   if (n_rows <= 0) return;
   MergeDev d{part, nullptr, nullptr, nullptr, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out,
              o_out};
-  const int blocks = (n_rows + kMergeWarps - 1) / kMergeWarps;
-  const size_t smem = (size_t)kMergeWarps * dim * sizeof(float);
-  k_merge<<<blocks, kMergeWarps * 32, smem, s>>>(d);
-  LC_CUDA(cudaGetLastError());
+  launch_merge_dev(d, s);
 }
 
 void launch_merge_parts(const float* m, const float* l, const float* o, int32_t n_parts, int32_t n_rows, int32_t dim,
                         const float* R, void* out, int32_t out_dtype, cudaStream_t s) {
   if (n_rows <= 0) return;
   MergeDev d{nullptr, m, l, o, nullptr, 1, n_parts, n_rows, dim, 1.0f, R, out, out_dtype, nullptr, nullptr, nullptr};
-  const int blocks = (n_rows + kMergeWarps - 1) / kMergeWarps;
-  const size_t smem = (size_t)kMergeWarps * dim * sizeof(float);
-  k_merge<<<blocks, kMergeWarps * 32, smem, s>>>(d);
-  LC_CUDA(cudaGetLastError());
+  launch_merge_dev(d, s);
 }
 
 }  // namespace lc
