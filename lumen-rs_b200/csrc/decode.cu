@@ -1353,8 +1353,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid
 
 // ---------------------------------------------------------------------------
 // Generic path: any bit width, head_dim = 32*KPL, GS query heads per CTA,
-// chunks of pages_per_chunk pages; partial slot = chunk. Each warp walks one
-// page at a time in tiles of gen_tt tokens (16 or 32), staged into shared
+// chunks of pages_per_chunk pages; partial slot = chunk. The warps of a block
+// take the chunk's tiles of gen_tt tokens (16 or 32) in turn, staged into shared
 // memory by a per-warp cp.async double buffer: K words, V words, sigma_K,
 // sigma_V of the tile are contiguous in the page, so a tile is three or four
 // flat 16-byte copies. Lane l owns dims l + 32k: its word index and bit
@@ -1427,24 +1427,30 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
         const int i = lane + 32 * r;
         pq[g][r] = (qjl && i < a.qjl_m) ? a.q_proj[((int64_t)s * a.hq + qh0 + g) * a.qjl_m + i] : 0.f;
       }
-    for (int pw = warp; pw < a.pages_per_chunk; pw += nw) {
-      const int64_t page_idx = (int64_t)chunk * a.pages_per_chunk + pw;
-      const int64_t tok0 = page_idx * kPageTokens;
-      if (tok0 >= n_valid) break;
-      const uint8_t* page = reinterpret_cast<const uint8_t*>(trow[page_idx]);
-      const uint8_t* kg = page + a.off_kw + (int64_t)kvh * kPageTokens * a.row_kw;
-      const uint8_t* vg = page + a.off_vw + (int64_t)kvh * kPageTokens * a.row_vw;
-      const uint8_t* ksg = page + a.off_ks + (int64_t)kvh * kPageTokens * 4;
-      const uint8_t* vsg = page + a.off_vs + (int64_t)kvh * kPageTokens * 4;
-      const uint64_t* kq = qjl ? reinterpret_cast<const uint64_t*>(page + a.off_kq + (int64_t)kvh * kPageTokens * a.row_kq)
-                               : nullptr;
-      const float* kr = qjl ? reinterpret_cast<const float*>(page + a.off_kr) + (int64_t)kvh * kPageTokens : nullptr;
-      const int nt = (int)(n_valid - tok0 < kPageTokens ? n_valid - tok0 : kPageTokens);
-      const int ntiles = (nt + TT - 1) / TT;
-      // whole tiles are copied: rows past n_valid exist in the page and are not used
-      auto issue = [&](int tl, int stg) {
+    {
+      // The chunk's 32- (or 16-) token tiles, strided over the warps: tile t
+      // is rows (t % tpp) TT .. of page chunk * pages_per_chunk + t / tpp,
+      // whose address lane t / tpp holds. Whole tiles are copied: rows past
+      // n_valid exist in the page and are not used.
+      const int64_t p0 = (int64_t)chunk * a.pages_per_chunk;
+      const int64_t ctok = n_valid - p0 * kPageTokens;
+      const int64_t cmax = (int64_t)a.pages_per_chunk * kPageTokens;
+      const int chunk_tok = (int)(ctok <= 0 ? 0 : (ctok < cmax ? ctok : cmax));
+      const int tpp = kPageTokens / TT;
+      const int ctiles = (chunk_tok + TT - 1) / TT;
+      const uint64_t my_page =
+          lane < a.pages_per_chunk && (p0 + lane) * kPageTokens < n_valid ? trow[p0 + lane] : 0ull;
+      auto page_of = [&](int t) {
+        return reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, my_page, t / tpp));
+      };
+      auto issue = [&](int t, int stg) {
+        const uint8_t* page = page_of(t);
+        const uint8_t* kg = page + a.off_kw + (int64_t)kvh * kPageTokens * a.row_kw;
+        const uint8_t* vg = page + a.off_vw + (int64_t)kvh * kPageTokens * a.row_vw;
+        const uint8_t* ksg = page + a.off_ks + (int64_t)kvh * kPageTokens * 4;
+        const uint8_t* vsg = page + a.off_vs + (int64_t)kvh * kPageTokens * 4;
         const uint32_t dst = st_s + stg * a.gen_stage;
-        const int r0 = tl * TT;
+        const int r0 = (t % tpp) * TT;
         for (int c = lane; c * 16 < kbytes; c += 32) cp_async16(dst + c * 16, kg + (int64_t)r0 * a.row_kw + c * 16);
         for (int c = lane; c * 16 < vbytes; c += 32)
           cp_async16(dst + kbytes + c * 16, vg + (int64_t)r0 * a.row_vw + c * 16);
@@ -1455,21 +1461,26 @@ __global__ void __launch_bounds__(128) k_decode_generic(const __grid_constant__ 
         }
         cp_commit();
       };
-      issue(0, 0);
-      for (int tl = 0; tl < ntiles; ++tl) {
-        if (tl + 1 < ntiles) {
-          issue(tl + 1, (tl + 1) & 1);
+      if (warp < ctiles) issue(warp, 0);
+      for (int t = warp, it = 0; t < ctiles; t += nw, ++it) {
+        if (t + nw < ctiles) {
+          issue(t + nw, (it + 1) & 1);
           cp_wait_one();
         } else {
           cp_wait_all();
         }
         __syncwarp();
-        const uint8_t* st = stage0 + (tl & 1) * a.gen_stage;
+        const uint8_t* st = stage0 + (it & 1) * a.gen_stage;
         const uint64_t* kw = reinterpret_cast<const uint64_t*>(st);
         const uint64_t* vw = reinterpret_cast<const uint64_t*>(st + kbytes);
         const float* ks = reinterpret_cast<const float*>(st + kbytes + vbytes);
         const float* vs = ks + TT;
-        const int cnt = min(TT, nt - tl * TT);
+        const int tl = t % tpp;
+        const uint8_t* page = page_of(t);
+        const uint64_t* kq = qjl ? reinterpret_cast<const uint64_t*>(page + a.off_kq + (int64_t)kvh * kPageTokens * a.row_kq)
+                                 : nullptr;
+        const float* kr = qjl ? reinterpret_cast<const float*>(page + a.off_kr) + (int64_t)kvh * kPageTokens : nullptr;
+        const int cnt = min(TT, chunk_tok - t * TT);
         for (int tt = 0; tt < cnt; ++tt) {
           float part[GS];
 #pragma unroll
@@ -1842,8 +1853,12 @@ DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int di
     int64_t mx = 0;
     for (int64_t L : lens) mx = L > mx ? L : mx;
     const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
-    p.pages_per_chunk = 4;
-    p.n_chunks = (int32_t)((pages + 3) / 4 > 0 ? (pages + 3) / 4 : 1);
+    // 4 pages per chunk, or fewer when that leaves too few (sequence, kv
+    // head, chunk) items to fill the GPU (short contexts, sliding windows)
+    int ppc = 4;
+    while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < 8LL * num_sms()) ppc >>= 1;
+    p.pages_per_chunk = ppc;
+    p.n_chunks = (int32_t)((pages + ppc - 1) / ppc > 0 ? (pages + ppc - 1) / ppc : 1);
     p.max_slots = p.n_chunks;
     for (auto& c : p.cnt) c = p.n_chunks;
   }
