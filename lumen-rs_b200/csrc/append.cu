@@ -322,6 +322,7 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
 // products in parallel and added in order by lane 0 (the same f32 result
 // as the reference's fold). Operation order as k_append_strict.
 constexpr int kWarpVecs = 4;
+constexpr int kRtChunk = 32;  // rows of R^T per shared-memory chunk when R^T does not fit
 
 __device__ __forceinline__ float seq_sum(const float* v, int n, float init) {
   float s = init;
@@ -392,25 +393,58 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   __syncthreads();
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const int64_t v = (int64_t)blockIdx.x * kWarpVecs + warp;
-  if (v >= n_vec) return;  // no block-wide barrier after this point
+  const bool active = v < n_vec;
+  if (TAB && !active) return;  // TAB: no block-wide barrier after this point
   const void* src = a.src[side];
+  if (active) {
 #pragma unroll
-  for (int r = 0; r < R; ++r) x[lane + 32 * r] = load_elem(src, a.dtype, v * D + lane + 32 * r);
-  __syncwarp();
-  if (side == 0 && a.rope_cs) {
-    const int64_t slot = (v / ((int64_t)a.h_in * a.n_tok)) * a.n_tok + v % a.n_tok;
-    for (int i = lane; i < a.rope_half; i += 32) rope_pair(x, a, slot, i);
+    for (int r = 0; r < R; ++r) x[lane + 32 * r] = load_elem(src, a.dtype, v * D + lane + 32 * r);
     __syncwarp();
+    if (side == 0 && a.rope_cs) {
+      const int64_t slot = (v / ((int64_t)a.h_in * a.n_tok)) * a.n_tok + v % a.n_tok;
+      for (int i = lane; i < a.rope_half; i += 32) rope_pair(x, a, slot, i);
+      __syncwarp();
+    }
   }
   // ---- rotated[i] = sum_j R[i][j] x[j] (rotation.rs:91-99) ----
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = -0.0f;
+  if constexpr (TAB) {
 #pragma unroll 4
-  for (int j = 0; j < D; ++j) {
-    const float xj = x[j];
+    for (int j = 0; j < D; ++j) {
+      const float xj = x[j];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(RT[j * D + lane + 32 * r], xj));
+      for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(RT[j * D + lane + 32 * r], xj));
+    }
+  } else {
+    // R^T does not fit: the block streams it through shared memory in
+    // chunks of kRtChunk rows (double-buffered cp.async), each chunk read
+    // by all of the block's vectors; the sum over j keeps its order
+    float* rbuf = reinterpret_cast<float*>(smem + 2048 + (size_t)kWarpVecs * (3 * D * 4 + 64 + D));
+    constexpr int NC = D / kRtChunk;
+    stage16(rbuf, c.RT, kRtChunk * D / 4);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    for (int ch = 0; ch < NC; ++ch) {
+      if (ch + 1 < NC) {
+        stage16(rbuf + ((ch + 1) & 1) * kRtChunk * D, c.RT + (size_t)(ch + 1) * kRtChunk * D, kRtChunk * D / 4);
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;\n" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      }
+      __syncthreads();
+      const float* rt = rbuf + (ch & 1) * kRtChunk * D;
+      if (active) {
+#pragma unroll 4
+        for (int jj = 0; jj < kRtChunk; ++jj) {
+          const float xj = x[ch * kRtChunk + jj];
+#pragma unroll
+          for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(rt[jj * D + lane + 32 * r], xj));
+        }
+      }
+      __syncthreads();  // the buffer is read before it is refilled
+    }
+    if (!active) return;  // no block-wide barrier after this point
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -516,7 +550,7 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
   const size_t base = 2048 + (size_t)kWarpVecs * (3 * D * 4 + 64 + D);
   const size_t tables = (size_t)D * D * 4 + (stage2 ? (size_t)(D * D + D * M) * 4 : 0);
   const bool tab = base + tables <= 200 * 1024;
-  const size_t smem = base + (tab ? tables : 0);
+  const size_t smem = base + (tab ? tables : (size_t)2 * kRtChunk * D * 4);
   static bool attr = false;
   if (!attr) {
     LC_CUDA(cudaFuncSetAttribute(k_append_warp<R, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
