@@ -169,3 +169,26 @@ def test_sparse_partials_path(lc, orc, gpu):
     out = cache.merge_partials(m[None], l[None], o[None]).reshape(fused.shape)
     np.testing.assert_allclose(out, fused, rtol=0, atol=2e-5)
     cache.close()
+
+
+def test_sparse_after_lkv2_reload_and_fork(lc, orc, gpu, tmp_path):
+    """A sequence loaded from an LKV2 snapshot re-digests its pages, and a
+    request forked from a long sequence (pages shared copy-on-write) digests
+    the shared pages again: both decode page-sparse exactly like the source."""
+    lens = [18000, 0, 0]
+    t, cache = _cache(lc, orc, lens)
+    refs, _ = _fill(cache, orc, t, lens[:1], 800)
+    q = helpers.queries(orc, 801, 1, HQ, DIM, std=DIM ** -0.5)
+    scale = 1.0 / np.sqrt(DIM)
+    src = cache.decode_attn(0, [0], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    p = tmp_path / "sparse.lkv"
+    cache.save_lkv2(0, p)
+    cache.load_lkv2(1, p)
+    loaded = cache.decode_attn(0, [1], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    np.testing.assert_array_equal(loaded, src)
+    cache.fork(0, 2, lens[0])
+    forked = cache.decode_attn(0, [2], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    np.testing.assert_array_equal(forked, src)
+    again = cache.decode_attn(0, [0], q, HQ, scale, flags=lc.LC_SPARSE_PAGES)
+    np.testing.assert_array_equal(again, src)  # the source is untouched by the fork's digests
+    cache.close()
