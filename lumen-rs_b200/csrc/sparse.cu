@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   float* ring = qx + G * D;                   // [warps][kSelStages][256] digest pages
   uint32_t* key = reinterpret_cast<uint32_t*>(ring + (kSelThreads / 32) * kSelStages * 256);  // [npad]
   uint64_t* pg = reinterpret_cast<uint64_t*>(key + ((a.npad + 1) & ~1));  // [npad / 4] page addresses
+  float* red = reinterpret_cast<float*>(pg + a.npad / kGroupsPerPage + 1);    // [4][G][D] rotation partials
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel[2];
 
@@ -145,17 +146,24 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
     sel_commit();
   }
 
-  // q'_i = sum_j R[i][j] q_j: thread t takes output dim i = t % 128 of heads
-  // t / 128, t / 128 + 4, ...; RT = R^T keeps each step's reads coalesced
-  for (int r = tid; r < G * D; r += NT) {
-    const int g = r / D, i = r % D;
-    float s = 0.f;
-    if (a.q_rotated) {
-      s = qx[r];
-    } else {
-#pragma unroll 16
-      for (int j = 0; j < D; ++j) s = fmaf(a.RT[j * D + i], qx[g * D + j], s);
+  // q'_i = sum_j R[i][j] q_j: thread t sums j in [32 (t / 128), + 32) for
+  // output dim i = t % 128 of every head (its 32 loads of R^T in flight
+  // together, coalesced); the 4 partial sums are added through shared memory
+  if (!a.q_rotated) {
+    const int i = tid % D, js = tid / D;
+    float rv[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) rv[u] = a.RT[(32 * js + u) * D + i];
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int u = 0; u < 32; ++u) s = fmaf(rv[u], qx[g * D + 32 * js + u], s);
+      red[(js * G + g) * D + i] = s;
     }
+    __syncthreads();
+  }
+  for (int r = tid; r < G * D; r += NT) {
+    const float s = a.q_rotated ? qx[r] : (red[r] + red[G * D + r]) + (red[2 * G * D + r] + red[3 * G * D + r]);
     qp[r] = fmaxf(s, 0.f);
     qn[r] = fminf(s, 0.f);
   }
@@ -338,7 +346,8 @@ void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t 
 void launch_page_select(const SelectDev& a, cudaStream_t s) {
   LC_REQUIRE(a.dim == 128 && a.G >= 1 && a.G <= 4, LC_ERR_INVALID, "page-sparse decode: head_dim 128, GQA <= 4");
   const size_t smem = (size_t)3 * a.G * a.dim * 4 + (size_t)(kSelThreads / 32) * kSelStages * 1024 +
-                      (size_t)((a.npad + 1) & ~1) * 4 + (size_t)(a.npad / kGroupsPerPage + 1) * 8;
+                      (size_t)((a.npad + 1) & ~1) * 4 + (size_t)(a.npad / kGroupsPerPage + 1) * 8 +
+                      (size_t)4 * a.G * a.dim * 4;
   static size_t max_dyn = 0;  // 227 KB less the static histogram
   if (max_dyn == 0) {
     cudaFuncAttributes fa;
