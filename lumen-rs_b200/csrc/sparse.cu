@@ -22,30 +22,43 @@ namespace lc {
 
 namespace {
 
-__device__ __forceinline__ int code_of(const uint64_t* words, int j, int bits) {
-  const int cpw = 64 / bits;
-  return (int)((words[j / cpw] >> ((j % cpw) * bits)) & ((1ull << bits) - 1));
-}
-
-// One CTA (head_dim threads) per (page group, head): item k of the list is
-// page address pages[k], first row row0[k] (a multiple of 64) within it.
+// One CTA (head_dim threads) per (page, head): item k of the list is page
+// address pages[k], first row row0[k] (a multiple of 64) within it. Thread d
+// takes dim d: its word and shift are fixed, the centroids sit in shared
+// memory, and 8 tokens' words and sigmas are loaded before they are used
+// (min and max do not depend on the order).
 __global__ void k_digest(DigestDev a) {
+  __shared__ float sc[256];
   const int64_t item = blockIdx.x;
   const int h = blockIdx.y;
   const int d = threadIdx.x;
+  for (int k = d; k < (1 << a.bits); k += blockDim.x) sc[k] = a.cent[k];
   const uint8_t* page = reinterpret_cast<const uint8_t*>(a.pages[item]);
   const int row0 = a.row0[item];
+  const int cpw = 64 / a.bits;
+  const int wi = d / cpw, sh = (d % cpw) * a.bits;
+  const uint64_t mask = (1ull << a.bits) - 1;
+  const int64_t hr0 = (int64_t)h * kPageTokens + row0;
+  const uint8_t* kw = page + a.off_kw + hr0 * a.row_kw + wi * 8;
+  const float* ks = reinterpret_cast<const float*>(page + a.off_ks) + hr0;
+  __syncthreads();
   float mn = FLT_MAX, mx = -FLT_MAX;
-  for (int t = 0; t < kDigestPage; ++t) {
-    const int64_t hr = (int64_t)h * kPageTokens + row0 + t;
-    const uint64_t* words = reinterpret_cast<const uint64_t*>(page + a.off_kw + hr * a.row_kw);
-    const float sigma = *reinterpret_cast<const float*>(page + a.off_ks + hr * 4);
-    const float v = __fmul_rn(a.cent[code_of(words, d, a.bits)], sigma);
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
+  for (int t0 = 0; t0 < kDigestPage; t0 += 8) {
+    uint64_t w[8];
+    float sg[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      w[u] = *reinterpret_cast<const uint64_t*>(kw + (int64_t)(t0 + u) * a.row_kw);
+      sg[u] = ks[t0 + u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float v = __fmul_rn(sc[(int)((w[u] >> sh) & mask)], sg[u]);
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
   }
-  float* dg = reinterpret_cast<float*>(const_cast<uint8_t*>(page) + a.off_dg +
-                                       ((int64_t)h * kPageTokens + row0) * a.row_dg);
+  float* dg = reinterpret_cast<float*>(const_cast<uint8_t*>(page) + a.off_dg + hr0 * a.row_dg);
   dg[d] = mn;
   dg[a.dim + d] = mx;
 }
