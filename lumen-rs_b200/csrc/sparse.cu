@@ -63,6 +63,66 @@ __global__ void k_digest(DigestDev a) {
   dg[a.dim + d] = mx;
 }
 
+// The 4-bit, head_dim 128 digest (the page-sparse geometry): a warp per
+// (page, head), 4 warps (heads) per block. Lane l reads word l % 8 of token
+// rows l / 8, + 4, + 8, ... (each load instruction covers 4 whole 64-byte
+// rows), keeps the min and max of its word's 16 dims, and the 4 lanes that
+// share a word combine theirs at the end.
+__global__ void __launch_bounds__(128) k_digest4(DigestDev a, int heads) {
+  __shared__ float sc[16];
+  if (threadIdx.x < 16) sc[threadIdx.x] = a.cent[threadIdx.x];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * 4 + warp;
+  if (h >= heads) return;
+  const uint8_t* page = reinterpret_cast<const uint8_t*>(a.pages[blockIdx.x]);
+  const int64_t hr0 = (int64_t)h * kPageTokens + a.row0[blockIdx.x];
+  const int lt = lane >> 3, lw = lane & 7;
+  const uint8_t* kw = page + a.off_kw + (hr0 + lt) * 64 + lw * 8;
+  const float* ks = reinterpret_cast<const float*>(page + a.off_ks) + hr0 + lt;
+  float mn[16], mx[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    mn[k] = FLT_MAX;
+    mx[k] = -FLT_MAX;
+  }
+#pragma unroll 1
+  for (int t0 = 0; t0 < kDigestPage; t0 += 16) {
+    uint2 w[4];
+    float sg[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      w[u] = *reinterpret_cast<const uint2*>(kw + (int64_t)(t0 + 4 * u) * 64);
+      sg[u] = ks[t0 + 4 * u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t half = k < 8 ? w[u].x : w[u].y;
+        const float v = __fmul_rn(sc[(half >> (4 * (k & 7))) & 15u], sg[u]);
+        mn[k] = fminf(mn[k], v);
+        mx[k] = fmaxf(mx[k], v);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    mn[k] = fminf(mn[k], __shfl_xor_sync(0xffffffffu, mn[k], 8));
+    mn[k] = fminf(mn[k], __shfl_xor_sync(0xffffffffu, mn[k], 16));
+    mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], 8));
+    mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], 16));
+  }
+  if (lt == 0) {
+    float4* dg = reinterpret_cast<float4*>(const_cast<uint8_t*>(page) + a.off_dg + hr0 * a.row_dg);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      dg[4 * lw + k] = make_float4(mn[4 * k], mn[4 * k + 1], mn[4 * k + 2], mn[4 * k + 3]);
+      dg[32 + 4 * lw + k] = make_float4(mx[4 * k], mx[4 * k + 1], mx[4 * k + 2], mx[4 * k + 3]);
+    }
+  }
+}
+
 // Query element i of an f32 / bf16 / f16 array.
 __device__ __forceinline__ float q_elem(const void* p, int dtype, int64_t i) {
   if (dtype == LC_F32) return reinterpret_cast<const float*>(p)[i];
@@ -352,7 +412,11 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
 
 void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t s) {
   if (n_items <= 0) return;
-  k_digest<<<dim3((unsigned)n_items, (unsigned)heads), a.dim, 0, s>>>(a);
+  if (a.bits == 4 && a.dim == 128 && a.row_kw == 64) {
+    k_digest4<<<dim3((unsigned)n_items, (unsigned)((heads + 3) / 4)), 128, 0, s>>>(a, heads);
+  } else {
+    k_digest<<<dim3((unsigned)n_items, (unsigned)heads), a.dim, 0, s>>>(a);
+  }
   LC_CUDA(cudaGetLastError());
 }
 
