@@ -339,6 +339,9 @@ int lc_prefill_attn(lc_cache* cache, int32_t layer, int32_t seq, const void* q, 
  *  - Every call on a device, from any cache, uses the same scratch: calls
  *    that overlap on the GPU (issued on different streams without ordering)
  *    race and return wrong results. Issue them on one stream, or order them.
+ *    A NULL stream means the cache's own stream, which differs between
+ *    caches: a caller with several caches on one device passes them one
+ *    shared stream, or orders the calls itself.
  *  - The kernels it launches are not timed by lc_cache_timing. */
 int lc_decode_attn_noalloc(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
                            const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags,

@@ -1281,6 +1281,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   a.vcent = c->dv.cent_d;
   a.kalpha = kalpha;
   a.valpha = valpha;
+  a.klo_thr = decode_klo_thr(c->dk.lo_max);
   a.part = c->part.p;
   if (sparse) {
     a.tile_map = c->tile_map.p;
@@ -1575,6 +1576,7 @@ int lc_decode_attn_noalloc(lc_cache* c, int32_t layer, int32_t n_seqs, const int
     a.vcent = c->dv.cent_d;
     a.kalpha = kalpha;
     a.valpha = valpha;
+    a.klo_thr = decode_klo_thr(c->dk.lo_max);
     a.part = part;
     launch_decode_partials(a, plan, s);
     ++c->launches;

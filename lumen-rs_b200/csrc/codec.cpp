@@ -305,6 +305,13 @@ void CodecOnDevice::upload(const Codec& c) {
   up(thr_d, thr);
   up(cent_d, cent);
   alpha = c.bits <= 4 ? f16_table_scale(c.cents) : 1.0f;
+  lo_max = 0.0f;
+  for (size_t k = 0; k < n; ++k) {
+    const float x = cent[k] * alpha;  // the f32 product the kernels round to f16
+    const double ax = std::fabs((double)x);
+    if (ax == 0) continue;
+    lo_max = std::max(lo_max, (float)std::fabs(round_f16(ax) - ax));
+  }
 }
 
 void CodecOnDevice::free() {

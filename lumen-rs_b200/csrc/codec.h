@@ -38,6 +38,10 @@ struct CodecOnDevice {
   // rounds to f16 with the smallest worst-case relative error over the
   // codebook (1 when not searched). Scores and outputs divide it back out.
   float alpha = 1.0f;
+  // Largest |alpha c_k - f16(alpha c_k)| over the codebook (alpha c_k taken in
+  // f32, as the kernels form it): the scale of the f16 table's rounding,
+  // which the decode's score-precision test weighs against the query norm.
+  float lo_max = 0.0f;
   float* R = nullptr;
   float* RTd = nullptr;
   float* PTd = nullptr;

@@ -234,6 +234,7 @@ struct DecodeDev {
   const float* kcent;
   const float* vcent;
   float kalpha, valpha;
+  float klo_thr;  // precise-score threshold numerator (DecodeArgs::klo_thr)
   float* part;
   // fused path (k_decode_pair<G, true>)
   const void* q_in;
@@ -493,9 +494,10 @@ struct PrefetchProducer {
   }
 };
 
-// 16 tokens of the tile (rows r0..r0+15): S^T = K_dq Q^T into sc.
-__device__ __forceinline__ void qk16(const uint8_t* st, int r0, int g, int t, uint32_t lanebase,
-                                     const uint32_t (&qb)[8][2], float* sc) {
+// 16 tokens (rows r0..r0+15): S^T = K_dq (Q_hi + Q_lo)^T into sc, two MMAs
+// per K fragment (the f16 value and residual of every query element).
+__device__ __forceinline__ void qk16_hl(const uint8_t* st, int r0, int g, int t, uint32_t lanebase,
+                                        const uint32_t (&qb)[8][2], const uint32_t (&ql)[8][2], float* sc) {
   const uint4 k0 = *reinterpret_cast<const uint4*>(st + kStK + (r0 + g) * 64 + 16 * t);
   const uint4 k1 = *reinterpret_cast<const uint4*>(st + kStK + (r0 + g + 8) * 64 + 16 * t);
   const uint32_t kx[4] = {k0.x, k0.y, k0.z, k0.w};
@@ -509,7 +511,61 @@ __device__ __forceinline__ void qk16(const uint8_t* st, int r0, int g, int t, ui
       const uint32_t a1 = lut_k(ky[j], lanebase, 2 * h);
       const uint32_t a3 = lut_k(ky[j], lanebase, 2 * h + 1);
       mma16816(sc, a0, a1, a2, a3, qb[2 * j + h][0], qb[2 * j + h][1]);
+      mma16816(sc, a0, a1, a2, a3, ql[2 * j + h][0], ql[2 * j + h][1]);
     }
+  }
+}
+
+// ---- K table residuals (f32-accurate scores) ----
+// The f16 table holds alpha c_k rounded; its residuals r_k = alpha c_k -
+// f16(alpha c_k) (exact in f32), scaled by 2^11 to stay normal f16 numbers,
+// sit in a 16-entry table with one copy per lane: entry (code n, lane l) at
+// byte n * 128 + l * 4, r_n in both f16 halves, so lookups are
+// conflict-free. A tile that needs the precision multiplies the residuals of
+// its codes by the same Q^T fragments and adds 2^-11 times the product.
+constexpr float kLoScale = 2048.f, kLoUnscale = 1.f / 2048.f;
+constexpr int kLoTabWords = 16 * 32;
+
+// Entry idx (< 512) of the residual table: code idx / 32, lane idx % 32.
+__device__ __forceinline__ void build_klo(uint32_t* tab, const DecodeDev& a, int idx) {
+  const float x = a.kcent[idx >> 5] * a.kalpha;  // the f32 product the f16 table rounds
+  const float r = (x - __half2float(__float2half_rn(x))) * kLoScale;
+  tab[idx] = h2_as_u32(__floats2half2_rn(r, r));
+}
+
+// Residual pair of byte k of x (the two codes of one A-fragment register):
+// low nibble -> low half, high nibble -> high half. lane4 = lane * 4.
+__device__ __forceinline__ uint32_t klo_pair(const uint32_t* tab, uint32_t x, int k, uint32_t lane4) {
+  auto off = [&](int p) {  // byte offset of the entry of the nibble at bit p
+    const uint32_t v = p >= 7 ? (x >> (p - 7)) : (x << (7 - p));
+    return (v & 0x780u) | lane4;
+  };
+  const char* base = reinterpret_cast<const char*>(tab);
+  const uint32_t e0 = *reinterpret_cast<const uint32_t*>(base + off(8 * k));
+  const uint32_t e1 = *reinterpret_cast<const uint32_t*>(base + off(8 * k + 4));
+  return __byte_perm(e0, e1, 0x7610);
+}
+
+// 16 tokens (rows r0..r0+15): c += Kres Q^T with the K fragments of qk16_2.
+// Not unrolled, one code word per row at a time: it runs inside the main
+// loop with everything else live, and must not raise the loop's register
+// demand (its tiles are the minority, and only in peaked regimes).
+__device__ __forceinline__ void qk16_lo(const uint8_t* st, int r0, int g, int t, const uint32_t* tab,
+                                        uint32_t lane4, const uint32_t (&qb)[8][2], float* c) {
+  const uint32_t* kr0 = reinterpret_cast<const uint32_t*>(st + kStK + (r0 + g) * 64 + 16 * t);
+  const uint32_t* kr1 = kr0 + 128;  // row + 8
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t kx = kr0[j], ky = kr1[j];
+    uint32_t b00, b01, b10, b11;  // qb[2j], qb[2j + 1], picked without dynamic indexing
+    b00 = qb[0][0]; b01 = qb[0][1]; b10 = qb[1][0]; b11 = qb[1][1];
+    if (j == 1) { b00 = qb[2][0]; b01 = qb[2][1]; b10 = qb[3][0]; b11 = qb[3][1]; }
+    if (j == 2) { b00 = qb[4][0]; b01 = qb[4][1]; b10 = qb[5][0]; b11 = qb[5][1]; }
+    if (j == 3) { b00 = qb[6][0]; b01 = qb[6][1]; b10 = qb[7][0]; b11 = qb[7][1]; }
+    mma16816(c, klo_pair(tab, kx, 0, lane4), klo_pair(tab, ky, 0, lane4), klo_pair(tab, kx, 1, lane4),
+             klo_pair(tab, ky, 1, lane4), b00, b01);
+    mma16816(c, klo_pair(tab, kx, 2, lane4), klo_pair(tab, ky, 2, lane4), klo_pair(tab, kx, 3, lane4),
+             klo_pair(tab, ky, 3, lane4), b10, b11);
   }
 }
 
@@ -796,6 +852,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
   pr.win_t0 = 0;
   float* qs = reinterpret_cast<float*>(smem + kFlatSmem);  // [kFusedRows][D]
   __shared__ int merged[kFusedSegs];
+  __shared__ uint32_t s_klo[kLoTabWords];  // K table residuals (precise tiles)
   // first (sequence, kv head) segment of this CTA and its query-row count,
   // kept in shared memory (read once per segment; no register in the loop)
   __shared__ int cta_seg[2];
@@ -834,9 +891,11 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       sid0 = f.b * a.hkv + f.kvh;
       nrows = (e.b * a.hkv + e.kvh - sid0 + 1) * G;
     }
-    // the centroid-pair table from constants, while the reads above are in
-    // flight (read only after the barrier that follows the rotation)
+    // the centroid-pair and residual tables from constants, while the reads
+    // above are in flight (read only after the barrier that follows the
+    // rotation)
     build_lut(lut, cl);
+    build_klo(s_klo, a, threadIdx.x);
   }
   // fused: everything above reads constants (codec tables, launch
   // parameters, the block table); the queries, the cache pages, the arrival
@@ -911,6 +970,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     }
   } else {
     build_lut(lut, cl);
+    build_klo(s_klo, a, threadIdx.x);
   }
   __syncthreads();  // the table, and the fused q' rows
   if (!FUSED && begin >= end) return;  // no block-wide barrier after this point
@@ -931,6 +991,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
     const int seg_end = min(end, seg_first + cw.nt);
     // B fragments of Q: column g = (head g/2, part g&1), dims 32t + 4s + {0,1} / {2,3}
     uint32_t qb[8][2];
+    float ss = 0.f;
     {
       const int head = g >> 1;
       const bool lo = g & 1;
@@ -949,8 +1010,16 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
         }
         qb[s][0] = head < G ? r0 : 0u;
         qb[s][1] = head < G ? r1 : 0u;
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
       }
     }
+    // precise tiles need sigma_K > lthr: ||q'|| of the group's largest row
+    // (lanes t = 0..3 of head g / 2 hold its 128 dims)
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss = fmaxf(ss, __shfl_xor_sync(0xffffffffu, ss, 8));
+    ss = fmaxf(ss, __shfl_xor_sync(0xffffffffu, ss, 16));
+    const float lthr = a.klo_thr * rsqrtf(ss);
     float m = -INFINITY, l = 0.f;
     float oacc[8][4];
 #pragma unroll
@@ -970,10 +1039,28 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
       // this lane: head t, tokens u0 = g, u1 = g + 8, u2 = 16 + g, u3 = 24 + g
       const bool ok0 = !MASKED || tok + g < n_valid, ok1 = !MASKED || tok + g + 8 < n_valid;
       const bool ok2 = !MASKED || tok + g + 16 < n_valid, ok3 = !MASKED || tok + g + 24 < n_valid;
-      const float z0 = ((sa0[0] + sa1[0]) + (sa0[1] + sa1[1])) * ks[g];
-      const float z1 = ((sa0[2] + sa1[2]) + (sa0[3] + sa1[3])) * ks[g + 8];
-      const float z2 = ((sb0[0] + sb1[0]) + (sb0[1] + sb1[1])) * ks[g + 16];
-      const float z3 = ((sb0[2] + sb1[2]) + (sb0[3] + sb1[3])) * ks[g + 24];
+      const float k0 = ks[g], k1 = ks[g + 8], k2 = ks[g + 16], k3 = ks[g + 24];
+      float y0 = (sa0[0] + sa1[0]) + (sa0[1] + sa1[1]);
+      float y1 = (sa0[2] + sa1[2]) + (sa0[3] + sa1[3]);
+      float y2 = (sb0[0] + sb1[0]) + (sb0[1] + sb1[1]);
+      float y3 = (sb0[2] + sb1[2]) + (sb0[3] + sb1[3]);
+      // f32-accurate scores where the f16 table's rounding could move the
+      // softmax: large sigma_K x ||q'||, and a score near the running max
+      if (__any_sync(0xffffffffu, t < G && fmaxf(fmaxf(k0, k1), fmaxf(k2, k3)) > lthr)) {
+        const float zm = fmaxf(fmaxf(ok0 ? y0 * k0 : -INFINITY, ok1 ? y1 * k1 : -INFINITY),
+                               fmaxf(ok2 ? y2 * k2 : -INFINITY, ok3 ? y3 * k3 : -INFINITY));
+        if (__any_sync(0xffffffffu, t < G && fmaxf(fmaxf(k0, k1), fmaxf(k2, k3)) > lthr && zm > m - kLoTheta)) {
+          float la[4] = {0.f, 0.f, 0.f, 0.f};
+          qk16_lo(st, 0, g, t, s_klo, lanebase & 0xFFu, qb, la);
+          y0 = fmaf(la[0] + la[1], kLoUnscale, y0);
+          y1 = fmaf(la[2] + la[3], kLoUnscale, y1);
+          la[0] = la[1] = la[2] = la[3] = 0.f;
+          qk16_lo(st, 16, g, t, s_klo, lanebase & 0xFFu, qb, la);
+          y2 = fmaf(la[0] + la[1], kLoUnscale, y2);
+          y3 = fmaf(la[2] + la[3], kLoUnscale, y3);
+        }
+      }
+      const float z0 = y0 * k0, z1 = y1 * k1, z2 = y2 * k2, z3 = y3 * k3;
       const float s0_ = ok0 ? z0 : -INFINITY, s1_ = ok1 ? z1 : -INFINITY;
       const float s2_ = ok2 ? z2 : -INFINITY, s3_ = ok3 ? z3 : -INFINITY;
       // lazy rescale: the running max m moves only when some score exceeds it
@@ -1192,6 +1279,8 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid
   const uint32_t lut_off = (65536u - (s0 & 0xFFFFu)) & 0xFFFFu;
   const int n_before = (int)(lut_off / kWarpBytes);
   uint8_t* lut = smem + lut_off;
+  __shared__ uint32_t s_klo[kLoTabWords];  // K table residuals (precise tiles)
+  build_klo(s_klo, a, threadIdx.x);
 
   for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
     const int e = idx >> 6, slot = idx & 63;
@@ -1203,6 +1292,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
+  const uint32_t lane4 = (uint32_t)lane << 2;
   const uint32_t lanebase = ((s0 + lut_off) & 0xFFFF0000u) | ((uint32_t)lane << 2);
   const int64_t w = (int64_t)blockIdx.x * kFlatWarps + warp;
   const int64_t begin = w * a.per_warp;
@@ -1235,16 +1325,30 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid
     const int64_t seg_first = a.sg()[b] + (int64_t)kvh * cw.nt;
     const int64_t seg_end = min(end, seg_first + cw.nt);
     const int64_t slot_base = ((int64_t)b * a.hkv + kvh) * a.max_slots + (w - seg_first / a.per_warp);
-    uint32_t qb[8][2];
+    // B fragments of Q (column g = head g): f16 values and residuals of the
+    // f32 rotated query, dims 32t + 4j + {0,1} / {2,3}
+    uint32_t qb[8][2], ql[8][2];
+    float ss = 0.f;
     {
-      const __half* qrow = a.q_h + ((int64_t)b * a.hq + (int64_t)kvh * G + (g < G ? g : 0)) * D;
+      const float* qrow = a.q_rot + ((int64_t)b * a.hq + (int64_t)kvh * G + (g < G ? g : 0)) * D + 32 * t;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(qrow + 32 * t + 4 * j);
-        qb[j][0] = g < G ? p[0] : 0u;
-        qb[j][1] = g < G ? p[1] : 0u;
+        const float4 v = *reinterpret_cast<const float4*>(qrow + 4 * j);
+        uint32_t h0, l0, h1, l1;
+        split_h2(v.x, v.y, h0, l0);
+        split_h2(v.z, v.w, h1, l1);
+        qb[j][0] = g < G ? h0 : 0u;
+        qb[j][1] = g < G ? h1 : 0u;
+        ql[j][0] = g < G ? l0 : 0u;
+        ql[j][1] = g < G ? l1 : 0u;
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
       }
     }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) ss = fmaxf(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float lthr = a.klo_thr * rsqrtf(ss);
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float oacc[8][4];
 #pragma unroll
@@ -1257,14 +1361,34 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_flat(const __grid
       const int tok = cw.tile * kTileTok;
       const uint8_t* st = stages + stage * kStageBytes;
       float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-      qk16(st, 0, g, t, lanebase, qb, sa);
-      qk16(st, 16, g, t, lanebase, qb, sb);
+      qk16_hl(st, 0, g, t, lanebase, qb, ql, sa);
+      qk16_hl(st, 16, g, t, lanebase, qb, ql, sb);
       const float* ks = reinterpret_cast<const float*>(st + kStKs);
       const float* vs = reinterpret_cast<const float*>(st + kStVs);
       // tokens of this thread: u0 = g, u1 = g+8, u2 = 16+g, u3 = 24+g
       const bool ok0 = !MASKED || tok + g < n_valid, ok1 = !MASKED || tok + g + 8 < n_valid;
       const bool ok2 = !MASKED || tok + g + 16 < n_valid, ok3 = !MASKED || tok + g + 24 < n_valid;
       const float k0 = ks[g], k1 = ks[g + 8], k2 = ks[g + 16], k3 = ks[g + 24];
+      // f32-accurate scores where the f16 table's rounding could move the
+      // softmax (see k_decode_pair)
+      const bool live0 = 2 * t < G, live1 = 2 * t + 1 < G;
+      if (__any_sync(0xffffffffu, live0 && fmaxf(fmaxf(k0, k1), fmaxf(k2, k3)) > lthr)) {
+        const float za = fmaxf(fmaxf(ok0 ? sa[0] * k0 : -INFINITY, ok1 ? sa[2] * k1 : -INFINITY),
+                               fmaxf(ok2 ? sb[0] * k2 : -INFINITY, ok3 ? sb[2] * k3 : -INFINITY));
+        const float zb = fmaxf(fmaxf(ok0 ? sa[1] * k0 : -INFINITY, ok1 ? sa[3] * k1 : -INFINITY),
+                               fmaxf(ok2 ? sb[1] * k2 : -INFINITY, ok3 ? sb[3] * k3 : -INFINITY));
+        const bool near = (live0 && za > m0 - kLoTheta) || (live1 && zb > m1 - kLoTheta);
+        if (__any_sync(0xffffffffu, near && fmaxf(fmaxf(k0, k1), fmaxf(k2, k3)) > lthr)) {
+          float la[4] = {0.f, 0.f, 0.f, 0.f}, lb[4] = {0.f, 0.f, 0.f, 0.f};
+          qk16_lo(st, 0, g, t, s_klo, lane4, qb, la);
+          qk16_lo(st, 16, g, t, s_klo, lane4, qb, lb);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            sa[e] = fmaf(la[e], kLoUnscale, sa[e]);
+            sb[e] = fmaf(lb[e], kLoUnscale, sb[e]);
+          }
+        }
+      }
       // s[u][e]: token u, head 2t+e (log2 domain)
       const float s00 = ok0 ? sa[0] * k0 : -INFINITY, s01 = ok0 ? sa[1] * k0 : -INFINITY;
       const float s10 = ok1 ? sa[2] * k1 : -INFINITY, s11 = ok1 ? sa[3] * k1 : -INFINITY;
@@ -1821,55 +1945,14 @@ static int32_t max_cta_segments(const int64_t* seg, const int64_t* lens, int n, 
   return (int32_t)mx;
 }
 
-DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits,
-                       bool generic_only) {
-  DecodePlan p;
-  const int G = hq / hkv;
-  const int n = (int)lens.size();
-  p.cnt.assign((size_t)n * hkv, 0);
-  if (!generic_only && decode_fast_path(dim, kbits, vbits, G)) {
-    p.flat = true;
-    p.grid = num_sms();
-    p.seg.assign(n + 1, 0);
-    for (int b = 0; b < n; ++b) p.seg[b + 1] = p.seg[b] + (int64_t)hkv * ((lens[b] + kTileTok - 1) / kTileTok);
-    p.total_tiles = p.seg[n];
-    const int64_t W = (int64_t)p.grid * kFlatWarps;
-    p.per_warp = p.total_tiles > 0 ? (p.total_tiles + W - 1) / W : 1;
-    int32_t mx = 1;
-    for (int b = 0; b < n; ++b) {
-      const int64_t nt = (lens[b] + kTileTok - 1) / kTileTok;
-      if (nt == 0) continue;
-      for (int h = 0; h < hkv; ++h) {
-        const int64_t s0 = p.seg[b] + (int64_t)h * nt;
-        const int32_t c = (int32_t)((s0 + nt - 1) / p.per_warp - s0 / p.per_warp + 1);
-        p.cnt[(size_t)b * hkv + h] = c;
-        mx = c > mx ? c : mx;
-      }
-    }
-    p.max_slots = mx;
-    p.max_cta_segs = max_cta_segments(p.seg.data(), lens.data(), n, hkv, p.total_tiles, p.per_warp, p.grid);
-  } else {
-    p.flat = false;
-    int64_t mx = 0;
-    for (int64_t L : lens) mx = L > mx ? L : mx;
-    const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
-    // 4 pages per chunk, or fewer when that leaves too few (sequence, kv
-    // head, chunk) items to fill the GPU (short contexts, sliding windows)
-    int ppc = 4;
-    while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < 8LL * num_sms()) ppc >>= 1;
-    p.pages_per_chunk = ppc;
-    p.n_chunks = (int32_t)((pages + ppc - 1) / ppc > 0 ? (pages + ppc - 1) / ppc : 1);
-    p.max_slots = p.n_chunks;
-    for (auto& c : p.cnt) c = p.n_chunks;
-  }
-  return p;
-}
-
-void plan_decode_into(const int64_t* lens, int n, int hkv, int hq, int dim, int kbits, int vbits, DecodePlan& p,
-                      int64_t* seg, int32_t* cnt) {
+// The partition of one decode call, written into seg [n + 1] (flat path) and
+// cnt [n * hkv]; shared by plan_decode (vectors it owns) and
+// plan_decode_into (caller arrays, no allocation).
+static void plan_core(const int64_t* lens, int n, int hkv, int hq, int dim, int kbits, int vbits, bool generic_only,
+                      DecodePlan& p, int64_t* seg, int32_t* cnt) {
   const int G = hq / hkv;
   for (int64_t i = 0; i < (int64_t)n * hkv; ++i) cnt[i] = 0;
-  if (decode_fast_path(dim, kbits, vbits, G)) {
+  if (!generic_only && decode_fast_path(dim, kbits, vbits, G)) {
     p.flat = true;
     p.grid = num_sms();
     seg[0] = 0;
@@ -1889,16 +1972,37 @@ void plan_decode_into(const int64_t* lens, int n, int hkv, int hq, int dim, int 
       }
     }
     p.max_slots = mx;
+    p.max_cta_segs = max_cta_segments(seg, lens, n, hkv, p.total_tiles, p.per_warp, p.grid);
   } else {
     p.flat = false;
     int64_t mx = 0;
     for (int b = 0; b < n; ++b) mx = lens[b] > mx ? lens[b] : mx;
     const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
-    p.pages_per_chunk = 4;
-    p.n_chunks = (int32_t)((pages + 3) / 4 > 0 ? (pages + 3) / 4 : 1);
+    // 4 pages per chunk, or fewer when that leaves too few (sequence, kv
+    // head, chunk) items to fill the GPU (short contexts, sliding windows)
+    int ppc = 4;
+    while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < 8LL * num_sms()) ppc >>= 1;
+    p.pages_per_chunk = ppc;
+    p.n_chunks = (int32_t)((pages + ppc - 1) / ppc > 0 ? (pages + ppc - 1) / ppc : 1);
     p.max_slots = p.n_chunks;
     for (int64_t i = 0; i < (int64_t)n * hkv; ++i) cnt[i] = p.n_chunks;
   }
+}
+
+DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits,
+                       bool generic_only) {
+  DecodePlan p;
+  const int n = (int)lens.size();
+  p.cnt.assign((size_t)n * hkv, 0);
+  p.seg.assign(n + 1, 0);
+  plan_core(lens.data(), n, hkv, hq, dim, kbits, vbits, generic_only, p, p.seg.data(), p.cnt.data());
+  if (!p.flat) p.seg.clear();
+  return p;
+}
+
+void plan_decode_into(const int64_t* lens, int n, int hkv, int hq, int dim, int kbits, int vbits, DecodePlan& p,
+                      int64_t* seg, int32_t* cnt) {
+  plan_core(lens, n, hkv, hq, dim, kbits, vbits, false, p, seg, cnt);
 }
 
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* RT,
@@ -1958,6 +2062,7 @@ static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
   d.vcent = a.vcent;
   d.kalpha = a.kalpha;
   d.valpha = a.valpha;
+  d.klo_thr = a.klo_thr;
   d.part = a.part;
   d.tile_map = a.tile_map;
   d.map_stride = a.map_stride;

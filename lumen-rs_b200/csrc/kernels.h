@@ -78,6 +78,11 @@ struct DecodeArgs {
   const float* kcent = nullptr;   // [2^kbits]
   const float* vcent = nullptr;   // [2^vbits]
   float kalpha = 1.0f, valpha = 1.0f;  // f16 table scales of the fast path
+  // Fast path score precision: a tile adds the K table's f16 residuals
+  // (alpha c_k - f16(alpha c_k)) to its scores when some token's sigma_K
+  // exceeds klo_thr / ||q'|| (q' = the head group's scaled rotated queries)
+  // and it lies within kLoTheta of the running max (decode_klo_thr).
+  float klo_thr = 0.0f;
   float* part = nullptr;          // [n_seqs][hkv][max_slots][G][dim + 2]  (m, l, o...)
   // With seqinfo == nullptr the per-call arrays are host copies passed in the
   // launch parameters (decode_inline_fits): seqinfo, seg, cnt as above.
@@ -209,6 +214,20 @@ void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_
 void launch_merge_parts(const float* m, const float* l, const float* o, int32_t n_parts, int32_t n_rows, int32_t dim,
                         const float* R, void* out, int32_t out_dtype, cudaStream_t s);
 bool decode_fast_path(int dim, int kbits, int vbits, int G);
+
+// Score precision of the fast path's f16 K table. The table rounds alpha c_k
+// by at most lo_max (CodecOnDevice::lo_max), so a score z_t (log2 units) is
+// off by about sigma_t * ||q'|| * lo_max. A tile whose largest such figure
+// exceeds kLoEta, and which holds a score within kLoTheta of its head's
+// running max, also multiplies the f16 residual table (the rounding errors,
+// scaled by 2^11) by q' on the tensor cores and adds it, which leaves the
+// scores f32-accurate. kLoEta sits between the figures of q ~ N(0, 1/d) and
+// of q ~ N(0, 1) at scale 1 (the reference's Gemma call, RMS-normalised q),
+// about 1.5e-3 and 1.7e-2 for 4-bit codes with x8 outlier channels; tokens
+// kLoTheta below the max weigh under 2^-20 of it.
+constexpr float kLoEta = 2e-3f;
+constexpr float kLoTheta = 20.0f;
+inline float decode_klo_thr(float lo_max) { return lo_max > 0.0f ? kLoEta / lo_max : 3.0e38f; }
 
 // ---- fixed scratch of lc_decode_attn_noalloc (noalloc.cu) -----------------
 // plan_decode's partition written into caller arrays seg [n + 1] (flat path

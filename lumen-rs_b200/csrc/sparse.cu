@@ -3,9 +3,9 @@
 // selection of sdpa_page_sparse (native_attention.rs:217-329), with the keys
 // taken as the decode sees them: rotated and dequantized, c[code] * sigma.
 //
-//   k_digest       min and max over each full 64-token page, per head and dim,
+//   k_digest4      min and max over each full 64-token page, per head and dim,
 //                  into the page's digest role (64 rows of head_dim / 8 bytes:
-//                  min[D] f32 then max[D] f32)
+//                  min[D] f32 then max[D] f32); 4-bit codes, head_dim 128
 //   k_page_select  per (sequence, kv head): bound of every digested page
 //                  = max over the head's query group of
 //                    sum_d max(q'_d * max_d, q'_d * min_d),
@@ -21,47 +21,6 @@
 namespace lc {
 
 namespace {
-
-// One CTA (head_dim threads) per (page, head): item k of the list is page
-// address pages[k], first row row0[k] (a multiple of 64) within it. Thread d
-// takes dim d: its word and shift are fixed, the centroids sit in shared
-// memory, and 8 tokens' words and sigmas are loaded before they are used
-// (min and max do not depend on the order).
-__global__ void k_digest(DigestDev a) {
-  __shared__ float sc[256];
-  const int64_t item = blockIdx.x;
-  const int h = blockIdx.y;
-  const int d = threadIdx.x;
-  for (int k = d; k < (1 << a.bits); k += blockDim.x) sc[k] = a.cent[k];
-  const uint8_t* page = reinterpret_cast<const uint8_t*>(a.pages[item]);
-  const int row0 = a.row0[item];
-  const int cpw = 64 / a.bits;
-  const int wi = d / cpw, sh = (d % cpw) * a.bits;
-  const uint64_t mask = (1ull << a.bits) - 1;
-  const int64_t hr0 = (int64_t)h * kPageTokens + row0;
-  const uint8_t* kw = page + a.off_kw + hr0 * a.row_kw + wi * 8;
-  const float* ks = reinterpret_cast<const float*>(page + a.off_ks) + hr0;
-  __syncthreads();
-  float mn = FLT_MAX, mx = -FLT_MAX;
-  for (int t0 = 0; t0 < kDigestPage; t0 += 8) {
-    uint64_t w[8];
-    float sg[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      w[u] = *reinterpret_cast<const uint64_t*>(kw + (int64_t)(t0 + u) * a.row_kw);
-      sg[u] = ks[t0 + u];
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float v = __fmul_rn(sc[(int)((w[u] >> sh) & mask)], sg[u]);
-      mn = fminf(mn, v);
-      mx = fmaxf(mx, v);
-    }
-  }
-  float* dg = reinterpret_cast<float*>(const_cast<uint8_t*>(page) + a.off_dg + hr0 * a.row_dg);
-  dg[d] = mn;
-  dg[a.dim + d] = mx;
-}
 
 // The 4-bit, head_dim 128 digest (the page-sparse geometry): a warp per
 // (page, head), 4 warps (heads) per block. Lane l reads word l % 8 of token
@@ -412,11 +371,11 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
 
 void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t s) {
   if (n_items <= 0) return;
-  if (a.bits == 4 && a.dim == 128 && a.row_kw == 64) {
-    k_digest4<<<dim3((unsigned)n_items, (unsigned)((heads + 3) / 4)), 128, 0, s>>>(a, heads);
-  } else {
-    k_digest<<<dim3((unsigned)n_items, (unsigned)heads), a.dim, 0, s>>>(a);
-  }
+  // page-sparse decode takes the fast-path geometry only (lc_decode_attn
+  // refuses the rest before digesting)
+  LC_REQUIRE(a.bits == 4 && a.dim == 128 && a.row_kw == 64, LC_ERR_INVALID,
+             "page digest: 4-bit codes, head_dim 128 only");
+  k_digest4<<<dim3((unsigned)n_items, (unsigned)((heads + 3) / 4)), 128, 0, s>>>(a, heads);
   LC_CUDA(cudaGetLastError());
 }
 

@@ -1,14 +1,15 @@
 """GPU: the path at BASELINE's full sizes, checked through size-independent
-properties plus one oracle slice.
+properties plus oracle slices.
 
 Config 1 (32 sequences x 8192 tokens, 32 q / 8 kv heads, d 128, 4-bit K/V,
 bf16 K/V with outlier channels, queries N(0, 1/sqrt(128)), scale 1):
 - the one-launch fused decode equals the partials path (split-K partials,
   then the slot merge and un-rotation of lc_merge_partials);
 - a sequence decoded alone equals its row of the batched decode;
-- one full (sequence, kv head) slice: codes and sigmas bit-exact against the
-  oracle's compressor, attention within the decode tolerance of the
-  oracle's attend_keys -> softmax -> attend_values.
+- 8 full (sequence, kv head) slices spread over the batch and the heads:
+  codes and sigmas bit-exact against the oracle's compressor, attention
+  within the decode tolerance of the oracle's attend_keys -> softmax ->
+  attend_values.
 
 Config 2 (d 256, 3-bit K / 2-bit V, 16 q / 8 kv heads, a 1024-token sliding
 ring wrapped 4x): decode over the wrapped ring equals decode over a fresh
@@ -71,24 +72,28 @@ def test_config1_full_size(lc, orc, gpu):
     one = cache.decode_attn(0, [b], q[b:b + 1].float().cpu().numpy(), HQ, 1.0)
     np.testing.assert_allclose(one[0], fused[b], rtol=0, atol=2e-5)
 
-    # the oracle on one full (sequence, kv head): codes, then attention
-    h = 3
-    Kh = K[b, h].float().cpu().numpy()
-    Vh = V[b, h].float().cpu().numpy()
-    ref = orc.SimpleCache(orc.Compressor(tk), orc.Compressor(tv), 1, 1, D)
-    ref.store(0, 0, Kh, Vh, N)
-    f = cache.fetch(b, 0)
-    words, _, _, sigma = ref.read(0, 0, 0)
-    np.testing.assert_array_equal(f["k_words"][h], words)
-    np.testing.assert_array_equal(f["k_sigma"][h].view(np.uint32), np.asarray(sigma, np.float32).view(np.uint32))
-    vwords, _, _, vsigma = ref.read(0, 0, 1)
-    np.testing.assert_array_equal(f["v_words"][h], vwords)
-    np.testing.assert_array_equal(f["v_sigma"][h].view(np.uint32), np.asarray(vsigma, np.float32).view(np.uint32))
+    # the oracle on 8 full (sequence, kv head) slices spread over the batch
+    # and the heads: codes and sigmas, then attention
     G = HQ // HKV
-    qb = q[b].float().cpu().numpy()
-    want = np.stack([ref.attend(0, 0, qb[h * G + g], 1.0) for g in range(G)])
-    ok, msg = helpers.attn_close(fused[b, h * G:(h + 1) * G], want)
-    assert ok, msg
+    ok_c, ok_v = orc.Compressor(tk), orc.Compressor(tv)
+    for b, h in [(0, 0), (5, 3), (9, 7), (14, 1), (18, 4), (23, 6), (27, 2), (31, 5)]:
+        Kh = K[b, h].float().cpu().numpy()
+        Vh = V[b, h].float().cpu().numpy()
+        ref = orc.SimpleCache(ok_c, ok_v, 1, 1, D)
+        ref.store(0, 0, Kh, Vh, N)
+        f = cache.fetch(b, 0)
+        words, _, _, sigma = ref.read(0, 0, 0)
+        np.testing.assert_array_equal(f["k_words"][h], words)
+        np.testing.assert_array_equal(f["k_sigma"][h].view(np.uint32),
+                                      np.asarray(sigma, np.float32).view(np.uint32))
+        vwords, _, _, vsigma = ref.read(0, 0, 1)
+        np.testing.assert_array_equal(f["v_words"][h], vwords)
+        np.testing.assert_array_equal(f["v_sigma"][h].view(np.uint32),
+                                      np.asarray(vsigma, np.float32).view(np.uint32))
+        qb = q[b].float().cpu().numpy()
+        want = np.stack([ref.attend(0, 0, qb[h * G + g], 1.0) for g in range(G)])
+        ok, msg = helpers.attn_close(fused[b, h * G:(h + 1) * G], want)
+        assert ok, f"slice ({b}, {h}): {msg}"
     cache.close()
 
 

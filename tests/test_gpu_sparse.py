@@ -8,9 +8,9 @@ most recent full pages pinned, keep = max(pages / 8, 64), plus the
 undigested tail. The GPU output must match the oracle's attention over that
 token set (orc_sc_attend_mask) at the decode tolerance. The data is checked
 to leave no near-tie at the selection boundary. Queries use the configs'
-scale (std 1/sqrt(128)), which keeps the softmax clear of the f16 centroid
-limit of very peaked scores. A sequence below 16384 keys in the same call is
-dense.
+scale (std 1/sqrt(128)), and one test the peaked regime of the reference's
+Gemma call (q ~ N(0, 1), scale 1). A sequence below 16384 keys in the same
+call is dense.
 """
 import numpy as np
 import pytest
@@ -88,6 +88,23 @@ def test_sparse_decode_matches_oracle(lc, orc, gpu):
     dense = cache.decode_attn(0, [0, 1], q, HQ, scale)
     assert np.abs(dense[0] - got[0]).max() > 1e-4  # the long sequence really went sparse
     ok, msg = helpers.attn_close(got[1:], dense[1:])  # the short one stayed dense
+    assert ok, msg
+    cache.close()
+
+
+def test_sparse_decode_peaked(lc, orc, gpu):
+    """q ~ N(0, 1) at scale 1: the sparse decode's tiles take the K table's
+    f16 residuals like the dense ones, and the selection is unchanged."""
+    lens = [20000]
+    t, cache = _cache(lc, orc, lens)
+    # the keys and query directions of test_sparse_decode_matches_oracle (its
+    # selection boundary has no near-tie; scaling q keeps the page order)
+    refs, _ = _fill(cache, orc, t, lens, 300)
+    q = helpers.queries(orc, 301, 1, HQ, DIM)
+    got = cache.decode_attn(0, [0], q, HQ, 1.0, flags=lc.LC_SPARSE_PAGES)
+    ref, gap = _oracle(orc, t, refs, q, 1.0)
+    assert gap > 1e-4, gap
+    ok, msg = helpers.attn_close(got, ref)
     assert ok, msg
     cache.close()
 

@@ -1,5 +1,7 @@
 """GPU: lc_decode_attn_noalloc, the decode entry point whose scratch is a
-fixed device array, against lc_decode_attn on the same cache and queries.
+fixed device array, against lc_decode_attn on the same cache and queries,
+and against the oracle where the no-alloc call uploads block-table rows
+itself.
 
 Called through the C ABI with device tensors. The two entry points run the
 same kernels, so the bar is the decode tolerance of helpers.attn_close
@@ -75,6 +77,65 @@ def test_noalloc_fast_path(lc, orc, gpu):
 def test_noalloc_generic_rotated_bf16(lc, orc, gpu):
     """3-bit K / 2-bit V, d=256 (the chunked kernel), rotated q and output, bf16 out."""
     _check_case(lc, orc, 256, 3, 2, 8, 16, [700, 1300], lc.LC_Q_ROTATED | lc.LC_OUT_ROTATED, lc.LC_BF16)
+
+
+def test_noalloc_uploads_its_own_block_table(lc, orc, gpu):
+    """Called straight after appends, with no lc_decode_attn before it: the
+    block-table rows of the sequences are dirty, and lc_decode_attn_noalloc
+    stages them through its fixed host array and uploads them itself (three
+    rows, so the staging offset steps). Appending past a page boundary makes
+    two rows dirty again for the second call. Both calls are checked against
+    the oracle's attend_keys -> softmax -> attend_values, and the second also
+    against lc_decode_attn, which runs only afterwards."""
+    import torch
+
+    dim, hkv, hq = 128, 8, 32
+    t = orc.Tables.generate(dim, 4, 64, 42)
+    ck = lc.TurboQuantCompressor.from_tables(t.R, t.bounds, t.cents, t.proj)
+    lens = [250, 510, 100]
+    cache = lc.CudaKvCache(1, hkv, dim, ck, max_seqs=3, max_pages=24, max_pages_per_seq=4)
+    comp = orc.Compressor(t)
+    refs = [orc.SimpleCache(comp, comp, 1, hkv, dim) for _ in lens]
+
+    def add(b, n, seed):
+        K = helpers.kv(orc, seed, 1, hkv, n, dim)
+        V = helpers.kv(orc, seed + 1, 1, hkv, n, dim)
+        cache.append(0, [b], K, V)
+        for h in range(hkv):
+            refs[b].store(0, h, K[0, h], V[0, h], n)
+
+    for b, n in enumerate(lens):
+        add(b, n, 40 + 2 * b)
+    ids = np.array([2, 0, 1], np.int32)
+    qn = helpers.queries(orc, 41, 3, hq, dim, std=dim ** -0.5)
+    q = torch.from_numpy(qn).cuda()
+    scale = float(dim ** -0.5)
+
+    def oracle():
+        return np.stack([np.stack([refs[b].attend(0, h // (hq // hkv), qn[i, h], scale) for h in range(hq)])
+                         for i, b in enumerate(ids)])
+
+    out = torch.full((3, hq, dim), float("nan"), device="cuda")
+    st = _noalloc(lc, cache, ids, q, hq, scale, 0, out, lc.LC_F32)
+    assert st == lc.LC_OK, lc.lib().lc_last_error().decode()
+    torch.cuda.synchronize()
+    ok, msg = helpers.attn_close(out.cpu().numpy(), oracle())
+    assert ok, f"first call: {msg}"
+    add(0, 20, 60)  # 250 -> 270 tokens: a second page
+    add(1, 20, 62)  # 510 -> 530 tokens: a third page
+    out2 = torch.full((3, hq, dim), float("nan"), device="cuda")
+    st = _noalloc(lc, cache, ids, q, hq, scale, 0, out2, lc.LC_F32)
+    assert st == lc.LC_OK, lc.lib().lc_last_error().decode()
+    torch.cuda.synchronize()
+    got2 = out2.cpu().numpy()
+    ok, msg = helpers.attn_close(got2, oracle())
+    assert ok, f"second call: {msg}"
+    ref = torch.empty((3, hq, dim), device="cuda")
+    cache.decode_attn(0, ids, q, hq, scale, out=ref, out_dtype=lc.LC_F32)
+    torch.cuda.synchronize()
+    ok, msg = helpers.attn_close(got2, ref.cpu().numpy())
+    assert ok, f"second call vs lc_decode_attn: {msg}"
+    cache.close()
 
 
 def test_noalloc_refusals(lc, orc, gpu):
