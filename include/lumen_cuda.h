@@ -366,6 +366,55 @@ int lc_merge_partials(lc_cache* cache, int32_t n_parts, int32_t n_rows, const fl
                       const float* l, const float* o, uint32_t flags, void* out, int32_t out_dtype,
                       void* stream);
 
+/* ---- one context split by tokens over GPUs ------------------------------
+ * The reference keeps a sequence on one device; its merge of partial
+ * softmax states (native_quant_attention.rs:190-207) combines chunks of one
+ * context. A group is the set of ranks (one process per GPU, one node)
+ * that each hold a contiguous token shard of the same sequences in their
+ * own cache: lc_decode_attn_split computes this rank's partials, exchanges
+ * them with every rank and merges, with no host round trip. */
+typedef struct lc_group lc_group;
+#define LC_GROUP_ID_BYTES 128
+/* Force the NCCL all-gather exchange instead of peer stores. */
+#define LC_GROUP_NCCL 1u
+
+/* A new group id (ncclGetUniqueId): made by one rank, sent to the others
+ * by the caller (any side channel). */
+int lc_group_id(uint8_t* id);
+
+/* Collective: every rank of the group calls it with the same id, world,
+ * max_rows and head_dim. max_rows bounds n_seqs * n_q_heads of a call.
+ * The ranks map each other's exchange buffers (CUDA IPC) and exchange
+ * partials by stores over NVLink with release flags; where that mapping
+ * fails on any rank (or with LC_GROUP_NCCL) all ranks use an in-place
+ * ncclAllGather instead. world <= 8. */
+int lc_group_create(int32_t world, int32_t rank, const uint8_t* id, int32_t device, int32_t max_rows,
+                    int32_t head_dim, uint32_t flags, lc_group** out);
+
+/* world, rank, and 1 if the exchange uses peer stores (0: NCCL). */
+int lc_group_info(const lc_group* group, int32_t* world, int32_t* rank, int32_t* peer_stores);
+
+/* LC_ERR_TIMEOUT once an exchange's bounded wait for a peer's partials ran
+ * out (a rank failed or stopped calling); its output rows were NaN and the
+ * group takes no more calls. LC_OK otherwise. Reads a host word, no sync. */
+int lc_group_status(const lc_group* group);
+
+/* Local: waits for this device's work, unmaps the peers and frees. Peers
+ * write into this rank's buffer, so every rank must be past its last
+ * lc_decode_attn_split (a barrier of the caller's) before any destroys. */
+int lc_group_destroy(lc_group* group);
+
+/* lc_decode_attn over sequences whose tokens are split across the group's
+ * ranks: seq_ids name this rank's shard slots in `cache`; every rank calls
+ * it with the same layer, n_seqs, n_q_heads, scale, flags and queries (the
+ * same q on every rank) in the same order. Each rank's out receives the
+ * attention over the whole split context. Flags as lc_decode_attn except
+ * LC_SPARSE_PAGES. LC_ERR_TIMEOUT if an earlier exchange of the group
+ * timed out (lc_group_status). */
+int lc_decode_attn_split(lc_cache* cache, lc_group* group, int32_t layer, int32_t n_seqs,
+                         const int32_t* seq_ids, const void* q, int32_t q_dtype, int32_t n_q_heads,
+                         float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream);
+
 /* Device id, stream and last-kernel count (kernels this library launched). */
 int lc_cache_info(const lc_cache* cache, int32_t* device, void** stream, uint64_t* kernel_launches);
 

@@ -25,7 +25,7 @@ import numpy as np
 
 __all__ = [
     "LumenError", "lib", "TurboQuantConfig", "TurboQuantCompressor", "CudaKvCache", "KVCache", "SimpleCache",
-    "NativeRotatingKvCacheTurboQuant", "RawRing", "packed_words", "LC_F32", "LC_BF16", "LC_F16",
+    "NativeRotatingKvCacheTurboQuant", "RawRing", "SplitGroup", "packed_words", "LC_F32", "LC_BF16", "LC_F16",
     "LC_Q_ROTATED", "LC_OUT_ROTATED", "LC_STORE_K_QJL", "LC_STORE_V_QJL",
 ]
 
@@ -38,6 +38,7 @@ LC_F32, LC_BF16, LC_F16 = 0, 1, 2
 LC_STORE_K_QJL, LC_STORE_V_QJL, LC_STORE_DIGEST = 1, 2, 4
 LC_FETCH_VIEW, LC_FETCH_BACKING = 0, 1
 LC_Q_ROTATED, LC_OUT_ROTATED, LC_QJL_SCORES, LC_SPARSE_PAGES = 1, 2, 4, 8
+LC_GROUP_ID_BYTES, LC_GROUP_NCCL = 128, 1
 # cudaStreamLegacy: the legacy default stream (torch's default stream, handle 0).
 # A NULL stream in the C ABI means the library's own stream instead.
 CUDA_STREAM_LEGACY = 0x1
@@ -49,6 +50,7 @@ ABI_SYMBOLS = [
     "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_keys_qjl", "lc_attend_values", "lc_seq_len", "lc_clear",
     "lc_truncate", "lc_append", "lc_append_rope", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
     "lc_decode_attn", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
+    "lc_group_id", "lc_group_create", "lc_group_info", "lc_group_status", "lc_group_destroy", "lc_decode_attn_split",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
     "lc_ring_deep_clone", "lc_ring_destroy", "lc_version", "lc_save_lkv2", "lc_load_lkv2", "lc_lkv2_info",
@@ -128,6 +130,12 @@ def lib():
         "lc_prefill_attn": (C.c_int, [vp, i32, i32, vp, i32, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_partials": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, vp, vp, vp]),
         "lc_merge_partials": (C.c_int, [vp, i32, i32, vp, vp, vp, u32, vp, i32, vp]),
+        "lc_group_id": (C.c_int, [vp]),
+        "lc_group_create": (C.c_int, [i32, i32, vp, i32, i32, i32, u32, pp]),
+        "lc_group_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
+        "lc_group_status": (C.c_int, [vp]),
+        "lc_group_destroy": (C.c_int, [vp]),
+        "lc_decode_attn_split": (C.c_int, [vp, vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_ring_create": (C.c_int, [i32, i64, i64, i32, vp, i32, pp]),
         "lc_ring_update": (C.c_int, [vp, vp, i64, i32, vp]),
         "lc_ring_truncate_to": (C.c_int, [vp, i64]),
@@ -445,6 +453,20 @@ class CudaKvCache:
                                              scale, flags, _ptr(m), _ptr(l), _ptr(o), stream))
         return m, l, o
 
+    def decode_attn_split(self, group: "SplitGroup", layer: int, seq_ids, q, n_q_heads: int, scale: float = 1.0,
+                          flags: int = 0, out=None, out_dtype: int = LC_F32, stream=None):
+        """decode_attn over sequences split by tokens across `group`'s ranks:
+        this cache holds this rank's shard in seq_ids; every rank calls with
+        the same queries and gets the attention over the whole context."""
+        ids = np.ascontiguousarray(seq_ids, np.int32)
+        if out is None:
+            out = np.empty((len(ids), n_q_heads, self.head_dim), np.float32)
+            out_dtype = LC_F32
+        stream = _auto_stream(stream, q, out)
+        _check(lib().lc_decode_attn_split(self._h, group._h, layer, len(ids), _ptr(ids), _ptr(q), _dtype_code(q),
+                                          n_q_heads, scale, flags, _ptr(out), out_dtype, stream))
+        return out
+
     def merge_partials(self, m, l, o, flags: int = 0, out=None, out_dtype: int = LC_F32, stream=None):
         """m, l [n_parts, n_rows]; o [n_parts, n_rows, head_dim] -> out [n_rows, head_dim]."""
         n_parts, n_rows = m.shape
@@ -494,6 +516,41 @@ class CudaKvCache:
 
     def truncate(self, seq, layer, n_keep):
         _check(lib().lc_truncate(self._h, seq, layer, n_keep))
+
+
+class SplitGroup:
+    """lc_group: the ranks (one process per GPU) that hold token shards of the
+    same sequences. Collective: every rank creates it with the same id (from
+    `SplitGroup.new_id()` on one rank, sent by any side channel)."""
+
+    @staticmethod
+    def new_id() -> bytes:
+        buf = (C.c_uint8 * LC_GROUP_ID_BYTES)()
+        _check(lib().lc_group_id(buf))
+        return bytes(buf)
+
+    def __init__(self, world: int, rank: int, group_id: bytes, max_rows: int, head_dim: int, device: int = 0,
+                 nccl: bool = False):
+        if len(group_id) != LC_GROUP_ID_BYTES:
+            raise ValueError(f"group id must be {LC_GROUP_ID_BYTES} bytes")
+        idb = (C.c_uint8 * LC_GROUP_ID_BYTES).from_buffer_copy(group_id)
+        h = C.c_void_p()
+        _check(lib().lc_group_create(world, rank, idb, device, max_rows, head_dim, LC_GROUP_NCCL if nccl else 0,
+                                     C.byref(h)))
+        self._h = h.value
+
+    def info(self) -> dict:
+        w, r, p = C.c_int32(), C.c_int32(), C.c_int32()
+        _check(lib().lc_group_info(self._h, C.byref(w), C.byref(r), C.byref(p)))
+        return {"world": w.value, "rank": r.value, "peer_stores": bool(p.value)}
+
+    def status(self) -> int:
+        return lib().lc_group_status(self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            h, self._h = self._h, None
+            _check(lib().lc_group_destroy(h))
 
 
 class KVCache:

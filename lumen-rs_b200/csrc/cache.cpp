@@ -21,6 +21,7 @@
 #include <memory>
 
 #include "codec.h"
+#include "group.h"
 #include "kernels.h"
 #include "lkv2.h"
 #include "ring.h"
@@ -1451,6 +1452,47 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
     ++c->launches;
     if (host_out) LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
     if (host_out || !dev) LC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+// One long context split by tokens over the ranks of a group: this rank's
+// partials of its shard (the decode kernels plus the slot merge, written
+// straight into its block of the group's exchange buffer), the exchange,
+// then the merge of all ranks' partials (native_quant_attention.rs:190-207)
+// and the un-rotation, all on the stream.
+int lc_decode_attn_split(lc_cache* c, lc_group* g, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+                         const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, void* out,
+                         int32_t out_dtype, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && g && out, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_seqs > 0 && n_q_heads > 0, LC_ERR_INVALID, "bad decode arguments");
+    LC_REQUIRE(!(flags & LC_SPARSE_PAGES), LC_ERR_INVALID, "lc_decode_attn_split does not take LC_SPARSE_PAGES");
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    const int32_t D = c->cfg.head_dim;
+    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    LC_REQUIRE(rows <= INT32_MAX, LC_ERR_INVALID, "too many rows");
+    const SplitCall x = group_begin(g, c->cfg.device, D, (int32_t)rows);
+    cudaStream_t s = c->pick(stream);
+    const DecodeRun run = decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s);
+    launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D, nullptr, nullptr, LC_F32, x.block,
+                 x.block + rows, x.block + 2 * rows, run.oscale, s);
+    ++c->launches;
+    group_exchange(g, x, s);
+    const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
+    const bool host_out = !is_device_ptr(out);
+    void* dout = out;
+    if (host_out) {
+      c->outbuf.ensure(obytes, s);
+      dout = c->outbuf.p;
+    }
+    launch_merge_split(x, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, s);
+    ++c->launches;
+    if (host_out) {
+      LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
+      LC_CUDA(cudaStreamSynchronize(s));
+    } else if (run.host_q) {
+      LC_CUDA(cudaEventSynchronize(c->ev_copy));
+    }
   });
 }
 

@@ -35,6 +35,7 @@
 #include <cstring>
 #include <type_traits>
 
+#include "group.h"
 #include "kernels.h"
 
 namespace lc {
@@ -1722,7 +1723,24 @@ struct MergeDev {
   float* m_out;
   float* l_out;
   float* o_out;
+  // separate arrays: floats between slots (0: n_rows for m / l, n_rows * D for o)
+  int64_t pstride;
+  // split exchange: wait (bounded) until wait_flags[0..wait_n) reach epoch;
+  // on a timeout set *status and write NaN rows
+  const uint32_t* wait_flags;
+  int32_t wait_n;
+  uint32_t epoch;
+  uint32_t* status;
 };
+
+// Bounded acquire-wait of the split exchange: about 2^22 polls of at least
+// 256 ns each (over a second) before it gives up.
+constexpr uint32_t kSpinLimit = 1u << 22;
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // One warp per row merges the row's split partials: lane c holds slot c's
 // max and weight (32 slots at a time, shuffled to the warp as the slots are
@@ -1740,6 +1758,30 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
   const int per = D / 32;  // dims per lane (even)
   const int row = blockIdx.x * kMergeWarps + warp;
   float* orow = so + warp * D;
+  if (a.wait_flags) {  // peers' partials: every flag at this call's epoch
+    __shared__ int s_late;
+    if (threadIdx.x == 0) s_late = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.wait_n; i += blockDim.x) {
+      uint32_t n = 0;
+      while ((int32_t)(ld_acquire_sys(a.wait_flags + i) - a.epoch) < 0) {
+        if (++n > kSpinLimit) {
+          s_late = 1;
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+    __syncthreads();
+    if (s_late) {
+      if (threadIdx.x == 0) asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(a.status), "r"(1u) : "memory");
+      for (int u = threadIdx.x; u < kMergeWarps * D; u += blockDim.x) {
+        const int rr = blockIdx.x * kMergeWarps + u / D;
+        if (rr < a.n_rows && a.out) store_any(a.out, a.out_dtype, (int64_t)rr * D + u % D, __int_as_float(0x7fc00000));
+      }
+      return;
+    }
+  }
   if (row < a.n_rows) {
     const int64_t group = row / a.G;
     const int gh = row % a.G;
@@ -1757,11 +1799,11 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
       pm = a.m_in + row;
       pl = a.l_in + row;
       po = a.o_in + (int64_t)row * D;
-      ms = a.n_rows;
-      os = (int64_t)a.n_rows * D;
+      ms = a.pstride ? a.pstride : a.n_rows;
+      os = a.pstride ? a.pstride : (int64_t)a.n_rows * D;
     }
     float M = -INFINITY;
-    for (int c = lane; c < n; c += 32) M = fmaxf(M, pm[c * ms]);
+    for (int c = lane; c < n; c += 32) M = fmaxf(M, __ldcg(pm + c * ms));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float L = 0.f;
@@ -1771,9 +1813,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
     for (int c0 = 0; c0 < n; c0 += 32) {
       float wl = 0.f;
       if (c0 + lane < n) {
-        const float mc = pm[(c0 + lane) * ms];
+        const float mc = __ldcg(pm + (c0 + lane) * ms);
         wl = mc == -INFINITY ? 0.f : exp2f(mc - M);
-        L += wl * pl[(c0 + lane) * ms];
+        L += wl * __ldcg(pl + (c0 + lane) * ms);
       }
       const int nn = min(32, n - c0);
 #pragma unroll 8
@@ -1783,7 +1825,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           if (2 * k < per) {
-            const float2 v = pc[k];
+            const float2 v = __ldcg(pc + k);
             O[2 * k] = fmaf(w, v.x, O[2 * k]);
             O[2 * k + 1] = fmaf(w, v.y, O[2 * k + 1]);
           }
@@ -2165,14 +2207,23 @@ void launch_merge(const float* part, const int32_t* cnt, int32_t G, int32_t max_
                   float oscale, cudaStream_t s) {
   if (n_rows <= 0) return;
   MergeDev d{part, nullptr, nullptr, nullptr, cnt, G, max_slots, n_rows, dim, oscale, R, out, out_dtype, m_out, l_out,
-             o_out};
+             o_out, 0, nullptr, 0, 0u, nullptr};
   launch_merge_dev(d, s);
 }
 
 void launch_merge_parts(const float* m, const float* l, const float* o, int32_t n_parts, int32_t n_rows, int32_t dim,
                         const float* R, void* out, int32_t out_dtype, cudaStream_t s) {
   if (n_rows <= 0) return;
-  MergeDev d{nullptr, m, l, o, nullptr, 1, n_parts, n_rows, dim, 1.0f, R, out, out_dtype, nullptr, nullptr, nullptr};
+  MergeDev d{nullptr, m, l, o, nullptr, 1, n_parts, n_rows, dim, 1.0f, R, out, out_dtype, nullptr, nullptr, nullptr,
+             0, nullptr, 0, 0u, nullptr};
+  launch_merge_dev(d, s);
+}
+
+void launch_merge_split(const SplitCall& x, int32_t D, const float* R, void* out, int32_t out_dtype,
+                        cudaStream_t s) {
+  MergeDev d{nullptr, x.parts, x.parts + x.rows, x.parts + 2 * (int64_t)x.rows, nullptr, 1, x.world, x.rows, D, 1.0f,
+             R, out, out_dtype, nullptr, nullptr, nullptr, x.block_stride, x.wait_flags, x.wait_n, x.epoch,
+             x.status};
   launch_merge_dev(d, s);
 }
 

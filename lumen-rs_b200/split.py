@@ -9,10 +9,15 @@ sequence of the benchmark's scale-out config) is split by tokens:
 - Each rank computes, for every query head, the softmax partials of its
   range: m is the log2-domain max, l the sum of 2^(s - m), and o the
   unnormalised rotated output (`lc_decode_attn_partials`).
-- The ranks all-gather the partials in one collective per layer: NCCL over
-  NVLink, or gloo on CPU. That is rows * (head_dim + 2) f32 per rank.
-- Every rank merges them (`lc_merge_partials`), the combine of partial
-  softmax states in lumen-mlx native_quant_attention.rs:190-207.
+- The ranks exchange the partials once per layer, rows * (head_dim + 2)
+  f32 per rank. On GPUs the library does it (`lc_decode_attn_split` over an
+  `lc_group`): each rank stores its partials straight into every peer's
+  buffer over NVLink and raises a flag there, and every rank merges once
+  all flags are up, all on the stream. Without a group (CPU tests, gloo),
+  a torch.distributed all-gather stands in.
+- Every rank merges them (`lc_merge_partials` / the group's merge), the
+  combine of partial softmax states in lumen-mlx
+  native_quant_attention.rs:190-207.
 
 New tokens go to the rank holding the sequence's end (`owner_of_next`).
 """
@@ -38,6 +43,21 @@ def owner_of_next(world: int) -> int:
     return world - 1
 
 
+def make_group(max_rows: int, head_dim: int, device: int, pg=None, nccl: bool = False):
+    """The library's exchange group (lc_group) for the ranks of torch.distributed
+    process group `pg`: rank 0 makes the id, a broadcast carries it (plumbing
+    only; the per-layer exchange never goes through torch)."""
+    import importlib
+
+    import torch.distributed as dist
+
+    lc = importlib.import_module("lumen-rs_b200")
+    world, rank = dist.get_world_size(pg), dist.get_rank(pg)
+    box = [lc.SplitGroup.new_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=dist.get_global_rank(pg, 0) if pg is not None else 0, group=pg)
+    return lc.SplitGroup(world, rank, box[0], max_rows, head_dim, device=device, nccl=nccl)
+
+
 class SplitSequenceDecoder:
     """Decode attention for one sequence whose tokens are sharded over ranks.
 
@@ -49,10 +69,11 @@ class SplitSequenceDecoder:
     no process group is initialised).
     """
 
-    def __init__(self, cache, seq_id: int = 0, group=None, gather: Optional[Callable] = None):
+    def __init__(self, cache, seq_id: int = 0, group=None, gather: Optional[Callable] = None, lc_group=None):
         self.cache = cache
         self.seq_id = seq_id
         self.group = group
+        self.lc_group = lc_group  # a SplitGroup: the library exchanges and merges
         self._gather = gather or self._dist_gather
 
     def _dist_gather(self, x):
@@ -75,6 +96,13 @@ class SplitSequenceDecoder:
 
         rows, d = n_q_heads, self.cache.head_dim
         dev = q.device if hasattr(q, "device") else None
+        if self.lc_group is not None:
+            if out is None:
+                out = torch.empty((rows, d), dtype=torch.float32, device=dev)
+                out_dtype = 0
+            self.cache.decode_attn_split(self.lc_group, layer, [self.seq_id], q, n_q_heads, scale, flags, out=out,
+                                         out_dtype=0 if out_dtype is None else out_dtype)
+            return out
         # one buffer [m | l | o] per rank, so one collective moves all three
         buf = torch.empty(rows * (d + 2), dtype=torch.float32, device=dev)
         m, l, o = buf[:rows], buf[rows:2 * rows], buf[2 * rows:].view(rows, d)
