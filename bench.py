@@ -262,6 +262,220 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------------------
+# Scale-out workloads of config 4 (and config 1 split by kv heads), measured
+# at every N beside the default line: strong scaling, fixed total work.
+# ----------------------------------------------------------------------------
+def _bf16_kv(torch, gen, dev, B, hkv, n, D, scale_vec):
+    x = torch.randn((B, hkv, n, D), generator=gen, device=dev, dtype=torch.float32) * scale_vec
+    return x.to(torch.bfloat16).contiguous()
+
+
+def _outlier_scale(torch, hkv, D, dev):
+    sel = torch.Generator(device="cpu")
+    sel.manual_seed(99)
+    v = torch.ones(hkv, D)
+    for h in range(hkv):
+        v[h, torch.randperm(D, generator=sel)[:4]] = 8.0
+    return v.to(dev).view(1, hkv, 1, D)
+
+
+def _time_steps(torch, dist, step, steps, warm, world):
+    """Device time of `steps` calls of step() on torch's current stream, max over ranks (ms)."""
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def _request_shard(args, lc, torch, dist, dev, local, rank, world, codec, peak):
+    """Config 4, first half: 256 concurrent requests at context 32768 (4-bit,
+    GQA 32/8, d 128) split by request over the ranks, no collective."""
+    total, ctx, L, hq, hkv, D = 256, 32768, args.c4_layers, CFG["hq"], CFG["hkv"], CFG["dim"]
+    B = total // world
+    steps, warm = max(3, args.steps // 2), 3
+    pps = (ctx + steps + warm + 8 + 255) // 256 + 1
+    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=B, max_pages=L * B * pps + 64, max_pages_per_seq=pps,
+                           device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5000 + rank)
+    sv = _outlier_scale(torch, hkv, D, dev)
+    ids = list(range(B))
+    t0 = time.time()
+    for layer in range(L):
+        for c0 in range(0, ctx, 2048):
+            cache.append(layer, ids, _bf16_kv(torch, gen, dev, B, hkv, 2048, D, sv),
+                         _bf16_kv(torch, gen, dev, B, hkv, 2048, D, sv))
+    torch.cuda.synchronize()
+    fill_s = time.time() - t0
+    qs = (torch.randn((L, B, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    k1 = [_bf16_kv(torch, gen, dev, B, hkv, 1, D, sv) for _ in range(L)]
+    v1 = [_bf16_kv(torch, gen, dev, B, hkv, 1, D, sv) for _ in range(L)]
+    out = torch.empty((L, B, hq, D), device=dev, dtype=torch.bfloat16)
+
+    def step():
+        for layer in range(L):
+            cache.append(layer, ids, k1[layer], v1[layer])
+            cache.decode_attn(layer, ids, qs[layer], hq, 1.0, out=out[layer], out_dtype=lc.LC_BF16)
+
+    ms = _time_steps(torch, dist, step, steps, warm, world)
+    n0 = cache.ring_state(0, 0)["view_len"]
+    cache.timing(1)
+    for _ in range(2):
+        step()
+    dec_ms, dec_n, _, _, other_ms = cache.timing(0)
+    launch_ms = dec_ms / max(dec_n, 1)
+    bytes_launch = B * hkv * BYTES_PER_TOKEN_HEAD * (n0 + 1.5)
+    achieved = bytes_launch / (launch_ms / 1e3) / 1e9
+    cache.close()
+    del qs, k1, v1, out
+    torch.cuda.empty_cache()
+    return {"value": total * steps / (ms / 1e3), "unit": "tok/s", "scaling": "strong", "ms_per_step": ms / steps,
+            "workload": f"config4: {total} requests x {ctx} tokens over {world} GPU(s) ({B} per GPU), {L} layers, "
+                        f"32q/8kv, d128, 4-bit K/V; append + decode per layer",
+            "per_gpu": {"requests": B, "decode_avg_launch_us": launch_ms * 1e3, "decode_gbs": achieved,
+                        "roofline_frac": achieved / peak, "merge_and_rotation_ms_per_step": other_ms / 2},
+            "fill_s": fill_s}
+
+
+def _head_shard(args, lc, torch, dist, dev, local, rank, world, codec, peak):
+    """Config 1 split by kv-head groups: rank r holds kv heads [r * 8/N,
+    (r + 1) * 8/N) of all 32 sequences and their query groups; no collective
+    (each q head reads only its kv head)."""
+    B, hq, hkv, D, ctx, L = CFG["batch"], CFG["hq"], CFG["hkv"], CFG["dim"], CFG["ctx"], args.heads_layers
+    split = importlib.import_module("lumen-rs_b200.split")
+    h0, h1 = split.head_shard(hkv, rank, world)
+    hk = h1 - h0
+    G = hq // hkv
+    steps, warm = max(3, args.steps // 2), 3
+    pps = (ctx + steps + warm + 8 + 255) // 256 + 1
+    cache = lc.CudaKvCache(L, hk, D, codec, codec, max_seqs=B, max_pages=L * B * pps + 64, max_pages_per_seq=pps,
+                           device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6000 + rank)
+    sv = _outlier_scale(torch, hkv, D, dev)[:, h0:h1]
+    ids = list(range(B))
+    for layer in range(L):
+        for c0 in range(0, ctx, 2048):
+            cache.append(layer, ids, _bf16_kv(torch, gen, dev, B, hk, 2048, D, sv),
+                         _bf16_kv(torch, gen, dev, B, hk, 2048, D, sv))
+    qs = (torch.randn((L, B, hk * G, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    k1 = [_bf16_kv(torch, gen, dev, B, hk, 1, D, sv) for _ in range(L)]
+    v1 = [_bf16_kv(torch, gen, dev, B, hk, 1, D, sv) for _ in range(L)]
+    out = torch.empty((L, B, hk * G, D), device=dev, dtype=torch.bfloat16)
+
+    def step():
+        for layer in range(L):
+            cache.append(layer, ids, k1[layer], v1[layer])
+            cache.decode_attn(layer, ids, qs[layer], hk * G, 1.0, out=out[layer], out_dtype=lc.LC_BF16)
+
+    ms = _time_steps(torch, dist, step, steps, warm, world)
+    n0 = cache.ring_state(0, 0)["view_len"]
+    cache.timing(1)
+    for _ in range(2):
+        step()
+    dec_ms, dec_n, _, _, _ = cache.timing(0)
+    launch_ms = dec_ms / max(dec_n, 1)
+    achieved = B * hk * BYTES_PER_TOKEN_HEAD * (n0 + 1.5) / (launch_ms / 1e3) / 1e9
+    cache.close()
+    del qs, k1, v1, out
+    torch.cuda.empty_cache()
+    return {"value": B * steps / (ms / 1e3), "unit": "tok/s", "scaling": "strong", "ms_per_step": ms / steps,
+            "workload": f"config1 by kv-head groups: {B} sequences x {ctx} tokens, {hkv} kv heads split {world} "
+                        f"way(s) ({hk} kv / {hk * G} q heads per GPU), {L} layers, 4-bit K/V",
+            "per_gpu": {"kv_heads": hk, "decode_avg_launch_us": launch_ms * 1e3, "decode_gbs": achieved,
+                        "roofline_frac": achieved / peak}}
+
+
+def _longctx_split(args, lc, torch, dist, dev, local, rank, world, codec, peak, n_ctx, L, steps, warm):
+    """Config 4, second half: one n_ctx-token sequence split by tokens over
+    the ranks. Per layer each rank decodes its shard's partials, the library
+    exchanges them (peer stores over NVLink) and merges (lc_decode_attn_split)."""
+    split = importlib.import_module("lumen-rs_b200.split")
+    hq, hkv, D = CFG["hq"], CFG["hkv"], CFG["dim"]
+    lo, hi = split.shard_range(n_ctx, rank, world)
+    owner = rank == split.owner_of_next(world)
+    extra = steps + warm + 8 if owner else 0
+    pages = (hi - lo + extra + 255) // 256 + 1
+    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=1, max_pages=L * pages + 16, max_pages_per_seq=pages,
+                           device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242 + rank)
+    sv = _outlier_scale(torch, hkv, D, dev)
+    t0 = time.time()
+    for layer in range(L):
+        for c0 in range(lo, hi, 16384):
+            n = min(16384, hi - c0)
+            cache.append(layer, [0], _bf16_kv(torch, gen, dev, 1, hkv, n, D, sv),
+                         _bf16_kv(torch, gen, dev, 1, hkv, n, D, sv))
+    torch.cuda.synchronize()
+    fill_s = time.time() - t0
+    group = split.make_group(hq, D, local) if world > 1 else lc.SplitGroup(1, 0, lc.SplitGroup.new_id(), hq, D,
+                                                                            device=local)
+    dec = split.SplitSequenceDecoder(cache, 0, lc_group=group)
+    qs = (torch.randn((L, 1, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    k1 = [_bf16_kv(torch, gen, dev, 1, hkv, 1, D, sv) for _ in range(L)]
+    v1 = [_bf16_kv(torch, gen, dev, 1, hkv, 1, D, sv) for _ in range(L)]
+    out = torch.empty((L, hq, D), device=dev, dtype=torch.float32)
+
+    def step():
+        for layer in range(L):
+            if owner:
+                cache.append(layer, [0], k1[layer], v1[layer])
+            dec.decode(layer, qs[layer], hq, 1.0, out=out[layer])
+
+    ms = _time_steps(torch, dist, step, steps, warm, world)
+    status = group.status()
+    # the same layers' local partials alone (no exchange, no merge of ranks)
+    m = torch.empty((hq,), device=dev)
+    l_ = torch.empty((hq,), device=dev)
+    o = torch.empty((hq, D), device=dev)
+
+    def local_step():
+        for layer in range(L):
+            cache.decode_partials(layer, [0], qs[layer], hq, 1.0, m=m, l=l_, o=o)
+
+    local_ms = _time_steps(torch, dist, local_step, steps, warm, world)
+    peer = group.info()["peer_stores"]
+    if world > 1:
+        dist.barrier()  # every rank past its last exchange before buffers are freed
+    group.close()
+    cache.close()
+    del qs, k1, v1, out
+    torch.cuda.empty_cache()
+    kv_bytes = n_ctx * hkv * BYTES_PER_TOKEN_HEAD * L
+    return {"value": steps / (ms / 1e3), "unit": "tok/s", "scaling": "strong", "ms_per_step": ms / steps,
+            "ms_per_layer": ms / steps / L, "local_partials_ms_per_layer": local_ms / steps / L,
+            "exchange_and_merge_ms_per_layer": (ms - local_ms) / steps / L,
+            "exchange": ("peer stores over NVLink + release flags (lc_decode_attn_split)" if peer else
+                         "in-place ncclAllGather (lc_decode_attn_split)") if world > 1 else "none (one rank)",
+            "group_status": status, "decode_gbs": kv_bytes / (ms / steps / 1e3) / 1e9,
+            "workload": f"config4 long context: 1 sequence of {n_ctx} tokens split over {world} GPU(s), {L} layers, "
+                        f"32q/8kv, d128, 4-bit K/V", "fill_s": fill_s}
+
+
+def scale_out(args, lc, torch, dist, dev, local, rank, world, codec, peak):
+    res = {}
+    res["config4_request_shard"] = _request_shard(args, lc, torch, dist, dev, local, rank, world, codec, peak)
+    res["config1_head_shard"] = _head_shard(args, lc, torch, dist, dev, local, rank, world, codec, peak)
+    res["config4_longctx_split"] = _longctx_split(args, lc, torch, dist, dev, local, rank, world, codec, peak,
+                                                  1 << 20, args.longctx_layers, max(3, args.steps // 2), 3)
+    return res
+
+
+# ----------------------------------------------------------------------------
 # Our arm
 # ----------------------------------------------------------------------------
 def run_ours(args):
@@ -485,10 +699,11 @@ def run_ours(args):
     if rank == 0:
         # ---- CPU baseline: oracle decode of one (seq, layer) sample ----
         cpu = None
-        if world == 1 and not args.no_cpu:
+        if not args.no_cpu:
             f = cache.fetch(0, 0)
             data = [(f["k_words"][h], f["k_sigma"][h], f["v_words"][h], f["v_sigma"][h]) for h in range(hkv)]
-            sample_s, heads = cpu_attend_sample(data, hq, hkv, D, threads=1, budget_s=args.cpu_budget)
+            budget = args.cpu_budget if world == 1 else args.cpu_budget / 4
+            sample_s, heads = cpu_attend_sample(data, hq, hkv, D, threads=1, budget_s=budget)
             cpu_tok_s = B / (sample_s * L * B)
             cpu = {"value": cpu_tok_s, "unit": "tok/s", "cores": 1, "kind": "port",
                    "sample": f"{heads} of {hq} query heads of one (sequence, layer) over {ctx1} tokens "
@@ -530,11 +745,20 @@ def run_ours(args):
             "clocks": clk.summary(),
             "fill_s": fill_s,
         }
+    cache.close()
+    del qs, k1, v1, out, ind, od, inh, oh, qd, kd, vd
+    torch.cuda.empty_cache()
+    if not args.no_scale_out:
+        # strong-scaling workloads of config 4 (and config 1 by kv heads),
+        # every rank in the same order; rank 0 reports them on this line
+        so = scale_out(args, lc, torch, dist, dev, local, rank, world, codec, measured_peaks()[0])
+        if rank == 0:
+            result.update(so)
+    if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    cache.close()
 
 
 # ----------------------------------------------------------------------------
@@ -552,80 +776,23 @@ def run_longctx(args):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     lc = importlib.import_module("lumen-rs_b200")
-    split = importlib.import_module("lumen-rs_b200.split")
-    hq, hkv, D, L = CFG["hq"], CFG["hkv"], CFG["dim"], args.layers
-    n_ctx = args.ctx_tokens
-    lo, hi = split.shard_range(n_ctx, rank, world)
-    steps, warm = args.steps, args.warmup
-    extra = steps + warm + 8 if rank == split.owner_of_next(world) else 0
-    pages = (hi - lo + extra + 255) // 256 + 1
-    codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
-    cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=1, max_pages=L * pages + 16, max_pages_per_seq=pages,
-                           device=local)
-    s = torch.cuda.ExternalStream(cache.stream(), device=dev)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(4242 + rank)
-    t_fill = time.time()
-    chunk = 16384
-    with torch.cuda.stream(s):
-        for layer in range(L):
-            for c0 in range(lo, hi, chunk):
-                n = min(chunk, hi - c0)
-                k = torch.randn((1, hkv, n, D), generator=gen, device=dev).to(torch.bfloat16)
-                v = torch.randn((1, hkv, n, D), generator=gen, device=dev).to(torch.bfloat16)
-                torch.cuda.current_stream().synchronize()
-                cache.append(layer, [0], k, v, stream=cache.stream())
-    torch.cuda.synchronize()
-    fill_s = time.time() - t_fill
-    dec = split.SplitSequenceDecoder(cache, seq_id=0)
-    owner = rank == split.owner_of_next(world)
-    qs = (torch.randn((L, 1, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
-    k1 = torch.randn((L, 1, hkv, 1, D), generator=gen, device=dev).to(torch.bfloat16)
-    v1 = torch.randn((L, 1, hkv, 1, D), generator=gen, device=dev).to(torch.bfloat16)
-    out = torch.empty((L, hq, D), device=dev, dtype=torch.float32)
-
-    def step():
-        for layer in range(L):
-            if owner:
-                cache.append(layer, [0], k1[layer], v1[layer])
-            dec.decode(layer, qs[layer], hq, 1.0, out=out[layer])
-
-    for _ in range(warm):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, CFG["dim"]))
+    peak, _ = measured_peaks()
     with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
-        ev0.record()
-        for _ in range(steps):
-            step()
-        ev1.record()
-        ev1.synchronize()
-    elapsed_ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    ms_step = elapsed_ms / steps
-    kv_bytes = n_ctx * hkv * BYTES_PER_TOKEN_HEAD * L  # one pass over the whole context, all ranks together
+        r = _longctx_split(args, lc, torch, dist, dev, local, rank, world, codec, peak, args.ctx_tokens, args.layers,
+                           args.steps, args.warmup)
     if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "value": steps / (elapsed_ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": steps,
-            "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"config4 long context: 1 sequence of {n_ctx} tokens split by sequence over "
-                                   f"{world} GPU(s), {L} layers, 32q/8kv, d128, 4-bit K/V; per layer partials + "
-                                   f"NCCL all-gather of (m, l, o) + merge",
-                       "global_batch": 1, "seq_len": n_ctx, "parallelism": f"sequence-split x{world}"},
-            "decode_gbs": kv_bytes / (ms_step / 1e3) / 1e9,
-            "clocks": clk.summary(), "fill_s": fill_s, "mode": "longctx",
-        }), flush=True)
+        line = {"metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": r["workload"], "global_batch": 1, "seq_len": args.ctx_tokens,
+                           "parallelism": f"sequence-split x{world}"},
+                "clocks": clk.summary(), "mode": "longctx"}
+        line.update({k: v for k, v in r.items() if k not in line and k != "workload"})
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    cache.close()
 
 
 # ----------------------------------------------------------------------------
@@ -873,6 +1040,11 @@ def main():
                          "sequence; prefill: config 3 chunked quantize-append and prefix reuse; window: config 2 "
                          "mixed precision with rotating windows")
     ap.add_argument("--ctx-tokens", type=int, default=1 << 20, help="longctx: tokens of the split sequence")
+    ap.add_argument("--no-scale-out", action="store_true",
+                    help="skip the strong-scaling workloads reported beside the default line")
+    ap.add_argument("--c4-layers", type=int, default=4, help="layers of config 4's 256 x 32K request-shard run")
+    ap.add_argument("--heads-layers", type=int, default=8, help="layers of the kv-head-shard run of config 1")
+    ap.add_argument("--longctx-layers", type=int, default=8, help="layers of the 1M-token split run")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

@@ -38,6 +38,14 @@ def shard_range(n_tokens: int, rank: int, world: int) -> Tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
+def head_shard(n_kv_heads: int, rank: int, world: int) -> Tuple[int, int]:
+    """Kv heads [lo, hi) of `rank` when a model's kv heads are split over the
+    ranks (each rank also takes those heads' query groups): attention of a
+    query head reads only its kv head, so the shards need no communication.
+    Near-equal contiguous shares, as shard_range."""
+    return shard_range(n_kv_heads, rank, world)
+
+
 def owner_of_next(world: int) -> int:
     """Rank that appends the sequence's new tokens: the one holding its end."""
     return world - 1
