@@ -1097,7 +1097,7 @@ struct PrefillView {
 static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* q,
                                int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, cudaStream_t s,
                                void* fused_out = nullptr, int32_t out_dtype = LC_F32,
-                               const PrefillView* prefill = nullptr) {
+                               const PrefillView* prefill = nullptr, float* fused_parts = nullptr) {
   LC_REQUIRE(c && (seq_ids || prefill) && q, LC_ERR_INVALID, "null argument");
   LC_REQUIRE(n_seqs > 0, LC_ERR_INVALID, "n_seqs must be > 0");
   const int32_t hkv = c->cfg.n_kv_heads;
@@ -1192,7 +1192,9 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     }
   }
   const DecodePlan plan = plan_decode(lens, hkv, n_q_heads, D, (int)c->kc.bits, (int)c->vc.bits, qjl);
-  const bool fused = fused_out && decode_fusable(plan, n_q_heads / hkv);
+  bool fused = (fused_out || fused_parts) && decode_fusable(plan, n_q_heads / hkv);
+  if (fused_parts)  // empty sequences' partial rows (m = -inf) come from the split path's merge
+    for (int32_t b = 0; b < n_seqs; ++b) fused = fused && lens[b] > 0;
   // The one-launch path of small calls passes its arrays in the launch
   // parameters; otherwise one upload: [seqinfo i64 | seg i64 | cnt i32].
   const bool inl = fused && decode_inline_fits(n_seqs, hkv);
@@ -1300,7 +1302,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     c->ctr.ensure(nctr, s);
     if (c->ctr.n != before) LC_CUDA(cudaMemsetAsync(c->ctr.p, 0, c->ctr.n * sizeof(int32_t), s));
     const size_t esz = dtype_size(out_dtype);
-    for (int32_t b = 0; b < n_seqs; ++b)  // rows of empty sequences are zero
+    for (int32_t b = 0; b < n_seqs && fused_out; ++b)  // rows of empty sequences are zero
       if (lens[b] == 0)
         LC_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(fused_out) + (size_t)b * n_q_heads * D * esz, 0,
                                 (size_t)n_q_heads * D * esz, s));
@@ -1316,6 +1318,11 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     f.out = fused_out;
     f.out_dtype = out_dtype;
     f.oscale = 1.0f / valpha;
+    if (fused_parts) {
+      f.parts = fused_parts;
+      f.parts_rows = (int32_t)rows;
+      f.vRT = nullptr;
+    }
     c->timed(c->t_decode, s, [&] { launch_decode_fused(a, plan, f, s); });
   } else {
     c->timed(c->t_decode, s, [&] { launch_decode_partials(a, plan, s); });
@@ -1473,10 +1480,16 @@ int lc_decode_attn_split(lc_cache* c, lc_group* g, int32_t layer, int32_t n_seqs
     LC_REQUIRE(rows <= INT32_MAX, LC_ERR_INVALID, "too many rows");
     const SplitCall x = group_begin(g, c->cfg.device, D, (int32_t)rows);
     cudaStream_t s = c->pick(stream);
-    const DecodeRun run = decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s);
-    launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D, nullptr, nullptr, LC_F32, x.block,
-                 x.block + rows, x.block + 2 * rows, run.oscale, s);
-    ++c->launches;
+    // the one-launch decode writes the shard's partials into this rank's
+    // block when it applies; else the split-K slots are merged into it
+    const DecodeRun run =
+        decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, nullptr, LC_F32, nullptr,
+                      x.block);
+    if (!run.fused) {
+      launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D, nullptr, nullptr, LC_F32, x.block,
+                   x.block + rows, x.block + 2 * rows, run.oscale, s);
+      ++c->launches;
+    }
     group_exchange(g, x, s);
     const size_t obytes = (size_t)rows * D * dtype_size(out_dtype);
     const bool host_out = !is_device_ptr(out);

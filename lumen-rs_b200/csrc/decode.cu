@@ -248,6 +248,11 @@ struct DecodeDev {
   void* out;
   int32_t out_dtype;
   float oscale;
+  // fused path, partials instead of the output: per row r (of `parts_rows`)
+  // m at parts[r], l at parts[parts_rows + r], o (rotated, unnormalised) at
+  // parts[2 parts_rows + r * D]; null: write `out`
+  float* parts;
+  int32_t parts_rows;
   // QJL stage-2 scores (generic path): see DecodeArgs
   const float* q_proj;
   int64_t off_kq, off_kr;
@@ -1233,11 +1238,24 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 1) k_decode_pair(const __grid
         }
         M = Mn;
       }
+      if (a.parts) {  // the row's softmax partials (a split context's shard)
+        const int sid = sid0 + r / G;
+        const int64_t orow = (int64_t)(sid / a.hkv) * a.hq + (int64_t)(sid % a.hkv) * G + r % G;
+        float* po = a.parts + 2 * (int64_t)a.parts_rows + orow * D;
+        *reinterpret_cast<float2*>(po + 2 * lane) = make_float2(acc[0] * a.oscale, acc[1] * a.oscale);
+        *reinterpret_cast<float2*>(po + 64 + 2 * lane) = make_float2(acc[2] * a.oscale, acc[3] * a.oscale);
+        if (lane == 0) {
+          a.parts[orow] = M;
+          a.parts[a.parts_rows + orow] = L;
+        }
+        continue;
+      }
       const float li = L > 0.f ? a.oscale / L : 0.f;
       *reinterpret_cast<float2*>(om + rot_swz(k, 2 * lane)) = make_float2(acc[0] * li, acc[1] * li);
       *reinterpret_cast<float2*>(om + rot_swz(k, 64 + 2 * lane)) = make_float2(acc[2] * li, acc[3] * li);
     }
     cp_wait_all();
+    if (a.parts) return;  // uniform over the CTA; no barrier follows
     __syncthreads();
     // out = R^T o on the tensor cores: warp w computes output dims 16 (w & 7)
     // .. + 15 of compacted row blocks (w >> 3) and (w >> 3) + 2
@@ -2173,6 +2191,8 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
   d.out = f.out;
   d.out_dtype = f.out_dtype;
   d.oscale = f.oscale;
+  d.parts = f.parts;
+  d.parts_rows = f.parts_rows;
   if (d.tile_map) {  // page-sparse
     switch (d.G) {
       case 1: return launch_pair_g<1, true, true>(d, p.grid, s);

@@ -185,6 +185,10 @@ struct FusedArgs {
   void* out = nullptr;
   int32_t out_dtype = 0;
   float oscale = 1.0f;           // 1 / valpha
+  // softmax partials instead of `out` (m [rows], l [rows], o [rows][dim],
+  // rotated and unnormalised, back to back), for a split context's shard
+  float* parts = nullptr;
+  int32_t parts_rows = 0;
 };
 bool decode_fusable(const DecodePlan& p, int G);
 void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedArgs& f, cudaStream_t s);
