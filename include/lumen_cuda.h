@@ -107,6 +107,13 @@ typedef struct lc_cache lc_cache;
  * elementwise min and max of the dequantized rotated keys of every full
  * 64-token page, the PageDigest of native_cache.rs:350-365 over the codes */
 #define LC_STORE_DIGEST 4u
+/* store V un-rotated, the Qwen TurboQuant layout (qwen3_5_moe.rs:2774-2781:
+ * V is Lloyd-Max quantized as it is, "so no un-rotation step is needed on
+ * read"): the V codec's rotation is taken as the identity, so codes, sigma,
+ * QJL bits and lc_fetch hold the un-rotated quantization, and decode writes
+ * sum_t p_t v_t with no R^T. K stays rotated. Not recorded in LKV2 files:
+ * load a snapshot into a cache created with the same flag. */
+#define LC_STORE_V_UNROTATED 8u
 
 typedef struct lc_cache_config {
   int32_t n_layers;

@@ -35,7 +35,7 @@ LIB_PATH = os.path.join(HERE, "liblumen_cuda.so")
 LC_OK, LC_ERR_INVALID, LC_ERR_BITS, LC_ERR_REFUSED, LC_ERR_CUDA = 0, -1, -2, -3, -4
 LC_ERR_TIMEOUT, LC_ERR_NOMEM, LC_ERR_IO, LC_ERR_MAGIC, LC_ERR_STATE = -5, -6, -7, -8, -9
 LC_F32, LC_BF16, LC_F16 = 0, 1, 2
-LC_STORE_K_QJL, LC_STORE_V_QJL, LC_STORE_DIGEST = 1, 2, 4
+LC_STORE_K_QJL, LC_STORE_V_QJL, LC_STORE_DIGEST, LC_STORE_V_UNROTATED = 1, 2, 4, 8
 LC_FETCH_VIEW, LC_FETCH_BACKING = 0, 1
 LC_Q_ROTATED, LC_OUT_ROTATED, LC_QJL_SCORES, LC_SPARSE_PAGES = 1, 2, 4, 8
 LC_GROUP_ID_BYTES, LC_GROUP_NCCL = 128, 1

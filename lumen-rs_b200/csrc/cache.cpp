@@ -129,6 +129,13 @@ struct lc_cache {
     return d_table + ((size_t)layer * cfg.max_seqs + seq) * cfg.max_pages_per_seq;
   }
   cudaStream_t pick(void* s) const { return s ? static_cast<cudaStream_t>(s) : stream; }
+  // V's R (row-major) / R^T for the output's un-rotation, or null when the
+  // caller keeps the output rotated or V is stored un-rotated
+  bool out_unrotated(uint32_t flags) const {
+    return (flags & LC_OUT_ROTATED) || (cfg.store_flags & LC_STORE_V_UNROTATED);
+  }
+  const float* v_R(uint32_t flags) const { return out_unrotated(flags) ? nullptr : dv.R; }
+  const float* v_RT(uint32_t flags) const { return out_unrotated(flags) ? nullptr : dv.RTd; }
 
   // Device work on the cache is serialised across streams: before work on
   // `s`, wait for everything issued on the stream used last.
@@ -278,6 +285,11 @@ int lc_cache_create(const lc_cache_config* cfg, const lc_codec* kcodec, const lc
     }
     c->kc = kcodec->c;
     c->vc = vcodec->c;
+    if (cfg->store_flags & LC_STORE_V_UNROTATED) {  // V quantized as it is: R = I
+      const size_t d = c->vc.dim;
+      c->vc.R.assign(d * d, 0.0f);
+      for (size_t i = 0; i < d; ++i) c->vc.R[i * d + i] = 1.0f;
+    }
     LC_CUDA(cudaSetDevice(cfg->device));
     LC_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     LC_CUDA(cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming));
@@ -1312,7 +1324,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     f.q_rotated = (flags & LC_Q_ROTATED) ? 1 : 0;
     f.qscale = qscale;
     f.qR = c->dk.R;
-    f.vRT = (flags & LC_OUT_ROTATED) ? nullptr : c->dv.RTd;
+    f.vRT = c->v_RT(flags);
     f.cnt = dcnt;
     f.ctr = c->ctr.p;
     f.out = fused_out;
@@ -1363,7 +1375,7 @@ static void attn_call(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t*
   if (!run.fused) {
     c->timed(c->t_other, s, [&] {
       launch_merge(c->part.p, run.cnt, run.G, run.max_slots, (int32_t)rows, D,
-                   (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, nullptr, nullptr, nullptr,
+                   c->v_R(flags), dout, out_dtype, nullptr, nullptr, nullptr,
                    run.oscale, s);
     });
     ++c->launches;
@@ -1454,7 +1466,7 @@ int lc_merge_partials(lc_cache* c, int32_t n_parts, int32_t n_rows, const float*
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    launch_merge_parts(dm, dl, dov, n_parts, n_rows, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype,
+    launch_merge_parts(dm, dl, dov, n_parts, n_rows, D, c->v_R(flags), dout, out_dtype,
                        s);
     ++c->launches;
     if (host_out) LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
@@ -1498,7 +1510,7 @@ int lc_decode_attn_split(lc_cache* c, lc_group* g, int32_t layer, int32_t n_seqs
       c->outbuf.ensure(obytes, s);
       dout = c->outbuf.p;
     }
-    launch_merge_split(x, D, (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, dout, out_dtype, s);
+    launch_merge_split(x, D, c->v_R(flags), dout, out_dtype, s);
     ++c->launches;
     if (host_out) {
       LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
@@ -1636,7 +1648,7 @@ int lc_decode_attn_noalloc(lc_cache* c, int32_t layer, int32_t n_seqs, const int
     launch_decode_partials(a, plan, s);
     ++c->launches;
     launch_merge(part, dcnt, n_q_heads / hkv, plan.max_slots, (int32_t)rows, D,
-                 (flags & LC_OUT_ROTATED) ? nullptr : c->dv.R, out, out_dtype, nullptr, nullptr, nullptr,
+                 c->v_R(flags), out, out_dtype, nullptr, nullptr, nullptr,
                  1.0f / valpha, s);
     ++c->launches;
   });
