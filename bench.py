@@ -7,7 +7,7 @@ Workload (config 1): batch 32 per GPU, 32 query heads / 8 kv heads,
 head_dim 128, 8192 cached tokens per sequence, 32 layers, 4-bit K and V
 packed. One step = for every layer: quantize-append the new token's K and V
 of all 32 sequences, then decode attention for the 32 query heads over the
-whole context. Synthetic seeded data: K, V ~ N(0, 1) with 4 outlier channels
+whole context (lc_decode_step: the append launch also rotates the queries). Synthetic seeded data: K, V ~ N(0, 1) with 4 outlier channels
 per kv head scaled x8; queries ~ N(0, 1/sqrt(128)) read as a standard
 deviation, softmax scale 1. The 9 GB cache is far larger than L2 (126 MB),
 so every step streams it from HBM (no flush needed).
@@ -327,8 +327,8 @@ def _request_shard(args, lc, torch, dist, dev, local, rank, world, codec, peak):
 
     def step():
         for layer in range(L):
-            cache.append(layer, ids, k1[layer], v1[layer])
-            cache.decode_attn(layer, ids, qs[layer], hq, 1.0, out=out[layer], out_dtype=lc.LC_BF16)
+            cache.decode_step(layer, ids, k1[layer], v1[layer], qs[layer], hq, 1.0, out=out[layer],
+                              out_dtype=lc.LC_BF16)
 
     ms = _time_steps(torch, dist, step, steps, warm, world)
     n0 = cache.ring_state(0, 0)["view_len"]
@@ -378,8 +378,8 @@ def _head_shard(args, lc, torch, dist, dev, local, rank, world, codec, peak):
 
     def step():
         for layer in range(L):
-            cache.append(layer, ids, k1[layer], v1[layer])
-            cache.decode_attn(layer, ids, qs[layer], hk * G, 1.0, out=out[layer], out_dtype=lc.LC_BF16)
+            cache.decode_step(layer, ids, k1[layer], v1[layer], qs[layer], hk * G, 1.0, out=out[layer],
+                              out_dtype=lc.LC_BF16)
 
     ms = _time_steps(torch, dist, step, steps, warm, world)
     n0 = cache.ring_state(0, 0)["view_len"]
@@ -534,10 +534,11 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     def step():
+        # per layer: append the new token and attend (lc_decode_step; the
+        # append launch also rotates the queries)
         for layer in range(L):
-            cache.append(layer, ids, k1[layer], v1[layer], stream=stream_ptr)
-            cache.decode_attn(layer, ids, qs[layer], hq, 1.0, out=out[layer], out_dtype=lc.LC_BF16,
-                              stream=stream_ptr)
+            cache.decode_step(layer, ids, k1[layer], v1[layer], qs[layer], hq, 1.0, out=out[layer],
+                              out_dtype=lc.LC_BF16, stream=stream_ptr)
 
     for _ in range(warm):
         step()
@@ -573,8 +574,7 @@ def run_ours(args):
     cache.timing(1)
     for _ in range(t_steps):
         for layer in range(L):
-            cache.append(layer, ids, k1[layer], v1[layer], stream=stream_ptr)
-            cache.decode_attn(layer, ids, qs[layer], hq, 1.0, flags=rot_flags, out=out[layer],
+            cache.decode_step(layer, ids, k1[layer], v1[layer], qs[layer], hq, 1.0, flags=rot_flags, out=out[layer],
                               out_dtype=lc.LC_BF16, stream=stream_ptr)
     rdec_ms, rdec_n, _, _, _ = cache.timing(0)
     ctx3 = cache.ring_state(0, 0)["view_len"]
@@ -667,8 +667,8 @@ def run_ours(args):
         for i, (c0, c1) in enumerate(bounds):
             comp.wait_event(ev_in[st][i])
             for layer in range(c0, c1):
-                cache.append(layer, ids, kd[st][layer], vd[st][layer])
-                cache.decode_attn(layer, ids, qd[st][layer], hq, 1.0, out=od[st][layer], out_dtype=lc.LC_BF16)
+                cache.decode_step(layer, ids, kd[st][layer], vd[st][layer], qd[st][layer], hq, 1.0,
+                                  out=od[st][layer], out_dtype=lc.LC_BF16)
             ev_out[st][i].record(comp)
             down.wait_event(ev_out[st][i])
             with torch.cuda.stream(down):
