@@ -319,6 +319,17 @@ int lc_prefill_attn(lc_cache* cache, int32_t layer, int32_t seq, const void* q, 
                     int32_t n_q_tokens, int32_t n_q_heads, float scale, uint32_t flags, void* out,
                     int32_t out_dtype, void* stream);
 
+/* One decode step of a layer: NativeRotatingKvCacheTurboQuant::
+ * update_and_fetch of each sequence's new token followed by
+ * turboquant_fused_attn on the rotated query (gemma4_moe.rs:4245-4797), as
+ * lc_append (keys / values [n_seqs, n_kv_heads, 1, head_dim]) then
+ * lc_decode_attn. The queries are rotated by the launch that rotates and
+ * quantizes the new keys, and the attention takes them rotated; results as
+ * the two calls (same flags, including LC_OUT_ROTATED). */
+int lc_decode_step(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+                   const void* values, int32_t kv_dtype, const void* q, int32_t q_dtype, int32_t n_q_heads,
+                   float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream);
+
 /* Bytes of the fixed device scratch lc_decode_attn_noalloc uses, per device. */
 #define LC_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 

@@ -49,7 +49,7 @@ ABI_SYMBOLS = [
     "lc_codec_tables", "lc_codec_shape", "lc_codec_free", "lc_packed_words", "lc_cache_create",
     "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_keys_qjl", "lc_attend_values", "lc_seq_len", "lc_clear",
     "lc_truncate", "lc_append", "lc_append_rope", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
-    "lc_decode_attn", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
+    "lc_decode_attn", "lc_decode_step", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_group_id", "lc_group_create", "lc_group_info", "lc_group_status", "lc_group_destroy", "lc_decode_attn_split",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
@@ -127,6 +127,7 @@ def lib():
         "lc_lkv2_info": (C.c_int, [C.c_char_p, C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_uint64)]),
         "lc_decode_attn": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_noalloc": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
+        "lc_decode_step": (C.c_int, [vp, i32, i32, vp, vp, vp, i32, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_prefill_attn": (C.c_int, [vp, i32, i32, vp, i32, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_partials": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, vp, vp, vp]),
         "lc_merge_partials": (C.c_int, [vp, i32, i32, vp, vp, vp, u32, vp, i32, vp]),
@@ -425,6 +426,22 @@ class CudaKvCache:
         stream = _auto_stream(stream, q, out)
         _check(lib().lc_decode_attn(self._h, layer, len(ids), _ptr(ids), _ptr(q), _dtype_code(q), n_q_heads,
                                     scale, flags, _ptr(out), out_dtype, stream))
+        return out
+
+    def decode_step(self, layer: int, seq_ids, keys, values, q, n_q_heads: int, scale: float = 1.0, flags: int = 0,
+                    out=None, out_dtype: int = LC_F32, stream=None):
+        """append each sequence's new token (keys / values [n_seqs, n_kv_heads, 1, head_dim]), then
+        decode_attn; the queries are rotated by the append launch."""
+        ids = np.ascontiguousarray(seq_ids, np.int32)
+        if isinstance(keys, np.ndarray):
+            keys = np.ascontiguousarray(keys, np.float32)
+            values = np.ascontiguousarray(values, np.float32)
+        if out is None:
+            out = np.empty((len(ids), n_q_heads, self.head_dim), np.float32)
+            out_dtype = LC_F32
+        stream = _auto_stream(stream, q, keys, out)
+        _check(lib().lc_decode_step(self._h, layer, len(ids), _ptr(ids), _ptr(keys), _ptr(values), _dtype_code(keys),
+                                    _ptr(q), _dtype_code(q), n_q_heads, scale, flags, _ptr(out), out_dtype, stream))
         return out
 
     def prefill_attn(self, layer: int, seq: int, q, n_q_heads: int, scale: float = 1.0, flags: int = 0, out=None,

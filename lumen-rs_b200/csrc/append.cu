@@ -26,6 +26,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace lc {
@@ -51,6 +53,10 @@ struct AppendDev {
   // RoPE on the K side (lc_append_rope), see AppendArgs
   const float* rope_cs;
   int32_t rope_half, rope_traditional;
+  // decode-step queries rotated in the same launch (grid row 2), see AppendArgs
+  const void* q;
+  int32_t q_dtype, q_rows;
+  float* q_out;
   // small calls (decode steps): destinations in the launch parameters
   uint64_t ipage[kAppendInline];
   int32_t irow[kAppendInline];
@@ -337,6 +343,7 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
 // products in parallel and added in order by lane 0 (the same f32 result
 // as the reference's fold). Operation order as k_append_strict.
 constexpr int kWarpVecs = 4;
+constexpr int kQRows = 3;  // decode-step query rows per warp (grid row 2)
 constexpr int kRtChunk = 32;  // rows of R^T per shared-memory chunk when R^T does not fit
 
 __device__ __forceinline__ float seq_sum(const float* v, int n, float init) {
@@ -365,10 +372,11 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   constexpr int D = 32 * R;
   pdl_launch_dependents();
   extern __shared__ __align__(16) uint8_t smem[];
-  const int side = blockIdx.y;
-  const CodecDev& c = a.codec[side];
+  const int side = blockIdx.y;  // 0 K, 1 V, 2 the step's queries (K's rotation)
+  const int cs = side == 1 ? 1 : 0;
+  const CodecDev& c = a.codec[cs];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool stage2 = a.role_qjl[side] >= 0;
+  const bool stage2 = a.role_qjl[cs] >= 0;
   const int M = c.m;
   const int n1 = c.n_levels - 1;
   // ---- shared: [thr 256][cent 256][per warp: x, y, r (D each), sq 16 u32, codes D][tables] ----
@@ -406,6 +414,47 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   // written below may belong to the previous kernel of the stream
   pdl_wait();
   __syncthreads();
+  if (TAB && side == 2) {
+    // q'[i] = sum_j R[i][j] q[j] for kQRows query rows per warp (plain f32
+    // FMAs: the decode scores are not bit-exact work), rows in the warp's
+    // x, y and res buffers, R^T from the staged table
+    const int64_t r0 = ((int64_t)blockIdx.x * kWarpVecs + warp) * kQRows;
+    float* rows[kQRows] = {x, y, res};
+    bool live[kQRows];
+#pragma unroll
+    for (int k = 0; k < kQRows; ++k) {
+      live[k] = r0 + k < a.q_rows;
+      if (live[k]) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) rows[k][lane + 32 * r] = load_elem(a.q, a.q_dtype, (r0 + k) * D + lane + 32 * r);
+      }
+    }
+    __syncwarp();
+    float qa[kQRows][R];
+#pragma unroll
+    for (int k = 0; k < kQRows; ++k)
+#pragma unroll
+      for (int r = 0; r < R; ++r) qa[k][r] = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < D; ++j) {
+      float w[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) w[r] = RT[j * D + lane + 32 * r];
+#pragma unroll
+      for (int k = 0; k < kQRows; ++k) {
+        const float qj = rows[k][j];
+#pragma unroll
+        for (int r = 0; r < R; ++r) qa[k][r] = fmaf(w[r], qj, qa[k][r]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kQRows; ++k)
+      if (live[k]) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) a.q_out[(r0 + k) * D + lane + 32 * r] = qa[k][r];
+      }
+    return;  // TAB: no block-wide barrier after this point
+  }
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const int64_t v = (int64_t)blockIdx.x * kWarpVecs + warp;
   const bool active = v < n_vec;
@@ -575,7 +624,9 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
   // Programmatic serialization: the table staging overlaps the previous
   // kernel's tail (the kernel waits for it before touching inputs or pages).
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((n_vec + kWarpVecs - 1) / kWarpVecs), 2);
+  int64_t gx = (n_vec + kWarpVecs - 1) / kWarpVecs;
+  if (d.q) gx = std::max<int64_t>(gx, (d.q_rows + kWarpVecs * kQRows - 1) / (kWarpVecs * kQRows));
+  cfg.gridDim = dim3((unsigned)gx, d.q ? 3 : 2);
   cfg.blockDim = dim3(kWarpVecs * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -589,6 +640,13 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
 }
 
 }  // namespace
+
+bool append_rotates_queries(int64_t n_vec, int dim, int m_max, bool stage2) {
+  if (n_vec > kSmallAppend || m_max > 512 || !(dim == 64 || dim == 128)) return false;
+  const size_t base = 2048 + (size_t)kWarpVecs * (3 * dim * 4 + 64 + dim);
+  const size_t tables = (size_t)dim * dim * 4 + (stage2 ? (size_t)(dim * dim + dim * m_max) * 4 : 0);
+  return base + tables <= 200 * 1024;  // the warp kernel with R^T staged (TAB)
+}
 
 size_t append_smem_bytes(int d, int m) {
   const int qw32 = (m + 31) / 32;
@@ -636,6 +694,13 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
   }
   const int D = a.codec[0].dim;
   const int M = a.codec[0].m > a.codec[1].m ? a.codec[0].m : a.codec[1].m;
+  if (a.q) {
+    LC_REQUIRE(append_rotates_queries(n_vec, D, M, stage2), LC_ERR_STATE, "append cannot rotate these queries");
+    d.q = a.q;
+    d.q_dtype = a.q_dtype;
+    d.q_rows = a.q_rows;
+    d.q_out = a.q_out;
+  }
   if (n_vec <= kSmallAppend && M <= 512 && (D == 64 || D == 128 || D == 256)) {
     if (D == 64) launch_warp_append<2>(d, stage2, M, n_vec, s);
     else if (D == 128) launch_warp_append<4>(d, stage2, M, n_vec, s);

@@ -85,7 +85,7 @@ struct lc_cache {
   uint64_t* d_table = nullptr;  // [n_layers][max_seqs][max_pages_per_seq]
   cudaEvent_t ev_copy = nullptr;
   DevBuf<uint8_t> in_k, in_v, qbuf, outbuf, fetchbuf;
-  DevBuf<float> q_rot, part, hook_a, hook_b, hook_c, q_proj;
+  DevBuf<float> q_rot, part, hook_a, hook_b, hook_c, q_proj, q_step;
   DevBuf<__half> q_h;
   DevBuf<int32_t> ctr;  // fused decode arrival counters (zero between launches)
   DevBuf<int32_t> tile_map;  // page-sparse decode: logical -> physical tiles
@@ -201,10 +201,24 @@ struct RopeArgs {
   std::vector<float> cs;  // [n_seqs * n_tok][dims / 2][cos, sin]
 };
 
+// A decode step's queries for the append launch to rotate (lc_decode_step).
+struct StepQ {
+  const void* q = nullptr;  // device rows [rows][head_dim]
+  int32_t dtype = LC_F32, rows = 0;
+  float* out = nullptr;     // device [rows][head_dim] f32: R q
+};
+
 void run_append(lc_cache* c, int32_t n_seqs, int32_t h_in, int32_t h_base, int64_t n_tok,
                 const std::vector<uint64_t>& dst_page, const std::vector<int32_t>& dst_row, const void* k,
-                const void* v, int32_t dtype, cudaStream_t s, const RopeArgs* rope = nullptr) {
+                const void* v, int32_t dtype, cudaStream_t s, const RopeArgs* rope = nullptr,
+                const StepQ* sq = nullptr) {
   AppendArgs a;
+  if (sq) {
+    a.q = sq->q;
+    a.q_dtype = sq->dtype;
+    a.q_rows = sq->rows;
+    a.q_out = sq->out;
+  }
   if (rope) {
     a.rope_cs = static_cast<const float*>(c->arena.put(rope->cs.data(), rope->cs.size() * sizeof(float), s));
     a.rope_half = rope->dims / 2;
@@ -380,7 +394,8 @@ int lc_cache_timing(lc_cache* c, int32_t mode, double* decode_ms, uint64_t* deco
 }
 
 static void append_impl(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
-                        const void* values, int32_t dtype, int64_t n_tokens, void* stream, RopeArgs* rope) {
+                        const void* values, int32_t dtype, int64_t n_tokens, void* stream, RopeArgs* rope,
+                        const StepQ* sq = nullptr) {
   {
     LC_REQUIRE(c && seq_ids && keys && values, LC_ERR_INVALID, "null argument");
     LC_REQUIRE(n_seqs > 0 && n_tokens > 0, LC_ERR_INVALID, "n_seqs and n_tokens must be > 0");
@@ -447,7 +462,7 @@ static void append_impl(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_
     const void* dk = c->stage_in(keys, bytes, c->in_k, s, hk);
     const void* dv = c->stage_in(values, bytes, c->in_v, s, hv);
     if (hk || hv) LC_CUDA(cudaEventRecord(c->ev_copy, s));
-    run_append(c, n_seqs, H, 0, n_tokens, dst_page, dst_row, dk, dv, dtype, s, rope);
+    run_append(c, n_seqs, H, 0, n_tokens, dst_page, dst_row, dk, dv, dtype, s, rope, sq);
     if (hk || hv) LC_CUDA(cudaEventSynchronize(c->ev_copy));
     c->ops.stream = c->stream;
   }
@@ -1402,6 +1417,47 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
                    void* stream) {
   return abi_guard([&] {
     attn_call(c, layer, n_seqs, seq_ids, nullptr, q, q_dtype, n_q_heads, scale, flags, out, out_dtype, stream);
+  });
+}
+
+// One decode step of a layer: append each sequence's new token, then attend
+// (the reference's update_and_fetch followed by turboquant_fused_attn on the
+// rotated query, gemma4_moe.rs:4245-4797). The queries are rotated by the
+// same launch that rotates and quantizes the new keys, so the attention
+// kernel takes them rotated and skips its own rotation.
+int lc_decode_step(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+                   const void* values, int32_t kv_dtype, const void* q, int32_t q_dtype, int32_t n_q_heads,
+                   float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream) {
+  return abi_guard([&] {
+    LC_REQUIRE(c && seq_ids && keys && values && q && out, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_seqs > 0 && n_q_heads > 0, LC_ERR_INVALID, "bad decode arguments");
+    dtype_size(q_dtype);
+    LC_CUDA(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = c->pick(stream);
+    const int32_t D = c->cfg.head_dim, H = c->cfg.n_kv_heads;
+    const bool stage2 = (c->cfg.store_flags & (LC_STORE_K_QJL | LC_STORE_V_QJL)) != 0;
+    const int m_max = (int)std::max(c->kc.m, c->vc.m);
+    const bool rot = !(flags & (LC_Q_ROTATED | LC_QJL_SCORES)) &&
+                     append_rotates_queries((int64_t)n_seqs * H, D, m_max, stage2);
+    if (!rot) {
+      append_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, 1, stream, nullptr);
+      attn_call(c, layer, n_seqs, seq_ids, nullptr, q, q_dtype, n_q_heads, scale, flags, out, out_dtype, stream);
+      return;
+    }
+    const int64_t rows = (int64_t)n_seqs * n_q_heads;
+    c->order(s);
+    bool hq = false;
+    const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
+    c->q_step.ensure((size_t)rows * D, s);
+    StepQ sq;
+    sq.q = dq;
+    sq.dtype = q_dtype;
+    sq.rows = (int32_t)rows;
+    sq.out = c->q_step.p;
+    append_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, 1, stream, nullptr, &sq);
+    attn_call(c, layer, n_seqs, seq_ids, nullptr, c->q_step.p, LC_F32, n_q_heads, scale, flags | LC_Q_ROTATED, out,
+              out_dtype, stream);
+    if (hq) LC_CUDA(cudaStreamSynchronize(s));  // the staged queries are read before the host reuses them
   });
 }
 

@@ -55,7 +55,15 @@ struct AppendArgs {
   // token) slot rope_half (cos, sin) f32 pairs; null: no RoPE
   const float* rope_cs = nullptr;
   int32_t rope_half = 0, rope_traditional = 0;
+  // queries of the same decode step to rotate in this launch (lc_decode_step):
+  // q_out[r][:] = R q[r][:] (K codec R, f32) for r < q_rows; null: none
+  const void* q = nullptr;
+  int32_t q_dtype = LC_F32, q_rows = 0;
+  float* q_out = nullptr;
 };
+// Whether launch_append can rotate a decode step's queries in the same
+// launch (warp kernel with the K rotation staged in shared memory).
+bool append_rotates_queries(int64_t n_vec, int dim, int m_max, bool stage2);
 // Appends of at most this many (sequence, token) slots pass their destinations
 // in the launch parameters.
 constexpr int kAppendInline = 64;
