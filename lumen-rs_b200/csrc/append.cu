@@ -122,24 +122,6 @@ __device__ __forceinline__ void seq_matvec(const float* M, int ld, const float* 
   }
 }
 
-// Sum of 128..512 exact squares in index order, s = fl(s + sq[k]) for k
-// ascending (compressor.rs:70 / :88-93): vector v's squares sit rotated by
-// 4v in its row (sq[v * D + (k + 4v) % D]), so the kNB summing threads'
-// float4 reads fall in distinct banks, and the loads run ahead of the
-// dependent adds.
-__device__ __forceinline__ float ordered_square_sum(const float* sq_row, int v, int D, float s) {
-  const int sh = (4 * v) % D;
-#pragma unroll 8
-  for (int k = 0; k < D; k += 4) {
-    const float4 q = *reinterpret_cast<const float4*>(sq_row + (k + sh) % D);
-    s = __fadd_rn(s, q.x);
-    s = __fadd_rn(s, q.y);
-    s = __fadd_rn(s, q.z);
-    s = __fadd_rn(s, q.w);
-  }
-  return s;
-}
-
 // Shared memory of the batched kernel, per group: xs, ys, rs [kNB][D],
 // vscale, vinv, vrn [kNB], qbits, codes.
 struct GroupBufs {
@@ -222,15 +204,16 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
     for (int v = 0; v < kNB; ++v) acc[v] = -0.0f;
     seq_matvec(RT, D, xs, D, i, acc);
 #pragma unroll
-    for (int v = 0; v < kNB; ++v) {
-      ys[v * D + i] = acc[v];
-      rs[v * D + (i + 4 * v) % D] = __fmul_rn(acc[v], acc[v]);  // exact squares, skewed rows
-    }
+    for (int v = 0; v < kNB; ++v) ys[v * D + i] = acc[v];
     __syncthreads();
 
     // ---- scale = sqrt(norm_sq / d), one vector per thread (compressor.rs:70-71) ----
     if (i < kNB) {
-      const float s = ordered_square_sum(rs + i * D, i, D, -0.0f);
+      float s = -0.0f;
+      for (int k = 0; k < D; ++k) {
+        const float y = ys[i * D + k];
+        s = __fadd_rn(s, __fmul_rn(y, y));
+      }
       const float sc = __fsqrt_rn(__fdiv_rn(s, (float)D));
       vscale[i] = sc;
       vinv[i] = __fdiv_rn(1.0f, sc);
@@ -260,16 +243,18 @@ __global__ void k_append_strict(const __grid_constant__ AppendDev a) {
 #pragma unroll
       for (int v = 0; v < kNB; ++v) acc[v] = 0.0f;
       seq_matvec(R, D, ys, D, i, acc);
-      __syncthreads();  // every thread is done reading ys (the dequantized values)
 #pragma unroll
-      for (int v = 0; v < kNB; ++v) {
-        const float r = __fsub_rn(xs[v * D + i], acc[v]);
-        rs[v * D + i] = r;
-        ys[v * D + (i + 4 * v) % D] = __fmul_rn(r, r);  // exact squares, skewed rows
-      }
+      for (int v = 0; v < kNB; ++v) rs[v * D + i] = __fsub_rn(xs[v * D + i], acc[v]);
       __syncthreads();
       // ---- residual norm (compressor.rs:88-93) ----
-      if (i < kNB) vrn[i] = __fsqrt_rn(ordered_square_sum(ys + i * D, i, D, 0.0f));
+      if (i < kNB) {
+        float s = 0.0f;
+        for (int k = 0; k < D; ++k) {
+          const float r = rs[i * D + k];
+          s = __fadd_rn(s, __fmul_rn(r, r));
+        }
+        vrn[i] = __fsqrt_rn(s);
+      }
       // ---- QJL sign bits (qjl.rs:57-74) ----
       for (int rbase = 0; rbase < M; rbase += D) {
         const int r = rbase + i;
