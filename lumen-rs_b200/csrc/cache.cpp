@@ -1242,7 +1242,8 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   const int64_t rows = (int64_t)n_seqs * n_q_heads;
   bool hq = false;
   const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
-  const float kalpha = plan.flat ? c->dk.alpha : 1.0f, valpha = plan.flat ? c->dv.alpha : 1.0f;
+  const float kalpha = (plan.flat || plan.mma) ? c->dk.alpha : 1.0f,
+              valpha = (plan.flat || plan.mma) ? c->dv.alpha : 1.0f;
   const float qscale = scale * 1.4426950408889634f / kalpha;
   if (!fused) {
     c->q_rot.ensure((size_t)rows * D, s);
@@ -1673,7 +1674,8 @@ int lc_decode_attn_noalloc(lc_cache* c, int32_t layer, int32_t n_seqs, const int
     __half* const q_h = reinterpret_cast<__half*>(dscr + d_meta + d_qrot);
     float* const part = reinterpret_cast<float*>(dscr + d_meta + d_qrot + d_qh);
 
-    const float kalpha = plan.flat ? c->dk.alpha : 1.0f, valpha = plan.flat ? c->dv.alpha : 1.0f;
+    const float kalpha = (plan.flat || plan.mma) ? c->dk.alpha : 1.0f,
+              valpha = (plan.flat || plan.mma) ? c->dv.alpha : 1.0f;
     launch_rotate_q(q, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0,
                     scale * 1.4426950408889634f / kalpha, q_rot, q_h, s);
     ++c->launches;

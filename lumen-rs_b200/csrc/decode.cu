@@ -1885,6 +1885,347 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// 3-bit K / 2-bit V at head_dim 256 on the tensor cores (the sliding and
+// global layers of the mixed-precision geometry). Same partition as the
+// generic path: an item is (sequence, kv head, chunk of pages) with all
+// G <= 4 query heads; the block's warps take the chunk's 16-token tiles in
+// turn through a per-warp cp.async double buffer, and the block merges its
+// warps' partials into the chunk's slot. One block per SM.
+//
+// QK^T (S^T = K_dq Q^T: 16 tokens x 8 columns, column n = (head n / 2, f16
+// part n % 2) as in the pair layout of the 4-bit path). A K word holds 21
+// 3-bit codes (bit 63 zero, bitpack.rs); codes are read in pairs, pair p at
+// bits 6p..6p+5 (the 11th pair's second code is the zero bit). Lane t of an
+// MMA owns word 4v + t of word group v: in k-step j of the group its slots
+// t and t + 4 are pairs 2j and 2j + 1 of that word, so every shift is a
+// compile-time constant. Groups 0..2 (words 0..11) take 6 k-steps each, word
+// 12 (dims 252..255) one: 19 k-steps. A pair indexes a 64-entry table of f16
+// pairs (alpha c_a, alpha c_b), one copy per lane; the query fragments hold
+// zeros at the slots of pair 11, of bit 63 and past dim 255, so whatever the
+// table returns there adds nothing.
+//
+// PV (O^T = V_dq^T P^T, 16 m-tiles of dims). A V u32 holds 16 2-bit codes.
+// Two tokens' u32s interleave into nibbles (token a's code | token b's << 2),
+// one word for the even dims and one for the odd; byte k of either indexes a
+// 256-entry table of u32 pairs (its two nibbles dequantized as f16 pairs), so
+// one PRMT-addressed 8-byte load feeds two m-tiles. M-tile i, row g is dim
+// 16 g + i and row g + 8 is dim 128 + 16 g + i; the k columns are tokens
+// (t, t + 8) and (t + 4, t + 12) as in the 4-bit path.
+//
+// Precise tiles (large sigma_K x ||q'||, see kLoEta): the K pass is run a
+// second time over the residual table (alpha c - f16(alpha c)) x 2^11.
+// ---------------------------------------------------------------------------
+constexpr int kM3Warps = 16;
+constexpr int kM3TT = 16;
+constexpr int kM3KRow = 104, kM3VRow = 64;  // bytes per token: 13 K words, 8 V words
+constexpr int kM3KWords = 13;
+constexpr int kM3Stage = kM3TT * (kM3KRow + kM3VRow) + 2 * kM3TT * 4;  // 2816
+constexpr int kM3Unit = 2 * kM3Stage;  // a warp's two stages
+constexpr int kM3KSteps = 19;
+constexpr int kM3D = 256, kM3PS = kM3D + 2;
+// tables, contiguous from a 64 KiB-aligned shared address: V bytes (256 x 32
+// lanes x 8 B), K pairs (64 x 32 x 4 B), K pair residuals (64 x 32 x 4 B)
+constexpr int kM3TabK = 65536, kM3TabKLo = 65536 + 8192, kM3Tab = 65536 + 2 * 8192;
+// units of kM3Unit bytes around the tables: one per warp (its stages, then
+// its partial of the item), one for the query fragments and head norms
+constexpr int kM3Units = kM3Warps + 1;
+constexpr int kM3Smem = kM3Tab + (kM3Units + 1) * kM3Unit;
+static_assert(kM3KSteps * 32 * 8 + 4 * 4 <= kM3Unit, "query fragments fit a unit");
+static_assert(4 * kM3PS * 4 <= kM3Unit, "a warp partial fits its unit");
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+// address of the K table entry of the 6-bit field at bit s of x (s constant
+// after unrolling): field << 7 | base (base: 8 KiB-aligned table | lane * 4)
+__device__ __forceinline__ uint32_t m3_kaddr(uint64_t x, int s, uint32_t base) {
+  const uint32_t f = s >= 7 ? (uint32_t)(x >> (s - 7)) : (uint32_t)x << (7 - s);
+  return (f & (63u << 7)) | base;
+}
+// J k-steps of one word group: x0 / x1 the lane's word of tokens g / g + 8
+template <int J>
+__device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab, uint32_t qf, float (&c)[4]) {
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const uint32_t a0 = lds32(m3_kaddr(x0, 12 * j, tab)), a1 = lds32(m3_kaddr(x1, 12 * j, tab));
+    uint32_t a2 = 0u, a3 = 0u;
+    if (j < 5) {
+      a2 = lds32(m3_kaddr(x0, 12 * j + 6, tab));
+      a3 = lds32(m3_kaddr(x1, 12 * j + 6, tab));
+    }
+    const uint2 b = lds64(qf + j * 256);
+    mma16816(c, a0, a1, a2, a3, b.x, b.y);
+  }
+}
+// S^T += Ktab(K) Q^T over the 19 k-steps; kb: the stage's K words
+__device__ __forceinline__ void m3_qk(const uint64_t* kb, int g, int t, uint32_t tab, uint32_t qf, float (&c)[4]) {
+#pragma unroll 1
+  for (int v = 0; v < 3; ++v)
+    m3_group<6>(kb[g * kM3KWords + 4 * v + t], kb[(g + 8) * kM3KWords + 4 * v + t], tab, qf + v * 6 * 256, c);
+  // word 12 + t: lanes t > 0 read the next row's words (zero query slots)
+  m3_group<1>(kb[g * kM3KWords + 12 + t], kb[(g + 8) * kM3KWords + 12 + t], tab, qf + 18 * 256, c);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_constant__ DecodeDev a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+  const uint32_t tab_off = (65536u - (s0 & 0xFFFFu)) & 0xFFFFu;
+  const int n_before = min((int)(tab_off / kM3Unit), kM3Units);
+  auto unit = [&](int u) -> uint8_t* {
+    return u < n_before ? smem + u * kM3Unit : smem + tab_off + kM3Tab + (u - n_before) * kM3Unit;
+  };
+  uint8_t* tab = smem + tab_off;
+  const uint32_t tab_s = s0 + tab_off;  // 64 KiB-aligned
+  {
+    uint32_t* vt = reinterpret_cast<uint32_t*>(tab);
+    for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
+      const int b = idx >> 6, n = (idx & 1) ? b >> 4 : b & 15;
+      vt[idx] = h2_as_u32(__floats2half2_rn(a.vcent[n & 3] * a.valpha, a.vcent[n >> 2] * a.valpha));
+    }
+    uint32_t* kt = reinterpret_cast<uint32_t*>(tab + kM3TabK);
+    uint32_t* kl = reinterpret_cast<uint32_t*>(tab + kM3TabKLo);
+    for (int idx = threadIdx.x; idx < 64 * 32; idx += blockDim.x) {
+      const int e = idx >> 5;
+      const float x0 = a.kcent[e & 7] * a.kalpha, x1 = a.kcent[e >> 3] * a.kalpha;
+      kt[idx] = h2_as_u32(__floats2half2_rn(x0, x1));
+      kl[idx] = h2_as_u32(__floats2half2_rn((x0 - __half2float(__float2half_rn(x0))) * kLoScale,
+                                            (x1 - __half2float(__float2half_rn(x1))) * kLoScale));
+    }
+  }
+  const uint32_t vlane = tab_s | ((uint32_t)lane << 3);
+  const uint32_t ktab_s = tab_s + kM3TabK + ((uint32_t)lane << 2);
+  const uint32_t klo_s = tab_s + kM3TabKLo + ((uint32_t)lane << 2);
+  uint8_t* qunit = unit(kM3Warps);
+  uint32_t* qfrag = reinterpret_cast<uint32_t*>(qunit);
+  float* qnorm = reinterpret_cast<float*>(qunit + kM3KSteps * 32 * 8);
+  const uint32_t qf_s = (uint32_t)__cvta_generic_to_shared(qunit) + lane * 8;
+  uint8_t* wunit = unit(warp);
+  const uint32_t st_s = (uint32_t)__cvta_generic_to_shared(wunit);
+
+  const int64_t total = (int64_t)a.n_seqs * a.hkv * a.n_chunks;
+  for (int64_t item = blockIdx.x; item < total; item += gridDim.x) {
+    const int chunk = (int)(item % a.n_chunks);
+    const int64_t rest = item / a.n_chunks;
+    const int kvh = (int)(rest % a.hkv);
+    const int sq = (int)(rest / a.hkv);
+    const int64_t n_valid = a.si()[2 * sq];
+    const uint64_t* trow = a.table + a.si()[2 * sq + 1] * a.table_stride;
+    const float* qrow = a.q_rot + ((int64_t)sq * a.hq + (int64_t)kvh * G) * kM3D;
+    // query fragments in slot order: k-step ks, lane (n, tt) holds column n
+    // = (head n / 2, f16 part n % 2) at the pairs of slots tt and tt + 4
+    for (int u = threadIdx.x; u < kM3KSteps * 32; u += blockDim.x) {
+      const int ks = u >> 5, ln = u & 31, n = ln >> 2, tt = ln & 3;
+      const int head = n >> 1, part = n & 1;
+      const int v = ks < 18 ? ks / 6 : 3, j = ks < 18 ? ks % 6 : 0;
+      const int w = 4 * v + tt;
+      uint32_t bb[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float x[2] = {0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int pos = 2 * (2 * j + h) + e, d = 21 * w + pos;
+          if (head < G && pos < 21 && d < kM3D) x[e] = qrow[head * kM3D + d];
+        }
+        const __half2 hv = __floats2half2_rn(x[0], x[1]);
+        const float2 f = __half22float2(hv);
+        bb[h] = part ? h2_as_u32(__floats2half2_rn(x[0] - f.x, x[1] - f.y)) : h2_as_u32(hv);
+      }
+      qfrag[u * 2] = bb[0];
+      qfrag[u * 2 + 1] = bb[1];
+    }
+    if (warp < G) {  // ||q'||^2 per head, for the precise-tile test
+      float s2 = 0.f;
+      for (int d = lane; d < kM3D; d += 32) {
+        const float v = qrow[warp * kM3D + d];
+        s2 = fmaf(v, v, s2);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      if (lane == 0) qnorm[warp] = s2;
+    }
+    __syncthreads();
+    float qn2 = 0.f;
+#pragma unroll
+    for (int h = 0; h < G; ++h) qn2 = fmaxf(qn2, qnorm[h]);
+    const float lthr = a.klo_thr * rsqrtf(qn2);
+
+    float m = -INFINITY, l = 0.f;
+    float oacc[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+    const int p0 = chunk * a.pages_per_chunk;
+    const int64_t ctok = n_valid - (int64_t)p0 * kPageTokens;
+    const int64_t cmax = (int64_t)a.pages_per_chunk * kPageTokens;
+    const int chunk_tok = (int)(ctok <= 0 ? 0 : (ctok < cmax ? ctok : cmax));
+    constexpr int tpp = kPageTokens / kM3TT;
+    const int ctiles = (chunk_tok + kM3TT - 1) / kM3TT;
+    const uint64_t my_page = lane < a.pages_per_chunk && (int64_t)(p0 + lane) * kPageTokens < n_valid ? trow[p0 + lane] : 0ull;
+    // a tile: K words, V words, sigma_K, sigma_V of 16 consecutive rows
+    auto issue = [&](int tl, int stg) {
+      const uint8_t* page = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, my_page, tl / tpp));
+      const int64_t r0 = (int64_t)kvh * kPageTokens + (tl % tpp) * kM3TT;
+      const uint8_t* kg = page + a.off_kw + r0 * kM3KRow;
+      const uint8_t* vg = page + a.off_vw + r0 * kM3VRow;
+      const uint8_t* ksg = page + a.off_ks + r0 * 4;
+      const uint8_t* vsg = page + a.off_vs + r0 * 4;
+      const uint32_t dst = st_s + stg * kM3Stage;
+      for (int c = lane; c < kM3TT * kM3KRow / 16; c += 32) cp_async16(dst + c * 16, kg + c * 16);
+      for (int c = lane; c < kM3TT * kM3VRow / 16; c += 32) cp_async16(dst + kM3TT * kM3KRow + c * 16, vg + c * 16);
+      if (lane < 8) cp_async16(dst + kM3TT * (kM3KRow + kM3VRow) + lane * 16, (lane < 4 ? ksg : vsg) + (lane & 3) * 16);
+      cp_commit();
+    };
+    if (warp < ctiles) issue(warp, 0);
+    for (int tl = warp, it = 0; tl < ctiles; tl += kM3Warps, ++it) {
+      if (tl + kM3Warps < ctiles) {
+        issue(tl + kM3Warps, (it + 1) & 1);
+        cp_wait_one();
+      } else {
+        cp_wait_all();
+      }
+      __syncwarp();
+      const uint8_t* st = wunit + (it & 1) * kM3Stage;
+      const uint32_t st_a = st_s + (it & 1) * kM3Stage;
+      const uint64_t* kb = reinterpret_cast<const uint64_t*>(st);
+      const uint32_t* vb = reinterpret_cast<const uint32_t*>(st + kM3TT * kM3KRow);
+      const float* ks = reinterpret_cast<const float*>(st + kM3TT * (kM3KRow + kM3VRow));
+      const float* vs = ks + kM3TT;
+      const int tok = tl * kM3TT;
+      const bool ok0 = tok + g < chunk_tok, ok1 = tok + g + 8 < chunk_tok;
+      // ---- S^T: lane (g, t) gets head t at tokens g and g + 8 ----
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      m3_qk(kb, g, t, ktab_s, qf_s, c);
+      float y0 = c[0] + c[1], y1 = c[2] + c[3];
+      const float k0 = ks[g], k1 = ks[g + 8];
+      if (__any_sync(0xffffffffu, t < G && fmaxf(k0, k1) > lthr)) {
+        const float zm = fmaxf(ok0 ? y0 * k0 : -INFINITY, ok1 ? y1 * k1 : -INFINITY);
+        if (__any_sync(0xffffffffu, t < G && fmaxf(k0, k1) > lthr && zm > m - kLoTheta)) {
+          float cl[4] = {0.f, 0.f, 0.f, 0.f};
+          m3_qk(kb, g, t, klo_s, qf_s, cl);
+          y0 = fmaf(cl[0] + cl[1], kLoUnscale, y0);
+          y1 = fmaf(cl[2] + cl[3], kLoUnscale, y1);
+        }
+      }
+      const float s0_ = ok0 ? y0 * k0 : -INFINITY, s1_ = ok1 ? y1 * k1 : -INFINITY;
+      float mx = fmaxf(s0_, s1_);
+      if (__any_sync(0xffffffffu, mx > m + kTau)) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        if (mx > m + kTau) {
+          const float al = ex2(m - mx);
+          l *= al;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            oacc[i][0] *= al;
+            oacc[i][1] *= al;
+            oacc[i][2] *= al;
+            oacc[i][3] *= al;
+          }
+          m = mx;
+        }
+      }
+      const float pp0 = ex2(s0_ - m), pp1 = ex2(s1_ - m);
+      l += pp0 + pp1;
+      // V words of tokens (t, t + 8) and (t + 4, t + 12), read before the
+      // P^T exchange reuses the stage's K area
+      uint32_t ev[2][2], od[2][2];  // [word g / g + 8][token pair]
+#pragma unroll
+      for (int wv = 0; wv < 2; ++wv)
+#pragma unroll
+        for (int tp = 0; tp < 2; ++tp) {
+          const uint32_t va = vb[(t + 4 * tp) * 16 + g + 8 * wv], vbb = vb[(t + 8 + 4 * tp) * 16 + g + 8 * wv];
+          ev[wv][tp] = (va & 0x33333333u) | ((vbb & 0x33333333u) << 2);
+          od[wv][tp] = ((va >> 2) & 0x33333333u) | (vbb & 0xCCCCCCCCu);
+        }
+      // P^T fragments: lane (g, t) holds p' of head t at tokens g, g + 8 and
+      // reads column g = (head g / 2, part g & 1) at token pairs t, t + 4
+      // (the layout of p_exchange, one 16-token half)
+      uint32_t pb0, pb1;
+      {
+        const float pa = ok0 ? pp0 * vs[g] : 0.f, pz = ok1 ? pp1 * vs[g + 8] : 0.f;
+        uint32_t* ps = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(st));
+        const __half2 h0 = __floats2half2_rn(pa, pz);
+        const float2 f0 = __half22float2(h0);
+        const uint32_t l0 = h2_as_u32(__floats2half2_rn(pa - f0.x, pz - f0.y));
+        __syncwarp();
+        ps[t * 8 + g] = h2_as_u32(h0);
+        ps[32 + t * 8 + (g ^ 4)] = l0;
+        __syncwarp();
+        const int head = g >> 1, part = g & 1;
+        const int base = part * 32 + head * 8, sw = part << 2;
+        pb0 = head < G ? ps[base + (t ^ sw)] : 0u;
+        pb1 = head < G ? ps[base + ((t + 4) ^ sw)] : 0u;
+      }
+      (void)st_a;
+      // ---- O^T += V^T P^T ----
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int par = 0; par < 2; ++par) {
+          const uint32_t sel = 0x7604u | ((uint32_t)k << 4);
+          const uint2 r0 = lds64(__byte_perm(par ? od[0][0] : ev[0][0], vlane, sel));
+          const uint2 r1 = lds64(__byte_perm(par ? od[1][0] : ev[1][0], vlane, sel));
+          const uint2 r2 = lds64(__byte_perm(par ? od[0][1] : ev[0][1], vlane, sel));
+          const uint2 r3 = lds64(__byte_perm(par ? od[1][1] : ev[1][1], vlane, sel));
+          mma16816(oacc[4 * k + par], r0.x, r1.x, r2.x, r3.x, pb0, pb1);
+          mma16816(oacc[4 * k + 2 + par], r0.y, r1.y, r2.y, r3.y, pb0, pb1);
+        }
+      __syncwarp();  // the stage is refilled by the next issue
+    }
+    // ---- the warp's partial of the chunk in its unit (its copies are done):
+    // head t, dims 16 g + i (rows g) and 128 + 16 g + i (rows g + 8) ----
+    float L = l;
+    L += __shfl_xor_sync(0xffffffffu, L, 4);
+    L += __shfl_xor_sync(0xffffffffu, L, 8);
+    L += __shfl_xor_sync(0xffffffffu, L, 16);
+    __syncwarp();
+    float* wp = reinterpret_cast<float*>(wunit) + (t < G ? t : 0) * kM3PS;
+    if (t < G) {
+      if (g == 0) {
+        wp[0] = m;
+        wp[1] = L;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        wp[2 + 16 * g + i] = oacc[i][0] + oacc[i][1];
+        wp[2 + 128 + 16 * g + i] = oacc[i][2] + oacc[i][3];
+      }
+    }
+    __syncthreads();
+    for (int u = threadIdx.x; u < G * kM3PS; u += blockDim.x) {
+      const int hd = u / kM3PS, k = u % kM3PS;
+      float M = -INFINITY;
+      for (int w2 = 0; w2 < kM3Warps; ++w2) M = fmaxf(M, reinterpret_cast<const float*>(unit(w2))[hd * kM3PS]);
+      float val;
+      if (k == 0) {
+        val = M;
+      } else {
+        val = 0.f;
+        for (int w2 = 0; w2 < kM3Warps; ++w2) {
+          const float* wq = reinterpret_cast<const float*>(unit(w2)) + hd * kM3PS;
+          if (wq[0] != -INFINITY) val += exp2f(wq[0] - M) * wq[k];
+        }
+      }
+      const int64_t slot = ((int64_t)sq * a.hkv + kvh) * a.max_slots + chunk;
+      a.part[(slot * G + hd) * kM3PS + k] = val;
+    }
+    __syncthreads();
+  }
+}
+
 int g_num_sms = 0;
 
 template <int G>
@@ -1923,6 +2264,20 @@ void launch_pair_g(const DecodeDev& d, int grid, cudaStream_t s) {
     k_decode_pair<G, FUSED, SPARSE><<<(unsigned)grid, kFlatWarps * 32, smem, s>>>(d);
     LC_CUDA(cudaGetLastError());
   }
+}
+
+template <int G>
+void launch_mma32_g(const DecodeDev& d, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_decode_mma32<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kM3Smem));
+    attr = true;
+  }
+  const int64_t total = (int64_t)d.n_seqs * d.hkv * d.n_chunks;
+  const int64_t grid = std::min<int64_t>((int64_t)num_sms(), total);
+  if (grid <= 0) return;
+  k_decode_mma32<G><<<(unsigned)grid, kM3Warps * 32, kM3Smem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
 }
 
 template <int KPL, int GS, bool QJL>
@@ -1980,6 +2335,10 @@ bool decode_fast_path(int dim, int kbits, int vbits, int G) {
   return dim == 128 && kbits == 4 && vbits == 4 && G >= 1 && G <= 8;
 }
 
+bool decode_mma_path(int dim, int kbits, int vbits, int G) {
+  return dim == 256 && kbits == 3 && vbits == 2 && G >= 1 && G <= 4;
+}
+
 // Most (sequence, kv head) segments any CTA's tile range touches.
 static int32_t max_cta_segments(const int64_t* seg, const int64_t* lens, int n, int hkv, int64_t total, int64_t pw,
                                 int grid) {
@@ -2035,13 +2394,16 @@ static void plan_core(const int64_t* lens, int n, int hkv, int hq, int dim, int 
     p.max_cta_segs = max_cta_segments(seg, lens, n, hkv, p.total_tiles, p.per_warp, p.grid);
   } else {
     p.flat = false;
+    p.mma = !generic_only && decode_mma_path(dim, kbits, vbits, G);
     int64_t mx = 0;
     for (int b = 0; b < n; ++b) mx = lens[b] > mx ? lens[b] : mx;
     const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
-    // 4 pages per chunk, or fewer when that leaves too few (sequence, kv
-    // head, chunk) items to fill the GPU (short contexts, sliding windows)
-    int ppc = 4;
-    while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < 8LL * num_sms()) ppc >>= 1;
+    // 4 pages per chunk (8 on the tensor-core path, whose one block per SM
+    // has 16 warps), or fewer when that leaves too few (sequence, kv head,
+    // chunk) items to fill the GPU (short contexts, sliding windows)
+    int ppc = p.mma ? 8 : 4;
+    const int64_t want = (p.mma ? 4LL : 8LL) * num_sms();
+    while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < want) ppc >>= 1;
     p.pages_per_chunk = ppc;
     p.n_chunks = (int32_t)((pages + ppc - 1) / ppc > 0 ? (pages + ppc - 1) / ppc : 1);
     p.max_slots = p.n_chunks;
@@ -2161,6 +2523,16 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
       case 6: return launch_flat_g<6>(d, p.grid, s);
       case 7: return launch_flat_g<7>(d, p.grid, s);
       default: return launch_flat_g<8>(d, p.grid, s);
+    }
+  }
+  if (p.mma) {
+    LC_REQUIRE(!d.tile_map && !d.q_proj && d.row_kw == kM3KRow && d.row_vw == kM3VRow, LC_ERR_STATE,
+               "decode: the tensor-core 3/2-bit path takes dense calls without QJL");
+    switch (d.G) {
+      case 1: return launch_mma32_g<1>(d, s);
+      case 2: return launch_mma32_g<2>(d, s);
+      case 3: return launch_mma32_g<3>(d, s);
+      default: return launch_mma32_g<4>(d, s);
     }
   }
   switch (a.dim) {

@@ -159,6 +159,7 @@ inline bool decode_inline_fits(int n_seqs, int hkv) {
 // (one slot per chunk of pages_per_chunk pages).
 struct DecodePlan {
   bool flat = false;
+  bool mma = false;  // chunked, on the tensor cores (decode_mma_path geometry)
   int32_t grid = 0;
   int64_t per_warp = 1, total_tiles = 0;
   int32_t max_slots = 1;
@@ -172,6 +173,9 @@ struct DecodePlan {
 DecodePlan plan_decode(const std::vector<int64_t>& lens, int hkv, int hq, int dim, int kbits, int vbits,
                        bool generic_only = false);
 int num_sms();
+// The chunked geometry with a tensor-core kernel: 3-bit K, 2-bit V, head_dim
+// 256, up to 4 query heads per kv head.
+bool decode_mma_path(int dim, int kbits, int vbits, int G);
 
 // q_rot[s][h][:] = (R q[s][h]) * qscale (R applied unless q_is_rotated)
 void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim, const float* R,
