@@ -895,16 +895,33 @@ def run_window(args):
     dec_ms, dec_n, app_ms, app_n, other_ms = cache.timing(0)
     bpt = 8 * lc.packed_words(D, 3) + 8 * lc.packed_words(D, 2) + 8  # 176 B per (token, kv head)
     kv_bytes = B * hkv * bpt * sum(views)
+    # the global layer's decode kernel alone: per-launch CUDA events (the
+    # partials kernel; the query rotation and the slot merge are timed apart),
+    # 738 MB of packed KV per launch, above L2
+    g_layer = layers.index(0)
+    n_g = 10
+    torch.cuda.synchronize()
+    cache.timing(1)
+    for _ in range(n_g):
+        cache.decode_attn(g_layer, ids, qs[g_layer], hq, 1.0 / D ** 0.5, out=out[g_layer], out_dtype=lc.LC_BF16)
+    g_ms, g_n, _, _, g_other = cache.timing(0)
+    g_us = g_ms / max(1, g_n) * 1e3
+    g_bytes = B * hkv * bpt * views[g_layer]
+    peak, peak_kind = measured_peaks()
+    g_gbs = g_bytes / (g_us * 1e-6) / 1e9
     print(json.dumps({
         "metric": METRIC, "value": B / (ms_step / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": steps,
         "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32 (generic kernel)", "data": "synthetic", "mode": "window",
+        "dtype": "f16 tensor-core products, f32 softmax", "data": "synthetic", "mode": "window",
         "config": {"workload": f"config2: batch {B}, {hq}q/{hkv}kv, d{D}, 3-bit K / 2-bit V, 5 sliding layers "
                                f"(ring {win}, wrapped 4x) + 1 global layer ({glob_ctx} tokens); append + decode "
                                f"per layer", "views": views},
         "decode_gbs": kv_bytes / (ms_step / 1e3) / 1e9, "bytes_per_token_head": bpt,
         "breakdown_ms_per_step": {"decode_attn": dec_ms / t_steps, "append": app_ms / t_steps,
                                   "other_kernels (query rotation, merge)": other_ms / t_steps},
+        "roofline": {"bound": "hbm", "kernel": "k_decode_mma32 (global layer)", "achieved": g_gbs, "peak": peak,
+                     "unit": "GB/s", "frac": g_gbs / peak, "us_per_launch": g_us, "bytes_per_launch": g_bytes,
+                     "other_kernels_us": g_other / n_g * 1e3, "peak_source": f"{peak_kind} hbm_gbs"},
         "clocks": clk.summary(), "fill_s": fill_s,
     }), flush=True)
     cache.close()

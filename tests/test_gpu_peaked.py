@@ -16,7 +16,9 @@ against the oracle's attend_keys -> softmax(scale * s) -> attend_values.
 
 Covered: config 0 with q ~ N(0, 1) at scale 1; config 1's shape (GQA 4,
 8192 tokens) with unit-RMS q at scale 1; GQA 1-3 and 5-8 (the pair and flat
-kernels); the unfused partials path; page-sparse decode (test_gpu_sparse).
+kernels); the unfused partials path; config 2's geometry (3-bit K, 2-bit V,
+head_dim 256: the tensor-core chunked kernel) with unit-RMS q at scale 1 and
+GQA 1-4; page-sparse decode (test_gpu_sparse).
 """
 import numpy as np
 import pytest
@@ -28,23 +30,23 @@ pytestmark = pytest.mark.gpu
 DIM = 128
 
 
-def _setup(lc, orc, hkv, lens, seed):
-    tk = orc.Tables.generate(DIM, 4, 64, 42)
-    tv = orc.Tables.generate(DIM, 4, 64, 42)
+def _setup(lc, orc, hkv, lens, seed, dim=DIM, kbits=4, vbits=4):
+    tk = orc.Tables.generate(dim, kbits, 64, 42)
+    tv = orc.Tables.generate(dim, vbits, 64, 42)
     ck = lc.TurboQuantCompressor.from_tables(tk.R, tk.bounds, tk.cents, tk.proj)
     cv = lc.TurboQuantCompressor.from_tables(tv.R, tv.bounds, tv.cents, tv.proj)
     pages = (max(lens) + 255) // 256 + 1
-    cache = lc.CudaKvCache(1, hkv, DIM, ck, cv, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
+    cache = lc.CudaKvCache(1, hkv, dim, ck, cv, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
                            max_pages_per_seq=pages)
     ok, ov = orc.Compressor(tk), orc.Compressor(tv)
     refs = []
     for b, n in enumerate(lens):
-        K = helpers.kv(orc, seed + 2 * b, 1, hkv, n, DIM)
-        V = helpers.kv(orc, seed + 2 * b + 1, 1, hkv, n, DIM)
+        K = helpers.kv(orc, seed + 2 * b, 1, hkv, n, dim)
+        V = helpers.kv(orc, seed + 2 * b + 1, 1, hkv, n, dim)
         for c0 in range(0, n, 4096):
             c1 = min(n, c0 + 4096)
             cache.append(0, [b], np.ascontiguousarray(K[:, :, c0:c1]), np.ascontiguousarray(V[:, :, c0:c1]))
-        ref = orc.SimpleCache(ok, ov, 1, hkv, DIM)
+        ref = orc.SimpleCache(ok, ov, 1, hkv, dim)
         for h in range(hkv):
             ref.store(0, h, K[0, h], V[0, h], n)
         refs.append(ref)
@@ -139,4 +141,16 @@ def test_flat_regime_unchanged_by_precision_path(lc, orc, gpu):
     err = np.abs(got - ref)
     bound = 2e-3 + 1e-3 * np.abs(ref).max(-1, keepdims=True)
     assert (err / bound).max() < 0.5
+    cache.close()
+
+
+@pytest.mark.parametrize("hkv,hq,lens", [(8, 16, [6000, 1024]), (4, 4, [2500, 17]), (4, 12, [3000, 700]),
+                                         (2, 8, [4100, 256, 1])])
+def test_config2_geometry_unit_rms_q_scale1(lc, orc, gpu, hkv, hq, lens):
+    """3-bit K / 2-bit V at head_dim 256 (the Gemma geometry of config 2),
+    unit-RMS queries at scale 1.0, GQA 1-4, ragged and short lengths."""
+    cache, refs = _setup(lc, orc, hkv, lens, 400 + hq, dim=256, kbits=3, vbits=2)
+    q = _unit_rms(helpers.queries(orc, 40 + hq, len(lens), hq, 256))
+    got = cache.decode_attn(0, list(range(len(lens))), q, hq, 1.0)
+    _close(got, _oracle(refs, q, hkv, 1.0))
     cache.close()
