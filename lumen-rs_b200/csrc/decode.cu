@@ -330,6 +330,42 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
+// One-thread bulk copies global -> this CTA's shared memory, completing on an
+// mbarrier (complete_tx). Sources are this GPU's own memory; no multicast.
+// Waits are bounded: mbar_wait returns false when the phase did not complete
+// within kMbarSpin polls, and the caller poisons its result instead of
+// hanging.
+constexpr int kMbarSpin = 1 << 20;
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < kMbarSpin; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// orders this thread's generic-proxy shared accesses before later async-proxy
+// (bulk copy) writes to the same bytes
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Walks (sequence, kv head, tile) in flat order; nt = tiles per kv head of b.
 struct Walk {
   int b, kvh, tile, nt;
@@ -1917,7 +1953,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
 // Precise tiles (large sigma_K x ||q'||, see kLoEta): the K pass is run a
 // second time over the residual table (alpha c - f16(alpha c)) x 2^11.
 // ---------------------------------------------------------------------------
-constexpr int kM3Warps = 16;
+constexpr int kM3Warps = 12;
 constexpr int kM3TT = 16;
 constexpr int kM3KRow = 104, kM3VRow = 64;  // bytes per token: 13 K words, 8 V words
 constexpr int kM3KWords = 13;
@@ -1932,7 +1968,9 @@ constexpr int kM3TabK = 65536, kM3TabKLo = 65536 + 8192, kM3Tab = 65536 + 2 * 81
 // its partial of the item), one for the query fragments and head norms
 constexpr int kM3Units = kM3Warps + 1;
 constexpr int kM3Smem = kM3Tab + (kM3Units + 1) * kM3Unit;
-static_assert(kM3KSteps * 32 * 8 + 4 * 4 <= kM3Unit, "query fragments fit a unit");
+// the query unit: fragments, head norms [4], the warps' stage mbarriers [warps][2]
+constexpr int kM3OffNorm = kM3KSteps * 32 * 8, kM3OffBar = kM3OffNorm + 16;
+static_assert(kM3OffBar + kM3Warps * 16 <= kM3Unit, "query unit overflow");
 static_assert(4 * kM3PS * 4 <= kM3Unit, "a warp partial fits its unit");
 
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
@@ -2009,10 +2047,18 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
   const uint32_t klo_s = tab_s + kM3TabKLo + ((uint32_t)lane << 2);
   uint8_t* qunit = unit(kM3Warps);
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(qunit);
-  float* qnorm = reinterpret_cast<float*>(qunit + kM3KSteps * 32 * 8);
+  float* qnorm = reinterpret_cast<float*>(qunit + kM3OffNorm);
+  const uint32_t bar_s = (uint32_t)__cvta_generic_to_shared(qunit) + kM3OffBar + warp * 16;  // stage s: + 8 s
   const uint32_t qf_s = (uint32_t)__cvta_generic_to_shared(qunit) + lane * 8;
   uint8_t* wunit = unit(warp);
   const uint32_t st_s = (uint32_t)__cvta_generic_to_shared(wunit);
+  if (lane == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_s + 8, 1);
+    mbar_init_fence();
+  }
+  uint32_t ring = 0, cons = 0;  // tiles this warp issued / computed: stage count & 1, phase (count >> 1) & 1
+  bool err = false;             // a stage wait ran out: the warp's partials become NaN
 
   const int64_t total = (int64_t)a.n_seqs * a.hkv * a.n_chunks;
   for (int64_t item = blockIdx.x; item < total; item += gridDim.x) {
@@ -2073,31 +2119,32 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
     constexpr int tpp = kPageTokens / kM3TT;
     const int ctiles = (chunk_tok + kM3TT - 1) / kM3TT;
     const uint64_t my_page = lane < a.pages_per_chunk && (int64_t)(p0 + lane) * kPageTokens < n_valid ? trow[p0 + lane] : 0ull;
-    // a tile: K words, V words, sigma_K, sigma_V of 16 consecutive rows
-    auto issue = [&](int tl, int stg) {
-      const uint8_t* page = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, my_page, tl / tpp));
-      const int64_t r0 = (int64_t)kvh * kPageTokens + (tl % tpp) * kM3TT;
-      const uint8_t* kg = page + a.off_kw + r0 * kM3KRow;
-      const uint8_t* vg = page + a.off_vw + r0 * kM3VRow;
-      const uint8_t* ksg = page + a.off_ks + r0 * 4;
-      const uint8_t* vsg = page + a.off_vs + r0 * 4;
-      const uint32_t dst = st_s + stg * kM3Stage;
-      for (int c = lane; c < kM3TT * kM3KRow / 16; c += 32) cp_async16(dst + c * 16, kg + c * 16);
-      for (int c = lane; c < kM3TT * kM3VRow / 16; c += 32) cp_async16(dst + kM3TT * kM3KRow + c * 16, vg + c * 16);
-      if (lane < 8) cp_async16(dst + kM3TT * (kM3KRow + kM3VRow) + lane * 16, (lane < 4 ? ksg : vsg) + (lane & 3) * 16);
-      cp_commit();
-    };
-    if (warp < ctiles) issue(warp, 0);
-    for (int tl = warp, it = 0; tl < ctiles; tl += kM3Warps, ++it) {
-      if (tl + kM3Warps < ctiles) {
-        issue(tl + kM3Warps, (it + 1) & 1);
-        cp_wait_one();
-      } else {
-        cp_wait_all();
-      }
+    auto my_page_of = [&](int i) { return __shfl_sync(0xffffffffu, my_page, i); };
+    // a tile: K words, V words, sigma_K, sigma_V of 16 consecutive rows, four
+    // contiguous runs of the page, copied by lane 0 into stage ring & 1
+    auto issue = [&](int tl) {
+      fence_proxy_async();  // the stage's earlier reads and P^T writes come first
       __syncwarp();
-      const uint8_t* st = wunit + (it & 1) * kM3Stage;
-      const uint32_t st_a = st_s + (it & 1) * kM3Stage;
+      const uint8_t* page = reinterpret_cast<const uint8_t*>(my_page_of(tl / tpp));
+      if (lane == 0) {
+        const int64_t r0 = (int64_t)kvh * kPageTokens + (tl % tpp) * kM3TT;
+        const uint32_t dst = st_s + (ring & 1) * kM3Stage, bar = bar_s + (ring & 1) * 8;
+        mbar_expect_tx(bar, kM3Stage);
+        bulk_g2s(dst, page + a.off_kw + r0 * kM3KRow, kM3TT * kM3KRow, bar);
+        bulk_g2s(dst + kM3TT * kM3KRow, page + a.off_vw + r0 * kM3VRow, kM3TT * kM3VRow, bar);
+        bulk_g2s(dst + kM3TT * (kM3KRow + kM3VRow), page + a.off_ks + r0 * 4, kM3TT * 4, bar);
+        bulk_g2s(dst + kM3TT * (kM3KRow + kM3VRow + 4), page + a.off_vs + r0 * 4, kM3TT * 4, bar);
+      }
+      ++ring;
+    };
+    if (warp < ctiles) issue(warp);
+    for (int tl = warp; tl < ctiles; tl += kM3Warps) {
+      if (tl + kM3Warps < ctiles) issue(tl + kM3Warps);
+      const uint32_t stg = cons & 1;
+      if (!mbar_wait(bar_s + stg * 8, (cons >> 1) & 1)) err = true;
+      ++cons;
+      __syncwarp();
+      const uint8_t* st = wunit + stg * kM3Stage;
       const uint64_t* kb = reinterpret_cast<const uint64_t*>(st);
       const uint32_t* vb = reinterpret_cast<const uint32_t*>(st + kM3TT * kM3KRow);
       const float* ks = reinterpret_cast<const float*>(st + kM3TT * (kM3KRow + kM3VRow));
@@ -2139,17 +2186,26 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       }
       const float pp0 = ex2(s0_ - m), pp1 = ex2(s1_ - m);
       l += pp0 + pp1;
-      // V words of tokens (t, t + 8) and (t + 4, t + 12), read before the
-      // P^T exchange reuses the stage's K area
-      uint32_t ev[2][2], od[2][2];  // [word g / g + 8][token pair]
+      // V words g and g + 8 of tokens (t, t + 8) and (t + 4, t + 12), read
+      // before the P^T exchange reuses the stage's K area. Index word
+      // xv[tp][h][par], byte k: the token pair's nibble (a | b << 2) at dim
+      // 4k + 2h + par of word g, then the same of word g + 8, so that one
+      // 8-byte table entry is (row g, row g + 8) of an m-tile's A operand.
+      uint32_t xv[2][2][2];
 #pragma unroll
-      for (int wv = 0; wv < 2; ++wv)
+      for (int tp = 0; tp < 2; ++tp) {
+        uint32_t ev[2], od[2];  // word g, word g + 8
 #pragma unroll
-        for (int tp = 0; tp < 2; ++tp) {
+        for (int wv = 0; wv < 2; ++wv) {
           const uint32_t va = vb[(t + 4 * tp) * 16 + g + 8 * wv], vbb = vb[(t + 8 + 4 * tp) * 16 + g + 8 * wv];
-          ev[wv][tp] = (va & 0x33333333u) | ((vbb & 0x33333333u) << 2);
-          od[wv][tp] = ((va >> 2) & 0x33333333u) | (vbb & 0xCCCCCCCCu);
+          ev[wv] = (va & 0x33333333u) | ((vbb & 0x33333333u) << 2);
+          od[wv] = ((va >> 2) & 0x33333333u) | (vbb & 0xCCCCCCCCu);
         }
+        xv[tp][0][0] = (ev[0] & 0x0F0F0F0Fu) | ((ev[1] & 0x0F0F0F0Fu) << 4);
+        xv[tp][1][0] = ((ev[0] >> 4) & 0x0F0F0F0Fu) | (ev[1] & 0xF0F0F0F0u);
+        xv[tp][0][1] = (od[0] & 0x0F0F0F0Fu) | ((od[1] & 0x0F0F0F0Fu) << 4);
+        xv[tp][1][1] = ((od[0] >> 4) & 0x0F0F0F0Fu) | (od[1] & 0xF0F0F0F0u);
+      }
       // P^T fragments: lane (g, t) holds p' of head t at tokens g, g + 8 and
       // reads column g = (head g / 2, part g & 1) at token pairs t, t + 4
       // (the layout of p_exchange, one 16-token half)
@@ -2169,20 +2225,18 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
         pb0 = head < G ? ps[base + (t ^ sw)] : 0u;
         pb1 = head < G ? ps[base + ((t + 4) ^ sw)] : 0u;
       }
-      (void)st_a;
-      // ---- O^T += V^T P^T ----
+      // ---- O^T += V^T P^T: m-tile 4k + 2h + par ----
 #pragma unroll
       for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int par = 0; par < 2; ++par) {
-          const uint32_t sel = 0x7604u | ((uint32_t)k << 4);
-          const uint2 r0 = lds64(__byte_perm(par ? od[0][0] : ev[0][0], vlane, sel));
-          const uint2 r1 = lds64(__byte_perm(par ? od[1][0] : ev[1][0], vlane, sel));
-          const uint2 r2 = lds64(__byte_perm(par ? od[0][1] : ev[0][1], vlane, sel));
-          const uint2 r3 = lds64(__byte_perm(par ? od[1][1] : ev[1][1], vlane, sel));
-          mma16816(oacc[4 * k + par], r0.x, r1.x, r2.x, r3.x, pb0, pb1);
-          mma16816(oacc[4 * k + 2 + par], r0.y, r1.y, r2.y, r3.y, pb0, pb1);
-        }
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int par = 0; par < 2; ++par) {
+            const uint32_t sel = 0x7604u | ((uint32_t)k << 4);
+            const uint2 r0 = lds64(__byte_perm(xv[0][h][par], vlane, sel));  // a0, a1
+            const uint2 r1 = lds64(__byte_perm(xv[1][h][par], vlane, sel));  // a2, a3
+            mma16816(oacc[4 * k + 2 * h + par], r0.x, r0.y, r1.x, r1.y, pb0, pb1);
+          }
       __syncwarp();  // the stage is refilled by the next issue
     }
     // ---- the warp's partial of the chunk in its unit (its copies are done):
@@ -2191,6 +2245,7 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
     L += __shfl_xor_sync(0xffffffffu, L, 4);
     L += __shfl_xor_sync(0xffffffffu, L, 8);
     L += __shfl_xor_sync(0xffffffffu, L, 16);
+    if (__any_sync(0xffffffffu, err)) L = __int_as_float(0x7fc00000);  // NaN: the merged row shows it
     __syncwarp();
     float* wp = reinterpret_cast<float*>(wunit) + (t < G ? t : 0) * kM3PS;
     if (t < G) {
@@ -2223,6 +2278,13 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       a.part[(slot * G + hd) * kM3PS + k] = val;
     }
     __syncthreads();
+  }
+  // after a wait that ran out, the copies may still be in flight: wait for
+  // each stage's last phase (bounded) before the block's shared memory goes
+  if (__any_sync(0xffffffffu, err)) {
+    const uint32_t uses0 = (ring + 1) >> 1, uses1 = ring >> 1;
+    if (uses0) mbar_wait(bar_s, (uses0 - 1) & 1);
+    if (uses1) mbar_wait(bar_s + 8, (uses1 - 1) & 1);
   }
 }
 
@@ -2399,7 +2461,7 @@ static void plan_core(const int64_t* lens, int n, int hkv, int hq, int dim, int 
     for (int b = 0; b < n; ++b) mx = lens[b] > mx ? lens[b] : mx;
     const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
     // 4 pages per chunk (8 on the tensor-core path, whose one block per SM
-    // has 16 warps), or fewer when that leaves too few (sequence, kv head,
+    // has 12 warps), or fewer when that leaves too few (sequence, kv head,
     // chunk) items to fill the GPU (short contexts, sliding windows)
     int ppc = p.mma ? 8 : 4;
     const int64_t want = (p.mma ? 4LL : 8LL) * num_sms();
