@@ -1005,7 +1005,7 @@ def run_prefill(args):
     hkv, D, L = CFG["hkv"], CFG["dim"], 1
     B, n_new, chunk, prefix, n_req = 16, 16384, 2048, 4096, 64
     codec = lc.TurboQuantCompressor(lc.TurboQuantConfig(CFG["k_bits"], 64, 42, 1000, D))
-    pages = (n_new + 255) // 256 + 1
+    pages = (n_new + chunk + 255) // 256 + 1
     cache = lc.CudaKvCache(L, hkv, D, codec, codec, max_seqs=B + 1 + n_req,
                            max_pages=(B + 1) * pages + n_req * 2 + 64, max_pages_per_seq=pages, device=local)
     gen = torch.Generator(device=dev)
@@ -1037,6 +1037,41 @@ def run_prefill(args):
     ms = ev0.elapsed_time(ev1)
     vectors = B * n_new * hkv * 2
     bytes_alg = vectors * (D * 2 + 8 * 8 + 4)  # bf16 in; packed words + sigma out
+    # prefill attention: one more 2048-token chunk on sequence 0 (view 16384 +
+    # 2048), its queries attending causally over the view (lc_prefill_attn)
+    cache.append(0, [0], ks[0][:1].contiguous(), vs[0][:1].contiguous())
+    hq = CFG["hq"]
+    qp = (torch.randn((chunk, hq, D), generator=gen, device=dev) * D ** -0.5).to(torch.bfloat16)
+    outq = torch.empty((chunk, hq, D), device=dev, dtype=torch.bfloat16)
+    for _ in range(2):
+        cache.prefill_attn(0, 0, qp, hq, D ** -0.5, out=outq, out_dtype=lc.LC_BF16)
+    torch.cuda.synchronize()
+    reps = 5
+    cache.timing(1)
+    ev0.record()
+    for _ in range(reps):
+        cache.prefill_attn(0, 0, qp, hq, D ** -0.5, out=outq, out_dtype=lc.LC_BF16)
+    ev1.record()
+    ev1.synchronize()
+    pf_ms = ev0.elapsed_time(ev1) / reps
+    pk_ms, pk_n, _, _, po_ms = cache.timing(0)
+    view = n_new + chunk
+    pf_bytes = view * hkv * (8 * lc.packed_words(D, 4) * 2 + 8)  # the view's packed K/V read once: 136 B per (token, kv head)
+    visible = chunk * (view - chunk) + chunk * (chunk + 1) // 2  # (query token, key) pairs under the causal mask
+    pf_flops = 4.0 * D * hq * visible  # QK and PV multiply-adds
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    bf16_peak = peaks.get("bf16_tflops", 1590.0)
+    prefill_attn = {
+        "chunk_tokens": chunk, "view_tokens": view, "ms_per_chunk": pf_ms,
+        "kernel_ms": pk_ms / max(1, pk_n), "rotate_merge_ms": po_ms / max(1, pk_n),
+        "query_tokens_per_s": chunk / (pf_ms / 1e3),
+        "kv_gbs": pf_bytes / (pf_ms / 1e3) / 1e9, "kv_bytes_per_chunk": pf_bytes,
+        "useful_tflops": pf_flops / (pk_ms / max(1, pk_n) / 1e3) / 1e12,
+        "tensor_frac_of_bf16_peak": pf_flops / (pk_ms / max(1, pk_n) / 1e3) / 1e12 / bf16_peak,
+        "note": "k_prefill_tiled: each 64-key tile dequantized once per (kv head, 32 query tokens x 4 heads); "
+                "QK and PV as f16 hi/lo m16n8k16 MMAs (2x the useful FLOPs issued)",
+    }
     # prefix reuse: one 4096-token prefix shared by 64 requests through the block table
     src = B
     cache.append(0, [src], ks[0][:1, :, :prefix // 2].contiguous(), vs[0][:1, :, :prefix // 2].contiguous())
@@ -1066,6 +1101,7 @@ def run_prefill(args):
                    "ms_per_chunk": ms / (n_new // chunk)},
         "prefix": {"fork_us_per_request": fork_us, "pages_shared_per_request": prefix // 256,
                    "max_abs_fork_vs_source_decode": fork_vs_src},
+        "prefill_attn": prefill_attn,
         "clocks": clk.summary(),
     }), flush=True)
     cache.close()

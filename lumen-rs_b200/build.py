@@ -33,7 +33,7 @@ def _sources():
 
 
 def _headers_mtime():
-    hs = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+    hs = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
     return max((os.path.getmtime(h) for h in hs), default=0.0)
 
 

@@ -1368,6 +1368,71 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   return r;
 }
 
+// lc_prefill_attn on the tensor cores (prefill.cu) where the geometry has
+// the tiled kernel (4-bit K and V, head_dim 128, GQA <= 8) and no QJL or
+// page-sparse scores are asked for: the chunk's queries are rotated, the
+// kernel writes one (m, l, o) part per row, and the merge normalises and
+// un-rotates into `dout`. Returns false (nothing issued) for other calls,
+// which take the split-K decode with one virtual sequence per query token.
+static bool prefill_tiled(lc_cache* c, int32_t layer, int32_t seq, const void* q, int32_t q_dtype, int32_t L,
+                          int32_t n_q_heads, float scale, uint32_t flags, void* dout, int32_t out_dtype,
+                          cudaStream_t s, bool& host_q) {
+  const int32_t hkv = c->cfg.n_kv_heads, D = c->cfg.head_dim;
+  if (flags & (LC_QJL_SCORES | LC_SPARSE_PAGES)) return false;
+  if (n_q_heads % hkv != 0 || !prefill_tiled_path(D, (int)c->kc.bits, (int)c->vc.bits, n_q_heads / hkv)) return false;
+  c->check(seq, layer);
+  SeqLayer& sl = c->at(seq, layer);
+  int64_t n = sl.ring.view_len;
+  if (!sl.head_len.empty()) {
+    for (int64_t hl : sl.head_len)
+      LC_REQUIRE(hl == sl.head_len[0], LC_ERR_STATE, "heads of this layer hold different lengths");
+    n = sl.head_len[0];
+  }
+  LC_REQUIRE(sl.head_len.empty() ? sl.ring.offset <= sl.ring.max_size : true, LC_ERR_STATE,
+             "prefill attention over a ring that has wrapped is not supported");
+  LC_REQUIRE(n >= L, LC_ERR_INVALID, "prefill: more query tokens than the sequence holds");
+  c->order(s);
+  c->ops.stream = s;
+  c->sync_table(seq, layer, s);
+  const int64_t rows = (int64_t)L * n_q_heads;
+  const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, host_q);
+  c->q_rot.ensure((size_t)rows * D, s);
+  c->q_h.ensure((size_t)rows * D, s);
+  const float qscale = scale * 1.4426950408889634f / c->dk.alpha;
+  c->timed(c->t_other, s, [&] {
+    launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0, qscale, c->q_rot.p,
+                    c->q_h.p, s);
+  });
+  if (host_q) LC_CUDA(cudaEventRecord(c->ev_copy, s));
+  c->part.ensure((size_t)rows * (D + 2), s);
+  PrefillArgs a;
+  a.table_row = c->table_row(seq, layer);
+  a.n_total = n;
+  a.L = L;
+  a.hkv = hkv;
+  a.hq = n_q_heads;
+  a.off_kw = c->layout.off[R_KW];
+  a.off_vw = c->layout.off[R_VW];
+  a.off_ks = c->layout.off[R_KS];
+  a.off_vs = c->layout.off[R_VS];
+  a.q_rot = c->q_rot.p;
+  a.kcent = c->dk.cent_d;
+  a.vcent = c->dv.cent_d;
+  a.kalpha = c->dk.alpha;
+  a.valpha = c->dv.alpha;
+  a.pthr = decode_klo_thr(c->dk.lo_max);
+  a.m_out = c->part.p;
+  a.l_out = c->part.p + rows;
+  a.o_out = c->part.p + 2 * rows;
+  c->timed(c->t_decode, s, [&] { launch_prefill_tiled(a, s); });
+  c->timed(c->t_other, s, [&] {
+    launch_merge_rows(a.m_out, a.l_out, a.o_out, (int32_t)rows, D, c->v_R(flags), dout, out_dtype,
+                      1.0f / c->dv.alpha, s);
+  });
+  c->launches += 3;
+  return true;
+}
+
 // lc_decode_attn and lc_prefill_attn: decode, merge if the one-launch path
 // was not taken, copy a host output back.
 static void attn_call(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const PrefillView* prefill,
@@ -1385,6 +1450,17 @@ static void attn_call(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t*
   if (host_out) {
     c->outbuf.ensure(obytes, s);
     dout = c->outbuf.p;
+  }
+  bool tiled_host_q = false;
+  if (prefill && prefill_tiled(c, layer, prefill->seq, q, q_dtype, n_seqs, n_q_heads, scale, flags, dout, out_dtype, s,
+                               tiled_host_q)) {
+    if (host_out) {
+      LC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s));
+      LC_CUDA(cudaStreamSynchronize(s));
+    } else if (tiled_host_q) {
+      LC_CUDA(cudaEventSynchronize(c->ev_copy));
+    }
+    return;
   }
   const DecodeRun run =
       decode_common(c, layer, n_seqs, seq_ids, q, q_dtype, n_q_heads, scale, flags, s, dout, out_dtype, prefill);

@@ -60,11 +60,70 @@ def test_prefill_matches_oracle(lc, orc, gpu, dim, kb, vb, hkv, hq, prefix, chun
 
 
 def test_prefill_one_token_is_decode(lc, orc, gpu):
-    cache, _ = _setup(lc, orc, 128, 4, 4, 8, 700, 1, 5)
+    """A one-token chunk is a decode step of that token (the tiled prefill
+    kernel and the decode kernel agree within the decode tolerance)."""
+    cache, ref = _setup(lc, orc, 128, 4, 4, 8, 700, 1, 5)
     q = helpers.queries(orc, 8, 1, 32, 128)
     a = cache.prefill_attn(0, 0, q, 32, 0.1)
     b = cache.decode_attn(0, [0], q, 32, 0.1)
-    np.testing.assert_array_equal(a, b)
+    ok, msg = helpers.attn_close(a, b)
+    assert ok, msg
+    ok, msg = helpers.attn_close(a, _oracle(ref, q, 8, 0.1, 701))
+    assert ok, msg
+    cache.close()
+
+
+@pytest.mark.parametrize("hkv,hq,prefix,chunk", [
+    (4, 4, 700, 130),    # G 1: 128 tokens per block, two blocks
+    (8, 24, 3000, 64),   # G 3: 42 tokens per block, 2 rows per block unused
+    (2, 12, 1000, 77),   # G 6: 21 tokens per block
+    (2, 16, 256, 200),   # G 8: 16 tokens per block, a page-aligned prefix
+    (8, 32, 63, 65),     # G 4: the chunk straddles key tiles
+])
+def test_prefill_tiled_group_sizes(lc, orc, gpu, hkv, hq, prefix, chunk):
+    """The tensor-core prefill kernel (4-bit, d 128) over GQA 1-8, ragged
+    chunks and prefixes that do not align with the 64-key tiles."""
+    cache, ref = _setup(lc, orc, 128, 4, 4, hkv, prefix, chunk, 300 + hq + chunk)
+    q = helpers.queries(orc, 11 + hq, chunk, hq, 128)
+    scale = 1.0 / np.sqrt(128)
+    got = cache.prefill_attn(0, 0, q, hq, scale)
+    ok, msg = helpers.attn_close(got, _oracle(ref, q, hkv, scale, prefix + chunk))
+    assert ok, msg
+    cache.close()
+
+
+def _unit_rms(q):
+    return (q / np.sqrt(np.mean(q.astype(np.float64) ** 2, axis=-1, keepdims=True))).astype(np.float32)
+
+
+def test_prefill_tiled_peaked_scale1(lc, orc, gpu):
+    """The reference's production regime (scale 1.0 on unit-RMS queries,
+    gemma4_moe.rs:4642-4660): peaked softmax, where the kernel's precise
+    tiles (K table residuals) must keep the decode tolerance. Device bf16
+    queries, f32 output on the device."""
+    import torch
+
+    cache, ref = _setup(lc, orc, 128, 4, 4, 8, 2000, 96, 41)
+    q = _unit_rms(helpers.queries(orc, 12, 96, 32, 128))
+    qt, qv = helpers.to_bf16(q)
+    out = torch.empty((96, 32, 128), dtype=torch.float32, device="cuda")
+    cache.prefill_attn(0, 0, qt.cuda(), 32, 1.0, out=out, out_dtype=lc.LC_F32)
+    torch.cuda.synchronize()
+    ok, msg = helpers.attn_close(out.cpu().numpy(), _oracle(ref, qv, 8, 1.0, 2096))
+    assert ok, msg
+    cache.close()
+
+
+def test_prefill_tiled_out_rotated(lc, orc, gpu):
+    """LC_OUT_ROTATED leaves the tiled prefill's output in V's rotated basis:
+    un-rotating it on the host gives the normal output."""
+    cache, ref = _setup(lc, orc, 128, 4, 4, 8, 500, 40, 77)
+    q = helpers.queries(orc, 13, 40, 32, 128)
+    a = cache.prefill_attn(0, 0, q, 32, 0.1)
+    b = cache.prefill_attn(0, 0, q, 32, 0.1, flags=lc.LC_OUT_ROTATED)
+    tv = orc.Tables.generate(128, 4, 64, 42)
+    R = np.asarray(tv.R, np.float64).reshape(128, 128)
+    np.testing.assert_allclose(b.astype(np.float64) @ R, a, atol=2e-4)
     cache.close()
 
 
