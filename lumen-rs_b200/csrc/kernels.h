@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <mutex>
 #include <vector>
@@ -89,8 +90,7 @@ struct PrefillArgs {
   const float* vcent = nullptr;  // [16]
   float kalpha = 1.0f, valpha = 1.0f;
   // precise tiles: when max sigma_K of a tile x max ||q'|| of the block
-  // exceeds pthr, the scores add the query's f16 residual and the K table's
-  // residual products (see prefill_pthr)
+  // exceeds pthr, the scores add the K table's residual products (decode_klo_thr, as the decode kernels)
   float pthr = 3.0e38f;
   float* m_out = nullptr;  // [L * hq]
   float* l_out = nullptr;  // [L * hq]
