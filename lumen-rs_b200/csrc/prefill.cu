@@ -233,17 +233,24 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid
     float s[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    // per k-step: the four B loads, then the eight hi and the eight lo MMAs,
+    // so that MMAs on one accumulator stand eight apart
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t b[4][4];
+#pragma unroll
+      for (int np = 0; np < 4; ++np) ldsm_x4(k_s + pf_swz(16 * np + (mi >> 1) * 8 + mr, 2 * kk + (mi & 1)), b[np]);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
-        uint32_t b[4];
-        ldsm_x4(k_s + pf_swz(16 * np + (mi >> 1) * 8 + mr, 2 * kk + (mi & 1)), b);
-        mma16816(s[2 * np], qh[kk][0], qh[kk][1], qh[kk][2], qh[kk][3], b[0], b[1]);
-        mma16816(s[2 * np + 1], qh[kk][0], qh[kk][1], qh[kk][2], qh[kk][3], b[2], b[3]);
-        mma16816(s[2 * np], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3], b[0], b[1]);
-        mma16816(s[2 * np + 1], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3], b[2], b[3]);
+        mma16816(s[2 * np], qh[kk][0], qh[kk][1], qh[kk][2], qh[kk][3], b[np][0], b[np][1]);
+        mma16816(s[2 * np + 1], qh[kk][0], qh[kk][1], qh[kk][2], qh[kk][3], b[np][2], b[np][3]);
       }
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        mma16816(s[2 * np], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3], b[np][0], b[np][1]);
+        mma16816(s[2 * np + 1], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3], b[np][2], b[np][3]);
+      }
+    }
     if (lo) {  // + Q (K table residuals) x 2^-11, two n-tiles at a time
 #pragma unroll 1
       for (int np = 0; np < 4; ++np) {
