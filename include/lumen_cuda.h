@@ -313,8 +313,11 @@ int lc_decode_attn(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t
  * query i attends to the first view_len - n_q_tokens + i + 1 tokens. out has
  * q's shape. Flags as lc_decode_attn. LC_ERR_STATE on a sliding layer whose
  * ring has wrapped (its view is not in token order); LC_ERR_INVALID if
- * n_q_tokens exceeds the view. Each query reads its whole prefix, so the
- * cost grows as n_q_tokens x prefix. */
+ * n_q_tokens exceeds the view. 4-bit K/V at head_dim 128 with GQA <= 8
+ * (and no QJL / sparse flag) runs a tensor-core kernel that dequantizes each
+ * key tile once for 128 (token, head) query rows; other geometries run the
+ * split-K decode with one virtual sequence per query token, whose cost grows
+ * as n_q_tokens x prefix. */
 int lc_prefill_attn(lc_cache* cache, int32_t layer, int32_t seq, const void* q, int32_t q_dtype,
                     int32_t n_q_tokens, int32_t n_q_heads, float scale, uint32_t flags, void* out,
                     int32_t out_dtype, void* stream);

@@ -8,22 +8,33 @@
 // accumulated in the rotated basis and un-rotated once per query head.
 //
 // Kernels
-//  k_rotate_q       q' = (R q) * scale * log2(e), f32 + f16 copies.
-//  k_decode_flat    4-bit K/V, d = 128 (the hot path). Persistent: one CTA of
-//                   16 warps per SM. The (sequence, kv head, 16-token tile)
-//                   space is cut into equal contiguous ranges, one per warp,
-//                   so ragged batches stay balanced; a warp writes one softmax
-//                   partial per (sequence, kv head) segment it touches. Each
-//                   warp streams its tiles through a 3-stage cp.async ring in
-//                   shared memory (coalesced 16-byte copies of the packed K/V
-//                   words and sigmas straight from the pages). Codes are
-//                   dequantized into mma.sync fragments through a 256-entry
-//                   byte -> half2 centroid-pair table kept once per lane
-//                   (bank-conflict-free lookups); S^T = K_dq Q^T and
-//                   O^T = V_dq^T P^T run as m16n8k16 f16 MMAs with f32
-//                   accumulation, the GQA query heads of a kv head forming the
-//                   MMA's N dimension.
-//  k_decode_generic any bit width / head_dim: CUDA-core fallback, chunked.
+//  k_rotate_q       q' = (R q) * scale * log2(e) / alpha_K, f32 + f16 copies.
+//  k_decode_pair    4-bit K/V, d = 128, GQA <= 4: the hot path. Persistent:
+//                   one CTA of 16 warps per SM. The (sequence, kv head,
+//                   32-token tile) space is cut into equal contiguous ranges,
+//                   one per warp, so ragged batches stay balanced; a warp
+//                   writes one softmax partial per (sequence, kv head)
+//                   segment it touches. Each warp streams its tiles through a
+//                   2-stage cp.async ring (16-byte copies of the packed words
+//                   and sigmas straight from the pages). Codes become
+//                   mma.sync fragments through a byte -> half2 centroid-pair
+//                   table kept once per lane (one byte permute forms the
+//                   address); S^T = K_dq Q^T and O^T = V_dq^T P^T run as
+//                   m16n8k16 f16 MMAs with f32 accumulation, the MMA's N
+//                   columns being (query head, f16 hi / lo part) so the query
+//                   and P are f32-accurate. Precise tiles add the K table's
+//                   f16 residuals (kLoEta). The fused variant rotates the
+//                   queries on the tensor cores, merges a segment's partials
+//                   in its last-arriving warp and un-rotates the output in
+//                   the same launch.
+//  k_decode_flat    4-bit K/V, d = 128, GQA 5..8: the same partition and
+//                   tiles, with the query heads filling the N columns and the
+//                   query hi / lo parts as two MMAs.
+//  k_decode_mma32   3-bit K / 2-bit V, d = 256, GQA <= 4 (config 2): chunked
+//                   items, one-lane bulk copies into per-warp stages, 6-bit
+//                   K pair tables and a byte-indexed V table on m16n8k16.
+//  k_decode_generic any other bit width / head_dim, and QJL scores:
+//                   CUDA-core, chunked.
 //  k_merge          combines the partials, normalises, un-rotates (R^T).
 // Roofline: HBM. Algorithmic bytes per (token, kv head) = 8*words_K +
 // 8*words_V + 8 (136 B for 4-bit d=128), read once.
