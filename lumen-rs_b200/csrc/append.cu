@@ -624,6 +624,186 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
   else LC_CUDA(cudaLaunchKernelEx(&cfg, k_append_warp<R, false>, d));
 }
 
+// Large appends without QJL stage 2 at head_dim 64 / 128: a warp takes
+// kTileVecs vectors at a time and lane l owns the R consecutive outputs
+// R l .. R l + R - 1 of all of them (R = dim / 32). Per step j of the
+// rotation's ascending sum a lane reads its R coefficients R^T[j][R l ..] as
+// one vector load and each vector's x[j] as a broadcast, so a lane keeps
+// kTileVecs x R independent chains and the loads are ~5 % of the FP32 work
+// (the batched kernel above reads one coefficient per output and chain).
+// Every f32 operation and sum order is the strict one: the rotation sums j
+// ascending from -0, the squares are formed in parallel and added in order
+// i ascending by one lane per vector, the codes are the threshold count, so
+// codes and sigma are bit-identical to k_append_strict.
+constexpr int kTileWarps = 16, kTileVecs = 8;
+
+template <int R>
+__host__ __device__ constexpr size_t tile_warp_bytes() {
+  constexpr int D = 32 * R;
+  return (size_t)kTileVecs * D * 4 + (size_t)kTileVecs * (D + 1) * 4 + (size_t)kTileVecs * D;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid_constant__ AppendDev a) {
+  constexpr int D = 32 * R;
+  constexpr int NV = kTileVecs;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int side = blockIdx.y;
+  const CodecDev& c = a.codec[side];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* rt = reinterpret_cast<float*>(smem);  // R^T [D][D]
+  float* sthr = rt + D * D;                    // [256]
+  uint8_t* wb = smem + (size_t)D * D * 4 + 1024 + (size_t)warp * tile_warp_bytes<R>();
+  float* x = reinterpret_cast<float*>(wb);  // [NV][D]
+  float* sq = x + NV * D;                   // [NV][D + 1] squares (rows padded: lane v reads row v)
+  uint8_t* codes = reinterpret_cast<uint8_t*>(sq + NV * (D + 1));  // [NV][D]
+  stage16(rt, c.RT, D * D / 4);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  for (int k = threadIdx.x; k < c.n_levels - 1; k += blockDim.x) sthr[k] = c.thr[k];
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  __syncthreads();
+
+  const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
+  const void* src = a.src[side];
+  const int cpw = 64 / c.bits, W = c.words;
+  const int rw = a.role_words[side], rsg = a.role_sigma[side];
+  for (int64_t v0 = ((int64_t)blockIdx.x * kTileWarps + warp) * NV; v0 < n_vec;
+       v0 += (int64_t)gridDim.x * kTileWarps * NV) {
+    const int nv = (int)(n_vec - v0 < NV ? n_vec - v0 : NV);
+    // ---- load (input layout [n_seqs][h_in][n_tok][D]) ----
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      float e[R];
+      int64_t idx[R];
+      bool ok[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        idx[r] = (v0 + v) * D + R * lane + r;
+        ok[r] = v < nv;
+      }
+      load_n_elem(src, a.dtype, idx, ok, e);
+#pragma unroll
+      for (int r = 0; r < R; ++r) x[v * D + R * lane + r] = e[r];
+    }
+    __syncwarp();
+    if (side == 0 && a.rope_cs) {
+      for (int v = 0; v < nv; ++v) {
+        const int64_t vi = v0 + v;
+        const int64_t slot = (vi / ((int64_t)a.h_in * a.n_tok)) * a.n_tok + vi % a.n_tok;
+        for (int i = lane; i < a.rope_half; i += 32) rope_pair(x + v * D, a, slot, i);
+      }
+      __syncwarp();
+    }
+    // ---- rotated[i] = sum_j R[i][j] x[j], j ascending (rotation.rs:91-99) ----
+    float acc[NV][R];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[v][r] = -0.0f;
+#pragma unroll 1
+    for (int j = 0; j < D; j += 4) {
+      float w[4][R];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        if constexpr (R == 4) {
+          const float4 q = *reinterpret_cast<const float4*>(rt + (j + jj) * D + 4 * lane);
+          w[jj][0] = q.x;
+          w[jj][1] = q.y;
+          w[jj][2] = q.z;
+          w[jj][3] = q.w;
+        } else {
+          const float2 q = *reinterpret_cast<const float2*>(rt + (j + jj) * D + 2 * lane);
+          w[jj][0] = q.x;
+          w[jj][1] = q.y;
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const float4 xq = *reinterpret_cast<const float4*>(x + v * D + j);
+        const float xs[4] = {xq.x, xq.y, xq.z, xq.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+          for (int r = 0; r < R; ++r) acc[v][r] = __fadd_rn(acc[v][r], __fmul_rn(w[jj][r], xs[jj]));
+      }
+    }
+    // ---- scale = sqrt(norm_sq / d): squares in parallel, lane v adds vector
+    // v's in order (compressor.rs:70-71) ----
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int r = 0; r < R; ++r) sq[v * (D + 1) + R * lane + r] = __fmul_rn(acc[v][r], acc[v][r]);
+    __syncwarp();
+    float sc = 0.f, inv = 0.f;
+    if (lane < nv) {
+      const float* row = sq + lane * (D + 1);
+      float s2 = -0.0f;
+#pragma unroll 8
+      for (int k = 0; k < D; ++k) s2 = __fadd_rn(s2, row[k]);
+      sc = __fsqrt_rn(__fdiv_rn(s2, (float)D));
+      inv = __fdiv_rn(1.0f, sc);
+    }
+    // ---- codes: the count of thresholds t with !(yn < t) (lloyd_max.rs:132-143),
+    // by binary search over the ascending thresholds ----
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const float scv = __shfl_sync(0xffffffffu, sc, v), invv = __shfl_sync(0xffffffffu, inv, v);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        int code = 0;
+        if (!(scv < 1e-10f)) {
+          const float yn = __fmul_rn(acc[v][r], invv);
+          for (int step = c.n_levels >> 1; step > 0; step >>= 1)
+            if (!(yn < sthr[code + step - 1])) code += step;
+        }
+        codes[v * D + R * lane + r] = (uint8_t)code;
+      }
+    }
+    __syncwarp();
+    // ---- pack and write (bitpack.rs:17-30) ----
+    for (int u = lane; u < nv * W; u += 32) {
+      const int v = u / W, w = u % W;
+      uint64_t word = 0;
+      for (int k = 0; k < cpw; ++k) {
+        const int idx = w * cpw + k;
+        if (idx < D) word |= (uint64_t)codes[v * D + idx] << (k * c.bits);
+      }
+      const int64_t g = v0 + v;
+      const int64_t t = g % a.n_tok, sh = g / a.n_tok;
+      const int hl = (int)(sh % a.h_in);
+      const int64_t slot = (sh / a.h_in) * a.n_tok + t;
+      uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
+      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
+      reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
+    }
+    if (lane < nv) {
+      const int64_t g = v0 + lane;
+      const int64_t t = g % a.n_tok, sh = g / a.n_tok;
+      const int hl = (int)(sh % a.h_in);
+      const int64_t slot = (sh / a.h_in) * a.n_tok + t;
+      uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
+      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
+      *reinterpret_cast<float*>(page + a.off[rsg] + hr * a.row[rsg]) = sc;
+    }
+    __syncwarp();  // x, sq and codes are refilled by the next batch
+  }
+}
+
+template <int R>
+void launch_tile_append(const AppendDev& d, int64_t n_vec, cudaStream_t s) {
+  constexpr int D = 32 * R;
+  const size_t smem = (size_t)D * D * 4 + 1024 + (size_t)kTileWarps * tile_warp_bytes<R>();
+  static bool attr = false;
+  if (!attr) {
+    LC_CUDA(cudaFuncSetAttribute(k_append_tile<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  const int64_t batches = (n_vec + (int64_t)kTileWarps * kTileVecs - 1) / ((int64_t)kTileWarps * kTileVecs);
+  const int64_t grid = std::min<int64_t>(batches, num_sms());
+  k_append_tile<R><<<dim3((unsigned)grid, 2), kTileWarps * 32, smem, s>>>(d);
+  LC_CUDA(cudaGetLastError());
+}
+
 }  // namespace
 
 bool append_rotates_queries(int64_t n_vec, int dim, int m_max, bool stage2) {
@@ -690,6 +870,12 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
     if (D == 64) launch_warp_append<2>(d, stage2, M, n_vec, s);
     else if (D == 128) launch_warp_append<4>(d, stage2, M, n_vec, s);
     else launch_warp_append<8>(d, stage2, M, n_vec, s);
+    return;
+  }
+  if (!stage2 && !a.q && (D == 64 || D == 128) && a.codec[0].bits <= 8 && a.codec[1].bits <= 8 &&
+      a.codec[0].dim == a.codec[1].dim) {
+    if (D == 64) launch_tile_append<2>(d, n_vec, s);
+    else launch_tile_append<4>(d, n_vec, s);
     return;
   }
   const int groups = D <= 256 ? 2 : 1;

@@ -141,6 +141,46 @@ def test_append_batched_bit_exact(lc, orc, gpu, dtype):
     assert cache.ring_state(1, 1)["view_len"] == 0
 
 
+@pytest.mark.parametrize("dim,kb,vb,qjl,dtype", [
+    (128, 4, 4, False, "bf16"),  # config 3's chunk append: the register-blocked tile kernel
+    (128, 4, 4, False, "f32"),
+    (64, 2, 3, False, "bf16"),   # d 64, 2-bit K / 3-bit V (3-bit words hold 21 codes)
+    (128, 4, 4, True, "bf16"),   # QJL stage 2: the batched strict kernel
+])
+def test_append_large_bit_exact(lc, orc, gpu, dim, kb, vb, qjl, dtype):
+    """One append of more than 16384 vectors per side (3 x 8 x 801 = 19224,
+    not a multiple of any batch): codes, sigmas (and QJL bits, residual
+    norms) bit-identical to the oracle's compress of the same values."""
+    import torch
+
+    H, S, n = 8, 3, 801
+    tk, tv, ck, cv = _codecs(lc, orc, dim, kb, vb, 64)
+    pages = (n + 255) // 256 + 2
+    cache = lc.CudaKvCache(1, H, dim, ck, cv, max_seqs=S, max_pages=S * pages + 8, max_pages_per_seq=pages,
+                           store_flags=(lc.LC_STORE_K_QJL | lc.LC_STORE_V_QJL) if qjl else 0)
+    K = helpers.kv(orc, 21, S, H, n, dim)
+    V = helpers.kv(orc, 22, S, H, n, dim)
+    if dtype == "bf16":
+        Kt, K = helpers.to_bf16(K)
+        Vt, V = helpers.to_bf16(V)
+        Kt, Vt = Kt.cuda(), Vt.cuda()
+    else:
+        Kt, Vt = torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda()
+    cache.append(0, [0, 1, 2], Kt, Vt)
+    ok, ov = orc.Compressor(tk), orc.Compressor(tv)
+    for b in range(S):
+        got = cache.fetch(b, 0)
+        for h in range(H):
+            for p, x, comp in (("k", K[b, h], ok), ("v", V[b, h], ov)):
+                s1, s2, rn, sc = comp.compress(x)
+                np.testing.assert_array_equal(got[f"{p}_words"][h], s1, err_msg=f"{b} {h} {p}")
+                np.testing.assert_array_equal(got[f"{p}_sigma"][h].view(np.uint32), sc.view(np.uint32))
+                if qjl:
+                    np.testing.assert_array_equal(got[f"{p}_qjl"][h], s2)
+                    np.testing.assert_array_equal(got[f"{p}_rnorm"][h].view(np.uint32), rn.view(np.uint32))
+    cache.close()
+
+
 def test_append_errors(lc, orc, gpu):
     tk, tv, ck, cv = _codecs(lc, orc, 128, 4, 4, 64)
     cache = lc.CudaKvCache(1, 2, 128, ck, max_seqs=2, max_pages=4, max_pages_per_seq=2)

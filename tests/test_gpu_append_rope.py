@@ -3,8 +3,9 @@ oracle applying the same RoPE (orc_rope) and then compress_one.
 
 Positions continue each sequence's layer: the sequences start at different
 lengths, and the chunk sizes reach both append kernels (the warp kernel for
-decode steps, the batched kernel past 16384 vectors). Both pair layouts and
-partial rotary dims are covered. Values are not rotated.
+decode steps; past 16384 vectors the batched kernel with QJL stage 2, the
+register-blocked tile kernel without). Both pair layouts and partial rotary
+dims are covered. Values are not rotated.
 """
 import numpy as np
 import pytest
@@ -14,12 +15,13 @@ import helpers
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("dim,kb,vb,m,rot,trad,chunks", [
-    (128, 4, 4, 64, 128, False, [5, 1, 1]),        # warp kernel, half-split pairs
-    (128, 3, 2, 64, 64, True, [3, 1]),             # partial rotary, traditional pairs
-    (128, 4, 4, 64, 128, False, [2300]),           # 2 x 8 x 2300 vectors: the batched kernel
+@pytest.mark.parametrize("dim,kb,vb,m,rot,trad,chunks,qjl", [
+    (128, 4, 4, 64, 128, False, [5, 1, 1], True),        # warp kernel, half-split pairs
+    (128, 3, 2, 64, 64, True, [3, 1], True),             # partial rotary, traditional pairs
+    (128, 4, 4, 64, 128, False, [2300], True),           # 2 x 8 x 2300 vectors: the batched kernel
+    (128, 4, 4, 64, 96, True, [1100, 1201], False),      # no QJL: the register-blocked tile kernel
 ])
-def test_append_rope_bit_exact(lc, orc, gpu, dim, kb, vb, m, rot, trad, chunks):
+def test_append_rope_bit_exact(lc, orc, gpu, dim, kb, vb, m, rot, trad, chunks, qjl):
     tk = orc.Tables.generate(dim, kb, m, 42)
     tv = orc.Tables.generate(dim, vb, m, 42)
     ck = lc.TurboQuantCompressor.from_tables(tk.R, tk.bounds, tk.cents, tk.proj)
@@ -29,7 +31,7 @@ def test_append_rope_bit_exact(lc, orc, gpu, dim, kb, vb, m, rot, trad, chunks):
     total = [start[b] + sum(chunks) for b in range(B)]
     pages = (max(total) + 255) // 256 + 3  # the append bounds prealloc growth up front
     cache = lc.CudaKvCache(1, H, dim, ck, cv, max_seqs=B, max_pages=B * pages + 8, max_pages_per_seq=pages,
-                           store_flags=lc.LC_STORE_K_QJL | lc.LC_STORE_V_QJL)
+                           store_flags=(lc.LC_STORE_K_QJL | lc.LC_STORE_V_QJL) if qjl else 0)
     K = [helpers.kv(orc, 500 + b, 1, H, total[b], dim)[0] for b in range(B)]
     V = [helpers.kv(orc, 600 + b, 1, H, total[b], dim)[0] for b in range(B)]
     for b in range(B):  # plain appends first: the prefix without RoPE
@@ -52,8 +54,9 @@ def test_append_rope_bit_exact(lc, orc, gpu, dim, kb, vb, m, rot, trad, chunks):
                 p = "kv"[side]
                 np.testing.assert_array_equal(f[f"{p}_words"][h], s1, err_msg=f"{b} {h} {p}")
                 np.testing.assert_array_equal(f[f"{p}_sigma"][h].view(np.uint32), sc.view(np.uint32))
-                np.testing.assert_array_equal(f[f"{p}_qjl"][h], s2)
-                np.testing.assert_array_equal(f[f"{p}_rnorm"][h].view(np.uint32), rn.view(np.uint32))
+                if qjl:
+                    np.testing.assert_array_equal(f[f"{p}_qjl"][h], s2)
+                    np.testing.assert_array_equal(f[f"{p}_rnorm"][h].view(np.uint32), rn.view(np.uint32))
     cache.close()
 
 
