@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdint>
 
 #include "kernels.h"
 
@@ -633,14 +634,15 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
 // (the batched kernel above reads one coefficient per output and chain).
 // Every f32 operation and sum order is the strict one: the rotation sums j
 // ascending from -0, the squares are formed in parallel and added in order
-// i ascending by one lane per vector, the codes are the threshold count, so
+// i ascending by one lane per vector (rows padded to d + 4 floats, so the
+// lanes' 16-byte reads fall in distinct banks), the codes are the threshold count, so
 // codes and sigma are bit-identical to k_append_strict.
-constexpr int kTileWarps = 16, kTileVecs = 8;
+constexpr int kTileWarps = 32, kTileVecs = 4;
 
 template <int R>
 __host__ __device__ constexpr size_t tile_warp_bytes() {
   constexpr int D = 32 * R;
-  return (size_t)kTileVecs * D * 4 + (size_t)kTileVecs * (D + 1) * 4 + (size_t)kTileVecs * D;
+  return (size_t)kTileVecs * D * 4 + (size_t)kTileVecs * (D + 4) * 4 + (size_t)kTileVecs * D;
 }
 
 template <int R>
@@ -655,8 +657,8 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
   float* sthr = rt + D * D;                    // [256]
   uint8_t* wb = smem + (size_t)D * D * 4 + 1024 + (size_t)warp * tile_warp_bytes<R>();
   float* x = reinterpret_cast<float*>(wb);  // [NV][D]
-  float* sq = x + NV * D;                   // [NV][D + 1] squares (rows padded: lane v reads row v)
-  uint8_t* codes = reinterpret_cast<uint8_t*>(sq + NV * (D + 1));  // [NV][D]
+  float* sq = x + NV * D;                   // [NV][D + 4] squares (rows padded: lane v reads row v)
+  uint8_t* codes = reinterpret_cast<uint8_t*>(sq + NV * (D + 4));  // [NV][D]
   stage16(rt, c.RT, D * D / 4);
   asm volatile("cp.async.commit_group;\n" ::: "memory");
   for (int k = threadIdx.x; k < c.n_levels - 1; k += blockDim.x) sthr[k] = c.thr[k];
@@ -670,18 +672,46 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
   for (int64_t v0 = ((int64_t)blockIdx.x * kTileWarps + warp) * NV; v0 < n_vec;
        v0 += (int64_t)gridDim.x * kTileWarps * NV) {
     const int nv = (int)(n_vec - v0 < NV ? n_vec - v0 : NV);
-    // ---- load (input layout [n_seqs][h_in][n_tok][D]) ----
+    // ---- load (input layout [n_seqs][h_in][n_tok][D]): lane l's R
+    // consecutive elements of each vector as one vector load ----
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       float e[R];
-      int64_t idx[R];
-      bool ok[R];
+      const int64_t base = (v0 + v) * D + R * lane;
+      if (v >= nv) {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        idx[r] = (v0 + v) * D + R * lane + r;
-        ok[r] = v < nv;
+        for (int r = 0; r < R; ++r) e[r] = 0.0f;
+      } else if (a.dtype == LC_F32) {
+        const float* q = static_cast<const float*>(src) + base;
+        if constexpr (R == 4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(q);
+          e[0] = t4.x;
+          e[1] = t4.y;
+          e[2] = t4.z;
+          e[3] = t4.w;
+        } else {
+          const float2 t2 = *reinterpret_cast<const float2*>(q);
+          e[0] = t2.x;
+          e[1] = t2.y;
+        }
+      } else {
+        const unsigned short* q = static_cast<const unsigned short*>(src) + base;
+        uint32_t h[R / 2];
+        if constexpr (R == 4) {
+          const uint2 t2 = *reinterpret_cast<const uint2*>(q);
+          h[0] = t2.x;
+          h[1] = t2.y;
+        } else {
+          h[0] = *reinterpret_cast<const uint32_t*>(q);
+        }
+#pragma unroll
+        for (int k = 0; k < R / 2; ++k) {
+          const uint32_t lo = h[k] & 0xFFFFu, hi = h[k] >> 16;
+          e[2 * k] = a.dtype == LC_BF16 ? __uint_as_float(lo << 16) : __half2float(__ushort_as_half((unsigned short)lo));
+          e[2 * k + 1] =
+              a.dtype == LC_BF16 ? __uint_as_float(hi << 16) : __half2float(__ushort_as_half((unsigned short)hi));
+        }
       }
-      load_n_elem(src, a.dtype, idx, ok, e);
 #pragma unroll
       for (int r = 0; r < R; ++r) x[v * D + R * lane + r] = e[r];
     }
@@ -732,14 +762,20 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
 #pragma unroll
     for (int v = 0; v < NV; ++v)
 #pragma unroll
-      for (int r = 0; r < R; ++r) sq[v * (D + 1) + R * lane + r] = __fmul_rn(acc[v][r], acc[v][r]);
+      for (int r = 0; r < R; ++r) sq[v * (D + 4) + R * lane + r] = __fmul_rn(acc[v][r], acc[v][r]);
     __syncwarp();
     float sc = 0.f, inv = 0.f;
     if (lane < nv) {
-      const float* row = sq + lane * (D + 1);
+      const float4* row = reinterpret_cast<const float4*>(sq + lane * (D + 4));
       float s2 = -0.0f;
-#pragma unroll 8
-      for (int k = 0; k < D; ++k) s2 = __fadd_rn(s2, row[k]);
+#pragma unroll 4
+      for (int k = 0; k < D / 4; ++k) {
+        const float4 q4 = row[k];
+        s2 = __fadd_rn(s2, q4.x);
+        s2 = __fadd_rn(s2, q4.y);
+        s2 = __fadd_rn(s2, q4.z);
+        s2 = __fadd_rn(s2, q4.w);
+      }
       sc = __fsqrt_rn(__fdiv_rn(s2, (float)D));
       inv = __fdiv_rn(1.0f, sc);
     }
@@ -760,30 +796,49 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
       }
     }
     __syncwarp();
-    // ---- pack and write (bitpack.rs:17-30) ----
-    for (int u = lane; u < nv * W; u += 32) {
-      const int v = u / W, w = u % W;
-      uint64_t word = 0;
-      for (int k = 0; k < cpw; ++k) {
-        const int idx = w * cpw + k;
-        if (idx < D) word |= (uint64_t)codes[v * D + idx] << (k * c.bits);
-      }
-      const int64_t g = v0 + v;
-      const int64_t t = g % a.n_tok, sh = g / a.n_tok;
-      const int hl = (int)(sh % a.h_in);
-      const int64_t slot = (sh / a.h_in) * a.n_tok + t;
-      uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
-      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
-      reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
+    // ---- pack and write (bitpack.rs:17-30): lane v finds vector v's page
+    // row, the word writers take it by shuffle ----
+    uint64_t pg = 0;
+    int64_t hr = 0;
+    // (sequence, head, token) of v0: lane 0 divides, lane v steps v tokens on
+    int64_t t = 0, sq_i = 0;
+    int hl = 0;
+    if (lane == 0) {
+      const int64_t sh = v0 / a.n_tok;
+      t = v0 - sh * a.n_tok;
+      hl = (int)(sh % a.h_in);
+      sq_i = sh / a.h_in;
     }
+    t = __shfl_sync(0xffffffffu, t, 0);
+    hl = __shfl_sync(0xffffffffu, hl, 0);
+    sq_i = __shfl_sync(0xffffffffu, sq_i, 0);
     if (lane < nv) {
-      const int64_t g = v0 + lane;
-      const int64_t t = g % a.n_tok, sh = g / a.n_tok;
-      const int hl = (int)(sh % a.h_in);
-      const int64_t slot = (sh / a.h_in) * a.n_tok + t;
-      uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
-      const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
-      *reinterpret_cast<float*>(page + a.off[rsg] + hr * a.row[rsg]) = sc;
+      t += lane;
+      while (t >= a.n_tok) {
+        t -= a.n_tok;
+        if (++hl == a.h_in) {
+          hl = 0;
+          ++sq_i;
+        }
+      }
+      const int64_t slot = sq_i * a.n_tok + t;
+      pg = a.page_of(slot);
+      hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
+      *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(pg) + a.off[rsg] + hr * a.row[rsg]) = sc;
+    }
+    for (int u0 = 0; u0 < nv * W; u0 += 32) {
+      const int u = u0 + lane;
+      const int v = u / W, w = u - v * W;
+      const uint64_t pv = __shfl_sync(0xffffffffu, pg, v < NV ? v : 0);
+      const int64_t hv = __shfl_sync(0xffffffffu, hr, v < NV ? v : 0);
+      if (u < nv * W) {
+        uint64_t word = 0;
+        for (int k = 0; k < cpw; ++k) {
+          const int idx = w * cpw + k;
+          if (idx < D) word |= (uint64_t)codes[v * D + idx] << (k * c.bits);
+        }
+        reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(pv) + a.off[rw] + hv * a.row[rw])[w] = word;
+      }
     }
     __syncwarp();  // x, sq and codes are refilled by the next batch
   }
@@ -872,7 +927,11 @@ void launch_append(const AppendArgs& a, cudaStream_t s) {
     else launch_warp_append<8>(d, stage2, M, n_vec, s);
     return;
   }
-  if (!stage2 && !a.q && (D == 64 || D == 128) && a.codec[0].bits <= 8 && a.codec[1].bits <= 8 &&
+  // the tile kernel reads each lane's elements as one vector load: the
+  // inputs must sit on 16-byte (f32) / 8-byte (bf16, f16) boundaries
+  const uintptr_t in_align = a.dtype == LC_F32 ? 16 : 8;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.src[0]) | reinterpret_cast<uintptr_t>(a.src[1])) % in_align) == 0;
+  if (!stage2 && !a.q && aligned && (D == 64 || D == 128) && a.codec[0].bits <= 8 && a.codec[1].bits <= 8 &&
       a.codec[0].dim == a.codec[1].dim) {
     if (D == 64) launch_tile_append<2>(d, n_vec, s);
     else launch_tile_append<4>(d, n_vec, s);

@@ -141,13 +141,14 @@ def test_append_batched_bit_exact(lc, orc, gpu, dtype):
     assert cache.ring_state(1, 1)["view_len"] == 0
 
 
-@pytest.mark.parametrize("dim,kb,vb,qjl,dtype", [
-    (128, 4, 4, False, "bf16"),  # config 3's chunk append: the register-blocked tile kernel
-    (128, 4, 4, False, "f32"),
-    (64, 2, 3, False, "bf16"),   # d 64, 2-bit K / 3-bit V (3-bit words hold 21 codes)
-    (128, 4, 4, True, "bf16"),   # QJL stage 2: the batched strict kernel
+@pytest.mark.parametrize("dim,kb,vb,qjl,dtype,offset", [
+    (128, 4, 4, False, "bf16", 0),  # config 3's chunk append: the register-blocked tile kernel
+    (128, 4, 4, False, "f32", 0),
+    (64, 2, 3, False, "bf16", 0),   # d 64, 2-bit K / 3-bit V (3-bit words hold 21 codes)
+    (128, 4, 4, True, "bf16", 0),   # QJL stage 2: the batched strict kernel
+    (128, 4, 4, False, "bf16", 1),  # inputs off the 8-byte boundary: the strict kernel takes them
 ])
-def test_append_large_bit_exact(lc, orc, gpu, dim, kb, vb, qjl, dtype):
+def test_append_large_bit_exact(lc, orc, gpu, dim, kb, vb, qjl, dtype, offset):
     """One append of more than 16384 vectors per side (3 x 8 x 801 = 19224,
     not a multiple of any batch): codes, sigmas (and QJL bits, residual
     norms) bit-identical to the oracle's compress of the same values."""
@@ -166,6 +167,12 @@ def test_append_large_bit_exact(lc, orc, gpu, dim, kb, vb, qjl, dtype):
         Kt, Vt = Kt.cuda(), Vt.cuda()
     else:
         Kt, Vt = torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda()
+    if offset:  # the same values starting `offset` elements into a larger buffer
+        def shift(t):
+            buf = torch.zeros(t.numel() + offset, dtype=t.dtype, device=t.device)
+            buf[offset:] = t.reshape(-1)
+            return buf[offset:].view(t.shape)
+        Kt, Vt = shift(Kt), shift(Vt)
     cache.append(0, [0, 1, 2], Kt, Vt)
     ok, ov = orc.Compressor(tk), orc.Compressor(tv)
     for b in range(S):
