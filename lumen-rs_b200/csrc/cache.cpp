@@ -1370,15 +1370,16 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
 
 // lc_prefill_attn on the tensor cores (prefill.cu) where the geometry has
 // the tiled kernel (4-bit K and V, head_dim 128, GQA <= 8) and no QJL or
-// page-sparse scores are asked for: the chunk's queries are rotated, the
-// kernel writes one (m, l, o) part per row, and the merge normalises and
-// un-rotates into `dout`. Returns false (nothing issued) for other calls,
+// page-sparse scores are asked for: one launch rotates the chunk's queries,
+// attends and writes the normalised, un-rotated rows into `dout`. Returns false (nothing issued) for other calls,
 // which take the split-K decode with one virtual sequence per query token.
 static bool prefill_tiled(lc_cache* c, int32_t layer, int32_t seq, const void* q, int32_t q_dtype, int32_t L,
                           int32_t n_q_heads, float scale, uint32_t flags, void* dout, int32_t out_dtype,
                           cudaStream_t s, bool& host_q) {
   const int32_t hkv = c->cfg.n_kv_heads, D = c->cfg.head_dim;
   if (flags & (LC_QJL_SCORES | LC_SPARSE_PAGES)) return false;
+  // the kernel writes output pairs as 8-byte (f32) / 4-byte (bf16, f16) stores
+  if (reinterpret_cast<uintptr_t>(dout) % (out_dtype == LC_F32 ? 8 : 4) != 0) return false;
   if (n_q_heads % hkv != 0 || !prefill_tiled_path(D, (int)c->kc.bits, (int)c->vc.bits, n_q_heads / hkv)) return false;
   c->check(seq, layer);
   SeqLayer& sl = c->at(seq, layer);
@@ -1395,16 +1396,14 @@ static bool prefill_tiled(lc_cache* c, int32_t layer, int32_t seq, const void* q
   c->ops.stream = s;
   c->sync_table(seq, layer, s);
   const int64_t rows = (int64_t)L * n_q_heads;
-  const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, host_q);
-  c->q_rot.ensure((size_t)rows * D, s);
-  c->q_h.ensure((size_t)rows * D, s);
-  const float qscale = scale * 1.4426950408889634f / c->dk.alpha;
-  c->timed(c->t_other, s, [&] {
-    launch_rotate_q(dq, q_dtype, (int32_t)rows, D, c->dk.RTd, (flags & LC_Q_ROTATED) != 0, qscale, c->q_rot.p,
-                    c->q_h.p, s);
-  });
-  if (host_q) LC_CUDA(cudaEventRecord(c->ev_copy, s));
-  c->part.ensure((size_t)rows * (D + 2), s);
+  const size_t qbytes = (size_t)rows * D * dtype_size(q_dtype);
+  const void* dq = c->stage_in(q, qbytes, c->qbuf, s, host_q);
+  // the kernel reads query pairs as 8-byte (f32) / 4-byte (bf16, f16) loads
+  if (reinterpret_cast<uintptr_t>(dq) % (q_dtype == LC_F32 ? 8 : 4) != 0) {
+    c->qbuf.ensure(qbytes, s);
+    LC_CUDA(cudaMemcpyAsync(c->qbuf.p, dq, qbytes, cudaMemcpyDeviceToDevice, s));
+    dq = c->qbuf.p;
+  }
   PrefillArgs a;
   a.table_row = c->table_row(seq, layer);
   a.n_total = n;
@@ -1415,21 +1414,23 @@ static bool prefill_tiled(lc_cache* c, int32_t layer, int32_t seq, const void* q
   a.off_vw = c->layout.off[R_VW];
   a.off_ks = c->layout.off[R_KS];
   a.off_vs = c->layout.off[R_VS];
-  a.q_rot = c->q_rot.p;
+  a.q = dq;
+  a.q_dtype = q_dtype;
+  a.q_rotated = (flags & LC_Q_ROTATED) ? 1 : 0;
+  a.qscale = scale * 1.4426950408889634f / c->dk.alpha;
+  a.kR = c->dk.R;
+  a.vRT = c->v_RT(flags);
   a.kcent = c->dk.cent_d;
   a.vcent = c->dv.cent_d;
   a.kalpha = c->dk.alpha;
   a.valpha = c->dv.alpha;
   a.pthr = decode_klo_thr(c->dk.lo_max);
-  a.m_out = c->part.p;
-  a.l_out = c->part.p + rows;
-  a.o_out = c->part.p + 2 * rows;
+  a.out = dout;
+  a.out_dtype = out_dtype;
+  a.oscale = 1.0f / c->dv.alpha;
   c->timed(c->t_decode, s, [&] { launch_prefill_tiled(a, s); });
-  c->timed(c->t_other, s, [&] {
-    launch_merge_rows(a.m_out, a.l_out, a.o_out, (int32_t)rows, D, c->v_R(flags), dout, out_dtype,
-                      1.0f / c->dv.alpha, s);
-  });
-  c->launches += 3;
+  if (host_q) LC_CUDA(cudaEventRecord(c->ev_copy, s));
+  ++c->launches;
   return true;
 }
 

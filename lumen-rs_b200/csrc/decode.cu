@@ -2630,14 +2630,6 @@ void launch_merge_parts(const float* m, const float* l, const float* o, int32_t 
   launch_merge_dev(d, s);
 }
 
-void launch_merge_rows(const float* m, const float* l, const float* o, int32_t n_rows, int32_t dim, const float* R,
-                       void* out, int32_t out_dtype, float oscale, cudaStream_t s) {
-  if (n_rows <= 0) return;
-  MergeDev d{nullptr, m, l, o, nullptr, 1, 1, n_rows, dim, oscale, R, out, out_dtype, nullptr, nullptr, nullptr,
-             0, nullptr, 0, 0u, nullptr};
-  launch_merge_dev(d, s);
-}
-
 void launch_merge_split(const SplitCall& x, int32_t D, const float* R, void* out, int32_t out_dtype,
                         cudaStream_t s) {
   MergeDev d{nullptr, x.parts, x.parts + x.rows, x.parts + 2 * (int64_t)x.rows, nullptr, 1, x.world, x.rows, D, 1.0f,

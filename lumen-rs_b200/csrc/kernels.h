@@ -77,30 +77,32 @@ size_t append_smem_bytes(int d, int m);
 // to the view: query token i (0-based in the chunk) sees keys 0 ..
 // n_total - L + i. A CTA takes one kv head and a block of query tokens (all
 // G heads of each); every 64-key tile is dequantized once into shared memory
-// for its 128 query rows. 4-bit K and V, head_dim 128, G <= 8. The kernel
-// writes rotated, unnormalised partials (m in log2 units, l, o) per row
-// (token * hq + head); the merge normalises and un-rotates.
+// for its 128 query rows. 4-bit K and V, head_dim 128, G <= 8. One launch:
+// the kernel rotates its queries and writes the normalised, un-rotated rows
+// (token * hq + head) itself.
 struct PrefillArgs {
   const uint64_t* table_row = nullptr;  // the sequence's block-table row (page addresses)
   int64_t n_total = 0;                  // tokens in the view
   int32_t L = 0, hkv = 0, hq = 0;
   int64_t off_kw = 0, off_vw = 0, off_ks = 0, off_vs = 0;  // PageLayout offsets
-  const float* q_rot = nullptr;  // [L][hq][128] R q * scale * log2(e) / kalpha
-  const float* kcent = nullptr;  // [16]
-  const float* vcent = nullptr;  // [16]
+  const void* q = nullptr;  // [L][hq][128] raw queries (f32 / bf16 / f16)
+  int32_t q_dtype = 0, q_rotated = 0;  // q_rotated: q is already R q
+  float qscale = 1.0f;                 // scale * log2(e) / kalpha
+  const float* kR = nullptr;           // K codec R (row-major): q' = R q
+  const float* vRT = nullptr;          // V codec R^T (row-major); null leaves the output rotated
+  const float* kcent = nullptr;        // [16]
+  const float* vcent = nullptr;        // [16]
   float kalpha = 1.0f, valpha = 1.0f;
   // precise tiles: when max sigma_K of a tile x max ||q'|| of the block
-  // exceeds pthr, the scores add the K table's residual products (decode_klo_thr, as the decode kernels)
+  // exceeds pthr, the scores add the K table's residual products
+  // (decode_klo_thr, as the decode kernels)
   float pthr = 3.0e38f;
-  float* m_out = nullptr;  // [L * hq]
-  float* l_out = nullptr;  // [L * hq]
-  float* o_out = nullptr;  // [L * hq][128]
+  void* out = nullptr;  // [L][hq][128], out_dtype
+  int32_t out_dtype = 0;
+  float oscale = 1.0f;  // 1 / valpha
 };
 bool prefill_tiled_path(int dim, int kbits, int vbits, int G);
 void launch_prefill_tiled(const PrefillArgs& a, cudaStream_t s);
-// merge of one part per row: out = R^T (o / l) * oscale (decode.cu)
-void launch_merge_rows(const float* m, const float* l, const float* o, int32_t n_rows, int32_t dim, const float* R,
-                       void* out, int32_t out_dtype, float oscale, cudaStream_t s);
 
 // ---- decode attention (decode.cu) ------------------------------------------
 struct DecodeArgs {

@@ -22,11 +22,16 @@
 // that visible (PrefillArgs::pthr, the decode kernels' criterion) the scores
 // add Q (alpha c - f16(alpha c)) x 2^11 from a second, residual K tile.
 //
+// One launch: the block also rotates its query rows (R q on the tensor cores,
+// f16 hi / lo splits of both operands) and normalises and un-rotates its
+// output rows (V's R^T, the same way) before writing them.
+//
 // Traffic: each key tile is read from HBM once per (kv head, query block)
 // and stays in L2 (the whole view of a 16K-token prefix is 17.8 MB for 8 kv
 // heads), so DRAM traffic is about view x 136 B per kv head, not L x view.
 // The roofline is the tensor pipe: two QK and one PV m16n8k16 MMA per
 // (16 rows x 8 keys x 16 dims) on the common path.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -99,6 +104,7 @@ __device__ __forceinline__ void pf_split(float x, float y, uint32_t& hi, uint32_
 }
 
 constexpr float kPfLoScale = 2048.f, kPfLoUnscale = 1.f / 2048.f;
+constexpr float kPfRotScale = 256.f, kPfRotUnscale = 1.f / 256.f;
 
 template <int G>
 __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid_constant__ PrefillArgs a) {
@@ -107,6 +113,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid
   __shared__ float s_qn[kPfWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
+  const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix and row of this lane's address
   const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
   const uint32_t lut_s = (s0 + 65535u) & ~65535u;
   uint8_t* base = smem + (lut_s - s0);
@@ -141,47 +148,118 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid
   };
   if (ntiles > 0) issue(0, 0);
 
-  // centroid-pair table: entry (byte b, slot) = (c[b & 15], c[b >> 4]) x alpha;
-  // K in slots 0..15, K residuals x 2^11 in 16..31, V in 32..63
-  if (threadIdx.x < 32) s_cent[threadIdx.x] = threadIdx.x < 16 ? a.kcent[threadIdx.x] * a.kalpha
-                                                                : a.vcent[threadIdx.x - 16] * a.valpha;
-  __syncthreads();
-  {
-    uint32_t* lut = reinterpret_cast<uint32_t*>(base);
-    for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
-      const int b = idx >> 6, slot = idx & 63, off = slot < 32 ? 0 : 16;
-      const float x0 = s_cent[off + (b & 15)], x1 = s_cent[off + (b >> 4)];
-      lut[idx] = slot >= 16 && slot < 32
-                     ? h2_as_u32(__floats2half2_rn((x0 - __half2float(__float2half_rn(x0))) * kPfLoScale,
-                                                   (x1 - __half2float(__float2half_rn(x1))) * kPfLoScale))
-                     : h2_as_u32(__floats2half2_rn(x0, x1));
-    }
-  }
-
   // ---- the warp's rows: R0 = 16 warp + g and R1 = R0 + 8, row R = (token
-  // tok0 + R / G, head R % G of the group); A fragments of Q, hi and lo ----
+  // tok0 + R / G, head R % G of the group) ----
   const int R0 = warp * 16 + g, R1 = R0 + 8;
   const bool v0 = R0 < TPC * G && R0 / G < ntok, v1 = R1 < TPC * G && R1 / G < ntok;
   const int tk0 = tok0 + R0 / G, tk1 = tok0 + R1 / G;
   const int64_t row0 = (int64_t)tk0 * a.hq + kvh * G + R0 % G, row1 = (int64_t)tk1 * a.hq + kvh * G + R1 % G;
-  uint32_t qh[8][4], ql[8][4];
-  float qn0 = 0.f, qn1 = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int d = 16 * kk + 8 * hh + 2 * t;
-      const float2 x0 = v0 ? *reinterpret_cast<const float2*>(a.q_rot + row0 * kPfD + d) : make_float2(0.f, 0.f);
-      const float2 x1 = v1 ? *reinterpret_cast<const float2*>(a.q_rot + row1 * kPfD + d) : make_float2(0.f, 0.f);
-      pf_split(x0.x, x0.y, qh[kk][2 * hh], ql[kk][2 * hh]);
-      pf_split(x1.x, x1.y, qh[kk][2 * hh + 1], ql[kk][2 * hh + 1]);
-      qn0 = fmaf(x0.x, x0.x, fmaf(x0.y, x0.y, qn0));
-      qn1 = fmaf(x1.x, x1.x, fmaf(x1.y, x1.y, qn1));
+
+  // ---- q' = (R q) * qscale on the tensor cores, into the A fragments of
+  // Q K^T (hi and lo parts). R, scaled by 2^8 so its f16 residuals stay
+  // normal, is staged as f16 hi / lo [i][j] tiles in the table's space
+  // (built afterwards); q rows are split as they load. D = q_hi R_hi +
+  // q_hi R_lo + q_lo R_hi (the dropped lo lo term is 2^-22 of the product).
+  // The rotation's accumulators (16 rows x 128 dims, n-tile j = dims 8j ..)
+  // are exactly the A fragments of k-step kk = n-tiles 2kk, 2kk + 1. ----
+  const uint32_t rh_s = lut_s, rl_s = lut_s + 32768;
+  if (!a.q_rotated) {
+    for (int u = threadIdx.x; u < kPfD * kPfD / 8; u += blockDim.x) {  // 8 elements per thread step
+      const int i = u >> 4, c = u & 15;
+      const float4 f0 = *reinterpret_cast<const float4*>(a.kR + i * kPfD + 8 * c);
+      const float4 f1 = *reinterpret_cast<const float4*>(a.kR + i * kPfD + 8 * c + 4);
+      uint32_t h[4], l[4];
+      pf_split(f0.x * kPfRotScale, f0.y * kPfRotScale, h[0], l[0]);
+      pf_split(f0.z * kPfRotScale, f0.w * kPfRotScale, h[1], l[1]);
+      pf_split(f1.x * kPfRotScale, f1.y * kPfRotScale, h[2], l[2]);
+      pf_split(f1.z * kPfRotScale, f1.w * kPfRotScale, h[3], l[3]);
+      const uint32_t off = pf_swz(i, c);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(rh_s + off), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+                   "r"(h[3])
+                   : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(rl_s + off), "r"(l[0]), "r"(l[1]), "r"(l[2]),
+                   "r"(l[3])
+                   : "memory");
     }
   }
-  float qn = fmaxf(qn0, qn1);
-  qn = fmaxf(qn, __shfl_xor_sync(0xffffffffu, qn, 1));
-  qn = fmaxf(qn, __shfl_xor_sync(0xffffffffu, qn, 2));
+  if (threadIdx.x < 32) s_cent[threadIdx.x] = threadIdx.x < 16 ? a.kcent[threadIdx.x] * a.kalpha
+                                                                : a.vcent[threadIdx.x - 16] * a.valpha;
+  __syncthreads();
+  uint32_t qh[8][4], ql[8][4];
+  float qn0 = 0.f, qn1 = 0.f;
+  {
+    // raw q of rows R0 / R1 at dims (d, d + 1), times qscale
+    auto qpair = [&](bool ok, int64_t row, int d) -> float2 {
+      if (!ok) return make_float2(0.f, 0.f);
+      const int64_t e = row * kPfD + d;
+      float2 f;
+      if (a.q_dtype == LC_F32) {
+        f = *reinterpret_cast<const float2*>(static_cast<const float*>(a.q) + e);
+      } else {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(a.q) + e);
+        if (a.q_dtype == LC_BF16) {
+          f = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+        } else {
+          f = make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))),
+                          __half2float(__ushort_as_half((unsigned short)(w >> 16))));
+        }
+      }
+      return make_float2(f.x * a.qscale, f.y * a.qscale);
+    };
+    if (a.q_rotated) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int d = 16 * kk + 8 * hh + 2 * t;
+          const float2 x0 = qpair(v0, row0, d), x1 = qpair(v1, row1, d);
+          pf_split(x0.x, x0.y, qh[kk][2 * hh], ql[kk][2 * hh]);
+          pf_split(x1.x, x1.y, qh[kk][2 * hh + 1], ql[kk][2 * hh + 1]);
+          qn0 = fmaf(x0.x, x0.x, fmaf(x0.y, x0.y, qn0));
+          qn1 = fmaf(x1.x, x1.x, fmaf(x1.y, x1.y, qn1));
+        }
+    } else {
+      float d[16][4];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {  // k-step: dims 16 kk .. of q
+        uint32_t ah[4], al[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int dd = 16 * kk + 8 * hh + 2 * t;
+          const float2 x0 = qpair(v0, row0, dd), x1 = qpair(v1, row1, dd);
+          pf_split(x0.x, x0.y, ah[2 * hh], al[2 * hh]);
+          pf_split(x1.x, x1.y, ah[2 * hh + 1], al[2 * hh + 1]);
+        }
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {  // output dims 16 np ..
+          uint32_t bh[4], bl[4];
+          const uint32_t off = pf_swz(16 * np + (mi >> 1) * 8 + mr, 2 * kk + (mi & 1));
+          ldsm_x4(rh_s + off, bh);
+          ldsm_x4(rl_s + off, bl);
+          mma16816(d[2 * np], ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+          mma16816(d[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bh[2], bh[3]);
+          mma16816(d[2 * np], ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+          mma16816(d[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bl[2], bl[3]);
+          mma16816(d[2 * np], al[0], al[1], al[2], al[3], bh[0], bh[1]);
+          mma16816(d[2 * np + 1], al[0], al[1], al[2], al[3], bh[2], bh[3]);
+        }
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float* e = d[2 * kk + hh];
+          const float x00 = e[0] * kPfRotUnscale, x01 = e[1] * kPfRotUnscale;
+          const float x10 = e[2] * kPfRotUnscale, x11 = e[3] * kPfRotUnscale;
+          pf_split(x00, x01, qh[kk][2 * hh], ql[kk][2 * hh]);
+          pf_split(x10, x11, qh[kk][2 * hh + 1], ql[kk][2 * hh + 1]);
+          qn0 = fmaf(x00, x00, fmaf(x01, x01, qn0));
+          qn1 = fmaf(x10, x10, fmaf(x11, x11, qn1));
+        }
+    }
+  }
   // per row the four lanes' sums add; the block's largest row norm bounds all
   {
     float r0n = qn0 + __shfl_xor_sync(0xffffffffu, qn0, 1);
@@ -193,8 +271,21 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid
     for (int o = 4; o < 32; o <<= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
     if (lane == 0) s_qn[warp] = w;
   }
-  (void)qn;
-  __syncthreads();
+  __syncthreads();  // the rotation's reads of R are done: the table replaces it
+
+  // centroid-pair table: entry (byte b, slot) = (c[b & 15], c[b >> 4]) x alpha;
+  // K in slots 0..15, K residuals x 2^11 in 16..31, V in 32..63
+  {
+    uint32_t* lut = reinterpret_cast<uint32_t*>(base);
+    for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
+      const int b = idx >> 6, slot = idx & 63, off = slot < 32 ? 0 : 16;
+      const float x0 = s_cent[off + (b & 15)], x1 = s_cent[off + (b >> 4)];
+      lut[idx] = slot >= 16 && slot < 32
+                     ? h2_as_u32(__floats2half2_rn((x0 - __half2float(__float2half_rn(x0))) * kPfLoScale,
+                                                   (x1 - __half2float(__float2half_rn(x1))) * kPfLoScale))
+                     : h2_as_u32(__floats2half2_rn(x0, x1));
+    }
+  }
   float qmax2 = 0.f;
 #pragma unroll
   for (int w = 0; w < kPfWarps; ++w) qmax2 = fmaxf(qmax2, s_qn[w]);
@@ -208,7 +299,6 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid
   float o[16][4];
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix and row of this lane's address
 
   for (int kt = 0; kt < ntiles; ++kt) {
     cp_wait_all();
@@ -330,28 +420,88 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) k_prefill_tiled(const __grid
     }
   }
 
-  // ---- the rows' partials: m (log2 units), l, O (rotated, V table units) ----
+  // ---- the rows: O / l * oscale, un-rotated by V's R^T on the tensor cores
+  // (out[i] = sum_j R[j][i] o[j]: A = the normalised O in its accumulator
+  // layout, B = R^T [i][j] staged as f16 hi / lo tiles x 2^8 in the table's
+  // space), written in the caller's dtype ----
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  if (v0) {
-    if (t == 0) {
-      a.m_out[row0] = m0;
-      a.l_out[row0] = l0;
-    }
+  const float n0 = l0 > 0.f ? a.oscale / l0 : 0.f, n1 = l1 > 0.f ? a.oscale / l1 : 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      *reinterpret_cast<float2*>(a.o_out + row0 * kPfD + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
+  for (int j = 0; j < 16; ++j) {
+    o[j][0] *= n0;
+    o[j][1] *= n0;
+    o[j][2] *= n1;
+    o[j][3] *= n1;
   }
-  if (v1) {
-    if (t == 0) {
-      a.m_out[row1] = m1;
-      a.l_out[row1] = l1;
+  if (a.vRT) {
+    __syncthreads();  // every warp is past its last tile: the table space is free
+    for (int u = threadIdx.x; u < kPfD * kPfD / 8; u += blockDim.x) {
+      const int i = u >> 4, c = u & 15;
+      const float4 f0 = *reinterpret_cast<const float4*>(a.vRT + i * kPfD + 8 * c);
+      const float4 f1 = *reinterpret_cast<const float4*>(a.vRT + i * kPfD + 8 * c + 4);
+      uint32_t h[4], l[4];
+      pf_split(f0.x * kPfRotScale, f0.y * kPfRotScale, h[0], l[0]);
+      pf_split(f0.z * kPfRotScale, f0.w * kPfRotScale, h[1], l[1]);
+      pf_split(f1.x * kPfRotScale, f1.y * kPfRotScale, h[2], l[2]);
+      pf_split(f1.z * kPfRotScale, f1.w * kPfRotScale, h[3], l[3]);
+      const uint32_t off = pf_swz(i, c);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(rh_s + off), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+                   "r"(h[3])
+                   : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(rl_s + off), "r"(l[0]), "r"(l[1]), "r"(l[2]),
+                   "r"(l[3])
+                   : "memory");
+    }
+    __syncthreads();
+    float d[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {  // k-step: dims 16 kk .. of o
+      uint32_t ah[4], al[4];
+      pf_split(o[2 * kk][0], o[2 * kk][1], ah[0], al[0]);
+      pf_split(o[2 * kk][2], o[2 * kk][3], ah[1], al[1]);
+      pf_split(o[2 * kk + 1][0], o[2 * kk + 1][1], ah[2], al[2]);
+      pf_split(o[2 * kk + 1][2], o[2 * kk + 1][3], ah[3], al[3]);
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        uint32_t bh[4], bl[4];
+        const uint32_t off = pf_swz(16 * np + (mi >> 1) * 8 + mr, 2 * kk + (mi & 1));
+        ldsm_x4(rh_s + off, bh);
+        ldsm_x4(rl_s + off, bl);
+        mma16816(d[2 * np], ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+        mma16816(d[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bh[2], bh[3]);
+        mma16816(d[2 * np], ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        mma16816(d[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bl[2], bl[3]);
+        mma16816(d[2 * np], al[0], al[1], al[2], al[3], bh[0], bh[1]);
+        mma16816(d[2 * np + 1], al[0], al[1], al[2], al[3], bh[2], bh[3]);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      *reinterpret_cast<float2*>(a.o_out + row1 * kPfD + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] = d[j][0] * kPfRotUnscale;
+      o[j][1] = d[j][1] * kPfRotUnscale;
+      o[j][2] = d[j][2] * kPfRotUnscale;
+      o[j][3] = d[j][3] * kPfRotUnscale;
+    }
+  }
+  auto put2 = [&](int64_t row, int dim, float x, float y) {
+    const int64_t e = row * kPfD + dim;
+    if (a.out_dtype == LC_F32) {
+      *reinterpret_cast<float2*>(static_cast<float*>(a.out) + e) = make_float2(x, y);
+    } else if (a.out_dtype == LC_BF16) {
+      *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(a.out) + e) = __floats2bfloat162_rn(x, y);
+    } else {
+      *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + e) = __floats2half2_rn(x, y);
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (v0) put2(row0, 8 * j + 2 * t, o[j][0], o[j][1]);
+    if (v1) put2(row1, 8 * j + 2 * t, o[j][2], o[j][3]);
   }
 }
 
