@@ -736,7 +736,7 @@ def run_ours(args):
         result = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic",
+            "dtype": "f16 tensor-core products (K/V centroid tables f16; queries and P as f16 hi+lo pairs, f32-accurate), f32 accumulation and softmax", "data": "synthetic",
             "config": {"workload": f"config1 decode: batch 32/GPU, 32q/8kv, d128, ctx 8192 (+1 per step), "
                                    f"{L} layers, 4-bit K/V packed; append + decode per layer",
                        "global_batch": world * B, "seq_len": ctx, "parallelism": f"request-shard x{world}",
@@ -814,7 +814,8 @@ def run_longctx(args):
     if rank == 0:
         line = {"metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16 tensor-core products (K/V centroid tables f16; queries and P as f16 hi+lo pairs, f32-accurate), f32 accumulation and softmax",
+                "data": "synthetic",
                 "config": {"workload": r["workload"], "global_batch": 1, "seq_len": args.ctx_tokens,
                            "parallelism": f"sequence-split x{world}"},
                 "clocks": clk.summary(), "mode": "longctx"}
@@ -912,7 +913,8 @@ def run_window(args):
     print(json.dumps({
         "metric": METRIC, "value": B / (ms_step / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": steps,
         "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f16 tensor-core products, f32 softmax", "data": "synthetic", "mode": "window",
+        "dtype": "f16 tensor-core products (K/V centroid tables f16; queries and P as f16 hi+lo pairs, f32-accurate), f32 accumulation and softmax", "data": "synthetic",
+        "mode": "window",
         "config": {"workload": f"config2: batch {B}, {hq}q/{hkv}kv, d{D}, 3-bit K / 2-bit V, 5 sliding layers "
                                f"(ring {win}, wrapped 4x) + 1 global layer ({glob_ctx} tokens); append + decode "
                                f"per layer", "views": views},
@@ -982,7 +984,8 @@ def run_sparse(args):
     print(json.dumps({
         "metric": METRIC, "value": B / (res["sparse"] / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": res["sparse"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic", "mode": "sparse",
+        "vs_baseline": None, "dtype": "f16 tensor-core products (K/V centroid tables f16; queries and P as f16 hi+lo pairs, f32-accurate), f32 accumulation and softmax",
+        "data": "synthetic", "mode": "sparse",
         "config": {"workload": f"config4 per-GPU share: {B} requests x {ctx} tokens, {hq}q/{hkv}kv, d{D}, 4-bit, "
                                f"{L} layers; page-sparse decode (64-token pages, keep max(pages/8, 64) + sink + "
                                f"recent + tail) vs dense", "kept_fraction": keep * 64 / ctx},
