@@ -421,11 +421,26 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
     for (int k = 0; k < kQRows; ++k)
 #pragma unroll
       for (int r = 0; r < R; ++r) qa[k][r] = 0.f;
+    // lane l owns outputs R l .. R l + R - 1 (d 64 / 128): one vector load
+    // of R^T[j][R l ..] per j
+    constexpr bool kQContig = R == 2 || R == 4;
 #pragma unroll 4
     for (int j = 0; j < D; ++j) {
       float w[R];
+      if constexpr (R == 4) {
+        const float4 q = *reinterpret_cast<const float4*>(RT + j * D + 4 * lane);
+        w[0] = q.x;
+        w[1] = q.y;
+        w[2] = q.z;
+        w[3] = q.w;
+      } else if constexpr (R == 2) {
+        const float2 q = *reinterpret_cast<const float2*>(RT + j * D + 2 * lane);
+        w[0] = q.x;
+        w[1] = q.y;
+      } else {
 #pragma unroll
-      for (int r = 0; r < R; ++r) w[r] = RT[j * D + lane + 32 * r];
+        for (int r = 0; r < R; ++r) w[r] = RT[j * D + lane + 32 * r];
+      }
 #pragma unroll
       for (int k = 0; k < kQRows; ++k) {
         const float qj = rows[k][j];
@@ -437,7 +452,7 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
     for (int k = 0; k < kQRows; ++k)
       if (live[k]) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) a.q_out[(r0 + k) * D + lane + 32 * r] = qa[k][r];
+        for (int r = 0; r < R; ++r) a.q_out[(r0 + k) * D + (kQContig ? R * lane + r : lane + 32 * r)] = qa[k][r];
       }
     return;  // TAB: no block-wide barrier after this point
   }
@@ -457,10 +472,39 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
     }
   }
   // ---- rotated[i] = sum_j R[i][j] x[j] (rotation.rs:91-99) ----
+  // With the table staged (d 64 / 128) lane l owns the R consecutive outputs
+  // R l .. R l + R - 1 and reads its coefficients R^T[j][R l ..] as one
+  // vector load per j; otherwise outputs l, l + 32, ... Every output's sum
+  // runs j ascending either way.
+  constexpr bool kContig = TAB && (R == 2 || R == 4);
+  auto own = [&](int r) { return kContig ? R * lane + r : lane + 32 * r; };
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = -0.0f;
-  if constexpr (TAB) {
+  if constexpr (kContig) {
+#pragma unroll 2
+    for (int j = 0; j < D; j += 4) {
+      const float4 x4 = *reinterpret_cast<const float4*>(x + j);
+      const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        float w[R];
+        if constexpr (R == 4) {
+          const float4 q = *reinterpret_cast<const float4*>(RT + (j + jj) * D + 4 * lane);
+          w[0] = q.x;
+          w[1] = q.y;
+          w[2] = q.z;
+          w[3] = q.w;
+        } else {
+          const float2 q = *reinterpret_cast<const float2*>(RT + (j + jj) * D + 2 * lane);
+          w[0] = q.x;
+          w[1] = q.y;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(w[r], xs[jj]));
+      }
+    }
+  } else if constexpr (TAB) {
 #pragma unroll 4
     for (int j = 0; j < D; ++j) {
       const float xj = x[j];
@@ -498,8 +542,8 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    y[lane + 32 * r] = acc[r];
-    res[lane + 32 * r] = __fmul_rn(acc[r], acc[r]);
+    y[own(r)] = acc[r];
+    res[own(r)] = __fmul_rn(acc[r], acc[r]);
   }
   __syncwarp();
   // ---- scale (compressor.rs:70-71) ----
@@ -512,7 +556,7 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   inv = __shfl_sync(0xffffffffu, inv, 0);
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int i = lane + 32 * r;
+    const int i = own(r);
     int code = 0;
     if (!(sc < 1e-10f)) {
       const float yn = __fmul_rn(acc[r], inv);
