@@ -154,6 +154,8 @@ __global__ void __launch_bounds__(kRotDims * kRotSplit) k_rotate_q(const void* q
                                                                 const float* RT, int rotated, float qscale,
                                                                 float* q_rot, __half* q_h) {
   extern __shared__ __align__(16) float sq[];  // [kRotRows][D], then [kRotSplit][kRotRows][kRotDims]
+  pdl_launch_dependents();
+  pdl_wait();  // q may come from the previous kernel of the stream
   float* red = sq + kRotRows * D;
   const int il = threadIdx.x % kRotDims, js = threadIdx.x / kRotDims;
   const int i = blockIdx.y * kRotDims + il;
@@ -313,13 +315,6 @@ __device__ __forceinline__ uint32_t lut_v(uint32_t x, uint32_t lanebase, uint32_
 }
 
 
-// Programmatic dependent launch (sm_90+). launch_dependents lets the next
-// kernel of the stream be scheduled while this one runs; its CTAs take SMs
-// as this grid's CTAs exit. pdl_wait returns once the previous kernel of the
-// stream has completed and its writes are visible. Both are no-ops for a
-// kernel launched without the programmatic-serialization attribute.
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 
 
@@ -1763,6 +1758,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 template <int kMergeWarps>
 __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
   extern __shared__ __align__(16) float so[];  // [kMergeWarps][D]
+  pdl_launch_dependents();
+  pdl_wait();  // the partials come from the previous kernel
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = a.D;
   const int PS = D + 2;
@@ -1973,6 +1970,7 @@ __device__ __forceinline__ void m3_qk(const uint64_t* kb, int g, int t, uint32_t
 template <int G>
 __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_constant__ DecodeDev a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
@@ -2016,6 +2014,9 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
   }
   uint32_t ring = 0, cons = 0;  // tiles this warp issued / computed: stage count & 1, phase (count >> 1) & 1
   bool err = false;             // a stage wait ran out: the warp's partials become NaN
+  // the tables above are the codecs' constants; the rotated queries and the
+  // pages may come from the previous kernels of the stream
+  pdl_wait();
 
   const int64_t total = (int64_t)a.n_seqs * a.hkv * a.n_chunks;
   for (int64_t item = blockIdx.x; item < total; item += gridDim.x) {
@@ -2295,8 +2296,7 @@ void launch_mma32_g(const DecodeDev& d, cudaStream_t s) {
   const int64_t total = (int64_t)d.n_seqs * d.hkv * d.n_chunks;
   const int64_t grid = std::min<int64_t>((int64_t)num_sms(), total);
   if (grid <= 0) return;
-  k_decode_mma32<G><<<(unsigned)grid, kM3Warps * 32, kM3Smem, s>>>(d);
-  LC_CUDA(cudaGetLastError());
+  launch_pdl(k_decode_mma32<G>, dim3((unsigned)grid), dim3(kM3Warps * 32), kM3Smem, s, d);
 }
 
 template <int KPL, int GS, bool QJL>
@@ -2452,8 +2452,8 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
   LC_REQUIRE(dim % 64 == 0, LC_ERR_INVALID, "decode: head_dim must be 64, 128, 256 or 512");
   const dim3 grid((unsigned)((n_rows + kRotRows - 1) / kRotRows), (unsigned)(dim / kRotDims));
   const size_t smem = ((size_t)kRotRows * dim + (size_t)kRotSplit * kRotRows * kRotDims) * sizeof(float);
-  k_rotate_q<<<grid, kRotDims * kRotSplit, smem, s>>>(q, q_dtype, n_rows, dim, RT, q_is_rotated ? 1 : 0, qscale,
-                                                      q_rot, q_h);
+launch_pdl(k_rotate_q, grid, dim3(kRotDims * kRotSplit), smem, s, q, q_dtype, n_rows, dim, RT,
+             q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
   LC_CUDA(cudaGetLastError());
 }
 
@@ -2604,7 +2604,7 @@ template <int W>
 static void launch_merge_w(const MergeDev& d, cudaStream_t s) {
   const int blocks = (d.n_rows + W - 1) / W;
   const size_t smem = (size_t)W * d.D * sizeof(float);
-  k_merge<W><<<blocks, W * 32, smem, s>>>(d);
+  launch_pdl(k_merge<W>, dim3(blocks), dim3(W * 32), smem, s, d);
   LC_CUDA(cudaGetLastError());
 }
 

@@ -1,11 +1,16 @@
 // Device helpers shared by the attention kernels: the m16n8k16 f16 MMA,
-// half2 packing, the SFU exp2, cp.async staging, and one-thread bulk copies
-// completing on an mbarrier with bounded waits.
+// half2 packing, the SFU exp2, cp.async staging, one-thread bulk copies
+// completing on an mbarrier with bounded waits, and programmatic dependent
+// launch.
 #pragma once
 
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 
 #include <cstdint>
+#include <utility>
+
+#include "common.h"
 
 namespace lc {
 namespace {
@@ -70,6 +75,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 // orders this thread's generic-proxy shared accesses before later async-proxy
 // (bulk copy) writes to the same bytes
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Programmatic dependent launch (sm_90+). launch_dependents lets the next
+// kernel of the stream be scheduled while this one runs; its CTAs take SMs
+// as this grid's CTAs exit. pdl_wait returns once the previous kernel of the
+// stream has completed and its writes are visible. Both are no-ops for a
+// kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel of the stream finishes; it must call pdl_wait before
+// touching anything that kernel writes.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  LC_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
