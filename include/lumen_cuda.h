@@ -291,9 +291,10 @@ int lc_lkv2_info(const char* path, int64_t* n_layers, int64_t* n_records, uint64
  * plus the first page and the 4 most recent full pages and the undigested
  * tail: max(pages / 8, 64) pages in all (sparse_keep_pages). q' is the
  * rotated query; min and max come from the digest. Needs a cache created with
- * LC_STORE_DIGEST (LC_ERR_STATE), a full (non-sliding) layer and the 4-bit,
- * head_dim 128, GQA <= 4 geometry (LC_ERR_INVALID otherwise); not combined
- * with LC_QJL_SCORES. Below 16384 keys the decode is dense. */
+ * LC_STORE_DIGEST (LC_ERR_STATE), a full (non-sliding) layer and one of the
+ * tensor-core geometries with GQA <= 4: 4-bit K/V at head_dim 128, or 3-bit
+ * K / 2-bit V at head_dim 256 (LC_ERR_INVALID otherwise); not combined with
+ * LC_QJL_SCORES. Below 16384 keys the decode is dense. */
 #define LC_SPARSE_PAGES 8u
 
 /* Decode attention over the compressed cache, one query token per

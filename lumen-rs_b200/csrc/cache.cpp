@@ -1175,8 +1175,11 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     LC_REQUIRE(!qjl && !prefill, LC_ERR_INVALID, "page-sparse decode: not with QJL scores or prefill attention");
     LC_REQUIRE(c->full(layer), LC_ERR_INVALID, "page-sparse decode: full (non-sliding) layers only");
     const int G = n_q_heads / hkv;
-    LC_REQUIRE(decode_fast_path(D, (int)c->kc.bits, (int)c->vc.bits, G) && G <= 4, LC_ERR_INVALID,
-               "page-sparse decode: 4-bit K/V, head_dim 128, GQA <= 4 only");
+    LC_REQUIRE(((decode_fast_path(D, (int)c->kc.bits, (int)c->vc.bits, G) && G <= 4) ||
+                decode_mma_path(D, (int)c->kc.bits, (int)c->vc.bits, G)),
+               LC_ERR_INVALID,
+               "page-sparse decode: the tensor-core geometries only (4-bit K/V at head_dim 128, or 3-bit K / "
+               "2-bit V at head_dim 256; GQA <= 4)");
     real_info = info;
     std::vector<uint64_t> dpages;
     std::vector<int32_t> drows;

@@ -1906,6 +1906,8 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 1) k_merge(MergeDev a) {
 //
 // Precise tiles (large sigma_K x ||q'||, see kLoEta): the K pass is run a
 // second time over the residual table (alpha c - f16(alpha c)) x 2^11.
+// Page-sparse calls pass a tile map: the items then cover the logical
+// (chosen) tokens and each tile is fetched from its mapped place.
 // ---------------------------------------------------------------------------
 constexpr int kM3Warps = 12;
 constexpr int kM3TT = 16;
@@ -2084,8 +2086,17 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       fence_proxy_async();  // the stage's earlier reads and P^T writes come first
       __syncwarp();
       const uint8_t* page = reinterpret_cast<const uint8_t*>(my_page_of(tl / tpp));
+      int rt = tl % tpp;  // 16-token tile within the page
+      if (a.tile_map) {
+        // page-sparse: logical 16-token tile lt of the (sequence, kv head) is
+        // half (lt & 1) of its mapped 32-token tile
+        const int64_t lt = (int64_t)chunk * a.pages_per_chunk * tpp + tl;
+        const int64_t p16 = 2 * (int64_t)a.tile_map[((int64_t)sq * a.hkv + kvh) * a.map_stride + (lt >> 1)] + (lt & 1);
+        page = reinterpret_cast<const uint8_t*>(trow[p16 / tpp]);
+        rt = (int)(p16 % tpp);
+      }
       if (lane == 0) {
-        const int64_t r0 = (int64_t)kvh * kPageTokens + (tl % tpp) * kM3TT;
+        const int64_t r0 = (int64_t)kvh * kPageTokens + rt * kM3TT;
         const uint32_t dst = st_s + (ring & 1) * kM3Stage, bar = bar_s + (ring & 1) * 8;
         mbar_expect_tx(bar, kM3Stage);
         bulk_g2s(dst, page + a.off_kw + r0 * kM3KRow, kM3TT * kM3KRow, bar);
@@ -2545,8 +2556,8 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
     }
   }
   if (p.mma) {
-    LC_REQUIRE(!d.tile_map && !d.q_proj && d.row_kw == kM3KRow && d.row_vw == kM3VRow, LC_ERR_STATE,
-               "decode: the tensor-core 3/2-bit path takes dense calls without QJL");
+    LC_REQUIRE(!d.q_proj && d.row_kw == kM3KRow && d.row_vw == kM3VRow, LC_ERR_STATE,
+               "decode: the tensor-core 3/2-bit path takes calls without QJL");
     switch (d.G) {
       case 1: return launch_mma32_g<1>(d, s);
       case 2: return launch_mma32_g<2>(d, s);

@@ -6,6 +6,7 @@
 //   k_digest4      min and max over each full 64-token page, per head and dim,
 //                  into the page's digest role (64 rows of head_dim / 8 bytes:
 //                  min[D] f32 then max[D] f32); 4-bit codes, head_dim 128
+//   k_digest_gen   the same for other bit widths at head_dim 128 / 256
 //   k_page_select  per (sequence, kv head): bound of every digested page
 //                  = max over the head's query group of
 //                    sum_d max(q'_d * max_d, q'_d * min_d),
@@ -82,6 +83,56 @@ __global__ void __launch_bounds__(128) k_digest4(DigestDev a, int heads) {
   }
 }
 
+// Any other bit width at head_dim 128 / 256 (the tensor-core geometries): a
+// warp per (page, head), 4 warps (heads) per block; lane l owns dims
+// l + 32 k, reads each token row's words through L1 and keeps the min and
+// max of f32(c[code]) * sigma of its dims.
+template <int D>
+__global__ void __launch_bounds__(128) k_digest_gen(DigestDev a, int heads) {
+  constexpr int KD = D / 32;
+  __shared__ float sc[256];
+  for (int k = threadIdx.x; k < (1 << a.bits); k += blockDim.x) sc[k] = a.cent[k];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * 4 + warp;
+  if (h >= heads) return;
+  const uint8_t* page = reinterpret_cast<const uint8_t*>(a.pages[blockIdx.x]);
+  const int64_t hr0 = (int64_t)h * kPageTokens + a.row0[blockIdx.x];
+  const int cpw = 64 / a.bits;
+  const uint64_t cmask = (1ull << a.bits) - 1ull;
+  int wi[KD], sh[KD];
+#pragma unroll
+  for (int k = 0; k < KD; ++k) {
+    const int d = lane + 32 * k;
+    wi[k] = d / cpw;
+    sh[k] = (d % cpw) * a.bits;
+  }
+  float mn[KD], mx[KD];
+#pragma unroll
+  for (int k = 0; k < KD; ++k) {
+    mn[k] = FLT_MAX;
+    mx[k] = -FLT_MAX;
+  }
+  const float* ks = reinterpret_cast<const float*>(page + a.off_ks) + hr0;
+#pragma unroll 2
+  for (int t = 0; t < kDigestPage; ++t) {
+    const uint64_t* w = reinterpret_cast<const uint64_t*>(page + a.off_kw + (hr0 + t) * a.row_kw);
+    const float sg = ks[t];
+#pragma unroll
+    for (int k = 0; k < KD; ++k) {
+      const float v = __fmul_rn(sc[(w[wi[k]] >> sh[k]) & cmask], sg);
+      mn[k] = fminf(mn[k], v);
+      mx[k] = fmaxf(mx[k], v);
+    }
+  }
+  float* dg = reinterpret_cast<float*>(const_cast<uint8_t*>(page) + a.off_dg + hr0 * a.row_dg);
+#pragma unroll
+  for (int k = 0; k < KD; ++k) {
+    dg[lane + 32 * k] = mn[k];
+    dg[D + lane + 32 * k] = mx[k];
+  }
+}
+
 // Query element i of an f32 / bf16 / f16 array.
 __device__ __forceinline__ float q_elem(const void* p, int dtype, int64_t i) {
   if (dtype == LC_F32) return reinterpret_cast<const float*>(p)[i];
@@ -97,7 +148,7 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 }
 constexpr uint32_t kPinnedKey = 0xFFFFFFFFu;
 constexpr int kSelThreads = 512;
-constexpr int kSelStages = 4;  // digest ring stages (1 KB pages) per warp: 3 in flight ahead
+constexpr int kSelStages = 4;  // digest ring stages (8 x head_dim bytes) per warp: 3 in flight ahead
 
 __device__ __forceinline__ void sel_cp16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
@@ -108,7 +159,7 @@ __device__ __forceinline__ void sel_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// One CTA per (sequence, kv head), head_dim 128, G <= 4:
+// One CTA per (sequence, kv head), head_dim D = 128 or 256, G <= 4:
 //   1. q' = R q for the G query heads (q as given unless already rotated),
 //      split into its positive and negative parts: the bound of a page is
 //      max_g sum_d (q'+_d max_d + q'-_d min_d), the same sum as
@@ -122,9 +173,10 @@ __device__ __forceinline__ void sel_wait() {
 //      prefix offsets), then the undigested tail.
 // The decode that follows is launched programmatically: its prologue reads
 // nothing this kernel writes and may start on SMs this grid has left.
-__global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
+template <int D>
+__global__ void __launch_bounds__(kSelThreads, D == 128 ? 2 : 1) k_page_select(SelectDev a) {
   extern __shared__ __align__(16) uint8_t sm[];
-  constexpr int D = 128, NT = kSelThreads;
+  constexpr int NT = kSelThreads, KD = D / 32, PGF = 2 * D;  // dims per lane, digest floats per page
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int b = blockIdx.x / a.hkv, kvh = blockIdx.x % a.hkv;
   const int G = a.G, tid = threadIdx.x;
@@ -143,8 +195,8 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   float* qp = reinterpret_cast<float*>(sm);  // [G][D] positive part of q'
   float* qn = qp + G * D;                     // [G][D] negative part
   float* qx = qn + G * D;                     // [G][D] the queries as given
-  float* ring = qx + G * D;                   // [warps][kSelStages][256] digest pages
-  uint32_t* key = reinterpret_cast<uint32_t*>(ring + (kSelThreads / 32) * kSelStages * 256);  // [npad]
+  float* ring = qx + G * D;                   // [warps][kSelStages][2 D] digest pages
+  uint32_t* key = reinterpret_cast<uint32_t*>(ring + (kSelThreads / 32) * kSelStages * PGF);  // [npad]
   uint64_t* pg = reinterpret_cast<uint64_t*>(key + ((a.npad + 1) & ~1));  // [npad / 4] page addresses
   float* red = reinterpret_cast<float*>(pg + a.npad / kGroupsPerPage + 1);    // [4][G][D] rotation partials
   __shared__ uint32_t hist[256];
@@ -159,7 +211,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   const int lane = tid & 31, warp = tid >> 5;
   constexpr int NW = NT / 32;
   const int K = warp < P ? (P - warp + NW - 1) / NW : 0;  // pages of this warp: warp + 16 k
-  float* wring = ring + warp * kSelStages * 256;
+  float* wring = ring + warp * kSelStages * PGF;
   const uint32_t ring0 = (uint32_t)__cvta_generic_to_shared(wring);
   auto live_page = [&](int p) { return p >= kSparseSink && p < P - kSparseRecent; };
   auto issue = [&](int k) {
@@ -167,9 +219,9 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
     if (k < K && live_page(p)) {
       const uint8_t* dg = reinterpret_cast<const uint8_t*>(pg[p / kGroupsPerPage]) + a.off_dg +
                           ((int64_t)kvh * kPageTokens + (p % kGroupsPerPage) * kDigestPage) * a.row_dg;
-      const uint32_t dst = ring0 + (k % kSelStages) * 1024;
-      sel_cp16(dst + lane * 16, dg + lane * 16);
-      sel_cp16(dst + 512 + lane * 16, dg + 512 + lane * 16);
+      const uint32_t dst = ring0 + (k % kSelStages) * PGF * 4;
+#pragma unroll
+      for (int o = 0; o < PGF * 4; o += 512) sel_cp16(dst + o + lane * 16, dg + o + lane * 16);
     }
   };
 #pragma unroll
@@ -181,35 +233,49 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
   // q'_i = sum_j R[i][j] q_j: thread t sums j in [32 (t / 128), + 32) for
   // output dim i = t % 128 of every head (its 32 loads of R^T in flight
   // together, coalesced); the 4 partial sums are added through shared memory
+  constexpr int NS = NT / D, SL = D / NS;  // slices of the sum over j, and their length
   if (!a.q_rotated) {
     const int i = tid % D, js = tid / D;
-    float rv[32];
+    float sg4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int u = 0; u < 32; ++u) rv[u] = a.RT[(32 * js + u) * D + i];
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
+    for (int c0 = 0; c0 < SL; c0 += 32) {
+      float rv[32];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) s = fmaf(rv[u], qx[g * D + 32 * js + u], s);
-      red[(js * G + g) * D + i] = s;
+      for (int u = 0; u < 32; ++u) rv[u] = a.RT[(SL * js + c0 + u) * D + i];
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        if (g < G) {
+#pragma unroll
+          for (int u = 0; u < 32; ++u) sg4[g] = fmaf(rv[u], qx[g * D + SL * js + c0 + u], sg4[g]);
+        }
     }
+    for (int g = 0; g < G; ++g) red[(js * G + g) * D + i] = sg4[g];
     __syncthreads();
   }
   for (int r = tid; r < G * D; r += NT) {
-    const float s = a.q_rotated ? qx[r] : (red[r] + red[G * D + r]) + (red[2 * G * D + r] + red[3 * G * D + r]);
+    float s = 0.f;
+    if (a.q_rotated) {
+      s = qx[r];
+    } else if constexpr (NS == 4) {
+      s = (red[r] + red[G * D + r]) + (red[2 * G * D + r] + red[3 * G * D + r]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NS; ++k) s += red[k * G * D + r];
+    }
     qp[r] = fmaxf(s, 0.f);
     qn[r] = fminf(s, 0.f);
   }
   __syncthreads();
 
-  // bounds: a warp per page; each page's digest (min[128] then max[128],
-  // 1 KB) streams into the warp's ring by cp.async, kSelStages - 1 pages
+  // bounds: a warp per page; each page's digest (min[D] then max[D], 8 D
+  // bytes) streams into the warp's ring by cp.async, kSelStages - 1 pages
   // ahead; lane l takes dims l + 32 j, whose q'+ and q'- for every head stay
   // in registers for the whole loop
-  float rp[4][4], rn[4][4];  // [head][j]
+  float rp[4][KD], rn[4][KD];  // [head][j]
 #pragma unroll
   for (int g = 0; g < 4; ++g)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < KD; ++j) {
       const int gg = g < G ? g : 0;  // heads past G repeat head 0: the max is unchanged
       rp[g][j] = qp[gg * D + lane + 32 * j];
       rn[g][j] = qn[gg * D + lane + 32 * j];
@@ -222,10 +288,10 @@ __global__ void __launch_bounds__(kSelThreads, 2) k_page_select(SelectDev a) {
     __syncwarp();
     const int p = warp + NW * k;
     if (live_page(p)) {
-      const float* st = wring + (k % kSelStages) * 256;
+      const float* st = wring + (k % kSelStages) * PGF;
       float sg[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < KD; ++j) {
         const float mn = st[lane + 32 * j], mx = st[D + lane + 32 * j];
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
@@ -373,27 +439,36 @@ void launch_digest(const DigestDev& a, int64_t n_items, int heads, cudaStream_t 
   if (n_items <= 0) return;
   // page-sparse decode takes the fast-path geometry only (lc_decode_attn
   // refuses the rest before digesting)
-  LC_REQUIRE(a.bits == 4 && a.dim == 128 && a.row_kw == 64, LC_ERR_INVALID,
-             "page digest: 4-bit codes, head_dim 128 only");
-  k_digest4<<<dim3((unsigned)n_items, (unsigned)((heads + 3) / 4)), 128, 0, s>>>(a, heads);
+  const dim3 grid((unsigned)n_items, (unsigned)((heads + 3) / 4));
+  if (a.bits == 4 && a.dim == 128 && a.row_kw == 64) k_digest4<<<grid, 128, 0, s>>>(a, heads);
+  else if (a.dim == 128 && a.bits <= 8) k_digest_gen<128><<<grid, 128, 0, s>>>(a, heads);
+  else if (a.dim == 256 && a.bits <= 8) k_digest_gen<256><<<grid, 128, 0, s>>>(a, heads);
+  else LC_THROW(LC_ERR_INVALID, "page digest: head_dim 128 or 256");
+  LC_CUDA(cudaGetLastError());
+}
+
+template <int D>
+static void launch_select_d(const SelectDev& a, cudaStream_t s) {
+  const size_t smem = (size_t)3 * a.G * D * 4 + (size_t)(kSelThreads / 32) * kSelStages * 2 * D * 4 +
+                      (size_t)((a.npad + 1) & ~1) * 4 + (size_t)(a.npad / kGroupsPerPage + 1) * 8 +
+                      (size_t)4 * a.G * D * 4;
+  static size_t max_dyn = 0;  // 227 KB less the static histogram
+  if (max_dyn == 0) {
+    cudaFuncAttributes fa;
+    LC_CUDA(cudaFuncGetAttributes(&fa, k_page_select<D>));
+    max_dyn = 227 * 1024 - fa.sharedSizeBytes;
+    LC_CUDA(cudaFuncSetAttribute(k_page_select<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dyn));
+  }
+  LC_REQUIRE(smem <= max_dyn, LC_ERR_INVALID, "page-sparse decode: too many pages for one selection block");
+  k_page_select<D><<<(unsigned)(a.n_seqs * a.hkv), kSelThreads, smem, s>>>(a);
   LC_CUDA(cudaGetLastError());
 }
 
 void launch_page_select(const SelectDev& a, cudaStream_t s) {
-  LC_REQUIRE(a.dim == 128 && a.G >= 1 && a.G <= 4, LC_ERR_INVALID, "page-sparse decode: head_dim 128, GQA <= 4");
-  const size_t smem = (size_t)3 * a.G * a.dim * 4 + (size_t)(kSelThreads / 32) * kSelStages * 1024 +
-                      (size_t)((a.npad + 1) & ~1) * 4 + (size_t)(a.npad / kGroupsPerPage + 1) * 8 +
-                      (size_t)4 * a.G * a.dim * 4;
-  static size_t max_dyn = 0;  // 227 KB less the static histogram
-  if (max_dyn == 0) {
-    cudaFuncAttributes fa;
-    LC_CUDA(cudaFuncGetAttributes(&fa, k_page_select));
-    max_dyn = 227 * 1024 - fa.sharedSizeBytes;
-    LC_CUDA(cudaFuncSetAttribute(k_page_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dyn));
-  }
-  LC_REQUIRE(smem <= max_dyn, LC_ERR_INVALID, "page-sparse decode: too many pages for one selection block");
-  k_page_select<<<(unsigned)(a.n_seqs * a.hkv), kSelThreads, smem, s>>>(a);
-  LC_CUDA(cudaGetLastError());
+  LC_REQUIRE((a.dim == 128 || a.dim == 256) && a.G >= 1 && a.G <= 4, LC_ERR_INVALID,
+             "page-sparse decode: head_dim 128 or 256, GQA <= 4");
+  if (a.dim == 128) launch_select_d<128>(a, s);
+  else launch_select_d<256>(a, s);
 }
 
 }  // namespace lc

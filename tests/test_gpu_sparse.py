@@ -10,7 +10,8 @@ token set (orc_sc_attend_mask) at the decode tolerance. The data is checked
 to leave no near-tie at the selection boundary. Queries use the configs'
 scale (std 1/sqrt(128)), and one test the peaked regime of the reference's
 Gemma call (q ~ N(0, 1), scale 1). A sequence below 16384 keys in the same
-call is dense.
+call is dense. Config 2's geometry (3-bit K / 2-bit V, head_dim 256) runs
+through the general digest and the tensor-core kernel's tile map.
 """
 import numpy as np
 import pytest
@@ -22,11 +23,18 @@ pytestmark = pytest.mark.gpu
 DIM, HKV, HQ = 128, 8, 32
 
 
-def _cache(lc, orc, lens, flags=None, max_size=0):
-    t = orc.Tables.generate(DIM, 4, 64, 42)
+def _cache(lc, orc, lens, flags=None, max_size=0, dim=DIM, kb=4, vb=4, hkv=HKV):
+    """The cache and the K codec's tables (the V codec's too when the bit
+    widths differ: returned as t.v)."""
+    t = orc.Tables.generate(dim, kb, 64, 42)
     c = lc.TurboQuantCompressor.from_tables(t.R, t.bounds, t.cents, t.proj)
+    tv, cv = t, None
+    if vb != kb:
+        tv = orc.Tables.generate(dim, vb, 64, 42)
+        cv = lc.TurboQuantCompressor.from_tables(tv.R, tv.bounds, tv.cents, tv.proj)
+    t.v, t.bits, t.dim, t.hkv = tv, kb, dim, hkv
     pages = (max(lens) + 400 + 255) // 256 + 2
-    cache = lc.CudaKvCache(1, HKV, DIM, c, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
+    cache = lc.CudaKvCache(1, hkv, dim, c, cv, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
                            max_pages_per_seq=pages,
                            store_flags=lc.LC_STORE_DIGEST if flags is None else flags,
                            layer_max_size=[max_size], layer_keep=[0])
@@ -39,19 +47,20 @@ def _fill(cache, orc, t, lens, seed):
     separate cleanly and the selection boundary has no near-tie."""
     refs, kv = [], []
     rng = np.random.default_rng(seed)
+    hkv, dim = t.hkv, t.dim
     for b, n in enumerate(lens):
-        K = helpers.kv(orc, seed + 2 * b, 1, HKV, n, DIM)
-        V = helpers.kv(orc, seed + 2 * b + 1, 1, HKV, n, DIM)
+        K = helpers.kv(orc, seed + 2 * b, 1, hkv, n, dim)
+        V = helpers.kv(orc, seed + 2 * b + 1, 1, hkv, n, dim)
         P = n // 64
         if P > 130:
-            for h in range(HKV):
+            for h in range(hkv):
                 for k, p in enumerate(rng.choice(np.arange(1, P - 4), size=120, replace=False)):
                     K[0, h, p * 64:(p + 1) * 64] *= np.float32(2.0 + 0.05 * k)
         for c0 in range(0, n, 4096):
             c1 = min(n, c0 + 4096)
             cache.append(0, [b], np.ascontiguousarray(K[:, :, c0:c1]), np.ascontiguousarray(V[:, :, c0:c1]))
-        ref = orc.SimpleCache(orc.Compressor(t), orc.Compressor(t), 1, HKV, DIM)
-        for h in range(HKV):
+        ref = orc.SimpleCache(orc.Compressor(t), orc.Compressor(t.v), 1, hkv, dim)
+        for h in range(hkv):
             ref.store(0, h, K[0, h], V[0, h], n)
         refs.append(ref)
         kv.append((K, V))
@@ -59,15 +68,16 @@ def _fill(cache, orc, t, lens, seed):
 
 
 def _oracle(orc, t, refs, q, scale, hq=HQ):
-    G = hq // HKV
-    out = np.zeros((len(refs), hq, DIM), np.float32)
+    hkv, dim = t.hkv, t.dim
+    G = hq // hkv
+    out = np.zeros((len(refs), hq, dim), np.float32)
     min_gap = float("inf")
     R = t.R.astype(np.float64)
     for b, ref in enumerate(refs):
-        for kvh in range(HKV):
+        for kvh in range(hkv):
             words, _, _, sigma = ref.read(0, kvh, 0)
             qr = q[b, kvh * G:(kvh + 1) * G].astype(np.float64) @ R.T
-            mask, gap = orc.quest_select(words, sigma, t.cents, 4, DIM, qr)
+            mask, gap = orc.quest_select(words, sigma, t.cents, t.bits, dim, qr)
             min_gap = min(min_gap, gap)
             for g in range(G):
                 out[b, kvh * G + g] = ref.attend_mask(0, kvh, q[b, kvh * G + g], scale, mask)
@@ -127,6 +137,30 @@ def test_sparse_digest_follows_appends(lc, orc, gpu):
     assert gap > 1e-4, gap
     ok, msg = helpers.attn_close(got, ref)
     assert ok, msg
+    cache.close()
+
+
+@pytest.mark.parametrize("std,scale,spread", [(1e-3, 256 ** -0.5, True), (256 ** -0.5, 256 ** -0.5, False),
+                                              (1.0, 1.0, False)])
+def test_sparse_decode_config2_geometry(lc, orc, gpu, std, scale, spread):
+    """3-bit K / 2-bit V at head_dim 256 (config 2's global layer, GQA 2):
+    the general digest, the head_dim-256 selection and the tensor-core
+    kernel through the tile map, against the oracle's selection + masked
+    attention; near-zero queries (nearly uniform weights, so the dropped
+    pages show in the output), the configs' query scale and the peaked
+    regime (where the chosen high-sigma pages hold the softmax mass)."""
+    lens = [20000, 5000]
+    t, cache = _cache(lc, orc, lens, dim=256, kb=3, vb=2, hkv=8)
+    refs, _ = _fill(cache, orc, t, lens, 500)
+    q = helpers.queries(orc, 501, len(lens), 16, 256, std=std)
+    got = cache.decode_attn(0, [0, 1], q, 16, scale, flags=lc.LC_SPARSE_PAGES)
+    ref, gap = _oracle(orc, t, refs, q, scale, hq=16)
+    assert gap > 1e-4, gap
+    ok, msg = helpers.attn_close(got, ref)
+    assert ok, msg
+    if spread:
+        dense = cache.decode_attn(0, [0, 1], q, 16, scale)
+        assert np.abs(dense[0] - got[0]).max() > 1e-3  # the long sequence really went sparse
     cache.close()
 
 
