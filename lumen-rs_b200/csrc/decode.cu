@@ -2575,7 +2575,9 @@ void launch_decode_partials(const DecodeArgs& a, const DecodePlan& p, cudaStream
 }
 
 bool decode_fusable(const DecodePlan& p, int G) {
-  return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs;
+  // segments of more than 64 slots (a long sequence over the whole grid)
+  // merge faster in the wide merge kernel than in one warp per row in-kernel
+  return p.flat && G >= 1 && G <= 4 && p.max_cta_segs <= kFusedSegs && p.max_slots <= 64;
 }
 
 void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedArgs& f, cudaStream_t s) {
@@ -2611,6 +2613,113 @@ void launch_decode_fused(const DecodeArgs& a, const DecodePlan& p, const FusedAr
   }
 }
 
+// Merge of rows with many slots (one long sequence split over all warps of
+// the grid: a few hundred slots per row, few rows): a block per row, its
+// kMergeWideWarps warps taking slots w, w + warps, ...; each warp's (M, L, O)
+// goes to shared memory and the block combines them, normalises and
+// un-rotates the row. The slot order inside a sum differs from k_merge's,
+// within f32 rounding.
+constexpr int kMergeWideWarps = 16;
+__global__ void __launch_bounds__(kMergeWideWarps * 32, 1) k_merge_wide(MergeDev a) {
+  extern __shared__ __align__(16) float sw[];  // [warps][D] O, then [warps] M, [warps] L, then [D] the row
+  pdl_launch_dependents();
+  pdl_wait();  // the partials come from the previous kernel
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int D = a.D, PS = D + 2, per = D / 32;
+  const int row = blockIdx.x;
+  float* wo = sw + warp * D;
+  float* wm = sw + kMergeWideWarps * D;
+  float* wl = wm + kMergeWideWarps;
+  float* orow = wl + kMergeWideWarps;
+  const int64_t group = row / a.G;
+  const int gh = row % a.G;
+  const int n = a.cnt ? a.cnt[group] : a.max_slots;
+  const float *pm, *pl, *po;
+  int64_t ms, os;
+  if (a.part) {
+    const float* p = a.part + (group * a.max_slots * a.G + gh) * PS;
+    pm = p;
+    pl = p + 1;
+    po = p + 2;
+    ms = os = (int64_t)a.G * PS;
+  } else {
+    pm = a.m_in + row;
+    pl = a.l_in + row;
+    po = a.o_in + (int64_t)row * D;
+    ms = a.pstride ? a.pstride : a.n_rows;
+    os = a.pstride ? a.pstride : (int64_t)a.n_rows * D;
+  }
+  // this warp's slots: c = warp + kMergeWideWarps k
+  float M = -INFINITY;
+  for (int c = warp + kMergeWideWarps * lane; c < n; c += kMergeWideWarps * 32) M = fmaxf(M, __ldcg(pm + c * ms));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float L = 0.f;
+  float O[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) O[k] = 0.f;
+  for (int c0 = warp; c0 < n; c0 += kMergeWideWarps * 32) {
+    const int c = c0 + kMergeWideWarps * lane;
+    float wgt = 0.f;
+    if (c < n) {
+      const float mc = __ldcg(pm + c * ms);
+      wgt = mc == -INFINITY ? 0.f : exp2f(mc - M);
+      L += wgt * __ldcg(pl + c * ms);
+    }
+    const int nn = min(32, (n - c0 + kMergeWideWarps - 1) / kMergeWideWarps);
+#pragma unroll 4
+    for (int u = 0; u < nn; ++u) {
+      const float w = __shfl_sync(0xffffffffu, wgt, u);
+      const float2* pc = reinterpret_cast<const float2*>(po + (int64_t)(c0 + kMergeWideWarps * u) * os + lane * per);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (2 * k < per) {
+          const float2 v = __ldcg(pc + k);
+          O[2 * k] = fmaf(w, v.x, O[2 * k]);
+          O[2 * k + 1] = fmaf(w, v.y, O[2 * k + 1]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < per) wo[lane * per + k] = O[k];
+  if (lane == 0) {
+    wm[warp] = M;
+    wl[warp] = L;
+  }
+  __syncthreads();
+  float Mt = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kMergeWideWarps; ++w) Mt = fmaxf(Mt, wm[w]);
+  float Lt = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMergeWideWarps; ++w)
+    if (wm[w] != -INFINITY) Lt += exp2f(wm[w] - Mt) * wl[w];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWideWarps; ++w)
+      if (wm[w] != -INFINITY) v += exp2f(wm[w] - Mt) * sw[w * D + i];
+    const float ov = v * a.oscale;
+    if (a.o_out) a.o_out[(int64_t)row * D + i] = ov;
+    orow[i] = Lt > 0.f ? ov / Lt : 0.f;
+  }
+  if (a.o_out && threadIdx.x == 0) {
+    a.m_out[row] = Mt;
+    a.l_out[row] = Lt;
+  }
+  if (!a.out) return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float acc[1] = {a.R ? 0.f : orow[i]};
+    if (a.R) mat_col<1>(a.R, D, i, orow, acc);
+    store_any(a.out, a.out_dtype, (int64_t)row * D + i, acc[0]);
+  }
+}
+
 template <int W>
 static void launch_merge_w(const MergeDev& d, cudaStream_t s) {
   const int blocks = (d.n_rows + W - 1) / W;
@@ -2620,6 +2729,11 @@ static void launch_merge_w(const MergeDev& d, cudaStream_t s) {
 }
 
 static void launch_merge_dev(const MergeDev& d, cudaStream_t s) {
+  if (!d.wait_flags && d.max_slots > 64) {  // few rows of many slots: a block per row
+    const size_t smem = ((size_t)kMergeWideWarps * d.D + 2 * kMergeWideWarps + d.D) * sizeof(float);
+    launch_pdl(k_merge_wide, dim3((unsigned)d.n_rows), dim3(kMergeWideWarps * 32), smem, s, d);
+    return;
+  }
   if (d.D >= 256) launch_merge_w<4>(d, s);
   else launch_merge_w<8>(d, s);
 }
