@@ -873,9 +873,11 @@ def run_window(args):
     out = torch.empty((L, B, hq, D), device=dev, dtype=torch.bfloat16)
 
     def step():
+        # lc_decode_step per layer: the append launch also rotates the step's
+        # queries, which the decode kernel reads as given
         for layer in range(L):
-            cache.append(layer, ids, k1[layer], v1[layer])
-            cache.decode_attn(layer, ids, qs[layer], hq, 1.0 / D ** 0.5, out=out[layer], out_dtype=lc.LC_BF16)
+            cache.decode_step(layer, ids, k1[layer], v1[layer], qs[layer], hq, 1.0 / D ** 0.5, out=out[layer],
+                              out_dtype=lc.LC_BF16)
 
     for _ in range(warm):
         step()
@@ -939,8 +941,8 @@ def run_window(args):
         "dtype": "f16 tensor-core products (K/V centroid tables f16; queries and P as f16 hi+lo pairs, f32-accurate), f32 accumulation and softmax", "data": "synthetic",
         "mode": "window",
         "config": {"workload": f"config2: batch {B}, {hq}q/{hkv}kv, d{D}, 3-bit K / 2-bit V, 5 sliding layers "
-                               f"(ring {win}, wrapped 4x) + 1 global layer ({glob_ctx} tokens); append + decode "
-                               f"per layer", "views": views},
+                               f"(ring {win}, wrapped 4x) + 1 global layer ({glob_ctx} tokens); lc_decode_step "
+                               f"(append + decode) per layer", "views": views},
         "decode_gbs": kv_bytes / (ms_step / 1e3) / 1e9, "bytes_per_token_head": bpt,
         "breakdown_ms_per_step": {"decode_attn": dec_ms / t_steps, "append": app_ms / t_steps,
                                   "other_kernels (query rotation, merge)": other_ms / t_steps},

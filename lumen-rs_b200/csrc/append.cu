@@ -456,6 +456,62 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
       }
     return;  // TAB: no block-wide barrier after this point
   }
+  if (!TAB && side == 2) {
+    // the step's query rows with R^T streamed through shared memory in
+    // chunks of kRtChunk rows (head_dim 256: R^T does not fit); plain f32
+    // FMAs as in the staged case, outputs lane + 32 r
+    const int64_t r0 = ((int64_t)blockIdx.x * kWarpVecs + warp) * kQRows;
+    float* rows[kQRows] = {x, y, res};
+    bool live[kQRows];
+#pragma unroll
+    for (int k = 0; k < kQRows; ++k) {
+      live[k] = r0 + k < a.q_rows;
+      if (live[k]) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) rows[k][lane + 32 * r] = load_elem(a.q, a.q_dtype, (r0 + k) * D + lane + 32 * r);
+      }
+    }
+    __syncwarp();
+    float qa[kQRows][R];
+#pragma unroll
+    for (int k = 0; k < kQRows; ++k)
+#pragma unroll
+      for (int r = 0; r < R; ++r) qa[k][r] = 0.f;
+    float* rbuf = reinterpret_cast<float*>(smem + 2048 + (size_t)kWarpVecs * (3 * D * 4 + 64 + D));
+    constexpr int NC = D / kRtChunk;
+    stage16(rbuf, c.RT, kRtChunk * D / 4);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    for (int ch = 0; ch < NC; ++ch) {
+      if (ch + 1 < NC) {
+        stage16(rbuf + ((ch + 1) & 1) * kRtChunk * D, c.RT + (size_t)(ch + 1) * kRtChunk * D, kRtChunk * D / 4);
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;\n" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      }
+      __syncthreads();
+      const float* rt = rbuf + (ch & 1) * kRtChunk * D;
+#pragma unroll 4
+      for (int jj = 0; jj < kRtChunk; ++jj) {
+        float w[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) w[r] = rt[jj * D + lane + 32 * r];
+#pragma unroll
+        for (int k = 0; k < kQRows; ++k) {
+          const float qj = rows[k][ch * kRtChunk + jj];
+#pragma unroll
+          for (int r = 0; r < R; ++r) qa[k][r] = fmaf(w[r], qj, qa[k][r]);
+        }
+      }
+      __syncthreads();  // the buffer is read before it is refilled
+    }
+#pragma unroll
+    for (int k = 0; k < kQRows; ++k)
+      if (live[k]) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) a.q_out[(r0 + k) * D + lane + 32 * r] = qa[k][r];
+      }
+    return;  // no block-wide barrier after this point
+  }
   const int64_t n_vec = (int64_t)a.n_seqs * a.h_in * a.n_tok;
   const int64_t v = (int64_t)blockIdx.x * kWarpVecs + warp;
   const bool active = v < n_vec;
@@ -906,7 +962,9 @@ void launch_tile_append(const AppendDev& d, int64_t n_vec, cudaStream_t s) {
 }  // namespace
 
 bool append_rotates_queries(int64_t n_vec, int dim, int m_max, bool stage2) {
-  if (n_vec > kSmallAppend || m_max > 512 || !(dim == 64 || dim == 128)) return false;
+  if (n_vec > kSmallAppend || m_max > 512) return false;
+  if (dim == 256) return true;  // the warp kernel streaming R^T (its query rows stream it too)
+  if (!(dim == 64 || dim == 128)) return false;
   const size_t base = 2048 + (size_t)kWarpVecs * (3 * dim * 4 + 64 + dim);
   const size_t tables = (size_t)dim * dim * 4 + (stage2 ? (size_t)(dim * dim + dim * m_max) * 4 : 0);
   return base + tables <= 200 * 1024;  // the warp kernel with R^T staged (TAB)

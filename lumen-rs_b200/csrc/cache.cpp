@@ -1248,7 +1248,10 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   const float kalpha = (plan.flat || plan.mma) ? c->dk.alpha : 1.0f,
               valpha = (plan.flat || plan.mma) ? c->dv.alpha : 1.0f;
   const float qscale = scale * 1.4426950408889634f / kalpha;
-  if (!fused) {
+  // the 3/2-bit tensor-core kernel takes rotated queries as given (scaled as
+  // it reads them), so a decode step's rotated rows need no launch here
+  const bool raw_q = plan.mma && (flags & LC_Q_ROTATED) && !qjl && !sparse;
+  if (!fused && !raw_q) {
     c->q_rot.ensure((size_t)rows * D, s);
     c->q_h.ensure((size_t)rows * D, s);
     c->timed(c->t_other, s, [&] {
@@ -1311,6 +1314,11 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   a.vbits = (int)c->vc.bits;
   a.q_rot = c->q_rot.p;
   a.q_h = c->q_h.p;
+  if (raw_q) {
+    a.q_raw = dq;
+    a.q_raw_dtype = q_dtype;
+    a.q_raw_scale = qscale;
+  }
   a.kcent = c->dk.cent_d;
   a.vcent = c->dv.cent_d;
   a.kalpha = kalpha;

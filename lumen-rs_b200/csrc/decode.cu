@@ -2028,7 +2028,12 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
     const int sq = (int)(rest / a.hkv);
     const int64_t n_valid = a.si()[2 * sq];
     const uint64_t* trow = a.table + a.si()[2 * sq + 1] * a.table_stride;
-    const float* qrow = a.q_rot + ((int64_t)sq * a.hq + (int64_t)kvh * G) * kM3D;
+    const int64_t qrow0 = ((int64_t)sq * a.hq + (int64_t)kvh * G) * kM3D;
+    // q' of head h at dim d: the rotated f32 rows, or the caller's rotated
+    // rows scaled here
+    auto qv = [&](int h, int d) {
+      return a.q_in ? load_any(a.q_in, a.q_dtype, qrow0 + h * kM3D + d) * a.qscale : a.q_rot[qrow0 + h * kM3D + d];
+    };
     // query fragments in slot order: k-step ks, lane (n, tt) holds column n
     // = (head n / 2, f16 part n % 2) at the pairs of slots tt and tt + 4
     for (int u = threadIdx.x; u < kM3KSteps * 32; u += blockDim.x) {
@@ -2043,7 +2048,7 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int pos = 2 * (2 * j + h) + e, d = 21 * w + pos;
-          if (head < G && pos < 21 && d < kM3D) x[e] = qrow[head * kM3D + d];
+          if (head < G && pos < 21 && d < kM3D) x[e] = qv(head, d);
         }
         const __half2 hv = __floats2half2_rn(x[0], x[1]);
         const float2 f = __half22float2(hv);
@@ -2055,7 +2060,7 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
     if (warp < G) {  // ||q'||^2 per head, for the precise-tile test
       float s2 = 0.f;
       for (int d = lane; d < kM3D; d += 32) {
-        const float v = qrow[warp * kM3D + d];
+        const float v = qv(warp, d);
         s2 = fmaf(v, v, s2);
       }
 #pragma unroll
@@ -2510,6 +2515,12 @@ static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
   d.G = a.hq / a.hkv;
   d.q_rot = a.q_rot;
   d.q_h = a.q_h;
+  if (a.q_raw) {
+    d.q_in = a.q_raw;
+    d.q_dtype = a.q_raw_dtype;
+    d.q_rotated = 1;
+    d.qscale = a.q_raw_scale;
+  }
   d.kcent = a.kcent;
   d.vcent = a.vcent;
   d.kalpha = a.kalpha;

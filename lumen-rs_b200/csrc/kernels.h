@@ -115,6 +115,12 @@ struct DecodeArgs {
   int32_t n_seqs = 0, hkv = 0, hq = 0, dim = 0;
   int32_t kbits = 4, vbits = 4;
   const float* q_rot = nullptr;   // [n_seqs][hq][dim] f32, rotated and scaled by scale*log2(e)
+  // the tensor-core 3/2-bit kernel can read already-rotated raw queries
+  // instead (q_rot then unused): q_raw [n_seqs][hq][dim] of q_raw_dtype, times
+  // q_raw_scale
+  const void* q_raw = nullptr;
+  int32_t q_raw_dtype = 0;
+  float q_raw_scale = 1.0f;
   const __half* q_h = nullptr;    // same in f16
   const float* kcent = nullptr;   // [2^kbits]
   const float* vcent = nullptr;   // [2^vbits]

@@ -16,20 +16,22 @@ import helpers
 pytestmark = pytest.mark.gpu
 
 
-def _pair(lc, orc, dim, hkv, lens, seed):
-    t = orc.Tables.generate(dim, 4, 64, 42)
-    ck = lc.TurboQuantCompressor.from_tables(t.R, t.bounds, t.cents, t.proj)
+def _pair(lc, orc, dim, hkv, lens, seed, kbits=4, vbits=4):
+    tk = orc.Tables.generate(dim, kbits, 64, 42)
+    tv = orc.Tables.generate(dim, vbits, 64, 42)
+    ck = lc.TurboQuantCompressor.from_tables(tk.R, tk.bounds, tk.cents, tk.proj)
+    cv = lc.TurboQuantCompressor.from_tables(tv.R, tv.bounds, tv.cents, tv.proj)
     pages = (max(lens) + 8 + 255) // 256 + 1
-    caches = [lc.CudaKvCache(1, hkv, dim, ck, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
+    caches = [lc.CudaKvCache(1, hkv, dim, ck, cv, max_seqs=len(lens), max_pages=len(lens) * pages + 8,
                              max_pages_per_seq=pages) for _ in range(2)]
-    comp = orc.Compressor(t)
+    comp, vcomp = orc.Compressor(tk), orc.Compressor(tv)
     refs, kvs = [], []
     for b, n in enumerate(lens):
         K = helpers.kv(orc, seed + 2 * b, 1, hkv, n + 1, dim)
         V = helpers.kv(orc, seed + 2 * b + 1, 1, hkv, n + 1, dim)
         for c in caches:
             c.append(0, [b], np.ascontiguousarray(K[:, :, :n]), np.ascontiguousarray(V[:, :, :n]))
-        ref = orc.SimpleCache(comp, comp, 1, hkv, dim)
+        ref = orc.SimpleCache(comp, vcomp, 1, hkv, dim)
         for h in range(hkv):
             ref.store(0, h, K[0, h], V[0, h], n + 1)
         refs.append(ref)
@@ -78,5 +80,41 @@ def test_decode_step_host_inputs_and_flags(lc, orc, gpu):
     want = a.decode_attn(0, [0], q, 32, 1.0)
     got = b.decode_step(0, [0], k1, v1, q, 32, 1.0)
     np.testing.assert_allclose(got, want, rtol=0, atol=2e-5)
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("hq,std", [(16, 256 ** -0.5), (16, 1.0), (8, 1.0), (32, 256 ** -0.5)])
+def test_decode_step_config2_geometry(lc, orc, gpu, hq, std):
+    """Config 2's geometry (head_dim 256, 3-bit K / 2-bit V, 8 KV heads, bf16
+    queries): the append launch rotates the queries with R^T streamed through
+    shared memory and the tensor-core kernel reads them as given (no rotation
+    launch)."""
+    import torch
+
+    hkv, dim, scale = 8, 256, 256 ** -0.5
+    lens = [2100, 300, 40]
+    (a, b), refs, k1, v1 = _pair(lc, orc, dim, hkv, lens, 170 + hq, kbits=3, vbits=2)
+    q = helpers.queries(orc, 171, len(lens), hq, dim, std=std)
+    ids = list(range(len(lens)))
+    qd = torch.from_numpy(q).cuda().to(torch.bfloat16)
+    kd, vd = torch.from_numpy(k1).cuda(), torch.from_numpy(v1).cuda()
+    a.append(0, ids, kd, vd)
+    want = torch.empty((len(lens), hq, dim), device="cuda")
+    a.decode_attn(0, ids, qd, hq, scale, out=want)
+    got = torch.empty((len(lens), hq, dim), device="cuda")
+    b.decode_step(0, ids, kd, vd, qd, hq, scale, out=got)
+    torch.cuda.synchronize()
+    want, got = want.cpu().numpy(), got.cpu().numpy()
+    for s in ids:
+        fa, fb = a.fetch(s, 0), b.fetch(s, 0)
+        np.testing.assert_array_equal(fa["k_words"], fb["k_words"])
+        np.testing.assert_array_equal(fa["v_words"], fb["v_words"])
+    np.testing.assert_allclose(got, want, rtol=0, atol=2e-5 * max(1.0, float(np.abs(want).max())))
+    G = hq // hkv
+    qb = qd.float().cpu().numpy()
+    ref = np.stack([np.stack([refs[s].attend(0, h // G, qb[s, h], scale) for h in range(hq)]) for s in ids])
+    ok, msg = helpers.attn_close(got, ref)
+    assert ok, msg
     a.close()
     b.close()
