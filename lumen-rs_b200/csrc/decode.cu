@@ -1945,9 +1945,22 @@ __device__ __forceinline__ uint32_t m3_kaddr(uint64_t x, int s, uint32_t base) {
   const uint32_t f = s >= 7 ? (uint32_t)(x >> (s - 7)) : (uint32_t)x << (7 - s);
   return (f & (63u << 7)) | base;
 }
-// J k-steps of one word group: x0 / x1 the lane's word of tokens g / g + 8
+// an 8-byte shared load by the lanes with live set (the others get zeros
+// and take no bank: a half-live warp's load is one wavefront)
+__device__ __forceinline__ uint2 lds64_if(uint32_t addr, bool live) {
+  uint2 v;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n mov.b32 %0, 0;\n mov.b32 %1, 0;\n"
+      " @p ld.shared.v2.u32 {%0, %1}, [%2];\n}"
+      : "=r"(v.x), "=r"(v.y)
+      : "r"(addr), "r"((int)live));
+  return v;
+}
+// J k-steps of one word group: x0 / x1 the lane's word of its tokens of MMA
+// rows g / g + 8; qlive: the lane's query column holds a head
 template <int J>
-__device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab, uint32_t qf, float (&c)[4]) {
+__device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab, uint32_t qf, bool qlive,
+                                         float (&c)[4]) {
 #pragma unroll
   for (int j = 0; j < J; ++j) {
     const uint32_t a0 = lds32(m3_kaddr(x0, 12 * j, tab)), a1 = lds32(m3_kaddr(x1, 12 * j, tab));
@@ -1956,17 +1969,19 @@ __device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab,
       a2 = lds32(m3_kaddr(x0, 12 * j + 6, tab));
       a3 = lds32(m3_kaddr(x1, 12 * j + 6, tab));
     }
-    const uint2 b = lds64(qf + j * 256);
+    const uint2 b = lds64_if(qf + j * 256, qlive);
     mma16816(c, a0, a1, a2, a3, b.x, b.y);
   }
 }
-// S^T += Ktab(K) Q^T over the 19 k-steps; kb: the stage's K words
-__device__ __forceinline__ void m3_qk(const uint64_t* kb, int g, int t, uint32_t tab, uint32_t qf, float (&c)[4]) {
+// S^T += Ktab(K) Q^T over the 19 k-steps; kb: the stage's K words, ra / rb
+// the tile rows (tokens) of the lane's MMA rows g / g + 8
+__device__ __forceinline__ void m3_qk(const uint64_t* kb, int ra, int rb, int t, uint32_t tab, uint32_t qf,
+                                      bool qlive, float (&c)[4]) {
 #pragma unroll 1
   for (int v = 0; v < 3; ++v)
-    m3_group<6>(kb[g * kM3KWords + 4 * v + t], kb[(g + 8) * kM3KWords + 4 * v + t], tab, qf + v * 6 * 256, c);
+    m3_group<6>(kb[ra * kM3KWords + 4 * v + t], kb[rb * kM3KWords + 4 * v + t], tab, qf + v * 6 * 256, qlive, c);
   // word 12 + t: lanes t > 0 read the next row's words (zero query slots)
-  m3_group<1>(kb[g * kM3KWords + 12 + t], kb[(g + 8) * kM3KWords + 12 + t], tab, qf + 18 * 256, c);
+  m3_group<1>(kb[ra * kM3KWords + 12 + t], kb[rb * kM3KWords + 12 + t], tab, qf + 18 * 256, qlive, c);
 }
 
 template <int G>
@@ -2111,6 +2126,15 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       }
       ++ring;
     };
+    // MMA row g (g + 8) of S^T is tile row ra (rb): rows 4 (g & 3) + (g >> 2)
+    // and 2 more, so that the four rows a half-warp reads K words of (104-byte
+    // rows) start 32 bytes apart mod 128 and take distinct banks. PV's token
+    // slots follow: lane t's k-slots 2t, 2t + 1 hold the pair a P^T writer
+    // lane gw0 = t + 4 (t & 1) holds (rows 4t + (t & 1) and 2 more), slots
+    // 2t + 8, 2t + 9 the pair of lane gw0 ^ 4.
+    const int ra = 4 * (g & 3) + (g >> 2), rb = ra + 2;
+    const int gw0 = t + 4 * (t & 1);
+    const bool qlive = g < 2 * G;
     if (warp < ctiles) issue(warp);
     for (int tl = warp; tl < ctiles; tl += kM3Warps) {
       if (tl + kM3Warps < ctiles) issue(tl + kM3Warps);
@@ -2124,17 +2148,17 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       const float* ks = reinterpret_cast<const float*>(st + kM3TT * (kM3KRow + kM3VRow));
       const float* vs = ks + kM3TT;
       const int tok = tl * kM3TT;
-      const bool ok0 = tok + g < chunk_tok, ok1 = tok + g + 8 < chunk_tok;
-      // ---- S^T: lane (g, t) gets head t at tokens g and g + 8 ----
+      const bool ok0 = tok + ra < chunk_tok, ok1 = tok + rb < chunk_tok;
+      // ---- S^T: lane (g, t) gets head t at tile rows ra and rb ----
       float c[4] = {0.f, 0.f, 0.f, 0.f};
-      m3_qk(kb, g, t, ktab_s, qf_s, c);
+      m3_qk(kb, ra, rb, t, ktab_s, qf_s, qlive, c);
       float y0 = c[0] + c[1], y1 = c[2] + c[3];
-      const float k0 = ks[g], k1 = ks[g + 8];
+      const float k0 = ks[ra], k1 = ks[rb];
       if (__any_sync(0xffffffffu, t < G && fmaxf(k0, k1) > lthr)) {
         const float zm = fmaxf(ok0 ? y0 * k0 : -INFINITY, ok1 ? y1 * k1 : -INFINITY);
         if (__any_sync(0xffffffffu, t < G && fmaxf(k0, k1) > lthr && zm > m - kLoTheta)) {
           float cl[4] = {0.f, 0.f, 0.f, 0.f};
-          m3_qk(kb, g, t, klo_s, qf_s, cl);
+          m3_qk(kb, ra, rb, t, klo_s, qf_s, qlive, cl);
           y0 = fmaf(cl[0] + cl[1], kLoUnscale, y0);
           y1 = fmaf(cl[2] + cl[3], kLoUnscale, y1);
         }
@@ -2160,7 +2184,8 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       }
       const float pp0 = ex2(s0_ - m), pp1 = ex2(s1_ - m);
       l += pp0 + pp1;
-      // V words g and g + 8 of tokens (t, t + 8) and (t + 4, t + 12), read
+      // V words g and g + 8 of the token pairs (4t + (tp ^ (t & 1)), + 2)
+      // for k-slot pair tp (the pairs of P^T lanes gw0, gw0 ^ 4), read
       // before the P^T exchange reuses the stage's K area. Index word
       // xv[tp][h][par], byte k: the token pair's nibble (a | b << 2) at dim
       // 4k + 2h + par of word g, then the same of word g + 8, so that one
@@ -2171,7 +2196,8 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
         uint32_t ev[2], od[2];  // word g, word g + 8
 #pragma unroll
         for (int wv = 0; wv < 2; ++wv) {
-          const uint32_t va = vb[(t + 4 * tp) * 16 + g + 8 * wv], vbb = vb[(t + 8 + 4 * tp) * 16 + g + 8 * wv];
+          const int rv = 4 * t + (tp ^ (t & 1));
+          const uint32_t va = vb[rv * 16 + g + 8 * wv], vbb = vb[(rv + 2) * 16 + g + 8 * wv];
           ev[wv] = (va & 0x33333333u) | ((vbb & 0x33333333u) << 2);
           od[wv] = ((va >> 2) & 0x33333333u) | (vbb & 0xCCCCCCCCu);
         }
@@ -2180,12 +2206,12 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
         xv[tp][0][1] = (od[0] & 0x0F0F0F0Fu) | ((od[1] & 0x0F0F0F0Fu) << 4);
         xv[tp][1][1] = ((od[0] >> 4) & 0x0F0F0F0Fu) | (od[1] & 0xF0F0F0F0u);
       }
-      // P^T fragments: lane (g, t) holds p' of head t at tokens g, g + 8 and
-      // reads column g = (head g / 2, part g & 1) at token pairs t, t + 4
-      // (the layout of p_exchange, one 16-token half)
+      // P^T fragments: lane (g, t) holds p' of head t at tile rows ra, rb and
+      // reads column g = (head g / 2, part g & 1) at the pairs of lanes gw0
+      // and gw0 ^ 4 (the layout of p_exchange, one 16-token half)
       uint32_t pb0, pb1;
       {
-        const float pa = ok0 ? pp0 * vs[g] : 0.f, pz = ok1 ? pp1 * vs[g + 8] : 0.f;
+        const float pa = ok0 ? pp0 * vs[ra] : 0.f, pz = ok1 ? pp1 * vs[rb] : 0.f;
         uint32_t* ps = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(st));
         const __half2 h0 = __floats2half2_rn(pa, pz);
         const float2 f0 = __half22float2(h0);
@@ -2196,8 +2222,8 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
         __syncwarp();
         const int head = g >> 1, part = g & 1;
         const int base = part * 32 + head * 8, sw = part << 2;
-        pb0 = head < G ? ps[base + (t ^ sw)] : 0u;
-        pb1 = head < G ? ps[base + ((t + 4) ^ sw)] : 0u;
+        pb0 = head < G ? ps[base + (gw0 ^ sw)] : 0u;
+        pb1 = head < G ? ps[base + ((gw0 ^ 4) ^ sw)] : 0u;
       }
       // ---- O^T += V^T P^T: m-tile 4k + 2h + par ----
 #pragma unroll
