@@ -1945,22 +1945,10 @@ __device__ __forceinline__ uint32_t m3_kaddr(uint64_t x, int s, uint32_t base) {
   const uint32_t f = s >= 7 ? (uint32_t)(x >> (s - 7)) : (uint32_t)x << (7 - s);
   return (f & (63u << 7)) | base;
 }
-// an 8-byte shared load by the lanes with live set (the others get zeros
-// and take no bank: a half-live warp's load is one wavefront)
-__device__ __forceinline__ uint2 lds64_if(uint32_t addr, bool live) {
-  uint2 v;
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n mov.b32 %0, 0;\n mov.b32 %1, 0;\n"
-      " @p ld.shared.v2.u32 {%0, %1}, [%2];\n}"
-      : "=r"(v.x), "=r"(v.y)
-      : "r"(addr), "r"((int)live));
-  return v;
-}
 // J k-steps of one word group: x0 / x1 the lane's word of its tokens of MMA
-// rows g / g + 8; qlive: the lane's query column holds a head
+// rows g / g + 8
 template <int J>
-__device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab, uint32_t qf, bool qlive,
-                                         float (&c)[4]) {
+__device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab, uint32_t qf, float (&c)[4]) {
 #pragma unroll
   for (int j = 0; j < J; ++j) {
     const uint32_t a0 = lds32(m3_kaddr(x0, 12 * j, tab)), a1 = lds32(m3_kaddr(x1, 12 * j, tab));
@@ -1969,19 +1957,19 @@ __device__ __forceinline__ void m3_group(uint64_t x0, uint64_t x1, uint32_t tab,
       a2 = lds32(m3_kaddr(x0, 12 * j + 6, tab));
       a3 = lds32(m3_kaddr(x1, 12 * j + 6, tab));
     }
-    const uint2 b = lds64_if(qf + j * 256, qlive);
+    const uint2 b = lds64(qf + j * 256);
     mma16816(c, a0, a1, a2, a3, b.x, b.y);
   }
 }
 // S^T += Ktab(K) Q^T over the 19 k-steps; kb: the stage's K words, ra / rb
 // the tile rows (tokens) of the lane's MMA rows g / g + 8
 __device__ __forceinline__ void m3_qk(const uint64_t* kb, int ra, int rb, int t, uint32_t tab, uint32_t qf,
-                                      bool qlive, float (&c)[4]) {
+                                      float (&c)[4]) {
 #pragma unroll 1
   for (int v = 0; v < 3; ++v)
-    m3_group<6>(kb[ra * kM3KWords + 4 * v + t], kb[rb * kM3KWords + 4 * v + t], tab, qf + v * 6 * 256, qlive, c);
+    m3_group<6>(kb[ra * kM3KWords + 4 * v + t], kb[rb * kM3KWords + 4 * v + t], tab, qf + v * 6 * 256, c);
   // word 12 + t: lanes t > 0 read the next row's words (zero query slots)
-  m3_group<1>(kb[ra * kM3KWords + 12 + t], kb[rb * kM3KWords + 12 + t], tab, qf + 18 * 256, qlive, c);
+  m3_group<1>(kb[ra * kM3KWords + 12 + t], kb[rb * kM3KWords + 12 + t], tab, qf + 18 * 256, c);
 }
 
 template <int G>
@@ -2021,7 +2009,10 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(qunit);
   float* qnorm = reinterpret_cast<float*>(qunit + kM3OffNorm);
   const uint32_t bar_s = (uint32_t)__cvta_generic_to_shared(qunit) + kM3OffBar + warp * 16;  // stage s: + 8 s
-  const uint32_t qf_s = (uint32_t)__cvta_generic_to_shared(qunit) + lane * 8;
+  // lanes whose query column holds no head (g >= 2G) read a live lane's
+  // fragment: the same addresses, so the load takes no extra bank wavefront
+  // (their score columns are not used)
+  const uint32_t qf_s = (uint32_t)__cvta_generic_to_shared(qunit) + (((g < 2 * G ? g : g % (2 * G)) << 2) | t) * 8;
   uint8_t* wunit = unit(warp);
   const uint32_t st_s = (uint32_t)__cvta_generic_to_shared(wunit);
   if (lane == 0) {
@@ -2049,6 +2040,50 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
     auto qv = [&](int h, int d) {
       return a.q_in ? load_any(a.q_in, a.q_dtype, qrow0 + h * kM3D + d) * a.qscale : a.q_rot[qrow0 + h * kM3D + d];
     };
+    const int p0 = chunk * a.pages_per_chunk;
+    const int64_t ctok = n_valid - (int64_t)p0 * kPageTokens;
+    const int64_t cmax = (int64_t)a.pages_per_chunk * kPageTokens;
+    const int chunk_tok = (int)(ctok <= 0 ? 0 : (ctok < cmax ? ctok : cmax));
+    constexpr int tpp = kPageTokens / kM3TT;
+    const int ctiles = (chunk_tok + kM3TT - 1) / kM3TT;
+    const uint64_t my_page = lane < a.pages_per_chunk && (int64_t)(p0 + lane) * kPageTokens < n_valid ? trow[p0 + lane] : 0ull;
+    auto my_page_of = [&](int i) { return __shfl_sync(0xffffffffu, my_page, i); };
+    // a tile: K words, V words, sigma_K, sigma_V of 16 consecutive rows, four
+    // contiguous runs of the page, copied by lane 0 into stage ring & 1
+    auto issue = [&](int tl) {
+      fence_proxy_async();  // the stage's earlier reads and P^T writes come first
+      __syncwarp();
+      const uint8_t* page = reinterpret_cast<const uint8_t*>(my_page_of(tl / tpp));
+      int rt = tl % tpp;  // 16-token tile within the page
+      if (a.tile_map) {
+        // page-sparse: logical 16-token tile lt of the (sequence, kv head) is
+        // half (lt & 1) of its mapped 32-token tile
+        const int64_t lt = (int64_t)chunk * a.pages_per_chunk * tpp + tl;
+        const int64_t p16 = 2 * (int64_t)a.tile_map[((int64_t)sq * a.hkv + kvh) * a.map_stride + (lt >> 1)] + (lt & 1);
+        page = reinterpret_cast<const uint8_t*>(trow[p16 / tpp]);
+        rt = (int)(p16 % tpp);
+      }
+      if (lane == 0) {
+        const int64_t r0 = (int64_t)kvh * kPageTokens + rt * kM3TT;
+        const uint32_t dst = st_s + (ring & 1) * kM3Stage, bar = bar_s + (ring & 1) * 8;
+        mbar_expect_tx(bar, kM3Stage);
+        bulk_g2s(dst, page + a.off_kw + r0 * kM3KRow, kM3TT * kM3KRow, bar);
+        bulk_g2s(dst + kM3TT * kM3KRow, page + a.off_vw + r0 * kM3VRow, kM3TT * kM3VRow, bar);
+        bulk_g2s(dst + kM3TT * (kM3KRow + kM3VRow), page + a.off_ks + r0 * 4, kM3TT * 4, bar);
+        bulk_g2s(dst + kM3TT * (kM3KRow + kM3VRow + 4), page + a.off_vs + r0 * 4, kM3TT * 4, bar);
+      }
+      ++ring;
+    };
+    // MMA row g (g + 8) of S^T is tile row ra (rb): rows 4 (g & 3) + (g >> 2)
+    // and 2 more, so that the four rows a half-warp reads K words of (104-byte
+    // rows) start 32 bytes apart mod 128 and take distinct banks. PV's token
+    // slots follow: lane t's k-slots 2t, 2t + 1 hold the pair a P^T writer
+    // lane gw0 = t + 4 (t & 1) holds (rows 4t + (t & 1) and 2 more), slots
+    // 2t + 8, 2t + 9 the pair of lane gw0 ^ 4.
+    const int ra = 4 * (g & 3) + (g >> 2), rb = ra + 2;
+    const int gw0 = t + 4 * (t & 1);
+    // the first tile's copy runs while the block builds the query fragments
+    if (warp < ctiles) issue(warp);
     // query fragments in slot order: k-step ks, lane (n, tt) holds column n
     // = (head n / 2, f16 part n % 2) at the pairs of slots tt and tt + 4
     for (int u = threadIdx.x; u < kM3KSteps * 32; u += blockDim.x) {
@@ -2092,50 +2127,6 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
     float oacc[16][4];
 #pragma unroll
     for (int i = 0; i < 16; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
-    const int p0 = chunk * a.pages_per_chunk;
-    const int64_t ctok = n_valid - (int64_t)p0 * kPageTokens;
-    const int64_t cmax = (int64_t)a.pages_per_chunk * kPageTokens;
-    const int chunk_tok = (int)(ctok <= 0 ? 0 : (ctok < cmax ? ctok : cmax));
-    constexpr int tpp = kPageTokens / kM3TT;
-    const int ctiles = (chunk_tok + kM3TT - 1) / kM3TT;
-    const uint64_t my_page = lane < a.pages_per_chunk && (int64_t)(p0 + lane) * kPageTokens < n_valid ? trow[p0 + lane] : 0ull;
-    auto my_page_of = [&](int i) { return __shfl_sync(0xffffffffu, my_page, i); };
-    // a tile: K words, V words, sigma_K, sigma_V of 16 consecutive rows, four
-    // contiguous runs of the page, copied by lane 0 into stage ring & 1
-    auto issue = [&](int tl) {
-      fence_proxy_async();  // the stage's earlier reads and P^T writes come first
-      __syncwarp();
-      const uint8_t* page = reinterpret_cast<const uint8_t*>(my_page_of(tl / tpp));
-      int rt = tl % tpp;  // 16-token tile within the page
-      if (a.tile_map) {
-        // page-sparse: logical 16-token tile lt of the (sequence, kv head) is
-        // half (lt & 1) of its mapped 32-token tile
-        const int64_t lt = (int64_t)chunk * a.pages_per_chunk * tpp + tl;
-        const int64_t p16 = 2 * (int64_t)a.tile_map[((int64_t)sq * a.hkv + kvh) * a.map_stride + (lt >> 1)] + (lt & 1);
-        page = reinterpret_cast<const uint8_t*>(trow[p16 / tpp]);
-        rt = (int)(p16 % tpp);
-      }
-      if (lane == 0) {
-        const int64_t r0 = (int64_t)kvh * kPageTokens + rt * kM3TT;
-        const uint32_t dst = st_s + (ring & 1) * kM3Stage, bar = bar_s + (ring & 1) * 8;
-        mbar_expect_tx(bar, kM3Stage);
-        bulk_g2s(dst, page + a.off_kw + r0 * kM3KRow, kM3TT * kM3KRow, bar);
-        bulk_g2s(dst + kM3TT * kM3KRow, page + a.off_vw + r0 * kM3VRow, kM3TT * kM3VRow, bar);
-        bulk_g2s(dst + kM3TT * (kM3KRow + kM3VRow), page + a.off_ks + r0 * 4, kM3TT * 4, bar);
-        bulk_g2s(dst + kM3TT * (kM3KRow + kM3VRow + 4), page + a.off_vs + r0 * 4, kM3TT * 4, bar);
-      }
-      ++ring;
-    };
-    // MMA row g (g + 8) of S^T is tile row ra (rb): rows 4 (g & 3) + (g >> 2)
-    // and 2 more, so that the four rows a half-warp reads K words of (104-byte
-    // rows) start 32 bytes apart mod 128 and take distinct banks. PV's token
-    // slots follow: lane t's k-slots 2t, 2t + 1 hold the pair a P^T writer
-    // lane gw0 = t + 4 (t & 1) holds (rows 4t + (t & 1) and 2 more), slots
-    // 2t + 8, 2t + 9 the pair of lane gw0 ^ 4.
-    const int ra = 4 * (g & 3) + (g >> 2), rb = ra + 2;
-    const int gw0 = t + 4 * (t & 1);
-    const bool qlive = g < 2 * G;
-    if (warp < ctiles) issue(warp);
     for (int tl = warp; tl < ctiles; tl += kM3Warps) {
       if (tl + kM3Warps < ctiles) issue(tl + kM3Warps);
       const uint32_t stg = cons & 1;
@@ -2151,14 +2142,14 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       const bool ok0 = tok + ra < chunk_tok, ok1 = tok + rb < chunk_tok;
       // ---- S^T: lane (g, t) gets head t at tile rows ra and rb ----
       float c[4] = {0.f, 0.f, 0.f, 0.f};
-      m3_qk(kb, ra, rb, t, ktab_s, qf_s, qlive, c);
+      m3_qk(kb, ra, rb, t, ktab_s, qf_s, c);
       float y0 = c[0] + c[1], y1 = c[2] + c[3];
       const float k0 = ks[ra], k1 = ks[rb];
       if (__any_sync(0xffffffffu, t < G && fmaxf(k0, k1) > lthr)) {
         const float zm = fmaxf(ok0 ? y0 * k0 : -INFINITY, ok1 ? y1 * k1 : -INFINITY);
         if (__any_sync(0xffffffffu, t < G && fmaxf(k0, k1) > lthr && zm > m - kLoTheta)) {
           float cl[4] = {0.f, 0.f, 0.f, 0.f};
-          m3_qk(kb, ra, rb, t, klo_s, qf_s, qlive, cl);
+          m3_qk(kb, ra, rb, t, klo_s, qf_s, cl);
           y0 = fmaf(cl[0] + cl[1], kLoUnscale, y0);
           y1 = fmaf(cl[2] + cl[3], kLoUnscale, y1);
         }
@@ -2462,7 +2453,7 @@ static void plan_core(const int64_t* lens, int n, int hkv, int hq, int dim, int 
     // 4 pages per chunk (8 on the tensor-core path, whose one block per SM
     // has 12 warps), or fewer when that leaves too few (sequence, kv head,
     // chunk) items to fill the GPU (short contexts, sliding windows)
-    int ppc = p.mma ? 8 : 4;
+    int ppc = p.mma ? 16 : 4;
     const int64_t want = (p.mma ? 4LL : 8LL) * num_sms();
     while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < want) ppc >>= 1;
     p.pages_per_chunk = ppc;
@@ -2494,7 +2485,7 @@ void launch_rotate_q(const void* q, int32_t q_dtype, int32_t n_rows, int32_t dim
   LC_REQUIRE(dim % 64 == 0, LC_ERR_INVALID, "decode: head_dim must be 64, 128, 256 or 512");
   const dim3 grid((unsigned)((n_rows + kRotRows - 1) / kRotRows), (unsigned)(dim / kRotDims));
   const size_t smem = ((size_t)kRotRows * dim + (size_t)kRotSplit * kRotRows * kRotDims) * sizeof(float);
-launch_pdl(k_rotate_q, grid, dim3(kRotDims * kRotSplit), smem, s, q, q_dtype, n_rows, dim, RT,
+  launch_pdl(k_rotate_q, grid, dim3(kRotDims * kRotSplit), smem, s, q, q_dtype, n_rows, dim, RT,
              q_is_rotated ? 1 : 0, qscale, q_rot, q_h);
   LC_CUDA(cudaGetLastError());
 }
