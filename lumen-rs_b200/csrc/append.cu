@@ -730,19 +730,69 @@ void launch_warp_append(const AppendDev& d, bool stage2, int M, int64_t n_vec, c
 // R l .. R l + R - 1 of all of them (R = dim / 32). Per step j of the
 // rotation's ascending sum a lane reads its R coefficients R^T[j][R l ..] as
 // one vector load and each vector's x[j] as a broadcast, so a lane keeps
-// kTileVecs x R independent chains and the loads are ~5 % of the FP32 work
+// kTileVecs x R independent chains and the loads are ~5 % of the f32 work
 // (the batched kernel above reads one coefficient per output and chain).
-// Every f32 operation and sum order is the strict one: the rotation sums j
-// ascending from -0, the squares are formed in parallel and added in order
-// i ascending by one lane per vector (rows padded to d + 4 floats, so the
-// lanes' 16-byte reads fall in distinct banks), the codes are the threshold count, so
-// codes and sigma are bit-identical to k_append_strict.
+// The sums run as paired f32 adds (add.rn.f32x2 on sm_100: two IEEE
+// round-to-nearest additions per lane and issue slot) over output pairs
+// (2m, 2m + 1); the products stay scalar round-to-nearest multiplies, since
+// a paired multiply feeding a paired add is contracted into a fused
+// multiply-add by the code generator even with explicit rounding (measured:
+// most sums then differ in the last bit). That is 3 issue slots per 2 terms
+// instead of 4. Every f32 operation and sum order is the strict one: the rotation sums j ascending from -0, the squares are formed in
+// parallel and added in order i ascending by one lane per vector (rows
+// padded to d + 4 floats, so the lanes' 16-byte reads fall in distinct
+// banks), the codes are the threshold count, so codes and sigma are
+// bit-identical to k_append_strict.
 constexpr int kTileWarps = 32, kTileVecs = 4;
 
+// per warp: x [NV][D] f32, squares [NV][D + 4] f32, codes [NV][D] u8
 template <int R>
 __host__ __device__ constexpr size_t tile_warp_bytes() {
   constexpr int D = 32 * R;
   return (size_t)kTileVecs * D * 4 + (size_t)kTileVecs * (D + 4) * 4 + (size_t)kTileVecs * D;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+
+// the code of yn: the count of ascending thresholds t with !(yn < t), by a
+// binary search of log2(L) steps
+template <int L>
+__device__ __forceinline__ int tile_code(float yn, const float* thr) {
+  int code = 0;
+#pragma unroll
+  for (int step = L >> 1; step > 0; step >>= 1)
+    if (!(yn < thr[code + step - 1])) code += step;
+  return code;
+}
+
+template <int R, int L>
+__device__ __forceinline__ void tile_codes(const float (&acc)[kTileVecs][R], const float* sc, const float* inv,
+                                           const float* thr, int n_levels, uint8_t* codes, int lane) {
+#pragma unroll
+  for (int v = 0; v < kTileVecs; ++v) {
+    const float scv = __shfl_sync(0xffffffffu, *sc, v), invv = __shfl_sync(0xffffffffu, *inv, v);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      int code = 0;
+      if (!(scv < 1e-10f)) {
+        const float yn = __fmul_rn(acc[v][r], invv);
+        if constexpr (L > 0) {
+          code = tile_code<L>(yn, thr);
+        } else {
+          for (int step = n_levels >> 1; step > 0; step >>= 1)
+            if (!(yn < thr[code + step - 1])) code += step;
+        }
+      }
+      codes[v * (32 * R) + R * lane + r] = (uint8_t)code;
+    }
+  }
 }
 
 template <int R>
@@ -756,8 +806,8 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
   float* rt = reinterpret_cast<float*>(smem);  // R^T [D][D]
   float* sthr = rt + D * D;                    // [256]
   uint8_t* wb = smem + (size_t)D * D * 4 + 1024 + (size_t)warp * tile_warp_bytes<R>();
-  float* x = reinterpret_cast<float*>(wb);  // [NV][D]
-  float* sq = x + NV * D;                   // [NV][D + 4] squares (rows padded: lane v reads row v)
+  float* x = reinterpret_cast<float*>(wb);                  // [NV][D]
+  float* sq = x + NV * D;                                   // [NV][D + 4] squares (rows padded: lane v reads row v)
   uint8_t* codes = reinterpret_cast<uint8_t*>(sq + NV * (D + 4));  // [NV][D]
   stage16(rt, c.RT, D * D / 4);
   asm volatile("cp.async.commit_group;\n" ::: "memory");
@@ -769,30 +819,31 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
   const void* src = a.src[side];
   const int cpw = 64 / c.bits, W = c.words;
   const int rw = a.role_words[side], rsg = a.role_sigma[side];
+  const bool rope = side == 0 && a.rope_cs;
   for (int64_t v0 = ((int64_t)blockIdx.x * kTileWarps + warp) * NV; v0 < n_vec;
        v0 += (int64_t)gridDim.x * kTileWarps * NV) {
     const int nv = (int)(n_vec - v0 < NV ? n_vec - v0 : NV);
     // ---- load (input layout [n_seqs][h_in][n_tok][D]): lane l's R
     // consecutive elements of each vector as one vector load ----
+    float e[NV][R];
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      float e[R];
       const int64_t base = (v0 + v) * D + R * lane;
       if (v >= nv) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) e[r] = 0.0f;
+        for (int r = 0; r < R; ++r) e[v][r] = 0.0f;
       } else if (a.dtype == LC_F32) {
         const float* q = static_cast<const float*>(src) + base;
         if constexpr (R == 4) {
           const float4 t4 = *reinterpret_cast<const float4*>(q);
-          e[0] = t4.x;
-          e[1] = t4.y;
-          e[2] = t4.z;
-          e[3] = t4.w;
+          e[v][0] = t4.x;
+          e[v][1] = t4.y;
+          e[v][2] = t4.z;
+          e[v][3] = t4.w;
         } else {
           const float2 t2 = *reinterpret_cast<const float2*>(q);
-          e[0] = t2.x;
-          e[1] = t2.y;
+          e[v][0] = t2.x;
+          e[v][1] = t2.y;
         }
       } else {
         const unsigned short* q = static_cast<const unsigned short*>(src) + base;
@@ -807,16 +858,19 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
 #pragma unroll
         for (int k = 0; k < R / 2; ++k) {
           const uint32_t lo = h[k] & 0xFFFFu, hi = h[k] >> 16;
-          e[2 * k] = a.dtype == LC_BF16 ? __uint_as_float(lo << 16) : __half2float(__ushort_as_half((unsigned short)lo));
-          e[2 * k + 1] =
+          e[v][2 * k] =
+              a.dtype == LC_BF16 ? __uint_as_float(lo << 16) : __half2float(__ushort_as_half((unsigned short)lo));
+          e[v][2 * k + 1] =
               a.dtype == LC_BF16 ? __uint_as_float(hi << 16) : __half2float(__ushort_as_half((unsigned short)hi));
         }
       }
-#pragma unroll
-      for (int r = 0; r < R; ++r) x[v * D + R * lane + r] = e[r];
     }
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int r = 0; r < R; ++r) x[v * D + R * lane + r] = e[v][r];
     __syncwarp();
-    if (side == 0 && a.rope_cs) {
+    if (rope) {  // RoPE on K before quantisation (pairs cross lanes)
       for (int v = 0; v < nv; ++v) {
         const int64_t vi = v0 + v;
         const int64_t slot = (vi / ((int64_t)a.h_in * a.n_tok)) * a.n_tok + vi % a.n_tok;
@@ -824,39 +878,50 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
       }
       __syncwarp();
     }
-    // ---- rotated[i] = sum_j R[i][j] x[j], j ascending (rotation.rs:91-99) ----
-    float acc[NV][R];
+    // ---- rotated[i] = sum_j R[i][j] x[j], j ascending (rotation.rs:91-99),
+    // on output pairs (R l + 2m, R l + 2m + 1) ----
+    constexpr int RP = R / 2;
+    constexpr uint64_t kNegZero2 = 0x8000000080000000ull;
+    uint64_t acc2[NV][RP];
 #pragma unroll
     for (int v = 0; v < NV; ++v)
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[v][r] = -0.0f;
+      for (int m = 0; m < RP; ++m) acc2[v][m] = kNegZero2;
 #pragma unroll 1
     for (int j = 0; j < D; j += 4) {
-      float w[4][R];
+      uint64_t w[4][RP];  // (R^T[j + jj][R l + 2m], R^T[j + jj][R l + 2m + 1])
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
         if constexpr (R == 4) {
-          const float4 q = *reinterpret_cast<const float4*>(rt + (j + jj) * D + 4 * lane);
+          const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(rt + (j + jj) * D + 4 * lane);
           w[jj][0] = q.x;
           w[jj][1] = q.y;
-          w[jj][2] = q.z;
-          w[jj][3] = q.w;
         } else {
-          const float2 q = *reinterpret_cast<const float2*>(rt + (j + jj) * D + 2 * lane);
-          w[jj][0] = q.x;
-          w[jj][1] = q.y;
+          w[jj][0] = *reinterpret_cast<const unsigned long long*>(rt + (j + jj) * D + 2 * lane);
         }
       }
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
-        const float4 xq = *reinterpret_cast<const float4*>(x + v * D + j);
-        const float xs[4] = {xq.x, xq.y, xq.z, xq.w};
+        const float4 x4 = *reinterpret_cast<const float4*>(x + v * D + j);
+        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
 #pragma unroll
-          for (int r = 0; r < R; ++r) acc[v][r] = __fadd_rn(acc[v][r], __fmul_rn(w[jj][r], xs[jj]));
+          for (int m = 0; m < RP; ++m) {
+            const float p0 = __fmul_rn(__uint_as_float((uint32_t)w[jj][m]), xs[jj]);
+            const float p1 = __fmul_rn(__uint_as_float((uint32_t)(w[jj][m] >> 32)), xs[jj]);
+            acc2[v][m] = f2_add(acc2[v][m], f2_pack(p0, p1));
+          }
       }
     }
+    float acc[NV][R];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int m = 0; m < RP; ++m) {
+        acc[v][2 * m] = __uint_as_float((uint32_t)acc2[v][m]);
+        acc[v][2 * m + 1] = __uint_as_float((uint32_t)(acc2[v][m] >> 32));
+      }
     // ---- scale = sqrt(norm_sq / d): squares in parallel, lane v adds vector
     // v's in order (compressor.rs:70-71) ----
 #pragma unroll
@@ -881,19 +946,11 @@ __global__ void __launch_bounds__(kTileWarps * 32, 1) k_append_tile(const __grid
     }
     // ---- codes: the count of thresholds t with !(yn < t) (lloyd_max.rs:132-143),
     // by binary search over the ascending thresholds ----
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const float scv = __shfl_sync(0xffffffffu, sc, v), invv = __shfl_sync(0xffffffffu, inv, v);
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        int code = 0;
-        if (!(scv < 1e-10f)) {
-          const float yn = __fmul_rn(acc[v][r], invv);
-          for (int step = c.n_levels >> 1; step > 0; step >>= 1)
-            if (!(yn < sthr[code + step - 1])) code += step;
-        }
-        codes[v * D + R * lane + r] = (uint8_t)code;
-      }
+    switch (c.n_levels) {
+      case 16: tile_codes<R, 16>(acc, &sc, &inv, sthr, 16, codes, lane); break;
+      case 8: tile_codes<R, 8>(acc, &sc, &inv, sthr, 8, codes, lane); break;
+      case 4: tile_codes<R, 4>(acc, &sc, &inv, sthr, 4, codes, lane); break;
+      default: tile_codes<R, 0>(acc, &sc, &inv, sthr, c.n_levels, codes, lane); break;
     }
     __syncwarp();
     // ---- pack and write (bitpack.rs:17-30): lane v finds vector v's page
