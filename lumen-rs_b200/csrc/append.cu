@@ -339,6 +339,46 @@ __device__ __forceinline__ float seq_sum(const float* v, int n, float init) {
   return s;
 }
 
+// seq_sum over n (a multiple of 4) floats on a 16-byte boundary: the same
+// ascending order, with the loads as 16-byte vectors issued ahead of the adds
+__device__ __forceinline__ float seq_sum4(const float* v, int n, float init) {
+  const float4* v4 = reinterpret_cast<const float4*>(v);
+  float s = init;
+#pragma unroll 8
+  for (int k = 0; k < n / 4; ++k) {
+    const float4 q = v4[k];
+    s = __fadd_rn(s, q.x);
+    s = __fadd_rn(s, q.y);
+    s = __fadd_rn(s, q.z);
+    s = __fadd_rn(s, q.w);
+  }
+  return s;
+}
+
+// the code of yn: the count of ascending thresholds t with !(yn < t)
+// (lloyd_max.rs:132-143), by a binary search of log2(L) steps
+template <int L>
+__device__ __forceinline__ int tile_code(float yn, const float* thr) {
+  int code = 0;
+#pragma unroll
+  for (int step = L >> 1; step > 0; step >>= 1)
+    if (!(yn < thr[code + step - 1])) code += step;
+  return code;
+}
+__device__ __forceinline__ int level_code(float yn, const float* thr, int n_levels) {
+  switch (n_levels) {
+    case 16: return tile_code<16>(yn, thr);
+    case 8: return tile_code<8>(yn, thr);
+    case 4: return tile_code<4>(yn, thr);
+    default: {
+      int code = 0;
+      for (int step = n_levels >> 1; step > 0; step >>= 1)
+        if (!(yn < thr[code + step - 1])) code += step;
+      return code;
+    }
+  }
+}
+
 // n16 16-byte chunks global -> shared with cp.async, issued without waiting.
 __device__ __forceinline__ void stage16(void* dst, const void* src, int n16) {
   const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
@@ -538,7 +578,7 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = -0.0f;
   if constexpr (kContig) {
-#pragma unroll 2
+#pragma unroll 8
     for (int j = 0; j < D; j += 4) {
       const float4 x4 = *reinterpret_cast<const float4*>(x + j);
       const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
@@ -605,20 +645,21 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   // ---- scale (compressor.rs:70-71) ----
   float sc = 0.f, inv = 0.f;
   if (lane == 0) {
-    sc = __fsqrt_rn(__fdiv_rn(seq_sum(res, D, -0.0f), (float)D));
+    sc = __fsqrt_rn(__fdiv_rn(seq_sum4(res, D, -0.0f), (float)D));
     inv = __fdiv_rn(1.0f, sc);
   }
   sc = __shfl_sync(0xffffffffu, sc, 0);
   inv = __shfl_sync(0xffffffffu, inv, 0);
+  // the count of thresholds with !(yn < t): a binary search over the
+  // ascending thresholds gives the same count
+  uint32_t chunk = 0;  // kContig: the lane's R codes, c.bits each
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = own(r);
     int code = 0;
-    if (!(sc < 1e-10f)) {
-      const float yn = __fmul_rn(acc[r], inv);
-      for (int k = 0; k < n1; ++k) code += !(yn < sthr[k]);
-    }
+    if (!(sc < 1e-10f)) code = level_code(__fmul_rn(acc[r], inv), sthr, n1 + 1);
     scode[i] = (uint8_t)code;
+    if constexpr (kContig) chunk |= (uint32_t)code << (c.bits * r);  // r bits <= 24
     y[i] = __fmul_rn(scent[code], sc);
   }
   __syncwarp();
@@ -668,14 +709,24 @@ __global__ void __launch_bounds__(kWarpVecs * 32, 1) k_append_warp(const __grid_
   uint8_t* page = reinterpret_cast<uint8_t*>(a.page_of(slot));
   const int64_t hr = (int64_t)(a.h_base + hl) * kPageTokens + a.row_of(slot);
   const int cpw = 64 / c.bits;
-  for (int w = lane; w < c.words; w += 32) {
-    uint64_t word = 0;
-    for (int k = 0; k < cpw; ++k) {
-      const int idx = w * cpw + k;
-      if (idx < D) word |= (uint64_t)scode[idx] << (k * c.bits);
+  const int rw = a.role_words[side];
+  uint64_t* wdst = reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw]);
+  if (kContig && (c.bits & (c.bits - 1)) == 0 && R * c.bits <= 32) {
+    // lanes own R consecutive codes: a word is the chunks of 64 / (R bits)
+    // neighbouring lanes, OR-combined by shuffles
+    const int lpw = 64 / (R * c.bits);
+    uint64_t word = (uint64_t)chunk << (R * c.bits * (lane & (lpw - 1)));
+    for (int o = 1; o < lpw; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+    if ((lane & (lpw - 1)) == 0) wdst[lane / lpw] = word;
+  } else {
+    for (int w = lane; w < c.words; w += 32) {
+      uint64_t word = 0;
+      for (int k = 0; k < cpw; ++k) {
+        const int idx = w * cpw + k;
+        if (idx < D) word |= (uint64_t)scode[idx] << (k * c.bits);
+      }
+      wdst[w] = word;
     }
-    const int rw = a.role_words[side];
-    reinterpret_cast<uint64_t*>(page + a.off[rw] + hr * a.row[rw])[w] = word;
   }
   if (lane == 0) {
     const int rsg = a.role_sigma[side];
@@ -759,17 +810,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 }
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
-}
-
-// the code of yn: the count of ascending thresholds t with !(yn < t), by a
-// binary search of log2(L) steps
-template <int L>
-__device__ __forceinline__ int tile_code(float yn, const float* thr) {
-  int code = 0;
-#pragma unroll
-  for (int step = L >> 1; step > 0; step >>= 1)
-    if (!(yn < thr[code + step - 1])) code += step;
-  return code;
 }
 
 template <int R, int L>
