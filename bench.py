@@ -559,6 +559,19 @@ def run_ours(args):
         ev1.synchronize()
     elapsed_ms = ev0.elapsed_time(ev1)
     launches = cache.kernel_launches() - launches0  # timed region only
+    # the host time to issue the same step from one native call
+    # (lc_decode_step_layers: the same launches, the layer loop in C++),
+    # against the per-layer calls timed above
+    import numpy as np
+
+    ids_np = np.asarray(ids, np.int32)
+    torch.cuda.synchronize()
+    hl_steps = max(2, min(steps, 5))
+    h0 = time.perf_counter()
+    for _ in range(hl_steps):
+        cache.decode_step_layers(0, ids_np, k1, v1, qs, hq, 1.0, out=out, out_dtype=lc.LC_BF16, stream=stream_ptr)
+    host_layers_ms = (time.perf_counter() - h0) * 1e3 / hl_steps
+    torch.cuda.synchronize()
     ctx1 = cache.ring_state(0, 0)["view_len"]
     # per-kernel device times: CUDA events around each launch, a separate pass
     t_steps = max(2, min(steps, 5))
@@ -771,7 +784,8 @@ def run_ours(args):
                               "issued back to back; wall clock over all steps to the last output in host memory"},
             "gpu_launches": launches,
             "breakdown_ms_per_step": {"decode_attn": dec_ms / t_steps, "append": app_ms / t_steps,
-                                      "other_kernels": other_ms / t_steps, "host_issue": host_ms},
+                                      "other_kernels": other_ms / t_steps, "host_issue": host_ms,
+                                      "host_issue_one_call": host_layers_ms},
             "clocks": clk.summary(),
             "fill_s": fill_s,
         }

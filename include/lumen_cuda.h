@@ -334,6 +334,20 @@ int lc_decode_step(lc_cache* cache, int32_t layer, int32_t n_seqs, const int32_t
                    const void* values, int32_t kv_dtype, const void* q, int32_t q_dtype, int32_t n_q_heads,
                    float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream);
 
+/* lc_decode_step for the layers layer0 .. layer0 + n_layers - 1 of one
+ * decode step, in order, from one call: the per-layer arrays are stacked
+ * [n_layers][...] (keys / values [n_layers][n_seqs][n_kv_heads][1][head_dim],
+ * q and out [n_layers][n_seqs][n_q_heads][head_dim]); results as n_layers
+ * lc_decode_step calls. No counterpart in the reference, whose layer loop
+ * (gemma4_moe.rs:4245-4797) makes the two calls per layer itself: this entry
+ * takes the per-layer crossing of a foreign-function boundary out of a
+ * caller's step, for callers (benchmarks, a replayed decode schedule) whose
+ * layers' inputs are ready together. */
+int lc_decode_step_layers(lc_cache* cache, int32_t layer0, int32_t n_layers, int32_t n_seqs,
+                          const int32_t* seq_ids, const void* keys, const void* values, int32_t kv_dtype,
+                          const void* q, int32_t q_dtype, int32_t n_q_heads, float scale, uint32_t flags, void* out,
+                          int32_t out_dtype, void* stream);
+
 /* Bytes of the fixed device scratch lc_decode_attn_noalloc uses, per device. */
 #define LC_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 

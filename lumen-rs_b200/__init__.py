@@ -49,7 +49,7 @@ ABI_SYMBOLS = [
     "lc_codec_tables", "lc_codec_shape", "lc_codec_free", "lc_packed_words", "lc_cache_create",
     "lc_cache_destroy", "lc_store", "lc_attend_keys", "lc_attend_keys_qjl", "lc_attend_values", "lc_seq_len", "lc_clear",
     "lc_truncate", "lc_append", "lc_append_rope", "lc_truncate_to", "lc_fork", "lc_release", "lc_ring_state", "lc_fetch",
-    "lc_decode_attn", "lc_decode_step", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
+    "lc_decode_attn", "lc_decode_step", "lc_decode_step_layers", "lc_prefill_attn", "lc_decode_attn_noalloc", "lc_decode_attn_partials", "lc_merge_partials", "lc_cache_info", "lc_cache_timing",
     "lc_group_id", "lc_group_create", "lc_group_info", "lc_group_status", "lc_group_destroy", "lc_decode_attn_split",
     "lc_ring_create",
     "lc_ring_update", "lc_ring_truncate_to", "lc_ring_counters", "lc_ring_read", "lc_ring_clear",
@@ -128,6 +128,8 @@ def lib():
         "lc_decode_attn": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_noalloc": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_step": (C.c_int, [vp, i32, i32, vp, vp, vp, i32, vp, i32, i32, C.c_float, u32, vp, i32, vp]),
+        "lc_decode_step_layers": (C.c_int, [vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32, C.c_float, u32, vp, i32,
+                                            vp]),
         "lc_prefill_attn": (C.c_int, [vp, i32, i32, vp, i32, i32, i32, C.c_float, u32, vp, i32, vp]),
         "lc_decode_attn_partials": (C.c_int, [vp, i32, i32, vp, vp, i32, i32, C.c_float, u32, vp, vp, vp, vp]),
         "lc_merge_partials": (C.c_int, [vp, i32, i32, vp, vp, vp, u32, vp, i32, vp]),
@@ -442,6 +444,26 @@ class CudaKvCache:
         stream = _auto_stream(stream, q, keys, out)
         _check(lib().lc_decode_step(self._h, layer, len(ids), _ptr(ids), _ptr(keys), _ptr(values), _dtype_code(keys),
                                     _ptr(q), _dtype_code(q), n_q_heads, scale, flags, _ptr(out), out_dtype, stream))
+        return out
+
+    def decode_step_layers(self, layer0: int, seq_ids, keys, values, q, n_q_heads: int, scale: float = 1.0,
+                           flags: int = 0, out=None, out_dtype: int = LC_F32, stream=None):
+        """decode_step for layers layer0 .. layer0 + len(keys) - 1 from one
+        native call: keys / values [n_layers, n_seqs, n_kv_heads, 1, head_dim],
+        q [n_layers, n_seqs, n_q_heads, head_dim], out like q (all contiguous)."""
+        ids = seq_ids if isinstance(seq_ids, np.ndarray) and seq_ids.dtype == np.int32 else \
+            np.ascontiguousarray(seq_ids, np.int32)
+        n_layers = keys.shape[0]
+        if isinstance(keys, np.ndarray):
+            keys = np.ascontiguousarray(keys, np.float32)
+            values = np.ascontiguousarray(values, np.float32)
+        if out is None:
+            out = np.empty((n_layers, len(ids), n_q_heads, self.head_dim), np.float32)
+            out_dtype = LC_F32
+        stream = _auto_stream(stream, q, keys, out)
+        _check(lib().lc_decode_step_layers(self._h, layer0, n_layers, len(ids), _ptr(ids), _ptr(keys), _ptr(values),
+                                           _dtype_code(keys), _ptr(q), _dtype_code(q), n_q_heads, scale, flags,
+                                           _ptr(out), out_dtype, stream))
         return out
 
     def prefill_attn(self, layer: int, seq: int, q, n_q_heads: int, scale: float = 1.0, flags: int = 0, out=None,

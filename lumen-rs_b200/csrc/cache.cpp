@@ -1513,40 +1513,69 @@ int lc_decode_attn(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* se
 // (the reference's update_and_fetch followed by turboquant_fused_attn on the
 // rotated query, gemma4_moe.rs:4245-4797). The queries are rotated by the
 // same launch that rotates and quantizes the new keys, so the attention
-// kernel takes them rotated and skips its own rotation.
+// kernel takes them rotated and skips its own rotation. The caller holds
+// abi_guard.
+static void decode_step_impl(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
+                             const void* values, int32_t kv_dtype, const void* q, int32_t q_dtype, int32_t n_q_heads,
+                             float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream) {
+  LC_REQUIRE(c && seq_ids && keys && values && q && out, LC_ERR_INVALID, "null argument");
+  LC_REQUIRE(n_seqs > 0 && n_q_heads > 0, LC_ERR_INVALID, "bad decode arguments");
+  dtype_size(q_dtype);
+  LC_CUDA(cudaSetDevice(c->cfg.device));
+  cudaStream_t s = c->pick(stream);
+  const int32_t D = c->cfg.head_dim, H = c->cfg.n_kv_heads;
+  const bool stage2 = (c->cfg.store_flags & (LC_STORE_K_QJL | LC_STORE_V_QJL)) != 0;
+  const int m_max = (int)std::max(c->kc.m, c->vc.m);
+  const bool rot = !(flags & (LC_Q_ROTATED | LC_QJL_SCORES)) &&
+                   append_rotates_queries((int64_t)n_seqs * H, D, m_max, stage2);
+  if (!rot) {
+    append_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, 1, stream, nullptr);
+    attn_call(c, layer, n_seqs, seq_ids, nullptr, q, q_dtype, n_q_heads, scale, flags, out, out_dtype, stream);
+    return;
+  }
+  const int64_t rows = (int64_t)n_seqs * n_q_heads;
+  c->order(s);
+  bool hq = false;
+  const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
+  c->q_step.ensure((size_t)rows * D, s);
+  StepQ sq;
+  sq.q = dq;
+  sq.dtype = q_dtype;
+  sq.rows = (int32_t)rows;
+  sq.out = c->q_step.p;
+  append_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, 1, stream, nullptr, &sq);
+  attn_call(c, layer, n_seqs, seq_ids, nullptr, c->q_step.p, LC_F32, n_q_heads, scale, flags | LC_Q_ROTATED, out,
+            out_dtype, stream);
+  if (hq) LC_CUDA(cudaStreamSynchronize(s));  // the staged queries are read before the host reuses them
+}
+
 int lc_decode_step(lc_cache* c, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, const void* keys,
                    const void* values, int32_t kv_dtype, const void* q, int32_t q_dtype, int32_t n_q_heads,
                    float scale, uint32_t flags, void* out, int32_t out_dtype, void* stream) {
   return abi_guard([&] {
+    decode_step_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, q, q_dtype, n_q_heads, scale, flags, out,
+                     out_dtype, stream);
+  });
+}
+
+int lc_decode_step_layers(lc_cache* c, int32_t layer0, int32_t n_layers, int32_t n_seqs, const int32_t* seq_ids,
+                          const void* keys, const void* values, int32_t kv_dtype, const void* q, int32_t q_dtype,
+                          int32_t n_q_heads, float scale, uint32_t flags, void* out, int32_t out_dtype,
+                          void* stream) {
+  return abi_guard([&] {
     LC_REQUIRE(c && seq_ids && keys && values && q && out, LC_ERR_INVALID, "null argument");
+    LC_REQUIRE(n_layers > 0 && layer0 >= 0 && layer0 + n_layers <= c->cfg.n_layers, LC_ERR_INVALID,
+               "layers out of range");
     LC_REQUIRE(n_seqs > 0 && n_q_heads > 0, LC_ERR_INVALID, "bad decode arguments");
-    dtype_size(q_dtype);
-    LC_CUDA(cudaSetDevice(c->cfg.device));
-    cudaStream_t s = c->pick(stream);
-    const int32_t D = c->cfg.head_dim, H = c->cfg.n_kv_heads;
-    const bool stage2 = (c->cfg.store_flags & (LC_STORE_K_QJL | LC_STORE_V_QJL)) != 0;
-    const int m_max = (int)std::max(c->kc.m, c->vc.m);
-    const bool rot = !(flags & (LC_Q_ROTATED | LC_QJL_SCORES)) &&
-                     append_rotates_queries((int64_t)n_seqs * H, D, m_max, stage2);
-    if (!rot) {
-      append_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, 1, stream, nullptr);
-      attn_call(c, layer, n_seqs, seq_ids, nullptr, q, q_dtype, n_q_heads, scale, flags, out, out_dtype, stream);
-      return;
-    }
-    const int64_t rows = (int64_t)n_seqs * n_q_heads;
-    c->order(s);
-    bool hq = false;
-    const void* dq = c->stage_in(q, (size_t)rows * D * dtype_size(q_dtype), c->qbuf, s, hq);
-    c->q_step.ensure((size_t)rows * D, s);
-    StepQ sq;
-    sq.q = dq;
-    sq.dtype = q_dtype;
-    sq.rows = (int32_t)rows;
-    sq.out = c->q_step.p;
-    append_impl(c, layer, n_seqs, seq_ids, keys, values, kv_dtype, 1, stream, nullptr, &sq);
-    attn_call(c, layer, n_seqs, seq_ids, nullptr, c->q_step.p, LC_F32, n_q_heads, scale, flags | LC_Q_ROTATED, out,
-              out_dtype, stream);
-    if (hq) LC_CUDA(cudaStreamSynchronize(s));  // the staged queries are read before the host reuses them
+    const size_t D = (size_t)c->cfg.head_dim;
+    const size_t kv_stride = (size_t)n_seqs * c->cfg.n_kv_heads * D * dtype_size(kv_dtype);
+    const size_t q_stride = (size_t)n_seqs * n_q_heads * D * dtype_size(q_dtype);
+    const size_t o_stride = (size_t)n_seqs * n_q_heads * D * dtype_size(out_dtype);
+    for (int32_t i = 0; i < n_layers; ++i)
+      decode_step_impl(c, layer0 + i, n_seqs, seq_ids, static_cast<const uint8_t*>(keys) + i * kv_stride,
+                       static_cast<const uint8_t*>(values) + i * kv_stride,
+                       kv_dtype, static_cast<const uint8_t*>(q) + i * q_stride, q_dtype, n_q_heads, scale, flags,
+                       static_cast<uint8_t*>(out) + i * o_stride, out_dtype, stream);
   });
 }
 

@@ -118,3 +118,48 @@ def test_decode_step_config2_geometry(lc, orc, gpu, hq, std):
     assert ok, msg
     a.close()
     b.close()
+
+
+def test_decode_step_layers_equals_per_layer_calls(lc, orc, gpu):
+    """lc_decode_step_layers over 3 stacked layers gives the results of 3
+    lc_decode_step calls (bit for bit: the same launches in the same order)."""
+    import torch
+
+    L, hkv, hq, dim, lens = 3, 8, 32, 128, [900, 300]
+    t = orc.Tables.generate(dim, 4, 64, 42)
+    ck = lc.TurboQuantCompressor.from_tables(t.R, t.bounds, t.cents, t.proj)
+    pages = (max(lens) + 2 * 256 + 255) // 256 + 1  # room for the ring's 256-token growth steps
+    caches = [lc.CudaKvCache(L, hkv, dim, ck, max_seqs=len(lens), max_pages=L * len(lens) * pages + 8,
+                             max_pages_per_seq=pages) for _ in range(2)]
+    ids = np.arange(len(lens), dtype=np.int32)
+    for layer in range(L):
+        for b, n in enumerate(lens):
+            K = helpers.kv(orc, 300 + 10 * layer + 2 * b, 1, hkv, n, dim)
+            V = helpers.kv(orc, 301 + 10 * layer + 2 * b, 1, hkv, n, dim)
+            for c in caches:
+                c.append(layer, [b], K, V)
+    k1 = torch.from_numpy(np.stack([helpers.kv(orc, 400 + l, len(lens), hkv, 1, dim) for l in range(L)])).cuda()
+    v1 = torch.from_numpy(np.stack([helpers.kv(orc, 500 + l, len(lens), hkv, 1, dim) for l in range(L)])).cuda()
+    q = torch.from_numpy(np.stack([helpers.queries(orc, 600 + l, len(lens), hq, dim, std=dim ** -0.5)
+                                   for l in range(L)])).cuda().to(torch.bfloat16)
+    want = torch.empty((L, len(lens), hq, dim), device="cuda", dtype=torch.bfloat16)
+    got = torch.empty_like(want)
+    for layer in range(L):
+        caches[0].decode_step(layer, ids, k1[layer], v1[layer], q[layer], hq, 1.0, out=want[layer],
+                              out_dtype=lc.LC_BF16)
+    caches[1].decode_step_layers(0, ids, k1, v1, q, hq, 1.0, out=got, out_dtype=lc.LC_BF16)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    for layer in range(L):
+        for b in range(len(lens)):
+            fa, fb = caches[0].fetch(b, layer), caches[1].fetch(b, layer)
+            np.testing.assert_array_equal(fa["k_words"], fb["k_words"])
+            np.testing.assert_array_equal(fa["v_sigma"].view(np.uint32), fb["v_sigma"].view(np.uint32))
+    # host inputs and a sub-range of layers
+    kh, vh = k1.cpu().numpy(), v1.cpu().numpy()
+    qh = q.float().cpu().numpy()
+    out_a = caches[0].decode_step(1, ids, kh[1], vh[1], qh[1], hq, 1.0)
+    out_b = caches[1].decode_step_layers(1, ids, kh[1:2], vh[1:2], qh[1:2], hq, 1.0)
+    np.testing.assert_array_equal(out_b[0], out_a)
+    for c in caches:
+        c.close()
