@@ -2450,12 +2450,33 @@ static void plan_core(const int64_t* lens, int n, int hkv, int hq, int dim, int 
     int64_t mx = 0;
     for (int b = 0; b < n; ++b) mx = lens[b] > mx ? lens[b] : mx;
     const int64_t pages = (mx + kPageTokens - 1) / kPageTokens;
-    // 4 pages per chunk (8 on the tensor-core path, whose one block per SM
-    // has 12 warps), or fewer when that leaves too few (sequence, kv head,
-    // chunk) items to fill the GPU (short contexts, sliding windows)
-    int ppc = p.mma ? 16 : 4;
-    const int64_t want = (p.mma ? 4LL : 8LL) * num_sms();
-    while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < want) ppc >>= 1;
+    int ppc = 4;
+    if (p.mma) {
+      // The tensor-core path (one block of 12 warps per SM, an item's
+      // 16-token tiles dealt to the warps in rounds): the chunk of 1 .. 16
+      // pages with the least modelled time, waves x (item set-up + rounds x
+      // round), with a set-up of ~2.7 tile rounds (the query fragments, the
+      // first tile's latency, the block merge; fitted to B200 timings of
+      // 1024-token and 32K-token layers). Short layers get one item per
+      // (sequence, kv head); long ones 16-page chunks.
+      const int64_t sms = num_sms();
+      double best = 0.0;
+      for (int c = 16; c >= 1; c >>= 1) {
+        const int64_t items = (int64_t)n * hkv * ((pages + c - 1) / c);
+        const int64_t waves = (items + sms - 1) / sms;
+        const int64_t rounds = (c * (kPageTokens / 16) + 11) / 12;
+        const double t = (double)waves * (2.7 + (double)rounds);
+        if (c == 16 || t < best) {
+          best = t;
+          ppc = c;
+        }
+      }
+    } else {
+      // 4 pages per chunk, or fewer when that leaves too few (sequence, kv
+      // head, chunk) items to fill the GPU (short contexts, sliding windows)
+      const int64_t want = 8LL * num_sms();
+      while (ppc > 1 && (int64_t)n * hkv * ((pages + ppc - 1) / ppc) < want) ppc >>= 1;
+    }
     p.pages_per_chunk = ppc;
     p.n_chunks = (int32_t)((pages + ppc - 1) / ppc > 0 ? (pages + ppc - 1) / ppc : 1);
     p.max_slots = p.n_chunks;
