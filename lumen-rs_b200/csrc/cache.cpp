@@ -1329,6 +1329,15 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
     a.tile_map = c->tile_map.p;
     a.map_stride = map_stride;
   }
+  // one chunk per (sequence, kv head) on the 3/2-bit tensor-core path (short
+  // and sliding layers): the kernel finishes the rows, no merge launch
+  const bool mma_fin = !fused && plan.mma && plan.n_chunks == 1 && fused_out && !fused_parts;
+  if (mma_fin) {
+    a.fin_out = fused_out;
+    a.fin_dtype = out_dtype;
+    a.fin_R = c->v_R(flags);
+    a.fin_oscale = 1.0f / valpha;
+  }
   if (qjl) {
     a.q_proj = c->q_proj.p;
     a.role_kq = R_KQ;
@@ -1369,7 +1378,7 @@ static DecodeRun decode_common(lc_cache* c, int32_t layer, int32_t n_seqs, const
   ++c->launches;
   if (hq) LC_CUDA(cudaEventRecord(c->ev_copy, s));
   DecodeRun r;
-  r.fused = fused;
+  r.fused = fused || mma_fin;
   r.rows = (int32_t)rows;
   r.G = n_q_heads / hkv;
   r.max_slots = plan.max_slots;

@@ -257,6 +257,7 @@ struct DecodeDev {
   float qscale;
   const float* qR;       // K codec R (row-major): q' = R q
   const float* vRT;      // V codec R^T (row-major): out = R^T o (null: leave rotated)
+  const float* out_R;    // k_decode_mma32 single-chunk finish: V codec R (row-major), null: leave rotated
   const int32_t* cnt;    // [n_seqs * hkv] partial slots
   int32_t* ctr;          // [n_seqs * hkv] arrival counters, zero between launches
   void* out;
@@ -2251,6 +2252,9 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
       }
     }
     __syncthreads();
+    // the chunk's slot; with one chunk per (sequence, kv head) it stays in
+    // the query unit (its fragments are spent) for the finish below
+    float* fin = reinterpret_cast<float*>(qunit);  // [G][kM3PS]
     for (int u = threadIdx.x; u < G * kM3PS; u += blockDim.x) {
       const int hd = u / kM3PS, k = u % kM3PS;
       float M = -INFINITY;
@@ -2265,10 +2269,35 @@ __global__ void __launch_bounds__(kM3Warps * 32, 1) k_decode_mma32(const __grid_
           if (wq[0] != -INFINITY) val += exp2f(wq[0] - M) * wq[k];
         }
       }
-      const int64_t slot = ((int64_t)sq * a.hkv + kvh) * a.max_slots + chunk;
-      a.part[(slot * G + hd) * kM3PS + k] = val;
+      if (a.out) {
+        fin[hd * kM3PS + k] = val;
+      } else {
+        const int64_t slot = ((int64_t)sq * a.hkv + kvh) * a.max_slots + chunk;
+        a.part[(slot * G + hd) * kM3PS + k] = val;
+      }
     }
     __syncthreads();
+    if (a.out) {
+      // out = R^T (o / l) x oscale, as the merge kernel would write it (a NaN
+      // l from a stage wait that ran out stays visible)
+      float* so = reinterpret_cast<float*>(unit(0));  // [G][kM3D]: warp 0's partial was read above
+      for (int u = threadIdx.x; u < G * kM3D; u += blockDim.x) {
+        const int hd = u / kM3D;
+        const float L = fin[hd * kM3PS + 1];
+        so[u] = (L > 0.f || L != L) ? fin[hd * kM3PS + 2 + u % kM3D] * a.oscale / L : 0.f;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < kM3D; i += blockDim.x) {
+        float acc[G];
+#pragma unroll
+        for (int r = 0; r < G; ++r) acc[r] = a.out_R ? 0.f : so[r * kM3D + i];
+        if (a.out_R) mat_col<G>(a.out_R, kM3D, i, so, acc);
+#pragma unroll
+        for (int r = 0; r < G; ++r)
+          store_any(a.out, a.out_dtype, ((int64_t)sq * a.hq + (int64_t)kvh * G + r) * kM3D + i, acc[r]);
+      }
+      __syncthreads();
+    }
   }
   // after a wait that ran out, the copies may still be in flight: wait for
   // each stage's last phase (bounded) before the block's shared memory goes
@@ -2558,6 +2587,12 @@ static DecodeDev make_dev(const DecodeArgs& a, const DecodePlan& p) {
     d.q_dtype = a.q_raw_dtype;
     d.q_rotated = 1;
     d.qscale = a.q_raw_scale;
+  }
+  if (a.fin_out) {
+    d.out = a.fin_out;
+    d.out_dtype = a.fin_dtype;
+    d.out_R = a.fin_R;
+    d.oscale = a.fin_oscale;
   }
   d.kcent = a.kcent;
   d.vcent = a.vcent;

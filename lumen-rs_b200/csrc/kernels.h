@@ -121,6 +121,14 @@ struct DecodeArgs {
   const void* q_raw = nullptr;
   int32_t q_raw_dtype = 0;
   float q_raw_scale = 1.0f;
+  // the tensor-core 3/2-bit kernel with one chunk per (sequence, kv head):
+  // it writes the normalised rows itself, out = R^T (o / l) x fin_oscale in
+  // fin_dtype (fin_R row-major R of the V codec; null leaves them rotated),
+  // and no merge follows; null fin_out: partials as usual
+  void* fin_out = nullptr;
+  int32_t fin_dtype = 0;
+  const float* fin_R = nullptr;
+  float fin_oscale = 1.0f;
   const __half* q_h = nullptr;    // same in f16
   const float* kcent = nullptr;   // [2^kbits]
   const float* vcent = nullptr;   // [2^vbits]
