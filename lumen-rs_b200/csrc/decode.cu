@@ -33,6 +33,8 @@
 //  k_decode_mma32   3-bit K / 2-bit V, d = 256, GQA <= 4 (config 2): chunked
 //                   items, one-lane bulk copies into per-warp stages, 6-bit
 //                   K pair tables and a byte-indexed V table on m16n8k16.
+//                   With one chunk per (sequence, kv head) it normalises and
+//                   un-rotates the rows itself (no merge launch).
 //  k_decode_generic any other bit width / head_dim, and QJL scores:
 //                   CUDA-core, chunked.
 //  k_merge          combines the partials, normalises, un-rotates (R^T).
